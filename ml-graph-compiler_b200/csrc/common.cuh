@@ -1,0 +1,79 @@
+// Shared helpers of libmgc_cuda: error reporting, status codes, element types.
+#pragma once
+
+#include <cuda_runtime.h>
+#include <stdint.h>
+#include <stdio.h>
+#include <stdarg.h>
+#include <string>
+
+#include "mgc_cuda.h"
+
+namespace mgc {
+
+// Text of the last error, per host thread (mgc_cuda_last_error).
+inline std::string &last_error() {
+    static thread_local std::string text;
+    return text;
+}
+
+inline int fail(int status, const char *fmt, ...) {
+    char buf[1024];
+    va_list ap;
+    va_start(ap, fmt);
+    vsnprintf(buf, sizeof buf, fmt, ap);
+    va_end(ap);
+    last_error() = buf;
+    return status;
+}
+
+inline int cuda_fail(cudaError_t err, const char *what) {
+    return fail(MGC_CUDA_CUDA_ERROR + (int)err, "%s: %s (%s)", what, cudaGetErrorString(err),
+                cudaGetErrorName(err));
+}
+
+#define MGC_CHECK_CUDA(call)                                                                 \
+    do {                                                                                     \
+        cudaError_t mgc_err_ = (call);                                                       \
+        if (mgc_err_ != cudaSuccess) return ::mgc::cuda_fail(mgc_err_, #call);               \
+    } while (0)
+
+#define MGC_CHECK(call)                                                                      \
+    do {                                                                                     \
+        int mgc_st_ = (call);                                                                \
+        if (mgc_st_ != MGC_CUDA_OK) return mgc_st_;                                          \
+    } while (0)
+
+// After a kernel launch: report a launch configuration error.
+inline int check_launch(const char *what) {
+    cudaError_t err = cudaGetLastError();
+    if (err != cudaSuccess) return cuda_fail(err, what);
+    return MGC_CUDA_OK;
+}
+
+inline int dtype_size(int dt) {
+    switch (dt) {
+    case MGC_F32: return 4;
+    case MGC_F64: return 8;
+    case MGC_I64: return 8;
+    case MGC_I32: return 4;
+    case MGC_I8: return 1;
+    case MGC_U8: return 1;
+    case MGC_BOOL: return 1;
+    default: return 0;
+    }
+}
+
+inline int64_t ceil_div(int64_t a, int64_t b) { return (a + b - 1) / b; }
+
+// Grid size for a grid-stride loop over `n` items: a multiple of the SM count (148 on B200),
+// capped, never zero.
+inline unsigned grid_for(int64_t n, int threads, int sms = 148, int per_sm = 8) {
+    int64_t blocks = ceil_div(n, threads);
+    int64_t cap = (int64_t)sms * per_sm;
+    if (blocks > cap) blocks = cap;
+    if (blocks < 1) blocks = 1;
+    return (unsigned)blocks;
+}
+
+}  // namespace mgc

@@ -1,0 +1,518 @@
+// Memory-bound kernels: the elementwise program VM (FusedElementwise and single elementwise ops),
+// strided copies (Transpose / Expand / Slice / Concat / Split / Pad / Tile), fills, Gather,
+// Range, generic reductions and ArgMax.
+//
+// Reference lowerings: c.py:360-405 (loop nests with collapsed dimensions and broadcast
+// strides), c.py:471-529 (elementwise programs), c.py:558-821 (data movement, Gather with its
+// out-of-range return, reductions with a double accumulator for float sum/mean/prod, ArgMax).
+// Semantics: ops.py:132-341 (elementwise), ops.py:1165-1202 (program format).
+#pragma once
+
+#include <math.h>
+#include "common.cuh"
+
+namespace mgc {
+
+// ---------------------------------------------------------------------------------------------
+// elementwise program VM
+// ---------------------------------------------------------------------------------------------
+// Operation codes of a program instruction; the Python lowering (mgc_cuda/lowering.py, EW_OPS)
+// uses the same numbering.
+enum EwOp : int16_t {
+    EW_ADD = 0, EW_SUB, EW_MUL, EW_DIV, EW_POW, EW_MAX, EW_MIN,
+    EW_EQ, EW_LT, EW_GT, EW_LE, EW_GE, EW_AND, EW_OR, EW_XOR,
+    EW_WHERE, EW_RELU, EW_SIGMOID, EW_TANH, EW_ERF, EW_SQRT, EW_EXP, EW_LOG,
+    EW_NEG, EW_ABS, EW_RECIP, EW_FLOOR, EW_CEIL, EW_SIN, EW_COS, EW_SOFTPLUS,
+    EW_IDENTITY, EW_NOT, EW_GELU, EW_LEAKYRELU, EW_HARDSIGMOID, EW_CLIP, EW_CAST,
+    EW_NUM_OPS
+};
+
+constexpr int EW_MAX_RANK = 6;
+constexpr int EW_MAX_LEAVES = 20;
+constexpr int EW_MAX_INSTR = 40;
+
+// Arithmetic class of a value: fp32, fp64 or integer (every integer type and bool).
+enum : int8_t { CL_F = 0, CL_D = 1, CL_I = 2 };
+
+__host__ __device__ inline int8_t class_of(int dt) {
+    return dt == MGC_F32 ? CL_F : dt == MGC_F64 ? CL_D : CL_I;
+}
+
+union Reg {
+    float f;
+    double d;
+    long long i;
+};
+
+struct EwLeaf {
+    const void *p;
+    long long strides[EW_MAX_RANK];  // element strides over the output dimensions (0: broadcast)
+    Reg lit;                         // value of a scalar constant leaf
+    int32_t dtype;
+    int32_t is_lit;
+};
+
+struct EwInstr {
+    int16_t op;
+    int16_t out_dt;
+    int16_t a[3];  // register numbers (leaves first, then instruction results); -1: absent
+    int16_t pad;
+    double imm[2]; // op attributes (Clip bounds, LeakyRelu alpha, HardSigmoid alpha/beta, Gelu kind)
+};
+
+struct EwParams {
+    long long shape[EW_MAX_RANK];
+    long long total;
+    void *out;
+    int32_t rank;
+    int32_t out_dt;
+    int32_t nleaves;
+    int32_t ninstr;
+    int32_t contiguous;  // rank 1 and every tensor leaf has stride 1 or 0
+    int8_t cls[EW_MAX_LEAVES + EW_MAX_INSTR];
+    EwLeaf leaves[EW_MAX_LEAVES];
+    EwInstr ins[EW_MAX_INSTR];
+};
+
+__device__ inline Reg load_elem(const void *p, int dt, long long i) {
+    Reg r;
+    switch (dt) {
+    case MGC_F32: r.f = ((const float *)p)[i]; break;
+    case MGC_F64: r.d = ((const double *)p)[i]; break;
+    case MGC_I64: r.i = ((const long long *)p)[i]; break;
+    case MGC_I32: r.i = ((const int *)p)[i]; break;
+    case MGC_I8: r.i = ((const signed char *)p)[i]; break;
+    default: r.i = ((const unsigned char *)p)[i]; break;  // U8, BOOL
+    }
+    return r;
+}
+
+__device__ inline void store_elem(void *p, int dt, long long i, Reg r) {
+    switch (dt) {
+    case MGC_F32: ((float *)p)[i] = r.f; break;
+    case MGC_F64: ((double *)p)[i] = r.d; break;
+    case MGC_I64: ((long long *)p)[i] = r.i; break;
+    case MGC_I32: ((int *)p)[i] = (int)r.i; break;
+    case MGC_I8: ((signed char *)p)[i] = (signed char)r.i; break;
+    case MGC_BOOL: ((unsigned char *)p)[i] = r.i != 0; break;
+    default: ((unsigned char *)p)[i] = (unsigned char)r.i; break;
+    }
+}
+
+__device__ inline double as_d(Reg r, int c) { return c == CL_F ? (double)r.f : c == CL_D ? r.d : (double)r.i; }
+__device__ inline float as_f(Reg r, int c) { return c == CL_F ? r.f : c == CL_D ? (float)r.d : (float)r.i; }
+__device__ inline long long as_i(Reg r, int c) {
+    return c == CL_F ? (long long)r.f : c == CL_D ? (long long)r.d : r.i;
+}
+
+// Convert a value of class `c` to the representation of dtype `dt` (bool: nonzero test).
+__device__ inline Reg convert(Reg r, int c, int dt) {
+    Reg o;
+    if (dt == MGC_F32) o.f = as_f(r, c);
+    else if (dt == MGC_F64) o.d = as_d(r, c);
+    else if (dt == MGC_BOOL) o.i = (c == CL_F ? r.f != 0.0f : c == CL_D ? r.d != 0.0 : r.i != 0);
+    else o.i = as_i(r, c);
+    return o;
+}
+
+__device__ inline float f_sigmoid(float x) { return 0.5f * (1.0f + tanhf(0.5f * x)); }
+__device__ inline double d_sigmoid(double x) { return 0.5 * (1.0 + tanh(0.5 * x)); }
+__device__ inline float f_gelu(float x) { return 0.5f * x * (1.0f + erff(x * 0.70710678118654752f)); }
+__device__ inline float f_gelu_tanh(float x) {
+    return 0.5f * x * (1.0f + tanhf(0.79788456080286536f * (x + 0.044715f * x * x * x)));
+}
+__device__ inline double d_gelu(double x) { return 0.5 * x * (1.0 + erf(x * 0.70710678118654752)); }
+__device__ inline double d_gelu_tanh(double x) {
+    return 0.5 * x * (1.0 + tanh(0.79788456080286536 * (x + 0.044715 * x * x * x)));
+}
+// log(1 + e^x) = max(x, 0) + log1p(e^-|x|)  (np.logaddexp(0, x), ops.py:259)
+__device__ inline float f_softplus(float x) { return fmaxf(x, 0.0f) + log1pf(expf(-fabsf(x))); }
+__device__ inline double d_softplus(double x) { return fmax(x, 0.0) + log1p(exp(-fabs(x))); }
+
+// Evaluate one instruction. `cls` gives the class of every register.
+__device__ inline Reg ew_eval(const EwInstr &in, const Reg *regs, const int8_t *cls) {
+    const int oc = class_of(in.out_dt);
+    const int a0 = in.a[0], a1 = in.a[1], a2 = in.a[2];
+    Reg x = regs[a0];
+    const int cx = cls[a0];
+    Reg y{}, r{};
+    int cy = CL_I;
+    if (a1 >= 0) { y = regs[a1]; cy = cls[a1]; }
+    int op = in.op;
+    if (op <= EW_MIN || (op >= EW_EQ && op <= EW_GE)) {
+        // binary arithmetic / comparison in the promoted class
+        const int pc = (cx == CL_D || cy == CL_D) ? CL_D : (cx == CL_F || cy == CL_F) ? CL_F : CL_I;
+        if (pc == CL_F) {
+            float u = as_f(x, cx), v = as_f(y, cy), w = 0.0f;
+            switch (op) {
+            case EW_ADD: w = u + v; break;
+            case EW_SUB: w = u - v; break;
+            case EW_MUL: w = u * v; break;
+            case EW_DIV: w = u / v; break;
+            case EW_POW: w = powf(u, v); break;
+            case EW_MAX: w = fmaxf(u, v); break;
+            case EW_MIN: w = fminf(u, v); break;
+            case EW_EQ: r.i = u == v; return r;
+            case EW_LT: r.i = u < v; return r;
+            case EW_GT: r.i = u > v; return r;
+            case EW_LE: r.i = u <= v; return r;
+            default: r.i = u >= v; return r;
+            }
+            Reg t; t.f = w;
+            return convert(t, CL_F, in.out_dt);
+        } else if (pc == CL_D) {
+            double u = as_d(x, cx), v = as_d(y, cy), w = 0.0;
+            switch (op) {
+            case EW_ADD: w = u + v; break;
+            case EW_SUB: w = u - v; break;
+            case EW_MUL: w = u * v; break;
+            case EW_DIV: w = u / v; break;
+            case EW_POW: w = pow(u, v); break;
+            case EW_MAX: w = fmax(u, v); break;
+            case EW_MIN: w = fmin(u, v); break;
+            case EW_EQ: r.i = u == v; return r;
+            case EW_LT: r.i = u < v; return r;
+            case EW_GT: r.i = u > v; return r;
+            case EW_LE: r.i = u <= v; return r;
+            default: r.i = u >= v; return r;
+            }
+            Reg t; t.d = w;
+            return convert(t, CL_D, in.out_dt);
+        } else {
+            long long u = x.i, v = y.i, w = 0;
+            switch (op) {
+            case EW_ADD: w = u + v; break;
+            case EW_SUB: w = u - v; break;
+            case EW_MUL: w = u * v; break;
+            case EW_DIV: w = v != 0 ? u / v : 0; break;  // truncation, as np.trunc(a / b)
+            case EW_POW: { long long acc = 1; for (long long k = 0; k < v && k < 64; ++k) acc *= u; w = v < 0 ? 0 : acc; } break;
+            case EW_MAX: w = u > v ? u : v; break;
+            case EW_MIN: w = u < v ? u : v; break;
+            case EW_EQ: r.i = u == v; return r;
+            case EW_LT: r.i = u < v; return r;
+            case EW_GT: r.i = u > v; return r;
+            case EW_LE: r.i = u <= v; return r;
+            default: r.i = u >= v; return r;
+            }
+            Reg t; t.i = w;
+            return convert(t, CL_I, in.out_dt);
+        }
+    }
+    switch (op) {
+    case EW_AND: r.i = (as_i(x, cx) != 0) && (as_i(y, cy) != 0); return r;
+    case EW_OR: r.i = (as_i(x, cx) != 0) || (as_i(y, cy) != 0); return r;
+    case EW_XOR: r.i = (as_i(x, cx) != 0) != (as_i(y, cy) != 0); return r;
+    case EW_NOT: r.i = as_i(x, cx) == 0; return r;
+    case EW_WHERE: {
+        Reg z = regs[a2];
+        return as_i(x, cx) != 0 ? convert(y, cy, in.out_dt) : convert(z, cls[a2], in.out_dt);
+    }
+    case EW_CAST: return convert(x, cx, in.out_dt);
+    case EW_IDENTITY: return convert(x, cx, in.out_dt);
+    case EW_CLIP: {
+        // bounds from optional inputs (a1, a2) or from the attributes (imm)
+        if (cx == CL_I) {
+            long long v = x.i;
+            if (a1 >= 0) { long long lo = as_i(y, cy); v = v < lo ? lo : v; }
+            if (a2 >= 0) { long long hi = as_i(regs[a2], cls[a2]); v = v > hi ? hi : v; }
+            Reg t; t.i = v;
+            return convert(t, CL_I, in.out_dt);
+        }
+        double lo = a1 >= 0 ? as_d(y, cy) : in.imm[0];
+        double hi = a2 >= 0 ? as_d(regs[a2], cls[a2]) : in.imm[1];
+        if (cx == CL_F) {
+            Reg t; t.f = fminf(fmaxf(x.f, (float)lo), (float)hi);
+            return convert(t, CL_F, in.out_dt);
+        }
+        Reg t; t.d = fmin(fmax(x.d, lo), hi);
+        return convert(t, CL_D, in.out_dt);
+    }
+    default: break;
+    }
+    // unary operators
+    if (cx == CL_I && (op == EW_RELU || op == EW_NEG || op == EW_ABS)) {
+        long long v = x.i;
+        Reg t;
+        t.i = op == EW_RELU ? (v > 0 ? v : 0) : op == EW_NEG ? -v : (v < 0 ? -v : v);
+        return convert(t, CL_I, in.out_dt);
+    }
+    if (cx == CL_F) {
+        float v = x.f, w;
+        switch (op) {
+        case EW_RELU: w = fmaxf(v, 0.0f); break;
+        case EW_SIGMOID: w = f_sigmoid(v); break;
+        case EW_TANH: w = tanhf(v); break;
+        case EW_ERF: w = erff(v); break;
+        case EW_SQRT: w = sqrtf(v); break;
+        case EW_EXP: w = expf(v); break;
+        case EW_LOG: w = logf(v); break;
+        case EW_NEG: w = -v; break;
+        case EW_ABS: w = fabsf(v); break;
+        case EW_RECIP: w = 1.0f / v; break;
+        case EW_FLOOR: w = floorf(v); break;
+        case EW_CEIL: w = ceilf(v); break;
+        case EW_SIN: w = sinf(v); break;
+        case EW_COS: w = cosf(v); break;
+        case EW_SOFTPLUS: w = f_softplus(v); break;
+        case EW_GELU: w = in.imm[0] != 0.0 ? f_gelu_tanh(v) : f_gelu(v); break;
+        case EW_LEAKYRELU: w = v >= 0.0f ? v : (float)in.imm[0] * v; break;
+        case EW_HARDSIGMOID: w = fminf(fmaxf((float)in.imm[0] * v + (float)in.imm[1], 0.0f), 1.0f); break;
+        default: w = v; break;
+        }
+        Reg t; t.f = w;
+        return convert(t, CL_F, in.out_dt);
+    }
+    double v = as_d(x, cx), w;
+    switch (op) {
+    case EW_RELU: w = fmax(v, 0.0); break;
+    case EW_SIGMOID: w = d_sigmoid(v); break;
+    case EW_TANH: w = tanh(v); break;
+    case EW_ERF: w = erf(v); break;
+    case EW_SQRT: w = sqrt(v); break;
+    case EW_EXP: w = exp(v); break;
+    case EW_LOG: w = log(v); break;
+    case EW_NEG: w = -v; break;
+    case EW_ABS: w = fabs(v); break;
+    case EW_RECIP: w = 1.0 / v; break;
+    case EW_FLOOR: w = floor(v); break;
+    case EW_CEIL: w = ceil(v); break;
+    case EW_SIN: w = sin(v); break;
+    case EW_COS: w = cos(v); break;
+    case EW_SOFTPLUS: w = d_softplus(v); break;
+    case EW_GELU: w = in.imm[0] != 0.0 ? d_gelu_tanh(v) : d_gelu(v); break;
+    case EW_LEAKYRELU: w = v >= 0.0 ? v : in.imm[0] * v; break;
+    case EW_HARDSIGMOID: w = fmin(fmax(in.imm[0] * v + in.imm[1], 0.0), 1.0); break;
+    default: w = v; break;
+    }
+    Reg t; t.d = w;
+    return convert(t, CL_D, in.out_dt);
+}
+
+__global__ void __launch_bounds__(256) ew_kernel(const __grid_constant__ EwParams P) {
+    Reg regs[EW_MAX_LEAVES + EW_MAX_INSTR];
+    const long long stride = (long long)gridDim.x * blockDim.x;
+    for (long long o = (long long)blockIdx.x * blockDim.x + threadIdx.x; o < P.total; o += stride) {
+        if (P.contiguous) {
+            for (int l = 0; l < P.nleaves; ++l) {
+                const EwLeaf &lf = P.leaves[l];
+                regs[l] = lf.is_lit ? lf.lit : load_elem(lf.p, lf.dtype, o * lf.strides[0]);
+            }
+        } else {
+            long long idx[EW_MAX_RANK];
+            long long rem = o;
+            for (int d = P.rank - 1; d >= 0; --d) {
+                idx[d] = rem % P.shape[d];
+                rem /= P.shape[d];
+            }
+            for (int l = 0; l < P.nleaves; ++l) {
+                const EwLeaf &lf = P.leaves[l];
+                if (lf.is_lit) {
+                    regs[l] = lf.lit;
+                    continue;
+                }
+                long long off = 0;
+                for (int d = 0; d < P.rank; ++d) off += idx[d] * lf.strides[d];
+                regs[l] = load_elem(lf.p, lf.dtype, off);
+            }
+        }
+        for (int k = 0; k < P.ninstr; ++k) regs[P.nleaves + k] = ew_eval(P.ins[k], regs, P.cls);
+        store_elem(P.out, P.out_dt, o, regs[P.nleaves + P.ninstr - 1]);
+    }
+}
+
+// ---------------------------------------------------------------------------------------------
+// strided copy: dst[dbase + sum idx*dstr] = src[sbase + sum idx*sstr] over `shape`
+// ---------------------------------------------------------------------------------------------
+constexpr int COPY_MAX_RANK = 8;
+
+struct CopyParams {
+    long long shape[COPY_MAX_RANK];
+    long long sstr[COPY_MAX_RANK];
+    long long dstr[COPY_MAX_RANK];
+    long long sbase, dbase, total;
+    const char *src;
+    char *dst;
+    int32_t rank;
+    int32_t esize;
+};
+
+template <typename T>
+__global__ void __launch_bounds__(256) copy_kernel(const __grid_constant__ CopyParams P) {
+    const T *src = (const T *)P.src;
+    T *dst = (T *)P.dst;
+    const long long stride = (long long)gridDim.x * blockDim.x;
+    for (long long o = (long long)blockIdx.x * blockDim.x + threadIdx.x; o < P.total; o += stride) {
+        long long rem = o, s = P.sbase, d = P.dbase;
+        for (int k = P.rank - 1; k >= 0; --k) {
+            long long i = rem % P.shape[k];
+            rem /= P.shape[k];
+            s += i * P.sstr[k];
+            d += i * P.dstr[k];
+        }
+        dst[d] = src[s];
+    }
+}
+
+// Tile: out[o] = x[src(o)] with src dims taken modulo the input shape (c.py:571-588).
+struct TileParams {
+    long long oshape[COPY_MAX_RANK];
+    long long xshape[COPY_MAX_RANK];
+    long long xstr[COPY_MAX_RANK];
+    long long total;
+    const char *src;
+    char *dst;
+    int32_t rank;
+    int32_t esize;
+};
+
+template <typename T>
+__global__ void __launch_bounds__(256) tile_kernel(const __grid_constant__ TileParams P) {
+    const T *src = (const T *)P.src;
+    T *dst = (T *)P.dst;
+    const long long stride = (long long)gridDim.x * blockDim.x;
+    for (long long o = (long long)blockIdx.x * blockDim.x + threadIdx.x; o < P.total; o += stride) {
+        long long rem = o, s = 0;
+        for (int k = P.rank - 1; k >= 0; --k) {
+            long long i = rem % P.oshape[k];
+            rem /= P.oshape[k];
+            s += (i % P.xshape[k]) * P.xstr[k];
+        }
+        dst[o] = src[s];
+    }
+}
+
+// ---------------------------------------------------------------------------------------------
+// fill / range / gather
+// ---------------------------------------------------------------------------------------------
+template <typename T>
+__global__ void fill_kernel(T *dst, long long n, T value) {
+    const long long stride = (long long)gridDim.x * blockDim.x;
+    for (long long o = (long long)blockIdx.x * blockDim.x + threadIdx.x; o < n; o += stride) dst[o] = value;
+}
+
+// y[i] = start + i * delta, start/delta read from device scalars of dtype dt (c.py:724-734).
+__global__ void range_kernel(void *y, int dt, long long n, const void *start, const void *delta) {
+    const long long stride = (long long)gridDim.x * blockDim.x;
+    Reg s = load_elem(start, dt, 0), d = load_elem(delta, dt, 0);
+    for (long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += stride) {
+        Reg v;
+        if (dt == MGC_F32) v.f = s.f + (float)i * d.f;
+        else if (dt == MGC_F64) v.d = s.d + (double)i * d.d;
+        else v.i = s.i + i * d.i;
+        store_elem(y, dt, i, v);
+    }
+}
+
+// out[(o * n + t) * inner + j] = x[(o * dim + k) * inner + j], k = idx[t] (+dim if negative).
+// An out-of-range index sets *status (the C backend returns 1 from mgc_run, c.py:678-680) and
+// writes zeros for that row.
+template <typename T>
+__global__ void __launch_bounds__(256) gather_kernel(const T *x, const void *idx, int idx_dt, T *out,
+                                                     long long outer, long long dim, long long inner,
+                                                     long long n, int *status) {
+    const long long total = outer * n * inner;
+    const long long stride = (long long)gridDim.x * blockDim.x;
+    for (long long e = (long long)blockIdx.x * blockDim.x + threadIdx.x; e < total; e += stride) {
+        long long j = e % inner;
+        long long t = (e / inner) % n;
+        long long o = e / (inner * n);
+        long long k = idx_dt == MGC_I32 ? (long long)((const int *)idx)[t] : ((const long long *)idx)[t];
+        if (k < 0) k += dim;
+        if (k < 0 || k >= dim) {
+            if (status) atomicExch(status, MGC_CUDA_GATHER_OOB);
+            out[e] = T(0);
+            continue;
+        }
+        out[e] = x[(o * dim + k) * inner + j];
+    }
+}
+
+// ---------------------------------------------------------------------------------------------
+// reductions over the middle axis of [outer, n, inner]
+// ---------------------------------------------------------------------------------------------
+// mgc_reduce_mid (mgc_kernels.c:593-612): float mean / max, sequential fp32 accumulation.
+__global__ void __launch_bounds__(256) reduce_mid_kernel(int is_max, long long outer, long long n,
+                                                         long long inner, const float *x, float *y) {
+    const long long total = outer * inner;
+    const long long stride = (long long)gridDim.x * blockDim.x;
+    const float inv = n > 0 ? 1.0f / (float)n : 0.0f;
+    for (long long e = (long long)blockIdx.x * blockDim.x + threadIdx.x; e < total; e += stride) {
+        long long o = e / inner, i = e % inner;
+        const float *src = x + o * n * inner + i;
+        float acc = is_max ? -INFINITY : 0.0f;
+        for (long long k = 0; k < n; ++k) {
+            float v = src[k * inner];
+            acc = is_max ? (v > acc ? v : acc) : acc + v;
+        }
+        y[e] = is_max ? acc : acc * inv;
+    }
+}
+
+// Generic ReduceSum/Mean/Prod/Max/Min (c.py:736-784): double accumulator for float sum, mean
+// and prod, the element type otherwise.
+enum { RED_SUM = 0, RED_MEAN = 1, RED_PROD = 2, RED_MAX = 3, RED_MIN = 4 };
+
+__global__ void __launch_bounds__(256) reduce_kernel(int kind, int dt, long long outer, long long n,
+                                                     long long inner, const void *x, void *y) {
+    const long long total = outer * inner;
+    const long long stride = (long long)gridDim.x * blockDim.x;
+    const int c = class_of(dt);
+    for (long long e = (long long)blockIdx.x * blockDim.x + threadIdx.x; e < total; e += stride) {
+        long long o = e / inner, i = e % inner;
+        long long base = o * n * inner + i;
+        Reg out;
+        if (c != CL_I) {
+            double acc = kind == RED_PROD ? 1.0 : kind == RED_MAX ? -INFINITY : kind == RED_MIN ? INFINITY : 0.0;
+            for (long long k = 0; k < n; ++k) {
+                double v = as_d(load_elem(x, dt, base + k * inner), c);
+                if (kind == RED_SUM || kind == RED_MEAN) acc += v;
+                else if (kind == RED_PROD) acc *= v;
+                else if (kind == RED_MAX) acc = v > acc ? v : acc;
+                else acc = v < acc ? v : acc;
+            }
+            if (kind == RED_MEAN) acc = acc / (double)n;
+            if (c == CL_F) out.f = (float)acc; else out.d = acc;
+        } else {
+            long long acc = kind == RED_PROD ? 1 : kind == RED_MAX ? LLONG_MIN : kind == RED_MIN ? LLONG_MAX : 0;
+            for (long long k = 0; k < n; ++k) {
+                long long v = load_elem(x, dt, base + k * inner).i;
+                if (kind == RED_SUM || kind == RED_MEAN) acc += v;
+                else if (kind == RED_PROD) acc *= v;
+                else if (kind == RED_MAX) acc = v > acc ? v : acc;
+                else acc = v < acc ? v : acc;
+            }
+            if (kind == RED_MEAN) acc = n ? acc / n : 0;
+            out.i = acc;
+        }
+        store_elem(y, dt, e, out);
+    }
+}
+
+// ArgMax along the middle axis, first maximum wins (c.py:801-821).
+__global__ void __launch_bounds__(256) argmax_kernel(int dt, long long outer, long long n, long long inner,
+                                                     const void *x, long long *y) {
+    const long long total = outer * inner;
+    const long long stride = (long long)gridDim.x * blockDim.x;
+    const int c = class_of(dt);
+    for (long long e = (long long)blockIdx.x * blockDim.x + threadIdx.x; e < total; e += stride) {
+        long long o = e / inner, i = e % inner;
+        long long base = o * n * inner + i;
+        long long best = 0;
+        if (c == CL_I) {
+            long long bv = load_elem(x, dt, base).i;
+            for (long long k = 1; k < n; ++k) {
+                long long v = load_elem(x, dt, base + k * inner).i;
+                if (v > bv) { bv = v; best = k; }
+            }
+        } else {
+            double bv = as_d(load_elem(x, dt, base), c);
+            for (long long k = 1; k < n; ++k) {
+                double v = as_d(load_elem(x, dt, base + k * inner), c);
+                if (v > bv) { bv = v; best = k; }
+            }
+        }
+        y[e] = best;
+    }
+}
+
+}  // namespace mgc

@@ -1,0 +1,371 @@
+// Decoding of mgc_cuda_launch records (built by mgc_cuda/lowering.py) into kernel parameters,
+// and the dispatch of one record onto a stream. The slot layout of every kind is documented at
+// the matching `_emit_*` function of the lowering; the two must stay in step.
+#pragma once
+
+#include <vector>
+
+#include "common.cuh"
+#include "gemm_simt.cuh"
+#include "gemm_umma.cuh"
+#include "kernels_mem.cuh"
+#include "kernels_norm.cuh"
+
+namespace mgc {
+
+// Device base addresses the references of a launch list resolve against.
+struct Bases {
+    char *arena = nullptr;
+    char *weights = nullptr;
+    const std::vector<char *> *inputs = nullptr;
+    const std::vector<char *> *outputs = nullptr;
+};
+
+inline int resolve(const mgc_cuda_ref &r, const Bases &b, void **out) {
+    switch (r.space) {
+    case MGC_SPACE_NONE: *out = nullptr; return MGC_CUDA_OK;
+    case MGC_SPACE_RAW: *out = (void *)(uintptr_t)r.offset; return MGC_CUDA_OK;
+    case MGC_SPACE_ARENA:
+        if (!b.arena) break;
+        *out = b.arena + r.offset;
+        return MGC_CUDA_OK;
+    case MGC_SPACE_WEIGHTS:
+        if (!b.weights) break;
+        *out = b.weights + r.offset;
+        return MGC_CUDA_OK;
+    case MGC_SPACE_INPUT:
+        if (!b.inputs || r.index < 0 || r.index >= (int)b.inputs->size()) break;
+        *out = (*b.inputs)[r.index] + r.offset;
+        return MGC_CUDA_OK;
+    case MGC_SPACE_OUTPUT:
+        if (!b.outputs || r.index < 0 || r.index >= (int)b.outputs->size()) break;
+        *out = (*b.outputs)[r.index] + r.offset;
+        return MGC_CUDA_OK;
+    default: break;
+    }
+    return fail(MGC_CUDA_BAD_ARGUMENT, "reference space %d (index %d) cannot be resolved here",
+                r.space, r.index);
+}
+
+#define MGC_RESOLVE(ref, ptr)                                                                \
+    do {                                                                                     \
+        void *mgc_p_ = nullptr;                                                              \
+        MGC_CHECK(resolve((ref), bases, &mgc_p_));                                           \
+        (ptr) = (decltype(ptr))mgc_p_;                                                       \
+    } while (0)
+
+// Run every GEMM-family launch: the tcgen05 kernel when it accepts the problem, else SIMT.
+inline int run_gemm(const GemmParams &p, cudaStream_t stream, int *used_tensor_cores = nullptr) {
+    int taken = 0;
+    MGC_CHECK(try_gemm_umma(p, stream, &taken));
+    if (used_tensor_cores) *used_tensor_cores = taken;
+    if (taken) return MGC_CUDA_OK;
+    return launch_gemm_simt(p, stream);
+}
+
+inline int decode_gemm(const mgc_cuda_launch &L, const Bases &bases, GemmParams &p) {
+    const int64_t *i = L.i;
+    p = GemmParams{};
+    p.M = (int)i[0]; p.N = (int)i[1]; p.K = (int)i[2];
+    p.nb = (int)i[3];
+    if (p.nb < 0 || p.nb > 4) return fail(MGC_CUDA_BAD_ARGUMENT, "gemm: %d batch dims", p.nb);
+    for (int d = 0; d < 4; ++d) {
+        p.bdims[d] = i[4 + d];
+        p.a_bs[d] = i[8 + d]; p.b_bs[d] = i[12 + d]; p.c_bs[d] = i[16 + d]; p.r_bs[d] = i[20 + d];
+    }
+    p.a_kind = (int)i[24]; p.a_rs = i[25]; p.a_cs = i[26];
+    p.H = (int)i[27]; p.W = (int)i[28]; p.C = (int)i[29]; p.KH = (int)i[30]; p.KW = (int)i[31];
+    p.SH = (int)i[32]; p.SW = (int)i[33]; p.DH = (int)i[34]; p.DW = (int)i[35];
+    p.PT = (int)i[36]; p.PL = (int)i[37]; p.OW = (int)i[38]; p.c_off = (int)i[39]; p.cg = (int)i[40];
+    p.b_kind = (int)i[41]; p.b_rs = i[42]; p.b_cs = i[43];
+    p.ldc = i[44]; p.bias_mode = (int)i[45]; p.ldr = i[46]; p.act = (int)i[47];
+    p.precision = (int)i[48]; p.OH = (int)i[49];
+    p.alpha = (float)L.f[0]; p.beta = (float)L.f[1]; p.lo = (float)L.f[2]; p.hi = (float)L.f[3];
+    MGC_RESOLVE(L.r[0], p.a);
+    MGC_RESOLVE(L.r[1], p.b);
+    MGC_RESOLVE(L.r[2], p.c);
+    MGC_RESOLVE(L.r[3], p.bias);
+    MGC_RESOLVE(L.r[4], p.res);
+    MGC_RESOLVE(L.r[5], p.b_lo);
+    if (!p.a || !p.b || !p.c) return fail(MGC_CUDA_BAD_ARGUMENT, "gemm: missing operand");
+    return MGC_CUDA_OK;
+}
+
+inline int decode_elementwise(const mgc_cuda_launch &L, const int64_t *aux, int64_t aux_len,
+                              const Bases &bases, EwParams &P) {
+    int64_t pos = L.aux_offset, end = L.aux_offset + L.aux_len;
+    if (pos < 0 || end > aux_len) return fail(MGC_CUDA_BAD_ARGUMENT, "elementwise: aux out of range");
+    auto next = [&](int64_t &v) -> bool {
+        if (pos >= end) return false;
+        v = aux[pos++];
+        return true;
+    };
+    int64_t v = 0;
+    memset(&P, 0, sizeof P);
+    if (!next(v) || v < 0 || v > EW_MAX_RANK) return fail(MGC_CUDA_UNSUPPORTED, "elementwise: rank %lld", (long long)v);
+    P.rank = (int)v;
+    P.total = 1;
+    for (int d = 0; d < P.rank; ++d) {
+        if (!next(v)) return fail(MGC_CUDA_BAD_ARGUMENT, "elementwise: truncated shape");
+        P.shape[d] = v;
+        P.total *= v;
+    }
+    int64_t sp, ix, off;
+    if (!next(v)) return fail(MGC_CUDA_BAD_ARGUMENT, "elementwise: truncated");
+    P.out_dt = (int)v;
+    if (!next(sp) || !next(ix) || !next(off)) return fail(MGC_CUDA_BAD_ARGUMENT, "elementwise: truncated");
+    mgc_cuda_ref oref{(int32_t)sp, (int32_t)ix, off};
+    MGC_RESOLVE(oref, P.out);
+    if (!next(v) || v < 0 || v > EW_MAX_LEAVES)
+        return fail(MGC_CUDA_UNSUPPORTED, "elementwise: %lld leaves (max %d)", (long long)v, EW_MAX_LEAVES);
+    P.nleaves = (int)v;
+    P.contiguous = P.rank <= 1 ? 1 : 0;
+    for (int l = 0; l < P.nleaves; ++l) {
+        EwLeaf &lf = P.leaves[l];
+        int64_t dt, lit, bits;
+        if (!next(dt) || !next(lit) || !next(bits) || !next(sp) || !next(ix) || !next(off))
+            return fail(MGC_CUDA_BAD_ARGUMENT, "elementwise: truncated leaf");
+        lf.dtype = (int)dt;
+        lf.is_lit = (int)lit;
+        P.cls[l] = class_of(lf.dtype);
+        if (lf.is_lit) {
+            double d;
+            memcpy(&d, &bits, sizeof d);
+            if (lf.dtype == MGC_F32) lf.lit.f = (float)d;
+            else if (lf.dtype == MGC_F64) lf.lit.d = d;
+            else lf.lit.i = bits;
+        } else {
+            mgc_cuda_ref r{(int32_t)sp, (int32_t)ix, off};
+            MGC_RESOLVE(r, lf.p);
+        }
+        for (int d = 0; d < P.rank; ++d) {
+            if (!next(v)) return fail(MGC_CUDA_BAD_ARGUMENT, "elementwise: truncated strides");
+            lf.strides[d] = v;
+            if (!lf.is_lit && P.rank == 1 && v != 0 && v != 1) P.contiguous = 0;
+        }
+        if (P.rank == 0) lf.strides[0] = 0;
+    }
+    if (!next(v) || v < 1 || v > EW_MAX_INSTR)
+        return fail(MGC_CUDA_UNSUPPORTED, "elementwise: %lld instructions (max %d)", (long long)v, EW_MAX_INSTR);
+    P.ninstr = (int)v;
+    for (int k = 0; k < P.ninstr; ++k) {
+        EwInstr &in = P.ins[k];
+        int64_t op, odt, a0, a1, a2, b0, b1;
+        if (!next(op) || !next(odt) || !next(a0) || !next(a1) || !next(a2) || !next(b0) || !next(b1))
+            return fail(MGC_CUDA_BAD_ARGUMENT, "elementwise: truncated instruction");
+        if (op < 0 || op >= EW_NUM_OPS) return fail(MGC_CUDA_UNSUPPORTED, "elementwise: op %lld", (long long)op);
+        const int64_t lim = P.nleaves + k;
+        if (a0 < 0 || a0 >= lim || a1 >= lim || a2 >= lim)
+            return fail(MGC_CUDA_BAD_ARGUMENT, "elementwise: instruction %d reads a later register", k);
+        in.op = (int16_t)op; in.out_dt = (int16_t)odt;
+        in.a[0] = (int16_t)a0; in.a[1] = (int16_t)a1; in.a[2] = (int16_t)a2;
+        memcpy(&in.imm[0], &b0, sizeof(double));
+        memcpy(&in.imm[1], &b1, sizeof(double));
+        P.cls[P.nleaves + k] = class_of(in.out_dt);
+    }
+    if (P.rank == 0) P.shape[0] = 1;
+    return MGC_CUDA_OK;
+}
+
+template <typename T>
+inline int launch_copy_t(const CopyParams &P, cudaStream_t s) {
+    copy_kernel<T><<<grid_for(P.total, 256), 256, 0, s>>>(P);
+    return check_launch("copy_kernel");
+}
+
+template <typename T>
+inline int launch_tile_t(const TileParams &P, cudaStream_t s) {
+    tile_kernel<T><<<grid_for(P.total, 256), 256, 0, s>>>(P);
+    return check_launch("tile_kernel");
+}
+
+// Launch one record. `kernels`, if not NULL, is incremented by the number of kernel launches.
+inline int launch_record(const mgc_cuda_launch &L, const int64_t *aux, int64_t aux_len,
+                         const Bases &bases, int *status_dev, cudaStream_t stream, int *kernels) {
+    const int64_t *i = L.i;
+    int launched = 1;
+    int st = MGC_CUDA_OK;
+    switch (L.kind) {
+    case MGC_K_GEMM: {
+        GemmParams p;
+        MGC_CHECK(decode_gemm(L, bases, p));
+        st = run_gemm(p, stream);
+        break;
+    }
+    case MGC_K_DEPTHWISE: {
+        DepthwiseParams p{};
+        p.N = (int)i[0]; p.H = (int)i[1]; p.W = (int)i[2]; p.C = (int)i[3]; p.KH = (int)i[4];
+        p.KW = (int)i[5]; p.SH = (int)i[6]; p.SW = (int)i[7]; p.DH = (int)i[8]; p.DW = (int)i[9];
+        p.PT = (int)i[10]; p.PL = (int)i[11]; p.OH = (int)i[12]; p.OW = (int)i[13];
+        p.nhwc = (int)i[14]; p.act = (int)i[15];
+        p.lo = (float)L.f[0]; p.hi = (float)L.f[1];
+        MGC_RESOLVE(L.r[0], p.x); MGC_RESOLVE(L.r[1], p.w); MGC_RESOLVE(L.r[2], p.bias);
+        MGC_RESOLVE(L.r[3], p.res); MGC_RESOLVE(L.r[4], p.y);
+        const long long total = (long long)p.N * p.OH * p.OW * p.C;
+        if (total == 0) { launched = 0; break; }
+        const bool vec4 = p.nhwc && p.C % 4 == 0 &&
+                          ((((uintptr_t)p.x) | ((uintptr_t)p.w) | ((uintptr_t)p.y) |
+                            ((uintptr_t)p.bias) | ((uintptr_t)p.res)) % 16 == 0);
+        if (vec4) depthwise_nhwc4_kernel<<<grid_for(total / 4, 256), 256, 0, stream>>>(p);
+        else depthwise_kernel<<<grid_for(total, 256), 256, 0, stream>>>(p);
+        st = check_launch("depthwise_kernel");
+        break;
+    }
+    case MGC_K_POOL: {
+        PoolParams p{};
+        p.is_max = (int)i[0]; p.N = (int)i[1]; p.H = (int)i[2]; p.W = (int)i[3]; p.C = (int)i[4];
+        p.KH = (int)i[5]; p.KW = (int)i[6]; p.SH = (int)i[7]; p.SW = (int)i[8]; p.DH = (int)i[9];
+        p.DW = (int)i[10]; p.PT = (int)i[11]; p.PL = (int)i[12]; p.PB = (int)i[13]; p.PR = (int)i[14];
+        p.OH = (int)i[15]; p.OW = (int)i[16]; p.include_pad = (int)i[17]; p.nhwc = (int)i[18];
+        MGC_RESOLVE(L.r[0], p.x); MGC_RESOLVE(L.r[1], p.y);
+        const long long total = (long long)p.N * p.OH * p.OW * p.C;
+        if (total == 0) { launched = 0; break; }
+        pool_kernel<<<grid_for(total, 256), 256, 0, stream>>>(p);
+        st = check_launch("pool_kernel");
+        break;
+    }
+    case MGC_K_REDUCE_MID: {
+        const float *x; float *y;
+        MGC_RESOLVE(L.r[0], x); MGC_RESOLVE(L.r[1], y);
+        const long long total = i[1] * i[3];
+        if (total == 0) { launched = 0; break; }
+        reduce_mid_kernel<<<grid_for(total, 256), 256, 0, stream>>>((int)i[0], i[1], i[2], i[3], x, y);
+        st = check_launch("reduce_mid_kernel");
+        break;
+    }
+    case MGC_K_SOFTMAX: {
+        const float *x; float *y;
+        MGC_RESOLVE(L.r[0], x); MGC_RESOLVE(L.r[1], y);
+        const long long rows = i[0] * i[2];
+        if (rows == 0 || i[1] == 0) { launched = 0; break; }
+        softmax_kernel<<<grid_for(rows, 8), 256, 0, stream>>>(i[0], i[1], i[2], x, y, (int)i[3]);
+        st = check_launch("softmax_kernel");
+        break;
+    }
+    case MGC_K_LAYER_NORM: {
+        const float *x, *g, *b; float *y;
+        MGC_RESOLVE(L.r[0], x); MGC_RESOLVE(L.r[1], g); MGC_RESOLVE(L.r[2], b); MGC_RESOLVE(L.r[3], y);
+        if (i[0] == 0 || i[1] == 0) { launched = 0; break; }
+        layer_norm_kernel<<<grid_for(i[0], 8), 256, 0, stream>>>(i[0], i[1], x, g, b, (float)L.f[0], y);
+        st = check_launch("layer_norm_kernel");
+        break;
+    }
+    case MGC_K_ELEMENTWISE: {
+        EwParams P;
+        MGC_CHECK(decode_elementwise(L, aux, aux_len, bases, P));
+        if (P.total == 0) { launched = 0; break; }
+        ew_kernel<<<grid_for(P.total, 256), 256, 0, stream>>>(P);
+        st = check_launch("ew_kernel");
+        break;
+    }
+    case MGC_K_COPY: {
+        const int rank = (int)i[0], esize = (int)i[1];
+        if (rank < 0 || rank > COPY_MAX_RANK) return fail(MGC_CUDA_UNSUPPORTED, "copy: rank %d", rank);
+        const char *src; char *dst;
+        MGC_RESOLVE(L.r[0], src); MGC_RESOLVE(L.r[1], dst);
+        long long total = 1;
+        for (int d = 0; d < rank; ++d) total *= i[2 + d];
+        if (total == 0) { launched = 0; break; }
+        if (i[28] == 1) {  // Tile
+            TileParams P{};
+            P.rank = rank; P.esize = esize; P.total = total; P.src = src; P.dst = dst;
+            for (int d = 0; d < rank; ++d) { P.oshape[d] = i[2 + d]; P.xshape[d] = i[10 + d]; P.xstr[d] = i[19 + d]; }
+            switch (esize) {
+            case 1: st = launch_tile_t<uint8_t>(P, stream); break;
+            case 2: st = launch_tile_t<uint16_t>(P, stream); break;
+            case 4: st = launch_tile_t<uint32_t>(P, stream); break;
+            case 8: st = launch_tile_t<uint64_t>(P, stream); break;
+            default: return fail(MGC_CUDA_UNSUPPORTED, "copy: element size %d", esize);
+            }
+            break;
+        }
+        CopyParams P{};
+        P.rank = rank; P.esize = esize; P.total = total; P.src = src; P.dst = dst;
+        for (int d = 0; d < rank; ++d) { P.shape[d] = i[2 + d]; P.sstr[d] = i[10 + d]; P.dstr[d] = i[19 + d]; }
+        P.sbase = i[18]; P.dbase = i[27];
+        switch (esize) {
+        case 1: st = launch_copy_t<uint8_t>(P, stream); break;
+        case 2: st = launch_copy_t<uint16_t>(P, stream); break;
+        case 4: st = launch_copy_t<uint32_t>(P, stream); break;
+        case 8: st = launch_copy_t<uint64_t>(P, stream); break;
+        default: return fail(MGC_CUDA_UNSUPPORTED, "copy: element size %d", esize);
+        }
+        break;
+    }
+    case MGC_K_FILL: {
+        char *dst;
+        MGC_RESOLVE(L.r[0], dst);
+        const long long n = i[0];
+        const int esize = (int)i[1];
+        const int64_t bits = i[2];
+        if (n == 0) { launched = 0; break; }
+        const unsigned g = grid_for(n, 256);
+        switch (esize) {
+        case 1: fill_kernel<uint8_t><<<g, 256, 0, stream>>>((uint8_t *)dst, n, (uint8_t)bits); break;
+        case 2: fill_kernel<uint16_t><<<g, 256, 0, stream>>>((uint16_t *)dst, n, (uint16_t)bits); break;
+        case 4: fill_kernel<uint32_t><<<g, 256, 0, stream>>>((uint32_t *)dst, n, (uint32_t)bits); break;
+        case 8: fill_kernel<uint64_t><<<g, 256, 0, stream>>>((uint64_t *)dst, n, (uint64_t)bits); break;
+        default: return fail(MGC_CUDA_UNSUPPORTED, "fill: element size %d", esize);
+        }
+        st = check_launch("fill_kernel");
+        break;
+    }
+    case MGC_K_GATHER: {
+        const char *x; const void *idx; char *out;
+        MGC_RESOLVE(L.r[0], x); MGC_RESOLVE(L.r[1], idx); MGC_RESOLVE(L.r[2], out);
+        const long long outer = i[0], dim = i[1], inner = i[2], n = i[3];
+        const int idt = (int)i[4], esize = (int)i[5];
+        const long long total = outer * n * inner;
+        if (total == 0) { launched = 0; break; }
+        const unsigned g = grid_for(total, 256);
+        switch (esize) {
+        case 1: gather_kernel<uint8_t><<<g, 256, 0, stream>>>((const uint8_t *)x, idx, idt, (uint8_t *)out, outer, dim, inner, n, status_dev); break;
+        case 4: gather_kernel<uint32_t><<<g, 256, 0, stream>>>((const uint32_t *)x, idx, idt, (uint32_t *)out, outer, dim, inner, n, status_dev); break;
+        case 8: gather_kernel<uint64_t><<<g, 256, 0, stream>>>((const uint64_t *)x, idx, idt, (uint64_t *)out, outer, dim, inner, n, status_dev); break;
+        default: return fail(MGC_CUDA_UNSUPPORTED, "gather: element size %d", esize);
+        }
+        st = check_launch("gather_kernel");
+        break;
+    }
+    case MGC_K_REDUCE: {
+        const void *x; void *y;
+        MGC_RESOLVE(L.r[0], x); MGC_RESOLVE(L.r[1], y);
+        const long long total = i[1] * i[3];
+        if (total == 0) { launched = 0; break; }
+        reduce_kernel<<<grid_for(total, 256), 256, 0, stream>>>((int)i[0], L.dtype, i[1], i[2], i[3], x, y);
+        st = check_launch("reduce_kernel");
+        break;
+    }
+    case MGC_K_ARGMAX: {
+        const void *x; long long *y;
+        MGC_RESOLVE(L.r[0], x); MGC_RESOLVE(L.r[1], y);
+        const long long total = i[0] * i[2];
+        if (total == 0) { launched = 0; break; }
+        argmax_kernel<<<grid_for(total, 256), 256, 0, stream>>>(L.dtype, i[0], i[1], i[2], x, y);
+        st = check_launch("argmax_kernel");
+        break;
+    }
+    case MGC_K_RANGE: {
+        void *y; const void *s0; const void *dl;
+        MGC_RESOLVE(L.r[0], y); MGC_RESOLVE(L.r[1], s0); MGC_RESOLVE(L.r[2], dl);
+        if (i[0] == 0) { launched = 0; break; }
+        range_kernel<<<grid_for(i[0], 256), 256, 0, stream>>>(y, L.dtype, i[0], s0, dl);
+        st = check_launch("range_kernel");
+        break;
+    }
+    case MGC_K_MEMCPY: {
+        const void *src; void *dst;
+        MGC_RESOLVE(L.r[0], src); MGC_RESOLVE(L.r[1], dst);
+        launched = 0;
+        if (i[0] > 0) MGC_CHECK_CUDA(cudaMemcpyAsync(dst, src, (size_t)i[0], cudaMemcpyDeviceToDevice, stream));
+        break;
+    }
+    default:
+        return fail(MGC_CUDA_UNSUPPORTED, "unknown launch kind %d (node %d)", L.kind, L.node);
+    }
+    if (st != MGC_CUDA_OK) return st;
+    if (kernels) *kernels += launched;
+    return MGC_CUDA_OK;
+}
+
+}  // namespace mgc

@@ -1,0 +1,994 @@
+"""Lowering of a scheduled, memory-planned graph to a CUDA launch list.
+
+This is the `cuda` target's counterpart of the reference's C emitter (``codegen/c.py``): it walks
+``graph.nodes`` in scheduled order, asks the reference planner (``memory.plan_memory``) where
+every value lives exactly as ``CEmitter.ptr`` does (``c.py:323-335``), and produces
+
+* one ``mgc_cuda_launch`` record (``include/mgc_cuda.h``) per kernel launch, whose tensor
+  references are (space, index, byte offset) triples: arena offsets from the plan, offsets into
+  the constant blob built here, or graph input / output numbers;
+* an ``aux`` int64 array with the variable-length data of elementwise programs;
+* the constant blob: every constant the kernels read, in the layout the kernels want (GEMM
+  right-hand sides K-major and split into a TF32-exact high part and an fp32 residual).
+
+Views (``memory.ALIAS_OPS``) emit nothing; output copies come from ``plan.copies``; an operator
+without a lowering raises ``CodegenError`` (there is no CPU fallback). The slot layout of each
+launch kind is written at its ``_emit_*`` function and read by ``csrc/launch.cuh``.
+"""
+
+from __future__ import annotations
+
+import ctypes
+import hashlib
+import struct
+from collections.abc import Sequence
+from dataclasses import dataclass, field
+from typing import Any
+
+import numpy as np
+
+from mgc_cuda import _reference  # noqa: F401
+from ml_graph_compiler import ops
+from ml_graph_compiler.codegen.c import CEmitter
+from ml_graph_compiler.errors import CodegenError
+from ml_graph_compiler.ir import Graph, Node, TensorType, Value
+from ml_graph_compiler.memory import ALIAS_OPS, MemoryPlan, Strategy, plan_memory
+
+# ---- constants mirrored from include/mgc_cuda.h ------------------------------------------------
+SPACE_NONE, SPACE_ARENA, SPACE_WEIGHTS, SPACE_INPUT, SPACE_OUTPUT, SPACE_RAW = range(6)
+DTYPES = {"float32": 0, "float64": 1, "int64": 2, "int32": 3, "int8": 4, "uint8": 5, "bool": 6}
+ACTS = {"none": 0, "relu": 1, "clip": 2, "gelu": 3, "gelu_tanh": 4, "tanh": 5, "sigmoid": 6}
+STRIDED, CONV_NHWC, CONV_NCHW = 0, 2, 3
+PRECISIONS = {"fp32": 0, "tf32": 1, "strict": 2}
+K_GEMM, K_DEPTHWISE, K_POOL, K_REDUCE_MID, K_SOFTMAX, K_LAYER_NORM = 1, 2, 3, 4, 5, 6
+K_ELEMENTWISE, K_COPY, K_FILL, K_GATHER, K_REDUCE, K_ARGMAX, K_RANGE, K_MEMCPY = range(7, 15)
+KIND_NAMES = {
+    K_GEMM: "gemm", K_DEPTHWISE: "depthwise", K_POOL: "pool", K_REDUCE_MID: "reduce",
+    K_SOFTMAX: "softmax", K_LAYER_NORM: "layer_norm", K_ELEMENTWISE: "elementwise",
+    K_COPY: "copy", K_FILL: "fill", K_GATHER: "gather", K_REDUCE: "reduce", K_ARGMAX: "argmax",
+    K_RANGE: "range", K_MEMCPY: "memcpy",
+}
+LAUNCH_INTS, LAUNCH_FLOATS, LAUNCH_REFS = 64, 8, 8
+# Elementwise program operations, numbered as csrc/kernels_mem.cuh EwOp.
+EW_OPS = [
+    "Add", "Sub", "Mul", "Div", "Pow", "Max", "Min",
+    "Equal", "Less", "Greater", "LessOrEqual", "GreaterOrEqual", "And", "Or", "Xor",
+    "Where", "Relu", "Sigmoid", "Tanh", "Erf", "Sqrt", "Exp", "Log",
+    "Neg", "Abs", "Reciprocal", "Floor", "Ceil", "Sin", "Cos", "Softplus",
+    "Identity", "Not", "Gelu", "LeakyRelu", "HardSigmoid", "Clip", "Cast",
+]
+EW_CODE = {name: i for i, name in enumerate(EW_OPS)}
+EW_MAX_RANK, EW_MAX_LEAVES, EW_MAX_INSTR, COPY_MAX_RANK = 6, 20, 40, 8
+BLOB_ALIGN = 256
+TF32_MASK = np.uint32(0xFFFFE000)
+
+
+class Ref(ctypes.Structure):
+    _fields_ = [("space", ctypes.c_int32), ("index", ctypes.c_int32), ("offset", ctypes.c_int64)]
+
+
+class Launch(ctypes.Structure):
+    _fields_ = [
+        ("kind", ctypes.c_int32),
+        ("node", ctypes.c_int32),
+        ("dtype", ctypes.c_int32),
+        ("flags", ctypes.c_int32),
+        ("i", ctypes.c_int64 * LAUNCH_INTS),
+        ("f", ctypes.c_double * LAUNCH_FLOATS),
+        ("r", Ref * LAUNCH_REFS),
+        ("aux_offset", ctypes.c_int64),
+        ("aux_len", ctypes.c_int64),
+    ]
+
+
+assert ctypes.sizeof(Launch) == 16 + 8 * LAUNCH_INTS + 8 * LAUNCH_FLOATS + 16 * LAUNCH_REFS + 16
+
+RefT = tuple[int, int, int]
+NO_REF: RefT = (SPACE_NONE, 0, 0)
+
+
+def tf32_split(a: np.ndarray) -> tuple[np.ndarray, np.ndarray]:
+    """(hi, lo) with hi = a rounded to the nearest TF32 value (10 mantissa bits, ties away from
+    zero) and lo = a - hi, exact in fp32; hi + lo == a bit for bit."""
+    a = np.ascontiguousarray(a, np.float32)
+    bits = a.view(np.uint32)
+    hi = ((bits + np.uint32(0x1000)) & TF32_MASK).view(np.float32)
+    finite = np.isfinite(a) & np.isfinite(hi)
+    hi = np.where(finite, hi, a).astype(np.float32)
+    lo = np.where(finite, a - hi, np.float32(0)).astype(np.float32)
+    return hi, lo
+
+
+@dataclass
+class Blob:
+    """Constants in one device blob with 256-byte aligned chunks (TMA needs 16, we keep lines)."""
+
+    chunks: list[tuple[int, np.ndarray]] = field(default_factory=list)
+    size: int = 0
+    by_key: dict[Any, int] = field(default_factory=dict)
+
+    def add(self, array: np.ndarray, key: Any = None) -> int:
+        if key is not None and key in self.by_key:
+            return self.by_key[key]
+        data = np.ascontiguousarray(array)
+        offset = self.size
+        self.chunks.append((offset, data))
+        self.size += data.nbytes
+        self.size += (-self.size) % BLOB_ALIGN
+        if key is not None:
+            self.by_key[key] = offset
+        return offset
+
+    @property
+    def nbytes(self) -> int:
+        return max(self.size, BLOB_ALIGN)
+
+    def tobytes_array(self) -> np.ndarray:
+        out = np.zeros(self.nbytes, np.uint8)
+        for offset, data in self.chunks:
+            out[offset : offset + data.nbytes] = data.reshape(-1).view(np.uint8)
+        return out
+
+    def digest(self) -> str:
+        h = hashlib.blake2b(digest_size=12)
+        for offset, data in self.chunks:
+            h.update(offset.to_bytes(8, "little"))
+            h.update(memoryview(data.reshape(-1).view(np.uint8)))
+        return h.hexdigest()
+
+
+@dataclass
+class LoweredModel:
+    launches: list[Launch]
+    aux: np.ndarray
+    weights: Blob
+    arena_bytes: int
+    inputs: list[tuple[str, TensorType]]
+    outputs: list[tuple[str, TensorType]]
+    plan: MemoryPlan
+    kernels: dict[str, int]
+    node_names: list[tuple[str, str]]
+    precision: str
+
+    def launch_array(self) -> ctypes.Array:
+        arr = (Launch * max(len(self.launches), 1))()
+        for k, rec in enumerate(self.launches):
+            arr[k] = rec
+        return arr
+
+
+def _strides(shape: Sequence[int]) -> list[int]:
+    out = [1] * len(shape)
+    for i in range(len(shape) - 2, -1, -1):
+        out[i] = out[i + 1] * int(shape[i + 1])
+    return out
+
+
+def _broadcast_strides(shape: Sequence[int], out_shape: Sequence[int]) -> list[int]:
+    """Element strides of ``shape`` broadcast right-aligned to ``out_shape`` (0 on broadcast)."""
+    src = _strides(shape)
+    pad = len(out_shape) - len(shape)
+    return [0 if d - pad < 0 or shape[d - pad] == 1 else src[d - pad] for d in range(len(out_shape))]
+
+
+def _collapse(dims: list[int], strides: list[list[int]]) -> tuple[list[int], list[list[int]]]:
+    """Drop size-1 dimensions and merge neighbours that are contiguous for every operand (the
+    collapsing of ``CEmitter.loops``, c.py:360-379)."""
+    keep = [i for i, d in enumerate(dims) if d != 1]
+    dims = [dims[i] for i in keep]
+    strides = [[s[i] for i in keep] for s in strides]
+    d = len(dims) - 1
+    while d > 0:
+        if all(s[d - 1] == s[d] * dims[d] for s in strides):
+            dims[d - 1] *= dims[d]
+            del dims[d]
+            for s in strides:
+                s[d - 1] = s[d]
+                del s[d]
+        d -= 1
+    return dims, strides
+
+
+def _bits(value: float) -> int:
+    return struct.unpack("<q", struct.pack("<d", float(value)))[0]
+
+
+class CudaEmitter:
+    """Builds the launch list for one scheduled graph (see the module docstring)."""
+
+    SUPPORTED = CEmitter.SUPPORTED
+
+    def __init__(
+        self,
+        graph: Graph,
+        strategy: Strategy = "greedy_by_size",
+        inplace: bool = True,
+        precision: str = "tf32",
+    ) -> None:
+        unsupported = sorted({n.op for n in graph.nodes} - self.SUPPORTED)
+        if unsupported:
+            raise CodegenError(f"the cuda backend has no kernel for: {', '.join(unsupported)}")
+        for v in graph.values():
+            if v.type is not None and v.type.dtype == "float16":
+                raise CodegenError(f"float16 tensors are not supported ({v.name})")
+        if precision not in PRECISIONS:
+            raise CodegenError(f"precision must be one of {sorted(PRECISIONS)}, got {precision!r}")
+        self.graph = graph
+        self.precision = precision
+        self.plan = plan_memory(graph, strategy=strategy, inplace=inplace)
+        self.weights = Blob()
+        self.launches: list[Launch] = []
+        self.aux: list[int] = []
+        self.kernels: dict[str, int] = {}
+        self._node = -1
+        self._keep_alive: list[Value] = []
+
+    # -- references ----------------------------------------------------------------------------
+    def _root(self, value: Value) -> Value:
+        while value.data is None and value.producer is not None and value.producer.op in ALIAS_OPS:
+            value = value.producer.input(0)
+        return value
+
+    def const_data(self, value: Value) -> np.ndarray:
+        root = self._root(value)
+        if root.data is None:
+            raise CodegenError(f"constant {value.name!r} has no data")
+        return root.data.reshape(value.tensor_type.shape)
+
+    def ref(self, value: Value | None, byte_offset: int = 0) -> RefT:
+        if value is None:
+            return NO_REF
+        loc = self.plan.location(value)
+        if loc.kind == "const":
+            root = self._root(value)
+            if root.data is None:
+                raise CodegenError(f"constant {value.name!r} has no data")
+            off = self.weights.add(root.data, key=("raw", id(root)))
+            return (SPACE_WEIGHTS, 0, off + byte_offset)
+        if loc.kind == "input":
+            return (SPACE_INPUT, loc.index, byte_offset)
+        if loc.kind == "output":
+            return (SPACE_OUTPUT, loc.index, byte_offset)
+        return (SPACE_ARENA, 0, loc.index + byte_offset)
+
+    def weights_ref(self, array: np.ndarray, key: Any = None) -> RefT:
+        return (SPACE_WEIGHTS, 0, self.weights.add(array, key=key))
+
+    # -- records -----------------------------------------------------------------------------------
+    def emit(
+        self,
+        kind: int,
+        ints: Sequence[int] = (),
+        floats: Sequence[float] = (),
+        refs: Sequence[RefT] = (),
+        dtype: int = 0,
+        aux: Sequence[int] | None = None,
+        count: str | None = None,
+    ) -> None:
+        if len(ints) > LAUNCH_INTS or len(floats) > LAUNCH_FLOATS or len(refs) > LAUNCH_REFS:
+            raise CodegenError("launch record overflow")
+        rec = Launch()
+        rec.kind = kind
+        rec.node = self._node
+        rec.dtype = dtype
+        for k, v in enumerate(ints):
+            rec.i[k] = int(v)
+        for k, v in enumerate(floats):
+            rec.f[k] = float(v)
+        for k, (space, index, offset) in enumerate(refs):
+            rec.r[k].space, rec.r[k].index, rec.r[k].offset = space, index, offset
+        if aux is not None:
+            rec.aux_offset = len(self.aux)
+            rec.aux_len = len(aux)
+            self.aux.extend(int(v) for v in aux)
+        self.launches.append(rec)
+        name = count or KIND_NAMES[kind]
+        self.kernels[name] = self.kernels.get(name, 0) + 1
+
+    # -- dispatch ------------------------------------------------------------------------------------
+    def node(self, node: Node) -> None:
+        if node.op in ALIAS_OPS:
+            if node.op == "Dropout" and len(node.outputs) > 1:
+                mask = node.outputs[1]
+                self._fill(mask, 1)
+            self.kernels["view"] = self.kernels.get("view", 0) + 1
+            return
+        if node.op == "FusedElementwise":
+            program = [(str(op), dict(a), [int(x) for x in args]) for op, a, args in node.attrs["program"]]
+            self._elementwise(node.output, program, list(node.inputs))
+            return
+        if ops.is_elementwise(node.op):
+            args = [i if node.inputs[i] is not None else -1 for i in range(len(node.inputs))]
+            self._elementwise(node.output, [(node.op, dict(node.attrs), args)], list(node.inputs))
+            return
+        handler = getattr(self, f"op_{node.op}", None)
+        if handler is None:
+            raise CodegenError(f"the cuda backend has no kernel for {node.op}")
+        handler(node)
+
+    # -- elementwise programs (c.py:471-529) -------------------------------------------------------
+    def _elementwise(
+        self, out_value: Value, program: list[tuple[str, dict[str, Any], list[int]]], leaves: list[Value | None]
+    ) -> None:
+        shape = list(out_value.tensor_type.shape)
+        if int(np.prod(shape)) == 0:
+            return
+        tensor_leaves = [
+            i for i, v in enumerate(leaves)
+            if v is not None and not (v.is_constant and v.data is not None and v.data.size == 1)
+        ]
+        all_strides = [_strides(shape)] + [
+            _broadcast_strides(leaves[i].tensor_type.shape, shape) for i in tensor_leaves  # type: ignore[union-attr]
+        ]
+        dims, coll = _collapse(list(shape), all_strides)
+        if len(dims) > EW_MAX_RANK:
+            raise CodegenError(f"elementwise loop nest of rank {len(dims)} (max {EW_MAX_RANK})")
+        present = [v for v in leaves if v is not None]
+        if len(leaves) > EW_MAX_LEAVES or len(program) > EW_MAX_INSTR:
+            raise CodegenError(f"elementwise program too large ({len(present)} leaves, {len(program)} ops)")
+        aux: list[int] = [len(dims), *dims]
+        aux += [DTYPES[out_value.tensor_type.dtype], *self.ref(out_value)]
+        aux.append(len(leaves))
+        types_all: list[TensorType | None] = []
+        consts: list[np.ndarray | None] = []
+        for i, v in enumerate(leaves):
+            if v is None:  # omitted optional input: never read
+                aux += [DTYPES["float32"], 1, 0, *NO_REF, *([0] * len(dims))]
+                types_all.append(None)
+                consts.append(None)
+                continue
+            t = v.tensor_type
+            types_all.append(t)
+            consts.append(v.data)
+            if i in tensor_leaves:
+                strides = coll[1 + tensor_leaves.index(i)]
+                aux += [DTYPES[t.dtype], 0, 0, *self.ref(v), *strides]
+            else:
+                scalar = self.const_data(v).reshape(()).item()
+                bits = _bits(scalar) if t.dtype in ("float32", "float64") else int(scalar)
+                aux += [DTYPES[t.dtype], 1, bits, *NO_REF, *([0] * len(dims))]
+        aux.append(len(program))
+        for op, attrs, args in program:
+            if op not in EW_CODE:
+                raise CodegenError(f"elementwise {op} has no cuda kernel")
+            sub = Node(op, [], [Value("_")], dict(attrs))
+            arg_types = [types_all[a] if a >= 0 else None for a in args]
+            out_t = ops.spec(op).infer(sub, arg_types, [consts[a] if a >= 0 else None for a in args])[0]
+            if out_t.dtype == "float16":
+                raise CodegenError("float16 is not supported")
+            types_all.append(out_t)
+            consts.append(None)
+            a = list(args) + [-1] * (3 - len(args))
+            imm = [0.0, 0.0]
+            if op == "Clip":
+                imm = [float(attrs.get("min", -np.inf)), float(attrs.get("max", np.inf))]
+            elif op == "Gelu":
+                imm = [1.0 if attrs.get("approximate", "none") == "tanh" else 0.0, 0.0]
+            elif op == "LeakyRelu":
+                imm = [float(attrs.get("alpha", 0.01)), 0.0]
+            elif op == "HardSigmoid":
+                imm = [float(attrs.get("alpha", 0.2)), float(attrs.get("beta", 0.5))]
+            aux += [EW_CODE[op], DTYPES[out_t.dtype], a[0], a[1], a[2], _bits(imm[0]), _bits(imm[1])]
+        self.emit(K_ELEMENTWISE, aux=aux, dtype=DTYPES[out_value.tensor_type.dtype], count="elementwise")
+
+    # -- copies (c.py:558-660) --------------------------------------------------------------------
+    def _copy(
+        self,
+        shape: Sequence[int],
+        src: RefT,
+        src_strides: Sequence[int],
+        src_base: int,
+        dst: RefT,
+        dst_strides: Sequence[int],
+        dst_base: int,
+        esize: int,
+        count: str = "copy",
+    ) -> None:
+        """K_COPY slots: i[0] rank, i[1] element bytes, i[2..9] shape, i[10..17] source strides,
+        i[18] source base, i[19..26] destination strides, i[27] destination base (elements),
+        i[28] 0 (1 selects Tile); r[0] source, r[1] destination."""
+        if int(np.prod([int(d) for d in shape])) == 0:
+            return
+        dims, (ss, ds) = _collapse([int(d) for d in shape], [list(src_strides), list(dst_strides)])
+        if len(dims) > COPY_MAX_RANK:
+            raise CodegenError(f"copy of rank {len(dims)} (max {COPY_MAX_RANK})")
+        ints = [0] * 29
+        ints[0], ints[1] = len(dims), esize
+        for d in range(len(dims)):
+            ints[2 + d], ints[10 + d], ints[19 + d] = dims[d], ss[d], ds[d]
+        ints[18], ints[27] = src_base, dst_base
+        self.emit(K_COPY, ints, refs=[src, dst], count=count)
+
+    def _copy_value(self, out_shape: Sequence[int], src: Value, dst_ref: RefT, dst_strides: Sequence[int],
+                    dst_base: int, count: str = "copy") -> None:
+        t = src.tensor_type
+        if src.is_constant and src.data is not None and src.data.size == 1:
+            # broadcast a scalar constant: a fill of the destination region
+            if list(dst_strides) == _strides(out_shape) and dst_base == 0:
+                self._fill_ref(dst_ref, int(np.prod(out_shape)), src.data.reshape(()).item(), t.dtype)
+                return
+        self._copy(out_shape, self.ref(src), _broadcast_strides(t.shape, out_shape), 0, dst_ref,
+                   dst_strides, dst_base, t.itemsize, count)
+
+    def op_Transpose(self, node: Node) -> None:
+        x = node.input(0)
+        perm = ops.transpose_perm(node, x.tensor_type.rank)
+        ss = _strides(x.tensor_type.shape)
+        shape = node.output.tensor_type.shape
+        self._copy(shape, self.ref(x), [ss[p] for p in perm], 0, self.ref(node.output), _strides(shape), 0,
+                   x.tensor_type.itemsize, count="transpose")
+
+    def op_Expand(self, node: Node) -> None:
+        shape = node.output.tensor_type.shape
+        self._copy_value(shape, node.input(0), self.ref(node.output), _strides(shape), 0)
+
+    def op_Tile(self, node: Node) -> None:
+        x = node.input(0)
+        xs, os_ = x.tensor_type.shape, node.output.tensor_type.shape
+        if len(os_) > COPY_MAX_RANK:
+            raise CodegenError(f"Tile of rank {len(os_)}")
+        if int(np.prod(os_)) == 0:
+            return
+        ints = [0] * 29
+        ints[0], ints[1], ints[28] = len(os_), x.tensor_type.itemsize, 1
+        xst = _strides(xs)
+        for d in range(len(os_)):
+            ints[2 + d], ints[10 + d], ints[19 + d] = os_[d], xs[d], xst[d]
+        self.emit(K_COPY, ints, refs=[self.ref(x), self.ref(node.output)], count="copy")
+
+    def _consts(self, node: Node) -> list[np.ndarray | None]:
+        return [v.data if v is not None else None for v in node.inputs]
+
+    def op_Slice(self, node: Node) -> None:
+        x = node.input(0)
+        xs = x.tensor_type.shape
+        slices = ops.slice_params(node, xs, self._consts(node))
+        ss = _strides(xs)
+        base = 0
+        strides = []
+        for sl, st in zip(slices, ss, strict=True):
+            base += int(sl.start or 0) * st
+            strides.append(int(sl.step or 1) * st)
+        shape = node.output.tensor_type.shape
+        self._copy(shape, self.ref(x), strides, base, self.ref(node.output), _strides(shape), 0,
+                   x.tensor_type.itemsize)
+
+    def op_Concat(self, node: Node) -> None:
+        out_t = node.output.tensor_type
+        axis = int(node.attrs.get("axis", 0))
+        axis = axis + out_t.rank if axis < 0 else axis
+        ost = _strides(out_t.shape)
+        offset = 0
+        for v in node.inputs:
+            if v is None:
+                continue
+            t = v.tensor_type
+            if t.size:
+                self._copy_value(t.shape, v, self.ref(node.output), ost, offset * ost[axis])
+            offset += t.shape[axis]
+
+    def op_Split(self, node: Node) -> None:
+        x = node.input(0)
+        xt = x.tensor_type
+        axis = int(node.attrs.get("axis", 0))
+        axis = axis + xt.rank if axis < 0 else axis
+        ss = _strides(xt.shape)
+        offset = 0
+        for out_v in node.outputs:
+            t = out_v.tensor_type
+            if out_v.users or out_v in self.graph.outputs:
+                self._copy(t.shape, self.ref(x), ss, offset * ss[axis], self.ref(out_v), _strides(t.shape), 0,
+                           xt.itemsize)
+            offset += t.shape[axis]
+
+    def op_Pad(self, node: Node) -> None:
+        if node.attrs.get("mode", "constant") != "constant":
+            raise CodegenError(f"Pad mode {node.attrs.get('mode')!r} has no cuda kernel")
+        x = node.input(0)
+        xt, ot = x.tensor_type, node.output.tensor_type
+        pads = ops.pad_amounts(node, xt.rank, self._consts(node))
+        if any(p < 0 for p in pads):
+            raise CodegenError("negative Pad amounts have no cuda kernel")
+        fill = 0.0
+        value_v = node.optional_input(2)
+        if value_v is not None:
+            if value_v.data is None:
+                raise CodegenError("Pad value must be a constant")
+            fill = value_v.data.reshape(()).item()
+        self._fill(node.output, fill)
+        ost = _strides(ot.shape)
+        base = sum(p * s for p, s in zip(pads[: xt.rank], ost, strict=True))
+        if xt.size:
+            self._copy_value(xt.shape, x, self.ref(node.output), ost, base)
+
+    # -- constants (c.py:690-734) -------------------------------------------------------------------
+    def _fill_ref(self, dst: RefT, count: int, value: Any, dtype: str) -> None:
+        """K_FILL slots: i[0] element count, i[1] element bytes, i[2] raw value bits; r[0] dst."""
+        if count == 0:
+            return
+        arr = np.asarray(value, dtype=np.dtype(dtype if dtype != "bool" else np.bool_))
+        raw = int.from_bytes(arr.tobytes(), "little", signed=False)
+        if raw >= 1 << 63:
+            raw -= 1 << 64
+        self.emit(K_FILL, [count, arr.itemsize, raw], refs=[dst], count="constant")
+
+    def _fill(self, value: Value, fill: Any) -> None:
+        t = value.tensor_type
+        self._fill_ref(self.ref(value), t.size, fill, t.dtype)
+
+    def _write_constant(self, value: Value, array: np.ndarray) -> None:
+        t = value.tensor_type
+        flat = np.asarray(array, dtype=np.dtype(t.dtype if t.dtype != "bool" else np.bool_)).reshape(-1)
+        if flat.size and np.all(flat == flat[0]):
+            self._fill_ref(self.ref(value), t.size, flat[0].item(), t.dtype)
+            return
+        src = self.weights_ref(flat)
+        self.emit(K_MEMCPY, [t.nbytes], refs=[src, self.ref(value)], count="constant")
+
+    def op_Shape(self, node: Node) -> None:
+        self._write_constant(node.output, ops.shape_value(node, node.input(0).tensor_type.shape))
+
+    def op_Size(self, node: Node) -> None:
+        self._write_constant(node.output, np.asarray([node.input(0).tensor_type.size], np.int64))
+
+    def op_ConstantOfShape(self, node: Node) -> None:
+        value = node.attrs.get("value")
+        fill = np.asarray(value).reshape(-1)[0].item() if value is not None else 0.0
+        self._fill(node.output, fill)
+
+    def op_Range(self, node: Node) -> None:
+        """K_RANGE slots: i[0] count; dtype; r[0] out, r[1] start scalar, r[2] delta scalar."""
+        t = node.output.tensor_type
+        self.emit(K_RANGE, [t.size], refs=[self.ref(node.output), self.ref(node.input(0)), self.ref(node.input(2))],
+                  dtype=DTYPES[t.dtype], count="constant")
+
+    # -- gather (c.py:662-688) -----------------------------------------------------------------------
+    def op_Gather(self, node: Node) -> None:
+        """K_GATHER slots: i[0] outer, i[1] axis extent, i[2] inner, i[3] index count, i[4] index
+        dtype, i[5] element bytes; r[0] data, r[1] indices, r[2] out."""
+        x, idx = node.input(0), node.input(1)
+        xt, it = x.tensor_type, idx.tensor_type
+        axis = int(node.attrs.get("axis", 0))
+        axis = axis + xt.rank if axis < 0 else axis
+        outer = int(np.prod(xt.shape[:axis])) if axis else 1
+        inner = int(np.prod(xt.shape[axis + 1 :])) if axis + 1 < xt.rank else 1
+        if it.dtype not in ("int64", "int32"):
+            raise CodegenError(f"Gather indices of type {it.dtype} have no cuda kernel")
+        if xt.itemsize not in (1, 4, 8):
+            raise CodegenError(f"Gather of {xt.dtype} has no cuda kernel")
+        self.emit(K_GATHER, [outer, xt.shape[axis], inner, it.size, DTYPES[it.dtype], xt.itemsize],
+                  refs=[self.ref(x), self.ref(idx), self.ref(node.output)], dtype=DTYPES[xt.dtype])
+
+    # -- reductions (c.py:736-821, 1255-1273) -------------------------------------------------------
+    def _reduce(self, node: Node, kind: str) -> None:
+        """K_REDUCE_MID slots: i[0] is_max, i[1] outer, i[2] n, i[3] inner; r[0] x, r[1] y.
+        K_REDUCE slots: i[0] kind (sum, mean, prod, max, min), i[1] outer, i[2] n, i[3] inner."""
+        x = node.input(0)
+        xt = x.tensor_type
+        axes = ops.reduce_axes(node, xt.rank, self._consts(node))
+        out = node.output
+        if not axes:
+            self._copy_value(xt.shape, x, self.ref(out), _strides(xt.shape), 0)
+            return
+        if list(axes) != list(range(axes[0], axes[-1] + 1)):
+            raise CodegenError(f"{node.op} over non-adjacent axes {axes} has no cuda kernel")
+        outer = int(np.prod(xt.shape[: axes[0]])) if axes[0] else 1
+        n = int(np.prod([xt.shape[a] for a in axes]))
+        inner = int(np.prod(xt.shape[axes[-1] + 1 :])) if axes[-1] + 1 < xt.rank else 1
+        if kind in ("mean", "max") and xt.dtype == "float32":
+            self.emit(K_REDUCE_MID, [int(kind == "max"), outer, n, inner], refs=[self.ref(x), self.ref(out)])
+            return
+        code = {"sum": 0, "mean": 1, "prod": 2, "max": 3, "min": 4}[kind]
+        self.emit(K_REDUCE, [code, outer, n, inner], refs=[self.ref(x), self.ref(out)], dtype=DTYPES[xt.dtype])
+
+    def op_ReduceMean(self, node: Node) -> None:
+        self._reduce(node, "mean")
+
+    def op_ReduceSum(self, node: Node) -> None:
+        self._reduce(node, "sum")
+
+    def op_ReduceMax(self, node: Node) -> None:
+        self._reduce(node, "max")
+
+    def op_ReduceMin(self, node: Node) -> None:
+        self._reduce(node, "min")
+
+    def op_ReduceProd(self, node: Node) -> None:
+        self._reduce(node, "prod")
+
+    def op_ArgMax(self, node: Node) -> None:
+        """K_ARGMAX slots: i[0] outer, i[1] n, i[2] inner; dtype of x; r[0] x, r[1] y (int64)."""
+        x = node.input(0)
+        xt = x.tensor_type
+        axis = int(node.attrs.get("axis", 0))
+        axis = axis + xt.rank if axis < 0 else axis
+        outer = int(np.prod(xt.shape[:axis])) if axis else 1
+        inner = int(np.prod(xt.shape[axis + 1 :])) if axis + 1 < xt.rank else 1
+        self.emit(K_ARGMAX, [outer, xt.shape[axis], inner], refs=[self.ref(x), self.ref(node.output)],
+                  dtype=DTYPES[xt.dtype], count="reduce")
+
+    def _global_pool(self, node: Node, is_max: int) -> None:
+        x = node.input(0)
+        xt = x.tensor_type
+        self._require_f32(node, xt)
+        if ops.conv_layout(node) == "NHWC":
+            outer, n, inner = xt.shape[0], int(np.prod(xt.shape[1:-1])), xt.shape[-1]
+        else:
+            outer, n, inner = xt.shape[0] * xt.shape[1], int(np.prod(xt.shape[2:])), 1
+        self.emit(K_REDUCE_MID, [is_max, outer, n, inner], refs=[self.ref(x), self.ref(node.output)])
+
+    def op_GlobalAveragePool(self, node: Node) -> None:
+        self._global_pool(node, 0)
+
+    def op_GlobalMaxPool(self, node: Node) -> None:
+        self._global_pool(node, 1)
+
+    # -- softmax, layer norm, batch norm (c.py:823-903) ----------------------------------------------
+    def _require_f32(self, node: Node, t: TensorType) -> None:
+        if t.dtype != "float32":
+            raise CodegenError(f"{node.op} on {t.dtype} has no cuda kernel")
+
+    def _softmax(self, node: Node, log: int) -> None:
+        """K_SOFTMAX slots: i[0] outer, i[1] n, i[2] inner, i[3] log; r[0] x, r[1] y."""
+        x = node.input(0)
+        xt = x.tensor_type
+        self._require_f32(node, xt)
+        axis = int(node.attrs.get("axis", -1))
+        axis = axis + xt.rank if axis < 0 else axis
+        outer = int(np.prod(xt.shape[:axis])) if axis else 1
+        inner = int(np.prod(xt.shape[axis + 1 :])) if axis + 1 < xt.rank else 1
+        self.emit(K_SOFTMAX, [outer, xt.shape[axis], inner, log], refs=[self.ref(x), self.ref(node.output)])
+
+    def op_Softmax(self, node: Node) -> None:
+        self._softmax(node, 0)
+
+    def op_LogSoftmax(self, node: Node) -> None:
+        self._softmax(node, 1)
+
+    def _vector_ref(self, value: Value | None, n: int, what: str) -> RefT:
+        if value is None:
+            return NO_REF
+        if value.tensor_type.size != n:
+            raise CodegenError(f"{what} must have {n} elements, got {value.tensor_type.shape}")
+        if value.tensor_type.dtype != "float32":
+            raise CodegenError(f"{what} must be float32")
+        return self.ref(value)
+
+    def op_LayerNormalization(self, node: Node) -> None:
+        """K_LAYER_NORM slots: i[0] rows, i[1] cols; f[0] eps; r[0] x, r[1] scale, r[2] bias, r[3] y."""
+        x = node.input(0)
+        xt = x.tensor_type
+        self._require_f32(node, xt)
+        axis = int(node.attrs.get("axis", -1))
+        axis = axis + xt.rank if axis < 0 else axis
+        cols = int(np.prod(xt.shape[axis:]))
+        rows = xt.size // max(cols, 1)
+        scale = self._vector_ref(node.optional_input(1), cols, "LayerNormalization scale")
+        bias = self._vector_ref(node.optional_input(2), cols, "LayerNormalization bias")
+        self.emit(K_LAYER_NORM, [rows, cols], [float(node.attrs.get("epsilon", 1e-5))],
+                  refs=[self.ref(x), scale, bias, self.ref(node.output)])
+
+    def op_BatchNormalization(self, node: Node) -> None:
+        x = node.input(0)
+        xt = x.tensor_type
+        self._require_f32(node, xt)
+        params = [v.data if v is not None else None for v in node.inputs[1:5]]
+        if any(p is None for p in params):
+            raise CodegenError("BatchNormalization parameters must be constants")
+        scale, bias, mean, var = (np.asarray(p, np.float64) for p in params)
+        inv = scale / np.sqrt(var + float(node.attrs.get("epsilon", 1e-5)))
+        shift = bias - mean * inv
+        c = inv.size
+        nhwc = node.attrs.get("layout") == "NHWC"
+        bshape = (c,) if nhwc else (c,) + (1,) * (xt.rank - 2)
+        # x * inv + shift as a two-instruction program; the folded constants are free-standing
+        # Values (Location "const"), kept alive here because blob keys use id()
+        g = Graph("bn")
+        mul = g.constant(inv.astype(np.float32).reshape(bshape), "bn_inv")
+        add = g.constant(shift.astype(np.float32).reshape(bshape), "bn_shift")
+        self._keep_alive += [mul, add]
+        self._elementwise(node.output, [("Mul", {}, [0, 1]), ("Add", {}, [3, 2])], [x, mul, add])
+
+    # -- GEMM family (c.py:905-1226) ------------------------------------------------------------------
+    def _prec(self) -> int:
+        return PRECISIONS[self.precision]
+
+    def _act(self, node: Node) -> tuple[int, float, float]:
+        return (
+            ACTS[str(node.attrs.get("activation", "none"))],
+            float(node.attrs.get("clip_min", 0.0)),
+            float(node.attrs.get("clip_max", 6.0)),
+        )
+
+    def _kmajor_b(self, matrix_kn: np.ndarray, key: Any) -> tuple[RefT, RefT, int, int]:
+        """Store a constant K x N right-hand side K-major ([N][K] rows) as hi + lo parts.
+        Returns (hi ref, lo ref, b_rs, b_cs) for element (k, n) at b[k*b_rs + n*b_cs]."""
+        k, n = matrix_kn.shape
+        if key in self.weights.by_key:
+            hi_off = self.weights.by_key[key]
+            lo_off = self.weights.by_key[(key, "lo")]
+        else:
+            kmaj = np.ascontiguousarray(np.asarray(matrix_kn, np.float32).T)
+            hi, lo = tf32_split(kmaj)
+            hi_off = self.weights.add(hi, key=key)
+            lo_off = self.weights.add(lo, key=(key, "lo"))
+        return (SPACE_WEIGHTS, 0, hi_off), (SPACE_WEIGHTS, 0, lo_off), 1, k
+
+    def _gemm(
+        self,
+        m: int,
+        n: int,
+        k: int,
+        a: RefT,
+        a_rs: int,
+        a_cs: int,
+        b: RefT,
+        b_rs: int,
+        b_cs: int,
+        c: RefT,
+        ldc: int,
+        *,
+        b_lo: RefT = NO_REF,
+        batch: Sequence[int] = (),
+        a_bs: Sequence[int] = (),
+        b_bs: Sequence[int] = (),
+        c_bs: Sequence[int] = (),
+        r_bs: Sequence[int] = (),
+        conv: dict[str, int] | None = None,
+        a_kind: int = STRIDED,
+        b_kind: int = STRIDED,
+        alpha: float = 1.0,
+        beta: float = 1.0,
+        bias: RefT = NO_REF,
+        bias_mode: int = 0,
+        res: RefT = NO_REF,
+        ldr: int = 0,
+        act: tuple[int, float, float] = (0, 0.0, 6.0),
+    ) -> None:
+        """K_GEMM slots: i[0..2] M, N, K; i[3] batch dims; i[4..7] batch extents; i[8..11],
+        i[12..15], i[16..19], i[20..23] per-dimension batch strides of A, B, C, residual;
+        i[24..26] A kind, row stride, column stride; i[27..40] conv geometry H, W, C, KH, KW, SH,
+        SW, DH, DW, PT, PL, OW, c_off, cg; i[41..43] B kind, row stride, column stride; i[44] ldc;
+        i[45] bias mode; i[46] ldr; i[47] activation; i[48] precision; i[49] OH.
+        f[0..3] alpha, beta, clip lo, clip hi. r[0] A, r[1] B, r[2] C, r[3] bias, r[4] residual,
+        r[5] residual of a split constant B."""
+        if len(batch) > 4:
+            raise CodegenError(f"GEMM with {len(batch)} batch dimensions")
+        ints = [0] * 50
+        ints[0], ints[1], ints[2], ints[3] = m, n, k, len(batch)
+        for d in range(len(batch)):
+            ints[4 + d] = batch[d]
+            ints[8 + d], ints[12 + d], ints[16 + d] = a_bs[d], b_bs[d], c_bs[d]
+            ints[20 + d] = r_bs[d] if r_bs else 0
+        ints[24], ints[25], ints[26] = a_kind, a_rs, a_cs
+        if conv is not None:
+            for j, key in enumerate(("H", "W", "C", "KH", "KW", "SH", "SW", "DH", "DW", "PT", "PL", "OW", "c_off", "cg")):
+                ints[27 + j] = conv[key]
+            ints[49] = conv["OH"]
+        ints[41], ints[42], ints[43] = b_kind, b_rs, b_cs
+        ints[44], ints[45], ints[46] = ldc, bias_mode if bias != NO_REF else 0, ldr
+        ints[47], ints[48] = act[0], self._prec()
+        self.emit(K_GEMM, ints, [alpha, beta, act[1], act[2]], [a, b, c, bias, res, b_lo], count="gemm")
+
+    def op_FusedGemm(self, node: Node) -> None:
+        a, b = node.input(0), node.input(1)
+        at, bt = a.tensor_type, b.tensor_type
+        self._require_f32(node, at)
+        trans = int(node.attrs.get("trans_b", 0))
+        k, n = (bt.shape[1], bt.shape[0]) if trans else bt.shape
+        m = at.size // max(k, 1)
+        if b.is_constant or self.plan.location(b).kind == "const":
+            data = self.const_data(b)
+            bref, blo, b_rs, b_cs = self._kmajor_b(data.T if trans else data, ("kmajor", id(self._root(b)), trans))
+        else:
+            bref, blo, b_rs, b_cs = self.ref(b), NO_REF, (1 if trans else n), (k if trans else 1)
+        bias_v, res_v = node.optional_input(2), node.optional_input(3)
+        self._gemm(
+            m, n, k, self.ref(a), k, 1, bref, b_rs, b_cs, self.ref(node.output), n, b_lo=blo,
+            bias=self._vector_ref(bias_v, n, "FusedGemm bias"), bias_mode=1,
+            res=self.ref(res_v), ldr=n, act=self._act(node),
+        )
+
+    def op_Gemm(self, node: Node) -> None:
+        a, b, c = node.input(0), node.input(1), node.optional_input(2)
+        at, bt = a.tensor_type, b.tensor_type
+        self._require_f32(node, at)
+        ta, tb = int(node.attrs.get("transA", 0)), int(node.attrs.get("transB", 0))
+        m, k = (at.shape[1], at.shape[0]) if ta else at.shape
+        n = bt.shape[0] if tb else bt.shape[1]
+        alpha = float(node.attrs.get("alpha", 1.0))
+        beta = float(node.attrs.get("beta", 1.0))
+        a_rs, a_cs = (1, m) if ta else (k, 1)
+        if b.is_constant or self.plan.location(b).kind == "const":
+            data = self.const_data(b)
+            bref, blo, b_rs, b_cs = self._kmajor_b(data.T if tb else data, ("kmajor", id(self._root(b)), tb))
+        else:
+            bref, blo = self.ref(b), NO_REF
+            b_rs, b_cs = (1, k) if tb else (n, 1)
+        bias, mode, res, ldr = NO_REF, 0, NO_REF, 0
+        if c is not None:
+            ct = c.tensor_type
+            full = np.broadcast_shapes(ct.shape, (m, n))
+            cdata = self.const_data(c) if (c.is_constant or self.plan.location(c).kind == "const") else None
+            if cdata is not None and ct.size in (1, n) and (ct.rank < 2 or ct.shape[0] == 1):
+                vec = np.broadcast_to(cdata.reshape(-1) * beta, (n,)).astype(np.float32)
+                bias, mode = self.weights_ref(vec), 1
+            elif cdata is not None and ct.rank == 2 and tuple(ct.shape) == (m, 1):
+                bias, mode = self.weights_ref((cdata.reshape(-1) * beta).astype(np.float32)), 2
+            elif tuple(ct.shape) == (m, n) and full == (m, n):
+                res, ldr = self.ref(c), n
+            else:
+                raise CodegenError(f"Gemm bias of shape {ct.shape} has no cuda lowering")
+        self._gemm(m, n, k, self.ref(a), a_rs, a_cs, bref, b_rs, b_cs, self.ref(node.output), n, b_lo=blo,
+                   alpha=alpha, beta=beta, bias=bias, bias_mode=mode, res=res, ldr=ldr)
+
+    def op_MatMul(self, node: Node) -> None:
+        a, b = node.input(0), node.input(1)
+        at, bt = a.tensor_type, b.tensor_type
+        self._require_f32(node, at)
+        ashape = (1, *at.shape) if at.rank == 1 else at.shape
+        bshape = (*bt.shape, 1) if bt.rank == 1 else bt.shape
+        m, k = ashape[-2], ashape[-1]
+        n = bshape[-1]
+        batch_shape = [int(d) for d in np.broadcast_shapes(ashape[:-2], bshape[:-2])]
+        a_bs = [s * m * k for s in _broadcast_strides(ashape[:-2], batch_shape)]
+        b_bs = [s * k * n for s in _broadcast_strides(bshape[:-2], batch_shape)]
+        c_bs = [s * m * n for s in _strides(batch_shape)]
+        dims, (a_bs, b_bs, c_bs) = _collapse(batch_shape, [a_bs, b_bs, c_bs])
+        bconst = b.is_constant or self.plan.location(b).kind == "const"
+        if bconst and not any(b_bs):
+            data = self.const_data(b).reshape(k, n)
+            bref, blo, b_rs, b_cs = self._kmajor_b(data, ("kmajor", id(self._root(b)), 0))
+        else:
+            bref, blo, b_rs, b_cs = self.ref(b), NO_REF, n, 1
+        self._gemm(m, n, k, self.ref(a), k, 1, bref, b_rs, b_cs, self.ref(node.output), n, b_lo=blo,
+                   batch=dims, a_bs=a_bs, b_bs=b_bs, c_bs=c_bs, r_bs=[0] * len(dims))
+
+    @staticmethod
+    def _depthwise(node: Node) -> bool:
+        return CEmitter._depthwise(node)
+
+    def op_Conv(self, node: Node) -> None:
+        self.op_FusedConv(node)
+
+    def op_FusedConv(self, node: Node) -> None:
+        x, w = node.input(0), node.input(1)
+        xt, wt = x.tensor_type, w.tensor_type
+        self._require_f32(node, xt)
+        nhwc = ops.conv_layout(node) == "NHWC"
+        group = int(node.attrs.get("group", 1))
+        if nhwc:
+            nb, h, wd, c = xt.shape
+            kh, kw, cg, kout = wt.shape
+        else:
+            nb, c, h, wd = xt.shape
+            kout, cg, kh, kw = wt.shape
+        g = ops.window_geometry(node, (h, wd), (kh, kw))
+        oh, ow = g.out_hw
+        pt, pl, _, _ = g.pads
+        bias_v, res_v = node.optional_input(2), node.optional_input(3)
+        act = self._act(node) if node.op == "FusedConv" else (0, 0.0, 6.0)
+        bias = self._vector_ref(bias_v, kout, "Conv bias")
+        res = self.ref(res_v)
+        if not (w.is_constant or self.plan.location(w).kind == "const"):
+            raise CodegenError("convolution weights must be constant for the cuda backend")
+        wdata = self.const_data(w)
+        if self._depthwise(node):
+            # K_DEPTHWISE slots: i[0..13] N, H, W, C, KH, KW, SH, SW, DH, DW, PT, PL, OH, OW,
+            # i[14] NHWC, i[15] activation; f[0..1] clip bounds; r[0] x, r[1] w, r[2] bias,
+            # r[3] residual, r[4] y. Weights HWC (NHWC) or CHW (NCHW), as mgc_depthwise_*.
+            wref = self.weights_ref(np.ascontiguousarray(wdata, np.float32), key=("raw", id(self._root(w))))
+            ints = [nb, h, wd, c, kh, kw, g.strides[0], g.strides[1], g.dilations[0], g.dilations[1],
+                    pt, pl, oh, ow, int(nhwc), act[0]]
+            self.emit(K_DEPTHWISE, ints, [act[1], act[2]], [self.ref(x), wref, bias, res, self.ref(node.output)])
+            return
+        kg = kout // group
+        geo = {"H": h, "W": wd, "C": c, "KH": kh, "KW": kw, "SH": g.strides[0], "SW": g.strides[1],
+               "DH": g.dilations[0], "DW": g.dilations[1], "PT": pt, "PL": pl, "OH": oh, "OW": ow}
+        for gi in range(group):
+            bias_g = bias if bias == NO_REF else (bias[0], bias[1], bias[2] + gi * kg * 4)
+            if nhwc:
+                wmat = wdata[:, :, :, gi * kg : (gi + 1) * kg].reshape(kh * kw * cg, kg)
+                bref, blo, b_rs, b_cs = self._kmajor_b(wmat, ("conv", id(self._root(w)), gi))
+                pointwise = kh == kw == 1 and g.strides == (1, 1) and g.pads == (0, 0, 0, 0)
+                xref = self.ref(x, gi * cg * 4) if pointwise else self.ref(x)
+                out_ref = self.ref(node.output, gi * kg * 4)
+                res_g = res if res == NO_REF else (res[0], res[1], res[2] + gi * kg * 4)
+                self._gemm(
+                    nb * oh * ow, kg, kh * kw * cg, xref, c, 1, bref, b_rs, b_cs, out_ref, kout, b_lo=blo,
+                    conv={**geo, "c_off": gi * cg, "cg": cg}, a_kind=STRIDED if pointwise else CONV_NHWC,
+                    bias=bias_g, bias_mode=1, res=res_g, ldr=kout, act=act,
+                )
+            else:
+                plane = oh * ow
+                amat = np.ascontiguousarray(wdata[gi * kg : (gi + 1) * kg].reshape(kg, cg * kh * kw), np.float32)
+                aref = self.weights_ref(amat, key=("convA", id(self._root(w)), gi))
+                out_ref = self.ref(node.output, gi * kg * plane * 4)
+                res_g = res if res == NO_REF else (res[0], res[1], res[2] + gi * kg * plane * 4)
+                self._gemm(
+                    kg, plane, cg * kh * kw, aref, cg * kh * kw, 1, self.ref(x), 0, 0, out_ref, plane,
+                    batch=[nb], a_bs=[0], b_bs=[c * h * wd], c_bs=[kout * plane],
+                    r_bs=[kout * plane], conv={**geo, "c_off": gi * cg, "cg": cg}, b_kind=CONV_NCHW,
+                    bias=bias_g, bias_mode=2, res=res_g, ldr=plane, act=act,
+                )
+
+    # -- pooling (c.py:1228-1253) ---------------------------------------------------------------------
+    def _pool(self, node: Node, is_max: int) -> None:
+        """K_POOL slots: i[0] is_max, i[1..17] N, H, W, C, KH, KW, SH, SW, DH, DW, PT, PL, PB, PR,
+        OH, OW, count_include_pad, i[18] NHWC; r[0] x, r[1] y."""
+        x = node.input(0)
+        xt = x.tensor_type
+        self._require_f32(node, xt)
+        nhwc = ops.conv_layout(node) == "NHWC"
+        nb, h, wd, c = xt.shape if nhwc else (xt.shape[0], xt.shape[2], xt.shape[3], xt.shape[1])
+        kernel = tuple(int(k) for k in node.attrs["kernel_shape"])
+        g = ops.window_geometry(node, (h, wd), (kernel[0], kernel[1]), bool(node.attrs.get("ceil_mode", 0)))
+        pt, pl, pb, pr = g.pads
+        oh, ow = g.out_hw
+        include = int(node.attrs.get("count_include_pad", 0))
+        self.emit(K_POOL, [is_max, nb, h, wd, c, kernel[0], kernel[1], g.strides[0], g.strides[1], g.dilations[0],
+                           g.dilations[1], pt, pl, pb, pr, oh, ow, include, int(nhwc)],
+                  refs=[self.ref(x), self.ref(node.output)])
+
+    def op_MaxPool(self, node: Node) -> None:
+        self._pool(node, 1)
+
+    def op_AveragePool(self, node: Node) -> None:
+        self._pool(node, 0)
+
+    # -- whole program ----------------------------------------------------------------------------------
+    def lower(self) -> LoweredModel:
+        for k, node in enumerate(self.graph.nodes):
+            self._node = k
+            self.node(node)
+        self._node = -1
+        for value, j in self.plan.copies:
+            t = value.tensor_type
+            if t.nbytes:
+                self.emit(K_MEMCPY, [t.nbytes], refs=[self.ref(value), (SPACE_OUTPUT, j, 0)], count="copy")
+        return LoweredModel(
+            launches=self.launches,
+            aux=np.asarray(self.aux if self.aux else [0], np.int64),
+            weights=self.weights,
+            arena_bytes=max(self.plan.arena_bytes, 64),
+            inputs=[(v.name, v.tensor_type) for v in self.graph.inputs],
+            outputs=[(name, v.tensor_type) for name, v in self.graph.named_outputs()],
+            plan=self.plan,
+            kernels=dict(sorted(self.kernels.items())),
+            node_names=[(n.op, n.name) for n in self.graph.nodes],
+            precision=self.precision,
+        )
+
+
+def lower_graph(
+    graph: Graph, strategy: Strategy = "greedy_by_size", inplace: bool = True, precision: str = "tf32"
+) -> LoweredModel:
+    """Lower an optimised, scheduled graph (nodes in execution order) to a launch list."""
+    return CudaEmitter(graph, strategy, inplace, precision).lower()
+
+
+def algorithmic_cost(graph: Graph) -> tuple[int, int]:
+    """(FLOPs, bytes) of one execution: FLOPs = sum of ``ops.flops`` (ops.py:1224-1239); bytes =
+    every scheduled node's non-constant inputs and outputs (views excluded) plus each constant
+    once."""
+    flops = 0
+    nbytes = 0
+    seen: set[int] = set()
+    for node in graph.nodes:
+        flops += ops.flops(node)
+        if node.op in ALIAS_OPS:
+            continue
+        for v in node.inputs:
+            if v is None:
+                continue
+            if v.is_constant:
+                if id(v) not in seen and v.data is not None:
+                    seen.add(id(v))
+                    nbytes += v.data.nbytes
+            else:
+                nbytes += v.tensor_type.nbytes
+        nbytes += sum(o.tensor_type.nbytes for o in node.outputs if o.type is not None)
+    return flops, nbytes
+
+
+__all__ = ["CudaEmitter", "Launch", "LoweredModel", "Ref", "algorithmic_cost", "lower_graph", "tf32_split"]

@@ -1,0 +1,137 @@
+"""The kernel ABI (mgc_cuda_gemm, _conv_nhwc, _softmax, _layer_norm, _pool_nhwc, _depthwise_nhwc,
+_reduce_mid) against a plain PyTorch fp32 reference of the same operation and, where it is
+built, the reference's own C kernels (oracle/_ref/libmgc_ref_kernels.so, mgc_kernels.c)."""
+
+from __future__ import annotations
+
+import ctypes
+from pathlib import Path
+
+import numpy as np
+import pytest
+
+from mgc_cuda.runtime import library, last_error
+
+pytestmark = pytest.mark.gpu
+
+torch = pytest.importorskip("torch")
+REF_LIB = Path(__file__).resolve().parents[1] / "oracle" / "_ref" / "libmgc_ref_kernels.so"
+
+
+def dev(a: np.ndarray) -> "torch.Tensor":
+    return torch.from_numpy(np.ascontiguousarray(a)).cuda()
+
+
+def ptr(t: "torch.Tensor | None") -> int | None:
+    return None if t is None else t.data_ptr()
+
+
+def stream() -> int:
+    return torch.cuda.current_stream().cuda_stream
+
+
+def ok(st: int) -> None:
+    assert st == 0, last_error()
+
+
+def ref_lib() -> ctypes.CDLL | None:
+    return ctypes.CDLL(str(REF_LIB)) if REF_LIB.exists() else None
+
+
+@pytest.mark.parametrize("precision", [0, 1, 2])
+@pytest.mark.parametrize("m,n,k,act", [(1, 1000, 2048, 0), (197, 77, 129, 1), (512, 256, 64, 3), (64, 3072, 768, 4)])
+def test_gemm_vs_torch(m: int, n: int, k: int, act: int, precision: int) -> None:
+    rng = np.random.default_rng(m + n + k)
+    a = rng.standard_normal((m, k)).astype(np.float32)
+    b = rng.standard_normal((k, n)).astype(np.float32) * 0.05
+    bias = rng.standard_normal(n).astype(np.float32)
+    res = rng.standard_normal((m, n)).astype(np.float32)
+    A, B, Bi, R = dev(a), dev(b), dev(bias), dev(res)
+    C = torch.empty((m, n), device="cuda")
+    lib = library()
+    ok(lib.mgc_cuda_gemm(m, n, k, 1, ptr(A), k, 1, 0, ptr(B), n, 1, 0, ptr(C), n, 0, 1.0, ptr(Bi), 1, ptr(R), n,
+                         0, 1.0, act, 0.0, 6.0, precision, stream()))
+    torch.cuda.synchronize()
+    with torch.no_grad():
+        prev = torch.backends.cuda.matmul.allow_tf32
+        torch.backends.cuda.matmul.allow_tf32 = False
+        y = A.double() @ B.double() + Bi.double() + R.double()
+        torch.backends.cuda.matmul.allow_tf32 = prev
+        y = {0: y, 1: torch.relu(y), 3: torch.nn.functional.gelu(y), 4: torch.nn.functional.gelu(y, approximate="tanh")}[act]
+    err = float((C.double() - y).abs().max())
+    scale = float(y.abs().max())
+    tol = 2e-2 if precision == 1 else 1e-5
+    assert err <= tol * max(scale, 1.0), f"err {err:.3g} scale {scale:.3g}"
+
+
+@pytest.mark.parametrize("shape", [(2, 14, 14, 64, 3, 1, 1), (1, 56, 56, 64, 1, 1, 0), (2, 28, 28, 32, 3, 2, 1), (1, 32, 32, 3, 7, 2, 3)])
+@pytest.mark.parametrize("precision", [0, 2])
+def test_conv_nhwc_vs_torch(shape: tuple, precision: int) -> None:
+    n, h, w, c, kk, s, p = shape
+    co = 48
+    rng = np.random.default_rng(h * c)
+    x = rng.standard_normal((n, h, w, c)).astype(np.float32)
+    wt = (rng.standard_normal((kk, kk, c, co)) * 0.1).astype(np.float32)
+    bias = rng.standard_normal(co).astype(np.float32)
+    oh = (h + 2 * p - kk) // s + 1
+    ow = (w + 2 * p - kk) // s + 1
+    X, W, Bi = dev(x), dev(wt), dev(bias)
+    Y = torch.empty((n, oh, ow, co), device="cuda")
+    ok(library().mgc_cuda_conv_nhwc(n, h, w, c, kk, kk, s, s, 1, 1, p, p, oh, ow, co, ptr(X), ptr(W), ptr(Bi), None,
+                                    1, 0.0, 6.0, ptr(Y), precision, stream()))
+    torch.cuda.synchronize()
+    ref = torch.nn.functional.conv2d(X.permute(0, 3, 1, 2).double(), W.permute(3, 2, 0, 1).double(), Bi.double(),
+                                     stride=s, padding=p).relu().permute(0, 2, 3, 1)
+    err = float((Y.double() - ref).abs().max())
+    assert err <= 1e-5 * max(float(ref.abs().max()), 1.0)
+
+
+def test_softmax_layer_norm_reduce_vs_torch_and_reference_c() -> None:
+    rng = np.random.default_rng(3)
+    x = (rng.standard_normal((48, 128)) * 4).astype(np.float32)
+    X = dev(x)
+    Y = torch.empty_like(X)
+    lib = library()
+    ok(lib.mgc_cuda_softmax(48, 128, 1, ptr(X), ptr(Y), 0, stream()))
+    torch.cuda.synchronize()
+    np.testing.assert_allclose(Y.cpu().numpy(), torch.softmax(X.double(), -1).cpu().numpy(), rtol=1e-5, atol=1e-7)
+    g = (rng.random(128) + 0.5).astype(np.float32)
+    b = rng.standard_normal(128).astype(np.float32)
+    G, B = dev(g), dev(b)
+    ok(lib.mgc_cuda_layer_norm(48, 128, ptr(X), ptr(G), ptr(B), 1e-5, ptr(Y), stream()))
+    torch.cuda.synchronize()
+    ln = torch.nn.functional.layer_norm(X.double(), (128,), G.double(), B.double(), 1e-5)
+    np.testing.assert_allclose(Y.cpu().numpy(), ln.cpu().numpy(), rtol=1e-5, atol=2e-5)
+    R = torch.empty((48,), device="cuda")
+    ok(lib.mgc_cuda_reduce_mid(0, 48, 128, 1, ptr(X), ptr(R), stream()))
+    torch.cuda.synchronize()
+    np.testing.assert_allclose(R.cpu().numpy(), x.astype(np.float64).mean(axis=1), rtol=1e-5, atol=1e-6)
+    ref = ref_lib()
+    if ref is not None:  # the reference's own C kernels, same inputs
+        out = np.empty_like(x)
+        ref.mgc_layer_norm.argtypes = [ctypes.c_long, ctypes.c_long] + [ctypes.c_void_p] * 3 + [ctypes.c_float, ctypes.c_void_p]
+        ref.mgc_layer_norm(48, 128, x.ctypes.data, g.ctypes.data, b.ctypes.data, 1e-5, out.ctypes.data)
+        ok(lib.mgc_cuda_layer_norm(48, 128, ptr(X), ptr(G), ptr(B), 1e-5, ptr(Y), stream()))
+        torch.cuda.synchronize()
+        np.testing.assert_allclose(Y.cpu().numpy(), out, rtol=1e-5, atol=2e-5)
+
+
+def test_pool_and_depthwise_vs_torch() -> None:
+    rng = np.random.default_rng(4)
+    x = rng.standard_normal((2, 17, 17, 32)).astype(np.float32)
+    X = dev(x)
+    Y = torch.empty((2, 9, 9, 32), device="cuda")
+    lib = library()
+    ok(lib.mgc_cuda_pool_nhwc(1, 2, 17, 17, 32, 3, 3, 2, 2, 1, 1, 1, 1, 1, 1, 9, 9, 0, ptr(X), ptr(Y), stream()))
+    torch.cuda.synchronize()
+    ref = torch.nn.functional.max_pool2d(X.permute(0, 3, 1, 2), 3, 2, 1).permute(0, 2, 3, 1)
+    np.testing.assert_array_equal(Y.cpu().numpy(), ref.cpu().numpy())
+    w = (rng.standard_normal((3, 3, 32)) * 0.3).astype(np.float32)
+    b = rng.standard_normal(32).astype(np.float32)
+    W, B = dev(w), dev(b)
+    ok(lib.mgc_cuda_depthwise_nhwc(2, 17, 17, 32, 3, 3, 2, 2, 1, 1, 1, 1, 9, 9, ptr(X), ptr(W), ptr(B), None, 2,
+                                   0.0, 6.0, ptr(Y), stream()))
+    torch.cuda.synchronize()
+    ref = torch.nn.functional.conv2d(X.permute(0, 3, 1, 2).double(), W.permute(2, 0, 1).unsqueeze(1).double(),
+                                     B.double(), stride=2, padding=1, groups=32).clamp(0, 6).permute(0, 2, 3, 1)
+    np.testing.assert_allclose(Y.cpu().numpy(), ref.cpu().numpy(), rtol=1e-5, atol=1e-5)

@@ -1,0 +1,159 @@
+"""Whole benchmark models on the GPU against the oracle and the reference's golden summaries,
+plus the behaviour of the compiled-model API (runtime_lib.py semantics)."""
+
+from __future__ import annotations
+
+import numpy as np
+import pytest
+
+import cases
+from mgc_cuda import zoo
+from mgc_cuda.runtime import CudaCompiledModel, compile_graph
+from ml_graph_compiler.errors import GraphError
+from ml_graph_compiler.ir import Graph, TensorType
+from ml_graph_compiler.memory import STRATEGIES
+from ml_graph_compiler.passes import optimize
+from ml_graph_compiler.schedule import schedule
+from ml_graph_compiler.shape_inference import infer_shapes
+from oracle import runner
+
+pytestmark = pytest.mark.gpu
+
+BIG = cases.big_model_cases()
+BUDGET = {"strict": 1e-4, "tf32": 2e-2}
+
+
+@pytest.fixture(scope="module")
+def prepared() -> dict:
+    out = {}
+    for case in BIG:
+        g, feeds = cases.prepare(case)
+        out[case.name] = (g, feeds, runner.run(g, feeds))
+    return out
+
+
+@pytest.mark.parametrize("precision", ["strict", "tf32"])
+@pytest.mark.parametrize("case", BIG, ids=[c.name for c in BIG])
+def test_model_logits_within_budget(case: cases.Case, precision: str, prepared: dict, golden_models: dict) -> None:
+    """Max abs error on the outputs <= 1e-4 (strict) / 2e-2 (tf32) and 100% argmax agreement,
+    against the oracle and the reference interpreter's summaries."""
+    g, feeds, want = prepared[case.name]
+    model = compile_graph(g, precision=precision)
+    try:
+        got = model.run(feeds)
+    finally:
+        model.close()
+    for name, w in want.items():
+        err = float(np.abs(got[name].astype(np.float64) - w).max())
+        assert err <= BUDGET[precision], f"{name}: max abs err {err:.3g} (|max| {float(np.abs(w).max()):.3g})"
+        if name == "logits":  # top-1 agreement on classifier / LM logits
+            rows_g = got[name].reshape(-1, w.shape[-1])
+            np.testing.assert_array_equal(rows_g.argmax(axis=1), golden_models[f"{case.name}|out|{name}|argmax"])
+        head = golden_models[f"{case.name}|out|{name}|head"]
+        assert float(np.abs(got[name].reshape(-1)[: head.size] - head).max()) <= BUDGET[precision] * 1.01
+
+
+def test_resnet50_batch_is_independent_per_image() -> None:
+    """Size-independent property at a larger batch: every image of a batch-8 run equals the
+    batch-1 model's output for that image (strict mode, bit-level batch independence is not
+    required, the strict budget is)."""
+    g1 = zoo.resnet50(batch=1)
+    optimize(g1, "O3")
+    schedule(g1)
+    g8 = zoo.resnet50(batch=8)
+    optimize(g8, "O3")
+    schedule(g8)
+    x = np.random.default_rng(5).standard_normal((8, 3, 224, 224)).astype(np.float32)
+    m8 = compile_graph(g8, precision="strict")
+    y8 = m8.run({"image": x})["logits"]
+    m8.close()
+    m1 = compile_graph(g1, precision="strict")
+    for i in (0, 3, 7):
+        y1 = m1.run({"image": x[i : i + 1]})["logits"]
+        assert float(np.abs(y1 - y8[i : i + 1]).max()) <= 1e-4
+    m1.close()
+
+
+def test_strategies_and_inplace_agree() -> None:
+    """All planner strategies x in-place give the same outputs (reference test_codegen.py:414-423;
+    the C backend is bit-identical, the CUDA kernels too since only offsets change)."""
+    g = zoo.tiny_cnn(batch=2)
+    optimize(g, "O3")
+    schedule(g)
+    feeds = zoo.feeds(g, 0)
+    results = []
+    for strategy in STRATEGIES:
+        for inplace in (True, False):
+            m = compile_graph(g, strategy=strategy, inplace=inplace, precision="strict")
+            results.append(m.run(feeds)["logits"])
+            m.close()
+    for r in results[1:]:
+        np.testing.assert_array_equal(r, results[0])
+
+
+def test_gather_out_of_range_raises_graph_error() -> None:
+    g = Graph("gather")
+    ids = g.add_input("ids", TensorType("int64", (4,)))
+    table = g.constant(np.arange(20, dtype=np.float32).reshape(10, 2))
+    g.add_output(g.add_node("Gather", [table, ids], attrs={"axis": 0}).output, "y")
+    infer_shapes(g)
+    m = compile_graph(g)
+    with pytest.raises(GraphError):
+        m.run({"ids": np.asarray([1, 2, 10, 3])})
+    # the handle stays usable and the flag is cleared on the next run
+    y = m.run({"ids": np.asarray([1, -1, 0, 9])})["y"]
+    np.testing.assert_array_equal(y, np.arange(20, dtype=np.float32).reshape(10, 2)[[1, 9, 0, 9]])
+    m.close()
+
+
+def test_input_validation() -> None:
+    g = zoo.mlp()
+    m = compile_graph(g)
+    with pytest.raises(GraphError):
+        m.run({})
+    with pytest.raises(GraphError):
+        m.run({"x": np.zeros((4, 16), np.float64)})
+    with pytest.raises(GraphError):
+        m.run({"x": np.zeros((4, 15), np.float32)})
+    m.close()
+
+
+def test_output_aliasing_copies() -> None:
+    """Outputs that are inputs, constants or duplicates are copied (plan.copies)."""
+    g = Graph("alias")
+    x = g.add_input("x", TensorType("float32", (3, 4)))
+    c = g.constant(np.full((2,), 7.0, np.float32))
+    y = g.add_node("Relu", [x]).output
+    g.add_output(x, "same")
+    g.add_output(c, "const")
+    g.add_output(y, "y")
+    g.add_output(y, "y_again")
+    infer_shapes(g)
+    m = compile_graph(g)
+    xv = np.random.default_rng(0).standard_normal((3, 4)).astype(np.float32)
+    out = m.run({"x": xv})
+    np.testing.assert_array_equal(out["same"], xv)
+    np.testing.assert_array_equal(out["const"], np.full((2,), 7.0, np.float32))
+    np.testing.assert_array_equal(out["y"], np.maximum(xv, 0))
+    np.testing.assert_array_equal(out["y_again"], np.maximum(xv, 0))
+    m.close()
+
+
+def test_profile_save_load_and_device_run(tmp_path) -> None:
+    g = zoo.tiny_cnn(batch=2)
+    optimize(g, "O3")
+    schedule(g)
+    feeds = zoo.feeds(g, 0)
+    m = compile_graph(g, precision="strict")
+    want = m.run(feeds)["logits"]
+    prof = m.profile()
+    assert len(prof) == len(g.nodes)
+    assert sum(t for _, _, t in prof) > 0
+    assert {op for op, _, _ in prof} >= {"FusedConv", "MaxPool"}
+    m.run_device(sync=True)
+    m.save(tmp_path / "saved")
+    m.close()
+    m2 = CudaCompiledModel.load(tmp_path / "saved")
+    np.testing.assert_array_equal(m2.run(feeds)["logits"], want)
+    assert m2.launch_count > 0
+    m2.close()

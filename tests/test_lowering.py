@@ -1,0 +1,113 @@
+"""Host-side lowering: the launch list follows the reference planner and C emitter exactly."""
+
+from __future__ import annotations
+
+import numpy as np
+import pytest
+
+import cases
+from mgc_cuda import lowering, zoo
+from mgc_cuda.lowering import CudaEmitter, lower_graph, tf32_split
+from ml_graph_compiler.codegen.c import generate_c
+from ml_graph_compiler.errors import CodegenError
+from ml_graph_compiler.ir import Graph, TensorType
+from ml_graph_compiler.passes import optimize
+from ml_graph_compiler.schedule import schedule
+from ml_graph_compiler.shape_inference import infer_shapes
+
+
+def o3(g: Graph) -> Graph:
+    optimize(g, "O3")
+    schedule(g)
+    return g
+
+
+@pytest.fixture(scope="module")
+def r50() -> Graph:
+    return o3(zoo.resnet50(batch=1))
+
+
+def test_resnet50_o3_matches_published_structure(r50: Graph) -> None:
+    """58 nodes; kernels gemm 54 / pool 1 / reduce 1 / transpose 1 / view 1; arena 7,225,344 B
+    (reference benchmarks/results/ablation_cnn.json, cumulative loopfuse for resnet50)."""
+    assert len(r50.nodes) == 58
+    low = lower_graph(r50)
+    assert low.kernels == {"gemm": 54, "pool": 1, "reduce": 1, "transpose": 1, "view": 1}
+    assert low.arena_bytes == 7_225_344
+    assert len(low.launches) == 57
+
+
+def test_same_kernel_mix_and_arena_as_the_c_backend() -> None:
+    for make in (lambda: zoo.tiny_cnn(batch=2), lambda: zoo.tiny_transformer(kind="gpt"), zoo.mlp):
+        g = o3(make())
+        ours = lower_graph(g)
+        theirs = generate_c(g)
+        assert ours.arena_bytes == max(theirs.arena_bytes, 64)
+        for kind in ("gemm", "depthwise", "pool", "softmax", "layer_norm", "gather"):
+            assert ours.kernels.get(kind, 0) == theirs.kernels.get(kind, 0), kind
+
+
+def test_every_arena_reference_stays_inside_the_arena(r50: Graph) -> None:
+    low = lower_graph(r50)
+    for rec in low.launches:
+        for ref in rec.r:
+            if ref.space == lowering.SPACE_ARENA:
+                assert 0 <= ref.offset < low.arena_bytes
+            if ref.space == lowering.SPACE_WEIGHTS:
+                assert 0 <= ref.offset < low.weights.nbytes
+                assert ref.offset % 4 == 0
+
+
+def test_conv_launches_use_nhwc_implicit_gemm(r50: Graph) -> None:
+    low = lower_graph(r50)
+    gemms = [r for r in low.launches if r.kind == lowering.K_GEMM]
+    kinds = {int(r.i[24]) for r in gemms}
+    assert kinds == {lowering.STRIDED, lowering.CONV_NHWC}
+    stem = gemms[0]
+    assert (stem.i[30], stem.i[31], stem.i[32]) == (7, 7, 2)  # KH, KW, SH
+    assert stem.i[0] == 112 * 112 and stem.i[1] == 64 and stem.i[2] == 7 * 7 * 3
+    fc = gemms[-1]
+    assert (fc.i[0], fc.i[1], fc.i[2]) == (1, 1000, 2048)
+
+
+def test_tf32_split_is_exact() -> None:
+    rng = np.random.default_rng(0)
+    a = (rng.standard_normal(10_000) * 10.0 ** rng.integers(-8, 8, 10_000)).astype(np.float32)
+    a[:4] = [0.0, -0.0, np.inf, -np.inf]
+    hi, lo = tf32_split(a)
+    assert np.all((hi.view(np.uint32) & 0x1FFF) == 0)
+    np.testing.assert_array_equal(hi + lo, a)
+    finite = np.isfinite(a) & (a != 0)
+    assert np.all(np.abs(lo[finite]) <= np.abs(a[finite]) * 2.0**-11)
+
+
+def test_unsupported_operator_is_a_compile_error() -> None:
+    g = Graph("bad")
+    x = g.add_input("x", TensorType("float32", (2, 3)))
+    g.add_output(g.add_node("Trilu", [x]).output, "y")
+    infer_shapes(g)
+    with pytest.raises(CodegenError, match="no kernel"):
+        CudaEmitter(g)
+
+
+def test_float16_is_rejected() -> None:
+    g = Graph("half")
+    x = g.add_input("x", TensorType("float16", (2, 3)))
+    g.add_output(g.add_node("Relu", [x]).output, "y")
+    infer_shapes(g)
+    with pytest.raises(CodegenError, match="float16"):
+        CudaEmitter(g)
+
+
+@pytest.mark.parametrize("case", cases.all_cases(), ids=[c.name for c in cases.all_cases()])
+def test_every_case_lowers(case: cases.Case) -> None:
+    g, _ = cases.prepare(case)
+    low = lower_graph(g, precision="strict")
+    assert low.launches or all(n.op in lowering.ALIAS_OPS for n in g.nodes)
+    assert all(0 <= r.kind <= lowering.K_MEMCPY for r in low.launches)
+
+
+def test_algorithmic_cost_of_resnet50(r50: Graph) -> None:
+    flops, nbytes = lowering.algorithmic_cost(r50)
+    assert abs(flops / 1e9 - 8.178) < 0.01
+    assert 200e6 < nbytes < 230e6
