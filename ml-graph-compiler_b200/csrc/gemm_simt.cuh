@@ -35,6 +35,11 @@ struct GemmParams {
     float lo, hi;
     int precision;
     const float *b_lo;            // residual of a split constant B (B = b + b_lo exactly), may be NULL
+    // tensor-core layout of a constant B: K-major [N][Kp] (for im2col, K = (kh, kw, channel
+    // padded to b_cpad)), TF32-rounded high part and fp32 residual; NULL when not provided
+    const float *b_umma, *b_umma_lo;
+    int b_cpad;
+    int *err;                     // device word for bounded-wait timeouts (may be NULL)
 };
 
 __device__ __forceinline__ float fetch_a(const GemmParams &p, const float *a, long long m, long long k) {

@@ -1,16 +1,589 @@
-// tcgen05 (UMMA) GEMM for sm_100a: placeholder that declines every problem until the tensor-core
-// kernel lands; run_gemm then uses the exact-fp32 SIMT kernel.
+// tcgen05 (UMMA) implicit-GEMM / GEMM for sm_100a with the fused FusedConv / FusedGemm epilogue.
+//
+// C[m, n] = act(alpha * sum_k A[m, k] * B[n, k] + bias[n] + R[m, n]), fp32 in and out.
+//
+// Data movement
+// * A (activations) is loaded by TMA into 128B-swizzled shared memory, 128 rows x 32 fp32 per
+//   K block: either a tiled 2-D box of a row-major [M, K] matrix (pointwise convolutions,
+//   FusedGemm, Gemm), or an im2col box of an NHWC image (3x3 / strided / dilated convolutions:
+//   128 consecutive output pixels x 32 channels at one filter tap; padding comes from the
+//   tensor map's bounding box, out-of-image taps read as zero).
+// * B (weights) is K-major [N][Kp] in the resident constant blob, stored by the lowering as a
+//   TF32-exact high part and the fp32 residual (hi + lo == B exactly); for im2col the K axis is
+//   (kh, kw, channel padded to 32).
+//
+// Arithmetic (measured on B200): the tensor core reads fp32 operands by
+// truncating them to TF32, and its accumulator rounds toward zero, a bias that compounds through
+// deep networks. Both are handled explicitly:
+// * MGC_PREC_TF32: A is loaded through a TFLOAT32 tensor map, which rounds it to the nearest
+//   TF32 value; each K step issues A*B_lo + A*B_hi (B exact to fp32), so the only operand error
+//   is the unbiased rounding of the activations.
+// * MGC_PREC_3XTF32 ("strict"): the epilogue warps split the raw A tile into hi = RN_tf32(A) and
+//   lo = A - hi in shared memory; each K step issues A_lo*B_hi + A_hi*B_lo + A_hi*B_hi.
+// * Accumulator promotion: every K block writes its products into a fresh TMEM region (double
+//   buffered); the four epilogue warps add each region into fp32 registers with round-to-nearest
+//   while the tensor core works on the next block. In strict mode each of the four K=8 steps of a
+//   block gets its own region, so no tensor-core accumulation chain is longer than one step.
+//
+// Roles: warp 0 lane 0 issues TMA; warp 1 allocates TMEM and lane 0 issues tcgen05.mma; warps 2-5
+// (128 threads, one TMEM lane each) split A (strict), drain TMEM, and run the epilogue.
+//
+// Every wait on an mbarrier is bounded (about a second of clock cycles); on timeout the kernel
+// records MGC_CUDA_TIMEOUT in the error word, drains what it issued, frees its TMEM and returns.
+// No TMA multicast is used anywhere.
 #pragma once
+
+#include <cuda.h>
+#include <cudaTypedefs.h>
+#include <string.h>
 
 #include "common.cuh"
 #include "gemm_simt.cuh"
+#include "kernels_norm.cuh"
 
 namespace mgc {
+namespace umma {
 
+constexpr int BM = 128;
+constexpr int BK = 32;                       // fp32 elements per K block: one 128-byte swizzle row
+constexpr uint32_t A_TILE_BYTES = BM * BK * 4;
+constexpr long long WAIT_LIMIT_CYCLES = 1ll << 31;  // ~1.1 s at 1.9 GHz
+
+enum Mode { TF32 = 0, STRICT = 1 };
+
+struct Params {
+    CUtensorMap tmA;
+    CUtensorMap tmB;
+    CUtensorMap tmBlo;
+    int M, N, num_kb, n_tiles;
+    int im2col;
+    int KW, DH, DW, cblocks;         // im2col: K block kb -> (kh, kw, channel block)
+    int OH, OW, SH, SW, PT, PL;      // im2col: output pixel -> window origin
+    float *c;
+    long long ldc;
+    const float *bias;
+    const float *res;
+    long long ldr;
+    float alpha, lo, hi;
+    int act;
+    int *err;
+};
+
+// ---- PTX wrappers -----------------------------------------------------------------------------
+__device__ __forceinline__ uint32_t smem_addr(const void *p) {
+    return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+
+__device__ __forceinline__ void mbar_init(uint64_t *bar, uint32_t count) {
+    asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_addr(bar)), "r"(count) : "memory");
+}
+
+__device__ __forceinline__ void mbar_expect_tx(uint64_t *bar, uint32_t bytes) {
+    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_addr(bar)), "r"(bytes)
+                 : "memory");
+}
+
+__device__ __forceinline__ void mbar_arrive(uint64_t *bar) {
+    asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_addr(bar)) : "memory");
+}
+
+__device__ __forceinline__ bool mbar_try_wait(uint64_t *bar, uint32_t parity) {
+    uint32_t done;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}\n"
+        : "=r"(done)
+        : "r"(smem_addr(bar)), "r"(parity)
+        : "memory");
+    return done != 0;
+}
+
+// Bounded wait for the phase with parity `parity` to complete. Returns false on timeout.
+__device__ __forceinline__ bool mbar_wait(uint64_t *bar, uint32_t parity) {
+    if (mbar_try_wait(bar, parity)) return true;
+    const long long t0 = clock64();
+    while (!mbar_try_wait(bar, parity)) {
+        if (clock64() - t0 > WAIT_LIMIT_CYCLES) return false;
+    }
+    return true;
+}
+
+__device__ __forceinline__ void fence_barrier_init() {
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+}
+
+__device__ __forceinline__ void fence_proxy_async_smem() {
+    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+}
+
+__device__ __forceinline__ void tma_load_2d(void *dst, const CUtensorMap *map, uint64_t *bar, int x, int y) {
+    asm volatile(
+        "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes"
+        " [%0], [%1, {%3, %4}], [%2];"
+        ::"r"(smem_addr(dst)), "l"(reinterpret_cast<uint64_t>(map)), "r"(smem_addr(bar)), "r"(x), "r"(y)
+        : "memory");
+}
+
+__device__ __forceinline__ void tma_load_im2col_4d(void *dst, const CUtensorMap *map, uint64_t *bar, int c, int w,
+                                                   int h, int n, uint16_t off_w, uint16_t off_h) {
+    asm volatile(
+        "cp.async.bulk.tensor.4d.shared::cluster.global.im2col.mbarrier::complete_tx::bytes"
+        " [%0], [%1, {%3, %4, %5, %6}], [%2], {%7, %8};"
+        ::"r"(smem_addr(dst)), "l"(reinterpret_cast<uint64_t>(map)), "r"(smem_addr(bar)), "r"(c), "r"(w), "r"(h),
+        "r"(n), "h"(off_w), "h"(off_h)
+        : "memory");
+}
+
+__device__ __forceinline__ void tmem_alloc(uint32_t *slot, uint32_t cols) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_addr(slot)),
+                 "r"(cols)
+                 : "memory");
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+}
+
+__device__ __forceinline__ void tmem_dealloc(uint32_t taddr, uint32_t cols) {
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(taddr), "r"(cols) : "memory");
+}
+
+__device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
+__device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
+
+// K-major operand in 128B-swizzled rows of 128 bytes, 8-row groups 1024 bytes apart.
+__device__ __forceinline__ uint64_t sw128_desc(uint32_t saddr) {
+    return (uint64_t)((saddr >> 4) & 0x3FFFu)      // start address
+           | ((uint64_t)1 << 16)                    // leading byte offset (unused for swizzled K-major)
+           | ((uint64_t)(1024 >> 4) << 32)          // stride byte offset: 8 rows x 128 B
+           | ((uint64_t)1 << 46)                    // descriptor version (sm_100)
+           | ((uint64_t)2 << 61);                   // 128-byte swizzle
+}
+
+// kind::tf32, fp32 accumulate, both operands K-major, M = 128.
+__host__ __device__ constexpr uint32_t instr_desc_tf32(int n) {
+    return (1u << 4)                 // D format f32
+           | (2u << 7)               // A format tf32
+           | (2u << 10)              // B format tf32
+           | ((uint32_t)(n >> 3) << 17)
+           | ((uint32_t)(BM >> 4) << 24);
+}
+
+__device__ __forceinline__ void mma_tf32(uint32_t tmem_d, uint64_t adesc, uint64_t bdesc, uint32_t idesc,
+                                         uint32_t accumulate) {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "setp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::1.kind::tf32 [%0], %1, %2, %3, p;\n\t}\n"
+        ::"r"(tmem_d), "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate)
+        : "memory");
+}
+
+__device__ __forceinline__ void mma_commit(uint64_t *bar) {
+    asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_addr(bar))
+                 : "memory");
+}
+
+// 16 consecutive fp32 columns of this thread's TMEM lane.
+__device__ __forceinline__ void tmem_ld16(uint32_t taddr, uint32_t (&r)[16]) {
+    asm volatile(
+        "tcgen05.ld.sync.aligned.32x32b.x16.b32 "
+        "{%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15}, [%16];"
+        : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+          "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
+        : "r"(taddr));
+}
+
+__device__ __forceinline__ void tmem_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
+
+__device__ __forceinline__ void set_error(int *err, int code) {
+    if (err) atomicExch(err, code);
+}
+
+// Round fp32 to the nearest TF32 value (10 explicit mantissa bits; ties away from zero), the
+// rounding a TFLOAT32 tensor map applies on load.
+__device__ __forceinline__ float tf32_hi(float x) {
+    uint32_t b = __float_as_uint(x);
+    uint32_t r = (b + 0x1000u) & 0xFFFFE000u;
+    return ((b & 0x7F800000u) == 0x7F800000u) ? x : __uint_as_float(r);
+}
+
+template <int BN, int MODE>
+struct Cfg {
+    static constexpr int REGIONS = MODE == STRICT ? 4 : 1;  // TMEM regions per K block
+    static constexpr uint32_t B_TILE_BYTES = BN * BK * 4;
+    // stage: A | B_hi | B_lo (| A_lo)
+    static constexpr uint32_t STAGE_BYTES = A_TILE_BYTES + 2 * B_TILE_BYTES + (MODE == STRICT ? A_TILE_BYTES : 0);
+    static constexpr int STAGES = (196608 / STAGE_BYTES) < 2 ? 2 : (196608 / STAGE_BYTES) > 8 ? 8 : (196608 / STAGE_BYTES);
+    static constexpr uint32_t TMEM_COLS = 2 * REGIONS * BN;  // double-buffered
+    static constexpr uint32_t SMEM_BYTES = STAGES * STAGE_BYTES + 1024 /*align*/ + 256 /*barriers*/;
+    static_assert(TMEM_COLS <= 512 && (TMEM_COLS & (TMEM_COLS - 1)) == 0, "TMEM columns");
+};
+
+template <int BN, int MODE>
+__global__ void __launch_bounds__(192, 1) umma_gemm_kernel(const __grid_constant__ Params p) {
+    using C = Cfg<BN, MODE>;
+    constexpr int S = C::STAGES;
+    constexpr int R = C::REGIONS;
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    auto a_tile = [&](int s) { return smem + (size_t)s * C::STAGE_BYTES; };
+    auto b_tile = [&](int s) { return smem + (size_t)s * C::STAGE_BYTES + A_TILE_BYTES; };
+    auto blo_tile = [&](int s) { return smem + (size_t)s * C::STAGE_BYTES + A_TILE_BYTES + C::B_TILE_BYTES; };
+    auto alo_tile = [&](int s) { return smem + (size_t)s * C::STAGE_BYTES + A_TILE_BYTES + 2 * C::B_TILE_BYTES; };
+    uint64_t *full = reinterpret_cast<uint64_t *>(smem + (size_t)S * C::STAGE_BYTES);
+    uint64_t *empty = full + S;
+    uint64_t *split = empty + S;
+    uint64_t *tfull = split + S;      // [2] a K block's products are in TMEM buffer b
+    uint64_t *tempty = tfull + 2;     // [2] the epilogue has drained TMEM buffer b
+    uint64_t *mma_done = tempty + 2;  // every issued MMA has completed
+    uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(mma_done + 1);
+
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int tile = blockIdx.x;
+    const int n_tile = tile % p.n_tiles, m_tile = tile / p.n_tiles;
+    const int m0 = m_tile * BM, n0 = n_tile * BN;
+    const int num_kb = p.num_kb;
+
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < S; ++s) {
+            mbar_init(&full[s], 1);
+            mbar_init(&empty[s], 1);
+            mbar_init(&split[s], 128);
+        }
+        for (int b = 0; b < 2; ++b) {
+            mbar_init(&tfull[b], 1);
+            mbar_init(&tempty[b], 128);
+        }
+        mbar_init(mma_done, 1);
+        fence_barrier_init();
+    }
+    if (warp == 1) tmem_alloc(tmem_slot, C::TMEM_COLS);
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem_base = *tmem_slot;
+
+    if (warp == 0) {
+        if (lane == 0) {
+            // ---------------- TMA producer ----------------
+            int wb = 0, hb = 0, nb = 0;
+            if (p.im2col) {
+                const int hw = p.OH * p.OW;
+                nb = m0 / hw;
+                const int rem = m0 - nb * hw;
+                const int oh = rem / p.OW, ow = rem - oh * p.OW;
+                wb = ow * p.SW - p.PL;
+                hb = oh * p.SH - p.PT;
+            }
+            constexpr uint32_t bytes = A_TILE_BYTES + 2 * C::B_TILE_BYTES;
+            int issued = 0;
+            for (int kb = 0; kb < num_kb; ++kb) {
+                const int s = kb % S;
+                const int round = kb / S;
+                if (round > 0 && !mbar_wait(&empty[s], (round - 1) & 1)) {
+                    set_error(p.err, MGC_CUDA_TIMEOUT);
+                    break;
+                }
+                mbar_expect_tx(&full[s], bytes);
+                if (p.im2col) {
+                    const int cb = kb % p.cblocks;
+                    const int t = kb / p.cblocks;
+                    const int kw = t % p.KW, kh = t / p.KW;
+                    tma_load_im2col_4d(a_tile(s), &p.tmA, &full[s], cb * BK, wb, hb, nb, (uint16_t)(kw * p.DW),
+                                       (uint16_t)(kh * p.DH));
+                } else {
+                    tma_load_2d(a_tile(s), &p.tmA, &full[s], kb * BK, m0);
+                }
+                tma_load_2d(b_tile(s), &p.tmB, &full[s], kb * BK, n0);
+                tma_load_2d(blo_tile(s), &p.tmBlo, &full[s], kb * BK, n0);
+                ++issued;
+            }
+            // the copies of the last (up to S) issued K blocks must have landed before exit
+            for (int kb = issued - 1; kb >= 0 && kb >= issued - S; --kb) {
+                if (!mbar_wait(&full[kb % S], (kb / S) & 1)) set_error(p.err, MGC_CUDA_TIMEOUT);
+            }
+        }
+    } else if (warp == 1) {
+        if (lane == 0) {
+            // ---------------- MMA issuer ----------------
+            constexpr uint32_t idesc = instr_desc_tf32(BN);
+            for (int kb = 0; kb < num_kb; ++kb) {
+                const int s = kb % S;
+                const int b = kb & 1;
+                if (!mbar_wait(MODE == STRICT ? &split[s] : &full[s], (kb / S) & 1)) {
+                    set_error(p.err, MGC_CUDA_TIMEOUT);
+                    break;
+                }
+                if (kb >= 2 && !mbar_wait(&tempty[b], ((kb >> 1) - 1) & 1)) {
+                    set_error(p.err, MGC_CUDA_TIMEOUT);
+                    break;
+                }
+                tc_fence_after();
+                const uint32_t a_addr = smem_addr(a_tile(s)), b_addr = smem_addr(b_tile(s));
+                const uint32_t bl_addr = smem_addr(blo_tile(s)), al_addr = smem_addr(alo_tile(s));
+                const uint32_t dbase = tmem_base + (uint32_t)(b * R * BN);
+#pragma unroll
+                for (int k = 0; k < BK / 8; ++k) {  // 8 tf32 = 32 bytes per MMA
+                    const uint64_t ad = sw128_desc(a_addr + k * 32), bd = sw128_desc(b_addr + k * 32);
+                    const uint64_t bld = sw128_desc(bl_addr + k * 32);
+                    if (MODE == STRICT) {
+                        const uint32_t d = dbase + (uint32_t)(k * BN);  // own region per K step
+                        const uint64_t ald = sw128_desc(al_addr + k * 32);
+                        mma_tf32(d, ald, bd, idesc, 0u);    // A_lo * B_hi (fresh region)
+                        mma_tf32(d, ad, bld, idesc, 1u);    // A_hi * B_lo
+                        mma_tf32(d, ad, bd, idesc, 1u);     // A_hi * B_hi
+                    } else {
+                        mma_tf32(dbase, ad, bld, idesc, k > 0 ? 1u : 0u);  // A * B_lo
+                        mma_tf32(dbase, ad, bd, idesc, 1u);                // A * B_hi
+                    }
+                }
+                mma_commit(&empty[s]);   // shared-memory slot free once these MMAs read it
+                mma_commit(&tfull[b]);   // TMEM buffer b holds this K block's products
+            }
+            mma_commit(mma_done);
+            if (!mbar_wait(mma_done, 0)) set_error(p.err, MGC_CUDA_TIMEOUT);
+        }
+    } else {
+        // ---------------- epilogue warps: A split (strict), TMEM drain, epilogue ----------------
+        const int et = threadIdx.x - 64;  // 0..127
+        const int q = warp & 3;           // TMEM lane quadrant this warp may access
+        const uint32_t lane_base = tmem_base + ((uint32_t)(q * 32) << 16);
+        float acc[BN];
+#pragma unroll
+        for (int j = 0; j < BN; ++j) acc[j] = 0.0f;
+        bool ok = true;
+        auto drain = [&](int kb) -> bool {
+            const int b = kb & 1;
+            if (!mbar_wait(&tfull[b], (kb >> 1) & 1)) return false;
+            tc_fence_after();
+#pragma unroll
+            for (int r = 0; r < R; ++r) {
+#pragma unroll
+                for (int c0 = 0; c0 < BN; c0 += 16) {
+                    uint32_t v[16];
+                    tmem_ld16(lane_base + (uint32_t)(b * R * BN + r * BN + c0), v);
+                    tmem_wait_ld();
+#pragma unroll
+                    for (int j = 0; j < 16; ++j) acc[c0 + j] += __uint_as_float(v[j]);
+                }
+            }
+            tc_fence_before();
+            mbar_arrive(&tempty[b]);
+            return true;
+        };
+        for (int kb = 0; kb < num_kb && ok; ++kb) {
+            if (MODE == STRICT) {
+                const int s = kb % S;
+                if (!mbar_wait(&full[s], (kb / S) & 1)) {
+                    ok = false;
+                    break;
+                }
+                float4 *a4 = reinterpret_cast<float4 *>(a_tile(s));
+                float4 *l4 = reinterpret_cast<float4 *>(alo_tile(s));
+#pragma unroll
+                for (int i = 0; i < (int)(A_TILE_BYTES / 16 / 128); ++i) {
+                    const int idx = i * 128 + et;
+                    const float4 v = a4[idx];
+                    float4 h, l;
+                    h.x = tf32_hi(v.x); h.y = tf32_hi(v.y); h.z = tf32_hi(v.z); h.w = tf32_hi(v.w);
+                    l.x = v.x - h.x; l.y = v.y - h.y; l.z = v.z - h.z; l.w = v.w - h.w;
+                    a4[idx] = h;
+                    l4[idx] = l;
+                }
+                fence_proxy_async_smem();
+                mbar_arrive(&split[s]);
+                if (kb >= 1 && !drain(kb - 1)) ok = false;  // one block behind the split
+            } else {
+                if (!drain(kb)) ok = false;
+            }
+        }
+        if (MODE == STRICT && ok && num_kb >= 1 && !drain(num_kb - 1)) ok = false;
+        if (!ok) set_error(p.err, MGC_CUDA_TIMEOUT);
+        // epilogue: act(alpha * acc + bias + residual)
+        const long long m = (long long)m0 + q * 32 + lane;
+        if (ok && m < p.M) {
+            float *crow = p.c + m * p.ldc;
+            const float *rrow = p.res ? p.res + m * p.ldr : nullptr;
+            const bool vec = ((p.ldc & 3) == 0) && ((reinterpret_cast<uintptr_t>(p.c) & 15) == 0) &&
+                             (!p.res || (((p.ldr & 3) == 0) && ((reinterpret_cast<uintptr_t>(p.res) & 15) == 0))) &&
+                             ((reinterpret_cast<uintptr_t>(p.bias) & 15) == 0);
+#pragma unroll
+            for (int c0 = 0; c0 < BN; c0 += 4) {
+                const int nb = n0 + c0;
+                if (vec && nb + 4 <= p.N) {
+                    float4 o;
+                    o.x = p.alpha * acc[c0 + 0];
+                    o.y = p.alpha * acc[c0 + 1];
+                    o.z = p.alpha * acc[c0 + 2];
+                    o.w = p.alpha * acc[c0 + 3];
+                    if (p.bias) {
+                        const float4 bv = __ldg(reinterpret_cast<const float4 *>(p.bias + nb));
+                        o.x += bv.x; o.y += bv.y; o.z += bv.z; o.w += bv.w;
+                    }
+                    if (rrow) {
+                        const float4 rv = *reinterpret_cast<const float4 *>(rrow + nb);
+                        o.x += rv.x; o.y += rv.y; o.z += rv.z; o.w += rv.w;
+                    }
+                    o.x = apply_act(o.x, p.act, p.lo, p.hi);
+                    o.y = apply_act(o.y, p.act, p.lo, p.hi);
+                    o.z = apply_act(o.z, p.act, p.lo, p.hi);
+                    o.w = apply_act(o.w, p.act, p.lo, p.hi);
+                    *reinterpret_cast<float4 *>(crow + nb) = o;
+                } else {
+#pragma unroll
+                    for (int j = 0; j < 4; ++j) {
+                        const int n = nb + j;
+                        if (n < p.N) {
+                            float x = p.alpha * acc[c0 + j];
+                            if (p.bias) x += p.bias[n];
+                            if (rrow) x += rrow[n];
+                            crow[n] = apply_act(x, p.act, p.lo, p.hi);
+                        }
+                    }
+                }
+            }
+        }
+    }
+    tc_fence_before();
+    __syncthreads();
+    if (warp == 1) {
+        tc_fence_after();
+        tmem_dealloc(tmem_base, C::TMEM_COLS);
+    }
+}
+
+// ---- host side ---------------------------------------------------------------------------------
+inline PFN_cuTensorMapEncodeTiled_v12000 encode_tiled_fn() {
+    static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+    if (!fn) {
+        cudaDriverEntryPointQueryResult q;
+        void *ptr = nullptr;
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &ptr, cudaEnableDefault, &q) == cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(ptr);
+        else
+            cudaGetLastError();
+    }
+    return fn;
+}
+
+inline PFN_cuTensorMapEncodeIm2col_v12000 encode_im2col_fn() {
+    static PFN_cuTensorMapEncodeIm2col_v12000 fn = nullptr;
+    if (!fn) {
+        cudaDriverEntryPointQueryResult q;
+        void *ptr = nullptr;
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeIm2col", &ptr, cudaEnableDefault, &q) == cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            fn = reinterpret_cast<PFN_cuTensorMapEncodeIm2col_v12000>(ptr);
+        else
+            cudaGetLastError();
+    }
+    return fn;
+}
+
+// Row-major fp32 matrix [rows, cols] with row stride `ld` elements, boxes of 32 x box_rows.
+// `tf32` selects the TFLOAT32 element type, which rounds to the nearest TF32 value on load.
+inline bool make_map_2d(CUtensorMap *map, const void *base, long long rows, long long cols, long long ld,
+                        int box_rows, bool tf32 = false) {
+    auto fn = encode_tiled_fn();
+    if (!fn) return false;
+    cuuint64_t dims[2] = {(cuuint64_t)cols, (cuuint64_t)rows};
+    cuuint64_t strides[1] = {(cuuint64_t)(ld * 4)};
+    cuuint32_t box[2] = {(cuuint32_t)BK, (cuuint32_t)box_rows};
+    cuuint32_t estr[2] = {1, 1};
+    CUresult r = fn(map, tf32 ? CU_TENSOR_MAP_DATA_TYPE_TFLOAT32 : CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2,
+                    const_cast<void *>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                    CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    return r == CUDA_SUCCESS;
+}
+
+// NHWC fp32 image, im2col boxes of 32 channels x 128 output pixels.
+inline bool make_map_im2col(CUtensorMap *map, const GemmParams &g, bool tf32) {
+    auto fn = encode_im2col_fn();
+    if (!fn) return false;
+    const long long nimg = (long long)g.M / ((long long)g.OH * g.OW);
+    cuuint64_t dims[4] = {(cuuint64_t)g.C, (cuuint64_t)g.W, (cuuint64_t)g.H, (cuuint64_t)nimg};
+    cuuint64_t strides[3] = {(cuuint64_t)g.C * 4, (cuuint64_t)g.W * g.C * 4, (cuuint64_t)g.H * g.W * g.C * 4};
+    // bounding box of window origins: from -pad to the last output's origin, W then H
+    int lower[2] = {-g.PL, -g.PT};
+    int upper[2] = {(g.OW - 1) * g.SW - g.PL - (g.W - 1), (g.OH - 1) * g.SH - g.PT - (g.H - 1)};
+    cuuint32_t estr[4] = {1, (cuuint32_t)g.SW, (cuuint32_t)g.SH, 1};
+    CUresult r = fn(map, tf32 ? CU_TENSOR_MAP_DATA_TYPE_TFLOAT32 : CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4,
+                    const_cast<float *>(g.a), dims, strides, lower, upper, BK, BM, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                    CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    return r == CUDA_SUCCESS;
+}
+
+template <int BN, int MODE>
+inline int launch(const Params &p, int tiles, cudaStream_t stream) {
+    using C = Cfg<BN, MODE>;
+    // per device (the attribute belongs to the current context); cheap, and allowed under capture
+    MGC_CHECK_CUDA(cudaFuncSetAttribute(umma_gemm_kernel<BN, MODE>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                        (int)C::SMEM_BYTES));
+    umma_gemm_kernel<BN, MODE><<<tiles, 192, C::SMEM_BYTES, stream>>>(p);
+    return check_launch("umma_gemm_kernel");
+}
+
+}  // namespace umma
+
+// Whether the tensor-core kernel takes this GEMM, and its launch. Requirements: tf32 or 3xtf32
+// precision, no batch dimensions, a constant K-major B in the layout the lowering provides
+// (b_umma + b_umma_lo), A as a unit-stride row-major matrix or an NHWC im2col operand with
+// 16-byte aligned rows, bias per column (or none), fp32 output.
 inline int try_gemm_umma(const GemmParams &p, cudaStream_t stream, int *taken) {
-    (void)p;
-    (void)stream;
     *taken = 0;
+    if (p.precision == MGC_PREC_FP32 || p.nb != 0 || !p.b_umma || !p.b_umma_lo || p.M <= 0 || p.N <= 0 || p.K <= 0)
+        return MGC_CUDA_OK;
+    if (p.bias && p.bias_mode != 1) return MGC_CUDA_OK;
+    const bool strict = p.precision == MGC_PREC_3XTF32;
+    if ((reinterpret_cast<uintptr_t>(p.a) & 15) || (reinterpret_cast<uintptr_t>(p.b_umma) & 15) ||
+        (reinterpret_cast<uintptr_t>(p.b_umma_lo) & 15))
+        return MGC_CUDA_OK;
+    umma::Params u;
+    memset(&u, 0, sizeof u);
+    u.M = p.M;
+    u.N = p.N;
+    // TF32 mode rounds A to nearest while loading; strict mode loads raw fp32 and splits it
+    const bool a_tf32 = !strict;
+    int kp;  // K extent of the B operand (padded)
+    if (p.a_kind == MGC_STRIDED) {
+        if (p.a_cs != 1 || (p.a_rs & 3) || p.a_rs < p.K || (p.K & 3)) return MGC_CUDA_OK;
+        kp = p.K;
+        if (!umma::make_map_2d(&u.tmA, p.a, p.M, p.K, p.a_rs, umma::BM, a_tf32)) return MGC_CUDA_OK;
+        u.im2col = 0;
+        u.num_kb = (int)ceil_div(p.K, umma::BK);
+    } else if (p.a_kind == MGC_CONV_NHWC) {
+        if (p.cg != p.C || p.c_off != 0 || (p.C & 3) || p.b_cpad <= 0) return MGC_CUDA_OK;
+        const int lw = -p.PL, lh = -p.PT;
+        const int uw = (p.OW - 1) * p.SW - p.PL - (p.W - 1), uh = (p.OH - 1) * p.SH - p.PT - (p.H - 1);
+        if (lw < -128 || lh < -128 || uw > 127 || uh > 127 || uw < -128 || uh < -128) return MGC_CUDA_OK;
+        if (p.SW > 8 || p.SH > 8 || (p.KW - 1) * p.DW > 65535 || (p.KH - 1) * p.DH > 65535) return MGC_CUDA_OK;
+        if (p.M % (p.OH * p.OW)) return MGC_CUDA_OK;
+        if (!umma::make_map_im2col(&u.tmA, p, a_tf32)) return MGC_CUDA_OK;
+        u.im2col = 1;
+        u.cblocks = p.b_cpad / umma::BK;
+        u.num_kb = p.KH * p.KW * u.cblocks;
+        kp = p.KH * p.KW * p.b_cpad;
+        u.KW = p.KW; u.DH = p.DH; u.DW = p.DW;
+        u.OH = p.OH; u.OW = p.OW; u.SH = p.SH; u.SW = p.SW; u.PT = p.PT; u.PL = p.PL;
+    } else {
+        return MGC_CUDA_OK;
+    }
+    // strict mode keeps four TMEM regions per K block, which fits only N tiles of 64
+    const int bn = (strict || p.N <= 64) ? 64 : 128;
+    if (!umma::make_map_2d(&u.tmB, p.b_umma, p.N, kp, kp, bn)) return MGC_CUDA_OK;
+    if (!umma::make_map_2d(&u.tmBlo, p.b_umma_lo, p.N, kp, kp, bn)) return MGC_CUDA_OK;
+    u.n_tiles = (int)ceil_div(p.N, bn);
+    const long long tiles = (long long)u.n_tiles * ceil_div(p.M, umma::BM);
+    if (tiles > 0x7FFFFFFF) return MGC_CUDA_OK;
+    u.c = p.c; u.ldc = p.ldc; u.bias = p.bias; u.res = p.res; u.ldr = p.ldr;
+    u.alpha = p.alpha; u.lo = p.lo; u.hi = p.hi; u.act = p.act;
+    u.err = p.err;
+    int st;
+    if (strict) st = umma::launch<64, umma::STRICT>(u, (int)tiles, stream);
+    else if (bn == 64) st = umma::launch<64, umma::TF32>(u, (int)tiles, stream);
+    else st = umma::launch<128, umma::TF32>(u, (int)tiles, stream);
+    if (st != MGC_CUDA_OK) return st;
+    *taken = 1;
     return MGC_CUDA_OK;
 }
 

@@ -87,6 +87,9 @@ inline int decode_gemm(const mgc_cuda_launch &L, const Bases &bases, GemmParams 
     MGC_RESOLVE(L.r[3], p.bias);
     MGC_RESOLVE(L.r[4], p.res);
     MGC_RESOLVE(L.r[5], p.b_lo);
+    MGC_RESOLVE(L.r[6], p.b_umma);
+    MGC_RESOLVE(L.r[7], p.b_umma_lo);
+    p.b_cpad = (int)i[50];
     if (!p.a || !p.b || !p.c) return fail(MGC_CUDA_BAD_ARGUMENT, "gemm: missing operand");
     return MGC_CUDA_OK;
 }
@@ -189,6 +192,7 @@ inline int launch_record(const mgc_cuda_launch &L, const int64_t *aux, int64_t a
     case MGC_K_GEMM: {
         GemmParams p;
         MGC_CHECK(decode_gemm(L, bases, p));
+        p.err = status_dev;
         st = run_gemm(p, stream);
         break;
     }

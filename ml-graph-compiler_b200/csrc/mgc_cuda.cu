@@ -135,8 +135,12 @@ int create(Model &m, const mgc_cuda_launch *launches, int n_launches, const int6
 int finish(Model &m) {
     MGC_CHECK_CUDA(cudaMemcpyAsync(m.status_host, m.status_dev, sizeof(int), cudaMemcpyDeviceToHost, m.stream));
     MGC_CHECK_CUDA(cudaStreamSynchronize(m.stream));
-    if (*m.status_host == MGC_CUDA_GATHER_OOB)
+    const int status = *m.status_host;
+    if (status == MGC_CUDA_GATHER_OOB)
         return fail(MGC_CUDA_GATHER_OOB, "compiled model reported an out-of-range Gather index");
+    if (status == MGC_CUDA_TIMEOUT)
+        return fail(MGC_CUDA_TIMEOUT, "a tensor-core kernel gave up on a bounded wait (results invalid)");
+    if (status != 0) return fail(status, "device status %d", status);
     return MGC_CUDA_OK;
 }
 
@@ -308,6 +312,7 @@ int mgc_cuda_gemm(int M, int N, int K, int batch, const float *a, int64_t a_rs, 
     p.c = c; p.ldc = ldc;
     p.alpha = alpha; p.beta = beta; p.bias = bias; p.bias_mode = bias ? bias_mode : 0;
     p.res = res; p.ldr = ldr; p.act = act; p.lo = lo; p.hi = hi; p.precision = precision;
+    if (batch == 1) p.nb = 0;
     return run_gemm(p, (cudaStream_t)stream);
 }
 

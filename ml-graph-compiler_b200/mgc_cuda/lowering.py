@@ -714,6 +714,29 @@ class CudaEmitter:
             lo_off = self.weights.add(lo, key=(key, "lo"))
         return (SPACE_WEIGHTS, 0, hi_off), (SPACE_WEIGHTS, 0, lo_off), 1, k
 
+    @staticmethod
+    def _umma_b(bref: RefT, blo: RefT) -> dict[str, RefT]:
+        """A constant B stored by ``_kmajor_b`` is already in the tensor-core layout."""
+        return {"b_umma": bref, "b_umma_lo": blo} if blo != NO_REF else {}
+
+    def _kmajor_conv_padded(self, w_hwio: np.ndarray, key: Any) -> tuple[RefT, RefT, int]:
+        """Tensor-core layout of HWIO convolution weights for im2col loads: [CO][KH][KW][Cp] with
+        the channel axis zero-padded to a multiple of 32 (one K block per filter tap and channel
+        block). Returns (hi ref, lo ref, Cp)."""
+        kh, kw, cg, kg = w_hwio.shape
+        cp = (cg + 31) // 32 * 32
+        if cp == cg:  # same bytes as the plain K-major layout
+            hi, lo, _, _ = self._kmajor_b(w_hwio.reshape(kh * kw * cg, kg), key)
+            return hi, lo, cp
+        pkey = ("padded", key)
+        if pkey not in self.weights.by_key:
+            full = np.zeros((kg, kh, kw, cp), np.float32)
+            full[:, :, :, :cg] = np.transpose(np.asarray(w_hwio, np.float32), (3, 0, 1, 2))
+            hi, lo = tf32_split(full)
+            self.weights.add(hi, key=pkey)
+            self.weights.add(lo, key=(pkey, "lo"))
+        return (SPACE_WEIGHTS, 0, self.weights.by_key[pkey]), (SPACE_WEIGHTS, 0, self.weights.by_key[(pkey, "lo")]), cp
+
     def _gemm(
         self,
         m: int,
@@ -744,17 +767,23 @@ class CudaEmitter:
         res: RefT = NO_REF,
         ldr: int = 0,
         act: tuple[int, float, float] = (0, 0.0, 6.0),
+        b_umma: RefT = NO_REF,
+        b_umma_lo: RefT = NO_REF,
+        b_cpad: int = 0,
     ) -> None:
         """K_GEMM slots: i[0..2] M, N, K; i[3] batch dims; i[4..7] batch extents; i[8..11],
         i[12..15], i[16..19], i[20..23] per-dimension batch strides of A, B, C, residual;
         i[24..26] A kind, row stride, column stride; i[27..40] conv geometry H, W, C, KH, KW, SH,
         SW, DH, DW, PT, PL, OW, c_off, cg; i[41..43] B kind, row stride, column stride; i[44] ldc;
         i[45] bias mode; i[46] ldr; i[47] activation; i[48] precision; i[49] OH.
-        f[0..3] alpha, beta, clip lo, clip hi. r[0] A, r[1] B, r[2] C, r[3] bias, r[4] residual,
-        r[5] residual of a split constant B."""
+        i[50] padded channel count of the tensor-core B layout of an im2col convolution (0 when
+        B is plain K-major). f[0..3] alpha, beta, clip lo, clip hi. r[0] A, r[1] B, r[2] C,
+        r[3] bias, r[4] residual, r[5] residual of a split constant B, r[6] / r[7] the
+        tensor-core layout of a constant B (TF32-rounded part / residual), absent otherwise."""
         if len(batch) > 4:
             raise CodegenError(f"GEMM with {len(batch)} batch dimensions")
-        ints = [0] * 50
+        ints = [0] * 51
+        ints[50] = b_cpad
         ints[0], ints[1], ints[2], ints[3] = m, n, k, len(batch)
         for d in range(len(batch)):
             ints[4 + d] = batch[d]
@@ -768,7 +797,8 @@ class CudaEmitter:
         ints[41], ints[42], ints[43] = b_kind, b_rs, b_cs
         ints[44], ints[45], ints[46] = ldc, bias_mode if bias != NO_REF else 0, ldr
         ints[47], ints[48] = act[0], self._prec()
-        self.emit(K_GEMM, ints, [alpha, beta, act[1], act[2]], [a, b, c, bias, res, b_lo], count="gemm")
+        self.emit(K_GEMM, ints, [alpha, beta, act[1], act[2]], [a, b, c, bias, res, b_lo, b_umma, b_umma_lo],
+                  count="gemm")
 
     def op_FusedGemm(self, node: Node) -> None:
         a, b = node.input(0), node.input(1)
@@ -784,7 +814,7 @@ class CudaEmitter:
             bref, blo, b_rs, b_cs = self.ref(b), NO_REF, (1 if trans else n), (k if trans else 1)
         bias_v, res_v = node.optional_input(2), node.optional_input(3)
         self._gemm(
-            m, n, k, self.ref(a), k, 1, bref, b_rs, b_cs, self.ref(node.output), n, b_lo=blo,
+            m, n, k, self.ref(a), k, 1, bref, b_rs, b_cs, self.ref(node.output), n, b_lo=blo, **self._umma_b(bref, blo),
             bias=self._vector_ref(bias_v, n, "FusedGemm bias"), bias_mode=1,
             res=self.ref(res_v), ldr=n, act=self._act(node),
         )
@@ -819,7 +849,7 @@ class CudaEmitter:
                 res, ldr = self.ref(c), n
             else:
                 raise CodegenError(f"Gemm bias of shape {ct.shape} has no cuda lowering")
-        self._gemm(m, n, k, self.ref(a), a_rs, a_cs, bref, b_rs, b_cs, self.ref(node.output), n, b_lo=blo,
+        self._gemm(m, n, k, self.ref(a), a_rs, a_cs, bref, b_rs, b_cs, self.ref(node.output), n, b_lo=blo, **self._umma_b(bref, blo),
                    alpha=alpha, beta=beta, bias=bias, bias_mode=mode, res=res, ldr=ldr)
 
     def op_MatMul(self, node: Node) -> None:
@@ -841,7 +871,7 @@ class CudaEmitter:
             bref, blo, b_rs, b_cs = self._kmajor_b(data, ("kmajor", id(self._root(b)), 0))
         else:
             bref, blo, b_rs, b_cs = self.ref(b), NO_REF, n, 1
-        self._gemm(m, n, k, self.ref(a), k, 1, bref, b_rs, b_cs, self.ref(node.output), n, b_lo=blo,
+        self._gemm(m, n, k, self.ref(a), k, 1, bref, b_rs, b_cs, self.ref(node.output), n, b_lo=blo, **self._umma_b(bref, blo),
                    batch=dims, a_bs=a_bs, b_bs=b_bs, c_bs=c_bs, r_bs=[0] * len(dims))
 
     @staticmethod
@@ -894,10 +924,18 @@ class CudaEmitter:
                 xref = self.ref(x, gi * cg * 4) if pointwise else self.ref(x)
                 out_ref = self.ref(node.output, gi * kg * 4)
                 res_g = res if res == NO_REF else (res[0], res[1], res[2] + gi * kg * 4)
+                if pointwise:
+                    umma = self._umma_b(bref, blo)
+                elif group == 1:
+                    whwio = wdata[:, :, :, gi * kg : (gi + 1) * kg]
+                    uhi, ulo, cp = self._kmajor_conv_padded(whwio, ("conv", id(self._root(w)), gi))
+                    umma = {"b_umma": uhi, "b_umma_lo": ulo, "b_cpad": cp}
+                else:
+                    umma = {}
                 self._gemm(
                     nb * oh * ow, kg, kh * kw * cg, xref, c, 1, bref, b_rs, b_cs, out_ref, kout, b_lo=blo,
                     conv={**geo, "c_off": gi * cg, "cg": cg}, a_kind=STRIDED if pointwise else CONV_NHWC,
-                    bias=bias_g, bias_mode=1, res=res_g, ldr=kout, act=act,
+                    bias=bias_g, bias_mode=1, res=res_g, ldr=kout, act=act, **umma,
                 )
             else:
                 plane = oh * ow

@@ -38,19 +38,27 @@ def ref_lib() -> ctypes.CDLL | None:
     return ctypes.CDLL(str(REF_LIB)) if REF_LIB.exists() else None
 
 
+@pytest.mark.parametrize("kmajor", [False, True])
 @pytest.mark.parametrize("precision", [0, 1, 2])
-@pytest.mark.parametrize("m,n,k,act", [(1, 1000, 2048, 0), (197, 77, 129, 1), (512, 256, 64, 3), (64, 3072, 768, 4)])
-def test_gemm_vs_torch(m: int, n: int, k: int, act: int, precision: int) -> None:
+@pytest.mark.parametrize("m,n,k,act", [(1, 1000, 2048, 0), (197, 77, 129, 1), (512, 256, 64, 3), (64, 3072, 768, 4),
+                                       (300, 200, 100, 1)])
+def test_gemm_vs_torch(m: int, n: int, k: int, act: int, precision: int, kmajor: bool) -> None:
+    """Row-major and K-major B through the strided kernel ABI (exact fp32 arithmetic); the
+    tensor-core kernel is reached through models, whose constant B the lowering stores split."""
     rng = np.random.default_rng(m + n + k)
     a = rng.standard_normal((m, k)).astype(np.float32)
     b = rng.standard_normal((k, n)).astype(np.float32) * 0.05
     bias = rng.standard_normal(n).astype(np.float32)
     res = rng.standard_normal((m, n)).astype(np.float32)
-    A, B, Bi, R = dev(a), dev(b), dev(bias), dev(res)
+    A, Bi, R = dev(a), dev(bias), dev(res)
+    B = dev(np.ascontiguousarray(b.T)) if kmajor else dev(b)
+    b_rs, b_cs = (1, k) if kmajor else (n, 1)
     C = torch.empty((m, n), device="cuda")
     lib = library()
-    ok(lib.mgc_cuda_gemm(m, n, k, 1, ptr(A), k, 1, 0, ptr(B), n, 1, 0, ptr(C), n, 0, 1.0, ptr(Bi), 1, ptr(R), n,
+    ok(lib.mgc_cuda_gemm(m, n, k, 1, ptr(A), k, 1, 0, ptr(B), b_rs, b_cs, 0, ptr(C), n, 0, 1.0, ptr(Bi), 1, ptr(R), n,
                          0, 1.0, act, 0.0, 6.0, precision, stream()))
+    if kmajor:
+        B = B.t()
     torch.cuda.synchronize()
     with torch.no_grad():
         prev = torch.backends.cuda.matmul.allow_tf32
