@@ -28,7 +28,7 @@
 extern "C" {
 #endif
 
-#define MGC_CUDA_ABI_VERSION 1
+#define MGC_CUDA_ABI_VERSION 2
 
 /* ---- status codes (runtime_lib.py:142-143 maps mgc_run's 1 to GraphError) ---------------- */
 enum {
@@ -47,7 +47,9 @@ enum {
     MGC_SPACE_WEIGHTS = 2,   /* byte offset into the resident constant blob */
     MGC_SPACE_INPUT = 3,     /* graph input `index`, byte offset within it */
     MGC_SPACE_OUTPUT = 4,    /* graph output `index`, byte offset within it */
-    MGC_SPACE_RAW = 5        /* `offset` is a device address (kernel ABI / mgc_cuda_execute) */
+    MGC_SPACE_RAW = 5,       /* `offset` is a device address (kernel ABI / mgc_cuda_execute) */
+    MGC_SPACE_WORKSPACE = 6  /* byte offset into the handle's scratch buffer (im2col of narrow
+                                convolutions); not part of the planner's arena */
 };
 
 /* ---- element types (ir.py:20-29) ------------------------------------------------------------ */
@@ -104,7 +106,10 @@ enum {
     MGC_K_REDUCE = 11,      /* generic reductions with a double accumulator (c.py:736-784) */
     MGC_K_ARGMAX = 12,      /* op_ArgMax (c.py:801-821) */
     MGC_K_RANGE = 13,       /* op_Range (c.py:724-734) */
-    MGC_K_MEMCPY = 14       /* output copies of plan.copies and constant stores (c.py:1283-1285) */
+    MGC_K_MEMCPY = 14,      /* output copies of plan.copies and constant stores (c.py:1283-1285) */
+    MGC_K_IM2COL = 15       /* explicit im2col of an NHWC image into the workspace, for
+                               convolutions whose channel rows TMA cannot address (C % 4 != 0);
+                               the packing of pack_a's MGC_CONV_NHWC branch, mgc_kernels.c:103-126 */
 };
 
 typedef struct {
@@ -140,11 +145,13 @@ typedef struct {
  * it uploads `weights_bytes` of constants once, allocates the arena (`arena_bytes`, the
  * planner's MemoryPlan.arena_bytes) and device buffers for the graph inputs and outputs,
  * resolves every record's references to device addresses, and captures the launch list into a
- * CUDA Graph on its own stream. `device` is the CUDA ordinal. */
+ * CUDA Graph on its own stream. `workspace_bytes` sizes the scratch buffer that MGC_SPACE_WORKSPACE
+ * references point into (0 when no launch uses one). `device` is the CUDA ordinal. */
 int mgc_cuda_create(const mgc_cuda_launch *launches, int n_launches, const int64_t *aux,
                     int64_t aux_len, const void *weights_host, int64_t weights_bytes,
-                    int64_t arena_bytes, const mgc_cuda_io *inputs, int n_inputs,
-                    const mgc_cuda_io *outputs, int n_outputs, int device, void **handle);
+                    int64_t arena_bytes, int64_t workspace_bytes, const mgc_cuda_io *inputs,
+                    int n_inputs, const mgc_cuda_io *outputs, int n_outputs, int device,
+                    void **handle);
 
 /* Replaces `int mgc_run(const void *const *inputs, void *const *outputs, A, W)` (c.py:1311-1312,
  * called at runtime_lib.py:135-140): copies each host input to the device (pinned host memory

@@ -66,6 +66,25 @@ inline int dtype_size(int dt) {
 
 inline int64_t ceil_div(int64_t a, int64_t b) { return (a + b - 1) / b; }
 
+// Number of SMs of the current device (cached per device ordinal).
+inline int sm_count() {
+    static int counts[64] = {0};
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) {
+        cudaGetLastError();
+        return 148;
+    }
+    if (!counts[dev]) {
+        int n = 0;
+        if (cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || n <= 0) {
+            cudaGetLastError();
+            n = 148;
+        }
+        counts[dev] = n;
+    }
+    return counts[dev];
+}
+
 // Grid size for a grid-stride loop over `n` items: a multiple of the SM count (148 on B200),
 // capped, never zero.
 inline unsigned grid_for(int64_t n, int threads, int sms = 148, int per_sm = 8) {

@@ -382,6 +382,48 @@ __global__ void __launch_bounds__(256) tile_kernel(const __grid_constant__ TileP
 }
 
 // ---------------------------------------------------------------------------------------------
+// explicit im2col of an NHWC image: out[m][k], m = (image, oh, ow), k = (kh, kw, c) for
+// k < KH*KW*cg and zero up to the row length kp (a multiple of 4); rows of kp fp32
+// ---------------------------------------------------------------------------------------------
+struct Im2colParams {
+    int N, H, W, C, KH, KW, SH, SW, DH, DW, PT, PL, OH, OW, kp, c_off, cg;
+    const float *x;
+    float *out;
+};
+
+__global__ void __launch_bounds__(256) im2col_nhwc_kernel(const __grid_constant__ Im2colParams p) {
+    const int kq = p.kp / 4;
+    const long long rows = (long long)p.N * p.OH * p.OW;
+    const long long total = rows * kq;
+    const int kreal = p.KH * p.KW * p.cg;
+    const long long stride = (long long)gridDim.x * blockDim.x;
+    for (long long e = (long long)blockIdx.x * blockDim.x + threadIdx.x; e < total; e += stride) {
+        const long long m = e / kq;
+        const int k0 = (int)(e - m * kq) * 4;
+        const long long hw = (long long)p.OH * p.OW;
+        const int img = (int)(m / hw);
+        const int pix = (int)(m - (long long)img * hw);
+        const int oh = pix / p.OW, ow = pix - oh * p.OW;
+        float v[4];
+#pragma unroll
+        for (int t = 0; t < 4; ++t) {
+            const int k = k0 + t;
+            float val = 0.0f;
+            if (k < kreal) {
+                const int kh = k / (p.KW * p.cg);
+                const int rem = k - kh * p.KW * p.cg;
+                const int kw = rem / p.cg, c = rem - kw * p.cg;
+                const int ih = oh * p.SH - p.PT + kh * p.DH, iw = ow * p.SW - p.PL + kw * p.DW;
+                if (ih >= 0 && ih < p.H && iw >= 0 && iw < p.W)
+                    val = p.x[(((long long)img * p.H + ih) * p.W + iw) * p.C + p.c_off + c];
+            }
+            v[t] = val;
+        }
+        *reinterpret_cast<float4 *>(p.out + m * p.kp + k0) = make_float4(v[0], v[1], v[2], v[3]);
+    }
+}
+
+// ---------------------------------------------------------------------------------------------
 // fill / range / gather
 // ---------------------------------------------------------------------------------------------
 template <typename T>

@@ -17,6 +17,7 @@ namespace mgc {
 struct Bases {
     char *arena = nullptr;
     char *weights = nullptr;
+    char *workspace = nullptr;
     const std::vector<char *> *inputs = nullptr;
     const std::vector<char *> *outputs = nullptr;
 };
@@ -32,6 +33,10 @@ inline int resolve(const mgc_cuda_ref &r, const Bases &b, void **out) {
     case MGC_SPACE_WEIGHTS:
         if (!b.weights) break;
         *out = b.weights + r.offset;
+        return MGC_CUDA_OK;
+    case MGC_SPACE_WORKSPACE:
+        if (!b.workspace) break;
+        *out = b.workspace + r.offset;
         return MGC_CUDA_OK;
     case MGC_SPACE_INPUT:
         if (!b.inputs || r.index < 0 || r.index >= (int)b.inputs->size()) break;
@@ -355,6 +360,21 @@ inline int launch_record(const mgc_cuda_launch &L, const int64_t *aux, int64_t a
         if (i[0] == 0) { launched = 0; break; }
         range_kernel<<<grid_for(i[0], 256), 256, 0, stream>>>(y, L.dtype, i[0], s0, dl);
         st = check_launch("range_kernel");
+        break;
+    }
+    case MGC_K_IM2COL: {
+        Im2colParams p{};
+        p.N = (int)i[0]; p.H = (int)i[1]; p.W = (int)i[2]; p.C = (int)i[3]; p.KH = (int)i[4];
+        p.KW = (int)i[5]; p.SH = (int)i[6]; p.SW = (int)i[7]; p.DH = (int)i[8]; p.DW = (int)i[9];
+        p.PT = (int)i[10]; p.PL = (int)i[11]; p.OH = (int)i[12]; p.OW = (int)i[13];
+        p.kp = (int)i[14]; p.c_off = (int)i[15]; p.cg = (int)i[16];
+        MGC_RESOLVE(L.r[0], p.x); MGC_RESOLVE(L.r[1], p.out);
+        if (p.kp <= 0 || (p.kp & 3) || (reinterpret_cast<uintptr_t>(p.out) & 15))
+            return fail(MGC_CUDA_BAD_ARGUMENT, "im2col: row length %d / output alignment", p.kp);
+        const long long total = (long long)p.N * p.OH * p.OW * (p.kp / 4);
+        if (total == 0) { launched = 0; break; }
+        im2col_nhwc_kernel<<<grid_for(total, 256), 256, 0, stream>>>(p);
+        st = check_launch("im2col_nhwc_kernel");
         break;
     }
     case MGC_K_MEMCPY: {

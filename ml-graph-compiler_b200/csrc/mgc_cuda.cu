@@ -26,6 +26,8 @@ struct Model {
     int64_t arena_bytes = 0;
     char *weights = nullptr;
     int64_t weights_bytes = 0;
+    char *workspace = nullptr;
+    int64_t workspace_bytes = 0;
     std::vector<char *> inputs, outputs;
     std::vector<int64_t> in_bytes, out_bytes;
     std::vector<mgc_cuda_launch> launches;
@@ -40,6 +42,7 @@ struct Model {
         Bases b;
         b.arena = arena;
         b.weights = weights;
+        b.workspace = workspace;
         b.inputs = &inputs;
         b.outputs = &outputs;
         return b;
@@ -63,10 +66,11 @@ struct Model {
         for (char *p : outputs) cudaFree(p);
         if (arena) cudaFree(arena);
         if (weights) cudaFree(weights);
+        if (workspace) cudaFree(workspace);
         if (status_dev) cudaFree(status_dev);
         if (status_host) cudaFreeHost(status_host);
         if (stream) cudaStreamDestroy(stream);
-        exec = nullptr; graph = nullptr; stream = nullptr; arena = nullptr; weights = nullptr;
+        exec = nullptr; graph = nullptr; stream = nullptr; arena = nullptr; weights = nullptr; workspace = nullptr;
         status_dev = nullptr; status_host = nullptr;
         inputs.clear(); outputs.clear();
     }
@@ -82,9 +86,9 @@ int alloc_bytes(char **p, int64_t n) {
 
 int create(Model &m, const mgc_cuda_launch *launches, int n_launches, const int64_t *aux,
            int64_t aux_len, const void *weights_host, int64_t weights_bytes, int64_t arena_bytes,
-           const mgc_cuda_io *inputs, int n_inputs, const mgc_cuda_io *outputs, int n_outputs,
-           int device) {
-    if (n_launches < 0 || aux_len < 0 || weights_bytes < 0 || arena_bytes < 0 || n_inputs < 0 ||
+           int64_t workspace_bytes, const mgc_cuda_io *inputs, int n_inputs, const mgc_cuda_io *outputs,
+           int n_outputs, int device) {
+    if (n_launches < 0 || aux_len < 0 || weights_bytes < 0 || arena_bytes < 0 || workspace_bytes < 0 || n_inputs < 0 ||
         n_outputs < 0 || (n_launches && !launches) || (aux_len && !aux) ||
         (weights_bytes && !weights_host))
         return fail(MGC_CUDA_BAD_ARGUMENT, "mgc_cuda_create: invalid arguments");
@@ -97,6 +101,10 @@ int create(Model &m, const mgc_cuda_launch *launches, int n_launches, const int6
     m.weights_bytes = weights_bytes;
     MGC_CHECK(alloc_bytes(&m.arena, arena_bytes));
     MGC_CHECK(alloc_bytes(&m.weights, weights_bytes));
+    if (workspace_bytes > 0) {
+        MGC_CHECK(alloc_bytes(&m.workspace, workspace_bytes));
+        m.workspace_bytes = workspace_bytes;
+    }
     if (weights_bytes)
         MGC_CHECK_CUDA(cudaMemcpy(m.weights, weights_host, (size_t)weights_bytes, cudaMemcpyHostToDevice));
     for (int k = 0; k < n_inputs; ++k) {
@@ -163,14 +171,15 @@ int mgc_cuda_device_supported(int device) {
 
 int mgc_cuda_create(const mgc_cuda_launch *launches, int n_launches, const int64_t *aux,
                     int64_t aux_len, const void *weights_host, int64_t weights_bytes,
-                    int64_t arena_bytes, const mgc_cuda_io *inputs, int n_inputs,
-                    const mgc_cuda_io *outputs, int n_outputs, int device, void **handle) {
+                    int64_t arena_bytes, int64_t workspace_bytes, const mgc_cuda_io *inputs,
+                    int n_inputs, const mgc_cuda_io *outputs, int n_outputs, int device,
+                    void **handle) {
     last_error().clear();
     if (!handle) return fail(MGC_CUDA_BAD_ARGUMENT, "mgc_cuda_create: handle is NULL");
     *handle = nullptr;
     std::unique_ptr<Model> m(new Model());
     int st = create(*m, launches, n_launches, aux, aux_len, weights_host, weights_bytes, arena_bytes,
-                    inputs, n_inputs, outputs, n_outputs, device);
+                    workspace_bytes, inputs, n_inputs, outputs, n_outputs, device);
     if (st != MGC_CUDA_OK) {
         std::string msg = last_error();
         m->release();

@@ -35,18 +35,18 @@ from ml_graph_compiler.ir import Graph, Node, TensorType, Value
 from ml_graph_compiler.memory import ALIAS_OPS, MemoryPlan, Strategy, plan_memory
 
 # ---- constants mirrored from include/mgc_cuda.h ------------------------------------------------
-SPACE_NONE, SPACE_ARENA, SPACE_WEIGHTS, SPACE_INPUT, SPACE_OUTPUT, SPACE_RAW = range(6)
+SPACE_NONE, SPACE_ARENA, SPACE_WEIGHTS, SPACE_INPUT, SPACE_OUTPUT, SPACE_RAW, SPACE_WORKSPACE = range(7)
 DTYPES = {"float32": 0, "float64": 1, "int64": 2, "int32": 3, "int8": 4, "uint8": 5, "bool": 6}
 ACTS = {"none": 0, "relu": 1, "clip": 2, "gelu": 3, "gelu_tanh": 4, "tanh": 5, "sigmoid": 6}
 STRIDED, CONV_NHWC, CONV_NCHW = 0, 2, 3
 PRECISIONS = {"fp32": 0, "tf32": 1, "strict": 2}
 K_GEMM, K_DEPTHWISE, K_POOL, K_REDUCE_MID, K_SOFTMAX, K_LAYER_NORM = 1, 2, 3, 4, 5, 6
-K_ELEMENTWISE, K_COPY, K_FILL, K_GATHER, K_REDUCE, K_ARGMAX, K_RANGE, K_MEMCPY = range(7, 15)
+K_ELEMENTWISE, K_COPY, K_FILL, K_GATHER, K_REDUCE, K_ARGMAX, K_RANGE, K_MEMCPY, K_IM2COL = range(7, 16)
 KIND_NAMES = {
     K_GEMM: "gemm", K_DEPTHWISE: "depthwise", K_POOL: "pool", K_REDUCE_MID: "reduce",
     K_SOFTMAX: "softmax", K_LAYER_NORM: "layer_norm", K_ELEMENTWISE: "elementwise",
     K_COPY: "copy", K_FILL: "fill", K_GATHER: "gather", K_REDUCE: "reduce", K_ARGMAX: "argmax",
-    K_RANGE: "range", K_MEMCPY: "memcpy",
+    K_RANGE: "range", K_MEMCPY: "memcpy", K_IM2COL: "im2col",
 }
 LAUNCH_INTS, LAUNCH_FLOATS, LAUNCH_REFS = 64, 8, 8
 # Elementwise program operations, numbered as csrc/kernels_mem.cuh EwOp.
@@ -143,6 +143,7 @@ class LoweredModel:
     aux: np.ndarray
     weights: Blob
     arena_bytes: int
+    workspace_bytes: int
     inputs: list[tuple[str, TensorType]]
     outputs: list[tuple[str, TensorType]]
     plan: MemoryPlan
@@ -222,6 +223,7 @@ class CudaEmitter:
         self.kernels: dict[str, int] = {}
         self._node = -1
         self._keep_alive: list[Value] = []
+        self.workspace_bytes = 0  # one scratch region, reused by every launch that needs one
 
     # -- references ----------------------------------------------------------------------------
     def _root(self, value: Value) -> Value:
@@ -915,12 +917,15 @@ class CudaEmitter:
         kg = kout // group
         geo = {"H": h, "W": wd, "C": c, "KH": kh, "KW": kw, "SH": g.strides[0], "SW": g.strides[1],
                "DH": g.dilations[0], "DW": g.dilations[1], "PT": pt, "PL": pl, "OH": oh, "OW": ow}
+        pointwise = kh == kw == 1 and g.strides == (1, 1) and g.pads == (0, 0, 0, 0)
+        if nhwc and group == 1 and not pointwise and cg % 4 and self.precision != "fp32":
+            self._conv_via_im2col(node, wdata, geo, nb, bias, res, act)
+            return
         for gi in range(group):
             bias_g = bias if bias == NO_REF else (bias[0], bias[1], bias[2] + gi * kg * 4)
             if nhwc:
                 wmat = wdata[:, :, :, gi * kg : (gi + 1) * kg].reshape(kh * kw * cg, kg)
                 bref, blo, b_rs, b_cs = self._kmajor_b(wmat, ("conv", id(self._root(w)), gi))
-                pointwise = kh == kw == 1 and g.strides == (1, 1) and g.pads == (0, 0, 0, 0)
                 xref = self.ref(x, gi * cg * 4) if pointwise else self.ref(x)
                 out_ref = self.ref(node.output, gi * kg * 4)
                 res_g = res if res == NO_REF else (res[0], res[1], res[2] + gi * kg * 4)
@@ -949,6 +954,29 @@ class CudaEmitter:
                     r_bs=[kout * plane], conv={**geo, "c_off": gi * cg, "cg": cg}, b_kind=CONV_NCHW,
                     bias=bias_g, bias_mode=2, res=res_g, ldr=plane, act=act,
                 )
+
+    def _conv_via_im2col(self, node: Node, w_hwio: np.ndarray, geo: dict[str, int], nb: int, bias: RefT,
+                         res: RefT, act: tuple[int, float, float]) -> None:
+        """NHWC convolution whose channel rows are not 16-byte multiples (the 3-channel stem):
+        K_IM2COL writes the [pixels, KH*KW*C] patch matrix, zero-padded to a multiple of 32
+        columns, into the workspace, and a plain GEMM consumes it.
+
+        K_IM2COL slots: i[0..13] N, H, W, C, KH, KW, SH, SW, DH, DW, PT, PL, OH, OW, i[14] row
+        length (padded K), i[15] channel offset, i[16] channels per group; r[0] x, r[1] out."""
+        kh, kw, cg, kg = w_hwio.shape
+        kreal = kh * kw * cg
+        kp = (kreal + 31) // 32 * 32
+        m = nb * geo["OH"] * geo["OW"]
+        self.workspace_bytes = max(self.workspace_bytes, m * kp * 4)
+        ws = (SPACE_WORKSPACE, 0, 0)
+        ints = [nb, geo["H"], geo["W"], geo["C"], kh, kw, geo["SH"], geo["SW"], geo["DH"], geo["DW"], geo["PT"],
+                geo["PL"], geo["OH"], geo["OW"], kp, 0, cg]
+        self.emit(K_IM2COL, ints, refs=[self.ref(node.input(0)), ws])
+        wmat = np.zeros((kp, kg), np.float32)
+        wmat[:kreal] = np.asarray(w_hwio, np.float32).reshape(kreal, kg)
+        bref, blo, b_rs, b_cs = self._kmajor_b(wmat, ("im2col", id(self._root(node.input(1)))))
+        self._gemm(m, kg, kp, ws, kp, 1, bref, b_rs, b_cs, self.ref(node.output), kg, b_lo=blo,
+                   bias=bias, bias_mode=1, res=res, ldr=kg, act=act, **self._umma_b(bref, blo))
 
     # -- pooling (c.py:1228-1253) ---------------------------------------------------------------------
     def _pool(self, node: Node, is_max: int) -> None:
@@ -989,6 +1017,7 @@ class CudaEmitter:
             aux=np.asarray(self.aux if self.aux else [0], np.int64),
             weights=self.weights,
             arena_bytes=max(self.plan.arena_bytes, 64),
+            workspace_bytes=self.workspace_bytes,
             inputs=[(v.name, v.tensor_type) for v in self.graph.inputs],
             outputs=[(name, v.tensor_type) for name, v in self.graph.named_outputs()],
             plan=self.plan,

@@ -37,7 +37,7 @@ SIGNATURES: dict[str, tuple[Any, list[Any]]] = {
     "mgc_cuda_abi_version": (_I, []),
     "mgc_cuda_last_error": (ctypes.c_char_p, []),
     "mgc_cuda_device_supported": (_I, [_I]),
-    "mgc_cuda_create": (_I, [_VP, _I, _VP, _I64, _VP, _I64, _I64, _VP, _I, _VP, _I, _I, ctypes.POINTER(_VP)]),
+    "mgc_cuda_create": (_I, [_VP, _I, _VP, _I64, _VP, _I64, _I64, _I64, _VP, _I, _VP, _I, _I, ctypes.POINTER(_VP)]),
     "mgc_cuda_run": (_I, [_VP, _VP, _VP]),
     "mgc_cuda_run_device": (_I, [_VP, _I]),
     "mgc_cuda_input_ptr": (_VP, [_VP, _I]),
@@ -136,7 +136,8 @@ class CudaCompiledModel:
         aux = np.ascontiguousarray(lowered.aux, np.int64)
         st = self.lib.mgc_cuda_create(
             ctypes.addressof(launches), len(lowered.launches), aux.ctypes.data, aux.size,
-            blob.ctypes.data, blob.nbytes, lowered.arena_bytes, ctypes.addressof(ins), len(self.inputs),
+            blob.ctypes.data, blob.nbytes, lowered.arena_bytes, lowered.workspace_bytes, ctypes.addressof(ins),
+            len(self.inputs),
             ctypes.addressof(outs), len(self.outputs), device, ctypes.byref(self._handle),
         )
         check(st, "mgc_cuda_create", self.lib)
@@ -241,6 +242,7 @@ class CudaCompiledModel:
         meta = {
             "format": "mgc-cuda-1",
             "arena_bytes": self.lowered.arena_bytes,
+            "workspace_bytes": self.lowered.workspace_bytes,
             "precision": self.lowered.precision,
             "inputs": [[n, t.dtype, list(t.shape)] for n, t in self.inputs],
             "outputs": [[n, t.dtype, list(t.shape)] for n, t in self.outputs],
@@ -269,6 +271,7 @@ class CudaCompiledModel:
             aux=np.fromfile(d / "aux.bin", dtype=np.int64),
             weights=blob,
             arena_bytes=int(meta["arena_bytes"]),
+            workspace_bytes=int(meta.get("workspace_bytes", 0)),
             inputs=io["inputs"],
             outputs=io["outputs"],
             plan=None,  # type: ignore[arg-type]

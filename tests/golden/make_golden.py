@@ -91,6 +91,9 @@ def main() -> None:
                     models[f"{case.name}|out|{k}|{sk}"] = sv
                 for sk, sv in summarize(cout[k]).items():
                     models[f"{case.name}|c|{k}|{sk}"] = sv
+                if v.size <= 4096:  # small outputs (classifier logits, pooler) are kept whole
+                    models[f"{case.name}|out|{k}|full"] = np.asarray(v)
+                    models[f"{case.name}|c|{k}|full"] = np.asarray(cout[k])
                 diff = float(np.abs(np.asarray(cout[k], np.float64) - ref[k]).max())
                 print(f"{case.name} {k}: interp {t1 - t0:.1f}s, C {t2 - t1:.1f}s, C vs interp max abs {diff:.3g}, "
                       f"|out| max {float(np.abs(ref[k]).max()):.4g}")

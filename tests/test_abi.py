@@ -44,7 +44,7 @@ def test_library_is_built_for_sm100a() -> None:
 
 def test_abi_version_and_errors_without_gpu() -> None:
     lib = runtime.library()
-    assert lib.mgc_cuda_abi_version() == 1
+    assert lib.mgc_cuda_abi_version() == 2
     # a NULL handle is rejected on the host, before any CUDA call
     assert lib.mgc_cuda_run(None, None, None) == 2
     assert "NULL" in runtime.last_error(lib)

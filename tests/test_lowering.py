@@ -31,10 +31,16 @@ def test_resnet50_o3_matches_published_structure(r50: Graph) -> None:
     """58 nodes; kernels gemm 54 / pool 1 / reduce 1 / transpose 1 / view 1; arena 7,225,344 B
     (reference benchmarks/results/ablation_cnn.json, cumulative loopfuse for resnet50)."""
     assert len(r50.nodes) == 58
-    low = lower_graph(r50)
+    low = lower_graph(r50, precision="fp32")
     assert low.kernels == {"gemm": 54, "pool": 1, "reduce": 1, "transpose": 1, "view": 1}
     assert low.arena_bytes == 7_225_344
     assert len(low.launches) == 57
+    assert low.workspace_bytes == 0
+    # on the tensor cores the 3-channel stem is fed by an explicit im2col in the workspace
+    tc = lower_graph(r50, precision="tf32")
+    assert tc.kernels == {"gemm": 54, "im2col": 1, "pool": 1, "reduce": 1, "transpose": 1, "view": 1}
+    assert tc.arena_bytes == 7_225_344
+    assert tc.workspace_bytes == 112 * 112 * 160 * 4
 
 
 def test_same_kernel_mix_and_arena_as_the_c_backend() -> None:
@@ -59,7 +65,7 @@ def test_every_arena_reference_stays_inside_the_arena(r50: Graph) -> None:
 
 
 def test_conv_launches_use_nhwc_implicit_gemm(r50: Graph) -> None:
-    low = lower_graph(r50)
+    low = lower_graph(r50, precision="fp32")
     gemms = [r for r in low.launches if r.kind == lowering.K_GEMM]
     kinds = {int(r.i[24]) for r in gemms}
     assert kinds == {lowering.STRIDED, lowering.CONV_NHWC}
@@ -104,7 +110,7 @@ def test_every_case_lowers(case: cases.Case) -> None:
     g, _ = cases.prepare(case)
     low = lower_graph(g, precision="strict")
     assert low.launches or all(n.op in lowering.ALIAS_OPS for n in g.nodes)
-    assert all(0 <= r.kind <= lowering.K_MEMCPY for r in low.launches)
+    assert all(lowering.K_GEMM <= r.kind <= lowering.K_IM2COL for r in low.launches)
 
 
 def test_algorithmic_cost_of_resnet50(r50: Graph) -> None:
