@@ -216,6 +216,23 @@ int mgc_cuda_conv_nhwc(int N, int H, int W, int C, int KH, int KW, int SH, int S
                        const float *bias, const float *res, int act, float lo, float hi,
                        float *y, int precision, void *stream);
 
+/* No counterpart in the reference. The same convolution as mgc_cuda_conv_nhwc, computed as an
+ * explicit im2col followed by an exact-fp32 GEMM, for callers that cannot allocate device memory:
+ * code that plans every byte up front and never allocates after start-up (the discipline of the
+ * reference's static arena, whose generated code allocates nothing), or code running where a
+ * cudaMalloc is not allowed or would stall other work. The im2col scratch lives in a fixed,
+ * file-scope device array of MGC_CUDA_NOALLOC_SCRATCH_BYTES (16 MiB) that every GPU loading the
+ * library holds until exit; a convolution whose patch matrix (N*OH*OW rows of KH*KW*C floats,
+ * rounded up to a multiple of 4) does not fit is rejected with MGC_CUDA_BAD_ARGUMENT. The first
+ * call on a device looks the array's device address up (cudaGetSymbolAddress), so make that first
+ * call before any stream capture. All calls share the array: calls that overlap on the GPU (other
+ * streams, other threads) race on it; serialise them. Nothing is allocated or freed. */
+#define MGC_CUDA_NOALLOC_SCRATCH_BYTES (16 * 1024 * 1024)
+int mgc_cuda_conv_nhwc_noalloc(int N, int H, int W, int C, int KH, int KW, int SH, int SW, int DH,
+                               int DW, int PT, int PL, int OH, int OW, int CO, const float *x,
+                               const float *w, const float *bias, const float *res, int act,
+                               float lo, float hi, float *y, void *stream);
+
 /* Same signatures as mgc_runtime.h:182-207, plus the stream. */
 int mgc_cuda_depthwise_nhwc(int N, int H, int W, int C, int KH, int KW, int SH, int SW, int DH,
                             int DW, int PT, int PL, int OH, int OW, const float *x, const float *w,

@@ -420,3 +420,71 @@ int mgc_cuda_layer_norm(int64_t rows, int64_t cols, const float *x, const float 
 }
 
 }  // extern "C"
+
+// ---------------------------------------------------------------------------------------------
+// Convolution without allocation: its im2col scratch is this fixed device array, shared by every
+// call (see mgc_cuda_conv_nhwc_noalloc in mgc_cuda.h for who needs it and the limits).
+// ---------------------------------------------------------------------------------------------
+static __device__ __align__(256) float g_noalloc_scratch[MGC_CUDA_NOALLOC_SCRATCH_BYTES / sizeof(float)];
+
+namespace {
+
+// Device address of g_noalloc_scratch on the current device, looked up once per device. In host
+// code the array's name is only a stand-in for the symbol, never a usable device pointer.
+int noalloc_scratch(float **out) {
+    static float *addr[64] = {nullptr};
+    int dev = 0;
+    MGC_CHECK_CUDA(cudaGetDevice(&dev));
+    if (dev < 0 || dev >= 64) return fail(MGC_CUDA_UNSUPPORTED, "device ordinal %d out of range", dev);
+    if (!addr[dev]) {
+        void *p = nullptr;
+        MGC_CHECK_CUDA(cudaGetSymbolAddress(&p, g_noalloc_scratch));
+        addr[dev] = static_cast<float *>(p);
+    }
+    *out = addr[dev];
+    return MGC_CUDA_OK;
+}
+
+}  // namespace
+
+extern "C" int mgc_cuda_conv_nhwc_noalloc(int N, int H, int W, int C, int KH, int KW, int SH, int SW,
+                                          int DH, int DW, int PT, int PL, int OH, int OW, int CO,
+                                          const float *x, const float *w, const float *bias,
+                                          const float *res, int act, float lo, float hi, float *y,
+                                          void *stream) {
+    last_error().clear();
+    if (!x || !w || !y || N < 0 || H <= 0 || W <= 0 || C <= 0 || KH <= 0 || KW <= 0 || SH <= 0 || SW <= 0 ||
+        DH <= 0 || DW <= 0 || OH < 0 || OW < 0 || CO < 0)
+        return fail(MGC_CUDA_BAD_ARGUMENT, "mgc_cuda_conv_nhwc_noalloc: bad arguments");
+    const long long rows = (long long)N * OH * OW;
+    const long long kreal = (long long)KH * KW * C;
+    const long long kp = (kreal + 3) / 4 * 4;
+    const long long bytes = rows * kp * (long long)sizeof(float);
+    if (bytes > MGC_CUDA_NOALLOC_SCRATCH_BYTES)
+        return fail(MGC_CUDA_BAD_ARGUMENT,
+                    "mgc_cuda_conv_nhwc_noalloc: the patch matrix needs %lld bytes, more than the %d-byte "
+                    "static scratch (N*OH*OW=%lld rows of %lld floats)",
+                    bytes, MGC_CUDA_NOALLOC_SCRATCH_BYTES, rows, kp);
+    if (rows == 0 || CO == 0) return MGC_CUDA_OK;
+    float *scratch = nullptr;
+    MGC_CHECK(noalloc_scratch(&scratch));
+    const cudaStream_t s = (cudaStream_t)stream;
+    // 1) patch matrix [rows][kp] into the scratch: every element written, padding columns zero
+    Im2colParams ip{};
+    ip.N = N; ip.H = H; ip.W = W; ip.C = C; ip.KH = KH; ip.KW = KW; ip.SH = SH; ip.SW = SW; ip.DH = DH; ip.DW = DW;
+    ip.PT = PT; ip.PL = PL; ip.OH = OH; ip.OW = OW; ip.kp = (int)kp; ip.c_off = 0; ip.cg = C;
+    ip.x = x;
+    ip.out = scratch;
+    im2col_nhwc_kernel<<<grid_for(rows * (kp / 4), 256), 256, 0, s>>>(ip);
+    MGC_CHECK(check_launch("im2col_nhwc_kernel"));
+    // 2) exact-fp32 GEMM: [rows, K] x HWIO weights [K, CO] with the FusedConv epilogue
+    GemmParams p{};
+    p.M = (int)rows; p.N = CO; p.K = (int)kreal;
+    p.nb = 0;
+    p.a_kind = MGC_STRIDED; p.a = scratch; p.a_rs = kp; p.a_cs = 1;
+    p.b_kind = MGC_STRIDED; p.b = w; p.b_rs = CO; p.b_cs = 1;
+    p.c = y; p.ldc = CO;
+    p.alpha = 1.0f; p.beta = 1.0f; p.bias = bias; p.bias_mode = bias ? 1 : 0;
+    p.res = res; p.ldr = CO; p.act = act; p.lo = lo; p.hi = hi; p.precision = MGC_PREC_FP32;
+    return launch_gemm_simt(p, s);
+}

@@ -58,6 +58,7 @@ SIGNATURES: dict[str, tuple[Any, list[Any]]] = {
         _I,
         [_I] * 15 + [_VP, _VP, _VP, _VP, _I, _F, _F, _VP, _I, _VP],
     ),
+    "mgc_cuda_conv_nhwc_noalloc": (_I, [_I] * 15 + [_VP, _VP, _VP, _VP, _I, _F, _F, _VP, _VP]),
     "mgc_cuda_depthwise_nhwc": (_I, [_I] * 14 + [_VP, _VP, _VP, _VP, _I, _F, _F, _VP, _VP]),
     "mgc_cuda_pool_nhwc": (_I, [_I] * 18 + [_VP, _VP, _VP]),
     "mgc_cuda_reduce_mid": (_I, [_I, _I64, _I64, _I64, _VP, _VP, _VP]),
