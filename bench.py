@@ -180,18 +180,11 @@ def main() -> None:
 
     import torch
 
-    world = int(os.environ.get("WORLD_SIZE", "1"))
-    rank = int(os.environ.get("RANK", "0"))
-    local = int(os.environ.get("LOCAL_RANK", "0"))
+    from mgc_cuda.replicas import ReplicaGroup
+
+    group = ReplicaGroup(backend="nccl", timeout_s=300)
+    world, rank, local = group.world, group.rank, group.local_rank
     torch.cuda.set_device(local)
-    dist = None
-    if world > 1:
-        import datetime
-
-        import torch.distributed as dist
-
-        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300),
-                                device_id=torch.device("cuda", local))
 
     from mgc_cuda.lowering import algorithmic_cost
     from mgc_cuda.runtime import compile_graph
@@ -206,11 +199,7 @@ def main() -> None:
     model.run({"image": x})
     stream = torch.cuda.ExternalStream(model.stream)
 
-    def barrier() -> None:
-        torch.cuda.synchronize()
-        if dist is not None:
-            dist.barrier()
-        torch.cuda.synchronize()
+    barrier = group.barrier
 
     for _ in range(args.warmup):
         model.run_device(sync=False)
@@ -223,11 +212,7 @@ def main() -> None:
         end.record(stream)
         end.synchronize()
     barrier()
-    ms = start.elapsed_time(end)
-    if dist is not None:
-        t = torch.tensor([ms], device="cuda", dtype=torch.float64)
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        ms = float(t.item())
+    ms = group.max(start.elapsed_time(end))
     ms_per_step = ms / args.steps
     value = world * args.batch * args.steps / (ms / 1e3)
 
@@ -241,11 +226,7 @@ def main() -> None:
     t0 = time.perf_counter()
     for _ in range(args.steps):
         model.run({"image": pinned_in}, out={"logits": pinned_out})
-    e2e_s = time.perf_counter() - t0
-    if dist is not None:
-        t = torch.tensor([e2e_s], device="cuda", dtype=torch.float64)
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        e2e_s = float(t.item())
+    e2e_s = group.max(time.perf_counter() - t0)
     e2e = world * args.batch * args.steps / e2e_s
 
     # dominant kernel: per-launch CUDA events (eager pass), GEMM-family nodes
@@ -325,9 +306,7 @@ def main() -> None:
                                     "sample": f"failed: {type(exc).__name__}: {exc}"[:200]}
     if rank == 0:
         print(json.dumps(line))
-    if dist is not None:
-        dist.barrier()
-        dist.destroy_process_group()
+    group.close()
 
 
 if __name__ == "__main__":
