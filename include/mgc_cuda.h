@@ -107,9 +107,13 @@ enum {
     MGC_K_ARGMAX = 12,      /* op_ArgMax (c.py:801-821) */
     MGC_K_RANGE = 13,       /* op_Range (c.py:724-734) */
     MGC_K_MEMCPY = 14,      /* output copies of plan.copies and constant stores (c.py:1283-1285) */
-    MGC_K_IM2COL = 15       /* explicit im2col of an NHWC image into the workspace, for
+    MGC_K_IM2COL = 15,      /* explicit im2col of an NHWC image into the workspace, for
                                convolutions whose channel rows TMA cannot address (C % 4 != 0);
                                the packing of pack_a's MGC_CONV_NHWC branch, mgc_kernels.c:103-126 */
+    MGC_K_PACK = 16         /* copy of a 4-D image with any strides into NHWC with the channels
+                               zero-padded to a multiple of 4, so that TMA can address its pixels
+                               (a narrow-channel convolution input, e.g. the 3-channel stem); no
+                               counterpart in the reference, whose C kernels read 3-float rows */
 };
 
 typedef struct {

@@ -70,8 +70,9 @@ struct Params {
     CUtensorMap tmR;                 // residual tile load (when tma_res)
     int tma_out, tma_res;
     int M, N, num_kb, n_tiles;
-    int im2col;
+    int im2col;                      // 0 tiled A, 1 im2col (32-channel blocks), 2 tap-packed im2col
     int KW, DH, DW, cblocks;         // im2col: K block kb -> (kh, kw, channel block)
+    int cpix, kreal;                 // tap-packed: channels per pixel (4..28), real K = KH*KW*cpix
     int OH, OW, SH, SW, PT, PL;      // im2col: output pixel -> window origin
     float *c;
     long long ldc;
@@ -185,6 +186,21 @@ __device__ __forceinline__ uint64_t sw128_desc(uint32_t saddr) {
            | ((uint64_t)1 << 46)                    // descriptor version (sm_100)
            | ((uint64_t)2 << 61);                   // 128-byte swizzle
 }
+
+// K-major operand without swizzle, in core matrices of 8 rows x 16 bytes (rows 16 bytes apart):
+// `lbo` bytes between core matrices adjacent in K, `sbo` bytes between those adjacent in M / N.
+__device__ __forceinline__ uint64_t plain_desc(uint32_t saddr, uint32_t lbo, uint32_t sbo) {
+    return (uint64_t)((saddr >> 4) & 0x3FFFu)
+           | ((uint64_t)((lbo >> 4) & 0x3FFFu) << 16)
+           | ((uint64_t)((sbo >> 4) & 0x3FFFu) << 32)
+           | ((uint64_t)1 << 46);                   // descriptor version (sm_100); layout 0: no swizzle
+}
+
+// Tap-packed A tile (narrow-channel convolutions): the K block's 32 fp32 columns are eight
+// 16-byte column groups, each an im2col box of 128 output pixels x 4 channels at one filter tap,
+// stored box after box (128 rows x 16 bytes = 2 KB each). Core matrices: 128 bytes apart along M,
+// 2 KB apart along K.
+constexpr uint32_t PACKED_BOX_BYTES = BM * 16;
 
 // kind::tf32, fp32 accumulate, both operands K-major, M = 128.
 __host__ __device__ constexpr uint32_t instr_desc_tf32(int n) {
@@ -344,7 +360,19 @@ __global__ void __launch_bounds__(192, 1) umma_gemm_kernel(const __grid_constant
                         break;
                     }
                     mbar_expect_tx(&full[s], bytes);
-                    if (p.im2col) {
+                    if (p.im2col == 2) {
+                        // eight 4-channel boxes; K column k = tap * cpix + channel. Columns past
+                        // the real K reload tap 0 (their weights are zero: B reads as zero there)
+#pragma unroll 1
+                        for (int j = 0; j < BK / 4; ++j) {
+                            const int k0 = kb * BK + j * 4;
+                            const int tap = k0 < p.kreal ? k0 / p.cpix : 0;
+                            const int ch = k0 < p.kreal ? k0 - tap * p.cpix : 0;
+                            const int kw = tap % p.KW, kh = tap / p.KW;
+                            tma_load_im2col_4d(a_tile(s) + j * PACKED_BOX_BYTES, &p.tmA, &full[s], ch, wb, hb, nb,
+                                               (uint16_t)(kw * p.DW), (uint16_t)(kh * p.DH));
+                        }
+                    } else if (p.im2col) {
                         const int cb = kb % p.cblocks;
                         const int t = kb / p.cblocks;
                         const int kw = t % p.KW, kh = t / p.KW;
@@ -388,11 +416,15 @@ __global__ void __launch_bounds__(192, 1) umma_gemm_kernel(const __grid_constant
                     const uint32_t dbase = tmem_base + (uint32_t)(b * C::BUF_COLS);
 #pragma unroll
                     for (int k = 0; k < BK / 8; ++k) {  // 8 tf32 = 32 bytes per MMA
-                        const uint64_t ad = sw128_desc(a_addr + k * 32), bd = sw128_desc(b_addr + k * 32);
+                        const bool packed = p.im2col == 2;
+                        const uint64_t ad = packed ? plain_desc(a_addr + k * 2 * PACKED_BOX_BYTES, PACKED_BOX_BYTES, 128)
+                                                   : sw128_desc(a_addr + k * 32);
+                        const uint64_t bd = sw128_desc(b_addr + k * 32);
                         const uint64_t bld = sw128_desc(bl_addr + k * 32);
                         if (MODE == STRICT) {
                             const uint32_t d = dbase + (uint32_t)(k * BN);  // own region per K step
-                            const uint64_t ald = sw128_desc(al_addr + k * 32);
+                            const uint64_t ald = packed ? plain_desc(al_addr + k * 2 * PACKED_BOX_BYTES, PACKED_BOX_BYTES, 128)
+                                                        : sw128_desc(al_addr + k * 32);
                             mma_tf32(d, ald, bd, idesc, 0u);    // A_lo * B_hi (fresh region)
                             mma_tf32(d, ad, bld, idesc, 1u);    // A_hi * B_lo
                             mma_tf32(d, ad, bd, idesc, 1u);     // A_hi * B_hi
@@ -672,8 +704,9 @@ inline bool make_map_2d(CUtensorMap *map, const void *base, long long rows, long
     return r == CUDA_SUCCESS;
 }
 
-// NHWC fp32 image, im2col boxes of 32 channels x 128 output pixels.
-inline bool make_map_im2col(CUtensorMap *map, const GemmParams &g, bool tf32) {
+// NHWC fp32 image, im2col boxes of `chans` channels x 128 output pixels: 32 channels in 128-byte
+// swizzled rows, or 4 channels in plain 16-byte rows (tap-packed).
+inline bool make_map_im2col(CUtensorMap *map, const GemmParams &g, bool tf32, int chans = BK) {
     auto fn = encode_im2col_fn();
     if (!fn) return false;
     const long long nimg = (long long)g.M / ((long long)g.OH * g.OW);
@@ -684,8 +717,9 @@ inline bool make_map_im2col(CUtensorMap *map, const GemmParams &g, bool tf32) {
     int upper[2] = {(g.OW - 1) * g.SW - g.PL - (g.W - 1), (g.OH - 1) * g.SH - g.PT - (g.H - 1)};
     cuuint32_t estr[4] = {1, (cuuint32_t)g.SW, (cuuint32_t)g.SH, 1};
     CUresult r = fn(map, tf32 ? CU_TENSOR_MAP_DATA_TYPE_TFLOAT32 : CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4,
-                    const_cast<float *>(g.a), dims, strides, lower, upper, BK, BM, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
-                    CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+                    const_cast<float *>(g.a), dims, strides, lower, upper, (cuuint32_t)chans, BM, estr,
+                    CU_TENSOR_MAP_INTERLEAVE_NONE, chans == BK ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_NONE,
+                    CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
     return r == CUDA_SUCCESS;
 }
 
@@ -734,11 +768,23 @@ inline int try_gemm_umma(const GemmParams &p, cudaStream_t stream, int *taken) {
         if (lw < -128 || lh < -128 || uw > 127 || uh > 127 || uw < -128 || uh < -128) return MGC_CUDA_OK;
         if (p.SW > 8 || p.SH > 8 || (p.KW - 1) * p.DW > 65535 || (p.KH - 1) * p.DH > 65535) return MGC_CUDA_OK;
         if (p.M % (p.OH * p.OW)) return MGC_CUDA_OK;
-        if (!umma::make_map_im2col(&u.tmA, p, a_tf32)) return MGC_CUDA_OK;
-        u.im2col = 1;
-        u.cblocks = p.b_cpad / umma::BK;
-        u.num_kb = p.KH * p.KW * u.cblocks;
-        kp = p.KH * p.KW * p.b_cpad;
+        // tap-packed when B is K-major over (kh, kw, channel) without channel padding (b_cpad ==
+        // C < 32); otherwise one K block per filter tap and 32-channel block
+        const bool packed = p.b_cpad == p.C && p.C < umma::BK;
+        if (!packed && (p.b_cpad & (umma::BK - 1))) return MGC_CUDA_OK;
+        if (!umma::make_map_im2col(&u.tmA, p, a_tf32, packed ? 4 : umma::BK)) return MGC_CUDA_OK;
+        if (packed) {
+            u.im2col = 2;
+            u.cpix = p.C;
+            u.kreal = p.KH * p.KW * p.C;
+            kp = u.kreal;
+            u.num_kb = (int)ceil_div(kp, umma::BK);
+        } else {
+            u.im2col = 1;
+            u.cblocks = p.b_cpad / umma::BK;
+            u.num_kb = p.KH * p.KW * u.cblocks;
+            kp = p.KH * p.KW * p.b_cpad;
+        }
         u.KW = p.KW; u.DH = p.DH; u.DW = p.DW;
         u.OH = p.OH; u.OW = p.OW; u.SH = p.SH; u.SW = p.SW; u.PT = p.PT; u.PL = p.PL;
     } else {

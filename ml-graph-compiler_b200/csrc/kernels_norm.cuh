@@ -192,6 +192,51 @@ __global__ void __launch_bounds__(256) pool_kernel(const __grid_constant__ PoolP
     }
 }
 
+// NHWC pooling, four channels per thread (C % 4 == 0, 16-byte aligned x and y): the same window
+// walk and the same comparisons as pool_kernel (a NaN never replaces the running maximum), with
+// 16-byte loads and stores and 32-bit index arithmetic (the caller checks the sizes fit).
+__global__ void __launch_bounds__(256) pool4_nhwc_kernel(const __grid_constant__ PoolParams p) {
+    const int c4n = p.C >> 2;
+    const unsigned total = (unsigned)p.N * p.OH * p.OW * c4n;
+    const unsigned stride = gridDim.x * blockDim.x;
+    const float4 *x4 = reinterpret_cast<const float4 *>(p.x);
+    float4 *y4 = reinterpret_cast<float4 *>(p.y);
+    for (unsigned e = blockIdx.x * blockDim.x + threadIdx.x; e < total; e += stride) {
+        const int c4 = (int)(e % c4n);
+        unsigned r = e / c4n;
+        const int ow = (int)(r % p.OW);
+        r /= p.OW;
+        const int oh = (int)(r % p.OH);
+        const int n = (int)(r / p.OH);
+        const float init = p.is_max ? -INFINITY : 0.0f;
+        float4 acc = make_float4(init, init, init, init);
+        for (int kh = 0; kh < p.KH; ++kh) {
+            const int ih = oh * p.SH - p.PT + kh * p.DH;
+            if (ih < 0 || ih >= p.H) continue;
+            const unsigned rowbase = ((unsigned)n * p.H + ih) * p.W;
+            for (int kw = 0; kw < p.KW; ++kw) {
+                const int iw = ow * p.SW - p.PL + kw * p.DW;
+                if (iw < 0 || iw >= p.W) continue;
+                const float4 v = __ldg(x4 + (size_t)(rowbase + iw) * c4n + c4);
+                if (p.is_max) {
+                    acc.x = v.x > acc.x ? v.x : acc.x;
+                    acc.y = v.y > acc.y ? v.y : acc.y;
+                    acc.z = v.z > acc.z ? v.z : acc.z;
+                    acc.w = v.w > acc.w ? v.w : acc.w;
+                } else {
+                    acc.x += v.x; acc.y += v.y; acc.z += v.z; acc.w += v.w;
+                }
+            }
+        }
+        if (!p.is_max) {
+            const int cnt = window_count(p, oh, ow);
+            const float inv = 1.0f / (float)cnt;
+            acc = cnt > 0 ? make_float4(acc.x * inv, acc.y * inv, acc.z * inv, acc.w * inv) : make_float4(0.f, 0.f, 0.f, 0.f);
+        }
+        y4[e] = acc;
+    }
+}
+
 // ---------------------------------------------------------------------------------------------
 // depthwise convolution (one input channel per group) with bias, residual and activation
 // ---------------------------------------------------------------------------------------------

@@ -229,6 +229,14 @@ inline int launch_record(const mgc_cuda_launch &L, const int64_t *aux, int64_t a
         MGC_RESOLVE(L.r[0], p.x); MGC_RESOLVE(L.r[1], p.y);
         const long long total = (long long)p.N * p.OH * p.OW * p.C;
         if (total == 0) { launched = 0; break; }
+        const bool vec = p.nhwc && (p.C & 3) == 0 && (reinterpret_cast<uintptr_t>(p.x) & 15) == 0 &&
+                         (reinterpret_cast<uintptr_t>(p.y) & 15) == 0 &&
+                         (long long)p.N * p.H * p.W < (1ll << 31) && total / 4 < (1ll << 31);
+        if (vec) {
+            pool4_nhwc_kernel<<<grid_for(total / 4, 256), 256, 0, stream>>>(p);
+            st = check_launch("pool4_nhwc_kernel");
+            break;
+        }
         pool_kernel<<<grid_for(total, 256), 256, 0, stream>>>(p);
         st = check_launch("pool_kernel");
         break;
@@ -375,6 +383,19 @@ inline int launch_record(const mgc_cuda_launch &L, const int64_t *aux, int64_t a
         if (total == 0) { launched = 0; break; }
         im2col_nhwc_kernel<<<grid_for(total, 256), 256, 0, stream>>>(p);
         st = check_launch("im2col_nhwc_kernel");
+        break;
+    }
+    case MGC_K_PACK: {
+        PackParams p{};
+        p.N = (int)i[0]; p.H = (int)i[1]; p.W = (int)i[2]; p.C = (int)i[3]; p.cp = (int)i[4];
+        p.sn = i[5]; p.sh = i[6]; p.sw = i[7]; p.sc = i[8];
+        MGC_RESOLVE(L.r[0], p.x); MGC_RESOLVE(L.r[1], p.out);
+        if (p.cp <= 0 || (p.cp & 3) || p.C > p.cp || (reinterpret_cast<uintptr_t>(p.out) & 15))
+            return fail(MGC_CUDA_BAD_ARGUMENT, "pack: %d of %d channels / output alignment", p.C, p.cp);
+        const long long total = (long long)p.N * p.H * p.W;
+        if (total == 0) { launched = 0; break; }
+        pack_nhwc_kernel<<<grid_for(total, 256), 256, 0, stream>>>(p);
+        st = check_launch("pack_nhwc_kernel");
         break;
     }
     case MGC_K_MEMCPY: {

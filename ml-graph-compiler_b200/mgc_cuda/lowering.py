@@ -39,14 +39,15 @@ SPACE_NONE, SPACE_ARENA, SPACE_WEIGHTS, SPACE_INPUT, SPACE_OUTPUT, SPACE_RAW, SP
 DTYPES = {"float32": 0, "float64": 1, "int64": 2, "int32": 3, "int8": 4, "uint8": 5, "bool": 6}
 ACTS = {"none": 0, "relu": 1, "clip": 2, "gelu": 3, "gelu_tanh": 4, "tanh": 5, "sigmoid": 6}
 STRIDED, CONV_NHWC, CONV_NCHW = 0, 2, 3
+PACKED_REGION = 1  # workspace reference index of a packed image until its offset is final
 PRECISIONS = {"fp32": 0, "tf32": 1, "strict": 2}
 K_GEMM, K_DEPTHWISE, K_POOL, K_REDUCE_MID, K_SOFTMAX, K_LAYER_NORM = 1, 2, 3, 4, 5, 6
-K_ELEMENTWISE, K_COPY, K_FILL, K_GATHER, K_REDUCE, K_ARGMAX, K_RANGE, K_MEMCPY, K_IM2COL = range(7, 16)
+K_ELEMENTWISE, K_COPY, K_FILL, K_GATHER, K_REDUCE, K_ARGMAX, K_RANGE, K_MEMCPY, K_IM2COL, K_PACK = range(7, 17)
 KIND_NAMES = {
     K_GEMM: "gemm", K_DEPTHWISE: "depthwise", K_POOL: "pool", K_REDUCE_MID: "reduce",
     K_SOFTMAX: "softmax", K_LAYER_NORM: "layer_norm", K_ELEMENTWISE: "elementwise",
     K_COPY: "copy", K_FILL: "fill", K_GATHER: "gather", K_REDUCE: "reduce", K_ARGMAX: "argmax",
-    K_RANGE: "range", K_MEMCPY: "memcpy", K_IM2COL: "im2col",
+    K_RANGE: "range", K_MEMCPY: "memcpy", K_IM2COL: "im2col", K_PACK: "pack",
 }
 LAUNCH_INTS, LAUNCH_FLOATS, LAUNCH_REFS = 64, 8, 8
 # Elementwise program operations, numbered as csrc/kernels_mem.cuh EwOp.
@@ -223,7 +224,10 @@ class CudaEmitter:
         self.kernels: dict[str, int] = {}
         self._node = -1
         self._keep_alive: list[Value] = []
-        self.workspace_bytes = 0  # one scratch region, reused by every launch that needs one
+        self.workspace_bytes = 0  # scratch regions (im2col patch matrices, channel-packed images)
+        self._im2col_bytes = 0    # the im2col region at offset 0, shared by every im2col launch
+        self._packed: dict[int, RefT] = {}  # id(value) -> its channel-packed copy in the workspace
+        self._pack_regions: list[tuple[int, int]] = []  # (offset, bytes) of each packed image
 
     # -- references ----------------------------------------------------------------------------
     def _root(self, value: Value) -> Value:
@@ -417,6 +421,15 @@ class CudaEmitter:
         perm = ops.transpose_perm(node, x.tensor_type.rank)
         ss = _strides(x.tensor_type.shape)
         shape = node.output.tensor_type.shape
+        out = node.output
+        users = out.users
+        if (len(users) == 1 and users[0].inputs and users[0].inputs[0] is out and self._tap_packed(users[0])
+                and shape[3] % 4 and all(v is not out for _, v in self.graph.named_outputs())):
+            # the only use is a narrow-channel convolution that needs its channels padded: write
+            # the padded NHWC copy straight from the source (the plain transposed copy is unused)
+            self._packed[id(out)] = self._emit_pack(self.ref(x), shape[0], shape[1], shape[2], shape[3],
+                                                    [ss[p] for p in perm])
+            return
         self._copy(shape, self.ref(x), [ss[p] for p in perm], 0, self.ref(node.output), _strides(shape), 0,
                    x.tensor_type.itemsize, count="transpose")
 
@@ -918,6 +931,9 @@ class CudaEmitter:
         geo = {"H": h, "W": wd, "C": c, "KH": kh, "KW": kw, "SH": g.strides[0], "SW": g.strides[1],
                "DH": g.dilations[0], "DW": g.dilations[1], "PT": pt, "PL": pl, "OH": oh, "OW": ow}
         pointwise = kh == kw == 1 and g.strides == (1, 1) and g.pads == (0, 0, 0, 0)
+        if self._tap_packed(node):
+            self._conv_tap_packed(node, wdata, geo, nb, bias, res, act)
+            return
         if nhwc and group == 1 and not pointwise and cg % 4 and self.precision != "fp32":
             self._conv_via_im2col(node, wdata, geo, nb, bias, res, act)
             return
@@ -967,7 +983,8 @@ class CudaEmitter:
         kreal = kh * kw * cg
         kp = (kreal + 31) // 32 * 32
         m = nb * geo["OH"] * geo["OW"]
-        self.workspace_bytes = max(self.workspace_bytes, m * kp * 4)
+        self._im2col_bytes = max(self._im2col_bytes, m * kp * 4)
+        self._layout_workspace()
         ws = (SPACE_WORKSPACE, 0, 0)
         ints = [nb, geo["H"], geo["W"], geo["C"], kh, kw, geo["SH"], geo["SW"], geo["DH"], geo["DW"], geo["PT"],
                 geo["PL"], geo["OH"], geo["OW"], kp, 0, cg]
@@ -977,6 +994,76 @@ class CudaEmitter:
         bref, blo, b_rs, b_cs = self._kmajor_b(wmat, ("im2col", id(self._root(node.input(1)))))
         self._gemm(m, kg, kp, ws, kp, 1, bref, b_rs, b_cs, self.ref(node.output), kg, b_lo=blo,
                    bias=bias, bias_mode=1, res=res, ldr=kg, act=act, **self._umma_b(bref, blo))
+
+    def _im2col_end(self) -> int:
+        return (self._im2col_bytes + 255) // 256 * 256
+
+    def _layout_workspace(self) -> None:
+        """Workspace layout: the im2col region at offset 0 (shared by every im2col launch, sized
+        for the largest), then one region per packed image (each lives from its pack launch to its
+        convolution, so none is shared)."""
+        packed = sum((size + 255) // 256 * 256 for _, size in self._pack_regions)
+        self.workspace_bytes = self._im2col_end() + packed
+
+    def _pack_region(self, nbytes: int) -> RefT:
+        """A fresh packed-image region. Its offset is relative to the end of the im2col region,
+        whose final size is known only after the last node; the reference carries index
+        PACKED_REGION until ``lower`` rebases it."""
+        off = sum((size + 255) // 256 * 256 for _, size in self._pack_regions)
+        self._pack_regions.append((off, nbytes))
+        self._layout_workspace()
+        return (SPACE_WORKSPACE, PACKED_REGION, off)
+
+    def _tap_packed(self, node: Node) -> bool:
+        """Whether a convolution takes the tap-packed tensor-core path: NHWC, one group, a real
+        window (not 1x1 / stride 1 / no padding), fewer than 32 input channels, tensor-core
+        precision."""
+        if node.op not in ("FusedConv", "Conv") or self.precision == "fp32" or self._depthwise(node):
+            return False
+        if ops.conv_layout(node) != "NHWC" or int(node.attrs.get("group", 1)) != 1:
+            return False
+        xt, wt = node.input(0).tensor_type, node.input(1).tensor_type
+        if xt.rank != 4 or xt.dtype != "float32":
+            return False
+        kh, kw, cg, _ = wt.shape
+        g = ops.window_geometry(node, (xt.shape[1], xt.shape[2]), (kh, kw))
+        pointwise = kh == kw == 1 and g.strides == (1, 1) and g.pads == (0, 0, 0, 0)
+        return not pointwise and cg < 32
+
+    def _emit_pack(self, src: RefT, nb: int, h: int, w: int, c: int, strides: Sequence[int]) -> RefT:
+        """K_PACK slots: i[0..4] N, H, W, C, padded C; i[5..8] source element strides of n, h, w,
+        c; r[0] source, r[1] packed NHWC destination."""
+        cp = (c + 3) // 4 * 4
+        dst = self._pack_region(nb * h * w * cp * 4)
+        self.emit(K_PACK, [nb, h, w, c, cp, *strides], refs=[src, dst])
+        return dst
+
+    def _conv_tap_packed(self, node: Node, w_hwio: np.ndarray, geo: dict[str, int], nb: int, bias: RefT,
+                         res: RefT, act: tuple[int, float, float]) -> None:
+        """Narrow-channel NHWC convolution (C < 32, e.g. the 3-channel stem) on the tensor cores:
+        K runs over (kh, kw, channel) with the channels padded only to a multiple of 4, so one
+        32-wide K block holds 32 / Cp filter taps. A channel count that is not a multiple of 4 is
+        packed first (K_PACK into the workspace; fused into the producing NCHW->NHWC transpose
+        when that transpose has no other use)."""
+        x = node.input(0)
+        kh, kw, cg, kg = w_hwio.shape
+        cp = (cg + 3) // 4 * 4
+        if cp == cg:
+            xref = self.ref(x)
+        elif id(x) in self._packed:
+            xref = self._packed[id(x)]
+        else:
+            xref = self._emit_pack(self.ref(x), nb, geo["H"], geo["W"], cg,
+                                   [geo["H"] * geo["W"] * cg, geo["W"] * cg, cg, 1])
+        wpad = np.zeros((kh, kw, cp, kg), np.float32)
+        wpad[:, :, :cg, :] = np.asarray(w_hwio, np.float32)
+        bref, blo, b_rs, b_cs = self._kmajor_b(wpad.reshape(kh * kw * cp, kg), ("tap-packed", id(self._root(node.input(1)))))
+        m = nb * geo["OH"] * geo["OW"]
+        self._gemm(
+            m, kg, kh * kw * cp, xref, cp, 1, bref, b_rs, b_cs, self.ref(node.output), kg, b_lo=blo,
+            conv={**geo, "C": cp, "c_off": 0, "cg": cp}, a_kind=CONV_NHWC, bias=bias, bias_mode=1, res=res,
+            ldr=kg, act=act, b_umma=bref, b_umma_lo=blo, b_cpad=cp,
+        )
 
     # -- pooling (c.py:1228-1253) ---------------------------------------------------------------------
     def _pool(self, node: Node, is_max: int) -> None:
@@ -1012,6 +1099,11 @@ class CudaEmitter:
             t = value.tensor_type
             if t.nbytes:
                 self.emit(K_MEMCPY, [t.nbytes], refs=[self.ref(value), (SPACE_OUTPUT, j, 0)], count="copy")
+        base = self._im2col_end()
+        for rec in self.launches:
+            for r in rec.r:
+                if r.space == SPACE_WORKSPACE and r.index == PACKED_REGION:
+                    r.index, r.offset = 0, r.offset + base
         return LoweredModel(
             launches=self.launches,
             aux=np.asarray(self.aux if self.aux else [0], np.int64),

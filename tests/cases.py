@@ -248,6 +248,37 @@ def _p_conv_block(r: np.random.Generator) -> tuple[Graph, dict[str, np.ndarray]]
     return g, {"x": f32(r, 2, 8, 10, 10)}
 
 
+def _p_narrow_convs(r: np.random.Generator) -> tuple[Graph, dict[str, np.ndarray]]:
+    """A chain of NHWC convolutions with fewer than 32 input channels (3, 8, 12, 6, 16, 28):
+    7x7 stride 2 stem, SAME_UPPER 4x4 (asymmetric padding), dilation 2, stride 2, with BN/ReLU
+    epilogues and a residual add, so every tap-packing arrangement of the K axis is exercised
+    (one to seven 4-channel groups per filter tap, a channel count that needs padding both at the
+    graph input and in the middle of the network)."""
+    g = Graph("narrow_convs")
+    x = g.add_input("x", TensorType("float32", (2, 3, 22, 18)))
+
+    def conv(v: Any, cin: int, cout: int, k: int, bn: bool = True, **attrs: Any) -> Any:
+        w = g.constant(f32(r, cout, cin, k, k, scale=0.5 / math.sqrt(cin * k * k) * 3))
+        y = g.add_node("Conv", [v, w, g.constant(f32(r, cout, scale=0.1))],
+                       attrs={"kernel_shape": [k, k], **attrs}).output
+        if bn:
+            ps = [g.constant(a) for a in (pos(r, cout), f32(r, cout, scale=0.1), f32(r, cout, scale=0.1), pos(r, cout))]
+            y = g.add_node("BatchNormalization", [y, *ps], attrs={"epsilon": 1e-5}).output
+        return y
+
+    h = g.add_node("Relu", [conv(x, 3, 8, 7, strides=[2, 2], pads=[3, 3, 3, 3])]).output
+    h2 = conv(h, 8, 12, 3, pads=[1, 1, 1, 1])
+    h3 = g.add_node("Relu", [conv(h2, 12, 6, 4, auto_pad="SAME_UPPER")]).output
+    h4 = conv(h3, 6, 8, 3, dilations=[2, 2], pads=[2, 2, 2, 2])
+    h5 = g.add_node("Relu", [g.add_node("Add", [h4, h]).output]).output
+    h6 = g.add_node("Relu", [conv(h5, 8, 16, 3, strides=[2, 2], pads=[1, 1, 1, 1])]).output
+    h7 = conv(h6, 16, 28, 3, pads=[1, 1, 1, 1])
+    y = conv(h7, 28, 5, 5, bn=False, pads=[2, 2, 2, 2])
+    g.add_output(y, "y")
+    infer_shapes(g)
+    return g, {"x": f32(r, 2, 3, 22, 18)}
+
+
 def _p_dense_gelu(r: np.random.Generator) -> tuple[Graph, dict[str, np.ndarray]]:
     """MatMul + bias + erf GELU subgraph, MatMul(x, Transpose(W)), residual Add, tanh GELU."""
     g = Graph("dense_gelu")
@@ -292,6 +323,7 @@ def _p_loopfuse(r: np.random.Generator) -> tuple[Graph, dict[str, np.ndarray]]:
 def pattern_cases() -> list[Case]:
     return [
         _pattern("conv_block", _p_conv_block),
+        _pattern("narrow_convs", _p_narrow_convs),
         _pattern("dense_gelu", _p_dense_gelu),
         _pattern("layer_norm", _p_layer_norm),
         _pattern("loopfuse", _p_loopfuse),

@@ -14,7 +14,8 @@ Run from the repository root in a checkout where the reference is importable::
 
     MGC_CC=/usr/bin/gcc python tests/golden/make_golden.py [--big]
 
-It imports the reference from ``/root/reference/src`` when that directory exists.
+It imports the reference's sources from ``$MGC_REFERENCE_SRC`` (the ``src`` directory of a
+reference checkout) when that directory exists, else the installed copy in ``baseline/_ref``.
 """
 
 from __future__ import annotations
@@ -30,8 +31,11 @@ import numpy as np
 
 HERE = Path(__file__).resolve().parent
 ROOT = HERE.parents[1]
-if Path("/root/reference/src").exists():
-    sys.path.insert(0, "/root/reference/src")
+_SRC = os.environ.get("MGC_REFERENCE_SRC", "/root/reference/src")
+if Path(_SRC).exists():
+    sys.path.insert(0, _SRC)
+else:
+    sys.path.insert(0, str(ROOT / "baseline" / "_ref"))
 sys.path.insert(0, str(ROOT / "tests"))
 
 import cases  # noqa: E402
@@ -98,14 +102,20 @@ def main() -> None:
                 print(f"{case.name} {k}: interp {t1 - t0:.1f}s, C {t2 - t1:.1f}s, C vs interp max abs {diff:.3g}, "
                       f"|out| max {float(np.abs(ref[k]).max()):.4g}")
         np.savez_compressed(HERE / "models.npz", **models)
-    manifest = {
-        "generator": "tests/golden/make_golden.py" + (" --big" if args.big else ""),
+    path = HERE / "manifest.json"
+    manifest = json.loads(path.read_text()) if path.exists() else {}
+    manifest.pop("generator", None)
+    made = {
         "reference_version": ml_graph_compiler.__version__,
         "reference_path": str(Path(ml_graph_compiler.__file__).parent),
         "numpy": np.__version__,
         "cc": os.environ.get("MGC_CC", ""),
     }
-    (HERE / "manifest.json").write_text(json.dumps(manifest, indent=2) + "\n")
+    manifest.update(made)
+    manifest["ops.npz"] = {"generator": "tests/golden/make_golden.py", **made}
+    if args.big:
+        manifest["models.npz"] = {"generator": "tests/golden/make_golden.py --big", **made}
+    path.write_text(json.dumps(manifest, indent=2) + "\n")
 
 
 if __name__ == "__main__":

@@ -7,7 +7,7 @@ import pytest
 
 import cases
 from mgc_cuda import lowering, zoo
-from mgc_cuda.lowering import CudaEmitter, lower_graph, tf32_split
+from mgc_cuda.lowering import K_GEMM, K_PACK, CudaEmitter, lower_graph, tf32_split
 from ml_graph_compiler.codegen.c import generate_c
 from ml_graph_compiler.errors import CodegenError
 from ml_graph_compiler.ir import Graph, TensorType
@@ -36,11 +36,30 @@ def test_resnet50_o3_matches_published_structure(r50: Graph) -> None:
     assert low.arena_bytes == 7_225_344
     assert len(low.launches) == 57
     assert low.workspace_bytes == 0
-    # on the tensor cores the 3-channel stem is fed by an explicit im2col in the workspace
+    # on the tensor cores the input transpose writes the image with its 3 channels padded to 4
+    # into the workspace, and the stem reads it as tap-packed im2col boxes
     tc = lower_graph(r50, precision="tf32")
-    assert tc.kernels == {"gemm": 54, "im2col": 1, "pool": 1, "reduce": 1, "transpose": 1, "view": 1}
+    assert tc.kernels == {"gemm": 54, "pack": 1, "pool": 1, "reduce": 1, "view": 1}
     assert tc.arena_bytes == 7_225_344
-    assert tc.workspace_bytes == 112 * 112 * 160 * 4
+    assert tc.workspace_bytes == 224 * 224 * 4 * 4
+    pack, stem = tc.launches[0], tc.launches[1]
+    assert pack.kind == K_PACK and list(pack.i[:9]) == [1, 224, 224, 3, 4, 3 * 224 * 224, 224, 1, 224 * 224]
+    assert stem.kind == K_GEMM and stem.i[2] == 7 * 7 * 4 and stem.i[50] == 4
+    assert (stem.r[0].space, stem.r[0].offset) == (pack.r[1].space, pack.r[1].offset)
+
+
+def test_workspace_regions_do_not_overlap() -> None:
+    """Two channel packs (one fused into the input transpose, one in the middle of the network)
+    get disjoint regions inside the workspace."""
+    c = [c for c in cases.all_cases() if c.name == "pattern_narrow_convs"][0]
+    g, _ = cases.prepare(c)
+    low = lower_graph(g, precision="tf32")
+    assert low.kernels["pack"] == 2 and "im2col" not in low.kernels
+    regions = sorted((r.i[0] * r.i[1] * r.i[2] * r.i[4] * 4, r.r[1].offset) for r in low.launches if r.kind == K_PACK)
+    spans = sorted((off, off + size) for size, off in regions)
+    assert all(a[1] <= b[0] for a, b in zip(spans, spans[1:]))
+    assert spans[-1][1] <= low.workspace_bytes
+    assert all(r.r[1].index == 0 for r in low.launches if r.kind == K_PACK)
 
 
 def test_same_kernel_mix_and_arena_as_the_c_backend() -> None:
@@ -110,7 +129,7 @@ def test_every_case_lowers(case: cases.Case) -> None:
     g, _ = cases.prepare(case)
     low = lower_graph(g, precision="strict")
     assert low.launches or all(n.op in lowering.ALIAS_OPS for n in g.nodes)
-    assert all(lowering.K_GEMM <= r.kind <= lowering.K_IM2COL for r in low.launches)
+    assert all(lowering.K_GEMM <= r.kind <= lowering.K_PACK for r in low.launches)
 
 
 def test_algorithmic_cost_of_resnet50(r50: Graph) -> None:
