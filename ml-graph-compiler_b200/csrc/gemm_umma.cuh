@@ -236,6 +236,17 @@ __device__ __forceinline__ void tmem_ld16(uint32_t taddr, uint32_t (&r)[16]) {
         : "r"(taddr));
 }
 
+__device__ __forceinline__ float4 lds4(uint32_t addr) {
+    float4 v;
+    asm volatile("ld.shared.v4.f32 {%0, %1, %2, %3}, [%4];" : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w) : "r"(addr));
+    return v;
+}
+
+__device__ __forceinline__ void sts4(uint32_t addr, float4 v) {
+    asm volatile("st.shared.v4.f32 [%0], {%1, %2, %3, %4};" ::"r"(addr), "f"(v.x), "f"(v.y), "f"(v.z), "f"(v.w)
+                 : "memory");
+}
+
 __device__ __forceinline__ void tmem_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
 
 __device__ __forceinline__ long long ceil_div_dev(long long a, long long b) { return (a + b - 1) / b; }
@@ -276,10 +287,14 @@ struct Cfg {
     static constexpr uint32_t STAGE_BUDGET = 212992 - OUT_BYTES;
     static constexpr int STAGES = (STAGE_BUDGET / STAGE_BYTES) < 2 ? 2
                                   : (STAGE_BUDGET / STAGE_BYTES) > 8 ? 8 : (STAGE_BUDGET / STAGE_BYTES);
-    static constexpr uint32_t BUF_COLS = REGIONS * BN;             // TMEM columns of one K block
+    // TMEM columns of one K block: strict, four step regions of BN; TF32, the products with B_hi
+    // (columns [0, BN)) and with B_lo ([BN, 2 BN)) from one N = 2 BN MMA per K step
+    static constexpr uint32_t BUF_COLS = MODE == STRICT ? REGIONS * BN : 2 * BN;
     static constexpr int TBUFS = (512 / BUF_COLS) > 4 ? 4 : (512 / BUF_COLS);  // TMEM buffers in the ring
     static constexpr uint32_t TMEM_COLS = TBUFS * BUF_COLS;
-    static constexpr uint32_t SMEM_BYTES = STAGES * STAGE_BYTES + OUT_BYTES + 1024 /*align*/ + 256 /*barriers*/;
+    static constexpr uint32_t BAR_BYTES = 512;                     // mbarriers and the TMEM address
+    static constexpr uint32_t SMEM_BYTES = STAGES * STAGE_BYTES + OUT_BYTES + 1024 /*align*/ + BAR_BYTES + BN * 4 /*bias*/;
+    static_assert((3 * 8 + 2 * 4 + 2) * 8 + 4 <= BAR_BYTES, "barrier area");
     static_assert(TMEM_COLS <= 512 && (TMEM_COLS & (TMEM_COLS - 1)) == 0, "TMEM columns");
     static_assert(TBUFS >= 2, "need at least two TMEM buffers");
 };
@@ -309,6 +324,7 @@ __global__ void __launch_bounds__(192, 1) umma_gemm_kernel(const __grid_constant
     uint64_t *mma_done = tempty + TB;  // every issued MMA has completed
     uint64_t *res_full = mma_done + 1; // a tile's residual has landed in the staging tile
     uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(res_full + 1);
+    float *bias_s = reinterpret_cast<float *>(out_tile + C::OUT_BYTES + C::BAR_BYTES);  // [BN] this tile's bias
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int num_kb = p.num_kb;
@@ -394,6 +410,7 @@ __global__ void __launch_bounds__(192, 1) umma_gemm_kernel(const __grid_constant
         if (lane == 0) {
             // ---------------- MMA issuer ----------------
             constexpr uint32_t idesc = instr_desc_tf32(BN);
+            constexpr uint32_t idesc2 = instr_desc_tf32(2 * BN);  // the stacked [B_hi; B_lo] tile
             long long g = 0;
             bool ok = true;
             for (int tile = blockIdx.x; tile < total_tiles && ok; tile += gridDim.x) {
@@ -429,8 +446,11 @@ __global__ void __launch_bounds__(192, 1) umma_gemm_kernel(const __grid_constant
                             mma_tf32(d, ad, bld, idesc, 1u);    // A_hi * B_lo
                             mma_tf32(d, ad, bd, idesc, 1u);     // A_hi * B_hi
                         } else {
-                            mma_tf32(dbase, ad, bld, idesc, k > 0 ? 1u : 0u);  // A * B_lo
-                            mma_tf32(dbase, ad, bd, idesc, 1u);                // A * B_hi
+                            // B_lo's tile directly follows B_hi's in the stage with the same
+                            // 128B-swizzled row layout, so one descriptor spans both as 2 BN rows:
+                            // one MMA, A read once per K step
+                            (void)bld;
+                            mma_tf32(dbase, ad, bd, idesc2, k > 0 ? 1u : 0u);
                         }
                     }
                     mma_commit(&empty[s]);   // shared-memory slot free once these MMAs read it
@@ -473,19 +493,16 @@ __global__ void __launch_bounds__(192, 1) umma_gemm_kernel(const __grid_constant
                     for (int j = 0; j < 32; ++j) acc[c0 + j] += (double)blk[j];
                 }
             } else {
+                // acc += (A B_hi + A B_lo) for 32 columns at a time: both halves loaded, one wait
 #pragma unroll
-                for (int c0 = 0; c0 < BN; c0 += 64) {
-                    uint32_t v0[32], v1[32];
+                for (int c0 = 0; c0 < BN; c0 += 32) {
+                    uint32_t vh[32], vl[32];
                     const uint32_t addr = lane_base + (uint32_t)(b * C::BUF_COLS + c0);
-                    tmem_ld32(addr, v0);
-                    if (c0 + 32 < BN) tmem_ld32(addr + 32, v1);
+                    tmem_ld32(addr, vh);
+                    tmem_ld32(addr + BN, vl);
                     tmem_wait_ld();
 #pragma unroll
-                    for (int j = 0; j < 32; ++j) acc[c0 + j] += __uint_as_float(v0[j]);
-                    if (c0 + 32 < BN) {
-#pragma unroll
-                        for (int j = 0; j < 32; ++j) acc[c0 + 32 + j] += __uint_as_float(v1[j]);
-                    }
+                    for (int j = 0; j < 32; ++j) acc[c0 + j] += __uint_as_float(vh[j]) + __uint_as_float(vl[j]);
                 }
             }
             tc_fence_before();
@@ -513,10 +530,13 @@ __global__ void __launch_bounds__(192, 1) umma_gemm_kernel(const __grid_constant
             ++gs;
             return true;
         };
-        auto stage_slot = [&](int r, int c0) {
+        // byte offset of columns c0..c0+3 of row r in the staging tile: BN / 32 slabs of 128 rows
+        // x 128 bytes, 16-byte chunks XOR-swizzled by the row (the TMA 128-byte swizzle)
+        auto stage_offset = [](int r, int c0) -> uint32_t {
             const int sl = c0 >> 5, j = (c0 & 31) >> 2;
-            return reinterpret_cast<float4 *>(out_tile + sl * (BM * 128) + r * 128 + ((j ^ (r & 7)) << 4));
+            return (uint32_t)(sl * (BM * 128) + r * 128 + ((j ^ (r & 7)) << 4));
         };
+        auto stage_slot = [&](int r, int c0) { return reinterpret_cast<float4 *>(out_tile + stage_offset(r, c0)); };
         // Output path. Step 1 (unrolled over the accumulator registers, no calls): alpha * acc +
         // bias (+ the residual, TMA-prefetched into the staging tile) and a ReLU / Clip, into the
         // 128B-swizzled staging tile. Step 2 (compact, own row): GELU / tanh / sigmoid. Then one
@@ -551,6 +571,11 @@ __global__ void __launch_bounds__(192, 1) umma_gemm_kernel(const __grid_constant
             }
             if (MODE == STRICT && ok && num_kb >= 1 && !drain()) ok = false;
             if (!ok) break;
+            // this tile's bias columns into shared memory, one coalesced load (the previous
+            // tile's readers have all passed its second barrier)
+            if (p.bias) {
+                for (int c = et; c < BN; c += 128) bias_s[c] = n0 + c < p.N ? __ldg(p.bias + n0 + c) : 0.0f;
+            }
             // the staging tile is free (the previous TMA store was read out) and, with a
             // residual, refilled with this tile's residual
             epilogue_sync();
@@ -558,51 +583,47 @@ __global__ void __launch_bounds__(192, 1) umma_gemm_kernel(const __grid_constant
                 ok = false;
                 break;
             }
+            // 32 columns at a time: the residual loads of a chunk are all issued before its
+            // stores, so no load waits behind a store to the same staging tile
+            const uint32_t out_s = smem_addr(out_tile);
+            const uint32_t bias_addr = smem_addr(bias_s);
 #pragma unroll
-            for (int c0 = 0; c0 < BN; c0 += 4) {
-                float4 *slot = stage_slot(row, c0);
-                const int nb = n0 + c0;
-                float4 o;
-                o.x = p.alpha * (float)acc[c0 + 0];
-                o.y = p.alpha * (float)acc[c0 + 1];
-                o.z = p.alpha * (float)acc[c0 + 2];
-                o.w = p.alpha * (float)acc[c0 + 3];
-                if (p.bias) {
-                    if (nb + 4 <= p.N && ((reinterpret_cast<uintptr_t>(p.bias + nb) & 15) == 0)) {
-                        const float4 bv = __ldg(reinterpret_cast<const float4 *>(p.bias + nb));
-                        o.x += bv.x; o.y += bv.y; o.z += bv.z; o.w += bv.w;
-                    } else {
-                        if (nb + 0 < p.N) o.x += p.bias[nb + 0];
-                        if (nb + 1 < p.N) o.y += p.bias[nb + 1];
-                        if (nb + 2 < p.N) o.z += p.bias[nb + 2];
-                        if (nb + 3 < p.N) o.w += p.bias[nb + 3];
-                    }
-                }
+            for (int c0 = 0; c0 < BN; c0 += 32) {
+                float4 rv[8];
                 if (res_tma) {
-                    const float4 rv = *slot;
-                    o.x += rv.x; o.y += rv.y; o.z += rv.z; o.w += rv.w;
-                }
-                if (MODE == STRICT) {  // the same sum in fp64 with the step-bias compensation
-                    const double sa = (double)p.alpha * (1.0 + STEP_BIAS);
-                    double d[4] = {sa * (double)acc[c0 + 0], sa * (double)acc[c0 + 1], sa * (double)acc[c0 + 2], sa * (double)acc[c0 + 3]};
-                    if (p.bias) {
 #pragma unroll
-                        for (int t = 0; t < 4; ++t)
-                            if (nb + t < p.N) d[t] += (double)p.bias[nb + t];
-                    }
-                    if (res_tma) {
-                        const float4 rv = *slot;
-                        d[0] += rv.x; d[1] += rv.y; d[2] += rv.z; d[3] += rv.w;
-                    }
-                    o.x = (float)d[0]; o.y = (float)d[1]; o.z = (float)d[2]; o.w = (float)d[3];
+                    for (int j = 0; j < 8; ++j) rv[j] = lds4(out_s + stage_offset(row, c0 + 4 * j));
                 }
-                if (act_in_step1 && p.act == MGC_ACT_RELU) {
-                    o.x = fmaxf(o.x, 0.0f); o.y = fmaxf(o.y, 0.0f); o.z = fmaxf(o.z, 0.0f); o.w = fmaxf(o.w, 0.0f);
-                } else if (act_in_step1 && p.act == MGC_ACT_CLIP) {
-                    o.x = fminf(fmaxf(o.x, p.lo), p.hi); o.y = fminf(fmaxf(o.y, p.lo), p.hi);
-                    o.z = fminf(fmaxf(o.z, p.lo), p.hi); o.w = fminf(fmaxf(o.w, p.lo), p.hi);
+#pragma unroll
+                for (int j = 0; j < 8; ++j) {
+                    const int c = c0 + 4 * j;
+                    const float4 bv = p.bias ? lds4(bias_addr + 4 * c) : make_float4(0.f, 0.f, 0.f, 0.f);
+                    float4 o;
+                    if (MODE == STRICT) {  // the same sum in fp64 with the step-bias compensation
+                        const double sa = (double)p.alpha * (1.0 + STEP_BIAS);
+                        double d0 = sa * (double)acc[c + 0] + (double)bv.x, d1 = sa * (double)acc[c + 1] + (double)bv.y;
+                        double d2 = sa * (double)acc[c + 2] + (double)bv.z, d3 = sa * (double)acc[c + 3] + (double)bv.w;
+                        if (res_tma) {
+                            d0 += rv[j].x; d1 += rv[j].y; d2 += rv[j].z; d3 += rv[j].w;
+                        }
+                        o = make_float4((float)d0, (float)d1, (float)d2, (float)d3);
+                    } else {
+                        o.x = p.alpha * (float)acc[c + 0] + bv.x;
+                        o.y = p.alpha * (float)acc[c + 1] + bv.y;
+                        o.z = p.alpha * (float)acc[c + 2] + bv.z;
+                        o.w = p.alpha * (float)acc[c + 3] + bv.w;
+                        if (res_tma) {
+                            o.x += rv[j].x; o.y += rv[j].y; o.z += rv[j].z; o.w += rv[j].w;
+                        }
+                    }
+                    if (act_in_step1 && p.act == MGC_ACT_RELU) {
+                        o.x = fmaxf(o.x, 0.0f); o.y = fmaxf(o.y, 0.0f); o.z = fmaxf(o.z, 0.0f); o.w = fmaxf(o.w, 0.0f);
+                    } else if (act_in_step1 && p.act == MGC_ACT_CLIP) {
+                        o.x = fminf(fmaxf(o.x, p.lo), p.hi); o.y = fminf(fmaxf(o.y, p.lo), p.hi);
+                        o.z = fminf(fmaxf(o.z, p.lo), p.hi); o.w = fminf(fmaxf(o.w, p.lo), p.hi);
+                    }
+                    sts4(out_s + stage_offset(row, c), o);
                 }
-                *slot = o;
             }
             if (!act_in_step1 && !res_direct) {  // transcendental activation on this thread's row
 #pragma unroll 1
