@@ -39,6 +39,9 @@ struct GemmParams {
     // padded to b_cpad)), TF32-rounded high part and fp32 residual; NULL when not provided
     const float *b_umma, *b_umma_lo;
     int b_cpad;
+    // window-row layout of an im2col convolution over a spatially padded image: output pixels per
+    // TMA box (0: not used) and the padded length of one window row (B is [N][KH][win_L])
+    int win_rows, win_L;
     int *err;                     // device word for bounded-wait timeouts (may be NULL)
 };
 

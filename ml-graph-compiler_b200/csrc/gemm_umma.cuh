@@ -73,6 +73,9 @@ struct Params {
     int im2col;                      // 0 tiled A, 1 im2col (32-channel blocks), 2 tap-packed im2col
     int KW, DH, DW, cblocks;         // im2col: K block kb -> (kh, kw, channel block)
     int cpix, kreal;                 // tap-packed: channels per pixel (4..28), real K = KH*KW*cpix
+    int wrows;                       // window rows (im2col 3): output pixels per box (divides OW)
+    int m_tiles;                     // ceil(M / 128)
+    uint32_t b_res_bytes;            // B-resident kernels: bytes of this CTA's whole B panel
     int OH, OW, SH, SW, PT, PL;      // im2col: output pixel -> window origin
     float *c;
     long long ldc;
@@ -147,6 +150,16 @@ __device__ __forceinline__ void tma_load_im2col_4d(void *dst, const CUtensorMap 
         " [%0], [%1, {%3, %4, %5, %6}], [%2], {%7, %8};"
         ::"r"(smem_addr(dst)), "l"(reinterpret_cast<uint64_t>(map)), "r"(smem_addr(bar)), "r"(c), "r"(w), "r"(h),
         "r"(n), "h"(off_w), "h"(off_h)
+        : "memory");
+}
+
+__device__ __forceinline__ void tma_load_5d(void *dst, const CUtensorMap *map, uint64_t *bar, int x, int y, int z,
+                                            int w, int v) {
+    asm volatile(
+        "cp.async.bulk.tensor.5d.shared::cluster.global.tile.mbarrier::complete_tx::bytes"
+        " [%0], [%1, {%3, %4, %5, %6, %7}], [%2];"
+        ::"r"(smem_addr(dst)), "l"(reinterpret_cast<uint64_t>(map)), "r"(smem_addr(bar)), "r"(x), "r"(y), "r"(z),
+        "r"(w), "r"(v)
         : "memory");
 }
 
@@ -276,16 +289,22 @@ __device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t (&r)[32]) {
         : "r"(taddr));
 }
 
-template <int BN, int MODE>
+constexpr uint32_t SMEM_LIMIT = 232448;  // dynamic shared memory per block on sm_100 (227 KB)
+
+// RB: B-resident variant. The CTA keeps one N tile for its whole life and loads that tile's B
+// panel (every K block, hi and lo) into shared memory once; the stages then carry A only.
+template <int BN, int MODE, int RB = 0>
 struct Cfg {
     static constexpr int REGIONS = MODE == STRICT ? 4 : 1;  // TMEM regions per K block
     static constexpr uint32_t B_TILE_BYTES = BN * BK * 4;
-    // stage: A | B_hi | B_lo (| A_lo)
-    static constexpr uint32_t STAGE_BYTES = A_TILE_BYTES + 2 * B_TILE_BYTES + (MODE == STRICT ? A_TILE_BYTES : 0);
+    // stage: A (| A_lo) (| B_hi | B_lo)
+    static constexpr uint32_t STAGE_BYTES =
+        A_TILE_BYTES + (MODE == STRICT ? A_TILE_BYTES : 0) + (RB ? 0 : 2 * B_TILE_BYTES);
     // output tile staging: BN/32 slabs of [128 rows][32 fp32] in the 128B-swizzled TMA layout
     static constexpr uint32_t OUT_BYTES = BM * BN * 4;
     static constexpr uint32_t STAGE_BUDGET = 212992 - OUT_BYTES;
-    static constexpr int STAGES = (STAGE_BUDGET / STAGE_BYTES) < 2 ? 2
+    static constexpr int STAGES = RB ? (MODE == STRICT ? 2 : 4)
+                                  : (STAGE_BUDGET / STAGE_BYTES) < 2 ? 2
                                   : (STAGE_BUDGET / STAGE_BYTES) > 8 ? 8 : (STAGE_BUDGET / STAGE_BYTES);
     // TMEM columns of one K block: strict, four step regions of BN; TF32, the products with B_hi
     // (columns [0, BN)) and with B_lo ([BN, 2 BN)) from one N = 2 BN MMA per K step
@@ -293,29 +312,38 @@ struct Cfg {
     static constexpr int TBUFS = (512 / BUF_COLS) > 4 ? 4 : (512 / BUF_COLS);  // TMEM buffers in the ring
     static constexpr uint32_t TMEM_COLS = TBUFS * BUF_COLS;
     static constexpr uint32_t BAR_BYTES = 512;                     // mbarriers and the TMEM address
+    // fixed part; a B-resident launch adds its B panel (b_res_bytes) in front of the stages
     static constexpr uint32_t SMEM_BYTES = STAGES * STAGE_BYTES + OUT_BYTES + 1024 /*align*/ + BAR_BYTES + BN * 4 /*bias*/;
-    static_assert((3 * 8 + 2 * 4 + 2) * 8 + 4 <= BAR_BYTES, "barrier area");
+    static constexpr uint32_t B_RES_MAX = RB ? SMEM_LIMIT - SMEM_BYTES : 0;
+    static_assert((3 * 8 + 2 * 4 + 3) * 8 + 4 <= BAR_BYTES, "barrier area");
     static_assert(TMEM_COLS <= 512 && (TMEM_COLS & (TMEM_COLS - 1)) == 0, "TMEM columns");
     static_assert(TBUFS >= 2, "need at least two TMEM buffers");
 };
 
-// Persistent: CTA b processes tiles b, b + gridDim.x, ... (N tile fastest, so the CTAs running
-// together share A tiles in L2). The shared-memory stage ring and the TMEM buffer ring run on
-// a K-block counter that continues across tiles, so the next tile's loads and MMAs overlap
-// this tile's drain and epilogue.
-template <int BN, int MODE>
+// Persistent. Default order: CTA b processes tiles b, b + gridDim.x, ... (N tile fastest, so the
+// CTAs running together share A tiles in L2). B-resident order: CTA b keeps N tile b % n_tiles
+// and walks the M tiles b / n_tiles, + gridDim.x / n_tiles, ... The shared-memory stage ring and
+// the TMEM buffer ring run on a K-block counter that continues across tiles, so the next tile's
+// loads and MMAs overlap this tile's drain and epilogue.
+template <int BN, int MODE, int RB>
 __global__ void __launch_bounds__(192, 1) umma_gemm_kernel(const __grid_constant__ Params p) {
-    using C = Cfg<BN, MODE>;
+    using C = Cfg<BN, MODE, RB>;
     constexpr int S = C::STAGES;
     constexpr int R = C::REGIONS;
     constexpr int TB = C::TBUFS;
     extern __shared__ uint8_t smem_raw[];
     uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-    auto a_tile = [&](int s) { return smem + (size_t)s * C::STAGE_BYTES; };
-    auto b_tile = [&](int s) { return smem + (size_t)s * C::STAGE_BYTES + A_TILE_BYTES; };
-    auto blo_tile = [&](int s) { return smem + (size_t)s * C::STAGE_BYTES + A_TILE_BYTES + C::B_TILE_BYTES; };
-    auto alo_tile = [&](int s) { return smem + (size_t)s * C::STAGE_BYTES + A_TILE_BYTES + 2 * C::B_TILE_BYTES; };
-    uint8_t *out_tile = smem + (size_t)S * C::STAGE_BYTES;  // 1024-aligned
+    // [B panel (B-resident only)] [stages] [output staging] [barriers] [bias]
+    uint8_t *b_panel = smem;
+    uint8_t *stages = smem + (RB ? p.b_res_bytes : 0u);
+    auto a_tile = [&](int s) { return stages + (size_t)s * C::STAGE_BYTES; };
+    auto alo_tile = [&](int s) { return stages + (size_t)s * C::STAGE_BYTES + A_TILE_BYTES; };
+    // B_hi of K block kb (B_lo follows it directly: the stacked [B_hi; B_lo] operand)
+    auto b_tile = [&](int s, int kb) {
+        return RB ? b_panel + (size_t)kb * 2 * C::B_TILE_BYTES
+                  : stages + (size_t)s * C::STAGE_BYTES + A_TILE_BYTES + (MODE == STRICT ? A_TILE_BYTES : 0);
+    };
+    uint8_t *out_tile = stages + (size_t)S * C::STAGE_BYTES;  // 1024-aligned
     uint64_t *full = reinterpret_cast<uint64_t *>(out_tile + C::OUT_BYTES);
     uint64_t *empty = full + S;
     uint64_t *split = empty + S;
@@ -323,12 +351,26 @@ __global__ void __launch_bounds__(192, 1) umma_gemm_kernel(const __grid_constant
     uint64_t *tempty = tfull + TB;     // [TB] the epilogue has drained TMEM buffer b
     uint64_t *mma_done = tempty + TB;  // every issued MMA has completed
     uint64_t *res_full = mma_done + 1; // a tile's residual has landed in the staging tile
-    uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(res_full + 1);
+    uint64_t *bres_full = res_full + 1; // the B panel has landed (B-resident)
+    uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(bres_full + 1);
     float *bias_s = reinterpret_cast<float *>(out_tile + C::OUT_BYTES + C::BAR_BYTES);  // [BN] this tile's bias
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int num_kb = p.num_kb;
-    const int total_tiles = p.n_tiles * (int)ceil_div_dev(p.M, BM);
+    const int total_tiles = p.n_tiles * p.m_tiles;
+    // the i-th tile of this CTA as (M tile, N tile); false past the last
+    auto tile_at = [&](int i, int &mt, int &nt) -> bool {
+        if (RB) {
+            const int per = (int)gridDim.x / p.n_tiles;
+            nt = (int)blockIdx.x % p.n_tiles;
+            mt = (int)blockIdx.x / p.n_tiles + i * per;
+            return (int)blockIdx.x < per * p.n_tiles && mt < p.m_tiles;
+        }
+        const int t = (int)blockIdx.x + i * (int)gridDim.x;
+        nt = t % p.n_tiles;
+        mt = t / p.n_tiles;
+        return t < total_tiles;
+    };
 
     if (threadIdx.x == 0) {
         for (int s = 0; s < S; ++s) {
@@ -342,6 +384,7 @@ __global__ void __launch_bounds__(192, 1) umma_gemm_kernel(const __grid_constant
         }
         mbar_init(mma_done, 1);
         mbar_init(res_full, 1);
+        mbar_init(bres_full, 1);
         fence_barrier_init();
     }
     if (warp == 1) tmem_alloc(tmem_slot, C::TMEM_COLS);
@@ -353,11 +396,20 @@ __global__ void __launch_bounds__(192, 1) umma_gemm_kernel(const __grid_constant
     if (warp == 0) {
         if (lane == 0) {
             // ---------------- TMA producer ----------------
-            constexpr uint32_t bytes = A_TILE_BYTES + 2 * C::B_TILE_BYTES;
+            constexpr uint32_t bytes = A_TILE_BYTES + (RB ? 0 : 2 * C::B_TILE_BYTES);
             long long g = 0;  // K blocks issued so far
             bool ok = true;
-            for (int tile = blockIdx.x; tile < total_tiles && ok; tile += gridDim.x) {
-                const int n0 = (tile % p.n_tiles) * BN, m0 = (tile / p.n_tiles) * BM;
+            int mt, nt;
+            if (RB && tile_at(0, mt, nt)) {  // this CTA's B panel, once
+                mbar_expect_tx(bres_full, p.b_res_bytes);
+#pragma unroll 1
+                for (int kb = 0; kb < num_kb; ++kb) {
+                    tma_load_2d(b_tile(0, kb), &p.tmB, bres_full, kb * BK, nt * BN);
+                    tma_load_2d(b_tile(0, kb) + C::B_TILE_BYTES, &p.tmBlo, bres_full, kb * BK, nt * BN);
+                }
+            }
+            for (int i = 0; ok && tile_at(i, mt, nt); ++i) {
+                const int n0 = nt * BN, m0 = mt * BM;
                 int wb = 0, hb = 0, nb = 0;
                 if (p.im2col) {
                     const int hw = p.OH * p.OW;
@@ -376,7 +428,19 @@ __global__ void __launch_bounds__(192, 1) umma_gemm_kernel(const __grid_constant
                         break;
                     }
                     mbar_expect_tx(&full[s], bytes);
-                    if (p.im2col == 2) {
+                    if (p.im2col == 3) {
+                        // window rows: the K block is 32 consecutive floats of the padded image
+                        // row (kh) starting at the window origin, for wrows output pixels per box
+                        const int kh = kb / p.cblocks, x0 = (kb - kh * p.cblocks) * BK;
+                        const int hw = p.OH * p.OW;
+#pragma unroll 1
+                        for (int r0 = 0; r0 < BM; r0 += p.wrows) {
+                            const int m = m0 + r0;
+                            const int img = m / hw, rem = m - img * hw;
+                            const int oh = rem / p.OW, ow = rem - oh * p.OW;
+                            tma_load_5d(a_tile(s) + r0 * 128, &p.tmA, &full[s], x0, ow, oh, img, kh);
+                        }
+                    } else if (p.im2col == 2) {
                         // eight 4-channel boxes; K column k = tap * cpix + channel. Columns past
                         // the real K reload tap 0 (their weights are zero: B reads as zero there)
 #pragma unroll 1
@@ -397,14 +461,17 @@ __global__ void __launch_bounds__(192, 1) umma_gemm_kernel(const __grid_constant
                     } else {
                         tma_load_2d(a_tile(s), &p.tmA, &full[s], kb * BK, m0);
                     }
-                    tma_load_2d(b_tile(s), &p.tmB, &full[s], kb * BK, n0);
-                    tma_load_2d(blo_tile(s), &p.tmBlo, &full[s], kb * BK, n0);
+                    if (!RB) {
+                        tma_load_2d(b_tile(s, kb), &p.tmB, &full[s], kb * BK, n0);
+                        tma_load_2d(b_tile(s, kb) + C::B_TILE_BYTES, &p.tmBlo, &full[s], kb * BK, n0);
+                    }
                 }
             }
             // the copies of the last (up to S) issued K blocks must have landed before exit
             for (long long k = g - 1; k >= 0 && k >= g - S; --k) {
                 if (!mbar_wait(&full[k % S], (uint32_t)((k / S) & 1))) set_error(p.err, MGC_CUDA_TIMEOUT);
             }
+            if (RB && tile_at(0, mt, nt) && !mbar_wait(bres_full, 0)) set_error(p.err, MGC_CUDA_TIMEOUT);
         }
     } else if (warp == 1) {
         if (lane == 0) {
@@ -413,7 +480,12 @@ __global__ void __launch_bounds__(192, 1) umma_gemm_kernel(const __grid_constant
             constexpr uint32_t idesc2 = instr_desc_tf32(2 * BN);  // the stacked [B_hi; B_lo] tile
             long long g = 0;
             bool ok = true;
-            for (int tile = blockIdx.x; tile < total_tiles && ok; tile += gridDim.x) {
+            int mt, nt;
+            if (RB && tile_at(0, mt, nt) && !mbar_wait(bres_full, 0)) {
+                set_error(p.err, MGC_CUDA_TIMEOUT);
+                ok = false;
+            }
+            for (int i = 0; ok && tile_at(i, mt, nt); ++i) {
                 for (int kb = 0; kb < num_kb; ++kb, ++g) {
                     const int s = (int)(g % S);
                     const int b = (int)(g % TB);
@@ -428,8 +500,8 @@ __global__ void __launch_bounds__(192, 1) umma_gemm_kernel(const __grid_constant
                         break;
                     }
                     tc_fence_after();
-                    const uint32_t a_addr = smem_addr(a_tile(s)), b_addr = smem_addr(b_tile(s));
-                    const uint32_t bl_addr = smem_addr(blo_tile(s)), al_addr = smem_addr(alo_tile(s));
+                    const uint32_t a_addr = smem_addr(a_tile(s)), b_addr = smem_addr(b_tile(s, kb));
+                    const uint32_t bl_addr = b_addr + C::B_TILE_BYTES, al_addr = smem_addr(alo_tile(s));
                     const uint32_t dbase = tmem_base + (uint32_t)(b * C::BUF_COLS);
 #pragma unroll
                     for (int k = 0; k < BK / 8; ++k) {  // 8 tf32 = 32 bytes per MMA
@@ -548,17 +620,18 @@ __global__ void __launch_bounds__(192, 1) umma_gemm_kernel(const __grid_constant
         const bool cheap = p.act == MGC_ACT_NONE || p.act == MGC_ACT_RELU || p.act == MGC_ACT_CLIP;
         const bool act_in_step1 = cheap && !res_direct;
         const bool issuer = warp == 2 && lane == 0;
-        auto issue_residual = [&](int t) {
-            const int tn0 = (t % p.n_tiles) * BN, tm0 = (t / p.n_tiles) * BM;
+        auto issue_residual = [&](int mt_, int nt_) {
+            const int tn0 = nt_ * BN, tm0 = mt_ * BM;
             mbar_expect_tx(res_full, C::OUT_BYTES);
 #pragma unroll 1
             for (int sl = 0; sl < BN / 32; ++sl)
                 tma_load_2d(out_tile + sl * (BM * 128), &p.tmR, res_full, tn0 + sl * 32, tm0);
         };
-        if (res_tma && issuer && (int)blockIdx.x < total_tiles) issue_residual(blockIdx.x);
+        int mt, nt;
+        if (res_tma && issuer && tile_at(0, mt, nt)) issue_residual(mt, nt);
         int local = 0;  // tiles this CTA has finished
-        for (int tile = blockIdx.x; tile < total_tiles && ok; tile += gridDim.x, ++local) {
-            const int n0 = (tile % p.n_tiles) * BN, m0 = (tile / p.n_tiles) * BM;
+        for (int i = 0; ok && tile_at(i, mt, nt); ++i, ++local) {
+            const int n0 = nt * BN, m0 = mt * BM;
 #pragma unroll
             for (int j = 0; j < BN; ++j) acc[j] = AccT(0);
             for (int kb = 0; kb < num_kb && ok; ++kb) {
@@ -663,7 +736,8 @@ __global__ void __launch_bounds__(192, 1) umma_gemm_kernel(const __grid_constant
                     for (int sl = 0; sl < BN / 32; ++sl)
                         tma_store_2d(&p.tmC, out_tile + sl * (BM * 128), n0 + sl * 32, m0);
                     tma_store_commit_and_wait();
-                    if (res_tma && tile + (int)gridDim.x < total_tiles) issue_residual(tile + gridDim.x);
+                    int mt2, nt2;
+                    if (res_tma && tile_at(i + 1, mt2, nt2)) issue_residual(mt2, nt2);
                 }
             }
         }
@@ -744,14 +818,52 @@ inline bool make_map_im2col(CUtensorMap *map, const GemmParams &g, bool tf32, in
     return r == CUDA_SUCCESS;
 }
 
-template <int BN, int MODE>
+// Window rows of a spatially padded NHWC image (C channels, Hp x Wp, no further padding needed):
+// element (x, ow, oh, n, kh) = image[n][oh*SH + kh*DH][ow*SW + x / C][x % C] for x < KW * C, the
+// contiguous run that one filter row of a window covers. Consecutive output pixels overlap (their
+// stride SW*C*4 bytes is below the 128-byte box row), so a TMA tile box {32, wrows, 1, 1, 1}
+// reads 128-byte rows with no gather; x past KW * C is outside the tensor and reads as zero.
+inline bool make_map_window(CUtensorMap *map, const GemmParams &g, int wrows, bool tf32) {
+    auto fn = encode_tiled_fn();
+    if (!fn) return false;
+    const long long nimg = (long long)g.M / ((long long)g.OH * g.OW);
+    const long long px = (long long)g.C * 4;  // bytes per pixel
+    cuuint64_t dims[5] = {(cuuint64_t)g.KW * g.C, (cuuint64_t)g.OW, (cuuint64_t)g.OH, (cuuint64_t)nimg, (cuuint64_t)g.KH};
+    cuuint64_t strides[4] = {(cuuint64_t)(g.SW * px), (cuuint64_t)(g.SH * g.W * px), (cuuint64_t)((long long)g.H * g.W * px),
+                             (cuuint64_t)(g.DH * g.W * px)};
+    cuuint32_t box[5] = {(cuuint32_t)BK, (cuuint32_t)wrows, 1, 1, 1};
+    cuuint32_t estr[5] = {1, 1, 1, 1, 1};
+    CUresult r = fn(map, tf32 ? CU_TENSOR_MAP_DATA_TYPE_TFLOAT32 : CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 5,
+                    const_cast<float *>(g.a), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                    CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    return r == CUDA_SUCCESS;
+}
+
+template <int BN, int MODE, int RB>
 inline int launch(const Params &p, int grid, cudaStream_t stream) {
-    using C = Cfg<BN, MODE>;
+    using C = Cfg<BN, MODE, RB>;
+    const uint32_t smem = C::SMEM_BYTES + (RB ? p.b_res_bytes : 0u);
     // per device (the attribute belongs to the current context); cheap, and allowed under capture
-    MGC_CHECK_CUDA(cudaFuncSetAttribute(umma_gemm_kernel<BN, MODE>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                        (int)C::SMEM_BYTES));
-    umma_gemm_kernel<BN, MODE><<<grid, 192, C::SMEM_BYTES, stream>>>(p);
+    MGC_CHECK_CUDA(cudaFuncSetAttribute(umma_gemm_kernel<BN, MODE, RB>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                        (int)smem));
+    umma_gemm_kernel<BN, MODE, RB><<<grid, 192, smem, stream>>>(p);
     return check_launch("umma_gemm_kernel");
+}
+
+// The B-resident variant when this CTA's B panel fits beside its stages and every CTA walks at
+// least two M tiles (else loading the panel per tile costs the same).
+template <int BN, int MODE>
+inline int launch_best(Params &p, long long m_tiles, cudaStream_t stream) {
+    const int sms = sm_count();
+    const uint32_t panel = (uint32_t)p.num_kb * 2u * Cfg<BN, MODE, 1>::B_TILE_BYTES;
+    const int per = p.n_tiles <= sms ? sms / p.n_tiles : 0;
+    if (per > 0 && panel <= Cfg<BN, MODE, 1>::B_RES_MAX && m_tiles >= 2LL * per) {
+        p.b_res_bytes = panel;
+        return launch<BN, MODE, 1>(p, per * p.n_tiles, stream);
+    }
+    p.b_res_bytes = 0;
+    const long long tiles = (long long)p.n_tiles * m_tiles;
+    return launch<BN, MODE, 0>(p, (int)(tiles < sms ? tiles : sms), stream);
 }
 
 }  // namespace umma
@@ -784,17 +896,35 @@ inline int try_gemm_umma(const GemmParams &p, cudaStream_t stream, int *taken) {
         u.num_kb = (int)ceil_div(p.K, umma::BK);
     } else if (p.a_kind == MGC_CONV_NHWC) {
         if (p.cg != p.C || p.c_off != 0 || (p.C & 3) || p.b_cpad <= 0) return MGC_CUDA_OK;
-        const int lw = -p.PL, lh = -p.PT;
-        const int uw = (p.OW - 1) * p.SW - p.PL - (p.W - 1), uh = (p.OH - 1) * p.SH - p.PT - (p.H - 1);
-        if (lw < -128 || lh < -128 || uw > 127 || uh > 127 || uw < -128 || uh < -128) return MGC_CUDA_OK;
-        if (p.SW > 8 || p.SH > 8 || (p.KW - 1) * p.DW > 65535 || (p.KH - 1) * p.DH > 65535) return MGC_CUDA_OK;
         if (p.M % (p.OH * p.OW)) return MGC_CUDA_OK;
+        // window rows when the lowering laid B out as [N][KH][L] over a padded image (win_rows);
         // tap-packed when B is K-major over (kh, kw, channel) without channel padding (b_cpad ==
         // C < 32); otherwise one K block per filter tap and 32-channel block
-        const bool packed = p.b_cpad == p.C && p.C < umma::BK;
-        if (!packed && (p.b_cpad & (umma::BK - 1))) return MGC_CUDA_OK;
-        if (!umma::make_map_im2col(&u.tmA, p, a_tf32, packed ? 4 : umma::BK)) return MGC_CUDA_OK;
-        if (packed) {
+        const bool window = p.win_rows > 0;
+        const bool packed = !window && p.b_cpad == p.C && p.C < umma::BK;
+        if (!window) {  // limits of the im2col tensor map: corner offsets, traversal strides
+            const int lw = -p.PL, lh = -p.PT;
+            const int uw = (p.OW - 1) * p.SW - p.PL - (p.W - 1), uh = (p.OH - 1) * p.SH - p.PT - (p.H - 1);
+            if (lw < -128 || lh < -128 || uw > 127 || uh > 127 || uw < -128 || uh < -128) return MGC_CUDA_OK;
+            if (p.SW > 8 || p.SH > 8 || (p.KW - 1) * p.DW > 65535 || (p.KH - 1) * p.DH > 65535) return MGC_CUDA_OK;
+        }
+        if (window) {
+            if (p.PT || p.PL || p.DW != 1 || p.OW % p.win_rows || umma::BM % p.win_rows ||
+                p.win_L != (int)ceil_div(p.KW * p.C, umma::BK) * umma::BK ||
+                (long long)(p.OW - 1) * p.SW + p.KW > p.W ||
+                (long long)(p.OH - 1) * p.SH + (long long)(p.KH - 1) * p.DH >= p.H)
+                return MGC_CUDA_OK;
+            if (!umma::make_map_window(&u.tmA, p, p.win_rows, a_tf32)) return MGC_CUDA_OK;
+            u.im2col = 3;
+            u.wrows = p.win_rows;
+            u.cblocks = p.win_L / umma::BK;
+            u.num_kb = p.KH * u.cblocks;
+            kp = p.KH * p.win_L;
+        } else if (!packed && (p.b_cpad & (umma::BK - 1))) {
+            return MGC_CUDA_OK;
+        } else if (!umma::make_map_im2col(&u.tmA, p, a_tf32, packed ? 4 : umma::BK)) {
+            return MGC_CUDA_OK;
+        } else if (packed) {
             u.im2col = 2;
             u.cpix = p.C;
             u.kreal = p.KH * p.KW * p.C;
@@ -816,8 +946,10 @@ inline int try_gemm_umma(const GemmParams &p, cudaStream_t stream, int *taken) {
     if (!umma::make_map_2d(&u.tmB, p.b_umma, p.N, kp, kp, bn)) return MGC_CUDA_OK;
     if (!umma::make_map_2d(&u.tmBlo, p.b_umma_lo, p.N, kp, kp, bn)) return MGC_CUDA_OK;
     u.n_tiles = (int)ceil_div(p.N, bn);
-    const long long tiles = (long long)u.n_tiles * ceil_div(p.M, umma::BM);
+    const long long m_tiles = ceil_div(p.M, umma::BM);
+    const long long tiles = (long long)u.n_tiles * m_tiles;
     if (tiles > 0x7FFFFFFF) return MGC_CUDA_OK;
+    u.m_tiles = (int)m_tiles;
     u.c = p.c; u.ldc = p.ldc; u.bias = p.bias; u.res = p.res; u.ldr = p.ldr;
     u.alpha = p.alpha; u.lo = p.lo; u.hi = p.hi; u.act = p.act;
     u.err = p.err;
@@ -829,11 +961,10 @@ inline int try_gemm_umma(const GemmParams &p, cudaStream_t stream, int *taken) {
                  umma::make_map_2d(&u.tmR, p.res, p.M, p.N, p.ldr, umma::BM)) ? 1 : 0;
     if (p.res && !u.tma_res) u.tma_out = 0;
     // persistent grid: one CTA per SM (the shared-memory footprint allows no more)
-    const int grid = (int)(tiles < sm_count() ? tiles : sm_count());
     int st;
-    if (strict) st = umma::launch<64, umma::STRICT>(u, grid, stream);
-    else if (bn == 64) st = umma::launch<64, umma::TF32>(u, grid, stream);
-    else st = umma::launch<128, umma::TF32>(u, grid, stream);
+    if (strict) st = umma::launch_best<64, umma::STRICT>(u, m_tiles, stream);
+    else if (bn == 64) st = umma::launch_best<64, umma::TF32>(u, m_tiles, stream);
+    else st = umma::launch_best<128, umma::TF32>(u, m_tiles, stream);
     if (st != MGC_CUDA_OK) return st;
     *taken = 1;
     return MGC_CUDA_OK;

@@ -423,31 +423,34 @@ __global__ void __launch_bounds__(256) im2col_nhwc_kernel(const __grid_constant_
     }
 }
 
-// Channel packing: out[n, h, w, c] (NHWC, cp channels, cp % 4 == 0) = x at n*sn + h*sh + w*sw +
-// c*sc for c < C, zero for C <= c < cp. One thread per pixel; the source reads of neighbouring
-// threads are neighbouring for both NCHW (sw = 1) and NHWC (sc = 1) sources, and every write is a
-// 16-byte store.
+// Channel packing with optional spatial padding: out is NHWC [N][Hp][Wp][cp] (cp % 4 == 0) with
+// out[n, PT + h, PL + w, c] = x at n*sn + h*sh + w*sw + c*sc for h < H, w < W, c < C, and zero
+// everywhere else (padding channels and the border). One thread per output pixel; the source
+// reads of neighbouring threads are neighbouring for both NCHW (sw = 1) and NHWC (sc = 1)
+// sources, and every write is a 16-byte store.
 struct PackParams {
-    int N, H, W, C, cp;
+    int N, H, W, C, cp, PT, PL, Hp, Wp;
     long long sn, sh, sw, sc;
     const float *x;
     float *out;
 };
 
 __global__ void __launch_bounds__(256) pack_nhwc_kernel(const __grid_constant__ PackParams p) {
-    const long long hw = (long long)p.H * p.W;
+    const long long hw = (long long)p.Hp * p.Wp;
     const long long total = (long long)p.N * hw;
     const long long stride = (long long)gridDim.x * blockDim.x;
     for (long long e = (long long)blockIdx.x * blockDim.x + threadIdx.x; e < total; e += stride) {
         const long long n = e / hw;
         const long long r = e - n * hw;
-        const long long h = r / p.W, w = r - h * p.W;
+        const long long h = r / p.Wp - p.PT, w = r % p.Wp - p.PL;
+        const bool inside = h >= 0 && h < p.H && w >= 0 && w < p.W;
         const float *src = p.x + n * p.sn + h * p.sh + w * p.sw;
         float4 *dst = reinterpret_cast<float4 *>(p.out + e * p.cp);
         for (int c0 = 0; c0 < p.cp; c0 += 4) {
             float v[4];
 #pragma unroll
-            for (int t = 0; t < 4; ++t) v[t] = c0 + t < p.C ? __ldg(src + (long long)(c0 + t) * p.sc) : 0.0f;
+            for (int t = 0; t < 4; ++t)
+                v[t] = inside && c0 + t < p.C ? __ldg(src + (long long)(c0 + t) * p.sc) : 0.0f;
             dst[c0 >> 2] = make_float4(v[0], v[1], v[2], v[3]);
         }
     }

@@ -95,6 +95,7 @@ inline int decode_gemm(const mgc_cuda_launch &L, const Bases &bases, GemmParams 
     MGC_RESOLVE(L.r[6], p.b_umma);
     MGC_RESOLVE(L.r[7], p.b_umma_lo);
     p.b_cpad = (int)i[50];
+    p.win_rows = (int)i[51]; p.win_L = (int)i[52];
     if (!p.a || !p.b || !p.c) return fail(MGC_CUDA_BAD_ARGUMENT, "gemm: missing operand");
     return MGC_CUDA_OK;
 }
@@ -389,10 +390,14 @@ inline int launch_record(const mgc_cuda_launch &L, const int64_t *aux, int64_t a
         PackParams p{};
         p.N = (int)i[0]; p.H = (int)i[1]; p.W = (int)i[2]; p.C = (int)i[3]; p.cp = (int)i[4];
         p.sn = i[5]; p.sh = i[6]; p.sw = i[7]; p.sc = i[8];
+        p.PT = (int)i[9]; p.PL = (int)i[10]; p.Hp = (int)i[11]; p.Wp = (int)i[12];
         MGC_RESOLVE(L.r[0], p.x); MGC_RESOLVE(L.r[1], p.out);
         if (p.cp <= 0 || (p.cp & 3) || p.C > p.cp || (reinterpret_cast<uintptr_t>(p.out) & 15))
             return fail(MGC_CUDA_BAD_ARGUMENT, "pack: %d of %d channels / output alignment", p.C, p.cp);
-        const long long total = (long long)p.N * p.H * p.W;
+        if (p.PT < 0 || p.PL < 0 || p.Hp < p.PT + p.H || p.Wp < p.PL + p.W)
+            return fail(MGC_CUDA_BAD_ARGUMENT, "pack: padded %dx%d cannot hold %dx%d at (%d, %d)", p.Hp, p.Wp,
+                        p.H, p.W, p.PT, p.PL);
+        const long long total = (long long)p.N * p.Hp * p.Wp;
         if (total == 0) { launched = 0; break; }
         pack_nhwc_kernel<<<grid_for(total, 256), 256, 0, stream>>>(p);
         st = check_launch("pack_nhwc_kernel");

@@ -424,12 +424,14 @@ class CudaEmitter:
         out = node.output
         users = out.users
         if (len(users) == 1 and users[0].inputs and users[0].inputs[0] is out and self._tap_packed(users[0])
-                and shape[3] % 4 and all(v is not out for _, v in self.graph.named_outputs())):
-            # the only use is a narrow-channel convolution that needs its channels padded: write
-            # the padded NHWC copy straight from the source (the plain transposed copy is unused)
-            self._packed[id(out)] = self._emit_pack(self.ref(x), shape[0], shape[1], shape[2], shape[3],
-                                                    [ss[p] for p in perm])
-            return
+                and all(v is not out for _, v in self.graph.named_outputs())):
+            plan = self._narrow_plan(users[0])
+            if shape[3] % 4 or plan["wrows"]:
+                # the only use is a narrow-channel convolution that reads a padded copy: write
+                # it straight from the source (the plain transposed copy would be unused)
+                self._packed[id(out)] = self._emit_pack(self.ref(x), shape[0], shape[1], shape[2], shape[3],
+                                                        [ss[p] for p in perm], plan)
+                return
         self._copy(shape, self.ref(x), [ss[p] for p in perm], 0, self.ref(node.output), _strides(shape), 0,
                    x.tensor_type.itemsize, count="transpose")
 
@@ -785,6 +787,8 @@ class CudaEmitter:
         b_umma: RefT = NO_REF,
         b_umma_lo: RefT = NO_REF,
         b_cpad: int = 0,
+        win_rows: int = 0,
+        win_L: int = 0,
     ) -> None:
         """K_GEMM slots: i[0..2] M, N, K; i[3] batch dims; i[4..7] batch extents; i[8..11],
         i[12..15], i[16..19], i[20..23] per-dimension batch strides of A, B, C, residual;
@@ -792,13 +796,15 @@ class CudaEmitter:
         SW, DH, DW, PT, PL, OW, c_off, cg; i[41..43] B kind, row stride, column stride; i[44] ldc;
         i[45] bias mode; i[46] ldr; i[47] activation; i[48] precision; i[49] OH.
         i[50] padded channel count of the tensor-core B layout of an im2col convolution (0 when
-        B is plain K-major). f[0..3] alpha, beta, clip lo, clip hi. r[0] A, r[1] B, r[2] C,
+        B is plain K-major). i[51] output pixels per window-row box and i[52] the padded window-row
+        length L when the tensor-core B is laid out [N][KH][L] over a spatially padded image (0
+        otherwise). f[0..3] alpha, beta, clip lo, clip hi. r[0] A, r[1] B, r[2] C,
         r[3] bias, r[4] residual, r[5] residual of a split constant B, r[6] / r[7] the
         tensor-core layout of a constant B (TF32-rounded part / residual), absent otherwise."""
         if len(batch) > 4:
             raise CodegenError(f"GEMM with {len(batch)} batch dimensions")
-        ints = [0] * 51
-        ints[50] = b_cpad
+        ints = [0] * 53
+        ints[50], ints[51], ints[52] = b_cpad, win_rows, win_L
         ints[0], ints[1], ints[2], ints[3] = m, n, k, len(batch)
         for d in range(len(batch)):
             ints[4 + d] = batch[d]
@@ -1030,12 +1036,35 @@ class CudaEmitter:
         pointwise = kh == kw == 1 and g.strides == (1, 1) and g.pads == (0, 0, 0, 0)
         return not pointwise and cg < 32
 
-    def _emit_pack(self, src: RefT, nb: int, h: int, w: int, c: int, strides: Sequence[int]) -> RefT:
+    def _narrow_plan(self, node: Node) -> dict[str, int]:
+        """Input layout of a tap-packed convolution: channels padded to ``cp`` (a multiple of 4)
+        and, for the window-row form (unit width dilation, OW a multiple of 8), the image padded
+        spatially to Hp x Wp with the convolution's own top / left padding, so that every window
+        row is KW * cp contiguous floats inside the image; ``wrows`` output pixels per TMA box,
+        ``L`` the window row rounded up to whole 32-float K blocks."""
+        xt, wt = node.input(0).tensor_type, node.input(1).tensor_type
+        _, h, w, _ = xt.shape
+        kh, kw, cg, _ = wt.shape
+        g = ops.window_geometry(node, (h, w), (kh, kw))
+        oh, ow = g.out_hw
+        pt, pl, _, _ = g.pads
+        cp = (cg + 3) // 4 * 4
+        wrows = 16 if ow % 16 == 0 else 8 if ow % 8 == 0 else 0
+        plan = {"cp": cp, "wrows": 0, "L": 0, "PT": 0, "PL": 0, "Hp": h, "Wp": w}
+        if wrows and g.dilations[1] == 1:
+            sh, sw = g.strides
+            plan.update(wrows=wrows, L=(kw * cp + 31) // 32 * 32, PT=pt, PL=pl,
+                        Hp=max(pt + h, (oh - 1) * sh + (kh - 1) * g.dilations[0] + 1),
+                        Wp=max(pl + w, (ow - 1) * sw + kw))
+        return plan
+
+    def _emit_pack(self, src: RefT, nb: int, h: int, w: int, c: int, strides: Sequence[int],
+                   plan: dict[str, int]) -> RefT:
         """K_PACK slots: i[0..4] N, H, W, C, padded C; i[5..8] source element strides of n, h, w,
-        c; r[0] source, r[1] packed NHWC destination."""
-        cp = (c + 3) // 4 * 4
-        dst = self._pack_region(nb * h * w * cp * 4)
-        self.emit(K_PACK, [nb, h, w, c, cp, *strides], refs=[src, dst])
+        c; i[9..12] PT, PL, padded H, padded W; r[0] source, r[1] packed NHWC destination."""
+        cp, hp, wp = plan["cp"], plan["Hp"], plan["Wp"]
+        dst = self._pack_region(nb * hp * wp * cp * 4)
+        self.emit(K_PACK, [nb, h, w, c, cp, *strides, plan["PT"], plan["PL"], hp, wp], refs=[src, dst])
         return dst
 
     def _conv_tap_packed(self, node: Node, w_hwio: np.ndarray, geo: dict[str, int], nb: int, bias: RefT,
@@ -1047,22 +1076,33 @@ class CudaEmitter:
         when that transpose has no other use)."""
         x = node.input(0)
         kh, kw, cg, kg = w_hwio.shape
-        cp = (cg + 3) // 4 * 4
-        if cp == cg:
+        plan = self._narrow_plan(node)
+        cp, window = plan["cp"], plan["wrows"] > 0
+        if cp == cg and not window:
             xref = self.ref(x)
         elif id(x) in self._packed:
             xref = self._packed[id(x)]
         else:
             xref = self._emit_pack(self.ref(x), nb, geo["H"], geo["W"], cg,
-                                   [geo["H"] * geo["W"] * cg, geo["W"] * cg, cg, 1])
+                                   [geo["H"] * geo["W"] * cg, geo["W"] * cg, cg, 1], plan)
+        wkey = id(self._root(node.input(1)))
         wpad = np.zeros((kh, kw, cp, kg), np.float32)
         wpad[:, :, :cg, :] = np.asarray(w_hwio, np.float32)
-        bref, blo, b_rs, b_cs = self._kmajor_b(wpad.reshape(kh * kw * cp, kg), ("tap-packed", id(self._root(node.input(1)))))
+        bref, blo, b_rs, b_cs = self._kmajor_b(wpad.reshape(kh * kw * cp, kg), ("tap-packed", wkey))
+        umma = {"b_umma": bref, "b_umma_lo": blo}
+        conv = {**geo, "C": cp, "c_off": 0, "cg": cp}
+        if window:
+            # the image is read from its padded copy: no padding left for the kernels to apply
+            conv.update(H=plan["Hp"], W=plan["Wp"], PT=0, PL=0)
+            # tensor-core B as [N][KH][L]: filter row kh's KW * cp weights, zero up to L
+            rows = np.zeros((kh, plan["L"], kg), np.float32)
+            rows[:, : kw * cp, :] = wpad.reshape(kh, kw * cp, kg)
+            uhi, ulo, _, _ = self._kmajor_b(rows.reshape(kh * plan["L"], kg), ("window-rows", wkey))
+            umma = {"b_umma": uhi, "b_umma_lo": ulo, "win_rows": plan["wrows"], "win_L": plan["L"]}
         m = nb * geo["OH"] * geo["OW"]
         self._gemm(
             m, kg, kh * kw * cp, xref, cp, 1, bref, b_rs, b_cs, self.ref(node.output), kg, b_lo=blo,
-            conv={**geo, "C": cp, "c_off": 0, "cg": cp}, a_kind=CONV_NHWC, bias=bias, bias_mode=1, res=res,
-            ldr=kg, act=act, b_umma=bref, b_umma_lo=blo, b_cpad=cp,
+            conv=conv, a_kind=CONV_NHWC, bias=bias, bias_mode=1, res=res, ldr=kg, act=act, b_cpad=cp, **umma,
         )
 
     # -- pooling (c.py:1228-1253) ---------------------------------------------------------------------

@@ -279,6 +279,33 @@ def _p_narrow_convs(r: np.random.Generator) -> tuple[Graph, dict[str, np.ndarray
     return g, {"x": f32(r, 2, 3, 22, 18)}
 
 
+def narrow_window_chain(r: np.random.Generator, batch: int = 2, h: int = 32, w: int = 48) -> tuple[Graph, dict[str, np.ndarray]]:
+    """Narrow-channel convolutions whose output width is a multiple of 8 (the window-row form):
+    a 7x7 stride-2 stem on 3 channels, 8 / 12 / 16 / 28 input channels with window rows of one
+    or two K blocks, height dilation 2 with width dilation 1, a residual add, and a final stride-2
+    layer whose output width (12 at the default size) falls back to tap-packed boxes."""
+    g = Graph("narrow_window")
+    x = g.add_input("x", TensorType("float32", (batch, 3, h, w)))
+
+    def conv(v: Any, cin: int, cout: int, k: tuple[int, int], **attrs: Any) -> Any:
+        wt = g.constant(f32(r, cout, cin, *k, scale=1.5 / math.sqrt(cin * k[0] * k[1])))
+        return g.add_node("Conv", [v, wt, g.constant(f32(r, cout, scale=0.1))],
+                          attrs={"kernel_shape": list(k), **attrs}).output
+
+    ps = [g.constant(a) for a in (pos(r, 8), f32(r, 8, scale=0.1), f32(r, 8, scale=0.1), pos(r, 8))]
+    h1 = conv(x, 3, 8, (7, 7), strides=[2, 2], pads=[3, 3, 3, 3])
+    h1 = g.add_node("Relu", [g.add_node("BatchNormalization", [h1, *ps], attrs={"epsilon": 1e-5}).output]).output
+    h2 = conv(h1, 8, 12, (3, 3), pads=[1, 1, 1, 1])
+    h3 = g.add_node("Relu", [conv(h2, 12, 16, (5, 5), pads=[2, 2, 2, 2])]).output
+    h4 = conv(h3, 16, 16, (3, 3), dilations=[2, 1], pads=[2, 1, 2, 1])
+    h4 = g.add_node("Relu", [g.add_node("Add", [h4, h3]).output]).output
+    h5 = g.add_node("Relu", [conv(h4, 16, 28, (3, 3), pads=[1, 1, 1, 1])]).output
+    y = conv(h5, 28, 8, (3, 3), strides=[2, 2], pads=[1, 1, 1, 1])
+    g.add_output(y, "y")
+    infer_shapes(g)
+    return g, {"x": f32(r, batch, 3, h, w)}
+
+
 def _p_dense_gelu(r: np.random.Generator) -> tuple[Graph, dict[str, np.ndarray]]:
     """MatMul + bias + erf GELU subgraph, MatMul(x, Transpose(W)), residual Add, tanh GELU."""
     g = Graph("dense_gelu")
@@ -324,6 +351,7 @@ def pattern_cases() -> list[Case]:
     return [
         _pattern("conv_block", _p_conv_block),
         _pattern("narrow_convs", _p_narrow_convs),
+        _pattern("narrow_window", narrow_window_chain),
         _pattern("dense_gelu", _p_dense_gelu),
         _pattern("layer_norm", _p_layer_norm),
         _pattern("loopfuse", _p_loopfuse),

@@ -1,0 +1,82 @@
+"""Convolution layers at sizes where the tensor-core kernel keeps each CTA's whole B panel in
+shared memory (every CTA walks at least two M tiles: M >= 2 * 148 * 128 rows for one N tile)
+and the narrow-channel window-row path runs at full width, against the float64 oracle.
+
+The small parity cases never reach these kernel variants; the benchmark models only do at
+large batch. Budgets as in the other GPU tests: 1e-4 (strict) / 2e-2 (tf32) relative to the
+largest |output|."""
+
+from __future__ import annotations
+
+import math
+
+import numpy as np
+import pytest
+
+import cases
+from mgc_cuda.runtime import compile_graph
+from ml_graph_compiler.ir import Graph, TensorType
+from ml_graph_compiler.passes import optimize
+from ml_graph_compiler.schedule import schedule
+from ml_graph_compiler.shape_inference import infer_shapes
+from oracle import runner
+
+pytestmark = pytest.mark.gpu
+
+TOL = {"strict": 1e-4, "tf32": 2e-2}
+
+
+def _bottleneck(batch: int) -> tuple[Graph, dict[str, np.ndarray]]:
+    """A ResNet-50 layer1 bottleneck (1x1 64->64, 3x3 64->64, 1x1 64->256 + projection
+    residual, ReLU) at 56x56: 1x1 K = 64 panels fit in shared memory for N tiles of 64 and 128."""
+    r = np.random.default_rng(11)
+    g = Graph("bottleneck")
+    x = g.add_input("x", TensorType("float32", (batch, 64, 56, 56)))
+
+    def conv(v, cin, cout, k):  # noqa: ANN001, ANN202
+        w = g.constant((r.standard_normal((cout, cin, k, k)) * (1.4 / math.sqrt(cin * k * k))).astype(np.float32))
+        b = g.constant((r.standard_normal(cout) * 0.1).astype(np.float32))
+        return g.add_node("Conv", [v, w, b], attrs={"kernel_shape": [k, k], "pads": [k // 2] * 4}).output
+
+    h = g.add_node("Relu", [conv(x, 64, 64, 1)]).output
+    h = g.add_node("Relu", [conv(h, 64, 64, 3)]).output
+    h = conv(h, 64, 256, 1)
+    y = g.add_node("Relu", [g.add_node("Add", [h, conv(x, 64, 256, 1)]).output]).output
+    g.add_output(y, "y")
+    infer_shapes(g)
+    optimize(g, "O3")
+    schedule(g)
+    return g, {"x": r.standard_normal((batch, 64, 56, 56)).astype(np.float32)}
+
+
+def _window_chain() -> tuple[Graph, dict[str, np.ndarray]]:
+    g, feeds = cases.narrow_window_chain(np.random.default_rng(5), batch=16, h=96, w=128)
+    optimize(g, "O3")
+    schedule(g)
+    return g, feeds
+
+
+@pytest.fixture(scope="module")
+def graphs() -> dict:
+    out = {}
+    for name, make in (("bottleneck_b16", lambda: _bottleneck(16)), ("narrow_window_b16", _window_chain)):
+        g, feeds = make()
+        out[name] = (g, feeds, runner.run(g, feeds))
+    return out
+
+
+@pytest.mark.parametrize("precision", ["strict", "tf32"])
+@pytest.mark.parametrize("name", ["bottleneck_b16", "narrow_window_b16"])
+def test_resident_panel_layers_match_oracle(name: str, precision: str, graphs: dict) -> None:
+    g, feeds, want = graphs[name]
+    model = compile_graph(g, precision=precision)
+    try:
+        got = model.run(feeds)
+        again = model.run(feeds)
+    finally:
+        model.close()
+    for k, w in want.items():
+        scale = max(float(np.abs(w).max()), 1.0)
+        err = float(np.abs(got[k].astype(np.float64) - w).max())
+        assert err <= TOL[precision] * scale, f"{name}:{k} max abs err {err:.3g} (scale {scale:.3g})"
+        np.testing.assert_array_equal(got[k], again[k])

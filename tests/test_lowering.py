@@ -37,14 +37,17 @@ def test_resnet50_o3_matches_published_structure(r50: Graph) -> None:
     assert len(low.launches) == 57
     assert low.workspace_bytes == 0
     # on the tensor cores the input transpose writes the image with its 3 channels padded to 4
-    # into the workspace, and the stem reads it as tap-packed im2col boxes
+    # and its 3-pixel border into the workspace (229 x 229: the last window row ends at column
+    # 2 * 111 + 7), and the stem reads window rows of it (B laid out [64][7][32])
     tc = lower_graph(r50, precision="tf32")
     assert tc.kernels == {"gemm": 54, "pack": 1, "pool": 1, "reduce": 1, "view": 1}
     assert tc.arena_bytes == 7_225_344
-    assert tc.workspace_bytes == 224 * 224 * 4 * 4
+    assert tc.workspace_bytes == (229 * 229 * 4 * 4 + 255) // 256 * 256
     pack, stem = tc.launches[0], tc.launches[1]
-    assert pack.kind == K_PACK and list(pack.i[:9]) == [1, 224, 224, 3, 4, 3 * 224 * 224, 224, 1, 224 * 224]
-    assert stem.kind == K_GEMM and stem.i[2] == 7 * 7 * 4 and stem.i[50] == 4
+    assert pack.kind == K_PACK
+    assert list(pack.i[:13]) == [1, 224, 224, 3, 4, 3 * 224 * 224, 224, 1, 224 * 224, 3, 3, 229, 229]
+    assert stem.kind == K_GEMM and stem.i[2] == 7 * 7 * 4 and list(stem.i[50:53]) == [4, 16, 32]
+    assert (stem.i[27], stem.i[28], stem.i[29], stem.i[36], stem.i[37]) == (229, 229, 4, 0, 0)
     assert (stem.r[0].space, stem.r[0].offset) == (pack.r[1].space, pack.r[1].offset)
 
 
