@@ -64,8 +64,8 @@ constexpr double STEP_BIAS = 2.5e-8;
 
 struct Params {
     CUtensorMap tmA;
-    CUtensorMap tmB;
-    CUtensorMap tmBlo;
+    CUtensorMap tmB;                 // B's TF32 part, K-major [N][Kp]
+    CUtensorMap tmBlo;               // B's residual, same layout
     CUtensorMap tmC;                 // output tile store (when tma_out)
     CUtensorMap tmR;                 // residual tile load (when tma_res)
     int tma_out, tma_res;
@@ -161,6 +161,11 @@ __device__ __forceinline__ void tma_load_5d(void *dst, const CUtensorMap *map, u
         ::"r"(smem_addr(dst)), "l"(reinterpret_cast<uint64_t>(map)), "r"(smem_addr(bar)), "r"(x), "r"(y), "r"(z),
         "r"(w), "r"(v)
         : "memory");
+}
+
+// Warm the TMA unit's descriptor cache with a tensor map (kernel-parameter copies included).
+__device__ __forceinline__ void prefetch_tmap(const CUtensorMap *map) {
+    asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(map)) : "memory");
 }
 
 __device__ __forceinline__ void tma_store_2d(const CUtensorMap *map, const void *src, int x, int y) {
@@ -393,9 +398,81 @@ __global__ void __launch_bounds__(192, 1) umma_gemm_kernel(const __grid_constant
     tc_fence_after();
     const uint32_t tmem_base = *tmem_slot;
 
-    if (warp == 0) {
+    if (warp == 0 && p.im2col >= 2) {
+        // ---------------- TMA producer, narrow-channel forms (the whole warp) ----------------
+        // A TMA instruction holds its issuing thread for a few hundred cycles. These forms need
+        // eight or more A boxes per K block, so lane j issues box j, all in one instruction.
+        // Lane 0 alone waits on the ring, arms the barrier and loads B; the warp reconverges
+        // before the loads.
+        constexpr uint32_t bytes = A_TILE_BYTES + (RB ? 0 : 2 * C::B_TILE_BYTES);
+        long long g = 0;  // K blocks issued so far
+        bool ok = true;
+        int mt, nt;
+        if (RB && tile_at(0, mt, nt)) {  // this CTA's B panel, once: lane j loads K blocks j, j+32, ...
+            if (lane == 0) mbar_expect_tx(bres_full, p.b_res_bytes);
+            __syncwarp();
+            for (int kb = lane; kb < num_kb; kb += 32) {
+                tma_load_2d(b_tile(0, kb), &p.tmB, bres_full, kb * BK, nt * BN);
+                tma_load_2d(b_tile(0, kb) + C::B_TILE_BYTES, &p.tmBlo, bres_full, kb * BK, nt * BN);
+            }
+        }
+        for (int i = 0; ok && tile_at(i, mt, nt); ++i) {
+            const int n0 = nt * BN, m0 = mt * BM;
+            const int hw = p.OH * p.OW;
+            const int nb = m0 / hw;
+            const int rem0 = m0 - nb * hw;
+            const int oh0 = rem0 / p.OW, ow0 = rem0 - oh0 * p.OW;
+            const int wb = ow0 * p.SW - p.PL, hb = oh0 * p.SH - p.PT;
+            for (int kb = 0; kb < num_kb; ++kb, ++g) {
+                const int s = (int)(g % S);
+                const long long round = g / S;
+                int waited = 1;
+                if (lane == 0) {
+                    if (round > 0 && !mbar_wait(&empty[s], (uint32_t)((round - 1) & 1))) waited = 0;
+                    else mbar_expect_tx(&full[s], bytes);
+                }
+                if (!__shfl_sync(0xffffffffu, waited, 0)) {
+                    if (lane == 0) set_error(p.err, MGC_CUDA_TIMEOUT);
+                    ok = false;
+                    break;
+                }
+                if (p.im2col == 3) {
+                    // window rows: the K block is 32 consecutive floats of the padded image row
+                    // (kh) starting at the window origin, for wrows output pixels per box
+                    const int kh = kb / p.cblocks, x0 = (kb - kh * p.cblocks) * BK;
+                    for (int r0 = lane * p.wrows; r0 < BM; r0 += 32 * p.wrows) {
+                        const int m = m0 + r0;
+                        const int img = m / hw, rem = m - img * hw;
+                        const int oh = rem / p.OW, ow = rem - oh * p.OW;
+                        tma_load_5d(a_tile(s) + r0 * 128, &p.tmA, &full[s], x0, ow, oh, img, kh);
+                    }
+                } else if (lane < BK / 4) {
+                    // tap-packed: eight 4-channel boxes; K column k = tap * cpix + channel.
+                    // Columns past the real K reload tap 0 (their weights are zero)
+                    const int k0 = kb * BK + lane * 4;
+                    const int tap = k0 < p.kreal ? k0 / p.cpix : 0;
+                    const int ch = k0 < p.kreal ? k0 - tap * p.cpix : 0;
+                    const int kw = tap % p.KW, kh = tap / p.KW;
+                    tma_load_im2col_4d(a_tile(s) + lane * PACKED_BOX_BYTES, &p.tmA, &full[s], ch, wb, hb, nb,
+                                       (uint16_t)(kw * p.DW), (uint16_t)(kh * p.DH));
+                }
+                if (!RB && lane == 0) {
+                    tma_load_2d(b_tile(s, kb), &p.tmB, &full[s], kb * BK, n0);
+                    tma_load_2d(b_tile(s, kb) + C::B_TILE_BYTES, &p.tmBlo, &full[s], kb * BK, n0);
+                }
+                __syncwarp();
+            }
+        }
+        // the copies of the last (up to S) issued K blocks must have landed before exit
         if (lane == 0) {
-            // ---------------- TMA producer ----------------
+            for (long long k = g - 1; k >= 0 && k >= g - S; --k) {
+                if (!mbar_wait(&full[k % S], (uint32_t)((k / S) & 1))) set_error(p.err, MGC_CUDA_TIMEOUT);
+            }
+            if (RB && tile_at(0, mt, nt) && !mbar_wait(bres_full, 0)) set_error(p.err, MGC_CUDA_TIMEOUT);
+        }
+    } else if (warp == 0) {
+        if (lane == 0) {
+            // ---------------- TMA producer: one A box per K block (lane 0) ----------------
             constexpr uint32_t bytes = A_TILE_BYTES + (RB ? 0 : 2 * C::B_TILE_BYTES);
             long long g = 0;  // K blocks issued so far
             bool ok = true;
@@ -428,31 +505,7 @@ __global__ void __launch_bounds__(192, 1) umma_gemm_kernel(const __grid_constant
                         break;
                     }
                     mbar_expect_tx(&full[s], bytes);
-                    if (p.im2col == 3) {
-                        // window rows: the K block is 32 consecutive floats of the padded image
-                        // row (kh) starting at the window origin, for wrows output pixels per box
-                        const int kh = kb / p.cblocks, x0 = (kb - kh * p.cblocks) * BK;
-                        const int hw = p.OH * p.OW;
-#pragma unroll 1
-                        for (int r0 = 0; r0 < BM; r0 += p.wrows) {
-                            const int m = m0 + r0;
-                            const int img = m / hw, rem = m - img * hw;
-                            const int oh = rem / p.OW, ow = rem - oh * p.OW;
-                            tma_load_5d(a_tile(s) + r0 * 128, &p.tmA, &full[s], x0, ow, oh, img, kh);
-                        }
-                    } else if (p.im2col == 2) {
-                        // eight 4-channel boxes; K column k = tap * cpix + channel. Columns past
-                        // the real K reload tap 0 (their weights are zero: B reads as zero there)
-#pragma unroll 1
-                        for (int j = 0; j < BK / 4; ++j) {
-                            const int k0 = kb * BK + j * 4;
-                            const int tap = k0 < p.kreal ? k0 / p.cpix : 0;
-                            const int ch = k0 < p.kreal ? k0 - tap * p.cpix : 0;
-                            const int kw = tap % p.KW, kh = tap / p.KW;
-                            tma_load_im2col_4d(a_tile(s) + j * PACKED_BOX_BYTES, &p.tmA, &full[s], ch, wb, hb, nb,
-                                               (uint16_t)(kw * p.DW), (uint16_t)(kh * p.DH));
-                        }
-                    } else if (p.im2col) {
+                    if (p.im2col) {
                         const int cb = kb % p.cblocks;
                         const int t = kb / p.cblocks;
                         const int kw = t % p.KW, kh = t / p.KW;
@@ -620,6 +673,8 @@ __global__ void __launch_bounds__(192, 1) umma_gemm_kernel(const __grid_constant
         const bool cheap = p.act == MGC_ACT_NONE || p.act == MGC_ACT_RELU || p.act == MGC_ACT_CLIP;
         const bool act_in_step1 = cheap && !res_direct;
         const bool issuer = warp == 2 && lane == 0;
+        if (issuer && p.tma_out) prefetch_tmap(&p.tmC);
+        if (issuer && p.tma_res) prefetch_tmap(&p.tmR);
         auto issue_residual = [&](int mt_, int nt_) {
             const int tn0 = nt_ * BN, tm0 = mt_ * BM;
             mbar_expect_tx(res_full, C::OUT_BYTES);

@@ -139,3 +139,4 @@ def test_algorithmic_cost_of_resnet50(r50: Graph) -> None:
     flops, nbytes = lowering.algorithmic_cost(r50)
     assert abs(flops / 1e9 - 8.178) < 0.01
     assert 200e6 < nbytes < 230e6
+
