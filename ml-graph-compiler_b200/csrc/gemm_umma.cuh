@@ -25,8 +25,9 @@
 //   while the tensor core works on the next block. In strict mode each of the four K=8 steps of a
 //   block gets its own region, so no tensor-core accumulation chain is longer than one step.
 //
-// Roles: warp 0 lane 0 issues TMA; warp 1 allocates TMEM and lane 0 issues tcgen05.mma; warps 2-5
-// (128 threads, one TMEM lane each) split A (strict), drain TMEM, and run the epilogue.
+// Roles: warp 0 issues TMA (lane 0, or the whole warp for the narrow-channel forms); warp 1
+// allocates TMEM and lane 0 issues tcgen05.mma; warps 2-9 (256 threads: two per TMEM lane, each
+// taking half of the tile's columns) split A (strict), drain TMEM, and run the epilogue.
 //
 // Every wait on an mbarrier is bounded (about a second of clock cycles); on timeout the kernel
 // records MGC_CUDA_TIMEOUT in the error word, drains what it issued, frees its TMEM and returns.
@@ -179,8 +180,12 @@ __device__ __forceinline__ void tma_store_commit_and_wait() {
     asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory");
 }
 
-// Barrier among the 128 epilogue threads only (named barrier 1).
-__device__ __forceinline__ void epilogue_sync() { asm volatile("bar.sync 1, 128;" ::: "memory"); }
+// Epilogue warps: two per TMEM lane quadrant, each taking half of the tile's columns.
+constexpr int EPI_THREADS = 256;
+constexpr int THREADS = 64 + EPI_THREADS;  // producer warp, MMA warp, eight epilogue warps
+
+// Barrier among the epilogue threads only (named barrier 1).
+__device__ __forceinline__ void epilogue_sync() { asm volatile("bar.sync 1, 256;" ::: "memory"); }
 
 __device__ __forceinline__ void tmem_alloc(uint32_t *slot, uint32_t cols) {
     asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_addr(slot)),
@@ -331,7 +336,7 @@ struct Cfg {
 // the TMEM buffer ring run on a K-block counter that continues across tiles, so the next tile's
 // loads and MMAs overlap this tile's drain and epilogue.
 template <int BN, int MODE, int RB>
-__global__ void __launch_bounds__(192, 1) umma_gemm_kernel(const __grid_constant__ Params p) {
+__global__ void __launch_bounds__(THREADS, 1) umma_gemm_kernel(const __grid_constant__ Params p) {
     using C = Cfg<BN, MODE, RB>;
     constexpr int S = C::STAGES;
     constexpr int R = C::REGIONS;
@@ -381,11 +386,11 @@ __global__ void __launch_bounds__(192, 1) umma_gemm_kernel(const __grid_constant
         for (int s = 0; s < S; ++s) {
             mbar_init(&full[s], 1);
             mbar_init(&empty[s], 1);
-            mbar_init(&split[s], 128);
+            mbar_init(&split[s], EPI_THREADS);
         }
         for (int b = 0; b < TB; ++b) {
             mbar_init(&tfull[b], 1);
-            mbar_init(&tempty[b], 128);
+            mbar_init(&tempty[b], EPI_THREADS);
         }
         mbar_init(mma_done, 1);
         mbar_init(res_full, 1);
@@ -587,24 +592,26 @@ __global__ void __launch_bounds__(192, 1) umma_gemm_kernel(const __grid_constant
         }
     } else {
         // ---------------- epilogue warps: A split (strict), TMEM drain, epilogue ----------------
-        const int et = threadIdx.x - 64;  // 0..127
-        const int q = warp & 3;           // TMEM lane quadrant this warp may access
-        const int row = q * 32 + lane;    // this thread's tile row (its TMEM lane)
-        const uint32_t lane_base = tmem_base + ((uint32_t)(q * 32) << 16);
+        constexpr int HALF = BN / 2;        // columns per epilogue thread
+        const int et = threadIdx.x - 64;    // 0..255
+        const int q = warp & 3;             // TMEM lane quadrant this warp may access
+        const int hc = ((warp - 2) >> 2) * HALF;  // first column of this warp's half
+        const int row = q * 32 + lane;      // this thread's tile row (its TMEM lane)
+        const uint32_t lane_base = tmem_base + ((uint32_t)(q * 32) << 16) + (uint32_t)hc;
         long long g = 0;       // K blocks drained
         long long gs = 0;      // K blocks split (strict)
         bool ok = true;
         // strict mode accumulates K blocks in fp64 (each block's four step regions summed in fp32
         // first); TF32 mode accumulates in fp32
         using AccT = typename std::conditional<MODE == STRICT, double, float>::type;
-        AccT acc[BN];
+        AccT acc[HALF];
         auto drain = [&]() -> bool {
             const int b = (int)(g % TB);
             if (!mbar_wait(&tfull[b], (uint32_t)((g / TB) & 1))) return false;
             tc_fence_after();
             if (MODE == STRICT) {
 #pragma unroll
-                for (int c0 = 0; c0 < BN; c0 += 32) {
+                for (int c0 = 0; c0 < HALF; c0 += 32) {
                     float blk[32];
 #pragma unroll
                     for (int r = 0; r < R; ++r) {
@@ -620,7 +627,7 @@ __global__ void __launch_bounds__(192, 1) umma_gemm_kernel(const __grid_constant
             } else {
                 // acc += (A B_hi + A B_lo) for 32 columns at a time: both halves loaded, one wait
 #pragma unroll
-                for (int c0 = 0; c0 < BN; c0 += 32) {
+                for (int c0 = 0; c0 < HALF; c0 += 32) {
                     uint32_t vh[32], vl[32];
                     const uint32_t addr = lane_base + (uint32_t)(b * C::BUF_COLS + c0);
                     tmem_ld32(addr, vh);
@@ -641,8 +648,8 @@ __global__ void __launch_bounds__(192, 1) umma_gemm_kernel(const __grid_constant
             float4 *a4 = reinterpret_cast<float4 *>(a_tile(s));
             float4 *l4 = reinterpret_cast<float4 *>(alo_tile(s));
 #pragma unroll
-            for (int i = 0; i < (int)(A_TILE_BYTES / 16 / 128); ++i) {
-                const int idx = i * 128 + et;
+            for (int i = 0; i < (int)(A_TILE_BYTES / 16 / EPI_THREADS); ++i) {
+                const int idx = i * EPI_THREADS + et;
                 const float4 v = a4[idx];
                 float4 h, l;
                 h.x = tf32_hi(v.x); h.y = tf32_hi(v.y); h.z = tf32_hi(v.z); h.w = tf32_hi(v.w);
@@ -688,7 +695,7 @@ __global__ void __launch_bounds__(192, 1) umma_gemm_kernel(const __grid_constant
         for (int i = 0; ok && tile_at(i, mt, nt); ++i, ++local) {
             const int n0 = nt * BN, m0 = mt * BM;
 #pragma unroll
-            for (int j = 0; j < BN; ++j) acc[j] = AccT(0);
+            for (int j = 0; j < HALF; ++j) acc[j] = AccT(0);
             for (int kb = 0; kb < num_kb && ok; ++kb) {
                 if (MODE == STRICT) {
                     if (!split_one()) ok = false;
@@ -702,7 +709,7 @@ __global__ void __launch_bounds__(192, 1) umma_gemm_kernel(const __grid_constant
             // this tile's bias columns into shared memory, one coalesced load (the previous
             // tile's readers have all passed its second barrier)
             if (p.bias) {
-                for (int c = et; c < BN; c += 128) bias_s[c] = n0 + c < p.N ? __ldg(p.bias + n0 + c) : 0.0f;
+                for (int c = et; c < BN; c += EPI_THREADS) bias_s[c] = n0 + c < p.N ? __ldg(p.bias + n0 + c) : 0.0f;
             }
             // the staging tile is free (the previous TMA store was read out) and, with a
             // residual, refilled with this tile's residual
@@ -711,21 +718,22 @@ __global__ void __launch_bounds__(192, 1) umma_gemm_kernel(const __grid_constant
                 ok = false;
                 break;
             }
-            // 32 columns at a time: the residual loads of a chunk are all issued before its
-            // stores, so no load waits behind a store to the same staging tile
+            // 32 columns at a time: the residual and bias loads of a chunk are all issued before
+            // its stores, so no load waits behind a store to the same staging tile
             const uint32_t out_s = smem_addr(out_tile);
             const uint32_t bias_addr = smem_addr(bias_s);
 #pragma unroll
-            for (int c0 = 0; c0 < BN; c0 += 32) {
-                float4 rv[8];
-                if (res_tma) {
+            for (int a0 = 0; a0 < HALF; a0 += 32) {  // a0: accumulator index; column hc + a0
+                float4 rv[8], bvs[8];
 #pragma unroll
-                    for (int j = 0; j < 8; ++j) rv[j] = lds4(out_s + stage_offset(row, c0 + 4 * j));
+                for (int j = 0; j < 8; ++j) {
+                    rv[j] = res_tma ? lds4(out_s + stage_offset(row, hc + a0 + 4 * j)) : make_float4(0.f, 0.f, 0.f, 0.f);
+                    bvs[j] = p.bias ? lds4(bias_addr + 4 * (hc + a0 + 4 * j)) : make_float4(0.f, 0.f, 0.f, 0.f);
                 }
 #pragma unroll
                 for (int j = 0; j < 8; ++j) {
-                    const int c = c0 + 4 * j;
-                    const float4 bv = p.bias ? lds4(bias_addr + 4 * c) : make_float4(0.f, 0.f, 0.f, 0.f);
+                    const int c = a0 + 4 * j;  // accumulator index
+                    const float4 bv = bvs[j];
                     float4 o;
                     if (MODE == STRICT) {  // the same sum in fp64 with the step-bias compensation
                         const double sa = (double)p.alpha * (1.0 + STEP_BIAS);
@@ -750,12 +758,12 @@ __global__ void __launch_bounds__(192, 1) umma_gemm_kernel(const __grid_constant
                         o.x = fminf(fmaxf(o.x, p.lo), p.hi); o.y = fminf(fmaxf(o.y, p.lo), p.hi);
                         o.z = fminf(fmaxf(o.z, p.lo), p.hi); o.w = fminf(fmaxf(o.w, p.lo), p.hi);
                     }
-                    sts4(out_s + stage_offset(row, c), o);
+                    sts4(out_s + stage_offset(row, hc + c), o);
                 }
             }
             if (!act_in_step1 && !res_direct) {  // transcendental activation on this thread's row
 #pragma unroll 1
-                for (int c0 = 0; c0 < BN; c0 += 4) {
+                for (int c0 = hc; c0 < hc + HALF; c0 += 4) {
                     float4 *slot = stage_slot(row, c0);
                     float4 o = *slot;
                     o.x = apply_act(o.x, p.act, p.lo, p.hi);
@@ -773,7 +781,7 @@ __global__ void __launch_bounds__(192, 1) umma_gemm_kernel(const __grid_constant
                     const long long m = (long long)m0 + r;
                     if (m >= p.M) continue;
 #pragma unroll
-                    for (int sl = 0; sl < BN / 32; ++sl) {
+                    for (int sl = hc / 32; sl < (hc + HALF) / 32; ++sl) {
                         const int c = sl * 32 + lane;
                         const int n = n0 + c;
                         if (n >= p.N) continue;
@@ -901,7 +909,7 @@ inline int launch(const Params &p, int grid, cudaStream_t stream) {
     // per device (the attribute belongs to the current context); cheap, and allowed under capture
     MGC_CHECK_CUDA(cudaFuncSetAttribute(umma_gemm_kernel<BN, MODE, RB>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                         (int)smem));
-    umma_gemm_kernel<BN, MODE, RB><<<grid, 192, smem, stream>>>(p);
+    umma_gemm_kernel<BN, MODE, RB><<<grid, THREADS, smem, stream>>>(p);
     return check_launch("umma_gemm_kernel");
 }
 
