@@ -52,59 +52,110 @@ def peaks() -> dict:
 
 
 class Clocks:
-    """Sample nvidia-smi clocks and throttle reasons while the timed region runs."""
+    """Sample SM clocks, power and clock-event (throttle) reasons every 20 ms while the timed
+    region runs, through NVML (the GPU found by its PCI bus id), else ``nvidia-smi -lms``."""
 
+    REASONS = {"hw_slowdown": 0x8, "hw_thermal_slowdown": 0x40, "sw_thermal_slowdown": 0x20, "sw_power_cap": 0x4}
     FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
               "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
               "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
 
-    def __init__(self, index: int) -> None:
-        self.index = index
+    def __init__(self, device: int) -> None:
+        self.device = device
+        self.samples: list[tuple[float, float, set[str]]] = []  # (sm MHz, max MHz, reasons)
         self.proc: subprocess.Popen | None = None
-        self.lines: list[str] = []
+        self._stop = threading.Event()
         self._thread: threading.Thread | None = None
+        self._nvml = None
+        self._handle = None
+
+    def _open_nvml(self) -> bool:
+        try:
+            import pynvml
+            import torch
+
+            pynvml.nvmlInit()
+            props = torch.cuda.get_device_properties(self.device)
+            bus = f"{props.pci_domain_id:08X}:{props.pci_bus_id:02X}:{props.pci_device_id:02X}.0"
+            try:
+                self._handle = pynvml.nvmlDeviceGetHandleByPciBusId(bus)
+            except pynvml.NVMLError:
+                self._handle = pynvml.nvmlDeviceGetHandleByIndex(self.device)
+            self._nvml = pynvml
+            return True
+        except Exception:
+            return False
+
+    def _poll_nvml(self) -> None:
+        nv, h = self._nvml, self._handle
+        get_reasons = getattr(nv, "nvmlDeviceGetCurrentClocksEventReasons", None) or nv.nvmlDeviceGetCurrentClocksThrottleReasons
+        mx = float(nv.nvmlDeviceGetMaxClockInfo(h, nv.NVML_CLOCK_SM))
+        while not self._stop.is_set():
+            try:
+                sm = float(nv.nvmlDeviceGetClockInfo(h, nv.NVML_CLOCK_SM))
+                bits = int(get_reasons(h))
+                self.samples.append((sm, mx, {k for k, v in self.REASONS.items() if bits & v}))
+            except Exception:
+                pass
+            self._stop.wait(0.02)
+
+    def _poll_smi(self) -> None:
+        assert self.proc is not None and self.proc.stdout is not None
+        names = ("hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap")
+        for line in self.proc.stdout:
+            parts = [x.strip() for x in line.split(",")]
+            if len(parts) < 9:
+                continue
+            try:
+                sm, mx = float(parts[1]), float(parts[2])
+            except ValueError:
+                continue
+            self.samples.append((sm, mx, {n for n, v in zip(names, parts[5:9]) if v.lower() == "active"}))
 
     def __enter__(self) -> "Clocks":
-        try:
-            self.proc = subprocess.Popen(
-                ["nvidia-smi", f"--id={self.index}", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
-                 "-lms", "200"], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
-            self._thread = threading.Thread(target=self._read, daemon=True)
+        if self._open_nvml():
+            self._thread = threading.Thread(target=self._poll_nvml, daemon=True)
+        else:
+            try:
+                self.proc = subprocess.Popen(
+                    ["nvidia-smi", f"--id={self.device}", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                     "-lms", "100"], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+                self._thread = threading.Thread(target=self._poll_smi, daemon=True)
+            except OSError:
+                self.proc = None
+        if self._thread is not None:
             self._thread.start()
-        except OSError:
-            self.proc = None
         return self
 
-    def _read(self) -> None:
-        assert self.proc is not None and self.proc.stdout is not None
-        for line in self.proc.stdout:
-            self.lines.append(line.strip())
-
     def __exit__(self, *exc: object) -> None:
+        self._stop.set()
         if self.proc is not None:
             self.proc.terminate()
             try:
                 self.proc.wait(timeout=5)
             except subprocess.TimeoutExpired:
                 self.proc.kill()
+        if self._thread is not None:
+            self._thread.join(timeout=5)
 
     def summary(self) -> dict:
-        sm, mx, reasons = [], 0.0, set()
-        names = ("hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap")
-        for line in self.lines:
-            parts = [p.strip() for p in line.split(",")]
-            if len(parts) < 9:
-                continue
-            try:
-                sm.append(float(parts[1]))
-                mx = max(mx, float(parts[2]))
-            except ValueError:
-                continue
-            for name, val in zip(names, parts[5:9], strict=False):
-                if val.lower() == "active":
-                    reasons.add(name)
-        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": mx or None,
-                "reasons": sorted(reasons), "samples": len(sm)}
+        sm = [x[0] for x in self.samples]
+        reasons = sorted(set().union(*[x[2] for x in self.samples])) if self.samples else []
+        return {"sm_mhz": statistics.median(sm) if sm else None,
+                "sm_max_mhz": max((x[1] for x in self.samples), default=None), "reasons": reasons,
+                "samples": len(sm), "source": "nvml" if self._nvml is not None else "nvidia-smi"}
+
+
+def measured_traffic(batch: int) -> int | None:
+    """DRAM bytes (read + write) of one step's GEMM launches, from the committed ncu summary
+    (measured at batch 32, scaled by the batch)."""
+    f = ROOT / "profiles" / "resnet50_step_launches.md"
+    if not f.exists():
+        return None
+    for line in f.read_text().splitlines():
+        if line.startswith("traffic_bytes_per_step_b32:"):
+            return int(int(line.split(":")[1]) * batch / 32)
+    return None
 
 
 def build_r50(batch: int, seed: int = 4):
@@ -163,7 +214,7 @@ def run_reference_arm(args: argparse.Namespace) -> None:
 def main() -> None:
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--steps", type=int, default=50)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--batch", type=int, default=256, help="images per GPU per step")
     ap.add_argument("--precision", default="tf32", choices=["tf32", "strict", "fp32"])
@@ -259,7 +310,9 @@ def main() -> None:
         "gpu_launches": model.launch_count * args.steps,
         "roofline": {
             "bound": "tensor", "achieved": round(achieved, 3), "peak": round(tf32_peak, 1), "unit": "TFLOP/s",
-            "frac": round(achieved / tf32_peak, 4), "traffic": None,
+            "frac": round(achieved / tf32_peak, 4), "traffic": measured_traffic(args.batch),
+            "traffic_note": "DRAM read+write bytes of the 54 GEMM launches of one step (ncu, batch 32, "
+                            "scaled by the batch; profiles/resnet50_step_launches.md)",
             "kernel": "implicit-GEMM conv/GEMM launches (54 per step)",
             "peak_note": f"dense TF32 = half the {pk['source']} bf16 cuBLAS rate",
             "gemm_share_of_step": round(gemm_s / total_prof, 4) if total_prof else None,
