@@ -16,8 +16,8 @@
 // truncating them to TF32, and its accumulator rounds toward zero, a bias that compounds through
 // deep networks. Both are handled explicitly:
 // * MGC_PREC_TF32: A is loaded through a TFLOAT32 tensor map, which rounds it to the nearest
-//   TF32 value; each K step issues A*B_lo + A*B_hi (B exact to fp32), so the only operand error
-//   is the unbiased rounding of the activations.
+//   TF32 value; each K step issues one MMA of A against the stacked [B_hi; B_lo] tile (B exact
+//   to fp32), so the only operand error is the unbiased rounding of the activations.
 // * MGC_PREC_3XTF32 ("strict"): the epilogue warps split the raw A tile into hi = RN_tf32(A) and
 //   lo = A - hi in shared memory; each K step issues A_lo*B_hi + A_hi*B_lo + A_hi*B_hi.
 // * Accumulator promotion: every K block writes its products into a fresh TMEM region (double
@@ -65,8 +65,7 @@ constexpr double STEP_BIAS = 2.5e-8;
 
 struct Params {
     CUtensorMap tmA;
-    CUtensorMap tmB;                 // B's TF32 part, K-major [N][Kp]
-    CUtensorMap tmBlo;               // B's residual, same layout
+    CUtensorMap tmB;                 // [2][N][Kp]: plane 0 B's TF32 part, plane 1 its residual
     CUtensorMap tmC;                 // output tile store (when tma_out)
     CUtensorMap tmR;                 // residual tile load (when tma_res)
     int tma_out, tma_res;
@@ -144,6 +143,14 @@ __device__ __forceinline__ void tma_load_2d(void *dst, const CUtensorMap *map, u
         : "memory");
 }
 
+__device__ __forceinline__ void tma_load_3d(void *dst, const CUtensorMap *map, uint64_t *bar, int x, int y, int z) {
+    asm volatile(
+        "cp.async.bulk.tensor.3d.shared::cluster.global.tile.mbarrier::complete_tx::bytes"
+        " [%0], [%1, {%3, %4, %5}], [%2];"
+        ::"r"(smem_addr(dst)), "l"(reinterpret_cast<uint64_t>(map)), "r"(smem_addr(bar)), "r"(x), "r"(y), "r"(z)
+        : "memory");
+}
+
 __device__ __forceinline__ void tma_load_im2col_4d(void *dst, const CUtensorMap *map, uint64_t *bar, int c, int w,
                                                    int h, int n, uint16_t off_w, uint16_t off_h) {
     asm volatile(
@@ -182,7 +189,11 @@ __device__ __forceinline__ void tma_store_commit_and_wait() {
 
 // Epilogue warps: two per TMEM lane quadrant, each taking half of the tile's columns.
 constexpr int EPI_THREADS = 256;
-constexpr int THREADS = 64 + EPI_THREADS;  // producer warp, MMA warp, eight epilogue warps
+// A TMA instruction holds its issuing thread for ~350 cycles (measured, any box size), so A and
+// B of a K block are issued by different warps: warp 0 (A), warp 10 (B, one 3-D box of both
+// planes).
+constexpr int B_WARP = 2 + EPI_THREADS / 32;
+constexpr int THREADS = 64 + EPI_THREADS + 32;  // A producer, MMA, eight epilogue warps, B producer
 
 // Barrier among the epilogue threads only (named barrier 1).
 __device__ __forceinline__ void epilogue_sync() { asm volatile("bar.sync 1, 256;" ::: "memory"); }
@@ -416,10 +427,7 @@ __global__ void __launch_bounds__(THREADS, 1) umma_gemm_kernel(const __grid_cons
         if (RB && tile_at(0, mt, nt)) {  // this CTA's B panel, once: lane j loads K blocks j, j+32, ...
             if (lane == 0) mbar_expect_tx(bres_full, p.b_res_bytes);
             __syncwarp();
-            for (int kb = lane; kb < num_kb; kb += 32) {
-                tma_load_2d(b_tile(0, kb), &p.tmB, bres_full, kb * BK, nt * BN);
-                tma_load_2d(b_tile(0, kb) + C::B_TILE_BYTES, &p.tmBlo, bres_full, kb * BK, nt * BN);
-            }
+            for (int kb = lane; kb < num_kb; kb += 32) tma_load_3d(b_tile(0, kb), &p.tmB, bres_full, kb * BK, nt * BN, 0);
         }
         for (int i = 0; ok && tile_at(i, mt, nt); ++i) {
             const int n0 = nt * BN, m0 = mt * BM;
@@ -461,10 +469,7 @@ __global__ void __launch_bounds__(THREADS, 1) umma_gemm_kernel(const __grid_cons
                     tma_load_im2col_4d(a_tile(s) + lane * PACKED_BOX_BYTES, &p.tmA, &full[s], ch, wb, hb, nb,
                                        (uint16_t)(kw * p.DW), (uint16_t)(kh * p.DH));
                 }
-                if (!RB && lane == 0) {
-                    tma_load_2d(b_tile(s, kb), &p.tmB, &full[s], kb * BK, n0);
-                    tma_load_2d(b_tile(s, kb) + C::B_TILE_BYTES, &p.tmBlo, &full[s], kb * BK, n0);
-                }
+                (void)n0;  // B comes from the B producer warp
                 __syncwarp();
             }
         }
@@ -485,10 +490,7 @@ __global__ void __launch_bounds__(THREADS, 1) umma_gemm_kernel(const __grid_cons
             if (RB && tile_at(0, mt, nt)) {  // this CTA's B panel, once
                 mbar_expect_tx(bres_full, p.b_res_bytes);
 #pragma unroll 1
-                for (int kb = 0; kb < num_kb; ++kb) {
-                    tma_load_2d(b_tile(0, kb), &p.tmB, bres_full, kb * BK, nt * BN);
-                    tma_load_2d(b_tile(0, kb) + C::B_TILE_BYTES, &p.tmBlo, bres_full, kb * BK, nt * BN);
-                }
+                for (int kb = 0; kb < num_kb; ++kb) tma_load_3d(b_tile(0, kb), &p.tmB, bres_full, kb * BK, nt * BN, 0);
             }
             for (int i = 0; ok && tile_at(i, mt, nt); ++i) {
                 const int n0 = nt * BN, m0 = mt * BM;
@@ -519,10 +521,7 @@ __global__ void __launch_bounds__(THREADS, 1) umma_gemm_kernel(const __grid_cons
                     } else {
                         tma_load_2d(a_tile(s), &p.tmA, &full[s], kb * BK, m0);
                     }
-                    if (!RB) {
-                        tma_load_2d(b_tile(s, kb), &p.tmB, &full[s], kb * BK, n0);
-                        tma_load_2d(b_tile(s, kb) + C::B_TILE_BYTES, &p.tmBlo, &full[s], kb * BK, n0);
-                    }
+                    (void)n0;  // B comes from the B producer warp
                 }
             }
             // the copies of the last (up to S) issued K blocks must have landed before exit
@@ -530,6 +529,25 @@ __global__ void __launch_bounds__(THREADS, 1) umma_gemm_kernel(const __grid_cons
                 if (!mbar_wait(&full[k % S], (uint32_t)((k / S) & 1))) set_error(p.err, MGC_CUDA_TIMEOUT);
             }
             if (RB && tile_at(0, mt, nt) && !mbar_wait(bres_full, 0)) set_error(p.err, MGC_CUDA_TIMEOUT);
+        }
+    } else if (warp == B_WARP) {
+        if (lane == 0 && !RB) {
+            // ---------------- B producer: one 3-D box (TF32 part and residual) per K block ----------------
+            long long g = 0;
+            bool ok = true;
+            int mt, nt;
+            for (int i = 0; ok && tile_at(i, mt, nt); ++i) {
+                for (int kb = 0; kb < num_kb; ++kb, ++g) {
+                    const int s = (int)(g % S);
+                    const long long round = g / S;
+                    if (round > 0 && !mbar_wait(&empty[s], (uint32_t)((round - 1) & 1))) {
+                        set_error(p.err, MGC_CUDA_TIMEOUT);
+                        ok = false;
+                        break;
+                    }
+                    tma_load_3d(b_tile(s, kb), &p.tmB, &full[s], kb * BK, nt * BN, 0);
+                }
+            }
         }
     } else if (warp == 1) {
         if (lane == 0) {
@@ -591,7 +609,7 @@ __global__ void __launch_bounds__(THREADS, 1) umma_gemm_kernel(const __grid_cons
             if (!mbar_wait(mma_done, 0)) set_error(p.err, MGC_CUDA_TIMEOUT);
         }
     } else {
-        // ---------------- epilogue warps: A split (strict), TMEM drain, epilogue ----------------
+        // ---------------- epilogue warps (2..9): A split (strict), TMEM drain, epilogue ----------------
         constexpr int HALF = BN / 2;        // columns per epilogue thread
         const int et = threadIdx.x - 64;    // 0..255
         const int q = warp & 3;             // TMEM lane quadrant this warp may access
@@ -862,6 +880,23 @@ inline bool make_map_2d(CUtensorMap *map, const void *base, long long rows, long
     return r == CUDA_SUCCESS;
 }
 
+// The two K-major planes of a constant B ([N][Kp] TF32 part at `hi`, residual at `lo`, lo > hi)
+// as one tensor [2][N][Kp]; a box {32, box_rows, 2} lands as the hi tile followed by the lo tile.
+inline bool make_map_b(CUtensorMap *map, const float *hi, const float *lo, long long rows, long long kp, int box_rows) {
+    auto fn = encode_tiled_fn();
+    if (!fn) return false;
+    const long long gap = reinterpret_cast<const char *>(lo) - reinterpret_cast<const char *>(hi);
+    if (gap <= 0 || (gap & 15) || gap >= (1ll << 40)) return false;
+    cuuint64_t dims[3] = {(cuuint64_t)kp, (cuuint64_t)rows, 2};
+    cuuint64_t strides[2] = {(cuuint64_t)(kp * 4), (cuuint64_t)gap};
+    cuuint32_t box[3] = {(cuuint32_t)BK, (cuuint32_t)box_rows, 2};
+    cuuint32_t estr[3] = {1, 1, 1};
+    CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 3, const_cast<float *>(hi), dims, strides, box, estr,
+                    CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                    CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    return r == CUDA_SUCCESS;
+}
+
 // NHWC fp32 image, im2col boxes of `chans` channels x 128 output pixels: 32 channels in 128-byte
 // swizzled rows, or 4 channels in plain 16-byte rows (tap-packed).
 inline bool make_map_im2col(CUtensorMap *map, const GemmParams &g, bool tf32, int chans = BK) {
@@ -1006,8 +1041,7 @@ inline int try_gemm_umma(const GemmParams &p, cudaStream_t stream, int *taken) {
     }
     // strict mode keeps four TMEM regions per K block, which fits only N tiles of 64
     const int bn = (strict || p.N <= 64) ? 64 : 128;
-    if (!umma::make_map_2d(&u.tmB, p.b_umma, p.N, kp, kp, bn)) return MGC_CUDA_OK;
-    if (!umma::make_map_2d(&u.tmBlo, p.b_umma_lo, p.N, kp, kp, bn)) return MGC_CUDA_OK;
+    if (!umma::make_map_b(&u.tmB, p.b_umma, p.b_umma_lo, p.N, kp, bn)) return MGC_CUDA_OK;
     u.n_tiles = (int)ceil_div(p.N, bn);
     const long long m_tiles = ceil_div(p.M, umma::BM);
     const long long tiles = (long long)u.n_tiles * m_tiles;

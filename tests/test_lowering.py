@@ -140,3 +140,14 @@ def test_algorithmic_cost_of_resnet50(r50: Graph) -> None:
     assert abs(flops / 1e9 - 8.178) < 0.01
     assert 200e6 < nbytes < 230e6
 
+
+
+def test_tensor_core_b_planes_are_ordered(r50: Graph) -> None:
+    """The kernel loads B's TF32 part and residual as the two planes of one 3-D tensor map, which
+    needs the residual stored after the TF32 part at a 16-byte multiple."""
+    for precision in ("tf32", "strict"):
+        low = lower_graph(r50, precision=precision)
+        for rec in low.launches:
+            if rec.kind == lowering.K_GEMM and rec.r[6].space == lowering.SPACE_WEIGHTS:
+                gap = rec.r[7].offset - rec.r[6].offset
+                assert gap > 0 and gap % 16 == 0
