@@ -52,6 +52,11 @@ constexpr int BK = 32;                       // fp32 elements per K block: one 1
 constexpr uint32_t A_TILE_BYTES = BM * BK * 4;
 constexpr long long WAIT_LIMIT_CYCLES = 1ll << 31;  // ~1.1 s at 1.9 GHz
 
+// TF32 mode: K blocks whose products share one TMEM accumulator before the epilogue promotes it
+// to registers (a tensor-core accumulation chain of 4 * PROMOTE_KB MMA steps). The epilogue's
+// drain then runs every PROMOTE_KB blocks, so the MMA warp rarely waits for a free buffer.
+constexpr int PROMOTE_KB = 2;
+
 enum Mode { TF32 = 0, STRICT = 1 };
 
 // Mean relative shrink toward zero of one kind::tf32 MMA step (eight exact TF32 products summed
@@ -561,16 +566,19 @@ __global__ void __launch_bounds__(THREADS, 1) umma_gemm_kernel(const __grid_cons
                 set_error(p.err, MGC_CUDA_TIMEOUT);
                 ok = false;
             }
+            constexpr int PG = MODE == STRICT ? 1 : PROMOTE_KB;  // K blocks per TMEM buffer
+            long long gq = 0;                                    // TMEM buffers filled so far
             for (int i = 0; ok && tile_at(i, mt, nt); ++i) {
                 for (int kb = 0; kb < num_kb; ++kb, ++g) {
                     const int s = (int)(g % S);
-                    const int b = (int)(g % TB);
+                    const int b = (int)(gq % TB);
+                    const bool first = kb % PG == 0, last = kb % PG == PG - 1 || kb == num_kb - 1;
                     if (!mbar_wait(MODE == STRICT ? &split[s] : &full[s], (uint32_t)((g / S) & 1))) {
                         set_error(p.err, MGC_CUDA_TIMEOUT);
                         ok = false;
                         break;
                     }
-                    if (g >= TB && !mbar_wait(&tempty[b], (uint32_t)(((g / TB) - 1) & 1))) {
+                    if (first && gq >= TB && !mbar_wait(&tempty[b], (uint32_t)(((gq / TB) - 1) & 1))) {
                         set_error(p.err, MGC_CUDA_TIMEOUT);
                         ok = false;
                         break;
@@ -598,11 +606,14 @@ __global__ void __launch_bounds__(THREADS, 1) umma_gemm_kernel(const __grid_cons
                             // 128B-swizzled row layout, so one descriptor spans both as 2 BN rows:
                             // one MMA, A read once per K step
                             (void)bld;
-                            mma_tf32(dbase, ad, bd, idesc2, k > 0 ? 1u : 0u);
+                            mma_tf32(dbase, ad, bd, idesc2, (!first || k > 0) ? 1u : 0u);
                         }
                     }
                     mma_commit(&empty[s]);   // shared-memory slot free once these MMAs read it
-                    mma_commit(&tfull[b]);   // TMEM buffer b holds this K block's products
+                    if (last) {
+                        mma_commit(&tfull[b]);  // TMEM buffer b holds this group's products
+                        ++gq;
+                    }
                 }
             }
             mma_commit(mma_done);
@@ -616,7 +627,7 @@ __global__ void __launch_bounds__(THREADS, 1) umma_gemm_kernel(const __grid_cons
         const int hc = ((warp - 2) >> 2) * HALF;  // first column of this warp's half
         const int row = q * 32 + lane;      // this thread's tile row (its TMEM lane)
         const uint32_t lane_base = tmem_base + ((uint32_t)(q * 32) << 16) + (uint32_t)hc;
-        long long g = 0;       // K blocks drained
+        long long g = 0;       // TMEM buffers drained
         long long gs = 0;      // K blocks split (strict)
         bool ok = true;
         // strict mode accumulates K blocks in fp64 (each block's four step regions summed in fp32
@@ -718,7 +729,7 @@ __global__ void __launch_bounds__(THREADS, 1) umma_gemm_kernel(const __grid_cons
                 if (MODE == STRICT) {
                     if (!split_one()) ok = false;
                     else if (kb >= 1 && !drain()) ok = false;  // one block behind the split
-                } else if (!drain()) {
+                } else if (kb % PROMOTE_KB == 0 && !drain()) {  // one drain per K-block group
                     ok = false;
                 }
             }
