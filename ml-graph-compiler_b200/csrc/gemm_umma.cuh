@@ -79,6 +79,8 @@ struct Params {
     int KW, DH, DW, cblocks;         // im2col: K block kb -> (kh, kw, channel block)
     int cpix, kreal;                 // tap-packed: channels per pixel (4..28), real K = KH*KW*cpix
     int wrows;                       // window rows (im2col 3): output pixels per box (divides OW)
+    int rt_rows, rt_per_img;         // row tiles (im2col 4): output rows per tile, tiles per image
+    uint32_t a_bytes;                // bytes of one K block's A boxes (row tiles fill rt_rows*OW rows)
     int m_tiles;                     // ceil(M / 128)
     uint32_t b_res_bytes;            // B-resident kernels: bytes of this CTA's whole B panel
     int OH, OW, SH, SW, PT, PL;      // im2col: output pixel -> window origin
@@ -179,6 +181,20 @@ __device__ __forceinline__ void tma_load_5d(void *dst, const CUtensorMap *map, u
 // Warm the TMA unit's descriptor cache with a tensor map (kernel-parameter copies included).
 __device__ __forceinline__ void prefetch_tmap(const CUtensorMap *map) {
     asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(map)) : "memory");
+}
+
+__device__ __forceinline__ void tma_load_4d(void *dst, const CUtensorMap *map, uint64_t *bar, int x, int y, int z, int w) {
+    asm volatile(
+        "cp.async.bulk.tensor.4d.shared::cluster.global.tile.mbarrier::complete_tx::bytes"
+        " [%0], [%1, {%3, %4, %5, %6}], [%2];"
+        ::"r"(smem_addr(dst)), "l"(reinterpret_cast<uint64_t>(map)), "r"(smem_addr(bar)), "r"(x), "r"(y), "r"(z), "r"(w)
+        : "memory");
+}
+
+__device__ __forceinline__ void tma_store_4d(const CUtensorMap *map, const void *src, int x, int y, int z, int w) {
+    asm volatile("cp.async.bulk.tensor.4d.global.shared::cta.tile.bulk_group [%0, {%2, %3, %4, %5}], [%1];"
+                 ::"l"(reinterpret_cast<uint64_t>(map)), "r"(smem_addr(src)), "r"(x), "r"(y), "r"(z), "r"(w)
+                 : "memory");
 }
 
 __device__ __forceinline__ void tma_store_2d(const CUtensorMap *map, const void *src, int x, int y) {
@@ -425,7 +441,7 @@ __global__ void __launch_bounds__(THREADS, 1) umma_gemm_kernel(const __grid_cons
         // eight or more A boxes per K block, so lane j issues box j, all in one instruction.
         // Lane 0 alone waits on the ring, arms the barrier and loads B; the warp reconverges
         // before the loads.
-        constexpr uint32_t bytes = A_TILE_BYTES + (RB ? 0 : 2 * C::B_TILE_BYTES);
+        const uint32_t bytes = p.a_bytes + (RB ? 0 : 2 * C::B_TILE_BYTES);
         long long g = 0;  // K blocks issued so far
         bool ok = true;
         int mt, nt;
@@ -454,7 +470,15 @@ __global__ void __launch_bounds__(THREADS, 1) umma_gemm_kernel(const __grid_cons
                     ok = false;
                     break;
                 }
-                if (p.im2col == 3) {
+                if (p.im2col == 4) {
+                    // row tiles: one box of rt_rows whole output rows (OW pixels each) of one
+                    // image; the tile's remaining smem rows are never loaded and never stored
+                    if (lane == 0) {
+                        const int kh = kb / p.cblocks, x0 = (kb - kh * p.cblocks) * BK;
+                        const int img = mt / p.rt_per_img, oh0 = (mt - img * p.rt_per_img) * p.rt_rows;
+                        tma_load_5d(a_tile(s), &p.tmA, &full[s], x0, 0, oh0, img, kh);
+                    }
+                } else if (p.im2col == 3) {
                     // window rows: the K block is 32 consecutive floats of the padded image row
                     // (kh) starting at the window origin, for wrows output pixels per box
                     const int kh = kb / p.cblocks, x0 = (kb - kh * p.cblocks) * BK;
@@ -711,8 +735,17 @@ __global__ void __launch_bounds__(THREADS, 1) umma_gemm_kernel(const __grid_cons
         const bool issuer = warp == 2 && lane == 0;
         if (issuer && p.tma_out) prefetch_tmap(&p.tmC);
         if (issuer && p.tma_res) prefetch_tmap(&p.tmR);
+        const bool rows = p.im2col == 4;
         auto issue_residual = [&](int mt_, int nt_) {
             const int tn0 = nt_ * BN, tm0 = mt_ * BM;
+            if (rows) {
+                const int img = mt_ / p.rt_per_img, oh0 = (mt_ - img * p.rt_per_img) * p.rt_rows;
+                mbar_expect_tx(res_full, (uint32_t)(BN / 32) * p.a_bytes);
+#pragma unroll 1
+                for (int sl = 0; sl < BN / 32; ++sl)
+                    tma_load_4d(out_tile + sl * (BM * 128), &p.tmR, res_full, tn0 + sl * 32, 0, oh0, img);
+                return;
+            }
             mbar_expect_tx(res_full, C::OUT_BYTES);
 #pragma unroll 1
             for (int sl = 0; sl < BN / 32; ++sl)
@@ -824,9 +857,16 @@ __global__ void __launch_bounds__(THREADS, 1) umma_gemm_kernel(const __grid_cons
                 fence_proxy_async_smem();
                 epilogue_sync();
                 if (issuer) {
+                    if (rows) {  // the tile's rt_rows output rows; staging rows past them are dropped
+                        const int img = mt / p.rt_per_img, oh0 = (mt - img * p.rt_per_img) * p.rt_rows;
 #pragma unroll 1
-                    for (int sl = 0; sl < BN / 32; ++sl)
-                        tma_store_2d(&p.tmC, out_tile + sl * (BM * 128), n0 + sl * 32, m0);
+                        for (int sl = 0; sl < BN / 32; ++sl)
+                            tma_store_4d(&p.tmC, out_tile + sl * (BM * 128), n0 + sl * 32, 0, oh0, img);
+                    } else {
+#pragma unroll 1
+                        for (int sl = 0; sl < BN / 32; ++sl)
+                            tma_store_2d(&p.tmC, out_tile + sl * (BM * 128), n0 + sl * 32, m0);
+                    }
                     tma_store_commit_and_wait();
                     int mt2, nt2;
                     if (res_tma && tile_at(i + 1, mt2, nt2)) issue_residual(mt2, nt2);
@@ -932,7 +972,7 @@ inline bool make_map_im2col(CUtensorMap *map, const GemmParams &g, bool tf32, in
 // contiguous run that one filter row of a window covers. Consecutive output pixels overlap (their
 // stride SW*C*4 bytes is below the 128-byte box row), so a TMA tile box {32, wrows, 1, 1, 1}
 // reads 128-byte rows with no gather; x past KW * C is outside the tensor and reads as zero.
-inline bool make_map_window(CUtensorMap *map, const GemmParams &g, int wrows, bool tf32) {
+inline bool make_map_window(CUtensorMap *map, const GemmParams &g, int wrows, bool tf32, int box_oh = 1) {
     auto fn = encode_tiled_fn();
     if (!fn) return false;
     const long long nimg = (long long)g.M / ((long long)g.OH * g.OW);
@@ -940,11 +980,27 @@ inline bool make_map_window(CUtensorMap *map, const GemmParams &g, int wrows, bo
     cuuint64_t dims[5] = {(cuuint64_t)g.KW * g.C, (cuuint64_t)g.OW, (cuuint64_t)g.OH, (cuuint64_t)nimg, (cuuint64_t)g.KH};
     cuuint64_t strides[4] = {(cuuint64_t)(g.SW * px), (cuuint64_t)(g.SH * g.W * px), (cuuint64_t)((long long)g.H * g.W * px),
                              (cuuint64_t)(g.DH * g.W * px)};
-    cuuint32_t box[5] = {(cuuint32_t)BK, (cuuint32_t)wrows, 1, 1, 1};
+    cuuint32_t box[5] = {(cuuint32_t)BK, (cuuint32_t)wrows, (cuuint32_t)box_oh, 1, 1};
     cuuint32_t estr[5] = {1, 1, 1, 1, 1};
     CUresult r = fn(map, tf32 ? CU_TENSOR_MAP_DATA_TYPE_TFLOAT32 : CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 5,
                     const_cast<float *>(g.a), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
                     CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    return r == CUDA_SUCCESS;
+}
+
+// An NHWC output (or residual) [nimg][OH][OW][N] with row stride ld as a 4-D tensor {N, OW, OH,
+// nimg}; a box {32, OW, rows, 1} covers whole output rows (row tiles), clipped at OH.
+inline bool make_map_rows(CUtensorMap *map, const void *base, long long n, long long ld, int ow, int oh, long long nimg,
+                          int rows) {
+    auto fn = encode_tiled_fn();
+    if (!fn) return false;
+    cuuint64_t dims[4] = {(cuuint64_t)n, (cuuint64_t)ow, (cuuint64_t)oh, (cuuint64_t)nimg};
+    cuuint64_t strides[3] = {(cuuint64_t)(ld * 4), (cuuint64_t)(ow * ld * 4), (cuuint64_t)((long long)oh * ow * ld * 4)};
+    cuuint32_t box[4] = {(cuuint32_t)BK, (cuuint32_t)ow, (cuuint32_t)rows, 1};
+    cuuint32_t estr[4] = {1, 1, 1, 1};
+    CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, const_cast<void *>(base), dims, strides, box, estr,
+                    CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                    CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
     return r == CUDA_SUCCESS;
 }
 
@@ -1054,10 +1110,10 @@ inline int try_gemm_umma(const GemmParams &p, cudaStream_t stream, int *taken) {
     const int bn = (strict || p.N <= 64) ? 64 : 128;
     if (!umma::make_map_b(&u.tmB, p.b_umma, p.b_umma_lo, p.N, kp, bn)) return MGC_CUDA_OK;
     u.n_tiles = (int)ceil_div(p.N, bn);
-    const long long m_tiles = ceil_div(p.M, umma::BM);
+    long long m_tiles = ceil_div(p.M, umma::BM);
+    u.a_bytes = umma::A_TILE_BYTES;
     const long long tiles = (long long)u.n_tiles * m_tiles;
     if (tiles > 0x7FFFFFFF) return MGC_CUDA_OK;
-    u.m_tiles = (int)m_tiles;
     u.c = p.c; u.ldc = p.ldc; u.bias = p.bias; u.res = p.res; u.ldr = p.ldr;
     u.alpha = p.alpha; u.lo = p.lo; u.hi = p.hi; u.act = p.act;
     u.err = p.err;
@@ -1068,6 +1124,28 @@ inline int try_gemm_umma(const GemmParams &p, cudaStream_t stream, int *taken) {
     u.tma_res = (u.tma_out && p.res && (reinterpret_cast<uintptr_t>(p.res) & 15) == 0 && (p.ldr & 3) == 0 &&
                  umma::make_map_2d(&u.tmR, p.res, p.M, p.N, p.ldr, umma::BM)) ? 1 : 0;
     if (p.res && !u.tma_res) u.tma_out = 0;
+    // Window rows with OW <= 128: M tiles of whole output rows (rt_rows of them, one image), so a
+    // K block's A is one TMA box; output and residual move through 4-D maps that clip the rows
+    // past the tile's last output row.
+    if (u.im2col == 3 && u.tma_out && p.OW <= umma::BM) {
+        const long long nimg = (long long)p.M / ((long long)p.OH * p.OW);
+        const int rows = umma::BM / p.OW < p.OH ? umma::BM / p.OW : p.OH;
+        CUtensorMap a4, c4, r4;
+        bool okr = umma::make_map_window(&a4, p, p.OW, a_tf32, rows) &&
+                   umma::make_map_rows(&c4, p.c, p.N, p.ldc, p.OW, p.OH, nimg, rows);
+        if (okr && u.tma_res) okr = umma::make_map_rows(&r4, p.res, p.N, p.ldr, p.OW, p.OH, nimg, rows);
+        if (okr) {
+            u.tmA = a4;
+            u.tmC = c4;
+            if (u.tma_res) u.tmR = r4;
+            u.im2col = 4;
+            u.rt_rows = rows;
+            u.rt_per_img = (int)ceil_div(p.OH, rows);
+            m_tiles = nimg * u.rt_per_img;
+            u.a_bytes = (uint32_t)rows * p.OW * 128;
+        }
+    }
+    u.m_tiles = (int)m_tiles;
     // persistent grid: one CTA per SM (the shared-memory footprint allows no more)
     int st;
     if (strict) st = umma::launch_best<64, umma::STRICT>(u, m_tiles, stream);
