@@ -283,6 +283,63 @@ __global__ void __launch_bounds__(256) depthwise_nhwc4_kernel(const __grid_const
     }
 }
 
+// NHWC, C % 4 == 0, KH, KW <= 3, sizes below 2^31: each thread keeps one 4-channel group (the
+// block size is a multiple of C / 4, so the group never changes along the grid-stride loop) with
+// its bias and up to 3x3 weights in registers, and walks output pixels with 32-bit index
+// arithmetic. Same accumulation order as depthwise_nhwc4_kernel (bias, then taps row by row).
+__global__ void __launch_bounds__(256) depthwise_nhwc4_reg_kernel(const __grid_constant__ DepthwiseParams p) {
+    const int C4 = p.C >> 2;
+    const int c4 = (int)(threadIdx.x % (unsigned)C4);
+    const unsigned pix_per_block = blockDim.x / C4;
+    const unsigned npix = (unsigned)p.N * p.OH * p.OW;
+    const float4 *x4 = reinterpret_cast<const float4 *>(p.x);
+    const float4 *w4 = reinterpret_cast<const float4 *>(p.w);
+    float4 wk[9];  // [kh][kw] of a 3x3 frame, zero outside KH x KW (static indices only)
+#pragma unroll
+    for (int t = 0; t < 9; ++t) {
+        const int kh = t / 3, kw = t % 3;
+        wk[t] = (kh < p.KH && kw < p.KW) ? __ldg(w4 + (kh * p.KW + kw) * C4 + c4) : make_float4(0.f, 0.f, 0.f, 0.f);
+    }
+    const float4 b = p.bias ? __ldg(reinterpret_cast<const float4 *>(p.bias) + c4) : make_float4(0.f, 0.f, 0.f, 0.f);
+    for (unsigned pix = blockIdx.x * pix_per_block + threadIdx.x / C4; pix < npix; pix += gridDim.x * pix_per_block) {
+        const unsigned ow = pix % p.OW, r = pix / p.OW;
+        const unsigned oh = r % p.OH, n = r / p.OH;
+        float4 acc = b;
+#pragma unroll
+        for (int kh = 0; kh < 3; ++kh) {
+            if (kh >= p.KH) break;
+            const int ih = (int)oh * p.SH - p.PT + kh * p.DH;
+            if (ih < 0 || ih >= p.H) continue;
+            const unsigned rowbase = (n * p.H + ih) * p.W;
+#pragma unroll
+            for (int kw = 0; kw < 3; ++kw) {
+                if (kw >= p.KW) break;
+                const int iw = (int)ow * p.SW - p.PL + kw * p.DW;
+                if (iw < 0 || iw >= p.W) continue;
+                const float4 v = __ldg(x4 + (size_t)(rowbase + iw) * C4 + c4);
+                const float4 k = wk[kh * 3 + kw];
+                acc.x = fmaf(v.x, k.x, acc.x); acc.y = fmaf(v.y, k.y, acc.y);
+                acc.z = fmaf(v.z, k.z, acc.z); acc.w = fmaf(v.w, k.w, acc.w);
+            }
+        }
+        const size_t o = (size_t)pix * C4 + c4;
+        if (p.res) {
+            const float4 rr = reinterpret_cast<const float4 *>(p.res)[o];
+            acc.x += rr.x; acc.y += rr.y; acc.z += rr.z; acc.w += rr.w;
+        }
+        if (p.act == MGC_ACT_RELU) {
+            acc.x = fmaxf(acc.x, 0.0f); acc.y = fmaxf(acc.y, 0.0f); acc.z = fmaxf(acc.z, 0.0f); acc.w = fmaxf(acc.w, 0.0f);
+        } else if (p.act == MGC_ACT_CLIP) {
+            acc.x = fminf(fmaxf(acc.x, p.lo), p.hi); acc.y = fminf(fmaxf(acc.y, p.lo), p.hi);
+            acc.z = fminf(fmaxf(acc.z, p.lo), p.hi); acc.w = fminf(fmaxf(acc.w, p.lo), p.hi);
+        } else if (p.act != MGC_ACT_NONE) {
+            acc.x = apply_act(acc.x, p.act, p.lo, p.hi); acc.y = apply_act(acc.y, p.act, p.lo, p.hi);
+            acc.z = apply_act(acc.z, p.act, p.lo, p.hi); acc.w = apply_act(acc.w, p.act, p.lo, p.hi);
+        }
+        reinterpret_cast<float4 *>(p.y)[o] = acc;
+    }
+}
+
 // Any C, either layout (NCHW weights CHW).
 __global__ void __launch_bounds__(256) depthwise_kernel(const __grid_constant__ DepthwiseParams p) {
     const long long total = (long long)p.N * p.OH * p.OW * p.C;

@@ -216,8 +216,18 @@ inline int launch_record(const mgc_cuda_launch &L, const int64_t *aux, int64_t a
         const bool vec4 = p.nhwc && p.C % 4 == 0 &&
                           ((((uintptr_t)p.x) | ((uintptr_t)p.w) | ((uintptr_t)p.y) |
                             ((uintptr_t)p.bias) | ((uintptr_t)p.res)) % 16 == 0);
-        if (vec4) depthwise_nhwc4_kernel<<<grid_for(total / 4, 256), 256, 0, stream>>>(p);
-        else depthwise_kernel<<<grid_for(total, 256), 256, 0, stream>>>(p);
+        const int c4 = p.C / 4;
+        const bool reg = vec4 && p.KH <= 3 && p.KW <= 3 && c4 <= 256 &&
+                         (long long)p.N * p.H * p.W * c4 < (1ll << 31) && total / 4 < (1ll << 31);
+        if (reg) {
+            const int block = (256 / c4) * c4;  // a multiple of C / 4: each thread keeps its channels
+            const long long npix = (long long)p.N * p.OH * p.OW;
+            depthwise_nhwc4_reg_kernel<<<grid_for(npix, block / c4), block, 0, stream>>>(p);
+        } else if (vec4) {
+            depthwise_nhwc4_kernel<<<grid_for(total / 4, 256), 256, 0, stream>>>(p);
+        } else {
+            depthwise_kernel<<<grid_for(total, 256), 256, 0, stream>>>(p);
+        }
         st = check_launch("depthwise_kernel");
         break;
     }
