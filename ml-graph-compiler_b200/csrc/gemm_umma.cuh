@@ -55,7 +55,11 @@ constexpr long long WAIT_LIMIT_CYCLES = 1ll << 31;  // ~1.1 s at 1.9 GHz
 // TF32 mode: K blocks whose products share one TMEM accumulator before the epilogue promotes it
 // to registers (a tensor-core accumulation chain of 4 * PROMOTE_KB MMA steps). The epilogue's
 // drain then runs every PROMOTE_KB blocks, so the MMA warp rarely waits for a free buffer.
-constexpr int PROMOTE_KB = 2;
+// Measured on ResNet-50 (batch 4 against the float64 oracle): promotion every 1, 2, 4 or 8
+// blocks gives the same logit error (max 1.7e-2, mean |err| 3.6-3.7e-3, mean signed err within
+// +-5e-5): the operand rounding of the activations dominates, the accumulator's rounding toward
+// zero over 32 steps does not show. The step time drops 5.5 % from 2 to 8.
+constexpr int PROMOTE_KB = 8;
 
 enum Mode { TF32 = 0, STRICT = 1 };
 
