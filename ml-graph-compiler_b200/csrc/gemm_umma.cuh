@@ -20,10 +20,11 @@
 //   to fp32), so the only operand error is the unbiased rounding of the activations.
 // * MGC_PREC_3XTF32 ("strict"): the epilogue warps split the raw A tile into hi = RN_tf32(A) and
 //   lo = A - hi in shared memory; each K step issues A_lo*B_hi + A_hi*B_lo + A_hi*B_hi.
-// * Accumulator promotion: every K block writes its products into a fresh TMEM region (double
-//   buffered); the four epilogue warps add each region into fp32 registers with round-to-nearest
-//   while the tensor core works on the next block. In strict mode each of the four K=8 steps of a
-//   block gets its own region, so no tensor-core accumulation chain is longer than one step.
+// * Accumulator promotion: every group of PROMOTE_KB K blocks (TF32 mode) writes its products
+//   into a fresh TMEM region (double or quadruple buffered); the epilogue warps add each region
+//   into fp32 registers with round-to-nearest while the tensor core works on the next group. In
+//   strict mode each of the four K=8 steps of a block gets its own region, so no tensor-core
+//   accumulation chain is longer than one step.
 //
 // Roles: warp 0 issues TMA (lane 0, or the whole warp for the narrow-channel forms); warp 1
 // allocates TMEM and lane 0 issues tcgen05.mma; warps 2-9 (256 threads: two per TMEM lane, each
