@@ -353,6 +353,36 @@ __global__ void __launch_bounds__(256) copy_kernel(const __grid_constant__ CopyP
     }
 }
 
+// The same copy with 32-bit index arithmetic and V elements per thread along the innermost
+// dimension (contiguous on both sides): the caller passes the shape and strides in units of V
+// elements (innermost extent divided by V) and checks alignment and that every index fits.
+template <typename VT>
+__global__ void __launch_bounds__(256) copy_vec_kernel(const __grid_constant__ CopyParams P) {
+    const VT *src = (const VT *)P.src;
+    VT *dst = (VT *)P.dst;
+    int shape[COPY_MAX_RANK], sstr[COPY_MAX_RANK], dstr[COPY_MAX_RANK];
+#pragma unroll
+    for (int k = 0; k < COPY_MAX_RANK; ++k) {
+        shape[k] = k < P.rank ? (int)P.shape[k] : 1;
+        sstr[k] = k < P.rank ? (int)P.sstr[k] : 0;
+        dstr[k] = k < P.rank ? (int)P.dstr[k] : 0;
+    }
+    const unsigned total = (unsigned)P.total, stride = gridDim.x * blockDim.x;
+    for (unsigned o = blockIdx.x * blockDim.x + threadIdx.x; o < total; o += stride) {
+        unsigned rem = o;
+        int s = (int)P.sbase, d = (int)P.dbase;
+#pragma unroll
+        for (int k = COPY_MAX_RANK - 1; k >= 0; --k) {
+            if (k >= P.rank) continue;
+            const unsigned i = rem % (unsigned)shape[k];
+            rem /= (unsigned)shape[k];
+            s += (int)i * sstr[k];
+            d += (int)i * dstr[k];
+        }
+        dst[d] = src[s];
+    }
+}
+
 // Tile: out[o] = x[src(o)] with src dims taken modulo the input shape (c.py:571-588).
 struct TileParams {
     long long oshape[COPY_MAX_RANK];

@@ -178,6 +178,30 @@ inline int decode_elementwise(const mgc_cuda_launch &L, const int64_t *aux, int6
 
 template <typename T>
 inline int launch_copy_t(const CopyParams &P, cudaStream_t s) {
+    // Vectorised, 32-bit form: the innermost dimension contiguous on both sides, its extent,
+    // every stride and both bases multiples of 16 bytes, both pointers 16-byte aligned, and every
+    // index (in elements) below 2^31.
+    const int r = P.rank;
+    const long long v = 16 / (long long)sizeof(T);
+    bool vec = r >= 1 && P.sstr[r - 1] == 1 && P.dstr[r - 1] == 1 && P.shape[r - 1] % v == 0 &&
+               P.sbase % v == 0 && P.dbase % v == 0 && (reinterpret_cast<uintptr_t>(P.src) & 15) == 0 &&
+               (reinterpret_cast<uintptr_t>(P.dst) & 15) == 0;
+    long long smax = P.sbase, dmax = P.dbase;
+    for (int k = 0; k < r && vec; ++k) {
+        if (k < r - 1 && (P.sstr[k] % v || P.dstr[k] % v)) vec = false;
+        smax += (P.shape[k] - 1) * (P.sstr[k] < 0 ? 0 : P.sstr[k]);
+        dmax += (P.shape[k] - 1) * (P.dstr[k] < 0 ? 0 : P.dstr[k]);
+        if (P.sstr[k] < 0 || P.dstr[k] < 0) vec = false;
+    }
+    if (vec && P.total < (1ll << 31) && smax < (1ll << 31) && dmax < (1ll << 31)) {
+        CopyParams Q = P;
+        Q.shape[r - 1] = P.shape[r - 1] / v;
+        for (int k = 0; k < r - 1; ++k) { Q.sstr[k] = P.sstr[k] / v; Q.dstr[k] = P.dstr[k] / v; }
+        Q.sbase = P.sbase / v; Q.dbase = P.dbase / v;
+        Q.total = P.total / v;
+        copy_vec_kernel<uint4><<<grid_for(Q.total, 256), 256, 0, s>>>(Q);
+        return check_launch("copy_vec_kernel");
+    }
     copy_kernel<T><<<grid_for(P.total, 256), 256, 0, s>>>(P);
     return check_launch("copy_kernel");
 }
