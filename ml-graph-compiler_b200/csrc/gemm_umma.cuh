@@ -37,6 +37,7 @@
 
 #include <cuda.h>
 #include <cudaTypedefs.h>
+#include <stdlib.h>
 #include <string.h>
 
 #include <type_traits>
@@ -129,6 +130,20 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t *bar, uint32_t parity) {
     return done != 0;
 }
 
+// Non-blocking test of the same (the thread never suspends); the result is read later, so the
+// test's latency overlaps whatever the thread issues meanwhile.
+__device__ __forceinline__ bool mbar_test_wait(uint64_t *bar, uint32_t parity) {
+    uint32_t done;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.test_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}\n"
+        : "=r"(done)
+        : "r"(smem_addr(bar)), "r"(parity)
+        : "memory");
+    return done != 0;
+}
+
 // Bounded wait for the phase with parity `parity` to complete. Returns false on timeout.
 __device__ __forceinline__ bool mbar_wait(uint64_t *bar, uint32_t parity) {
     if (mbar_try_wait(bar, parity)) return true;
@@ -180,6 +195,64 @@ __device__ __forceinline__ void tma_load_5d(void *dst, const CUtensorMap *map, u
         " [%0], [%1, {%3, %4, %5, %6, %7}], [%2];"
         ::"r"(smem_addr(dst)), "l"(reinterpret_cast<uint64_t>(map)), "r"(smem_addr(bar)), "r"(x), "r"(y), "r"(z),
         "r"(w), "r"(v)
+        : "memory");
+}
+
+// ---- CTA pairs (cta_group::2) ------------------------------------------------------------------
+// A pair of CTAs (a cluster of two) computes one 256-row tile: each CTA loads its own 128 rows of
+// A and one plane of B (rank 0 the TF32 part, rank 1 the residual) into the same shared-memory
+// offsets, and rank 0 issues MMAs with M = 256 that read both CTAs' operands and write each CTA's
+// rows into its own TMEM. Every load of the pair completes on rank 0's stage barrier.
+__device__ __forceinline__ uint32_t cluster_rank() {
+    uint32_t r;
+    asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+    return r;
+}
+__device__ __forceinline__ uint32_t cluster_index() {
+    uint32_t r;
+    asm volatile("mov.u32 %0, %%clusterid.x;" : "=r"(r));
+    return r;
+}
+__device__ __forceinline__ uint32_t cluster_count() {
+    uint32_t r;
+    asm volatile("mov.u32 %0, %%nclusterid.x;" : "=r"(r));
+    return r;
+}
+// Address of the same shared variable in the pair's rank-0 CTA (shared::cluster window).
+__device__ __forceinline__ uint32_t leader_addr(const void *p) {
+    uint32_t r;
+    asm volatile("mapa.shared::cluster.u32 %0, %1, 0;" : "=r"(r) : "r"(smem_addr(p)));
+    return r;
+}
+// All threads of both CTAs; orders barrier initialisation before any remote arrive, and every
+// remote access before either CTA exits.
+__device__ __forceinline__ void cluster_sync_all() {
+    asm volatile("barrier.cluster.arrive.release;\n\tbarrier.cluster.wait.acquire;" ::: "memory");
+}
+__device__ __forceinline__ void mbar_arrive_remote(uint32_t cluster_addr) {
+    asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(cluster_addr) : "memory");
+}
+__device__ __forceinline__ void tma_load_2d_pair(void *dst, const CUtensorMap *map, uint32_t bar, int x, int y) {
+    asm volatile(
+        "cp.async.bulk.tensor.2d.cta_group::2.shared::cluster.global.mbarrier::complete_tx::bytes"
+        " [%0], [%1, {%3, %4}], [%2];"
+        ::"r"(smem_addr(dst)), "l"(reinterpret_cast<uint64_t>(map)), "r"(bar), "r"(x), "r"(y)
+        : "memory");
+}
+__device__ __forceinline__ void tma_load_3d_pair(void *dst, const CUtensorMap *map, uint32_t bar, int x, int y, int z) {
+    asm volatile(
+        "cp.async.bulk.tensor.3d.cta_group::2.shared::cluster.global.mbarrier::complete_tx::bytes"
+        " [%0], [%1, {%3, %4, %5}], [%2];"
+        ::"r"(smem_addr(dst)), "l"(reinterpret_cast<uint64_t>(map)), "r"(bar), "r"(x), "r"(y), "r"(z)
+        : "memory");
+}
+__device__ __forceinline__ void tma_load_im2col_4d_pair(void *dst, const CUtensorMap *map, uint32_t bar, int c, int w,
+                                                        int h, int n, uint16_t off_w, uint16_t off_h) {
+    asm volatile(
+        "cp.async.bulk.tensor.4d.im2col.cta_group::2.shared::cluster.global.mbarrier::complete_tx::bytes"
+        " [%0], [%1, {%3, %4, %5, %6}], [%2], {%7, %8};"
+        ::"r"(smem_addr(dst)), "l"(reinterpret_cast<uint64_t>(map)), "r"(bar), "r"(c), "r"(w), "r"(h), "r"(n),
+        "h"(off_w), "h"(off_h)
         : "memory");
 }
 
@@ -235,6 +308,18 @@ __device__ __forceinline__ void tmem_dealloc(uint32_t taddr, uint32_t cols) {
     asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(taddr), "r"(cols) : "memory");
 }
 
+// Pair forms: warp 1 of both CTAs allocates (and frees) the same columns in each CTA's TMEM.
+__device__ __forceinline__ void tmem_alloc_pair(uint32_t *slot, uint32_t cols) {
+    asm volatile("tcgen05.alloc.cta_group::2.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_addr(slot)),
+                 "r"(cols)
+                 : "memory");
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::2.sync.aligned;" ::: "memory");
+}
+
+__device__ __forceinline__ void tmem_dealloc_pair(uint32_t taddr, uint32_t cols) {
+    asm volatile("tcgen05.dealloc.cta_group::2.sync.aligned.b32 %0, %1;" ::"r"(taddr), "r"(cols) : "memory");
+}
+
 __device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
 __device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
 
@@ -262,13 +347,13 @@ __device__ __forceinline__ uint64_t plain_desc(uint32_t saddr, uint32_t lbo, uin
 // 2 KB apart along K.
 constexpr uint32_t PACKED_BOX_BYTES = BM * 16;
 
-// kind::tf32, fp32 accumulate, both operands K-major, M = 128.
-__host__ __device__ constexpr uint32_t instr_desc_tf32(int n) {
+// kind::tf32, fp32 accumulate, both operands K-major; M = 128 (one CTA) or 256 (a CTA pair).
+__host__ __device__ constexpr uint32_t instr_desc_tf32(int n, int m = BM) {
     return (1u << 4)                 // D format f32
            | (2u << 7)               // A format tf32
            | (2u << 10)              // B format tf32
            | ((uint32_t)(n >> 3) << 17)
-           | ((uint32_t)(BM >> 4) << 24);
+           | ((uint32_t)(m >> 4) << 24);
 }
 
 __device__ __forceinline__ void mma_tf32(uint32_t tmem_d, uint64_t adesc, uint64_t bdesc, uint32_t idesc,
@@ -283,6 +368,30 @@ __device__ __forceinline__ void mma_tf32(uint32_t tmem_d, uint64_t adesc, uint64
 
 __device__ __forceinline__ void mma_commit(uint64_t *bar) {
     asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_addr(bar))
+                 : "memory");
+}
+
+// Pair MMA (issued by rank 0): A rows 0-127 from rank 0's shared memory and 128-255 from rank 1's,
+// B rows [0, N/2) from rank 0 and [N/2, N) from rank 1; D rows land in each CTA's own TMEM.
+__device__ __forceinline__ void mma_tf32_pair(uint32_t tmem_d, uint64_t adesc, uint64_t bdesc, uint32_t idesc,
+                                              uint32_t accumulate) {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "setp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::2.kind::tf32 [%0], %1, %2, %3, p;\n\t}\n"
+        ::"r"(tmem_d), "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate)
+        : "memory");
+}
+
+// Arrive on `bar` (same offset) in both CTAs of the pair once the pair MMAs issued so far complete.
+__device__ __forceinline__ void mma_commit_pair(uint64_t *bar) {
+    asm volatile("tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.multicast::cluster.b64 [%0], %1;"
+                 ::"r"(smem_addr(bar)), "h"((uint16_t)3)
+                 : "memory");
+}
+
+__device__ __forceinline__ void mma_commit_pair_local(uint64_t *bar) {
+    asm volatile("tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_addr(bar))
                  : "memory");
 }
 
@@ -340,25 +449,33 @@ constexpr uint32_t SMEM_LIMIT = 232448;  // dynamic shared memory per block on s
 
 // RB: B-resident variant. The CTA keeps one N tile for its whole life and loads that tile's B
 // panel (every K block, hi and lo) into shared memory once; the stages then carry A only.
-template <int BN, int MODE, int RB = 0>
+// PAIR: CTA-pair variant (TF32 mode): 256-row tiles, each CTA holding one plane of B.
+template <int BN, int MODE, int RB = 0, int PAIR = 0>
 struct Cfg {
+    static_assert(!PAIR || MODE == TF32, "CTA pairs run TF32 mode only");
     static constexpr int REGIONS = MODE == STRICT ? 4 : 1;  // TMEM regions per K block
     static constexpr uint32_t B_TILE_BYTES = BN * BK * 4;
-    // stage: A (| A_lo) (| B_hi | B_lo)
+    static constexpr int B_PLANES = PAIR ? 1 : 2;            // B planes in this CTA's shared memory
+    static constexpr int TM = PAIR ? 2 * BM : BM;            // rows of one tile
+    // stage: A (| A_lo) (| B_hi | B_lo), or A | this rank's B plane
     static constexpr uint32_t STAGE_BYTES =
-        A_TILE_BYTES + (MODE == STRICT ? A_TILE_BYTES : 0) + (RB ? 0 : 2 * B_TILE_BYTES);
+        A_TILE_BYTES + (MODE == STRICT ? A_TILE_BYTES : 0) + (RB ? 0 : B_PLANES * B_TILE_BYTES);
     // output tile staging: BN/32 slabs of [128 rows][32 fp32] in the 128B-swizzled TMA layout
     static constexpr uint32_t OUT_BYTES = BM * BN * 4;
-    static constexpr uint32_t STAGE_BUDGET = 212992 - OUT_BYTES;
+    static constexpr uint32_t BAR_BYTES = 512;                     // mbarriers and the TMEM address
+    // everything else: output staging, alignment slack, barriers, the tile's bias
+    static constexpr uint32_t STAGE_BUDGET = SMEM_LIMIT - OUT_BYTES - 1024 - BAR_BYTES - BN * 4;
+    // (pairs: 4 stages measured faster than 5 on the ResNet-50 3x3 layers)
+    static constexpr int MAX_STAGES = PAIR ? 4 : 8;
     static constexpr int STAGES = RB ? (MODE == STRICT ? 2 : 4)
                                   : (STAGE_BUDGET / STAGE_BYTES) < 2 ? 2
-                                  : (STAGE_BUDGET / STAGE_BYTES) > 8 ? 8 : (STAGE_BUDGET / STAGE_BYTES);
+                                  : (int)(STAGE_BUDGET / STAGE_BYTES) > MAX_STAGES ? MAX_STAGES
+                                  : (STAGE_BUDGET / STAGE_BYTES);
     // TMEM columns of one K block: strict, four step regions of BN; TF32, the products with B_hi
     // (columns [0, BN)) and with B_lo ([BN, 2 BN)) from one N = 2 BN MMA per K step
     static constexpr uint32_t BUF_COLS = MODE == STRICT ? REGIONS * BN : 2 * BN;
     static constexpr int TBUFS = (512 / BUF_COLS) > 4 ? 4 : (512 / BUF_COLS);  // TMEM buffers in the ring
     static constexpr uint32_t TMEM_COLS = TBUFS * BUF_COLS;
-    static constexpr uint32_t BAR_BYTES = 512;                     // mbarriers and the TMEM address
     // fixed part; a B-resident launch adds its B panel (b_res_bytes) in front of the stages
     static constexpr uint32_t SMEM_BYTES = STAGES * STAGE_BYTES + OUT_BYTES + 1024 /*align*/ + BAR_BYTES + BN * 4 /*bias*/;
     static constexpr uint32_t B_RES_MAX = RB ? SMEM_LIMIT - SMEM_BYTES : 0;
@@ -372,9 +489,9 @@ struct Cfg {
 // and walks the M tiles b / n_tiles, + gridDim.x / n_tiles, ... The shared-memory stage ring and
 // the TMEM buffer ring run on a K-block counter that continues across tiles, so the next tile's
 // loads and MMAs overlap this tile's drain and epilogue.
-template <int BN, int MODE, int RB>
+template <int BN, int MODE, int RB, int PAIR>
 __global__ void __launch_bounds__(THREADS, 1) umma_gemm_kernel(const __grid_constant__ Params p) {
-    using C = Cfg<BN, MODE, RB>;
+    using C = Cfg<BN, MODE, RB, PAIR>;
     constexpr int S = C::STAGES;
     constexpr int R = C::REGIONS;
     constexpr int TB = C::TBUFS;
@@ -387,7 +504,7 @@ __global__ void __launch_bounds__(THREADS, 1) umma_gemm_kernel(const __grid_cons
     auto alo_tile = [&](int s) { return stages + (size_t)s * C::STAGE_BYTES + A_TILE_BYTES; };
     // B_hi of K block kb (B_lo follows it directly: the stacked [B_hi; B_lo] operand)
     auto b_tile = [&](int s, int kb) {
-        return RB ? b_panel + (size_t)kb * 2 * C::B_TILE_BYTES
+        return RB ? b_panel + (size_t)kb * C::B_PLANES * C::B_TILE_BYTES
                   : stages + (size_t)s * C::STAGE_BYTES + A_TILE_BYTES + (MODE == STRICT ? A_TILE_BYTES : 0);
     };
     uint8_t *out_tile = stages + (size_t)S * C::STAGE_BYTES;  // 1024-aligned
@@ -405,15 +522,20 @@ __global__ void __launch_bounds__(THREADS, 1) umma_gemm_kernel(const __grid_cons
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int num_kb = p.num_kb;
     const int total_tiles = p.n_tiles * p.m_tiles;
-    // the i-th tile of this CTA as (M tile, N tile); false past the last
+    // pairs: this CTA's rank (0 issues the MMAs) and the pair as the unit of the tile walk
+    const uint32_t rank = PAIR ? cluster_rank() : 0u;
+    const int unit = PAIR ? (int)cluster_index() : (int)blockIdx.x;
+    const int units = PAIR ? (int)cluster_count() : (int)gridDim.x;
+    const int row0 = (int)rank * BM;  // this CTA's first row within a tile
+    // the i-th tile of this CTA (or pair) as (M tile, N tile); false past the last
     auto tile_at = [&](int i, int &mt, int &nt) -> bool {
         if (RB) {
-            const int per = (int)gridDim.x / p.n_tiles;
-            nt = (int)blockIdx.x % p.n_tiles;
-            mt = (int)blockIdx.x / p.n_tiles + i * per;
-            return (int)blockIdx.x < per * p.n_tiles && mt < p.m_tiles;
+            const int per = units / p.n_tiles;
+            nt = unit % p.n_tiles;
+            mt = unit / p.n_tiles + i * per;
+            return unit < per * p.n_tiles && mt < p.m_tiles;
         }
-        const int t = (int)blockIdx.x + i * (int)gridDim.x;
+        const int t = unit + i * units;
         nt = t % p.n_tiles;
         mt = t / p.n_tiles;
         return t < total_tiles;
@@ -427,20 +549,25 @@ __global__ void __launch_bounds__(THREADS, 1) umma_gemm_kernel(const __grid_cons
         }
         for (int b = 0; b < TB; ++b) {
             mbar_init(&tfull[b], 1);
-            mbar_init(&tempty[b], EPI_THREADS);
+            // pairs: one arrival per epilogue warp of both CTAs, on rank 0's barrier
+            mbar_init(&tempty[b], PAIR ? 2 * (EPI_THREADS / 32) : EPI_THREADS);
         }
         mbar_init(mma_done, 1);
         mbar_init(res_full, 1);
         mbar_init(bres_full, 1);
         fence_barrier_init();
     }
-    if (warp == 1) tmem_alloc(tmem_slot, C::TMEM_COLS);
+    if (warp == 1) {
+        if (PAIR) tmem_alloc_pair(tmem_slot, C::TMEM_COLS);
+        else tmem_alloc(tmem_slot, C::TMEM_COLS);
+    }
     tc_fence_before();
     __syncthreads();
+    if (PAIR) cluster_sync_all();
     tc_fence_after();
     const uint32_t tmem_base = *tmem_slot;
 
-    if (warp == 0 && p.im2col >= 2) {
+    if (warp == 0 && !PAIR && p.im2col >= 2) {
         // ---------------- TMA producer, narrow-channel forms (the whole warp) ----------------
         // A TMA instruction holds its issuing thread for a few hundred cycles. These forms need
         // eight or more A boxes per K block, so lane j issues box j, all in one instruction.
@@ -517,17 +644,24 @@ __global__ void __launch_bounds__(THREADS, 1) umma_gemm_kernel(const __grid_cons
     } else if (warp == 0) {
         if (lane == 0) {
             // ---------------- TMA producer: one A box per K block (lane 0) ----------------
-            constexpr uint32_t bytes = A_TILE_BYTES + (RB ? 0 : 2 * C::B_TILE_BYTES);
+            // a pair's stage barrier (rank 0's) counts the bytes of both CTAs
+            constexpr uint32_t bytes = PAIR ? 2 * (A_TILE_BYTES + (RB ? 0 : C::B_TILE_BYTES))
+                                            : A_TILE_BYTES + (RB ? 0 : 2 * C::B_TILE_BYTES);
+            const bool arms = !PAIR || rank == 0;  // this thread arms the stage barriers
             long long g = 0;  // K blocks issued so far
             bool ok = true;
+            bool free_next = false;  // the slot of K block g was tested free
             int mt, nt;
-            if (RB && tile_at(0, mt, nt)) {  // this CTA's B panel, once
-                mbar_expect_tx(bres_full, p.b_res_bytes);
+            if (RB && tile_at(0, mt, nt)) {  // this CTA's B panel (its plane, for a pair), once
+                if (arms) mbar_expect_tx(bres_full, PAIR ? 2 * p.b_res_bytes : p.b_res_bytes);
 #pragma unroll 1
-                for (int kb = 0; kb < num_kb; ++kb) tma_load_3d(b_tile(0, kb), &p.tmB, bres_full, kb * BK, nt * BN, 0);
+                for (int kb = 0; kb < num_kb; ++kb) {
+                    if (PAIR) tma_load_3d_pair(b_tile(0, kb), &p.tmB, leader_addr(bres_full), kb * BK, nt * BN, (int)rank);
+                    else tma_load_3d(b_tile(0, kb), &p.tmB, bres_full, kb * BK, nt * BN, 0);
+                }
             }
             for (int i = 0; ok && tile_at(i, mt, nt); ++i) {
-                const int n0 = nt * BN, m0 = mt * BM;
+                const int n0 = nt * BN, m0 = mt * C::TM + row0;
                 int wb = 0, hb = 0, nb = 0;
                 if (p.im2col) {
                     const int hw = p.OH * p.OW;
@@ -540,54 +674,72 @@ __global__ void __launch_bounds__(THREADS, 1) umma_gemm_kernel(const __grid_cons
                 for (int kb = 0; kb < num_kb; ++kb, ++g) {
                     const int s = (int)(g % S);
                     const long long round = g / S;
-                    if (round > 0 && !mbar_wait(&empty[s], (uint32_t)((round - 1) & 1))) {
+                    if (round > 0 && !free_next && !mbar_wait(&empty[s], (uint32_t)((round - 1) & 1))) {
                         set_error(p.err, MGC_CUDA_TIMEOUT);
                         ok = false;
                         break;
                     }
-                    mbar_expect_tx(&full[s], bytes);
+                    // test the next K block's slot now; the test's latency overlaps this block's
+                    // TMA issue, and a slot found free needs no wait
+                    const long long round1 = (g + 1) / S;
+                    free_next = round1 == 0 || mbar_test_wait(&empty[(int)((g + 1) % S)], (uint32_t)((round1 - 1) & 1));
+                    if (arms) mbar_expect_tx(&full[s], bytes);
                     if (p.im2col) {
                         const int cb = kb % p.cblocks;
                         const int t = kb / p.cblocks;
                         const int kw = t % p.KW, kh = t / p.KW;
-                        tma_load_im2col_4d(a_tile(s), &p.tmA, &full[s], cb * BK, wb, hb, nb, (uint16_t)(kw * p.DW),
-                                           (uint16_t)(kh * p.DH));
+                        if (PAIR)
+                            tma_load_im2col_4d_pair(a_tile(s), &p.tmA, leader_addr(&full[s]), cb * BK, wb, hb, nb,
+                                                    (uint16_t)(kw * p.DW), (uint16_t)(kh * p.DH));
+                        else
+                            tma_load_im2col_4d(a_tile(s), &p.tmA, &full[s], cb * BK, wb, hb, nb, (uint16_t)(kw * p.DW),
+                                               (uint16_t)(kh * p.DH));
+                    } else if (PAIR) {
+                        tma_load_2d_pair(a_tile(s), &p.tmA, leader_addr(&full[s]), kb * BK, m0);
                     } else {
                         tma_load_2d(a_tile(s), &p.tmA, &full[s], kb * BK, m0);
                     }
                     (void)n0;  // B comes from the B producer warp
                 }
             }
-            // the copies of the last (up to S) issued K blocks must have landed before exit
-            for (long long k = g - 1; k >= 0 && k >= g - S; --k) {
-                if (!mbar_wait(&full[k % S], (uint32_t)((k / S) & 1))) set_error(p.err, MGC_CUDA_TIMEOUT);
+            // the copies of the last (up to S) issued K blocks must have landed before exit (a
+            // pair's rank 0 waits for both CTAs' copies; rank 1 leaves after the closing cluster
+            // barrier, which rank 0 reaches only after these waits)
+            if (arms) {
+                for (long long k = g - 1; k >= 0 && k >= g - S; --k) {
+                    if (!mbar_wait(&full[k % S], (uint32_t)((k / S) & 1))) set_error(p.err, MGC_CUDA_TIMEOUT);
+                }
+                if (RB && tile_at(0, mt, nt) && !mbar_wait(bres_full, 0)) set_error(p.err, MGC_CUDA_TIMEOUT);
             }
-            if (RB && tile_at(0, mt, nt) && !mbar_wait(bres_full, 0)) set_error(p.err, MGC_CUDA_TIMEOUT);
         }
     } else if (warp == B_WARP) {
         if (lane == 0 && !RB) {
             // ---------------- B producer: one 3-D box (TF32 part and residual) per K block ----------------
             long long g = 0;
             bool ok = true;
+            bool free_next = false;  // the slot of K block g was tested free
             int mt, nt;
             for (int i = 0; ok && tile_at(i, mt, nt); ++i) {
                 for (int kb = 0; kb < num_kb; ++kb, ++g) {
                     const int s = (int)(g % S);
                     const long long round = g / S;
-                    if (round > 0 && !mbar_wait(&empty[s], (uint32_t)((round - 1) & 1))) {
+                    if (round > 0 && !free_next && !mbar_wait(&empty[s], (uint32_t)((round - 1) & 1))) {
                         set_error(p.err, MGC_CUDA_TIMEOUT);
                         ok = false;
                         break;
                     }
-                    tma_load_3d(b_tile(s, kb), &p.tmB, &full[s], kb * BK, nt * BN, 0);
+                    const long long round1 = (g + 1) / S;
+                    free_next = round1 == 0 || mbar_test_wait(&empty[(int)((g + 1) % S)], (uint32_t)((round1 - 1) & 1));
+                    if (PAIR) tma_load_3d_pair(b_tile(s, kb), &p.tmB, leader_addr(&full[s]), kb * BK, nt * BN, (int)rank);
+                    else tma_load_3d(b_tile(s, kb), &p.tmB, &full[s], kb * BK, nt * BN, 0);
                 }
             }
         }
     } else if (warp == 1) {
-        if (lane == 0) {
-            // ---------------- MMA issuer ----------------
+        if (lane == 0 && rank == 0) {
+            // ---------------- MMA issuer (a pair's rank 0 issues for both CTAs) ----------------
             constexpr uint32_t idesc = instr_desc_tf32(BN);
-            constexpr uint32_t idesc2 = instr_desc_tf32(2 * BN);  // the stacked [B_hi; B_lo] tile
+            constexpr uint32_t idesc2 = instr_desc_tf32(2 * BN, C::TM);  // the stacked [B_hi; B_lo] tile
             long long g = 0;
             bool ok = true;
             int mt, nt;
@@ -597,25 +749,40 @@ __global__ void __launch_bounds__(THREADS, 1) umma_gemm_kernel(const __grid_cons
             }
             constexpr int PG = MODE == STRICT ? 1 : PROMOTE_KB;  // K blocks per TMEM buffer
             long long gq = 0;                                    // TMEM buffers filled so far
+            uint64_t *const ready = MODE == STRICT ? split : full;  // a stage's operands are in place
+            // MMA issue blocks while the tensor pipe is busy, so a barrier test between two K
+            // blocks would leave the pipe idle for its whole latency (~150 cycles). Instead the
+            // next K block's stage is tested right after this block's first MMA is issued, and
+            // a block whose stage tested complete skips its wait.
+            bool have = false;
             for (int i = 0; ok && tile_at(i, mt, nt); ++i) {
                 for (int kb = 0; kb < num_kb; ++kb, ++g) {
                     const int s = (int)(g % S);
                     const int b = (int)(gq % TB);
                     const bool first = kb % PG == 0, last = kb % PG == PG - 1 || kb == num_kb - 1;
-                    if (!mbar_wait(MODE == STRICT ? &split[s] : &full[s], (uint32_t)((g / S) & 1))) {
+                    if (!have && !mbar_wait(&ready[s], (uint32_t)((g / S) & 1))) {
                         set_error(p.err, MGC_CUDA_TIMEOUT);
                         ok = false;
                         break;
                     }
-                    if (first && gq >= TB && !mbar_wait(&tempty[b], (uint32_t)(((gq / TB) - 1) & 1))) {
-                        set_error(p.err, MGC_CUDA_TIMEOUT);
-                        ok = false;
-                        break;
+                    if (first && gq >= TB) {
+                        // the epilogue has drained this TMEM buffer; order the MMAs after its loads.
+                        // (The stage's operands need no tcgen05 fence: the TMA writes and the MMA
+                        // reads are both async-proxy accesses ordered by the stage barrier. A fence
+                        // per K block would also cost ~600 cycles: it waits for the MMA pipe.)
+                        if (!mbar_wait(&tempty[b], (uint32_t)(((gq / TB) - 1) & 1))) {
+                            set_error(p.err, MGC_CUDA_TIMEOUT);
+                            ok = false;
+                            break;
+                        }
+                        tc_fence_after();
                     }
-                    tc_fence_after();
                     const uint32_t a_addr = smem_addr(a_tile(s)), b_addr = smem_addr(b_tile(s, kb));
                     const uint32_t bl_addr = b_addr + C::B_TILE_BYTES, al_addr = smem_addr(alo_tile(s));
                     const uint32_t dbase = tmem_base + (uint32_t)(b * C::BUF_COLS);
+                    uint64_t *const next_ready = &ready[(int)((g + 1) % S)];
+                    const uint32_t next_parity = (uint32_t)(((g + 1) / S) & 1);
+                    bool peek = false;
 #pragma unroll
                     for (int k = 0; k < BK / 8; ++k) {  // 8 tf32 = 32 bytes per MMA
                         const bool packed = p.im2col == 2;
@@ -634,18 +801,27 @@ __global__ void __launch_bounds__(THREADS, 1) umma_gemm_kernel(const __grid_cons
                             // B_lo's tile directly follows B_hi's in the stage with the same
                             // 128B-swizzled row layout, so one descriptor spans both as 2 BN rows:
                             // one MMA, A read once per K step
+                            // (a pair: the same descriptor names B_hi in rank 0, B_lo in rank 1)
                             (void)bld;
-                            mma_tf32(dbase, ad, bd, idesc2, (!first || k > 0) ? 1u : 0u);
+                            if (PAIR) mma_tf32_pair(dbase, ad, bd, idesc2, (!first || k > 0) ? 1u : 0u);
+                            else mma_tf32(dbase, ad, bd, idesc2, (!first || k > 0) ? 1u : 0u);
                         }
+                        if (k == 0) peek = mbar_test_wait(next_ready, next_parity);
                     }
-                    mma_commit(&empty[s]);   // shared-memory slot free once these MMAs read it
+                    have = peek;
+                    // shared-memory slot free once these MMAs read it (in both CTAs of a pair)
+                    if (PAIR) mma_commit_pair(&empty[s]);
+                    else mma_commit(&empty[s]);
                     if (last) {
-                        mma_commit(&tfull[b]);  // TMEM buffer b holds this group's products
+                        // TMEM buffer b holds this group's products
+                        if (PAIR) mma_commit_pair(&tfull[b]);
+                        else mma_commit(&tfull[b]);
                         ++gq;
                     }
                 }
             }
-            mma_commit(mma_done);
+            if (PAIR) mma_commit_pair_local(mma_done);
+            else mma_commit(mma_done);
             if (!mbar_wait(mma_done, 0)) set_error(p.err, MGC_CUDA_TIMEOUT);
         }
     } else {
@@ -696,7 +872,12 @@ __global__ void __launch_bounds__(THREADS, 1) umma_gemm_kernel(const __grid_cons
                 }
             }
             tc_fence_before();
-            mbar_arrive(&tempty[b]);
+            if (PAIR) {  // one arrival per warp, on rank 0's barrier
+                __syncwarp();
+                if (lane == 0) mbar_arrive_remote(leader_addr(&tempty[b]));
+            } else {
+                mbar_arrive(&tempty[b]);
+            }
             ++g;
             return true;
         };
@@ -742,7 +923,7 @@ __global__ void __launch_bounds__(THREADS, 1) umma_gemm_kernel(const __grid_cons
         if (issuer && p.tma_res) prefetch_tmap(&p.tmR);
         const bool rows = p.im2col == 4;
         auto issue_residual = [&](int mt_, int nt_) {
-            const int tn0 = nt_ * BN, tm0 = mt_ * BM;
+            const int tn0 = nt_ * BN, tm0 = mt_ * C::TM + row0;
             if (rows) {
                 const int img = mt_ / p.rt_per_img, oh0 = (mt_ - img * p.rt_per_img) * p.rt_rows;
                 mbar_expect_tx(res_full, (uint32_t)(BN / 32) * p.a_bytes);
@@ -760,7 +941,7 @@ __global__ void __launch_bounds__(THREADS, 1) umma_gemm_kernel(const __grid_cons
         if (res_tma && issuer && tile_at(0, mt, nt)) issue_residual(mt, nt);
         int local = 0;  // tiles this CTA has finished
         for (int i = 0; ok && tile_at(i, mt, nt); ++i, ++local) {
-            const int n0 = nt * BN, m0 = mt * BM;
+            const int n0 = nt * BN, m0 = mt * C::TM + row0;
 #pragma unroll
             for (int j = 0; j < HALF; ++j) acc[j] = AccT(0);
             for (int kb = 0; kb < num_kb && ok; ++kb) {
@@ -867,7 +1048,7 @@ __global__ void __launch_bounds__(THREADS, 1) umma_gemm_kernel(const __grid_cons
 #pragma unroll 1
                         for (int sl = 0; sl < BN / 32; ++sl)
                             tma_store_4d(&p.tmC, out_tile + sl * (BM * 128), n0 + sl * 32, 0, oh0, img);
-                    } else {
+                    } else if (m0 < p.M) {  // (a pair's second half may lie wholly past the last row)
 #pragma unroll 1
                         for (int sl = 0; sl < BN / 32; ++sl)
                             tma_store_2d(&p.tmC, out_tile + sl * (BM * 128), n0 + sl * 32, m0);
@@ -885,9 +1066,11 @@ __global__ void __launch_bounds__(THREADS, 1) umma_gemm_kernel(const __grid_cons
     }
     tc_fence_before();
     __syncthreads();
+    if (PAIR) cluster_sync_all();  // no CTA of a pair leaves while its peer may still signal it
     if (warp == 1) {
         tc_fence_after();
-        tmem_dealloc(tmem_base, C::TMEM_COLS);
+        if (PAIR) tmem_dealloc_pair(tmem_base, C::TMEM_COLS);
+        else tmem_dealloc(tmem_base, C::TMEM_COLS);
     }
 }
 
@@ -937,15 +1120,17 @@ inline bool make_map_2d(CUtensorMap *map, const void *base, long long rows, long
 }
 
 // The two K-major planes of a constant B ([N][Kp] TF32 part at `hi`, residual at `lo`, lo > hi)
-// as one tensor [2][N][Kp]; a box {32, box_rows, 2} lands as the hi tile followed by the lo tile.
-inline bool make_map_b(CUtensorMap *map, const float *hi, const float *lo, long long rows, long long kp, int box_rows) {
+// as one tensor [2][N][Kp]; a box {32, box_rows, 2} lands as the hi tile followed by the lo tile,
+// a box {32, box_rows, 1} (planes = 1, CTA pairs) as the tile of one plane.
+inline bool make_map_b(CUtensorMap *map, const float *hi, const float *lo, long long rows, long long kp, int box_rows,
+                       int planes = 2) {
     auto fn = encode_tiled_fn();
     if (!fn) return false;
     const long long gap = reinterpret_cast<const char *>(lo) - reinterpret_cast<const char *>(hi);
     if (gap <= 0 || (gap & 15) || gap >= (1ll << 40)) return false;
     cuuint64_t dims[3] = {(cuuint64_t)kp, (cuuint64_t)rows, 2};
     cuuint64_t strides[2] = {(cuuint64_t)(kp * 4), (cuuint64_t)gap};
-    cuuint32_t box[3] = {(cuuint32_t)BK, (cuuint32_t)box_rows, 2};
+    cuuint32_t box[3] = {(cuuint32_t)BK, (cuuint32_t)box_rows, (cuuint32_t)planes};
     cuuint32_t estr[3] = {1, 1, 1};
     CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 3, const_cast<float *>(hi), dims, strides, box, estr,
                     CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
@@ -1009,15 +1194,39 @@ inline bool make_map_rows(CUtensorMap *map, const void *base, long long n, long 
     return r == CUDA_SUCCESS;
 }
 
-template <int BN, int MODE, int RB>
-inline int launch(const Params &p, int grid, cudaStream_t stream) {
-    using C = Cfg<BN, MODE, RB>;
+// Dynamic shared memory of a launch. Pair launches ask for more than half an SM's shared memory,
+// so no two CTAs (and no two TMEM allocations) ever share an SM.
+template <int BN, int MODE, int RB, int PAIR>
+inline uint32_t launch_smem(const Params &p) {
+    using C = Cfg<BN, MODE, RB, PAIR>;
     const uint32_t smem = C::SMEM_BYTES + (RB ? p.b_res_bytes : 0u);
+    return PAIR && smem < SMEM_LIMIT / 2 + 1024 ? SMEM_LIMIT / 2 + 1024 : smem;
+}
+
+template <int BN, int MODE, int RB, int PAIR>
+inline int launch(const Params &p, int grid, cudaStream_t stream) {
+    const uint32_t smem = launch_smem<BN, MODE, RB, PAIR>(p);
     // per device (the attribute belongs to the current context); cheap, and allowed under capture
-    MGC_CHECK_CUDA(cudaFuncSetAttribute(umma_gemm_kernel<BN, MODE, RB>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                        (int)smem));
-    umma_gemm_kernel<BN, MODE, RB><<<grid, THREADS, smem, stream>>>(p);
-    return check_launch("umma_gemm_kernel");
+    MGC_CHECK_CUDA(cudaFuncSetAttribute(umma_gemm_kernel<BN, MODE, RB, PAIR>,
+                                        cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+    if (!PAIR) {
+        umma_gemm_kernel<BN, MODE, RB, PAIR><<<grid, THREADS, smem, stream>>>(p);
+        return check_launch("umma_gemm_kernel");
+    }
+    cudaLaunchConfig_t cfg = {};
+    cudaLaunchAttribute attr[1] = {};
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = 2;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    cfg.gridDim = dim3((unsigned)grid);
+    cfg.blockDim = dim3(THREADS);
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = stream;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    MGC_CHECK_CUDA(cudaLaunchKernelEx(&cfg, umma_gemm_kernel<BN, MODE, RB, PAIR>, p));
+    return check_launch("umma_gemm_kernel (pair)");
 }
 
 // The B-resident variant when this CTA's B panel fits beside its stages and every CTA walks at
@@ -1029,11 +1238,64 @@ inline int launch_best(Params &p, long long m_tiles, cudaStream_t stream) {
     const int per = p.n_tiles <= sms ? sms / p.n_tiles : 0;
     if (per > 0 && panel <= Cfg<BN, MODE, 1>::B_RES_MAX && m_tiles >= 2LL * per) {
         p.b_res_bytes = panel;
-        return launch<BN, MODE, 1>(p, per * p.n_tiles, stream);
+        return launch<BN, MODE, 1, 0>(p, per * p.n_tiles, stream);
     }
     p.b_res_bytes = 0;
     const long long tiles = (long long)p.n_tiles * m_tiles;
-    return launch<BN, MODE, 0>(p, (int)(tiles < sms ? tiles : sms), stream);
+    return launch<BN, MODE, 0, 0>(p, (int)(tiles < sms ? tiles : sms), stream);
+}
+
+// Clusters of two that fit on the device at once (one CTA per SM), per kernel variant; 0 if
+// the query fails. Cached per device.
+template <int BN, int RB>
+inline int pair_clusters() {
+    static int cached[64];
+    static bool known[64];
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) {
+        cudaGetLastError();
+        return 0;
+    }
+    if (known[dev]) return cached[dev];
+    Params dummy;
+    memset(&dummy, 0, sizeof dummy);
+    const uint32_t smem = launch_smem<BN, TF32, RB, 1>(dummy);
+    int n = 0;
+    if (cudaFuncSetAttribute(umma_gemm_kernel<BN, TF32, RB, 1>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             (int)SMEM_LIMIT) == cudaSuccess) {
+        cudaLaunchConfig_t cfg = {};
+        cudaLaunchAttribute attr[1] = {};
+        attr[0].id = cudaLaunchAttributeClusterDimension;
+        attr[0].val.clusterDim.x = 2;
+        attr[0].val.clusterDim.y = 1;
+        attr[0].val.clusterDim.z = 1;
+        cfg.gridDim = dim3(2);
+        cfg.blockDim = dim3(THREADS);
+        cfg.dynamicSmemBytes = smem;
+        cfg.attrs = attr;
+        cfg.numAttrs = 1;
+        if (cudaOccupancyMaxActiveClusters(&n, umma_gemm_kernel<BN, TF32, RB, 1>, &cfg) != cudaSuccess) n = 0;
+    }
+    cudaGetLastError();
+    cached[dev] = n;
+    known[dev] = true;
+    return n;
+}
+
+// CTA-pair launch (TF32 mode, tiled or 32-channel im2col A): p.m_tiles counts 256-row tiles and
+// p.tmB boxes one plane. B-resident when this CTA's plane of the panel fits.
+template <int BN>
+inline int launch_pair(Params &p, int clusters, cudaStream_t stream) {
+    using C1 = Cfg<BN, TF32, 1, 1>;
+    const uint32_t panel = (uint32_t)p.num_kb * C1::B_TILE_BYTES;
+    const int per = p.n_tiles <= clusters ? clusters / p.n_tiles : 0;
+    if (per > 0 && panel <= C1::B_RES_MAX && p.m_tiles >= 2LL * per) {
+        p.b_res_bytes = panel;
+        return launch<BN, TF32, 1, 1>(p, 2 * per * p.n_tiles, stream);
+    }
+    p.b_res_bytes = 0;
+    const long long tiles = (long long)p.n_tiles * p.m_tiles;
+    return launch<BN, TF32, 0, 1>(p, 2 * (int)(tiles < clusters ? tiles : clusters), stream);
 }
 
 }  // namespace umma
@@ -1151,6 +1413,30 @@ inline int try_gemm_umma(const GemmParams &p, cudaStream_t stream, int *taken) {
         }
     }
     u.m_tiles = (int)m_tiles;
+    // CTA pairs (256-row tiles, B planes split between the two CTAs: a third less shared-memory
+    // fill per K block) for long-K GEMMs with N tiles of 128 and enough pair tiles to occupy
+    // every pair of SMs. Measured on ResNet-50 (batch 256): 8-15 % faster from K = 256 up
+    // (without a residual; from K = 512 with one), slower below, no gain for N tiles of 64.
+    // MGC_CUDA_PAIR=0 never uses them, =1 whenever the form allows (any size: tests).
+    static const int pair_env = [] {
+        const char *e = getenv("MGC_CUDA_PAIR");
+        return e && e[0] == '0' ? 0 : e && e[0] == '1' ? 1 : 2;
+    }();
+    if (!strict && pair_env != 0 && (u.im2col == 0 || u.im2col == 1)) {
+        const long long pair_m = ceil_div(p.M, 2 * umma::BM);
+        const bool worth = bn == 128 && u.num_kb >= (p.res ? 16 : 8);
+        const int clusters = bn == 64 ? umma::pair_clusters<64, 0>() : umma::pair_clusters<128, 0>();
+        CUtensorMap plane_map;
+        if (clusters > 0 && (pair_env == 1 || (worth && pair_m * u.n_tiles >= clusters)) &&
+            umma::make_map_b(&plane_map, p.b_umma, p.b_umma_lo, p.N, kp, bn, 1)) {
+            u.tmB = plane_map;
+            u.m_tiles = (int)pair_m;
+            const int st = bn == 64 ? umma::launch_pair<64>(u, clusters, stream) : umma::launch_pair<128>(u, clusters, stream);
+            if (st != MGC_CUDA_OK) return st;
+            *taken = 1;
+            return MGC_CUDA_OK;
+        }
+    }
     // persistent grid: one CTA per SM (the shared-memory footprint allows no more)
     int st;
     if (strict) st = umma::launch_best<64, umma::STRICT>(u, m_tiles, stream);
