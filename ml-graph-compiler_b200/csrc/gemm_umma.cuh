@@ -445,6 +445,28 @@ __device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t (&r)[32]) {
         : "r"(taddr));
 }
 
+// Position in a ring of N slots (shared-memory stages, TMEM buffers): the slot, the parity of
+// the current lap, and whether the ring has wrapped (a slot's previous use must then be waited
+// out). Advanced incrementally: no 64-bit division in the issue loops.
+template <int N>
+struct RingPos {
+    int slot = 0;
+    uint32_t phase = 0;
+    bool wrapped = false;
+    __device__ __forceinline__ void advance() {
+        if (++slot == N) {
+            slot = 0;
+            phase ^= 1u;
+            wrapped = true;
+        }
+    }
+    __device__ __forceinline__ RingPos next() const {
+        RingPos r = *this;
+        r.advance();
+        return r;
+    }
+};
+
 constexpr uint32_t SMEM_LIMIT = 232448;  // dynamic shared memory per block on sm_100 (227 KB)
 
 // RB: B-resident variant. The CTA keeps one N tile for its whole life and loads that tile's B
@@ -465,8 +487,7 @@ struct Cfg {
     static constexpr uint32_t BAR_BYTES = 512;                     // mbarriers and the TMEM address
     // everything else: output staging, alignment slack, barriers, the tile's bias
     static constexpr uint32_t STAGE_BUDGET = SMEM_LIMIT - OUT_BYTES - 1024 - BAR_BYTES - BN * 4;
-    // (pairs: 4 stages measured faster than 5 on the ResNet-50 3x3 layers)
-    static constexpr int MAX_STAGES = PAIR ? 4 : 8;
+    static constexpr int MAX_STAGES = 8;
     static constexpr int STAGES = RB ? (MODE == STRICT ? 2 : 4)
                                   : (STAGE_BUDGET / STAGE_BYTES) < 2 ? 2
                                   : (int)(STAGE_BUDGET / STAGE_BYTES) > MAX_STAGES ? MAX_STAGES
@@ -575,6 +596,7 @@ __global__ void __launch_bounds__(THREADS, 1) umma_gemm_kernel(const __grid_cons
         // before the loads.
         const uint32_t bytes = p.a_bytes + (RB ? 0 : 2 * C::B_TILE_BYTES);
         long long g = 0;  // K blocks issued so far
+        RingPos<S> pos;   // stage of K block g
         bool ok = true;
         int mt, nt;
         if (RB && tile_at(0, mt, nt)) {  // this CTA's B panel, once: lane j loads K blocks j, j+32, ...
@@ -589,12 +611,21 @@ __global__ void __launch_bounds__(THREADS, 1) umma_gemm_kernel(const __grid_cons
             const int rem0 = m0 - nb * hw;
             const int oh0 = rem0 / p.OW, ow0 = rem0 - oh0 * p.OW;
             const int wb = ow0 * p.SW - p.PL, hb = oh0 * p.SH - p.PT;
-            for (int kb = 0; kb < num_kb; ++kb, ++g) {
-                const int s = (int)(g % S);
-                const long long round = g / S;
+            // row tiles: the tile's image and first output row; window rows / row tiles: the K
+            // block's filter row kh and first column x0, advanced per block (no division)
+            const int rimg = p.im2col == 4 ? mt / p.rt_per_img : 0;
+            const int roh0 = p.im2col == 4 ? (mt - rimg * p.rt_per_img) * p.rt_rows : 0;
+            int kh_w = 0, cb_w = 0;
+            for (int kb = 0; kb < num_kb; ++kb, ++g, pos.advance()) {
+                const int s = pos.slot;
+                const int kh = kh_w, x0 = cb_w * BK;
+                if (++cb_w == p.cblocks) {
+                    cb_w = 0;
+                    ++kh_w;
+                }
                 int waited = 1;
                 if (lane == 0) {
-                    if (round > 0 && !mbar_wait(&empty[s], (uint32_t)((round - 1) & 1))) waited = 0;
+                    if (pos.wrapped && !mbar_wait(&empty[s], pos.phase ^ 1u)) waited = 0;
                     else mbar_expect_tx(&full[s], bytes);
                 }
                 if (!__shfl_sync(0xffffffffu, waited, 0)) {
@@ -605,15 +636,10 @@ __global__ void __launch_bounds__(THREADS, 1) umma_gemm_kernel(const __grid_cons
                 if (p.im2col == 4) {
                     // row tiles: one box of rt_rows whole output rows (OW pixels each) of one
                     // image; the tile's remaining smem rows are never loaded and never stored
-                    if (lane == 0) {
-                        const int kh = kb / p.cblocks, x0 = (kb - kh * p.cblocks) * BK;
-                        const int img = mt / p.rt_per_img, oh0 = (mt - img * p.rt_per_img) * p.rt_rows;
-                        tma_load_5d(a_tile(s), &p.tmA, &full[s], x0, 0, oh0, img, kh);
-                    }
+                    if (lane == 0) tma_load_5d(a_tile(s), &p.tmA, &full[s], x0, 0, roh0, rimg, kh);
                 } else if (p.im2col == 3) {
                     // window rows: the K block is 32 consecutive floats of the padded image row
                     // (kh) starting at the window origin, for wrows output pixels per box
-                    const int kh = kb / p.cblocks, x0 = (kb - kh * p.cblocks) * BK;
                     for (int r0 = lane * p.wrows; r0 < BM; r0 += 32 * p.wrows) {
                         const int m = m0 + r0;
                         const int img = m / hw, rem = m - img * hw;
@@ -649,6 +675,7 @@ __global__ void __launch_bounds__(THREADS, 1) umma_gemm_kernel(const __grid_cons
                                             : A_TILE_BYTES + (RB ? 0 : 2 * C::B_TILE_BYTES);
             const bool arms = !PAIR || rank == 0;  // this thread arms the stage barriers
             long long g = 0;  // K blocks issued so far
+            RingPos<S> pos;   // stage of K block g
             bool ok = true;
             bool free_next = false;  // the slot of K block g was tested free
             int mt, nt;
@@ -671,29 +698,37 @@ __global__ void __launch_bounds__(THREADS, 1) umma_gemm_kernel(const __grid_cons
                     wb = ow * p.SW - p.PL;
                     hb = oh * p.SH - p.PT;
                 }
-                for (int kb = 0; kb < num_kb; ++kb, ++g) {
-                    const int s = (int)(g % S);
-                    const long long round = g / S;
-                    if (round > 0 && !free_next && !mbar_wait(&empty[s], (uint32_t)((round - 1) & 1))) {
+                // im2col: K block kb -> (filter row kh, column kw, channel block cb), advanced
+                // per block; the tap offsets are kept as the box's 16-bit offsets
+                int cb = 0, kw = 0;
+                uint16_t off_w = 0, off_h = 0;
+                for (int kb = 0; kb < num_kb; ++kb, ++g, pos.advance()) {
+                    const int s = pos.slot;
+                    if (pos.wrapped && !free_next && !mbar_wait(&empty[s], pos.phase ^ 1u)) {
                         set_error(p.err, MGC_CUDA_TIMEOUT);
                         ok = false;
                         break;
                     }
                     // test the next K block's slot now; the test's latency overlaps this block's
                     // TMA issue, and a slot found free needs no wait
-                    const long long round1 = (g + 1) / S;
-                    free_next = round1 == 0 || mbar_test_wait(&empty[(int)((g + 1) % S)], (uint32_t)((round1 - 1) & 1));
+                    const RingPos<S> nx = pos.next();
+                    free_next = !nx.wrapped || mbar_test_wait(&empty[nx.slot], nx.phase ^ 1u);
                     if (arms) mbar_expect_tx(&full[s], bytes);
                     if (p.im2col) {
-                        const int cb = kb % p.cblocks;
-                        const int t = kb / p.cblocks;
-                        const int kw = t % p.KW, kh = t / p.KW;
                         if (PAIR)
                             tma_load_im2col_4d_pair(a_tile(s), &p.tmA, leader_addr(&full[s]), cb * BK, wb, hb, nb,
-                                                    (uint16_t)(kw * p.DW), (uint16_t)(kh * p.DH));
+                                                    off_w, off_h);
                         else
-                            tma_load_im2col_4d(a_tile(s), &p.tmA, &full[s], cb * BK, wb, hb, nb, (uint16_t)(kw * p.DW),
-                                               (uint16_t)(kh * p.DH));
+                            tma_load_im2col_4d(a_tile(s), &p.tmA, &full[s], cb * BK, wb, hb, nb, off_w, off_h);
+                        if (++cb == p.cblocks) {
+                            cb = 0;
+                            off_w = (uint16_t)(off_w + p.DW);
+                            if (++kw == p.KW) {
+                                kw = 0;
+                                off_w = 0;
+                                off_h = (uint16_t)(off_h + p.DH);
+                            }
+                        }
                     } else if (PAIR) {
                         tma_load_2d_pair(a_tile(s), &p.tmA, leader_addr(&full[s]), kb * BK, m0);
                     } else {
@@ -715,21 +750,20 @@ __global__ void __launch_bounds__(THREADS, 1) umma_gemm_kernel(const __grid_cons
     } else if (warp == B_WARP) {
         if (lane == 0 && !RB) {
             // ---------------- B producer: one 3-D box (TF32 part and residual) per K block ----------------
-            long long g = 0;
+            RingPos<S> pos;  // stage of the next K block
             bool ok = true;
-            bool free_next = false;  // the slot of K block g was tested free
+            bool free_next = false;  // that stage was tested free
             int mt, nt;
             for (int i = 0; ok && tile_at(i, mt, nt); ++i) {
-                for (int kb = 0; kb < num_kb; ++kb, ++g) {
-                    const int s = (int)(g % S);
-                    const long long round = g / S;
-                    if (round > 0 && !free_next && !mbar_wait(&empty[s], (uint32_t)((round - 1) & 1))) {
+                for (int kb = 0; kb < num_kb; ++kb, pos.advance()) {
+                    const int s = pos.slot;
+                    if (pos.wrapped && !free_next && !mbar_wait(&empty[s], pos.phase ^ 1u)) {
                         set_error(p.err, MGC_CUDA_TIMEOUT);
                         ok = false;
                         break;
                     }
-                    const long long round1 = (g + 1) / S;
-                    free_next = round1 == 0 || mbar_test_wait(&empty[(int)((g + 1) % S)], (uint32_t)((round1 - 1) & 1));
+                    const RingPos<S> nx = pos.next();
+                    free_next = !nx.wrapped || mbar_test_wait(&empty[nx.slot], nx.phase ^ 1u);
                     if (PAIR) tma_load_3d_pair(b_tile(s, kb), &p.tmB, leader_addr(&full[s]), kb * BK, nt * BN, (int)rank);
                     else tma_load_3d(b_tile(s, kb), &p.tmB, &full[s], kb * BK, nt * BN, 0);
                 }
@@ -740,7 +774,8 @@ __global__ void __launch_bounds__(THREADS, 1) umma_gemm_kernel(const __grid_cons
             // ---------------- MMA issuer (a pair's rank 0 issues for both CTAs) ----------------
             constexpr uint32_t idesc = instr_desc_tf32(BN);
             constexpr uint32_t idesc2 = instr_desc_tf32(2 * BN, C::TM);  // the stacked [B_hi; B_lo] tile
-            long long g = 0;
+            RingPos<S> pos;   // stage of the next K block
+            RingPos<TB> buf;  // TMEM buffer of the next K-block group
             bool ok = true;
             int mt, nt;
             if (RB && tile_at(0, mt, nt) && !mbar_wait(bres_full, 0)) {
@@ -748,7 +783,6 @@ __global__ void __launch_bounds__(THREADS, 1) umma_gemm_kernel(const __grid_cons
                 ok = false;
             }
             constexpr int PG = MODE == STRICT ? 1 : PROMOTE_KB;  // K blocks per TMEM buffer
-            long long gq = 0;                                    // TMEM buffers filled so far
             uint64_t *const ready = MODE == STRICT ? split : full;  // a stage's operands are in place
             // MMA issue blocks while the tensor pipe is busy, so a barrier test between two K
             // blocks would leave the pipe idle for its whole latency (~150 cycles). Instead the
@@ -756,21 +790,21 @@ __global__ void __launch_bounds__(THREADS, 1) umma_gemm_kernel(const __grid_cons
             // a block whose stage tested complete skips its wait.
             bool have = false;
             for (int i = 0; ok && tile_at(i, mt, nt); ++i) {
-                for (int kb = 0; kb < num_kb; ++kb, ++g) {
-                    const int s = (int)(g % S);
-                    const int b = (int)(gq % TB);
+                for (int kb = 0; kb < num_kb; ++kb, pos.advance()) {
+                    const int s = pos.slot;
+                    const int b = buf.slot;
                     const bool first = kb % PG == 0, last = kb % PG == PG - 1 || kb == num_kb - 1;
-                    if (!have && !mbar_wait(&ready[s], (uint32_t)((g / S) & 1))) {
+                    if (!have && !mbar_wait(&ready[s], pos.phase)) {
                         set_error(p.err, MGC_CUDA_TIMEOUT);
                         ok = false;
                         break;
                     }
-                    if (first && gq >= TB) {
+                    if (first && buf.wrapped) {
                         // the epilogue has drained this TMEM buffer; order the MMAs after its loads.
                         // (The stage's operands need no tcgen05 fence: the TMA writes and the MMA
                         // reads are both async-proxy accesses ordered by the stage barrier. A fence
                         // per K block would also cost ~600 cycles: it waits for the MMA pipe.)
-                        if (!mbar_wait(&tempty[b], (uint32_t)(((gq / TB) - 1) & 1))) {
+                        if (!mbar_wait(&tempty[b], buf.phase ^ 1u)) {
                             set_error(p.err, MGC_CUDA_TIMEOUT);
                             ok = false;
                             break;
@@ -780,8 +814,9 @@ __global__ void __launch_bounds__(THREADS, 1) umma_gemm_kernel(const __grid_cons
                     const uint32_t a_addr = smem_addr(a_tile(s)), b_addr = smem_addr(b_tile(s, kb));
                     const uint32_t bl_addr = b_addr + C::B_TILE_BYTES, al_addr = smem_addr(alo_tile(s));
                     const uint32_t dbase = tmem_base + (uint32_t)(b * C::BUF_COLS);
-                    uint64_t *const next_ready = &ready[(int)((g + 1) % S)];
-                    const uint32_t next_parity = (uint32_t)(((g + 1) / S) & 1);
+                    const RingPos<S> nx = pos.next();
+                    uint64_t *const next_ready = &ready[nx.slot];
+                    const uint32_t next_parity = nx.phase;
                     bool peek = false;
 #pragma unroll
                     for (int k = 0; k < BK / 8; ++k) {  // 8 tf32 = 32 bytes per MMA
@@ -816,7 +851,7 @@ __global__ void __launch_bounds__(THREADS, 1) umma_gemm_kernel(const __grid_cons
                         // TMEM buffer b holds this group's products
                         if (PAIR) mma_commit_pair(&tfull[b]);
                         else mma_commit(&tfull[b]);
-                        ++gq;
+                        buf.advance();
                     }
                 }
             }
@@ -832,16 +867,16 @@ __global__ void __launch_bounds__(THREADS, 1) umma_gemm_kernel(const __grid_cons
         const int hc = ((warp - 2) >> 2) * HALF;  // first column of this warp's half
         const int row = q * 32 + lane;      // this thread's tile row (its TMEM lane)
         const uint32_t lane_base = tmem_base + ((uint32_t)(q * 32) << 16) + (uint32_t)hc;
-        long long g = 0;       // TMEM buffers drained
-        long long gs = 0;      // K blocks split (strict)
+        RingPos<TB> dpos;      // TMEM buffer to drain next
+        RingPos<S> spos;       // stage to split next (strict)
         bool ok = true;
         // strict mode accumulates K blocks in fp64 (each block's four step regions summed in fp32
         // first); TF32 mode accumulates in fp32
         using AccT = typename std::conditional<MODE == STRICT, double, float>::type;
         AccT acc[HALF];
         auto drain = [&]() -> bool {
-            const int b = (int)(g % TB);
-            if (!mbar_wait(&tfull[b], (uint32_t)((g / TB) & 1))) return false;
+            const int b = dpos.slot;
+            if (!mbar_wait(&tfull[b], dpos.phase)) return false;
             tc_fence_after();
             if (MODE == STRICT) {
 #pragma unroll
@@ -878,12 +913,12 @@ __global__ void __launch_bounds__(THREADS, 1) umma_gemm_kernel(const __grid_cons
             } else {
                 mbar_arrive(&tempty[b]);
             }
-            ++g;
+            dpos.advance();
             return true;
         };
         auto split_one = [&]() -> bool {
-            const int s = (int)(gs % S);
-            if (!mbar_wait(&full[s], (uint32_t)((gs / S) & 1))) return false;
+            const int s = spos.slot;
+            if (!mbar_wait(&full[s], spos.phase)) return false;
             float4 *a4 = reinterpret_cast<float4 *>(a_tile(s));
             float4 *l4 = reinterpret_cast<float4 *>(alo_tile(s));
 #pragma unroll
@@ -898,7 +933,7 @@ __global__ void __launch_bounds__(THREADS, 1) umma_gemm_kernel(const __grid_cons
             }
             fence_proxy_async_smem();
             mbar_arrive(&split[s]);
-            ++gs;
+            spos.advance();
             return true;
         };
         // byte offset of columns c0..c0+3 of row r in the staging tile: BN / 32 slabs of 128 rows
