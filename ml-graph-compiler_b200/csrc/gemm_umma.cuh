@@ -20,11 +20,10 @@
 //   to fp32), so the only operand error is the unbiased rounding of the activations.
 // * MGC_PREC_3XTF32 ("strict"): the epilogue warps split the raw A tile into hi = RN_tf32(A) and
 //   lo = A - hi in shared memory; each K step issues A_lo*B_hi + A_hi*B_lo + A_hi*B_hi.
-// * Accumulator promotion: every group of PROMOTE_KB K blocks (TF32 mode) writes its products
-//   into a fresh TMEM region (double or quadruple buffered); the epilogue warps add each region
-//   into fp32 registers with round-to-nearest while the tensor core works on the next group. In
-//   strict mode each of the four K=8 steps of a block gets its own region, so no tensor-core
-//   accumulation chain is longer than one step.
+// * Accumulation: TF32 mode keeps a tile's whole K in one TMEM accumulator (double buffered
+//   across tiles). Strict mode gives each of the four K=8 steps of a block its own region, which
+//   the epilogue warps add into fp64 registers, so no tensor-core accumulation chain is longer
+//   than one step.
 //
 // Roles: warp 0 issues TMA (lane 0, or the whole warp for the narrow-channel forms); warp 1
 // allocates TMEM and lane 0 issues tcgen05.mma; warps 2-9 (256 threads: two per TMEM lane, each
@@ -54,14 +53,11 @@ constexpr int BK = 32;                       // fp32 elements per K block: one 1
 constexpr uint32_t A_TILE_BYTES = BM * BK * 4;
 constexpr long long WAIT_LIMIT_CYCLES = 1ll << 31;  // ~1.1 s at 1.9 GHz
 
-// TF32 mode: K blocks whose products share one TMEM accumulator before the epilogue promotes it
-// to registers (a tensor-core accumulation chain of 4 * PROMOTE_KB MMA steps). The epilogue's
-// drain then runs every PROMOTE_KB blocks, so the MMA warp rarely waits for a free buffer.
-// Measured on ResNet-50 (batch 4 against the float64 oracle): promotion every 1, 2, 4 or 8
-// blocks gives the same logit error (max 1.7e-2, mean |err| 3.6-3.7e-3, mean signed err within
-// +-5e-5): the operand rounding of the activations dominates, the accumulator's rounding toward
-// zero over 32 steps does not show. The step time drops 5.5 % from 2 to 8.
-constexpr int PROMOTE_KB = 8;
+// TF32 mode accumulates a tile's whole K in TMEM. Measured on ResNet-50 (batch 4 against the
+// float64 oracle): promoting the accumulator to fp32 registers every 1, 2, 4 or 8 K blocks, or
+// never, gives the same logit error (max 1.6-1.8e-2, mean |err| 3.6-3.7e-3, mean signed error
+// within +-8e-5): the rounding of the activations to TF32 dominates, the accumulator's rounding
+// toward zero over a long chain does not show.
 
 enum Mode { TF32 = 0, STRICT = 1 };
 
@@ -472,18 +468,26 @@ constexpr uint32_t SMEM_LIMIT = 232448;  // dynamic shared memory per block on s
 // RB: B-resident variant. The CTA keeps one N tile for its whole life and loads that tile's B
 // panel (every K block, hi and lo) into shared memory once; the stages then carry A only.
 // PAIR: CTA-pair variant (TF32 mode): 256-row tiles, each CTA holding one plane of B.
+// WIDE (a pair with BN = 256): 256 x 256 tiles; each CTA holds both planes of its 128 B rows and
+// the hi and lo products go to one accumulator through two N = 256 MMAs per K step.
 template <int BN, int MODE, int RB = 0, int PAIR = 0>
 struct Cfg {
     static_assert(!PAIR || MODE == TF32, "CTA pairs run TF32 mode only");
+    static constexpr bool WIDE = PAIR && BN == 256;
+    static_assert(BN <= 128 || (WIDE && RB == 0), "N tiles of 256 are pair-only, without B residency");
     static constexpr int REGIONS = MODE == STRICT ? 4 : 1;  // TMEM regions per K block
-    static constexpr uint32_t B_TILE_BYTES = BN * BK * 4;
-    static constexpr int B_PLANES = PAIR ? 1 : 2;            // B planes in this CTA's shared memory
+    static constexpr int BROWS = WIDE ? BN / 2 : BN;         // B rows of one plane in this CTA
+    static constexpr uint32_t B_TILE_BYTES = BROWS * BK * 4;
+    static constexpr int B_PLANES = PAIR && !WIDE ? 1 : 2;   // B planes in this CTA's shared memory
     static constexpr int TM = PAIR ? 2 * BM : BM;            // rows of one tile
+    static constexpr int EN = WIDE ? 64 : BN;                // columns of one epilogue pass
+    static constexpr int NH = BN / EN;                       // epilogue passes per tile
     // stage: A (| A_lo) (| B_hi | B_lo), or A | this rank's B plane
     static constexpr uint32_t STAGE_BYTES =
         A_TILE_BYTES + (MODE == STRICT ? A_TILE_BYTES : 0) + (RB ? 0 : B_PLANES * B_TILE_BYTES);
-    // output tile staging: BN/32 slabs of [128 rows][32 fp32] in the 128B-swizzled TMA layout
-    static constexpr uint32_t OUT_BYTES = BM * BN * 4;
+    // output staging of one epilogue pass: EN/32 slabs of [128 rows][32 fp32] in the
+    // 128B-swizzled TMA layout
+    static constexpr uint32_t OUT_BYTES = BM * EN * 4;
     static constexpr uint32_t BAR_BYTES = 512;                     // mbarriers and the TMEM address
     // everything else: output staging, alignment slack, barriers, the tile's bias
     static constexpr uint32_t STAGE_BUDGET = SMEM_LIMIT - OUT_BYTES - 1024 - BAR_BYTES - BN * 4;
@@ -492,9 +496,10 @@ struct Cfg {
                                   : (STAGE_BUDGET / STAGE_BYTES) < 2 ? 2
                                   : (int)(STAGE_BUDGET / STAGE_BYTES) > MAX_STAGES ? MAX_STAGES
                                   : (STAGE_BUDGET / STAGE_BYTES);
-    // TMEM columns of one K block: strict, four step regions of BN; TF32, the products with B_hi
-    // (columns [0, BN)) and with B_lo ([BN, 2 BN)) from one N = 2 BN MMA per K step
-    static constexpr uint32_t BUF_COLS = MODE == STRICT ? REGIONS * BN : 2 * BN;
+    // TMEM columns of one buffer: strict, four step regions of BN; TF32, the products with B_hi
+    // (columns [0, BN)) and with B_lo ([BN, 2 BN)) from one N = 2 BN MMA per K step; wide, one
+    // accumulator of BN columns
+    static constexpr uint32_t BUF_COLS = MODE == STRICT ? REGIONS * BN : WIDE ? BN : 2 * BN;
     static constexpr int TBUFS = (512 / BUF_COLS) > 4 ? 4 : (512 / BUF_COLS);  // TMEM buffers in the ring
     static constexpr uint32_t TMEM_COLS = TBUFS * BUF_COLS;
     // fixed part; a B-resident launch adds its B panel (b_res_bytes) in front of the stages
@@ -671,8 +676,7 @@ __global__ void __launch_bounds__(THREADS, 1) umma_gemm_kernel(const __grid_cons
         if (lane == 0) {
             // ---------------- TMA producer: one A box per K block (lane 0) ----------------
             // a pair's stage barrier (rank 0's) counts the bytes of both CTAs
-            constexpr uint32_t bytes = PAIR ? 2 * (A_TILE_BYTES + (RB ? 0 : C::B_TILE_BYTES))
-                                            : A_TILE_BYTES + (RB ? 0 : 2 * C::B_TILE_BYTES);
+            constexpr uint32_t bytes = (PAIR ? 2 : 1) * (A_TILE_BYTES + (RB ? 0 : C::B_PLANES * C::B_TILE_BYTES));
             const bool arms = !PAIR || rank == 0;  // this thread arms the stage barriers
             long long g = 0;  // K blocks issued so far
             RingPos<S> pos;   // stage of K block g
@@ -764,8 +768,14 @@ __global__ void __launch_bounds__(THREADS, 1) umma_gemm_kernel(const __grid_cons
                     }
                     const RingPos<S> nx = pos.next();
                     free_next = !nx.wrapped || mbar_test_wait(&empty[nx.slot], nx.phase ^ 1u);
-                    if (PAIR) tma_load_3d_pair(b_tile(s, kb), &p.tmB, leader_addr(&full[s]), kb * BK, nt * BN, (int)rank);
-                    else tma_load_3d(b_tile(s, kb), &p.tmB, &full[s], kb * BK, nt * BN, 0);
+                    // a pair: this rank's plane, or (wide) both planes of this rank's 128 rows
+                    if (C::WIDE)
+                        tma_load_3d_pair(b_tile(s, kb), &p.tmB, leader_addr(&full[s]), kb * BK,
+                                         nt * BN + (int)rank * C::BROWS, 0);
+                    else if (PAIR)
+                        tma_load_3d_pair(b_tile(s, kb), &p.tmB, leader_addr(&full[s]), kb * BK, nt * BN, (int)rank);
+                    else
+                        tma_load_3d(b_tile(s, kb), &p.tmB, &full[s], kb * BK, nt * BN, 0);
                 }
             }
         }
@@ -773,7 +783,8 @@ __global__ void __launch_bounds__(THREADS, 1) umma_gemm_kernel(const __grid_cons
         if (lane == 0 && rank == 0) {
             // ---------------- MMA issuer (a pair's rank 0 issues for both CTAs) ----------------
             constexpr uint32_t idesc = instr_desc_tf32(BN);
-            constexpr uint32_t idesc2 = instr_desc_tf32(2 * BN, C::TM);  // the stacked [B_hi; B_lo] tile
+            // the stacked [B_hi; B_lo] tile, or (wide) one plane of all BN columns
+            constexpr uint32_t idesc2 = instr_desc_tf32(C::WIDE ? BN : 2 * BN, C::TM);
             RingPos<S> pos;   // stage of the next K block
             RingPos<TB> buf;  // TMEM buffer of the next K-block group
             bool ok = true;
@@ -782,7 +793,6 @@ __global__ void __launch_bounds__(THREADS, 1) umma_gemm_kernel(const __grid_cons
                 set_error(p.err, MGC_CUDA_TIMEOUT);
                 ok = false;
             }
-            constexpr int PG = MODE == STRICT ? 1 : PROMOTE_KB;  // K blocks per TMEM buffer
             uint64_t *const ready = MODE == STRICT ? split : full;  // a stage's operands are in place
             // MMA issue blocks while the tensor pipe is busy, so a barrier test between two K
             // blocks would leave the pipe idle for its whole latency (~150 cycles). Instead the
@@ -793,7 +803,8 @@ __global__ void __launch_bounds__(THREADS, 1) umma_gemm_kernel(const __grid_cons
                 for (int kb = 0; kb < num_kb; ++kb, pos.advance()) {
                     const int s = pos.slot;
                     const int b = buf.slot;
-                    const bool first = kb % PG == 0, last = kb % PG == PG - 1 || kb == num_kb - 1;
+                    // a TMEM buffer per K block (strict) or per tile (TF32)
+                    const bool first = MODE == STRICT || kb == 0, last = MODE == STRICT || kb == num_kb - 1;
                     if (!have && !mbar_wait(&ready[s], pos.phase)) {
                         set_error(p.err, MGC_CUDA_TIMEOUT);
                         ok = false;
@@ -837,9 +848,15 @@ __global__ void __launch_bounds__(THREADS, 1) umma_gemm_kernel(const __grid_cons
                             // 128B-swizzled row layout, so one descriptor spans both as 2 BN rows:
                             // one MMA, A read once per K step
                             // (a pair: the same descriptor names B_hi in rank 0, B_lo in rank 1)
-                            (void)bld;
-                            if (PAIR) mma_tf32_pair(dbase, ad, bd, idesc2, (!first || k > 0) ? 1u : 0u);
-                            else mma_tf32(dbase, ad, bd, idesc2, (!first || k > 0) ? 1u : 0u);
+                            // (wide: B_hi's and B_lo's products into one accumulator)
+                            if (C::WIDE) {
+                                mma_tf32_pair(dbase, ad, bd, idesc2, (!first || k > 0) ? 1u : 0u);
+                                mma_tf32_pair(dbase, ad, bld, idesc2, 1u);
+                            } else if (PAIR) {
+                                mma_tf32_pair(dbase, ad, bd, idesc2, (!first || k > 0) ? 1u : 0u);
+                            } else {
+                                mma_tf32(dbase, ad, bd, idesc2, (!first || k > 0) ? 1u : 0u);
+                            }
                         }
                         if (k == 0) peek = mbar_test_wait(next_ready, next_parity);
                     }
@@ -861,7 +878,10 @@ __global__ void __launch_bounds__(THREADS, 1) umma_gemm_kernel(const __grid_cons
         }
     } else {
         // ---------------- epilogue warps (2..9): A split (strict), TMEM drain, epilogue ----------------
-        constexpr int HALF = BN / 2;        // columns per epilogue thread
+        // A tile's epilogue runs in NH passes of EN columns (one pass unless wide); each pass
+        // stages, stores and (with a residual) prefetches EN columns.
+        constexpr int EN = C::EN, NH = C::NH;
+        constexpr int HALF = EN / 2;        // columns per epilogue thread and pass
         const int et = threadIdx.x - 64;    // 0..255
         const int q = warp & 3;             // TMEM lane quadrant this warp may access
         const int hc = ((warp - 2) >> 2) * HALF;  // first column of this warp's half
@@ -874,11 +894,46 @@ __global__ void __launch_bounds__(THREADS, 1) umma_gemm_kernel(const __grid_cons
         // first); TF32 mode accumulates in fp32
         using AccT = typename std::conditional<MODE == STRICT, double, float>::type;
         AccT acc[HALF];
+        // hand TMEM buffer b back to the MMA warp (a pair: one arrival per warp, on rank 0's barrier)
+        auto release = [&](int b) {
+            tc_fence_before();
+            if (PAIR) {
+                __syncwarp();
+                if (lane == 0) mbar_arrive_remote(leader_addr(&tempty[b]));
+            } else {
+                mbar_arrive(&tempty[b]);
+            }
+            dpos.advance();
+        };
+        // TF32: this thread's HALF accumulator columns of pass h of the tile in TMEM buffer
+        // dpos (B_hi's and B_lo's products summed, or, wide, the one accumulator); the first
+        // pass waits for the buffer, the last hands it back
+        auto load_pass = [&](int h) -> bool {
+            const int b = dpos.slot;
+            if (h == 0) {
+                if (!mbar_wait(&tfull[b], dpos.phase)) return false;
+                tc_fence_after();
+            }
+#pragma unroll
+            for (int c0 = 0; c0 < HALF; c0 += 32) {
+                uint32_t vh[32], vl[32];
+                const uint32_t addr = lane_base + (uint32_t)(b * C::BUF_COLS + h * EN + c0);
+                tmem_ld32(addr, vh);
+                if (!C::WIDE) tmem_ld32(addr + BN, vl);
+                tmem_wait_ld();
+#pragma unroll
+                for (int j = 0; j < 32; ++j)
+                    acc[c0 + j] = C::WIDE ? __uint_as_float(vh[j]) : __uint_as_float(vh[j]) + __uint_as_float(vl[j]);
+            }
+            if (h == NH - 1) release(b);
+            return true;
+        };
+        // strict: add K block's four step regions into the fp64 accumulators
         auto drain = [&]() -> bool {
             const int b = dpos.slot;
             if (!mbar_wait(&tfull[b], dpos.phase)) return false;
             tc_fence_after();
-            if (MODE == STRICT) {
+            {
 #pragma unroll
                 for (int c0 = 0; c0 < HALF; c0 += 32) {
                     float blk[32];
@@ -893,27 +948,8 @@ __global__ void __launch_bounds__(THREADS, 1) umma_gemm_kernel(const __grid_cons
 #pragma unroll
                     for (int j = 0; j < 32; ++j) acc[c0 + j] += (double)blk[j];
                 }
-            } else {
-                // acc += (A B_hi + A B_lo) for 32 columns at a time: both halves loaded, one wait
-#pragma unroll
-                for (int c0 = 0; c0 < HALF; c0 += 32) {
-                    uint32_t vh[32], vl[32];
-                    const uint32_t addr = lane_base + (uint32_t)(b * C::BUF_COLS + c0);
-                    tmem_ld32(addr, vh);
-                    tmem_ld32(addr + BN, vl);
-                    tmem_wait_ld();
-#pragma unroll
-                    for (int j = 0; j < 32; ++j) acc[c0 + j] += __uint_as_float(vh[j]) + __uint_as_float(vl[j]);
-                }
             }
-            tc_fence_before();
-            if (PAIR) {  // one arrival per warp, on rank 0's barrier
-                __syncwarp();
-                if (lane == 0) mbar_arrive_remote(leader_addr(&tempty[b]));
-            } else {
-                mbar_arrive(&tempty[b]);
-            }
-            dpos.advance();
+            release(b);
             return true;
         };
         auto split_one = [&]() -> bool {
@@ -936,7 +972,7 @@ __global__ void __launch_bounds__(THREADS, 1) umma_gemm_kernel(const __grid_cons
             spos.advance();
             return true;
         };
-        // byte offset of columns c0..c0+3 of row r in the staging tile: BN / 32 slabs of 128 rows
+        // byte offset of columns c0..c0+3 of row r in the staging tile: EN / 32 slabs of 128 rows
         // x 128 bytes, 16-byte chunks XOR-swizzled by the row (the TMA 128-byte swizzle)
         auto stage_offset = [](int r, int c0) -> uint32_t {
             const int sl = c0 >> 5, j = (c0 & 31) >> 2;
@@ -957,42 +993,46 @@ __global__ void __launch_bounds__(THREADS, 1) umma_gemm_kernel(const __grid_cons
         if (issuer && p.tma_out) prefetch_tmap(&p.tmC);
         if (issuer && p.tma_res) prefetch_tmap(&p.tmR);
         const bool rows = p.im2col == 4;
-        auto issue_residual = [&](int mt_, int nt_) {
-            const int tn0 = nt_ * BN, tm0 = mt_ * C::TM + row0;
+        // the residual of pass h_ of tile (mt_, nt_) into the staging tile
+        auto issue_residual = [&](int mt_, int nt_, int h_) {
+            const int tn0 = nt_ * BN + h_ * EN, tm0 = mt_ * C::TM + row0;
             if (rows) {
                 const int img = mt_ / p.rt_per_img, oh0 = (mt_ - img * p.rt_per_img) * p.rt_rows;
-                mbar_expect_tx(res_full, (uint32_t)(BN / 32) * p.a_bytes);
+                mbar_expect_tx(res_full, (uint32_t)(EN / 32) * p.a_bytes);
 #pragma unroll 1
-                for (int sl = 0; sl < BN / 32; ++sl)
+                for (int sl = 0; sl < EN / 32; ++sl)
                     tma_load_4d(out_tile + sl * (BM * 128), &p.tmR, res_full, tn0 + sl * 32, 0, oh0, img);
                 return;
             }
             mbar_expect_tx(res_full, C::OUT_BYTES);
 #pragma unroll 1
-            for (int sl = 0; sl < BN / 32; ++sl)
+            for (int sl = 0; sl < EN / 32; ++sl)
                 tma_load_2d(out_tile + sl * (BM * 128), &p.tmR, res_full, tn0 + sl * 32, tm0);
         };
         int mt, nt;
-        if (res_tma && issuer && tile_at(0, mt, nt)) issue_residual(mt, nt);
-        int local = 0;  // tiles this CTA has finished
-        for (int i = 0; ok && tile_at(i, mt, nt); ++i, ++local) {
-            const int n0 = nt * BN, m0 = mt * C::TM + row0;
+        if (res_tma && issuer && tile_at(0, mt, nt)) issue_residual(mt, nt, 0);
+        int local = 0;  // epilogue passes this CTA has finished
+        for (int i = 0; ok && tile_at(i, mt, nt); ++i) {
+          const int m0 = mt * C::TM + row0;
+          if (MODE == STRICT) {
 #pragma unroll
             for (int j = 0; j < HALF; ++j) acc[j] = AccT(0);
             for (int kb = 0; kb < num_kb && ok; ++kb) {
-                if (MODE == STRICT) {
-                    if (!split_one()) ok = false;
-                    else if (kb >= 1 && !drain()) ok = false;  // one block behind the split
-                } else if (kb % PROMOTE_KB == 0 && !drain()) {  // one drain per K-block group
-                    ok = false;
-                }
+                if (!split_one()) ok = false;
+                else if (kb >= 1 && !drain()) ok = false;  // one block behind the split
             }
-            if (MODE == STRICT && ok && num_kb >= 1 && !drain()) ok = false;
-            if (!ok) break;
-            // this tile's bias columns into shared memory, one coalesced load (the previous
-            // tile's readers have all passed its second barrier)
+            if (ok && num_kb >= 1 && !drain()) ok = false;
+          }
+          for (int h = 0; ok && h < NH; ++h, ++local) {
+            const int n0 = nt * BN + h * EN;
+            if (MODE != STRICT && !load_pass(h)) {
+                ok = false;
+                break;
+            }
+            // this pass's bias columns into shared memory, one coalesced load (the previous
+            // pass's readers have all passed its second barrier)
             if (p.bias) {
-                for (int c = et; c < BN; c += EPI_THREADS) bias_s[c] = n0 + c < p.N ? __ldg(p.bias + n0 + c) : 0.0f;
+                for (int c = et; c < EN; c += EPI_THREADS) bias_s[c] = n0 + c < p.N ? __ldg(p.bias + n0 + c) : 0.0f;
             }
             // the staging tile is free (the previous TMA store was read out) and, with a
             // residual, refilled with this tile's residual
@@ -1081,18 +1121,22 @@ __global__ void __launch_bounds__(THREADS, 1) umma_gemm_kernel(const __grid_cons
                     if (rows) {  // the tile's rt_rows output rows; staging rows past them are dropped
                         const int img = mt / p.rt_per_img, oh0 = (mt - img * p.rt_per_img) * p.rt_rows;
 #pragma unroll 1
-                        for (int sl = 0; sl < BN / 32; ++sl)
+                        for (int sl = 0; sl < EN / 32; ++sl)
                             tma_store_4d(&p.tmC, out_tile + sl * (BM * 128), n0 + sl * 32, 0, oh0, img);
-                    } else if (m0 < p.M) {  // (a pair's second half may lie wholly past the last row)
+                    } else if (m0 < p.M && n0 < p.N) {  // (a pair's second half, or a wide tile's last
+                                                         // passes, may lie wholly past the edge)
 #pragma unroll 1
-                        for (int sl = 0; sl < BN / 32; ++sl)
+                        for (int sl = 0; sl < EN / 32; ++sl)
                             tma_store_2d(&p.tmC, out_tile + sl * (BM * 128), n0 + sl * 32, m0);
                     }
                     tma_store_commit_and_wait();
+                    // the next pass's residual: this tile's, or the next tile's first
                     int mt2, nt2;
-                    if (res_tma && tile_at(i + 1, mt2, nt2)) issue_residual(mt2, nt2);
+                    if (res_tma && h + 1 < NH) issue_residual(mt, nt, h + 1);
+                    else if (res_tma && tile_at(i + 1, mt2, nt2)) issue_residual(mt2, nt2, 0);
                 }
             }
+          }
         }
         if (!ok) set_error(p.err, MGC_CUDA_TIMEOUT);
         // a residual prefetch that no tile consumed must land before the CTA exits
@@ -1317,6 +1361,14 @@ inline int pair_clusters() {
     return n;
 }
 
+// Wide CTA-pair launch: 256 x 256 tiles (p.m_tiles and p.n_tiles count them; p.tmB boxes both
+// planes of 128 rows).
+inline int launch_wide(Params &p, int clusters, cudaStream_t stream) {
+    p.b_res_bytes = 0;
+    const long long tiles = (long long)p.n_tiles * p.m_tiles;
+    return launch<256, TF32, 0, 1>(p, 2 * (int)(tiles < clusters ? tiles : clusters), stream);
+}
+
 // CTA-pair launch (TF32 mode, tiled or 32-channel im2col A): p.m_tiles counts 256-row tiles and
 // p.tmB boxes one plane. B-resident when this CTA's plane of the panel fits.
 template <int BN>
@@ -1457,6 +1509,31 @@ inline int try_gemm_umma(const GemmParams &p, cudaStream_t stream, int *taken) {
         const char *e = getenv("MGC_CUDA_PAIR");
         return e && e[0] == '0' ? 0 : e && e[0] == '1' ? 1 : 2;
     }();
+    // Wide pairs (256 x 256 tiles: per K block a CTA loads 16 KB of A and 32 KB of B for 128 x
+    // 256 outputs, a quarter less than the 256 x 128 pair tile) for N >= 256 and long K.
+    // MGC_CUDA_WIDE=0 never uses them, =1 whenever the form allows.
+    static const int wide_env = [] {
+        const char *e = getenv("MGC_CUDA_WIDE");
+        return e && e[0] == '0' ? 0 : e && e[0] == '1' ? 1 : 2;
+    }();
+    // A wide tile does the work of two 256 x 128 pair tiles in about 0.88 of their time
+    // (measured, ResNet-50 3x3 layers), so it is taken when its waves of tiles over the pairs of
+    // SMs cost less than the pair form's.
+    if (!strict && pair_env != 0 && wide_env != 0 && (u.im2col == 0 || u.im2col == 1) && bn == 128 && p.N > 128) {
+        const long long pair_m = ceil_div(p.M, 2 * umma::BM), wide_n = ceil_div(p.N, 256);
+        const bool worth = u.num_kb >= (p.res ? 16 : 8);
+        const int clusters = umma::pair_clusters<256, 0>();
+        const long long waves_w = clusters > 0 ? ceil_div(pair_m * wide_n, clusters) : 0;
+        const long long waves_p = clusters > 0 ? ceil_div(pair_m * u.n_tiles, clusters) : 0;
+        if (clusters > 0 && (wide_env == 1 || (worth && pair_m * wide_n >= clusters && 176 * waves_w < 100 * waves_p))) {
+            u.m_tiles = (int)pair_m;
+            u.n_tiles = (int)wide_n;
+            const int st = umma::launch_wide(u, clusters, stream);
+            if (st != MGC_CUDA_OK) return st;
+            *taken = 1;
+            return MGC_CUDA_OK;
+        }
+    }
     if (!strict && pair_env != 0 && (u.im2col == 0 || u.im2col == 1)) {
         const long long pair_m = ceil_div(p.M, 2 * umma::BM);
         const bool worth = bn == 128 && u.num_kb >= (p.res ? 16 : 8);

@@ -80,3 +80,42 @@ def test_resident_panel_layers_match_oracle(name: str, precision: str, graphs: d
         err = float(np.abs(got[k].astype(np.float64) - w).max())
         assert err <= TOL[precision] * scale, f"{name}:{k} max abs err {err:.3g} (scale {scale:.3g})"
         np.testing.assert_array_equal(got[k], again[k])
+
+
+def _tf32_exact(a: np.ndarray) -> np.ndarray:
+    """Truncate fp32 values to TF32 (10 explicit mantissa bits), so that rounding them to TF32
+    changes nothing."""
+    return (a.view(np.uint32) & np.uint32(0xFFFFE000)).view(np.float32)
+
+
+# (M, K, N) reaching each tensor-core form: one CTA per 128-row tile; a CTA pair per 256-row
+# tile with one B plane in each CTA (N tiles of 128, long K, enough pair tiles to fill the
+# GPU); a wide pair (256 x 256 tiles, N > 128; N = 640 leaves a partial last tile)
+GEMM_FORMS = {"single": (1024, 512, 128), "pair": (20480, 512, 128), "wide": (9728, 512, 640)}
+
+
+@pytest.mark.parametrize("form", sorted(GEMM_FORMS))
+def test_tf32_gemm_keeps_weights_exact(form: str) -> None:
+    """With TF32-exact activations, the only error TF32 mode has left is the fp32 accumulation:
+    the weights enter exactly, as their TF32 part plus the residual, in every kernel form
+    (without the residual the error would be about 3e-4 of the largest output)."""
+    m, k, n = GEMM_FORMS[form]
+    r = np.random.default_rng(3)
+    x = _tf32_exact(r.standard_normal((m, k)).astype(np.float32))
+    w = r.standard_normal((k, n)).astype(np.float32)
+    bias = r.standard_normal(n).astype(np.float32)
+    g = Graph(f"gemm_{form}")
+    xi = g.add_input("x", TensorType("float32", (m, k)))
+    y = g.add_node("Gemm", [xi, g.constant(w), g.constant(bias)]).output
+    g.add_output(y, "y")
+    infer_shapes(g)
+    optimize(g, "O3")
+    schedule(g)
+    model = compile_graph(g, precision="tf32")
+    try:
+        got = model.run({"x": x})["y"].astype(np.float64)
+    finally:
+        model.close()
+    want = x.astype(np.float64) @ w.astype(np.float64) + bias.astype(np.float64)
+    err = float(np.abs(got - want).max() / np.abs(want).max())
+    assert err <= 2e-5, f"{form}: max error {err:.3g} of the largest output"
