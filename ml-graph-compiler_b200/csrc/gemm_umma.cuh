@@ -391,6 +391,69 @@ __device__ __forceinline__ void mma_commit_pair_local(uint64_t *bar) {
                  : "memory");
 }
 
+// A K block's four MMAs (K = 8 each) issued back to back from one asm block, with the test of
+// the next stage's barrier between the first and the second. tcgen05.mma holds the issuing
+// thread until the tensor pipe takes it, so any instruction between two MMAs adds to the
+// block's time; every descriptor is computed before the first. first_acc: whether the first
+// MMA accumulates. Returns the barrier test.
+#define MGC_MMA4_BODY(GROUP, A0, A1, A2, A3, B0, B1, B2, B3, EXTRA)                                       \
+    "{\n\t.reg .pred p, t, q;\n\t"                                                                      \
+    "setp.ne.b32 p, %12, 0;\n\t"                                                                         \
+    "setp.eq.b32 t, %12, %12;\n\t"                                                                       \
+    "tcgen05.mma.cta_group::" GROUP ".kind::tf32 [%1], " A0 ", " B0 ", %11, p;\n\t"                      \
+    "mbarrier.test_wait.parity.shared::cta.b64 q, [%13], %14;\n\t"                                      \
+    EXTRA                                                                                                 \
+    "tcgen05.mma.cta_group::" GROUP ".kind::tf32 [%1], " A1 ", " B1 ", %11, t;\n\t"                      \
+    "tcgen05.mma.cta_group::" GROUP ".kind::tf32 [%1], " A2 ", " B2 ", %11, t;\n\t"                      \
+    "tcgen05.mma.cta_group::" GROUP ".kind::tf32 [%1], " A3 ", " B3 ", %11, t;\n\t"                      \
+    "selp.u32 %0, 1, 0, q;\n\t}\n"
+
+template <int PAIR>
+__device__ __forceinline__ bool mma_block4(uint32_t d, const uint64_t (&ad)[4], const uint64_t (&bd)[4], uint32_t idesc,
+                                           uint32_t first_acc, uint64_t *next_bar, uint32_t next_parity) {
+    uint32_t ready;
+    if (PAIR)
+        asm volatile(MGC_MMA4_BODY("2", "%2", "%3", "%4", "%5", "%6", "%7", "%8", "%9", "")
+                     : "=r"(ready)
+                     : "r"(d), "l"(ad[0]), "l"(ad[1]), "l"(ad[2]), "l"(ad[3]), "l"(bd[0]), "l"(bd[1]), "l"(bd[2]),
+                       "l"(bd[3]), "r"(0), "r"(idesc), "r"(first_acc), "r"(smem_addr(next_bar)), "r"(next_parity)
+                     : "memory");
+    else
+        asm volatile(MGC_MMA4_BODY("1", "%2", "%3", "%4", "%5", "%6", "%7", "%8", "%9", "")
+                     : "=r"(ready)
+                     : "r"(d), "l"(ad[0]), "l"(ad[1]), "l"(ad[2]), "l"(ad[3]), "l"(bd[0]), "l"(bd[1]), "l"(bd[2]),
+                       "l"(bd[3]), "r"(0), "r"(idesc), "r"(first_acc), "r"(smem_addr(next_bar)), "r"(next_parity)
+                     : "memory");
+    return ready != 0;
+}
+
+// Wide pair: per K step the B_hi and the B_lo MMA into one accumulator (eight MMAs).
+__device__ __forceinline__ bool mma_block4_wide(uint32_t d, const uint64_t (&ad)[4], const uint64_t (&bd)[4],
+                                                const uint64_t (&bld)[4], uint32_t idesc, uint32_t first_acc,
+                                                uint64_t *next_bar, uint32_t next_parity) {
+    uint32_t ready;
+    asm volatile(
+        "{\n\t.reg .pred p, t, q;\n\t"
+        "setp.ne.b32 p, %15, 0;\n\t"
+        "setp.eq.b32 t, %15, %15;\n\t"
+        "tcgen05.mma.cta_group::2.kind::tf32 [%1], %2, %6, %14, p;\n\t"
+        "mbarrier.test_wait.parity.shared::cta.b64 q, [%16], %17;\n\t"
+        "tcgen05.mma.cta_group::2.kind::tf32 [%1], %2, %10, %14, t;\n\t"
+        "tcgen05.mma.cta_group::2.kind::tf32 [%1], %3, %7, %14, t;\n\t"
+        "tcgen05.mma.cta_group::2.kind::tf32 [%1], %3, %11, %14, t;\n\t"
+        "tcgen05.mma.cta_group::2.kind::tf32 [%1], %4, %8, %14, t;\n\t"
+        "tcgen05.mma.cta_group::2.kind::tf32 [%1], %4, %12, %14, t;\n\t"
+        "tcgen05.mma.cta_group::2.kind::tf32 [%1], %5, %9, %14, t;\n\t"
+        "tcgen05.mma.cta_group::2.kind::tf32 [%1], %5, %13, %14, t;\n\t"
+        "selp.u32 %0, 1, 0, q;\n\t}\n"
+        : "=r"(ready)
+        : "r"(d), "l"(ad[0]), "l"(ad[1]), "l"(ad[2]), "l"(ad[3]), "l"(bd[0]), "l"(bd[1]), "l"(bd[2]), "l"(bd[3]),
+          "l"(bld[0]), "l"(bld[1]), "l"(bld[2]), "l"(bld[3]), "r"(idesc), "r"(first_acc), "r"(smem_addr(next_bar)),
+          "r"(next_parity)
+        : "memory");
+    return ready != 0;
+}
+
 // 16 consecutive fp32 columns of this thread's TMEM lane.
 __device__ __forceinline__ void tmem_ld16(uint32_t taddr, uint32_t (&r)[16]) {
     asm volatile(
@@ -828,39 +891,39 @@ __global__ void __launch_bounds__(THREADS, 1) umma_gemm_kernel(const __grid_cons
                     const RingPos<S> nx = pos.next();
                     uint64_t *const next_ready = &ready[nx.slot];
                     const uint32_t next_parity = nx.phase;
-                    bool peek = false;
+                    const bool packed = p.im2col == 2;
+                    // the block's descriptors, all before the first MMA: 8 tf32 = 32 bytes per step
+                    uint64_t ad[BK / 8], bd[BK / 8], bld[BK / 8];
 #pragma unroll
-                    for (int k = 0; k < BK / 8; ++k) {  // 8 tf32 = 32 bytes per MMA
-                        const bool packed = p.im2col == 2;
-                        const uint64_t ad = packed ? plain_desc(a_addr + k * 2 * PACKED_BOX_BYTES, PACKED_BOX_BYTES, 128)
-                                                   : sw128_desc(a_addr + k * 32);
-                        const uint64_t bd = sw128_desc(b_addr + k * 32);
-                        const uint64_t bld = sw128_desc(bl_addr + k * 32);
-                        if (MODE == STRICT) {
+                    for (int k = 0; k < BK / 8; ++k) {
+                        ad[k] = packed ? plain_desc(a_addr + k * 2 * PACKED_BOX_BYTES, PACKED_BOX_BYTES, 128)
+                                       : sw128_desc(a_addr + k * 32);
+                        bd[k] = sw128_desc(b_addr + k * 32);
+                        bld[k] = sw128_desc(bl_addr + k * 32);
+                    }
+                    if (MODE == STRICT) {
+                        bool peek = false;
+#pragma unroll
+                        for (int k = 0; k < BK / 8; ++k) {
                             const uint32_t d = dbase + (uint32_t)(k * BN);  // own region per K step
                             const uint64_t ald = packed ? plain_desc(al_addr + k * 2 * PACKED_BOX_BYTES, PACKED_BOX_BYTES, 128)
                                                         : sw128_desc(al_addr + k * 32);
-                            mma_tf32(d, ald, bd, idesc, 0u);    // A_lo * B_hi (fresh region)
-                            mma_tf32(d, ad, bld, idesc, 1u);    // A_hi * B_lo
-                            mma_tf32(d, ad, bd, idesc, 1u);     // A_hi * B_hi
-                        } else {
-                            // B_lo's tile directly follows B_hi's in the stage with the same
-                            // 128B-swizzled row layout, so one descriptor spans both as 2 BN rows:
-                            // one MMA, A read once per K step
-                            // (a pair: the same descriptor names B_hi in rank 0, B_lo in rank 1)
-                            // (wide: B_hi's and B_lo's products into one accumulator)
-                            if (C::WIDE) {
-                                mma_tf32_pair(dbase, ad, bd, idesc2, (!first || k > 0) ? 1u : 0u);
-                                mma_tf32_pair(dbase, ad, bld, idesc2, 1u);
-                            } else if (PAIR) {
-                                mma_tf32_pair(dbase, ad, bd, idesc2, (!first || k > 0) ? 1u : 0u);
-                            } else {
-                                mma_tf32(dbase, ad, bd, idesc2, (!first || k > 0) ? 1u : 0u);
-                            }
+                            mma_tf32(d, ald, bd[k], idesc, 0u);    // A_lo * B_hi (fresh region)
+                            mma_tf32(d, ad[k], bld[k], idesc, 1u);  // A_hi * B_lo
+                            mma_tf32(d, ad[k], bd[k], idesc, 1u);   // A_hi * B_hi
+                            if (k == 0) peek = mbar_test_wait(next_ready, next_parity);
                         }
-                        if (k == 0) peek = mbar_test_wait(next_ready, next_parity);
+                        have = peek;
+                    } else if (C::WIDE) {
+                        // B_hi's and B_lo's products into one accumulator
+                        have = mma_block4_wide(dbase, ad, bd, bld, idesc2, first ? 0u : 1u, next_ready, next_parity);
+                    } else {
+                        // B_lo's tile directly follows B_hi's in the stage with the same
+                        // 128B-swizzled row layout, so one descriptor spans both as 2 BN rows: one
+                        // MMA, A read once per K step (a pair: the same descriptor names B_hi in
+                        // rank 0, B_lo in rank 1)
+                        have = mma_block4<PAIR>(dbase, ad, bd, idesc2, first ? 0u : 1u, next_ready, next_parity);
                     }
-                    have = peek;
                     // shared-memory slot free once these MMAs read it (in both CTAs of a pair)
                     if (PAIR) mma_commit_pair(&empty[s]);
                     else mma_commit(&empty[s]);
