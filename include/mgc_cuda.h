@@ -163,6 +163,28 @@ int mgc_cuda_create(const mgc_cuda_launch *launches, int n_launches, const int64
  * and waits. Returns MGC_CUDA_GATHER_OOB when a Gather index was out of range. */
 int mgc_cuda_run(void *handle, const void *const *inputs_host, void *const *outputs_host);
 
+/* Input-upload overlap for mgc_cuda_run (no counterpart in the reference, whose mgc_run reads
+ * host memory directly). After this call, mgc_cuda_run copies input 0 in `chunks` equal slices of
+ * `images / chunks` images on a copy stream and replays a second CUDA Graph in which the first
+ * `prefix` launch records run once per slice, each slice starting when its copy has landed, so
+ * the copy of slice j+1 overlaps the compute of slice j; the remaining records then run once on
+ * the whole batch. The caller (the lowering) guarantees that the prefix works image by image on
+ * batch-major tensors whose memory is not shared between different layouts. Each descriptor
+ * names one batch-dependent field of a prefix record: `what` 0, reference r[slot] advances by
+ * `per_image` bytes per image of the slice's start; `what` 1, integer i[slot] becomes `per_image`
+ * times the slice's images. mgc_cuda_run_device keeps the one-pass graph. Requires one graph
+ * input; chunks 2..16 dividing `images`, which divides input 0's bytes. */
+typedef struct {
+    int32_t launch;    /* index of the record, below `prefix` */
+    int32_t what;      /* 0 reference offset, 1 integer field */
+    int32_t slot;      /* r[] or i[] index */
+    int32_t reserved;
+    int64_t per_image; /* bytes (what 0) or count (what 1) per image */
+} mgc_cuda_chunk;
+
+int mgc_cuda_set_input_chunks(void *handle, int chunks, int prefix, int64_t images,
+                              const mgc_cuda_chunk *descs, int n_descs);
+
 /* The same replay with the inputs already in the handle's device input buffers and the outputs
  * left in its device output buffers; enqueued on the handle's stream without waiting when
  * `sync` is 0 (for device-timed throughput). */

@@ -37,6 +37,16 @@ struct Model {
     cudaGraph_t graph = nullptr;
     cudaGraphExec_t exec = nullptr;
     int kernel_launches = 0;
+    // input-upload overlap (mgc_cuda_set_input_chunks): a copy stream, one event per slice and
+    // the graph whose prefix runs slice by slice
+    int chunks = 0, prefix = 0;
+    int64_t images = 0;
+    std::vector<mgc_cuda_chunk> chunk_descs;
+    cudaStream_t copy_stream = nullptr;
+    std::vector<cudaEvent_t> slice_ready;
+    cudaEvent_t stream_done = nullptr;  // the copy stream starts after the stream's earlier work
+    cudaGraph_t graph_host = nullptr;
+    cudaGraphExec_t exec_host = nullptr;
 
     Bases bases() const {
         Bases b;
@@ -57,8 +67,43 @@ struct Model {
         return MGC_CUDA_OK;
     }
 
+    // The prefix once per input slice (each after its slice's copy), then the rest once.
+    int enqueue_sliced(int *kernels) {
+        MGC_CHECK_CUDA(cudaMemsetAsync(status_dev, 0, sizeof(int), stream));
+        Bases b = bases();
+        const int64_t per = images / chunks;
+        for (int j = 0; j < chunks; ++j) {
+            MGC_CHECK_CUDA(cudaStreamWaitEvent(stream, slice_ready[(size_t)j], cudaEventWaitExternal));
+            for (int r = 0; r < prefix; ++r) {
+                mgc_cuda_launch L = launches[(size_t)r];
+                for (const mgc_cuda_chunk &d : chunk_descs) {
+                    if (d.launch != r) continue;
+                    if (d.what == 0) L.r[d.slot].offset += (int64_t)j * per * d.per_image;
+                    else L.i[d.slot] = d.per_image * per;
+                }
+                MGC_CHECK(launch_record(L, aux.data(), (int64_t)aux.size(), b, status_dev, stream, kernels));
+            }
+        }
+        for (size_t r = (size_t)prefix; r < launches.size(); ++r)
+            MGC_CHECK(launch_record(launches[r], aux.data(), (int64_t)aux.size(), b, status_dev, stream, kernels));
+        return MGC_CUDA_OK;
+    }
+
+    void release_chunks() {
+        if (exec_host) cudaGraphExecDestroy(exec_host);
+        if (graph_host) cudaGraphDestroy(graph_host);
+        if (copy_stream) cudaStreamSynchronize(copy_stream);
+        for (cudaEvent_t e : slice_ready) cudaEventDestroy(e);
+        if (stream_done) cudaEventDestroy(stream_done);
+        if (copy_stream) cudaStreamDestroy(copy_stream);
+        exec_host = nullptr; graph_host = nullptr; copy_stream = nullptr; stream_done = nullptr;
+        slice_ready.clear();
+        chunks = 0; prefix = 0;
+    }
+
     void release() {
         if (device >= 0) cudaSetDevice(device);
+        release_chunks();
         if (exec) cudaGraphExecDestroy(exec);
         if (graph) cudaGraphDestroy(graph);
         if (stream) cudaStreamSynchronize(stream);
@@ -190,18 +235,85 @@ int mgc_cuda_create(const mgc_cuda_launch *launches, int n_launches, const int64
     return MGC_CUDA_OK;
 }
 
+int mgc_cuda_set_input_chunks(void *handle, int chunks, int prefix, int64_t images, const mgc_cuda_chunk *descs,
+                              int n_descs) {
+    last_error().clear();
+    Model *m = (Model *)handle;
+    if (!m) return fail(MGC_CUDA_BAD_ARGUMENT, "mgc_cuda_set_input_chunks: handle is NULL");
+    if (chunks < 2 || chunks > 16 || images <= 0 || images % chunks || prefix < 0 ||
+        prefix > (int)m->launches.size() || n_descs < 0 || (n_descs && !descs) || m->inputs.size() != 1 ||
+        m->in_bytes[0] % images)
+        return fail(MGC_CUDA_BAD_ARGUMENT, "mgc_cuda_set_input_chunks: invalid arguments");
+    for (int k = 0; k < n_descs; ++k) {
+        const mgc_cuda_chunk &d = descs[k];
+        if (d.launch < 0 || d.launch >= prefix || d.what < 0 || d.what > 1 || d.slot < 0 ||
+            d.slot >= (d.what == 0 ? MGC_LAUNCH_REFS : MGC_LAUNCH_INTS) || d.per_image < 0)
+            return fail(MGC_CUDA_BAD_ARGUMENT, "mgc_cuda_set_input_chunks: descriptor %d is invalid", k);
+    }
+    MGC_CHECK_CUDA(cudaSetDevice(m->device));
+    MGC_CHECK_CUDA(cudaStreamSynchronize(m->stream));
+    m->release_chunks();
+    m->chunks = chunks;
+    m->prefix = prefix;
+    m->images = images;
+    m->chunk_descs.assign(descs, descs + n_descs);
+    MGC_CHECK_CUDA(cudaStreamCreateWithFlags(&m->copy_stream, cudaStreamNonBlocking));
+    MGC_CHECK_CUDA(cudaEventCreateWithFlags(&m->stream_done, cudaEventDisableTiming));
+    for (int j = 0; j < chunks; ++j) {
+        cudaEvent_t e = nullptr;
+        MGC_CHECK_CUDA(cudaEventCreateWithFlags(&e, cudaEventDisableTiming));
+        m->slice_ready.push_back(e);
+    }
+    MGC_CHECK_CUDA(cudaStreamBeginCapture(m->stream, cudaStreamCaptureModeThreadLocal));
+    int kernels = 0;
+    const int st = m->enqueue_sliced(&kernels);
+    cudaGraph_t graph = nullptr;
+    const cudaError_t err = cudaStreamEndCapture(m->stream, &graph);
+    if (st != MGC_CUDA_OK || err != cudaSuccess) {
+        if (graph) cudaGraphDestroy(graph);
+        const std::string msg = last_error();
+        m->release_chunks();
+        if (st != MGC_CUDA_OK) return fail(st, "%s", msg.c_str());
+        return cuda_fail(err, "cudaStreamEndCapture");
+    }
+    m->graph_host = graph;
+    if (cudaGraphInstantiate(&m->exec_host, m->graph_host, 0) != cudaSuccess ||
+        cudaGraphUpload(m->exec_host, m->stream) != cudaSuccess || cudaStreamSynchronize(m->stream) != cudaSuccess) {
+        const cudaError_t e = cudaGetLastError();
+        m->release_chunks();
+        return cuda_fail(e, "instantiating the sliced graph");
+    }
+    return MGC_CUDA_OK;
+}
+
 int mgc_cuda_run(void *handle, const void *const *inputs_host, void *const *outputs_host) {
     last_error().clear();
     Model *m = (Model *)handle;
     if (!m) return fail(MGC_CUDA_BAD_ARGUMENT, "mgc_cuda_run: handle is NULL");
     MGC_CHECK_CUDA(cudaSetDevice(m->device));
-    for (size_t k = 0; k < m->inputs.size(); ++k) {
+    for (size_t k = 0; k < m->inputs.size(); ++k)
         if (!inputs_host || !inputs_host[k]) return fail(MGC_CUDA_BAD_ARGUMENT, "input %zu is NULL", k);
-        if (m->in_bytes[k])
-            MGC_CHECK_CUDA(cudaMemcpyAsync(m->inputs[k], inputs_host[k], (size_t)m->in_bytes[k],
-                                           cudaMemcpyHostToDevice, m->stream));
+    if (m->exec_host) {
+        // slice by slice on the copy stream; the sliced graph's prefix waits for each slice
+        const size_t slice = (size_t)(m->in_bytes[0] / m->chunks);
+        // no slice may land while work queued earlier on the stream still reads the input
+        MGC_CHECK_CUDA(cudaEventRecord(m->stream_done, m->stream));
+        MGC_CHECK_CUDA(cudaStreamWaitEvent(m->copy_stream, m->stream_done, 0));
+        for (int j = 0; j < m->chunks; ++j) {
+            MGC_CHECK_CUDA(cudaMemcpyAsync(m->inputs[0] + (size_t)j * slice,
+                                           (const char *)inputs_host[0] + (size_t)j * slice, slice,
+                                           cudaMemcpyHostToDevice, m->copy_stream));
+            MGC_CHECK_CUDA(cudaEventRecord(m->slice_ready[(size_t)j], m->copy_stream));
+        }
+        MGC_CHECK_CUDA(cudaGraphLaunch(m->exec_host, m->stream));
+    } else {
+        for (size_t k = 0; k < m->inputs.size(); ++k) {
+            if (m->in_bytes[k])
+                MGC_CHECK_CUDA(cudaMemcpyAsync(m->inputs[k], inputs_host[k], (size_t)m->in_bytes[k],
+                                               cudaMemcpyHostToDevice, m->stream));
+        }
+        MGC_CHECK_CUDA(cudaGraphLaunch(m->exec, m->stream));
     }
-    MGC_CHECK_CUDA(cudaGraphLaunch(m->exec, m->stream));
     for (size_t k = 0; k < m->outputs.size(); ++k) {
         if (!outputs_host || !outputs_host[k]) return fail(MGC_CUDA_BAD_ARGUMENT, "output %zu is NULL", k);
         if (m->out_bytes[k])

@@ -84,6 +84,13 @@ class Launch(ctypes.Structure):
 
 assert ctypes.sizeof(Launch) == 16 + 8 * LAUNCH_INTS + 8 * LAUNCH_FLOATS + 16 * LAUNCH_REFS + 16
 
+class Chunk(ctypes.Structure):
+    """mgc_cuda_chunk: one batch-dependent field of a record of the sliced prefix."""
+
+    _fields_ = [("launch", ctypes.c_int32), ("what", ctypes.c_int32), ("slot", ctypes.c_int32),
+                ("reserved", ctypes.c_int32), ("per_image", ctypes.c_int64)]
+
+
 RefT = tuple[int, int, int]
 NO_REF: RefT = (SPACE_NONE, 0, 0)
 
@@ -1191,3 +1198,113 @@ def algorithmic_cost(graph: Graph) -> tuple[int, int]:
 
 
 __all__ = ["CudaEmitter", "Launch", "LoweredModel", "Ref", "algorithmic_cost", "lower_graph", "tf32_split"]
+
+
+# ---- input-upload overlap -------------------------------------------------------------------------
+# A GEMM stays in the sliced prefix only while one slice still has rows for several waves of
+# 256-row tiles over all SMs.
+SLICE_MIN_ROWS = 2 * 148 * 256
+
+
+def _slice_fields(rec: Launch, images: int, per: int) -> list[tuple[int, int, int]] | None:
+    """(what, slot, per_image) of every batch-dependent field of a record that works image by image
+    on batch-major float32 tensors, or None when the record cannot run on a slice of the batch."""
+    i, r = rec.i, rec.r
+    if rec.dtype != DTYPES["float32"]:
+        return None
+    if rec.kind == K_PACK:
+        if i[0] != images:
+            return None
+        return [(1, 0, 1), (0, 0, i[5] * 4), (0, 1, i[11] * i[12] * i[4] * 4)]
+    if rec.kind == K_POOL:
+        if i[1] != images or not i[18]:
+            return None
+        return [(1, 1, 1), (0, 0, i[2] * i[3] * i[4] * 4), (0, 1, i[15] * i[16] * i[4] * 4)]
+    if rec.kind == K_GEMM:
+        h, w, c, ow, c_off, cg, oh = i[27], i[28], i[29], i[38], i[39], i[40], i[49]
+        if i[3] != 0 or oh <= 0 or ow <= 0 or c_off != 0 or cg != c or i[0] != images * oh * ow:
+            return None
+        if per * oh * ow < SLICE_MIN_ROWS:
+            return None
+        if i[24] == STRIDED:  # pointwise convolution: H x W rows of a_rs floats per image
+            a_img = h * w * i[25] * 4
+        elif i[24] == CONV_NHWC:
+            a_img = h * w * c * 4
+        else:
+            return None
+        out = [(1, 0, oh * ow), (0, 0, a_img), (0, 2, oh * ow * i[44] * 4)]
+        if r[4].space != SPACE_NONE:
+            out.append((0, 4, oh * ow * i[46] * 4))
+        return out
+    return None
+
+
+# reference slots each sliceable record kind writes (the others it reads)
+_SLICE_WRITES = {K_PACK: (1,), K_POOL: (1,), K_GEMM: (2,)}
+
+
+def input_slice_plan(lowered: LoweredModel, chunks: int = 4) -> tuple[int, int, list[Chunk]] | None:
+    """(prefix records, images, descriptors) for mgc_cuda_set_input_chunks, or None.
+
+    The prefix is the longest run of leading nodes whose records all work image by image on
+    batch-major tensors (_slice_fields), cut back until slicing it is safe. Slicing reorders the
+    prefix's accesses: slice j runs the whole prefix before slice j + 1 starts. A buffer written in
+    the prefix and read only inside it is consumed within its own slice's pass, so the planner's
+    reuse of memory stays valid there. A buffer that the rest of the graph reads must survive the
+    later slices' passes: no other prefix buffer may share its memory unless both have the same
+    start and bytes per image (then every slice keeps to its own range)."""
+    if len(lowered.inputs) != 1:
+        return None
+    shape = lowered.inputs[0][1].shape
+    if len(shape) < 2 or shape[0] < chunks or shape[0] % chunks:
+        return None
+    images = int(shape[0])
+    per = images // chunks
+    recs = lowered.launches
+    # the longest sliceable run of whole nodes
+    fields: list[list[tuple[int, int, int]]] = []
+    end, k = 0, 0
+    while k < len(recs):
+        j = k
+        while j < len(recs) and recs[j].node == recs[k].node:
+            j += 1
+        fs = [_slice_fields(recs[n], images, per) for n in range(k, j)]
+        if any(f is None for f in fs):
+            break
+        fields += fs
+        end, k = j, j
+    tracked = (SPACE_ARENA, SPACE_OUTPUT, SPACE_WORKSPACE)
+    while end > 0:
+        # buffers the prefix writes: (space, index, start, end, bytes per image, record)
+        writes = []
+        for n in range(end):
+            per_image = {slot: b for what, slot, b in fields[n] if what == 0}
+            for slot in _SLICE_WRITES[recs[n].kind]:
+                ref = recs[n].r[slot]
+                if ref.space not in tracked:
+                    return None
+                writes.append((ref.space, ref.index, ref.offset, ref.offset + per_image[slot] * images,
+                               per_image[slot], n))
+        suffix_refs = [(recs[n].r[t].space, recs[n].r[t].index, recs[n].r[t].offset)
+                       for n in range(end, len(recs)) for t in range(len(recs[n].r))]
+        cut = None
+        for sp, ix, lo, hi, pi, n in writes:
+            escapes = sp == SPACE_OUTPUT or any(s2 == sp and i2 == ix and lo <= o < hi for s2, i2, o in suffix_refs)
+            if not escapes:
+                continue
+            for sp2, ix2, lo2, hi2, pi2, n2 in writes:
+                if (sp2, ix2) == (sp, ix) and lo2 < hi and lo < hi2 and (lo2, pi2) != (lo, pi):
+                    later = max(n, n2)
+                    cut = later if cut is None else min(cut, later)
+        if cut is None:
+            break
+        # drop the node holding record `cut` and everything after it
+        node = recs[cut].node
+        while cut > 0 and recs[cut - 1].node == node:
+            cut -= 1
+        end = cut
+        fields = fields[:end]
+    if end == 0 or not any(recs[n].kind == K_GEMM for n in range(end)):
+        return None
+    descs = [Chunk(n, what, slot, 0, b) for n in range(end) for what, slot, b in fields[n]]
+    return end, images, descs

@@ -12,6 +12,7 @@ from __future__ import annotations
 
 import ctypes
 import json
+import os
 import threading
 import time
 from collections.abc import Mapping
@@ -23,7 +24,7 @@ import numpy as np
 
 from mgc_cuda import _reference  # noqa: F401
 from mgc_cuda import build as _build
-from mgc_cuda.lowering import Launch, LoweredModel, lower_graph
+from mgc_cuda.lowering import Chunk, Launch, LoweredModel, input_slice_plan, lower_graph
 from ml_graph_compiler.errors import CodegenError, GraphError
 from ml_graph_compiler.ir import Graph, TensorType, numpy_dtype
 from ml_graph_compiler.memory import Strategy
@@ -40,6 +41,7 @@ SIGNATURES: dict[str, tuple[Any, list[Any]]] = {
     "mgc_cuda_create": (_I, [_VP, _I, _VP, _I64, _VP, _I64, _I64, _I64, _VP, _I, _VP, _I, _I, ctypes.POINTER(_VP)]),
     "mgc_cuda_run": (_I, [_VP, _VP, _VP]),
     "mgc_cuda_run_device": (_I, [_VP, _I]),
+    "mgc_cuda_set_input_chunks": (_I, [_VP, _I, _I, _I64, _VP, _I]),
     "mgc_cuda_input_ptr": (_VP, [_VP, _I]),
     "mgc_cuda_output_ptr": (_VP, [_VP, _I]),
     "mgc_cuda_stream": (_VP, [_VP]),
@@ -142,6 +144,18 @@ class CudaCompiledModel:
             ctypes.addressof(outs), len(self.outputs), device, ctypes.byref(self._handle),
         )
         check(st, "mgc_cuda_create", self.lib)
+        # run(): upload the input in slices that overlap the first layers' compute
+        # (MGC_CUDA_SLICES=0 turns it off, =k uses k slices; 4 by default)
+        self.slices = 0
+        slices = int(os.environ.get("MGC_CUDA_SLICES", "4") or 0)
+        plan = input_slice_plan(lowered, slices) if slices >= 2 else None
+        if plan is not None:
+            prefix, images, descs = plan
+            arr = (Chunk * len(descs))(*descs)
+            st = self.lib.mgc_cuda_set_input_chunks(self._handle, slices, prefix, images, ctypes.addressof(arr),
+                                                    len(descs))
+            check(st, "mgc_cuda_set_input_chunks", self.lib)
+            self.slices = slices
         self._in_ptrs = (ctypes.c_void_p * max(len(self.inputs), 1))()
         self._out_ptrs = (ctypes.c_void_p * max(len(self.outputs), 1))()
 

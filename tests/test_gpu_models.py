@@ -167,3 +167,33 @@ def test_profile_save_load_and_device_run(tmp_path) -> None:
     np.testing.assert_array_equal(m2.run(feeds)["logits"], want)
     assert m2.launch_count > 0
     m2.close()
+
+
+@pytest.mark.parametrize("strategy", ["greedy_by_size", "naive"])
+def test_sliced_upload_matches_one_pass(strategy: str, monkeypatch: pytest.MonkeyPatch) -> None:
+    """run() with the input uploaded in four slices, the leading layers running slice by slice
+    as each lands, gives the one-pass graph's outputs bit for bit (strict mode: the kernels see
+    fewer rows per launch, each row computed the same way). The slice row threshold is lowered so
+    that the small model's convolutions join the prefix."""
+    from mgc_cuda import lowering
+
+    g = zoo.resnet50(batch=8)
+    optimize(g, "O3")
+    schedule(g)
+    x = np.random.default_rng(9).standard_normal((8, 3, 224, 224)).astype(np.float32)
+    monkeypatch.setattr(lowering, "SLICE_MIN_ROWS", 1)
+    monkeypatch.setenv("MGC_CUDA_SLICES", "0")
+    one = compile_graph(g, precision="strict", strategy=strategy)
+    want = one.run({"image": x})["logits"]
+    one.close()
+    monkeypatch.setenv("MGC_CUDA_SLICES", "4")
+    sliced = compile_graph(g, precision="strict", strategy=strategy)
+    plan = lowering.input_slice_plan(sliced.lowered, 4)
+    try:
+        assert sliced.slices == 4 and plan is not None and plan[0] >= 3
+        got = sliced.run({"image": x})["logits"]
+        again = sliced.run({"image": x})["logits"]
+    finally:
+        sliced.close()
+    np.testing.assert_array_equal(got, want)
+    np.testing.assert_array_equal(again, want)

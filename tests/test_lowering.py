@@ -151,3 +151,28 @@ def test_tensor_core_b_planes_are_ordered(r50: Graph) -> None:
             if rec.kind == lowering.K_GEMM and rec.r[6].space == lowering.SPACE_WEIGHTS:
                 gap = rec.r[7].offset - rec.r[6].offset
                 assert gap > 0 and gap % 16 == 0
+
+
+@pytest.mark.parametrize("strategy,records", [("greedy_by_size", 3), ("naive", 14)])
+def test_input_slice_plan_of_resnet50(strategy: str, records: int) -> None:
+    """The sliced prefix at batch 256: pack, stem and MaxPool under the default plan (the
+    planner then reuses the stem's memory for layer1 buffers of other layouts that later slices
+    would overwrite); with private buffers (naive) layer1 and the first layer2 convolution too,
+    up to the first GEMM whose slice has too few rows."""
+    g = o3(zoo.resnet50(batch=256))
+    low = lower_graph(g, strategy, True, "tf32")
+    plan = lowering.input_slice_plan(low, 4)
+    assert plan is not None
+    prefix, images, descs = plan
+    assert (prefix, images) == (records, 256)
+    stem = low.launches[1]
+    assert stem.kind == K_GEMM and low.launches[0].kind == K_PACK
+    fields = {(d.what, d.slot): d.per_image for d in descs if d.launch == 1}
+    # M = images * 112 * 112; A = the padded 229 x 229 x 4 image; C = 112 * 112 * 64 floats
+    assert fields == {(1, 0): 112 * 112, (0, 0): 229 * 229 * 4 * 4, (0, 2): 112 * 112 * 64 * 4}
+    assert all(d.launch < prefix for d in descs)
+
+
+def test_input_slice_plan_needs_a_batch() -> None:
+    low = lower_graph(o3(zoo.resnet50(batch=1)), "greedy_by_size", True, "tf32")
+    assert lowering.input_slice_plan(low, 4) is None
