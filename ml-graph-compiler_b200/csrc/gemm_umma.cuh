@@ -31,7 +31,8 @@
 //
 // Every wait on an mbarrier is bounded (about a second of clock cycles); on timeout the kernel
 // records MGC_CUDA_TIMEOUT in the error word, drains what it issued, frees its TMEM and returns.
-// No TMA multicast is used anywhere.
+// Every TMA copy lands in the shared memory of the CTA that issues it; a CTA pair shares B only
+// through its cta_group::2 MMAs.
 #pragma once
 
 #include <cuda.h>
