@@ -283,6 +283,11 @@ __device__ __forceinline__ void tma_store_commit_and_wait() {
     asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory");
 }
 
+__device__ __forceinline__ void tma_store_commit() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
+
+// Every committed store of this thread has finished reading shared memory.
+__device__ __forceinline__ void tma_store_wait_read() { asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory"); }
+
 // Epilogue warps: two per TMEM lane quadrant, each taking half of the tile's columns.
 constexpr int EPI_THREADS = 256;
 // A TMA instruction holds its issuing thread for ~350 cycles (measured, any box size), so A and
@@ -534,8 +539,11 @@ constexpr uint32_t SMEM_LIMIT = 232448;  // dynamic shared memory per block on s
 // PAIR: CTA-pair variant (TF32 mode): 256-row tiles, each CTA holding one plane of B.
 // WIDE (a pair with BN = 256): 256 x 256 tiles; each CTA holds both planes of its 128 B rows and
 // the hi and lo products go to one accumulator through two N = 256 MMAs per K step.
-template <int BN, int MODE, int RB = 0, int PAIR = 0>
+// SR (one CTA per tile, TF32, with a residual): the residual moves through its own staging
+// buffer, so the next tile's residual loads while this tile's output is stored.
+template <int BN, int MODE, int RB = 0, int PAIR = 0, int SR = 0>
 struct Cfg {
+    static_assert(!SR || (!PAIR && MODE == TF32), "a separate residual buffer is a one-CTA TF32 form");
     static_assert(!PAIR || MODE == TF32, "CTA pairs run TF32 mode only");
     static constexpr bool WIDE = PAIR && BN == 256;
     static_assert(BN <= 128 || (WIDE && RB == 0), "N tiles of 256 are pair-only, without B residency");
@@ -554,9 +562,10 @@ struct Cfg {
     static constexpr uint32_t OUT_BYTES = BM * EN * 4;
     static constexpr uint32_t BAR_BYTES = 512;                     // mbarriers and the TMEM address
     // everything else: output staging, alignment slack, barriers, the tile's bias
-    static constexpr uint32_t STAGE_BUDGET = SMEM_LIMIT - OUT_BYTES - 1024 - BAR_BYTES - BN * 4;
+    static constexpr uint32_t RES_BYTES = SR ? OUT_BYTES : 0;       // the residual's own staging
+    static constexpr uint32_t STAGE_BUDGET = SMEM_LIMIT - OUT_BYTES - RES_BYTES - 1024 - BAR_BYTES - BN * 4;
     static constexpr int MAX_STAGES = 8;
-    static constexpr int STAGES = RB ? (MODE == STRICT ? 2 : 4)
+    static constexpr int STAGES = RB ? (MODE == STRICT || SR ? 2 : 4)
                                   : (STAGE_BUDGET / STAGE_BYTES) < 2 ? 2
                                   : (int)(STAGE_BUDGET / STAGE_BYTES) > MAX_STAGES ? MAX_STAGES
                                   : (STAGE_BUDGET / STAGE_BYTES);
@@ -567,7 +576,8 @@ struct Cfg {
     static constexpr int TBUFS = (512 / BUF_COLS) > 4 ? 4 : (512 / BUF_COLS);  // TMEM buffers in the ring
     static constexpr uint32_t TMEM_COLS = TBUFS * BUF_COLS;
     // fixed part; a B-resident launch adds its B panel (b_res_bytes) in front of the stages
-    static constexpr uint32_t SMEM_BYTES = STAGES * STAGE_BYTES + OUT_BYTES + 1024 /*align*/ + BAR_BYTES + BN * 4 /*bias*/;
+    static constexpr uint32_t SMEM_BYTES =
+        STAGES * STAGE_BYTES + OUT_BYTES + RES_BYTES + 1024 /*align*/ + BAR_BYTES + BN * 4 /*bias*/;
     static constexpr uint32_t B_RES_MAX = RB ? SMEM_LIMIT - SMEM_BYTES : 0;
     static_assert((3 * 8 + 2 * 4 + 3) * 8 + 4 <= BAR_BYTES, "barrier area");
     static_assert(TMEM_COLS <= 512 && (TMEM_COLS & (TMEM_COLS - 1)) == 0, "TMEM columns");
@@ -579,9 +589,9 @@ struct Cfg {
 // and walks the M tiles b / n_tiles, + gridDim.x / n_tiles, ... The shared-memory stage ring and
 // the TMEM buffer ring run on a K-block counter that continues across tiles, so the next tile's
 // loads and MMAs overlap this tile's drain and epilogue.
-template <int BN, int MODE, int RB, int PAIR>
+template <int BN, int MODE, int RB, int PAIR, int SR>
 __global__ void __launch_bounds__(THREADS, 1) umma_gemm_kernel(const __grid_constant__ Params p) {
-    using C = Cfg<BN, MODE, RB, PAIR>;
+    using C = Cfg<BN, MODE, RB, PAIR, SR>;
     constexpr int S = C::STAGES;
     constexpr int R = C::REGIONS;
     constexpr int TB = C::TBUFS;
@@ -598,7 +608,8 @@ __global__ void __launch_bounds__(THREADS, 1) umma_gemm_kernel(const __grid_cons
                   : stages + (size_t)s * C::STAGE_BYTES + A_TILE_BYTES + (MODE == STRICT ? A_TILE_BYTES : 0);
     };
     uint8_t *out_tile = stages + (size_t)S * C::STAGE_BYTES;  // 1024-aligned
-    uint64_t *full = reinterpret_cast<uint64_t *>(out_tile + C::OUT_BYTES);
+    uint8_t *res_tile = SR ? out_tile + C::OUT_BYTES : out_tile;  // where a residual pass lands
+    uint64_t *full = reinterpret_cast<uint64_t *>(out_tile + C::OUT_BYTES + C::RES_BYTES);
     uint64_t *empty = full + S;
     uint64_t *split = empty + S;
     uint64_t *tfull = split + S;       // [TB] a K block's products are in TMEM buffer b
@@ -607,7 +618,7 @@ __global__ void __launch_bounds__(THREADS, 1) umma_gemm_kernel(const __grid_cons
     uint64_t *res_full = mma_done + 1; // a tile's residual has landed in the staging tile
     uint64_t *bres_full = res_full + 1; // the B panel has landed (B-resident)
     uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(bres_full + 1);
-    float *bias_s = reinterpret_cast<float *>(out_tile + C::OUT_BYTES + C::BAR_BYTES);  // [BN] this tile's bias
+    float *bias_s = reinterpret_cast<float *>(out_tile + C::OUT_BYTES + C::RES_BYTES + C::BAR_BYTES);  // [BN] bias
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int num_kb = p.num_kb;
@@ -1057,7 +1068,8 @@ __global__ void __launch_bounds__(THREADS, 1) umma_gemm_kernel(const __grid_cons
         if (issuer && p.tma_out) prefetch_tmap(&p.tmC);
         if (issuer && p.tma_res) prefetch_tmap(&p.tmR);
         const bool rows = p.im2col == 4;
-        // the residual of pass h_ of tile (mt_, nt_) into the staging tile
+        // the residual of pass h_ of tile (mt_, nt_) into its staging (the output staging tile,
+        // or with SR its own)
         auto issue_residual = [&](int mt_, int nt_, int h_) {
             const int tn0 = nt_ * BN + h_ * EN, tm0 = mt_ * C::TM + row0;
             if (rows) {
@@ -1065,13 +1077,13 @@ __global__ void __launch_bounds__(THREADS, 1) umma_gemm_kernel(const __grid_cons
                 mbar_expect_tx(res_full, (uint32_t)(EN / 32) * p.a_bytes);
 #pragma unroll 1
                 for (int sl = 0; sl < EN / 32; ++sl)
-                    tma_load_4d(out_tile + sl * (BM * 128), &p.tmR, res_full, tn0 + sl * 32, 0, oh0, img);
+                    tma_load_4d(res_tile + sl * (BM * 128), &p.tmR, res_full, tn0 + sl * 32, 0, oh0, img);
                 return;
             }
             mbar_expect_tx(res_full, C::OUT_BYTES);
 #pragma unroll 1
             for (int sl = 0; sl < EN / 32; ++sl)
-                tma_load_2d(out_tile + sl * (BM * 128), &p.tmR, res_full, tn0 + sl * 32, tm0);
+                tma_load_2d(res_tile + sl * (BM * 128), &p.tmR, res_full, tn0 + sl * 32, tm0);
         };
         int mt, nt;
         if (res_tma && issuer && tile_at(0, mt, nt)) issue_residual(mt, nt, 0);
@@ -1098,8 +1110,9 @@ __global__ void __launch_bounds__(THREADS, 1) umma_gemm_kernel(const __grid_cons
             if (p.bias) {
                 for (int c = et; c < EN; c += EPI_THREADS) bias_s[c] = n0 + c < p.N ? __ldg(p.bias + n0 + c) : 0.0f;
             }
-            // the staging tile is free (the previous TMA store was read out) and, with a
-            // residual, refilled with this tile's residual
+            // the staging tile is free (the previous TMA store was read out: SR waits for it
+            // here) and the residual staging holds this pass's residual
+            if (SR && issuer) tma_store_wait_read();
             epilogue_sync();
             if (res_tma && !mbar_wait(res_full, (uint32_t)(local & 1))) {
                 ok = false;
@@ -1107,14 +1120,14 @@ __global__ void __launch_bounds__(THREADS, 1) umma_gemm_kernel(const __grid_cons
             }
             // 32 columns at a time: the residual and bias loads of a chunk are all issued before
             // its stores, so no load waits behind a store to the same staging tile
-            const uint32_t out_s = smem_addr(out_tile);
+            const uint32_t out_s = smem_addr(out_tile), res_s = smem_addr(res_tile);
             const uint32_t bias_addr = smem_addr(bias_s);
 #pragma unroll
             for (int a0 = 0; a0 < HALF; a0 += 32) {  // a0: accumulator index; column hc + a0
                 float4 rv[8], bvs[8];
 #pragma unroll
                 for (int j = 0; j < 8; ++j) {
-                    rv[j] = res_tma ? lds4(out_s + stage_offset(row, hc + a0 + 4 * j)) : make_float4(0.f, 0.f, 0.f, 0.f);
+                    rv[j] = res_tma ? lds4(res_s + stage_offset(row, hc + a0 + 4 * j)) : make_float4(0.f, 0.f, 0.f, 0.f);
                     bvs[j] = p.bias ? lds4(bias_addr + 4 * (hc + a0 + 4 * j)) : make_float4(0.f, 0.f, 0.f, 0.f);
                 }
 #pragma unroll
@@ -1182,6 +1195,11 @@ __global__ void __launch_bounds__(THREADS, 1) umma_gemm_kernel(const __grid_cons
                 fence_proxy_async_smem();
                 epilogue_sync();
                 if (issuer) {
+                    int mt2, nt2;
+                    if (SR) {  // the residual staging is read out: the next pass's residual now
+                        if (res_tma && h + 1 < NH) issue_residual(mt, nt, h + 1);
+                        else if (res_tma && tile_at(i + 1, mt2, nt2)) issue_residual(mt2, nt2, 0);
+                    }
                     if (rows) {  // the tile's rt_rows output rows; staging rows past them are dropped
                         const int img = mt / p.rt_per_img, oh0 = (mt - img * p.rt_per_img) * p.rt_rows;
 #pragma unroll 1
@@ -1193,18 +1211,23 @@ __global__ void __launch_bounds__(THREADS, 1) umma_gemm_kernel(const __grid_cons
                         for (int sl = 0; sl < EN / 32; ++sl)
                             tma_store_2d(&p.tmC, out_tile + sl * (BM * 128), n0 + sl * 32, m0);
                     }
-                    tma_store_commit_and_wait();
-                    // the next pass's residual: this tile's, or the next tile's first
-                    int mt2, nt2;
-                    if (res_tma && h + 1 < NH) issue_residual(mt, nt, h + 1);
-                    else if (res_tma && tile_at(i + 1, mt2, nt2)) issue_residual(mt2, nt2, 0);
+                    if (SR) {
+                        tma_store_commit();  // read out before the next pass writes the staging tile
+                    } else {
+                        tma_store_commit_and_wait();
+                        // the next pass's residual: this tile's, or the next tile's first
+                        if (res_tma && h + 1 < NH) issue_residual(mt, nt, h + 1);
+                        else if (res_tma && tile_at(i + 1, mt2, nt2)) issue_residual(mt2, nt2, 0);
+                    }
                 }
             }
           }
         }
         if (!ok) set_error(p.err, MGC_CUDA_TIMEOUT);
-        // a residual prefetch that no tile consumed must land before the CTA exits
+        // a residual prefetch that no tile consumed must land, and the last store must have read
+        // the staging tile, before the CTA exits
         if (res_tma && issuer && !ok) mbar_wait(res_full, (uint32_t)(local & 1));
+        if (SR && issuer) tma_store_wait_read();
         (void)et;
     }
     tc_fence_before();
@@ -1339,21 +1362,21 @@ inline bool make_map_rows(CUtensorMap *map, const void *base, long long n, long 
 
 // Dynamic shared memory of a launch. Pair launches ask for more than half an SM's shared memory,
 // so no two CTAs (and no two TMEM allocations) ever share an SM.
-template <int BN, int MODE, int RB, int PAIR>
+template <int BN, int MODE, int RB, int PAIR, int SR = 0>
 inline uint32_t launch_smem(const Params &p) {
-    using C = Cfg<BN, MODE, RB, PAIR>;
+    using C = Cfg<BN, MODE, RB, PAIR, SR>;
     const uint32_t smem = C::SMEM_BYTES + (RB ? p.b_res_bytes : 0u);
     return PAIR && smem < SMEM_LIMIT / 2 + 1024 ? SMEM_LIMIT / 2 + 1024 : smem;
 }
 
-template <int BN, int MODE, int RB, int PAIR>
+template <int BN, int MODE, int RB, int PAIR, int SR = 0>
 inline int launch(const Params &p, int grid, cudaStream_t stream) {
-    const uint32_t smem = launch_smem<BN, MODE, RB, PAIR>(p);
+    const uint32_t smem = launch_smem<BN, MODE, RB, PAIR, SR>(p);
     // per device (the attribute belongs to the current context); cheap, and allowed under capture
-    MGC_CHECK_CUDA(cudaFuncSetAttribute(umma_gemm_kernel<BN, MODE, RB, PAIR>,
+    MGC_CHECK_CUDA(cudaFuncSetAttribute(umma_gemm_kernel<BN, MODE, RB, PAIR, SR>,
                                         cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
     if (!PAIR) {
-        umma_gemm_kernel<BN, MODE, RB, PAIR><<<grid, THREADS, smem, stream>>>(p);
+        umma_gemm_kernel<BN, MODE, RB, PAIR, SR><<<grid, THREADS, smem, stream>>>(p);
         return check_launch("umma_gemm_kernel");
     }
     cudaLaunchConfig_t cfg = {};
@@ -1368,7 +1391,7 @@ inline int launch(const Params &p, int grid, cudaStream_t stream) {
     cfg.stream = stream;
     cfg.attrs = attr;
     cfg.numAttrs = 1;
-    MGC_CHECK_CUDA(cudaLaunchKernelEx(&cfg, umma_gemm_kernel<BN, MODE, RB, PAIR>, p));
+    MGC_CHECK_CUDA(cudaLaunchKernelEx(&cfg, umma_gemm_kernel<BN, MODE, RB, PAIR, SR>, p));
     return check_launch("umma_gemm_kernel (pair)");
 }
 
@@ -1388,6 +1411,22 @@ inline int launch_best(Params &p, long long m_tiles, cudaStream_t stream) {
     return launch<BN, MODE, 0, 0>(p, (int)(tiles < sms ? tiles : sms), stream);
 }
 
+// One CTA per tile with a residual through its own staging buffer (N tiles of 128, TF32), when
+// the B panel fits beside a two-stage A ring (B-resident; measured on ResNet-50 batch 256: the
+// 1x1 C64->256 + residual layers 16 % faster). With B streamed, two stages starve the MMAs
+// (+33 % on 1x1 C256->1024 + residual), so the output staging is shared as before.
+inline int launch_best_sr(Params &p, long long m_tiles, cudaStream_t stream) {
+    using C1 = Cfg<128, TF32, 1, 0, 1>;
+    const int sms = sm_count();
+    const uint32_t panel = (uint32_t)p.num_kb * 2u * C1::B_TILE_BYTES;
+    const int per = p.n_tiles <= sms ? sms / p.n_tiles : 0;
+    if (per > 0 && panel <= C1::B_RES_MAX && m_tiles >= 2LL * per) {
+        p.b_res_bytes = panel;
+        return launch<128, TF32, 1, 0, 1>(p, per * p.n_tiles, stream);
+    }
+    return launch_best<128, TF32>(p, m_tiles, stream);
+}
+
 // Clusters of two that fit on the device at once (one CTA per SM), per kernel variant; 0 if
 // the query fails. Cached per device.
 template <int BN, int RB>
@@ -1404,7 +1443,7 @@ inline int pair_clusters() {
     memset(&dummy, 0, sizeof dummy);
     const uint32_t smem = launch_smem<BN, TF32, RB, 1>(dummy);
     int n = 0;
-    if (cudaFuncSetAttribute(umma_gemm_kernel<BN, TF32, RB, 1>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+    if (cudaFuncSetAttribute(umma_gemm_kernel<BN, TF32, RB, 1, 0>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                              (int)SMEM_LIMIT) == cudaSuccess) {
         cudaLaunchConfig_t cfg = {};
         cudaLaunchAttribute attr[1] = {};
@@ -1417,7 +1456,7 @@ inline int pair_clusters() {
         cfg.dynamicSmemBytes = smem;
         cfg.attrs = attr;
         cfg.numAttrs = 1;
-        if (cudaOccupancyMaxActiveClusters(&n, umma_gemm_kernel<BN, TF32, RB, 1>, &cfg) != cudaSuccess) n = 0;
+        if (cudaOccupancyMaxActiveClusters(&n, umma_gemm_kernel<BN, TF32, RB, 1, 0>, &cfg) != cudaSuccess) n = 0;
     }
     cudaGetLastError();
     cached[dev] = n;
@@ -1613,10 +1652,16 @@ inline int try_gemm_umma(const GemmParams &p, cudaStream_t stream, int *taken) {
             return MGC_CUDA_OK;
         }
     }
-    // persistent grid: one CTA per SM (the shared-memory footprint allows no more)
+    // persistent grid: one CTA per SM (the shared-memory footprint allows no more). With a
+    // residual, its own staging buffer (MGC_CUDA_SR=0 shares the output's)
+    static const bool sr_env = [] {
+        const char *e = getenv("MGC_CUDA_SR");
+        return !(e && e[0] == '0');
+    }();
     int st;
     if (strict) st = umma::launch_best<64, umma::STRICT>(u, m_tiles, stream);
     else if (bn == 64) st = umma::launch_best<64, umma::TF32>(u, m_tiles, stream);
+    else if (u.tma_res && sr_env) st = umma::launch_best_sr(u, m_tiles, stream);
     else st = umma::launch_best<128, umma::TF32>(u, m_tiles, stream);
     if (st != MGC_CUDA_OK) return st;
     *taken = 1;
