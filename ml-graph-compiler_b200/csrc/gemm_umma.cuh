@@ -540,7 +540,8 @@ constexpr uint32_t SMEM_LIMIT = 232448;  // dynamic shared memory per block on s
 // WIDE (a pair with BN = 256): 256 x 256 tiles; each CTA holds both planes of its 128 B rows and
 // the hi and lo products go to one accumulator through two N = 256 MMAs per K step.
 // SR (one CTA per tile, TF32, with a residual): the residual moves through its own staging
-// buffer, so the next tile's residual loads while this tile's output is stored.
+// buffer, so the next pass's residual loads while this pass's output is stored; SR = 2 runs the
+// epilogue in passes of 64 columns, so that both buffers take the shared memory of one.
 template <int BN, int MODE, int RB = 0, int PAIR = 0, int SR = 0>
 struct Cfg {
     static_assert(!SR || (!PAIR && MODE == TF32), "a separate residual buffer is a one-CTA TF32 form");
@@ -552,7 +553,7 @@ struct Cfg {
     static constexpr uint32_t B_TILE_BYTES = BROWS * BK * 4;
     static constexpr int B_PLANES = PAIR && !WIDE ? 1 : 2;   // B planes in this CTA's shared memory
     static constexpr int TM = PAIR ? 2 * BM : BM;            // rows of one tile
-    static constexpr int EN = WIDE ? 64 : BN;                // columns of one epilogue pass
+    static constexpr int EN = WIDE || SR == 2 ? 64 : BN;     // columns of one epilogue pass
     static constexpr int NH = BN / EN;                       // epilogue passes per tile
     // stage: A (| A_lo) (| B_hi | B_lo), or A | this rank's B plane
     static constexpr uint32_t STAGE_BYTES =
@@ -1424,7 +1425,9 @@ inline int launch_best_sr(Params &p, long long m_tiles, cudaStream_t stream) {
         p.b_res_bytes = panel;
         return launch<128, TF32, 1, 0, 1>(p, per * p.n_tiles, stream);
     }
-    return launch_best<128, TF32>(p, m_tiles, stream);
+    p.b_res_bytes = 0;
+    const long long tiles = (long long)p.n_tiles * m_tiles;
+    return launch<128, TF32, 0, 0, 2>(p, (int)(tiles < sms ? tiles : sms), stream);
 }
 
 // Clusters of two that fit on the device at once (one CTA per SM), per kernel variant; 0 if
