@@ -1425,6 +1425,11 @@ inline int launch_best_sr(Params &p, long long m_tiles, cudaStream_t stream) {
         p.b_res_bytes = panel;
         return launch<128, TF32, 1, 0, 1>(p, per * p.n_tiles, stream);
     }
+    // 64-column passes leave room for a B panel of up to 128 KB (1x1 C128->512)
+    if (per > 0 && panel <= Cfg<128, TF32, 1, 0, 2>::B_RES_MAX && m_tiles >= 2LL * per) {
+        p.b_res_bytes = panel;
+        return launch<128, TF32, 1, 0, 2>(p, per * p.n_tiles, stream);
+    }
     p.b_res_bytes = 0;
     const long long tiles = (long long)p.n_tiles * m_tiles;
     return launch<128, TF32, 0, 0, 2>(p, (int)(tiles < sms ? tiles : sms), stream);
