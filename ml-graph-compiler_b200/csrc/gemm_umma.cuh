@@ -60,7 +60,9 @@ constexpr long long WAIT_LIMIT_CYCLES = 1ll << 31;  // ~1.1 s at 1.9 GHz
 // within +-8e-5): the rounding of the activations to TF32 dominates, the accumulator's rounding
 // toward zero over a long chain does not show.
 
-enum Mode { TF32 = 0, STRICT = 1 };
+// DYN: TF32 with a dynamic B (an activation, rounded to TF32 by its tensor map like A): one
+// plane, one accumulator, tiles batched over up to two batch dimensions of 4-D tensor maps.
+enum Mode { TF32 = 0, STRICT = 1, DYN = 2 };
 
 // Mean relative shrink toward zero of one kind::tf32 MMA step (eight exact TF32 products summed
 // into a fresh fp32 accumulator), measured on B200 with TF32-exact random operands: -2.4e-8 to
@@ -84,7 +86,8 @@ struct Params {
     int wrows;                       // window rows (im2col 3): output pixels per box (divides OW)
     int rt_rows, rt_per_img;         // row tiles (im2col 4): output rows per tile, tiles per image
     uint32_t a_bytes;                // bytes of one K block's A boxes (row tiles fill rt_rows*OW rows)
-    int m_tiles;                     // ceil(M / 128)
+    int m_tiles;                     // ceil(M / 128) (DYN: times the batches)
+    int m_per_batch, nbatch1;        // DYN: M tiles per batch; extent of the first batch dimension
     uint32_t b_res_bytes;            // B-resident kernels: bytes of this CTA's whole B panel
     int OH, OW, SH, SW, PT, PL;      // im2col: output pixel -> window origin
     float *c;
@@ -548,10 +551,12 @@ struct Cfg {
     static_assert(!PAIR || MODE == TF32, "CTA pairs run TF32 mode only");
     static constexpr bool WIDE = PAIR && BN == 256;
     static_assert(BN <= 128 || (WIDE && RB == 0), "N tiles of 256 are pair-only, without B residency");
+    static_assert(MODE != DYN || (!PAIR && !RB && !SR), "dynamic-B GEMMs run one CTA per tile");
+    static constexpr bool ONEACC = WIDE || MODE == DYN;     // one accumulator (no B_lo columns)
     static constexpr int REGIONS = MODE == STRICT ? 4 : 1;  // TMEM regions per K block
     static constexpr int BROWS = WIDE ? BN / 2 : BN;         // B rows of one plane in this CTA
     static constexpr uint32_t B_TILE_BYTES = BROWS * BK * 4;
-    static constexpr int B_PLANES = PAIR && !WIDE ? 1 : 2;   // B planes in this CTA's shared memory
+    static constexpr int B_PLANES = (PAIR && !WIDE) || MODE == DYN ? 1 : 2;  // B planes in this CTA's smem
     static constexpr int TM = PAIR ? 2 * BM : BM;            // rows of one tile
     static constexpr int EN = WIDE || SR == 2 ? 64 : BN;     // columns of one epilogue pass
     static constexpr int NH = BN / EN;                       // epilogue passes per tile
@@ -573,7 +578,7 @@ struct Cfg {
     // TMEM columns of one buffer: strict, four step regions of BN; TF32, the products with B_hi
     // (columns [0, BN)) and with B_lo ([BN, 2 BN)) from one N = 2 BN MMA per K step; wide, one
     // accumulator of BN columns
-    static constexpr uint32_t BUF_COLS = MODE == STRICT ? REGIONS * BN : WIDE ? BN : 2 * BN;
+    static constexpr uint32_t BUF_COLS = MODE == STRICT ? REGIONS * BN : ONEACC ? BN : 2 * BN;
     static constexpr int TBUFS = (512 / BUF_COLS) > 4 ? 4 : (512 / BUF_COLS);  // TMEM buffers in the ring
     static constexpr uint32_t TMEM_COLS = TBUFS * BUF_COLS;
     // fixed part; a B-resident launch adds its B panel (b_res_bytes) in front of the stages
@@ -629,6 +634,14 @@ __global__ void __launch_bounds__(THREADS, 1) umma_gemm_kernel(const __grid_cons
     const int unit = PAIR ? (int)cluster_index() : (int)blockIdx.x;
     const int units = PAIR ? (int)cluster_count() : (int)gridDim.x;
     const int row0 = (int)rank * BM;  // this CTA's first row within a tile
+    // DYN: M tile mt of the flattened batch -> first row within its batch and the two batch
+    // coordinates of the 4-D tensor maps
+    auto dyn_rows = [&](int mt, int &m0, int &b1, int &b2) {
+        const int bt = mt / p.m_per_batch;
+        m0 = (mt - bt * p.m_per_batch) * BM;
+        b2 = bt / p.nbatch1;
+        b1 = bt - b2 * p.nbatch1;
+    };
     // the i-th tile of this CTA (or pair) as (M tile, N tile); false past the last
     auto tile_at = [&](int i, int &mt, int &nt) -> bool {
         if (RB) {
@@ -768,7 +781,9 @@ __global__ void __launch_bounds__(THREADS, 1) umma_gemm_kernel(const __grid_cons
                 }
             }
             for (int i = 0; ok && tile_at(i, mt, nt); ++i) {
-                const int n0 = nt * BN, m0 = mt * C::TM + row0;
+                const int n0 = nt * BN;
+                int m0 = mt * C::TM + row0, db1 = 0, db2 = 0;
+                if (MODE == DYN) dyn_rows(mt, m0, db1, db2);
                 int wb = 0, hb = 0, nb = 0;
                 if (p.im2col) {
                     const int hw = p.OH * p.OW;
@@ -811,6 +826,8 @@ __global__ void __launch_bounds__(THREADS, 1) umma_gemm_kernel(const __grid_cons
                         }
                     } else if (PAIR) {
                         tma_load_2d_pair(a_tile(s), &p.tmA, leader_addr(&full[s]), kb * BK, m0);
+                    } else if (MODE == DYN) {
+                        tma_load_4d(a_tile(s), &p.tmA, &full[s], kb * BK, m0, db1, db2);
                     } else {
                         tma_load_2d(a_tile(s), &p.tmA, &full[s], kb * BK, m0);
                     }
@@ -835,6 +852,8 @@ __global__ void __launch_bounds__(THREADS, 1) umma_gemm_kernel(const __grid_cons
             bool free_next = false;  // that stage was tested free
             int mt, nt;
             for (int i = 0; ok && tile_at(i, mt, nt); ++i) {
+                int dm0 = 0, db1 = 0, db2 = 0;
+                if (MODE == DYN) dyn_rows(mt, dm0, db1, db2);
                 for (int kb = 0; kb < num_kb; ++kb, pos.advance()) {
                     const int s = pos.slot;
                     if (pos.wrapped && !free_next && !mbar_wait(&empty[s], pos.phase ^ 1u)) {
@@ -844,8 +863,11 @@ __global__ void __launch_bounds__(THREADS, 1) umma_gemm_kernel(const __grid_cons
                     }
                     const RingPos<S> nx = pos.next();
                     free_next = !nx.wrapped || mbar_test_wait(&empty[nx.slot], nx.phase ^ 1u);
-                    // a pair: this rank's plane, or (wide) both planes of this rank's 128 rows
-                    if (C::WIDE)
+                    // a pair: this rank's plane, or (wide) both planes of this rank's 128 rows;
+                    // DYN: the batch's B rows
+                    if (MODE == DYN)
+                        tma_load_4d(b_tile(s, kb), &p.tmB, &full[s], kb * BK, nt * BN, db1, db2);
+                    else if (C::WIDE)
                         tma_load_3d_pair(b_tile(s, kb), &p.tmB, leader_addr(&full[s]), kb * BK,
                                          nt * BN + (int)rank * C::BROWS, 0);
                     else if (PAIR)
@@ -859,8 +881,8 @@ __global__ void __launch_bounds__(THREADS, 1) umma_gemm_kernel(const __grid_cons
         if (lane == 0 && rank == 0) {
             // ---------------- MMA issuer (a pair's rank 0 issues for both CTAs) ----------------
             constexpr uint32_t idesc = instr_desc_tf32(BN);
-            // the stacked [B_hi; B_lo] tile, or (wide) one plane of all BN columns
-            constexpr uint32_t idesc2 = instr_desc_tf32(C::WIDE ? BN : 2 * BN, C::TM);
+            // the stacked [B_hi; B_lo] tile, or (wide, DYN) one plane of all BN columns
+            constexpr uint32_t idesc2 = instr_desc_tf32(C::ONEACC ? BN : 2 * BN, C::TM);
             RingPos<S> pos;   // stage of the next K block
             RingPos<TB> buf;  // TMEM buffer of the next K-block group
             bool ok = true;
@@ -995,11 +1017,11 @@ __global__ void __launch_bounds__(THREADS, 1) umma_gemm_kernel(const __grid_cons
                 uint32_t vh[32], vl[32];
                 const uint32_t addr = lane_base + (uint32_t)(b * C::BUF_COLS + h * EN + c0);
                 tmem_ld32(addr, vh);
-                if (!C::WIDE) tmem_ld32(addr + BN, vl);
+                if (!C::ONEACC) tmem_ld32(addr + BN, vl);
                 tmem_wait_ld();
 #pragma unroll
                 for (int j = 0; j < 32; ++j)
-                    acc[c0 + j] = C::WIDE ? __uint_as_float(vh[j]) : __uint_as_float(vh[j]) + __uint_as_float(vl[j]);
+                    acc[c0 + j] = C::ONEACC ? __uint_as_float(vh[j]) : __uint_as_float(vh[j]) + __uint_as_float(vl[j]);
             }
             if (h == NH - 1) release(b);
             return true;
@@ -1090,7 +1112,8 @@ __global__ void __launch_bounds__(THREADS, 1) umma_gemm_kernel(const __grid_cons
         if (res_tma && issuer && tile_at(0, mt, nt)) issue_residual(mt, nt, 0);
         int local = 0;  // epilogue passes this CTA has finished
         for (int i = 0; ok && tile_at(i, mt, nt); ++i) {
-          const int m0 = mt * C::TM + row0;
+          int m0 = mt * C::TM + row0, db1 = 0, db2 = 0;
+          if (MODE == DYN) dyn_rows(mt, m0, db1, db2);
           if (MODE == STRICT) {
 #pragma unroll
             for (int j = 0; j < HALF; ++j) acc[j] = AccT(0);
@@ -1209,8 +1232,10 @@ __global__ void __launch_bounds__(THREADS, 1) umma_gemm_kernel(const __grid_cons
                     } else if (m0 < p.M && n0 < p.N) {  // (a pair's second half, or a wide tile's last
                                                          // passes, may lie wholly past the edge)
 #pragma unroll 1
-                        for (int sl = 0; sl < EN / 32; ++sl)
-                            tma_store_2d(&p.tmC, out_tile + sl * (BM * 128), n0 + sl * 32, m0);
+                        for (int sl = 0; sl < EN / 32; ++sl) {
+                            if (MODE == DYN) tma_store_4d(&p.tmC, out_tile + sl * (BM * 128), n0 + sl * 32, m0, db1, db2);
+                            else tma_store_2d(&p.tmC, out_tile + sl * (BM * 128), n0 + sl * 32, m0);
+                        }
                     }
                     if (SR) {
                         tma_store_commit();  // read out before the next pass writes the staging tile
@@ -1363,6 +1388,22 @@ inline bool make_map_rows(CUtensorMap *map, const void *base, long long n, long 
 
 // Dynamic shared memory of a launch. Pair launches ask for more than half an SM's shared memory,
 // so no two CTAs (and no two TMEM allocations) ever share an SM.
+// fp32 tensor [b2][b1][rows][cols] with element strides (row, b1, b2) as a 4-D map {cols, rows, b1,
+// b2}, boxes {32, box_rows, 1, 1}; TFLOAT32 rounds to the nearest TF32 value on load.
+inline bool make_map_4d(CUtensorMap *map, const void *base, long long cols, long long rows, long long b1, long long b2,
+                        long long row_stride, long long b1_stride, long long b2_stride, int box_rows, bool tf32) {
+    auto fn = encode_tiled_fn();
+    if (!fn) return false;
+    cuuint64_t dims[4] = {(cuuint64_t)cols, (cuuint64_t)rows, (cuuint64_t)b1, (cuuint64_t)b2};
+    cuuint64_t strides[3] = {(cuuint64_t)(row_stride * 4), (cuuint64_t)(b1_stride * 4), (cuuint64_t)(b2_stride * 4)};
+    cuuint32_t box[4] = {(cuuint32_t)BK, (cuuint32_t)box_rows, 1, 1};
+    cuuint32_t estr[4] = {1, 1, 1, 1};
+    CUresult r = fn(map, tf32 ? CU_TENSOR_MAP_DATA_TYPE_TFLOAT32 : CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4,
+                    const_cast<void *>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                    CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    return r == CUDA_SUCCESS;
+}
+
 template <int BN, int MODE, int RB, int PAIR, int SR = 0>
 inline uint32_t launch_smem(const Params &p) {
     using C = Cfg<BN, MODE, RB, PAIR, SR>;
@@ -1498,12 +1539,66 @@ inline int launch_pair(Params &p, int clusters, cudaStream_t stream) {
 
 }  // namespace umma
 
+// Batched GEMM with a dynamic B (attention's Q K^T and P V; any batched MatMul of activations):
+// TF32 mode, both operands K-major (k contiguous) and rounded to TF32 by their tensor maps, one or
+// two batch dimensions with strides TMA can address (no broadcast), no bias / residual /
+// activation. Each tile lies inside one batch, so rows past M are clipped per batch.
+inline int try_gemm_umma_dyn(const GemmParams &p, cudaStream_t stream, int *taken) {
+    *taken = 0;
+    if (p.precision != MGC_PREC_TF32 || p.nb < 1 || p.nb > 2 || p.b_umma || p.b_lo) return MGC_CUDA_OK;
+    if (p.a_kind != MGC_STRIDED || p.b_kind != MGC_STRIDED || p.a_cs != 1 || p.b_rs != 1) return MGC_CUDA_OK;
+    if (p.bias || p.res || p.act != MGC_ACT_NONE || p.alpha != 1.0f || p.M <= 0 || p.N <= 0 || p.K <= 0)
+        return MGC_CUDA_OK;
+    auto al = [](const void *q) { return (reinterpret_cast<uintptr_t>(q) & 15) == 0; };
+    auto st = [](long long v) { return v > 0 && (v & 3) == 0; };  // a 16-byte multiple, not a broadcast
+    if (!al(p.a) || !al(p.b) || !al(p.c) || !st(p.a_rs) || !st(p.b_cs) || !st(p.ldc) || (p.K & 3) || (p.N & 3))
+        return MGC_CUDA_OK;
+    const long long b1 = p.bdims[0], b2 = p.nb == 2 ? p.bdims[1] : 1;
+    if (b1 <= 0 || b2 <= 0) return MGC_CUDA_OK;
+    for (int d = 0; d < p.nb; ++d)
+        if (!st(p.a_bs[d]) || !st(p.b_bs[d]) || !st(p.c_bs[d])) return MGC_CUDA_OK;
+    // strides of a second batch dimension of extent 1 (unused): any valid value
+    const long long a2 = p.nb == 2 ? p.a_bs[1] : p.a_bs[0] * b1, bb2 = p.nb == 2 ? p.b_bs[1] : p.b_bs[0] * b1;
+    const long long c2 = p.nb == 2 ? p.c_bs[1] : p.c_bs[0] * b1;
+    const int bn = p.N <= 64 ? 64 : 128;
+    umma::Params u;
+    memset(&u, 0, sizeof u);
+    if (!umma::make_map_4d(&u.tmA, p.a, p.K, p.M, b1, b2, p.a_rs, p.a_bs[0], a2, umma::BM, true) ||
+        !umma::make_map_4d(&u.tmB, p.b, p.K, p.N, b1, b2, p.b_cs, p.b_bs[0], bb2, bn, true) ||
+        !umma::make_map_4d(&u.tmC, p.c, p.N, p.M, b1, b2, p.ldc, p.c_bs[0], c2, umma::BM, false))
+        return MGC_CUDA_OK;
+    const long long m_per = ceil_div(p.M, umma::BM), tiles_m = m_per * b1 * b2;
+    const long long n_tiles = ceil_div(p.N, bn);
+    if (tiles_m * n_tiles > 0x7FFFFFFF) return MGC_CUDA_OK;
+    u.M = p.M;
+    u.N = p.N;
+    u.num_kb = (int)ceil_div(p.K, umma::BK);
+    u.n_tiles = (int)n_tiles;
+    u.m_tiles = (int)tiles_m;
+    u.m_per_batch = (int)m_per;
+    u.nbatch1 = (int)b1;
+    u.a_bytes = umma::A_TILE_BYTES;
+    u.tma_out = 1;
+    u.c = p.c; u.ldc = p.ldc;
+    u.alpha = 1.0f; u.lo = p.lo; u.hi = p.hi; u.act = MGC_ACT_NONE;
+    u.err = p.err;
+    const int sms = sm_count();
+    const long long tiles = tiles_m * n_tiles;
+    const int grid = (int)(tiles < sms ? tiles : sms);
+    const int rc = bn == 64 ? umma::launch<64, umma::DYN, 0, 0>(u, grid, stream)
+                            : umma::launch<128, umma::DYN, 0, 0>(u, grid, stream);
+    if (rc != MGC_CUDA_OK) return rc;
+    *taken = 1;
+    return MGC_CUDA_OK;
+}
+
 // Whether the tensor-core kernel takes this GEMM, and its launch. Requirements: tf32 or 3xtf32
 // precision, no batch dimensions, a constant K-major B in the layout the lowering provides
 // (b_umma + b_umma_lo), A as a unit-stride row-major matrix or an NHWC im2col operand with
 // 16-byte aligned rows, bias per column (or none), fp32 output.
 inline int try_gemm_umma(const GemmParams &p, cudaStream_t stream, int *taken) {
     *taken = 0;
+    if (p.nb != 0 && !p.b_umma) return try_gemm_umma_dyn(p, stream, taken);
     if (p.precision == MGC_PREC_FP32 || p.nb != 0 || !p.b_umma || !p.b_umma_lo || p.M <= 0 || p.N <= 0 || p.K <= 0)
         return MGC_CUDA_OK;
     if (p.bias && p.bias_mode != 1) return MGC_CUDA_OK;

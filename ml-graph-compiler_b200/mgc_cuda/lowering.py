@@ -234,6 +234,8 @@ class CudaEmitter:
         self.workspace_bytes = 0  # scratch regions (im2col patch matrices, channel-packed images)
         self._im2col_bytes = 0    # the im2col region at offset 0, shared by every im2col launch
         self._packed: dict[int, RefT] = {}  # id(value) -> its channel-packed copy in the workspace
+        # id(value) -> (source, element strides) of a Transpose that MatMul reads through (not copied)
+        self._through: dict[int, tuple[Value, list[int]]] = {}
         self._pack_regions: list[tuple[int, int]] = []  # (offset, bytes) of each packed image
 
     # -- references ----------------------------------------------------------------------------
@@ -423,12 +425,55 @@ class CudaEmitter:
         self._copy(out_shape, self.ref(src), _broadcast_strides(t.shape, out_shape), 0, dst_ref,
                    dst_strides, dst_base, t.itemsize, count)
 
+    def _arena_range(self, value: Value) -> tuple[int, int] | None:
+        loc = self.plan.location(value)
+        if loc.kind != "arena":
+            return None
+        root = self._root(value)
+        return loc.index, loc.index + root.tensor_type.nbytes
+
+    def _read_through(self, node: Node, x: Value, view_strides: list[int]) -> bool:
+        """Whether the batched MatMul(s) using this Transpose's output can read its source through
+        strides instead of a copy (TF32 mode, where the tensor-core batched GEMM takes strided
+        operands): every user is a MatMul that finds k (A) or k or n (B) contiguous in the view,
+        the output is no graph output, and no node scheduled before the last such MatMul writes
+        memory the source occupies (the planner may reuse it once the Transpose has run)."""
+        out = node.output
+        if self.precision != "tf32" or out.tensor_type.rank < 3 or x.tensor_type.dtype != "float32":
+            return False
+        if any(v is out for _, v in self.graph.named_outputs()) or not out.users:
+            return False
+        for user in out.users:
+            if user.op != "MatMul" or user.input(0).tensor_type.rank < 3 or user.input(1).tensor_type.rank < 3:
+                return False
+            if user.input(0) is out and view_strides[-1] != 1:
+                return False
+            if user.input(1) is out and view_strides[-1] != 1 and view_strides[-2] != 1:
+                return False
+        src = self.plan.location(x)
+        if src.kind not in ("arena", "input"):
+            return False
+        own = self._arena_range(x)
+        order = {id(n): k for k, n in enumerate(self.graph.nodes)}
+        last = max(order[id(u)] for u in out.users)
+        for later in self.graph.nodes[order[id(node)] + 1 : last]:
+            if later.op in ALIAS_OPS:
+                continue
+            for v in later.outputs:
+                r = self._arena_range(v)
+                if own is not None and r is not None and r[0] < own[1] and own[0] < r[1]:
+                    return False
+        return True
+
     def op_Transpose(self, node: Node) -> None:
         x = node.input(0)
         perm = ops.transpose_perm(node, x.tensor_type.rank)
         ss = _strides(x.tensor_type.shape)
         shape = node.output.tensor_type.shape
         out = node.output
+        if self._read_through(node, x, [ss[p] for p in perm]):
+            self._through[id(out)] = (x, [ss[p] for p in perm])
+            return
         users = out.users
         if (len(users) == 1 and users[0].inputs and users[0].inputs[0] is out and self._tap_packed(users[0])
                 and all(v is not out for _, v in self.graph.named_outputs())):
@@ -880,6 +925,14 @@ class CudaEmitter:
         self._gemm(m, n, k, self.ref(a), a_rs, a_cs, bref, b_rs, b_cs, self.ref(node.output), n, b_lo=blo, **self._umma_b(bref, blo),
                    alpha=alpha, beta=beta, bias=bias, bias_mode=mode, res=res, ldr=ldr)
 
+    def _view(self, value: Value) -> tuple[RefT, list[int]]:
+        """Reference and per-dimension element strides of a MatMul operand: its own contiguous
+        buffer, or the source of a Transpose read through."""
+        if id(value) in self._through:
+            src, strides = self._through[id(value)]
+            return self.ref(src), list(strides)
+        return self.ref(value), _strides(value.tensor_type.shape)
+
     def op_MatMul(self, node: Node) -> None:
         a, b = node.input(0), node.input(1)
         at, bt = a.tensor_type, b.tensor_type
@@ -889,18 +942,47 @@ class CudaEmitter:
         m, k = ashape[-2], ashape[-1]
         n = bshape[-1]
         batch_shape = [int(d) for d in np.broadcast_shapes(ashape[:-2], bshape[:-2])]
-        a_bs = [s * m * k for s in _broadcast_strides(ashape[:-2], batch_shape)]
-        b_bs = [s * k * n for s in _broadcast_strides(bshape[:-2], batch_shape)]
+        aref, av = self._view(a) if at.rank >= 2 else (self.ref(a), [k, 1])
+        if bt.rank == 1:
+            bref, bv = self.ref(b), [1, 1]
+        else:
+            bref, bv = self._view(b)
+        a_rs, a_cs = av[-2], av[-1]
+        b_rs, b_cs = bv[-2], bv[-1]
+
+        def batch_strides(shape: Sequence[int], view: list[int]) -> list[int]:
+            # the view's strides of the broadcast batch dimensions (0 where broadcast)
+            own = list(shape[:-2])
+            lead = len(batch_shape) - len(own)
+            out = []
+            for d, extent in enumerate(batch_shape):
+                j = d - lead
+                out.append(0 if j < 0 or own[j] == 1 and extent != 1 else (view[j] if j < len(view) - 2 else 0))
+            return out
+
+        a_bs = batch_strides(ashape, av if at.rank >= 2 else [0, 0])
+        b_bs = batch_strides(bshape, bv if bt.rank >= 2 else [0, 0])
         c_bs = [s * m * n for s in _strides(batch_shape)]
-        dims, (a_bs, b_bs, c_bs) = _collapse(batch_shape, [a_bs, b_bs, c_bs])
         bconst = b.is_constant or self.plan.location(b).kind == "const"
-        if bconst and not any(b_bs):
+        if bconst and not any(b_bs) and id(b) not in self._through:
             data = self.const_data(b).reshape(k, n)
             bref, blo, b_rs, b_cs = self._kmajor_b(data, ("kmajor", id(self._root(b)), 0))
         else:
-            bref, blo, b_rs, b_cs = self.ref(b), NO_REF, n, 1
-        self._gemm(m, n, k, self.ref(a), k, 1, bref, b_rs, b_cs, self.ref(node.output), n, b_lo=blo, **self._umma_b(bref, blo),
-                   batch=dims, a_bs=a_bs, b_bs=b_bs, c_bs=c_bs, r_bs=[0] * len(dims))
+            blo = NO_REF
+            if self.precision == "tf32" and batch_shape and b_cs == 1 and b_rs != 1 and bt.rank >= 3:
+                # N-major B: one transposed copy into the workspace (K-major, [batch][n][k]) for
+                # the tensor-core batched GEMM, which reads B rows along K
+                own = [int(d) for d in bshape[:-2]]
+                tshape = [*own, n, k]
+                self._copy(tshape, bref, [*bv[:-2], b_cs, b_rs], 0, (SPACE_WORKSPACE, 0, 0), _strides(tshape), 0, 4,
+                           count="transpose")
+                self._im2col_bytes = max(self._im2col_bytes, int(np.prod(tshape)) * 4)
+                self._layout_workspace()
+                bref, b_rs, b_cs = (SPACE_WORKSPACE, 0, 0), 1, k
+                b_bs = batch_strides(bshape, [*_strides(own + [n * k])[:-1], 0, 0] if own else [0, 0])
+        dims, (a_bs, b_bs, c_bs) = _collapse(batch_shape, [a_bs, b_bs, c_bs])
+        self._gemm(m, n, k, aref, a_rs, a_cs, bref, b_rs, b_cs, self.ref(node.output), n, b_lo=blo,
+                   **self._umma_b(bref, blo), batch=dims, a_bs=a_bs, b_bs=b_bs, c_bs=c_bs, r_bs=[0] * len(dims))
 
     @staticmethod
     def _depthwise(node: Node) -> bool:

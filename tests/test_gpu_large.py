@@ -119,3 +119,40 @@ def test_tf32_gemm_keeps_weights_exact(form: str) -> None:
     want = x.astype(np.float64) @ w.astype(np.float64) + bias.astype(np.float64)
     err = float(np.abs(got - want).max() / np.abs(want).max())
     assert err <= 2e-5, f"{form}: max error {err:.3g} of the largest output"
+
+
+def test_tf32_batched_matmul_of_activations_is_exact_for_tf32_inputs() -> None:
+    """Attention-shaped batched MatMuls on the tensor cores: Q K^T with both operands read through
+    their head Transposes (two batch dimensions, strided rows), and P V with V N-major (copied
+    K-major into the workspace). With TF32-exact inputs the only error left is the fp32
+    accumulation (within 2e-5 of the largest output)."""
+    r = np.random.default_rng(13)
+    b, s, h, d = 2, 128, 12, 64
+
+    def exact(*shape: int) -> np.ndarray:
+        return _tf32_exact(r.standard_normal(shape).astype(np.float32))
+
+    g = Graph("attention_matmuls")
+    q = g.add_input("q", TensorType("float32", (b, s, h, d)))
+    k = g.add_input("k", TensorType("float32", (b, s, h, d)))
+    v = g.add_input("v", TensorType("float32", (b, s, h, d)))
+    pr = g.add_input("p", TensorType("float32", (b, h, s, s)))
+    qt = g.add_node("Transpose", [q], attrs={"perm": [0, 2, 1, 3]}).output
+    kt = g.add_node("Transpose", [k], attrs={"perm": [0, 2, 3, 1]}).output
+    vt = g.add_node("Transpose", [v], attrs={"perm": [0, 2, 1, 3]}).output
+    g.add_output(g.add_node("MatMul", [qt, kt]).output, "scores")
+    g.add_output(g.add_node("MatMul", [pr, vt]).output, "context")
+    infer_shapes(g)
+    optimize(g, "O3")
+    schedule(g)
+    feeds = {"q": exact(b, s, h, d), "k": exact(b, s, h, d), "v": exact(b, s, h, d), "p": exact(b, h, s, s)}
+    model = compile_graph(g, precision="tf32")
+    try:
+        got = model.run(feeds)
+    finally:
+        model.close()
+    q64, k64, v64 = (feeds[n].astype(np.float64).transpose(0, 2, 1, 3) for n in ("q", "k", "v"))
+    want = {"scores": q64 @ k64.transpose(0, 1, 3, 2), "context": feeds["p"].astype(np.float64) @ v64}
+    for name, w in want.items():
+        err = float(np.abs(got[name].astype(np.float64) - w).max() / np.abs(w).max())
+        assert err <= 2e-5, f"{name}: max error {err:.3g} of the largest output"
