@@ -320,6 +320,128 @@ __global__ void __launch_bounds__(256) ew_kernel(const __grid_constant__ EwParam
     }
 }
 
+// One fp32 instruction of an all-fp32 program: the fp32 branches of ew_eval, operand for operand
+// (ew_f32_ok below lists the operators this covers).
+__device__ __forceinline__ float ew_f32(const EwInstr &in, float x, float y, float z) {
+    switch (in.op) {
+    case EW_ADD: return x + y;
+    case EW_SUB: return x - y;
+    case EW_MUL: return x * y;
+    case EW_DIV: return x / y;
+    case EW_POW: return powf(x, y);
+    case EW_MAX: return fmaxf(x, y);
+    case EW_MIN: return fminf(x, y);
+    case EW_CLIP: {
+        const float lo = in.a[1] >= 0 ? y : (float)in.imm[0];
+        const float hi = in.a[2] >= 0 ? z : (float)in.imm[1];
+        return fminf(fmaxf(x, lo), hi);
+    }
+    case EW_RELU: return fmaxf(x, 0.0f);
+    case EW_SIGMOID: return f_sigmoid(x);
+    case EW_TANH: return tanhf(x);
+    case EW_ERF: return erff(x);
+    case EW_SQRT: return sqrtf(x);
+    case EW_EXP: return expf(x);
+    case EW_LOG: return logf(x);
+    case EW_NEG: return -x;
+    case EW_ABS: return fabsf(x);
+    case EW_RECIP: return 1.0f / x;
+    case EW_FLOOR: return floorf(x);
+    case EW_CEIL: return ceilf(x);
+    case EW_SIN: return sinf(x);
+    case EW_COS: return cosf(x);
+    case EW_SOFTPLUS: return f_softplus(x);
+    case EW_GELU: return in.imm[0] != 0.0 ? f_gelu_tanh(x) : f_gelu(x);
+    case EW_LEAKYRELU: return x >= 0.0f ? x : (float)in.imm[0] * x;
+    case EW_HARDSIGMOID: return fminf(fmaxf((float)in.imm[0] * x + (float)in.imm[1], 0.0f), 1.0f);
+    default: return x;  // EW_IDENTITY, EW_CAST
+    }
+}
+
+__host__ __device__ inline bool ew_f32_op(int op) {
+    return op <= EW_MIN || op == EW_CLIP || (op >= EW_RELU && op <= EW_SOFTPLUS) || op == EW_IDENTITY ||
+           op == EW_GELU || op == EW_LEAKYRELU || op == EW_HARDSIGMOID || op == EW_CAST;
+}
+
+// Index arithmetic of the four-wide forms: element 4v of the output in 32-bit arithmetic, one
+// offset per leaf (the innermost index is a multiple of 4, so a leaf of innermost stride 1 reads
+// elements off..off+3 and one of stride 0 reads element off four times).
+__device__ __forceinline__ void ew_offsets4(const EwParams &P, unsigned v, unsigned *off) {
+    unsigned idx[EW_MAX_RANK];
+    unsigned rem = v << 2;
+    for (int d = P.rank - 1; d > 0; --d) {
+        const unsigned e = (unsigned)P.shape[d];
+        const unsigned q = rem / e;
+        idx[d] = rem - q * e;
+        rem = q;
+    }
+    idx[0] = rem;
+    for (int l = 0; l < P.nleaves; ++l) {
+        const EwLeaf &lf = P.leaves[l];
+        unsigned o = 0;
+        if (!lf.is_lit)
+            for (int d = 0; d < P.rank; ++d) o += idx[d] * (unsigned)lf.strides[d];
+        off[l] = o;
+    }
+}
+
+// An all-fp32 program (every leaf fp32, every instruction fp32 in and out) over four consecutive
+// output elements per thread: registers hold four lanes, a leaf of innermost stride 1 comes in
+// as one 16-byte load when `vec_leaf` has its bit (aligned base, outer strides multiples of 4),
+// the output leaves as one 16-byte store when `vec_out`.
+__global__ void __launch_bounds__(256) ew_f32x4_kernel(const __grid_constant__ EwParams P, const unsigned vec_leaf,
+                                                       const int vec_out) {
+    float4 regs[EW_MAX_LEAVES + EW_MAX_INSTR];
+    const unsigned total4 = (unsigned)(P.total >> 2);
+    const unsigned step = gridDim.x * blockDim.x;
+    const int last = P.rank - 1;
+    for (unsigned v = blockIdx.x * blockDim.x + threadIdx.x; v < total4; v += step) {
+        unsigned off[EW_MAX_LEAVES];
+        ew_offsets4(P, v, off);
+        for (int l = 0; l < P.nleaves; ++l) {
+            const EwLeaf &lf = P.leaves[l];
+            const float *p = (const float *)lf.p + off[l];
+            if (lf.is_lit) regs[l] = make_float4(lf.lit.f, lf.lit.f, lf.lit.f, lf.lit.f);
+            else if (lf.strides[last] == 0) { const float t = __ldg(p); regs[l] = make_float4(t, t, t, t); }
+            else if ((vec_leaf >> l) & 1u) regs[l] = __ldg(reinterpret_cast<const float4 *>(p));
+            else regs[l] = make_float4(__ldg(p), __ldg(p + 1), __ldg(p + 2), __ldg(p + 3));
+        }
+        for (int k = 0; k < P.ninstr; ++k) {
+            const EwInstr &in = P.ins[k];
+            const float4 x = regs[in.a[0]];
+            const float4 y = in.a[1] >= 0 ? regs[in.a[1]] : x;
+            const float4 z = in.a[2] >= 0 ? regs[in.a[2]] : x;
+            regs[P.nleaves + k] = make_float4(ew_f32(in, x.x, y.x, z.x), ew_f32(in, x.y, y.y, z.y),
+                                              ew_f32(in, x.z, y.z, z.z), ew_f32(in, x.w, y.w, z.w));
+        }
+        const float4 r = regs[P.nleaves + P.ninstr - 1];
+        float *o = (float *)P.out + (v << 2);
+        if (vec_out) *reinterpret_cast<float4 *>(o) = r;
+        else { o[0] = r.x; o[1] = r.y; o[2] = r.z; o[3] = r.w; }
+    }
+}
+
+// Any program over four consecutive output elements per thread: the index arithmetic of
+// ew_f32x4_kernel, then the registers and ew_eval of ew_kernel element by element.
+__global__ void __launch_bounds__(256) ew_vec4_kernel(const __grid_constant__ EwParams P) {
+    Reg regs[EW_MAX_LEAVES + EW_MAX_INSTR];
+    const unsigned total4 = (unsigned)(P.total >> 2);
+    const unsigned step = gridDim.x * blockDim.x;
+    const int last = P.rank - 1;
+    for (unsigned v = blockIdx.x * blockDim.x + threadIdx.x; v < total4; v += step) {
+        unsigned off[EW_MAX_LEAVES];
+        ew_offsets4(P, v, off);
+        for (int j = 0; j < 4; ++j) {
+            for (int l = 0; l < P.nleaves; ++l) {
+                const EwLeaf &lf = P.leaves[l];
+                regs[l] = lf.is_lit ? lf.lit : load_elem(lf.p, lf.dtype, off[l] + (lf.strides[last] ? j : 0));
+            }
+            for (int k = 0; k < P.ninstr; ++k) regs[P.nleaves + k] = ew_eval(P.ins[k], regs, P.cls);
+            store_elem(P.out, P.out_dt, (long long)(v << 2) + j, regs[P.nleaves + P.ninstr - 1]);
+        }
+    }
+}
+
 // ---------------------------------------------------------------------------------------------
 // strided copy: dst[dbase + sum idx*dstr] = src[sbase + sum idx*sstr] over `shape`
 // ---------------------------------------------------------------------------------------------

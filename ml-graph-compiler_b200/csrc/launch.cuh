@@ -306,8 +306,38 @@ inline int launch_record(const mgc_cuda_launch &L, const int64_t *aux, int64_t a
         EwParams P;
         MGC_CHECK(decode_elementwise(L, aux, aux_len, bases, P));
         if (P.total == 0) { launched = 0; break; }
-        ew_kernel<<<grid_for(P.total, 256), 256, 0, stream>>>(P);
-        st = check_launch("ew_kernel");
+        // four elements per thread when the innermost dimension comes in groups of four that every
+        // leaf reads contiguously or broadcasts, and all offsets fit 32 bits
+        bool vec = P.rank >= 1 && P.shape[P.rank - 1] % 4 == 0 && P.total < (1ll << 31);
+        bool f32 = P.out_dt == MGC_F32;
+        unsigned vec_leaf = 0;
+        for (int l = 0; vec && l < P.nleaves; ++l) {
+            const EwLeaf &lf = P.leaves[l];
+            f32 = f32 && lf.dtype == MGC_F32;
+            if (lf.is_lit) continue;
+            const long long inner = lf.strides[P.rank - 1];
+            long long span = 0;
+            bool quad = (reinterpret_cast<uintptr_t>(lf.p) & 15) == 0;
+            for (int d = 0; d < P.rank; ++d) {
+                vec = vec && lf.strides[d] >= 0;
+                span += (P.shape[d] - 1) * lf.strides[d];
+                if (d < P.rank - 1) quad = quad && lf.strides[d] % 4 == 0;
+            }
+            vec = vec && (inner == 0 || inner == 1) && span < (1ll << 31);
+            if (inner == 1 && quad) vec_leaf |= 1u << l;
+        }
+        for (int k = 0; f32 && k < P.ninstr; ++k) f32 = P.ins[k].out_dt == MGC_F32 && ew_f32_op(P.ins[k].op);
+        if (vec && f32) {
+            const int vec_out = (reinterpret_cast<uintptr_t>(P.out) & 15) == 0;
+            ew_f32x4_kernel<<<grid_for(P.total / 4, 256), 256, 0, stream>>>(P, vec_leaf, vec_out);
+            st = check_launch("ew_f32x4_kernel");
+        } else if (vec) {
+            ew_vec4_kernel<<<grid_for(P.total / 4, 256), 256, 0, stream>>>(P);
+            st = check_launch("ew_vec4_kernel");
+        } else {
+            ew_kernel<<<grid_for(P.total, 256), 256, 0, stream>>>(P);
+            st = check_launch("ew_kernel");
+        }
         break;
     }
     case MGC_K_COPY: {

@@ -117,6 +117,12 @@ def op_cases() -> list[Case]:
     C(_simple("compare_all", lambda r: _chain(r, "compare")))
     C(_simple("logic_all", lambda r: _chain(r, "logic")))
     C(_simple("where", lambda r: op_graph("Where", [("in", r.random((3, 4)) > 0.5), ("in", f32(r, 3, 4)), ("in", f32(r, 1, 4))])))
+    # innermost extents that are multiples of 4: the four-wide elementwise forms (all-fp32, and
+    # mixed dtypes), with leaves broadcast along the innermost and along outer dimensions
+    C(_simple("add_inner_bcast", lambda r: op_graph("Add", [("in", f32(r, 2, 3, 8, 12)), ("in", f32(r, 2, 1, 8, 1))])))
+    C(_simple("mul_outer_bcast", lambda r: op_graph("Mul", [("in", f32(r, 3, 1, 16)), ("const", f32(r, 5, 16))])))
+    C(_simple("where_mask", lambda r: op_graph("Where", [("in", r.random((1, 1, 8, 8)) > 0.5), ("in", f32(r, 2, 3, 8, 8)), ("const", np.float32(-1e9))])))
+    C(_simple("clip_inputs_quad", lambda r: op_graph("Clip", [("in", f32(r, 6, 8, scale=5)), ("in", np.float32(-1.5)), ("const", np.float32(2))])))
     C(_simple("cast_f2i", lambda r: op_graph("Cast", [("in", f32(r, 4, 5, scale=10))], {"to": 7})))
     C(_simple("cast_i2f", lambda r: op_graph("Cast", [("in", r.integers(-50, 50, (4, 5)))], {"to": 1})))
     C(_simple("cast_f2b", lambda r: op_graph("Cast", [("in", np.round(f32(r, 4, 5)))], {"to": 9})))
