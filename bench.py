@@ -12,6 +12,8 @@ weak scaling: every GPU runs its own batch of ``--batch`` images, no collectives
 * ``roofline``: the dominant kernel (the implicit-GEMM convolution / GEMM launches) from one
   eagerly launched pass with CUDA events around every launch, against MEASURED_PEAKS.json;
 * ``latency_b1``: batch-1 p50 latency (public API and device-only replay);
+* ``bert``: BERT-base sequence-128 batch-32 seq/s, device-timed replays and
+  through ``run``;
 * ``cpu_baseline``: the reference's own C backend (gcc + OpenMP) on this host's cores, on a
   bounded batch.
 
@@ -170,6 +172,51 @@ def build_r50(batch: int, seed: int = 4):
     return g
 
 
+def bert_throughput(precision: str, device: int, steps: int, warmup: int) -> dict:
+    """BERT-base, sequence 128, batch 32 (the metric's seq/s): CUDA Graph
+    replays with resident inputs timed with CUDA events on the model's stream, and the same
+    through ``run`` (token ids and mask uploaded, every output read back each step)."""
+    import torch
+
+    from mgc_cuda import zoo
+    from mgc_cuda.runtime import compile_graph
+    from ml_graph_compiler.passes import optimize
+    from ml_graph_compiler.schedule import schedule
+
+    batch, seq = 32, 128
+    g = zoo.bert(batch=batch, seq=seq, seed=2)
+    optimize(g, "O3")
+    schedule(g)
+    m = compile_graph(g, precision=precision, device=device)
+    feeds = zoo.feeds(g, 2)
+    outs = m.run(feeds)
+    stream = torch.cuda.ExternalStream(m.stream)
+    for _ in range(warmup):
+        m.run_device(sync=False)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for _ in range(steps):
+        m.run_device(sync=False)
+    e1.record(stream)
+    e1.synchronize()
+    ms = e0.elapsed_time(e1) / steps
+    for _ in range(2):
+        m.run(feeds)
+    t0 = time.perf_counter()
+    for _ in range(steps):
+        m.run(feeds)
+    e2e_s = (time.perf_counter() - t0) / steps
+    m.close()
+    return {
+        "metric": "BERT-base seq128 seq/s (batch 32, O3 graph)", "value": round(batch / (ms / 1e3), 2),
+        "unit": "seq/s", "ms_per_step": round(ms, 4), "steps": steps, "warmup": warmup,
+        "e2e": {"value": round(batch / e2e_s, 2), "unit": "seq/s",
+                "h2d_bytes_per_step": int(sum(np.asarray(v).nbytes for v in feeds.values())),
+                "d2h_bytes_per_step": int(sum(np.asarray(v).nbytes for v in outs.values()))},
+        "l2": "weights (hi + lo TF32 parts) and activations stream through HBM every step, larger than L2",
+    }
+
+
 def cpu_reference_run(batch: int, steps: int, warmup: int) -> dict:
     """The reference C backend on this host: compile_graph(O3 graph) with gcc + OpenMP."""
     os.environ.setdefault("MGC_CC", "/usr/bin/gcc")
@@ -224,6 +271,7 @@ def main() -> None:
     ap.add_argument("--cpu-batch", type=int, default=8, help="images of the cpu_baseline sample")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-latency", action="store_true")
+    ap.add_argument("--no-bert", action="store_true", help="skip the BERT-base seq/s measurement")
     ap.add_argument("--strategy", default="naive", choices=["greedy_by_size", "first_fit", "naive"],
                     help="the reference planner's memory strategy for the benchmark model; naive gives every "
                          "buffer its own memory (11.7 GB arena at batch 256), which lets run() upload the image in "
@@ -354,6 +402,9 @@ def main() -> None:
         line["latency_b1"] = {"p50_ms": round(statistics.median(ts) * 1e3, 4),
                               "device_p50_ms": round(statistics.median(dts), 4), "unit": "ms"}
         m1.close()
+
+    if rank == 0 and world == 1 and not args.no_bert:
+        line["bert"] = bert_throughput(args.precision, local, steps=20, warmup=3)
 
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         try:

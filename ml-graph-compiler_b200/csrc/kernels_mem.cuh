@@ -320,8 +320,10 @@ __global__ void __launch_bounds__(256) ew_kernel(const __grid_constant__ EwParam
     }
 }
 
-// One fp32 instruction of an all-fp32 program: the fp32 branches of ew_eval, operand for operand
-// (ew_f32_ok below lists the operators this covers).
+// One instruction of the four-wide fp32 form: the fp32 branches of ew_eval, operand for operand.
+// Byte values (bool, uint8) enter as the fp32 number of their value, which is what ew_eval's fp32
+// arithmetic, Cast and Where read of them (ew_f32x4_form lists the operators and operand classes
+// this covers).
 __device__ __forceinline__ float ew_f32(const EwInstr &in, float x, float y, float z) {
     switch (in.op) {
     case EW_ADD: return x + y;
@@ -331,6 +333,7 @@ __device__ __forceinline__ float ew_f32(const EwInstr &in, float x, float y, flo
     case EW_POW: return powf(x, y);
     case EW_MAX: return fmaxf(x, y);
     case EW_MIN: return fminf(x, y);
+    case EW_WHERE: return x != 0.0f ? y : z;
     case EW_CLIP: {
         const float lo = in.a[1] >= 0 ? y : (float)in.imm[0];
         const float hi = in.a[2] >= 0 ? z : (float)in.imm[1];
@@ -358,24 +361,70 @@ __device__ __forceinline__ float ew_f32(const EwInstr &in, float x, float y, flo
     }
 }
 
-__host__ __device__ inline bool ew_f32_op(int op) {
-    return op <= EW_MIN || op == EW_CLIP || (op >= EW_RELU && op <= EW_SOFTPLUS) || op == EW_IDENTITY ||
-           op == EW_GELU || op == EW_LEAKYRELU || op == EW_HARDSIGMOID || op == EW_CAST;
+// Whether a program runs in the four-wide fp32 form with the results of ew_eval: fp32 output and
+// instruction results; fp32 or byte (bool, uint8) tensor leaves and fp32 literals; byte values
+// only where ew_eval converts them to fp32 (an operand of binary fp32 arithmetic next to an fp32
+// one, a Where condition or branch, a Cast or Identity, a Clip bound).
+inline bool ew_f32x4_form(const EwParams &P) {
+    if (P.out_dt != MGC_F32) return false;
+    for (int l = 0; l < P.nleaves; ++l) {
+        const EwLeaf &lf = P.leaves[l];
+        if (lf.is_lit ? lf.dtype != MGC_F32 : (lf.dtype != MGC_F32 && lf.dtype != MGC_BOOL && lf.dtype != MGC_U8))
+            return false;
+    }
+    for (int k = 0; k < P.ninstr; ++k) {
+        const EwInstr &in = P.ins[k];
+        if (in.out_dt != MGC_F32) return false;
+        const int op = in.op;
+        const bool f0 = P.cls[in.a[0]] == CL_F, f1 = in.a[1] >= 0 && P.cls[in.a[1]] == CL_F;
+        if (op <= EW_MIN) {
+            if (!f0 && !f1) return false;
+        } else if (op == EW_WHERE) {
+            if (f0) return false;  // an fp32 condition truncates to an integer in ew_eval
+        } else if (op == EW_CLIP || (op >= EW_RELU && op <= EW_SOFTPLUS) || op == EW_GELU ||
+                   op == EW_LEAKYRELU || op == EW_HARDSIGMOID) {
+            if (!f0) return false;
+        } else if (op != EW_IDENTITY && op != EW_CAST) {
+            return false;
+        }
+    }
+    return true;
 }
 
-// Index arithmetic of the four-wide forms: element 4v of the output in 32-bit arithmetic, one
-// offset per leaf (the innermost index is a multiple of 4, so a leaf of innermost stride 1 reads
-// elements off..off+3 and one of stride 0 reads element off four times).
-__device__ __forceinline__ void ew_offsets4(const EwParams &P, unsigned v, unsigned *off) {
-    unsigned idx[EW_MAX_RANK];
-    unsigned rem = v << 2;
-    for (int d = P.rank - 1; d > 0; --d) {
-        const unsigned e = (unsigned)P.shape[d];
-        const unsigned q = rem / e;
-        idx[d] = rem - q * e;
-        rem = q;
+// Whether the four-wide forms apply: the innermost dimension comes in groups of four that every
+// tensor leaf reads contiguously (stride 1) or broadcasts (stride 0), strides are non-negative and
+// every offset fits 32 bits. Bit l of vec_leaf: leaf l of stride 1 whose groups of four start on
+// 16 bytes (aligned base, outer strides multiples of 4).
+inline bool ew_vec4_form(const EwParams &P, unsigned &vec_leaf) {
+    vec_leaf = 0;
+    if (P.rank < 1 || P.shape[P.rank - 1] % 4 != 0 || P.total >= (1ll << 31)) return false;
+    for (int l = 0; l < P.nleaves; ++l) {
+        const EwLeaf &lf = P.leaves[l];
+        if (lf.is_lit) continue;
+        const long long inner = lf.strides[P.rank - 1];
+        long long span = 0;
+        bool quad = lf.dtype == MGC_F32 && (reinterpret_cast<uintptr_t>(lf.p) & 15) == 0;
+        for (int d = 0; d < P.rank; ++d) {
+            if (lf.strides[d] < 0) return false;
+            span += (P.shape[d] - 1) * lf.strides[d];
+            if (d < P.rank - 1) quad = quad && lf.strides[d] % 4 == 0;
+        }
+        if ((inner != 0 && inner != 1) || span >= (1ll << 31)) return false;
+        if (inner == 1 && quad) vec_leaf |= 1u << l;
     }
-    idx[0] = rem;
+    return true;
+}
+
+// Offsets of every leaf at output element e (32-bit arithmetic; ew_vec4_form bounds them).
+__device__ __forceinline__ void ew_offsets(const EwParams &P, unsigned e, unsigned *off) {
+    unsigned idx[EW_MAX_RANK];
+    for (int d = P.rank - 1; d > 0; --d) {
+        const unsigned n = (unsigned)P.shape[d];
+        const unsigned q = e / n;
+        idx[d] = e - q * n;
+        e = q;
+    }
+    idx[0] = e;
     for (int l = 0; l < P.nleaves; ++l) {
         const EwLeaf &lf = P.leaves[l];
         unsigned o = 0;
@@ -385,36 +434,175 @@ __device__ __forceinline__ void ew_offsets4(const EwParams &P, unsigned v, unsig
     }
 }
 
-// An all-fp32 program (every leaf fp32, every instruction fp32 in and out) over four consecutive
-// output elements per thread: registers hold four lanes, a leaf of innermost stride 1 comes in
-// as one 16-byte load when `vec_leaf` has its bit (aligned base, outer strides multiples of 4),
-// the output leaves as one 16-byte store when `vec_out`.
+// Four consecutive values of a leaf from its offset: a literal, a broadcast (innermost stride 0),
+// one 16-byte load (`quad`) or four loads; byte leaves as the fp32 number of their value.
+__device__ __forceinline__ float4 ew_leaf4(const EwLeaf &lf, unsigned off, bool bcast, bool quad) {
+    if (lf.is_lit) return make_float4(lf.lit.f, lf.lit.f, lf.lit.f, lf.lit.f);
+    if (lf.dtype == MGC_F32) {
+        const float *p = (const float *)lf.p + off;
+        if (bcast) { const float t = __ldg(p); return make_float4(t, t, t, t); }
+        if (quad) return __ldg(reinterpret_cast<const float4 *>(p));
+        return make_float4(__ldg(p), __ldg(p + 1), __ldg(p + 2), __ldg(p + 3));
+    }
+    const unsigned char *b = (const unsigned char *)lf.p + off;
+    if (bcast) { const float t = (float)__ldg(b); return make_float4(t, t, t, t); }
+    return make_float4((float)__ldg(b), (float)__ldg(b + 1), (float)__ldg(b + 2), (float)__ldg(b + 3));
+}
+
+// The program over the four elements whose leaf offsets are off[] (ew_f32x4_form programs);
+// `regs` is the caller's register file of four-lane values.
+__device__ __forceinline__ float4 ew_run4(const EwParams &P, const unsigned *off, unsigned vec_leaf, float4 *regs) {
+    const int last = P.rank - 1;
+    for (int l = 0; l < P.nleaves; ++l)
+        regs[l] = ew_leaf4(P.leaves[l], off[l], P.leaves[l].strides[last] == 0, (vec_leaf >> l) & 1u);
+    for (int k = 0; k < P.ninstr; ++k) {
+        const EwInstr &in = P.ins[k];
+        const float4 x = regs[in.a[0]];
+        const float4 y = in.a[1] >= 0 ? regs[in.a[1]] : x;
+        const float4 z = in.a[2] >= 0 ? regs[in.a[2]] : x;
+        regs[P.nleaves + k] = make_float4(ew_f32(in, x.x, y.x, z.x), ew_f32(in, x.y, y.y, z.y),
+                                          ew_f32(in, x.z, y.z, z.z), ew_f32(in, x.w, y.w, z.w));
+    }
+    return regs[P.nleaves + P.ninstr - 1];
+}
+
+// Whether a program is a chain: every operand is a leaf or the result of the instruction just
+// before, so the four-wide form needs no register file: one accumulator, and each leaf loaded
+// where an instruction uses it (the attention scale and mask, embedding sums, mask arithmetic).
+inline bool ew_chain_form(const EwParams &P) {
+    for (int k = 0; k < P.ninstr; ++k)
+        for (int j = 0; j < 3; ++j) {
+            const int a = P.ins[k].a[j];
+            if (a >= P.nleaves && a != P.nleaves + k - 1) return false;
+        }
+    return true;
+}
+
+// Output coordinates of element e; the loops unroll over EW_MAX_RANK so idx stays in registers.
+__device__ __forceinline__ void ew_coords(const EwParams &P, unsigned e, unsigned (&idx)[EW_MAX_RANK]) {
+#pragma unroll
+    for (int d = EW_MAX_RANK - 1; d > 0; --d) {
+        if (d < P.rank) {
+            const unsigned n = (unsigned)P.shape[d];
+            const unsigned q = e / n;
+            idx[d] = e - q * n;
+            e = q;
+        } else {
+            idx[d] = 0;
+        }
+    }
+    idx[0] = e;
+}
+
+__device__ __forceinline__ unsigned ew_leaf_offset(const EwParams &P, int l, const unsigned (&idx)[EW_MAX_RANK]) {
+    const EwLeaf &lf = P.leaves[l];
+    unsigned o = 0;
+#pragma unroll
+    for (int d = 0; d < EW_MAX_RANK; ++d)
+        if (d < P.rank) o += idx[d] * (unsigned)lf.strides[d];
+    return o;
+}
+
+__device__ __forceinline__ float4 ew_f32x4(const EwInstr &in, float4 x, float4 y, float4 z) {
+    return make_float4(ew_f32(in, x.x, y.x, z.x), ew_f32(in, x.y, y.y, z.y), ew_f32(in, x.z, y.z, z.z),
+                       ew_f32(in, x.w, y.w, z.w));
+}
+
+// One instruction of a chain program (ew_chain_form, ew_f32x4_form) over G groups of four
+// elements: operands are fetched for every live group (fetch(l, g): the four values of leaf l
+// for group g; an operand that is no leaf is the accumulator), then one switch on the operator
+// runs it over all groups, so the dispatch costs once per instruction and G groups rather than
+// once per element. The common operators are written out; the rest go lane by lane through
+// ew_f32 with the same arithmetic.
+template <int G, class Fetch>
+__device__ __forceinline__ void ew_chain_step(const EwInstr &in, int nleaves, float4 (&acc)[G], const bool (&live)[G],
+                                              Fetch fetch) {
+    const int a0 = in.a[0], a1 = in.a[1], a2 = in.a[2];
+    float4 x[G], y[G], z[G];
+#pragma unroll
+    for (int g = 0; g < G; ++g) {
+        if (!live[g]) continue;
+        x[g] = a0 < nleaves ? fetch(a0, g) : acc[g];
+        y[g] = a1 < 0 ? x[g] : a1 < nleaves ? fetch(a1, g) : acc[g];
+        z[g] = a2 < 0 ? x[g] : a2 < nleaves ? fetch(a2, g) : acc[g];
+    }
+#define MGC_EW_EACH(EXPR)                                                                          \
+    _Pragma("unroll") for (int g = 0; g < G; ++g) {                                                \
+        const float4 X = x[g], Y = y[g], Z = z[g];                                                 \
+        (void)Y; (void)Z;                                                                          \
+        acc[g] = make_float4(EXPR(X.x, Y.x, Z.x), EXPR(X.y, Y.y, Z.y), EXPR(X.z, Y.z, Z.z),        \
+                             EXPR(X.w, Y.w, Z.w));                                                 \
+    }
+#define MGC_EW_ADD(u, v, w) ((u) + (v))
+#define MGC_EW_SUB(u, v, w) ((u) - (v))
+#define MGC_EW_MUL(u, v, w) ((u) * (v))
+#define MGC_EW_DIV(u, v, w) ((u) / (v))
+#define MGC_EW_MAXF(u, v, w) fmaxf((u), (v))
+#define MGC_EW_MINF(u, v, w) fminf((u), (v))
+#define MGC_EW_WHERE(u, v, w) ((u) != 0.0f ? (v) : (w))
+#define MGC_EW_RELU(u, v, w) fmaxf((u), 0.0f)
+#define MGC_EW_COPY(u, v, w) (u)
+    switch (in.op) {
+    case EW_ADD: MGC_EW_EACH(MGC_EW_ADD) break;
+    case EW_SUB: MGC_EW_EACH(MGC_EW_SUB) break;
+    case EW_MUL: MGC_EW_EACH(MGC_EW_MUL) break;
+    case EW_DIV: MGC_EW_EACH(MGC_EW_DIV) break;
+    case EW_MAX: MGC_EW_EACH(MGC_EW_MAXF) break;
+    case EW_MIN: MGC_EW_EACH(MGC_EW_MINF) break;
+    case EW_WHERE: MGC_EW_EACH(MGC_EW_WHERE) break;
+    case EW_RELU: MGC_EW_EACH(MGC_EW_RELU) break;
+    case EW_IDENTITY:
+    case EW_CAST: MGC_EW_EACH(MGC_EW_COPY) break;
+    default:
+#pragma unroll
+        for (int g = 0; g < G; ++g) acc[g] = ew_f32x4(in, x[g], y[g], z[g]);
+        break;
+    }
+#undef MGC_EW_EACH
+#undef MGC_EW_ADD
+#undef MGC_EW_SUB
+#undef MGC_EW_MUL
+#undef MGC_EW_DIV
+#undef MGC_EW_MAXF
+#undef MGC_EW_MINF
+#undef MGC_EW_WHERE
+#undef MGC_EW_RELU
+#undef MGC_EW_COPY
+}
+
+// A chain program over four consecutive output elements per thread, with no register file.
+__global__ void __launch_bounds__(256) ew_chain4_kernel(const __grid_constant__ EwParams P, const unsigned vec_leaf,
+                                                        const int vec_out) {
+    const unsigned total4 = (unsigned)(P.total >> 2);
+    const unsigned step = gridDim.x * blockDim.x;
+    const int last = P.rank - 1;
+    for (unsigned v = blockIdx.x * blockDim.x + threadIdx.x; v < total4; v += step) {
+        unsigned idx[EW_MAX_RANK];
+        ew_coords(P, v << 2, idx);
+        float4 acc[1] = {make_float4(0.0f, 0.0f, 0.0f, 0.0f)};
+        const bool live[1] = {true};
+        for (int k = 0; k < P.ninstr; ++k)
+            ew_chain_step<1>(P.ins[k], P.nleaves, acc, live, [&](int l, int) {
+                const EwLeaf &lf = P.leaves[l];
+                return ew_leaf4(lf, ew_leaf_offset(P, l, idx), lf.strides[last] == 0, (vec_leaf >> l) & 1u);
+            });
+        float *o = (float *)P.out + (v << 2);
+        if (vec_out) *reinterpret_cast<float4 *>(o) = acc[0];
+        else { o[0] = acc[0].x; o[1] = acc[0].y; o[2] = acc[0].z; o[3] = acc[0].w; }
+    }
+}
+
+// An ew_f32x4_form program over four consecutive output elements per thread (ew_vec4_form
+// shapes); the output leaves as one 16-byte store when `vec_out`.
 __global__ void __launch_bounds__(256) ew_f32x4_kernel(const __grid_constant__ EwParams P, const unsigned vec_leaf,
                                                        const int vec_out) {
     float4 regs[EW_MAX_LEAVES + EW_MAX_INSTR];
     const unsigned total4 = (unsigned)(P.total >> 2);
     const unsigned step = gridDim.x * blockDim.x;
-    const int last = P.rank - 1;
     for (unsigned v = blockIdx.x * blockDim.x + threadIdx.x; v < total4; v += step) {
         unsigned off[EW_MAX_LEAVES];
-        ew_offsets4(P, v, off);
-        for (int l = 0; l < P.nleaves; ++l) {
-            const EwLeaf &lf = P.leaves[l];
-            const float *p = (const float *)lf.p + off[l];
-            if (lf.is_lit) regs[l] = make_float4(lf.lit.f, lf.lit.f, lf.lit.f, lf.lit.f);
-            else if (lf.strides[last] == 0) { const float t = __ldg(p); regs[l] = make_float4(t, t, t, t); }
-            else if ((vec_leaf >> l) & 1u) regs[l] = __ldg(reinterpret_cast<const float4 *>(p));
-            else regs[l] = make_float4(__ldg(p), __ldg(p + 1), __ldg(p + 2), __ldg(p + 3));
-        }
-        for (int k = 0; k < P.ninstr; ++k) {
-            const EwInstr &in = P.ins[k];
-            const float4 x = regs[in.a[0]];
-            const float4 y = in.a[1] >= 0 ? regs[in.a[1]] : x;
-            const float4 z = in.a[2] >= 0 ? regs[in.a[2]] : x;
-            regs[P.nleaves + k] = make_float4(ew_f32(in, x.x, y.x, z.x), ew_f32(in, x.y, y.y, z.y),
-                                              ew_f32(in, x.z, y.z, z.z), ew_f32(in, x.w, y.w, z.w));
-        }
-        const float4 r = regs[P.nleaves + P.ninstr - 1];
+        ew_offsets(P, v << 2, off);
+        const float4 r = ew_run4(P, off, vec_leaf, regs);
         float *o = (float *)P.out + (v << 2);
         if (vec_out) *reinterpret_cast<float4 *>(o) = r;
         else { o[0] = r.x; o[1] = r.y; o[2] = r.z; o[3] = r.w; }
@@ -430,7 +618,7 @@ __global__ void __launch_bounds__(256) ew_vec4_kernel(const __grid_constant__ Ew
     const int last = P.rank - 1;
     for (unsigned v = blockIdx.x * blockDim.x + threadIdx.x; v < total4; v += step) {
         unsigned off[EW_MAX_LEAVES];
-        ew_offsets4(P, v, off);
+        ew_offsets(P, v << 2, off);
         for (int j = 0; j < 4; ++j) {
             for (int l = 0; l < P.nleaves; ++l) {
                 const EwLeaf &lf = P.leaves[l];
@@ -502,6 +690,51 @@ __global__ void __launch_bounds__(256) copy_vec_kernel(const __grid_constant__ C
             d += (int)i * dstr[k];
         }
         dst[d] = src[s];
+    }
+}
+
+// A copy whose destination is contiguous along dimension ii (the last) and whose source is
+// contiguous along another dimension jj (a transpose, such as attention's (b, h, s, d) ->
+// (b, h, d, s)): 32 x 32 tiles staged in shared memory, read along jj and written along ii, so
+// both sides move whole 128-byte lines. The remaining dimensions index the tiles' batch; all
+// index arithmetic is 32-bit (the launcher checks that every offset fits).
+template <typename T>
+__global__ void __launch_bounds__(256) transpose_tile_kernel(const __grid_constant__ CopyParams P, const int jj,
+                                                             const unsigned nbatch) {
+    __shared__ T tile[32][33];
+    const T *src = (const T *)P.src;
+    T *dst = (T *)P.dst;
+    const int ii = P.rank - 1;
+    const unsigned ni = (unsigned)P.shape[ii], nj = (unsigned)P.shape[jj];
+    const unsigned ti_n = (ni + 31) / 32, tj_n = (nj + 31) / 32;
+    const unsigned tiles = nbatch * ti_n * tj_n;
+    const unsigned s_i = (unsigned)P.sstr[ii], s_j = (unsigned)P.sstr[jj];
+    const unsigned d_i = (unsigned)P.dstr[ii], d_j = (unsigned)P.dstr[jj];
+    const unsigned tx = threadIdx.x & 31, ty = threadIdx.x >> 5;
+    for (unsigned t = blockIdx.x; t < tiles; t += gridDim.x) {
+        const unsigned tq = t / tj_n, tj = t - tq * tj_n;
+        const unsigned tb = tq / ti_n, ti = tq - tb * ti_n;
+        unsigned rem = tb, sb = (unsigned)P.sbase, db = (unsigned)P.dbase;
+        for (int k = P.rank - 1; k >= 0; --k) {
+            if (k == ii || k == jj) continue;
+            const unsigned e = (unsigned)P.shape[k], q = rem / e, i = rem - q * e;
+            rem = q;
+            sb += i * (unsigned)P.sstr[k];
+            db += i * (unsigned)P.dstr[k];
+        }
+        const unsigned i0 = ti * 32, j0 = tj * 32;
+#pragma unroll
+        for (unsigned k = ty; k < 32; k += 8) {
+            const unsigned i = i0 + k, j = j0 + tx;
+            if (i < ni && j < nj) tile[k][tx] = src[sb + i * s_i + j * s_j];
+        }
+        __syncthreads();
+#pragma unroll
+        for (unsigned k = ty; k < 32; k += 8) {
+            const unsigned i = i0 + tx, j = j0 + k;
+            if (i < ni && j < nj) dst[db + i * d_i + j * d_j] = tile[tx][k];
+        }
+        __syncthreads();
     }
 }
 

@@ -8,6 +8,7 @@
 
 #include <math.h>
 #include "common.cuh"
+#include "kernels_mem.cuh"
 
 namespace mgc {
 
@@ -60,6 +61,299 @@ __global__ void __launch_bounds__(256) softmax_kernel(long long outer, long long
         } else {
             const float inv = 1.0f / s;
             for (long long k = lane; k < n; k += 32) dst[k * inner] = expf(src[k * inner] - m) * inv;
+        }
+    }
+}
+
+// Softmax / log-softmax of rows of n contiguous elements (n % 4 == 0, n <= 128 * CH): one warp
+// per R rows holds them in registers (CH groups of four per lane and row), so every row is read
+// once and written once, and the loads of R rows are in flight together. Exponentials use the
+// fast __expf (relative error about |x| * 6e-8 for an argument x <= 0, far inside the tf32 and
+// strict budgets). With PROG the rows are
+// the output of the elementwise program P (the scale and mask of attention scores) evaluated as
+// they are read, so that output never reaches memory: PROG 1 for chain programs (instruction by
+// instruction over all R x CH groups, each leaf's offset at a row start in shared memory),
+// PROG 2 for any other ew_f32x4_form program (ew_run4, register file in local memory), PROG 3
+// for the scale-and-mask form of attention scores (ScaleMask: no interpretation at all).
+constexpr int SOFTMAX_ROW_MAX = 1024;
+
+// Attention's score program, recognised so that the softmax runs it without interpreting it:
+// t = X * s or X / s (X fp32 laid out as the output, s an fp32 literal), then optionally
+// t + M, t - M (M an fp32 tensor leaf, any broadcast), Where(C, t, lit) or Where(C, lit, t)
+// (C a bool / uint8 leaf). The operations are the ones ew_f32 runs, in the same order.
+struct ScaleMask {
+    int x_leaf, s_leaf, div;  // t = X * s (div 0) or X / s (div 1)
+    int mode;                 // 0 t, 1 t + M, 2 t - M, 3 Where(C, t, lit), 4 Where(C, lit, t)
+    int m_leaf, lit_leaf;     // M or C; the Where literal
+};
+
+inline bool scale_mask_form(const EwParams &P, ScaleMask &sm) {
+    if (P.ninstr < 1 || P.ninstr > 2) return false;
+    auto tensor = [&](int a, bool f32) {
+        return a >= 0 && a < P.nleaves && !P.leaves[a].is_lit && (f32 ? P.leaves[a].dtype == MGC_F32
+                                                                       : (P.leaves[a].dtype == MGC_BOOL ||
+                                                                          P.leaves[a].dtype == MGC_U8));
+    };
+    auto literal = [&](int a) { return a >= 0 && a < P.nleaves && P.leaves[a].is_lit && P.leaves[a].dtype == MGC_F32; };
+    auto dense = [&](int a) {
+        long long want = 1;
+        for (int d = P.rank - 1; d >= 0; --d) {
+            if (P.shape[d] != 1 && P.leaves[a].strides[d] != want) return false;
+            want *= P.shape[d];
+        }
+        return true;
+    };
+    const EwInstr &i0 = P.ins[0];
+    if (i0.a[2] >= 0 || i0.out_dt != MGC_F32) return false;
+    if (i0.op == EW_MUL && tensor(i0.a[0], true) && literal(i0.a[1])) { sm.x_leaf = i0.a[0]; sm.s_leaf = i0.a[1]; }
+    else if (i0.op == EW_MUL && literal(i0.a[0]) && tensor(i0.a[1], true)) { sm.x_leaf = i0.a[1]; sm.s_leaf = i0.a[0]; }
+    else if (i0.op == EW_DIV && tensor(i0.a[0], true) && literal(i0.a[1])) { sm.x_leaf = i0.a[0]; sm.s_leaf = i0.a[1]; }
+    else return false;
+    sm.div = i0.op == EW_DIV;
+    if (!dense(sm.x_leaf)) return false;
+    sm.mode = 0;
+    sm.m_leaf = sm.lit_leaf = 0;
+    if (P.ninstr == 1) return true;
+    const EwInstr &i1 = P.ins[1];
+    const int t = P.nleaves;  // the register of the first instruction's result
+    if (i1.out_dt != MGC_F32) return false;
+    if (i1.op == EW_ADD && i1.a[2] < 0 && i1.a[0] == t && tensor(i1.a[1], true)) { sm.mode = 1; sm.m_leaf = i1.a[1]; }
+    else if (i1.op == EW_ADD && i1.a[2] < 0 && i1.a[1] == t && tensor(i1.a[0], true)) { sm.mode = 1; sm.m_leaf = i1.a[0]; }
+    else if (i1.op == EW_SUB && i1.a[2] < 0 && i1.a[0] == t && tensor(i1.a[1], true)) { sm.mode = 2; sm.m_leaf = i1.a[1]; }
+    else if (i1.op == EW_WHERE && tensor(i1.a[0], false) && i1.a[1] == t && literal(i1.a[2])) {
+        sm.mode = 3; sm.m_leaf = i1.a[0]; sm.lit_leaf = i1.a[2];
+    } else if (i1.op == EW_WHERE && tensor(i1.a[0], false) && literal(i1.a[1]) && i1.a[2] == t) {
+        sm.mode = 4; sm.m_leaf = i1.a[0]; sm.lit_leaf = i1.a[1];
+    } else {
+        return false;
+    }
+    return true;
+}
+
+template <int CH, int R, int PROG>
+__global__ void __launch_bounds__(256) softmax_rows_kernel(const __grid_constant__ EwParams P, const float *x,
+                                                           float *y, long long rows, int n, int log_softmax,
+                                                           unsigned vec_leaf, int vec_io, const ScaleMask sm) {
+    float4 regs[PROG == 2 ? EW_MAX_LEAVES + EW_MAX_INSTR : 1];
+    __shared__ unsigned row_base[8][R][PROG == 1 ? EW_MAX_LEAVES : 1];
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    const int nq = n >> 2;
+    const int last = P.rank - 1;
+    const long long groups = (rows + R - 1) / R;
+    const long long warps = (long long)gridDim.x * (blockDim.x >> 5);
+    for (long long g = (long long)blockIdx.x * (blockDim.x >> 5) + warp; g < groups; g += warps) {
+        const long long row0 = g * R;
+        const int nr = rows - row0 < R ? (int)(rows - row0) : R;
+        float4 v[R][CH];
+        if constexpr (PROG == 1) {
+            __syncwarp();
+            for (int t = lane; t < nr * P.nleaves; t += 32) {
+                const int r = t / P.nleaves, l = t - r * P.nleaves;
+                unsigned idx[EW_MAX_RANK];
+                ew_coords(P, (unsigned)((row0 + r) * n), idx);
+                row_base[warp][r][l] = ew_leaf_offset(P, l, idx);
+            }
+            __syncwarp();
+            float4 acc[R * CH];
+            bool live[R * CH];
+#pragma unroll
+            for (int g = 0; g < R * CH; ++g) {
+                live[g] = g / CH < nr && lane + 32 * (g % CH) < nq;
+                acc[g] = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+            }
+            for (int k = 0; k < P.ninstr; ++k)
+                ew_chain_step<R * CH>(P.ins[k], P.nleaves, acc, live, [&](int l, int g) {
+                    const EwLeaf &lf = P.leaves[l];
+                    const unsigned inner = (unsigned)lf.strides[last];
+                    const unsigned q = lane + 32 * (g % CH);
+                    return ew_leaf4(lf, row_base[warp][g / CH][l] + inner * 4u * q, inner == 0, (vec_leaf >> l) & 1u);
+                });
+#pragma unroll
+            for (int g = 0; g < R * CH; ++g) v[g / CH][g % CH] = acc[g];
+        } else if constexpr (PROG == 3) {
+            // the mask leaf's offset at each row start: lane r computes row r's
+            unsigned mb = 0;
+            if (sm.mode != 0 && lane < nr) {
+                unsigned idx[EW_MAX_RANK];
+                ew_coords(P, (unsigned)((row0 + lane) * n), idx);
+                mb = ew_leaf_offset(P, sm.m_leaf, idx);
+            }
+            const EwLeaf &xl = P.leaves[sm.x_leaf];
+            const EwLeaf &ml = P.leaves[sm.m_leaf];
+            const float sc = P.leaves[sm.s_leaf].lit.f, lit = P.leaves[sm.lit_leaf].lit.f;
+            const bool xq = (vec_leaf >> sm.x_leaf) & 1u, mq = (vec_leaf >> sm.m_leaf) & 1u;
+            const unsigned m_inner = (unsigned)ml.strides[last];
+#pragma unroll
+            for (int r = 0; r < R; ++r) {
+                const unsigned mrow = __shfl_sync(0xffffffffu, mb, r);
+                if (r >= nr) continue;
+#pragma unroll
+                for (int c = 0; c < CH; ++c) {
+                    const int q = lane + 32 * c;
+                    if (q >= nq) continue;
+                    float4 t = ew_leaf4(xl, (unsigned)((row0 + r) * n) + 4u * q, false, xq);
+                    if (sm.div) t = make_float4(t.x / sc, t.y / sc, t.z / sc, t.w / sc);
+                    else t = make_float4(t.x * sc, t.y * sc, t.z * sc, t.w * sc);
+                    if (sm.mode != 0) {
+                        const float4 mv = ew_leaf4(ml, mrow + m_inner * 4u * q, m_inner == 0, mq);
+                        if (sm.mode == 1) t = make_float4(t.x + mv.x, t.y + mv.y, t.z + mv.z, t.w + mv.w);
+                        else if (sm.mode == 2) t = make_float4(t.x - mv.x, t.y - mv.y, t.z - mv.z, t.w - mv.w);
+                        else if (sm.mode == 3)
+                            t = make_float4(mv.x != 0.0f ? t.x : lit, mv.y != 0.0f ? t.y : lit, mv.z != 0.0f ? t.z : lit,
+                                            mv.w != 0.0f ? t.w : lit);
+                        else
+                            t = make_float4(mv.x != 0.0f ? lit : t.x, mv.y != 0.0f ? lit : t.y, mv.z != 0.0f ? lit : t.z,
+                                            mv.w != 0.0f ? lit : t.w);
+                    }
+                    v[r][c] = t;
+                }
+            }
+        } else {
+#pragma unroll
+            for (int r = 0; r < R; ++r) {
+                if (r >= nr) break;
+                unsigned base[PROG == 2 ? EW_MAX_LEAVES : 1];
+                if constexpr (PROG == 2) ew_offsets(P, (unsigned)((row0 + r) * n), base);
+#pragma unroll
+                for (int c = 0; c < CH; ++c) {
+                    const int q = lane + 32 * c;
+                    if (q >= nq) break;
+                    if constexpr (PROG == 2) {
+                        unsigned off[EW_MAX_LEAVES];
+                        for (int l = 0; l < P.nleaves; ++l) off[l] = base[l] + (P.leaves[l].strides[last] ? 4u * q : 0u);
+                        v[r][c] = ew_run4(P, off, vec_leaf, regs);
+                    } else {
+                        const float *p = x + (row0 + r) * n + 4 * q;
+                        v[r][c] = vec_io ? __ldg(reinterpret_cast<const float4 *>(p)) : make_float4(p[0], p[1], p[2], p[3]);
+                    }
+                }
+            }
+        }
+        float m[R], s[R];
+#pragma unroll
+        for (int r = 0; r < R; ++r) {
+            m[r] = -INFINITY;
+#pragma unroll
+            for (int c = 0; c < CH; ++c)
+                if (r < nr && lane + 32 * c < nq)
+                    m[r] = fmaxf(m[r], fmaxf(fmaxf(v[r][c].x, v[r][c].y), fmaxf(v[r][c].z, v[r][c].w)));
+        }
+#pragma unroll
+        for (int r = 0; r < R; ++r) m[r] = warp_max(m[r]);
+#pragma unroll
+        for (int r = 0; r < R; ++r) {
+            s[r] = 0.0f;
+#pragma unroll
+            for (int c = 0; c < CH; ++c) {
+                if (r >= nr || lane + 32 * c >= nq) continue;
+                const float4 e = make_float4(__expf(v[r][c].x - m[r]), __expf(v[r][c].y - m[r]),
+                                             __expf(v[r][c].z - m[r]), __expf(v[r][c].w - m[r]));
+                s[r] += e.x + e.y + e.z + e.w;
+                if (!log_softmax) v[r][c] = e;
+            }
+        }
+#pragma unroll
+        for (int r = 0; r < R; ++r) s[r] = warp_sum(s[r]);
+#pragma unroll
+        for (int r = 0; r < R; ++r) {
+            if (r >= nr) break;
+            const float inv = log_softmax ? 0.0f : 1.0f / s[r], ls = log_softmax ? logf(s[r]) : 0.0f, mr = m[r];
+#pragma unroll
+            for (int c = 0; c < CH; ++c) {
+                const int q = lane + 32 * c;
+                if (q >= nq) break;
+                const float4 a = v[r][c];
+                const float4 o = log_softmax ? make_float4(a.x - mr - ls, a.y - mr - ls, a.z - mr - ls, a.w - mr - ls)
+                                             : make_float4(a.x * inv, a.y * inv, a.z * inv, a.w * inv);
+                float *d = y + (row0 + r) * n + 4 * q;
+                if (vec_io) *reinterpret_cast<float4 *>(d) = o;
+                else { d[0] = o.x; d[1] = o.y; d[2] = o.z; d[3] = o.w; }
+            }
+        }
+    }
+}
+
+// One block of 8 warps per 8 row groups, as many blocks as groups need: the hardware hands out
+// the blocks as SMs free up, with no grid-stride tail.
+template <int PROG>
+inline void launch_softmax_rows_t(const EwParams &P, const float *x, float *y, long long rows, int n, int log,
+                                  unsigned vec_leaf, int vec_io, const ScaleMask &sm, cudaStream_t stream) {
+    const int ch = (n + 127) / 128;
+    auto grid = [&](int r) { return (unsigned)((rows + 8ll * r - 1) / (8ll * r)); };
+    // two rows per warp for rows of up to 256 (measured on B200: more rows per warp cost more in
+    // occupancy than they gain in loads in flight)
+    constexpr int G = 2;
+    constexpr int R1 = G, R2 = G / 2 > 0 ? G / 2 : 1, R4 = G / 4 > 0 ? G / 4 : 1, R8 = G / 8 > 0 ? G / 8 : 1;
+    if (ch <= 1) softmax_rows_kernel<1, R1, PROG><<<grid(R1), 256, 0, stream>>>(P, x, y, rows, n, log, vec_leaf, vec_io, sm);
+    else if (ch <= 2) softmax_rows_kernel<2, R2, PROG><<<grid(R2), 256, 0, stream>>>(P, x, y, rows, n, log, vec_leaf, vec_io, sm);
+    else if (ch <= 4) softmax_rows_kernel<4, R4, PROG><<<grid(R4), 256, 0, stream>>>(P, x, y, rows, n, log, vec_leaf, vec_io, sm);
+    else softmax_rows_kernel<8, R8, PROG><<<grid(R8), 256, 0, stream>>>(P, x, y, rows, n, log, vec_leaf, vec_io, sm);
+}
+
+// Row softmax launcher: with `prog` the rows come from the program P (x unused), else from x.
+inline int launch_softmax_rows(const EwParams &P, bool prog, const float *x, float *y, long long rows, int n, int log,
+                               unsigned vec_leaf, int vec_io, cudaStream_t stream) {
+    ScaleMask sm{};
+    if (!prog) {
+        launch_softmax_rows_t<0>(P, x, y, rows, n, log, vec_leaf, vec_io, sm, stream);
+        return check_launch("softmax_rows_kernel");
+    }
+    vec_io = (reinterpret_cast<uintptr_t>(y) & 15) == 0;
+    if (scale_mask_form(P, sm)) launch_softmax_rows_t<3>(P, x, y, rows, n, log, vec_leaf, vec_io, sm, stream);
+    else if (ew_chain_form(P)) launch_softmax_rows_t<1>(P, x, y, rows, n, log, vec_leaf, vec_io, sm, stream);
+    else launch_softmax_rows_t<2>(P, x, y, rows, n, log, vec_leaf, vec_io, sm, stream);
+    return check_launch("softmax_rows_kernel(program)");
+}
+
+// Layer normalization of rows of at most 128 * CH fp32 values in groups of four (16-byte
+// aligned): one warp per row holds it in registers, so the row is read from memory once; the
+// mean, the sum of squared deviations and the output use layer_norm_kernel's arithmetic in the
+// same order.
+template <int CH>
+__global__ void __launch_bounds__(256) layer_norm_rows_kernel(long long rows, int cols, const float *x,
+                                                              const float *scale, const float *bias, float eps,
+                                                              float *y) {
+    const int lane = threadIdx.x & 31;
+    const long long warps = (long long)gridDim.x * (blockDim.x >> 5);
+    for (long long r = (long long)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5); r < rows; r += warps) {
+        const float *src = x + r * cols;
+        float *dst = y + r * cols;
+        float4 v[CH];
+        float s = 0.0f;
+#pragma unroll
+        for (int c = 0; c < CH; ++c) {
+            const int k = lane * 4 + 128 * c;
+            if (k < cols) {
+                v[c] = __ldg(reinterpret_cast<const float4 *>(src + k));
+                s += (v[c].x + v[c].y) + (v[c].z + v[c].w);
+            }
+        }
+        const float mean = warp_sum(s) / (float)cols;
+        float q = 0.0f;
+#pragma unroll
+        for (int c = 0; c < CH; ++c) {
+            if (lane * 4 + 128 * c < cols) {
+                const float a = v[c].x - mean, b = v[c].y - mean, cc = v[c].z - mean, d = v[c].w - mean;
+                q += (a * a + b * b) + (cc * cc + d * d);
+            }
+        }
+        const float inv = 1.0f / sqrtf(warp_sum(q) / (float)cols + eps);
+#pragma unroll
+        for (int c = 0; c < CH; ++c) {
+            const int k = lane * 4 + 128 * c;
+            if (k >= cols) continue;
+            float4 o;
+            o.x = (v[c].x - mean) * inv; o.y = (v[c].y - mean) * inv;
+            o.z = (v[c].z - mean) * inv; o.w = (v[c].w - mean) * inv;
+            if (scale) {
+                const float4 g = __ldg(reinterpret_cast<const float4 *>(scale + k));
+                o.x *= g.x; o.y *= g.y; o.z *= g.z; o.w *= g.w;
+            }
+            if (bias) {
+                const float4 b = __ldg(reinterpret_cast<const float4 *>(bias + k));
+                o.x += b.x; o.y += b.y; o.z += b.z; o.w += b.w;
+            }
+            *reinterpret_cast<float4 *>(dst + k) = o;
         }
     }
 }
@@ -382,4 +676,31 @@ __global__ void __launch_bounds__(256) depthwise_kernel(const __grid_constant__ 
     }
 }
 
+// Layer normalization launcher: the register-resident form for rows of up to 1024 values in
+// aligned groups of four, else layer_norm_kernel.
+inline int launch_layer_norm(long long rows, long long cols, const float *x, const float *g, const float *b, float eps,
+                             float *y, cudaStream_t stream) {
+    const bool vec = cols % 4 == 0 && cols <= 1024 &&
+                     ((reinterpret_cast<uintptr_t>(x) | reinterpret_cast<uintptr_t>(y) | reinterpret_cast<uintptr_t>(g) |
+                       reinterpret_cast<uintptr_t>(b)) & 15) == 0;
+    if (!vec) {
+        layer_norm_kernel<<<grid_for(rows, 8), 256, 0, stream>>>(rows, cols, x, g, b, eps, y);
+        return check_launch("layer_norm_kernel");
+    }
+    const unsigned grid = (unsigned)((rows + 7) / 8);
+    const int c = (int)cols, ch = (c + 127) / 128;
+    switch (ch) {
+    case 1: layer_norm_rows_kernel<1><<<grid, 256, 0, stream>>>(rows, c, x, g, b, eps, y); break;
+    case 2: layer_norm_rows_kernel<2><<<grid, 256, 0, stream>>>(rows, c, x, g, b, eps, y); break;
+    case 3: layer_norm_rows_kernel<3><<<grid, 256, 0, stream>>>(rows, c, x, g, b, eps, y); break;
+    case 4: layer_norm_rows_kernel<4><<<grid, 256, 0, stream>>>(rows, c, x, g, b, eps, y); break;
+    case 5: layer_norm_rows_kernel<5><<<grid, 256, 0, stream>>>(rows, c, x, g, b, eps, y); break;
+    case 6: layer_norm_rows_kernel<6><<<grid, 256, 0, stream>>>(rows, c, x, g, b, eps, y); break;
+    case 7: layer_norm_rows_kernel<7><<<grid, 256, 0, stream>>>(rows, c, x, g, b, eps, y); break;
+    default: layer_norm_rows_kernel<8><<<grid, 256, 0, stream>>>(rows, c, x, g, b, eps, y); break;
+    }
+    return check_launch("layer_norm_rows_kernel");
+}
+
 }  // namespace mgc
+

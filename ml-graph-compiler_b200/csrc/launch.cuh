@@ -202,6 +202,26 @@ inline int launch_copy_t(const CopyParams &P, cudaStream_t s) {
         copy_vec_kernel<uint4><<<grid_for(Q.total, 256), 256, 0, s>>>(Q);
         return check_launch("copy_vec_kernel");
     }
+    // Tiled transpose: the destination contiguous along the last dimension, the source along
+    // another one, both extents at least 16 (narrower ones waste most of a 32 x 32 tile).
+    if (r >= 2 && P.dstr[r - 1] == 1 && P.sstr[r - 1] != 1 && P.shape[r - 1] >= 16) {
+        int jj = -1;
+        for (int k = 0; k < r - 1; ++k)
+            if (P.sstr[k] == 1 && P.shape[k] >= 16) jj = k;
+        bool fits = true;
+        long long smax = P.sbase, dmax = P.dbase;
+        for (int k = 0; k < r; ++k) {
+            fits = fits && P.sstr[k] >= 0 && P.dstr[k] >= 0;
+            smax += (P.shape[k] - 1) * P.sstr[k];
+            dmax += (P.shape[k] - 1) * P.dstr[k];
+        }
+        const long long nbatch = jj >= 0 ? P.total / (P.shape[r - 1] * P.shape[jj]) : 0;
+        const long long tiles = nbatch * ((P.shape[r - 1] + 31) / 32) * (jj >= 0 ? (P.shape[jj] + 31) / 32 : 0);
+        if (jj >= 0 && fits && smax < (1ll << 31) && dmax < (1ll << 31) && tiles < (1ll << 31)) {
+            transpose_tile_kernel<T><<<grid_for(tiles, 1), 256, 0, s>>>(P, jj, (unsigned)nbatch);
+            return check_launch("transpose_tile_kernel");
+        }
+    }
     copy_kernel<T><<<grid_for(P.total, 256), 256, 0, s>>>(P);
     return check_launch("copy_kernel");
 }
@@ -286,48 +306,51 @@ inline int launch_record(const mgc_cuda_launch &L, const int64_t *aux, int64_t a
         break;
     }
     case MGC_K_SOFTMAX: {
-        const float *x; float *y;
-        MGC_RESOLVE(L.r[0], x); MGC_RESOLVE(L.r[1], y);
-        const long long rows = i[0] * i[2];
-        if (rows == 0 || i[1] == 0) { launched = 0; break; }
-        softmax_kernel<<<grid_for(rows, 8), 256, 0, stream>>>(i[0], i[1], i[2], x, y, (int)i[3]);
-        st = check_launch("softmax_kernel");
+        const float *x = nullptr; float *y;
+        MGC_RESOLVE(L.r[1], y);
+        const long long rows = i[0] * i[2], n = i[1];
+        if (rows == 0 || n == 0) { launched = 0; break; }
+        EwParams P;
+        unsigned vec_leaf = 0;
+        if (i[4]) {
+            // the rows are the output of an elementwise program (aux), evaluated as they are read
+            MGC_CHECK(decode_elementwise(L, aux, aux_len, bases, P));
+            if (i[2] != 1 || n % 4 || n > SOFTMAX_ROW_MAX || P.total != rows * n || !ew_vec4_form(P, vec_leaf) ||
+                !ew_f32x4_form(P) || P.shape[P.rank - 1] % n)
+                return fail(MGC_CUDA_UNSUPPORTED, "softmax of an elementwise program: rows of %lld", (long long)n);
+        } else {
+            MGC_RESOLVE(L.r[0], x);
+            P.rank = 0;
+        }
+        if (i[2] == 1 && n % 4 == 0 && n <= SOFTMAX_ROW_MAX && rows * n < (1ll << 31)) {
+            const int vec_io = ((reinterpret_cast<uintptr_t>(x) | reinterpret_cast<uintptr_t>(y)) & 15) == 0;
+            st = launch_softmax_rows(P, i[4] != 0, x, y, rows, (int)n, (int)i[3], vec_leaf, vec_io, stream);
+        } else {
+            softmax_kernel<<<grid_for(rows, 8), 256, 0, stream>>>(i[0], i[1], i[2], x, y, (int)i[3]);
+            st = check_launch("softmax_kernel");
+        }
         break;
     }
     case MGC_K_LAYER_NORM: {
         const float *x, *g, *b; float *y;
         MGC_RESOLVE(L.r[0], x); MGC_RESOLVE(L.r[1], g); MGC_RESOLVE(L.r[2], b); MGC_RESOLVE(L.r[3], y);
         if (i[0] == 0 || i[1] == 0) { launched = 0; break; }
-        layer_norm_kernel<<<grid_for(i[0], 8), 256, 0, stream>>>(i[0], i[1], x, g, b, (float)L.f[0], y);
-        st = check_launch("layer_norm_kernel");
+        st = launch_layer_norm(i[0], i[1], x, g, b, (float)L.f[0], y, stream);
         break;
     }
     case MGC_K_ELEMENTWISE: {
         EwParams P;
         MGC_CHECK(decode_elementwise(L, aux, aux_len, bases, P));
         if (P.total == 0) { launched = 0; break; }
-        // four elements per thread when the innermost dimension comes in groups of four that every
-        // leaf reads contiguously or broadcasts, and all offsets fit 32 bits
-        bool vec = P.rank >= 1 && P.shape[P.rank - 1] % 4 == 0 && P.total < (1ll << 31);
-        bool f32 = P.out_dt == MGC_F32;
+        // four elements per thread when the innermost dimension comes in groups of four
         unsigned vec_leaf = 0;
-        for (int l = 0; vec && l < P.nleaves; ++l) {
-            const EwLeaf &lf = P.leaves[l];
-            f32 = f32 && lf.dtype == MGC_F32;
-            if (lf.is_lit) continue;
-            const long long inner = lf.strides[P.rank - 1];
-            long long span = 0;
-            bool quad = (reinterpret_cast<uintptr_t>(lf.p) & 15) == 0;
-            for (int d = 0; d < P.rank; ++d) {
-                vec = vec && lf.strides[d] >= 0;
-                span += (P.shape[d] - 1) * lf.strides[d];
-                if (d < P.rank - 1) quad = quad && lf.strides[d] % 4 == 0;
-            }
-            vec = vec && (inner == 0 || inner == 1) && span < (1ll << 31);
-            if (inner == 1 && quad) vec_leaf |= 1u << l;
-        }
-        for (int k = 0; f32 && k < P.ninstr; ++k) f32 = P.ins[k].out_dt == MGC_F32 && ew_f32_op(P.ins[k].op);
-        if (vec && f32) {
+        const bool vec = ew_vec4_form(P, vec_leaf);
+        const bool f32 = vec && ew_f32x4_form(P);
+        if (vec && f32 && ew_chain_form(P)) {
+            const int vec_out = (reinterpret_cast<uintptr_t>(P.out) & 15) == 0;
+            ew_chain4_kernel<<<grid_for(P.total / 4, 256), 256, 0, stream>>>(P, vec_leaf, vec_out);
+            st = check_launch("ew_chain4_kernel");
+        } else if (vec && f32) {
             const int vec_out = (reinterpret_cast<uintptr_t>(P.out) & 15) == 0;
             ew_f32x4_kernel<<<grid_for(P.total / 4, 256), 256, 0, stream>>>(P, vec_leaf, vec_out);
             st = check_launch("ew_f32x4_kernel");

@@ -60,6 +60,22 @@ EW_OPS = [
 ]
 EW_CODE = {name: i for i, name in enumerate(EW_OPS)}
 EW_MAX_RANK, EW_MAX_LEAVES, EW_MAX_INSTR, COPY_MAX_RANK = 6, 20, 40, 8
+SOFTMAX_ROW_MAX = 1024  # longest row the register-resident softmax holds (kernels_norm.cuh)
+_EW_BINARY = {"Add", "Sub", "Mul", "Div", "Pow", "Max", "Min"}
+_EW_FLOAT_ONLY = {"Clip", "Relu", "Sigmoid", "Tanh", "Erf", "Sqrt", "Exp", "Log", "Neg", "Abs", "Reciprocal",
+                  "Floor", "Ceil", "Sin", "Cos", "Softplus", "Gelu", "LeakyRelu", "HardSigmoid"}
+
+
+def _f32x4_instr(op: str, cls: list[str]) -> bool:
+    """One instruction of the four-wide fp32 form (kernels_mem.cuh ``ew_f32x4_form``): byte
+    operands (class I) only where the typed program converts them to fp32 as well."""
+    if op in _EW_BINARY:
+        return "F" in cls[:2]
+    if op == "Where":
+        return cls[0] == "I"
+    if op in _EW_FLOAT_ONLY:
+        return cls[0] == "F"
+    return op in ("Identity", "Cast")
 BLOB_ALIGN = 256
 TF32_MASK = np.uint32(0xFFFFE000)
 
@@ -237,6 +253,10 @@ class CudaEmitter:
         # id(value) -> (source, element strides) of a Transpose that MatMul reads through (not copied)
         self._through: dict[int, tuple[Value, list[int]]] = {}
         self._pack_regions: list[tuple[int, int]] = []  # (offset, bytes) of each packed image
+        # Transposes whose input MatMul wrote their output directly (see _write_through)
+        self._written_through: set[int] = set()
+        # id(value) -> aux words of the elementwise program that the softmax reading it evaluates
+        self._row_programs: dict[int, list[int]] = {}
 
     # -- references ----------------------------------------------------------------------------
     def _root(self, value: Value) -> Value:
@@ -308,13 +328,19 @@ class CudaEmitter:
                 self._fill(mask, 1)
             self.kernels["view"] = self.kernels.get("view", 0) + 1
             return
-        if node.op == "FusedElementwise":
-            program = [(str(op), dict(a), [int(x) for x in args]) for op, a, args in node.attrs["program"]]
+        if node.op == "FusedElementwise" or ops.is_elementwise(node.op):
+            if node.op == "FusedElementwise":
+                program = [(str(op), dict(a), [int(x) for x in args]) for op, a, args in node.attrs["program"]]
+            else:
+                program = [(node.op, dict(node.attrs), [i if node.inputs[i] is not None else -1
+                                                        for i in range(len(node.inputs))])]
+            if self._softmax_reads(node):
+                made = self._elementwise(node.output, program, list(node.inputs), defer=True)
+                if made is not None and made[1] and made[0][made[0][0]] % node.output.tensor_type.shape[-1] == 0:
+                    self._row_programs[id(node.output)] = made[0]
+                    self.kernels["elementwise into softmax"] = self.kernels.get("elementwise into softmax", 0) + 1
+                    return
             self._elementwise(node.output, program, list(node.inputs))
-            return
-        if ops.is_elementwise(node.op):
-            args = [i if node.inputs[i] is not None else -1 for i in range(len(node.inputs))]
-            self._elementwise(node.output, [(node.op, dict(node.attrs), args)], list(node.inputs))
             return
         handler = getattr(self, f"op_{node.op}", None)
         if handler is None:
@@ -323,11 +349,14 @@ class CudaEmitter:
 
     # -- elementwise programs (c.py:471-529) -------------------------------------------------------
     def _elementwise(
-        self, out_value: Value, program: list[tuple[str, dict[str, Any], list[int]]], leaves: list[Value | None]
-    ) -> None:
+        self, out_value: Value, program: list[tuple[str, dict[str, Any], list[int]]], leaves: list[Value | None],
+        defer: bool = False,
+    ) -> tuple[list[int], bool] | None:
+        """Emit a K_ELEMENTWISE record for the program; with ``defer``, return its aux words instead,
+        with whether the program has the four-wide fp32 form (the kernels' ``ew_f32x4_form``)."""
         shape = list(out_value.tensor_type.shape)
         if int(np.prod(shape)) == 0:
-            return
+            return None
         tensor_leaves = [
             i for i, v in enumerate(leaves)
             if v is not None and not (v.is_constant and v.data is not None and v.data.size == 1)
@@ -346,11 +375,14 @@ class CudaEmitter:
         aux.append(len(leaves))
         types_all: list[TensorType | None] = []
         consts: list[np.ndarray | None] = []
+        # register classes of the four-wide fp32 form: F fp32, I bytes read as fp32, X neither
+        cls: list[str] = []
         for i, v in enumerate(leaves):
             if v is None:  # omitted optional input: never read
                 aux += [DTYPES["float32"], 1, 0, *NO_REF, *([0] * len(dims))]
                 types_all.append(None)
                 consts.append(None)
+                cls.append("F")
                 continue
             t = v.tensor_type
             types_all.append(t)
@@ -358,10 +390,13 @@ class CudaEmitter:
             if i in tensor_leaves:
                 strides = coll[1 + tensor_leaves.index(i)]
                 aux += [DTYPES[t.dtype], 0, 0, *self.ref(v), *strides]
+                cls.append("F" if t.dtype == "float32" else "I" if t.dtype in ("bool", "uint8") else "X")
             else:
                 scalar = self.const_data(v).reshape(()).item()
                 bits = _bits(scalar) if t.dtype in ("float32", "float64") else int(scalar)
                 aux += [DTYPES[t.dtype], 1, bits, *NO_REF, *([0] * len(dims))]
+                cls.append("F" if t.dtype == "float32" else "X")
+        f32x4 = out_value.tensor_type.dtype == "float32" and "X" not in cls
         aux.append(len(program))
         for op, attrs, args in program:
             if op not in EW_CODE:
@@ -384,7 +419,59 @@ class CudaEmitter:
             elif op == "HardSigmoid":
                 imm = [float(attrs.get("alpha", 0.2)), float(attrs.get("beta", 0.5))]
             aux += [EW_CODE[op], DTYPES[out_t.dtype], a[0], a[1], a[2], _bits(imm[0]), _bits(imm[1])]
+            f32x4 = f32x4 and out_t.dtype == "float32" and _f32x4_instr(op, [cls[x] if x >= 0 else "" for x in a])
+            cls.append("F" if out_t.dtype == "float32" else "X")
+        if defer:
+            return aux, f32x4
         self.emit(K_ELEMENTWISE, aux=aux, dtype=DTYPES[out_value.tensor_type.dtype], count="elementwise")
+        return None
+
+    def _clobbered(self, first: Node, last: Node, values: Sequence[Value]) -> bool:
+        """Whether a node scheduled strictly between ``first`` and ``last`` writes memory that one
+        of ``values`` occupies (the planner may reuse it once its last reader has run)."""
+        ranges = [r for r in (self._arena_range(v) for v in values) if r is not None]
+        if not ranges:
+            return False
+        order = {id(n): k for k, n in enumerate(self.graph.nodes)}
+        for later in self.graph.nodes[order[id(first)] + 1 : order[id(last)]]:
+            if later.op in ALIAS_OPS:
+                continue
+            for v in later.outputs:
+                r = self._arena_range(v)
+                if r is not None and any(r[0] < hi and lo < r[1] for lo, hi in ranges):
+                    return True
+        return False
+
+    def _softmax_reads(self, node: Node) -> bool:
+        """Whether this elementwise node's output is read only by a Softmax / LogSoftmax over its
+        last axis that can evaluate the program itself as it reads each row (the scale and mask of
+        attention scores; the fused output never reaches memory): rows of at most
+        SOFTMAX_ROW_MAX fp32 elements in groups of four, the program's tensor leaves untouched until
+        the softmax runs, and the softmax output either clear of every leaf or exactly on a leaf of
+        the same shape (each row is read whole before it is written)."""
+        out = node.output
+        t = out.tensor_type
+        if len(out.users) != 1 or any(v is out for _, v in self.graph.named_outputs()):
+            return False
+        user = out.users[0]
+        if user.op not in ("Softmax", "LogSoftmax") or user.input(0) is not out or t.dtype != "float32":
+            return False
+        axis = int(user.attrs.get("axis", -1))
+        axis = axis + t.rank if axis < 0 else axis
+        n = t.shape[-1] if t.rank else 0
+        if axis != t.rank - 1 or n == 0 or n % 4 or n > SOFTMAX_ROW_MAX or t.size >= 1 << 31:
+            return False
+        leaves = [v for v in node.inputs if v is not None and not v.is_constant]
+        if self._clobbered(node, user, leaves):
+            return False
+        dst = self._arena_range(user.output)
+        for v in leaves:
+            r = self._arena_range(v)
+            if dst is None or r is None or not (r[0] < dst[1] and dst[0] < r[1]):
+                continue
+            if tuple(v.tensor_type.shape) != tuple(t.shape) or r[0] != dst[0]:
+                return False
+        return True
 
     # -- copies (c.py:558-660) --------------------------------------------------------------------
     def _copy(
@@ -466,6 +553,9 @@ class CudaEmitter:
         return True
 
     def op_Transpose(self, node: Node) -> None:
+        if id(node) in self._written_through:
+            self.kernels["view"] = self.kernels.get("view", 0) + 1
+            return
         x = node.input(0)
         perm = ops.transpose_perm(node, x.tensor_type.rank)
         ss = _strides(x.tensor_type.shape)
@@ -698,7 +788,8 @@ class CudaEmitter:
             raise CodegenError(f"{node.op} on {t.dtype} has no cuda kernel")
 
     def _softmax(self, node: Node, log: int) -> None:
-        """K_SOFTMAX slots: i[0] outer, i[1] n, i[2] inner, i[3] log; r[0] x, r[1] y."""
+        """K_SOFTMAX slots: i[0] outer, i[1] n, i[2] inner, i[3] log, i[4] 1 when the input is the
+        elementwise program in aux (see _softmax_reads), read as the rows are; r[0] x, r[1] y."""
         x = node.input(0)
         xt = x.tensor_type
         self._require_f32(node, xt)
@@ -706,7 +797,9 @@ class CudaEmitter:
         axis = axis + xt.rank if axis < 0 else axis
         outer = int(np.prod(xt.shape[:axis])) if axis else 1
         inner = int(np.prod(xt.shape[axis + 1 :])) if axis + 1 < xt.rank else 1
-        self.emit(K_SOFTMAX, [outer, xt.shape[axis], inner, log], refs=[self.ref(x), self.ref(node.output)])
+        program = self._row_programs.pop(id(x), None)
+        self.emit(K_SOFTMAX, [outer, xt.shape[axis], inner, log, 0 if program is None else 1],
+                  refs=[self.ref(x), self.ref(node.output)], aux=program)
 
     def op_Softmax(self, node: Node) -> None:
         self._softmax(node, 0)
@@ -933,6 +1026,43 @@ class CudaEmitter:
             return self.ref(src), list(strides)
         return self.ref(value), _strides(value.tensor_type.shape)
 
+    def _write_through(self, node: Node) -> tuple[RefT, int, list[int]] | None:
+        """Where a batched MatMul whose only reader is a Transpose keeping the last axis in place
+        (attention's (b, h, s, d) -> (b, s, h, d) before the output projection) writes its product
+        straight into the Transpose's output, through strides: (reference, row stride, batch
+        strides), and the Transpose emits nothing. Only when the Transpose runs right after the
+        MatMul and its output memory is clear of everything the MatMul reads."""
+        out = node.output
+        rank = out.tensor_type.rank
+        if rank < 3 or len(out.users) != 1 or any(v is out for _, v in self.graph.named_outputs()):
+            return None
+        if node.input(0).tensor_type.rank < 2 or node.input(1).tensor_type.rank < 2:
+            return None
+        user = out.users[0]
+        if user.op != "Transpose" or user.input(0) is not out:
+            return None
+        perm = ops.transpose_perm(user, rank)
+        if perm[-1] != rank - 1 or list(perm) == list(range(rank)):
+            return None
+        dst = self._arena_range(user.output)
+        if dst is None or self.plan.location(user.output).kind != "arena":
+            return None
+        order = {id(n): k for k, n in enumerate(self.graph.nodes)}
+        if any(n.op not in ALIAS_OPS for n in self.graph.nodes[order[id(node)] + 1 : order[id(user)]]):
+            return None
+        reads = [node.input(0), node.input(1)]
+        reads += [self._through[id(v)][0] for v in reads if id(v) in self._through]
+        for v in reads:
+            r = self._arena_range(v)
+            if r is not None and r[0] < dst[1] and dst[0] < r[1]:
+                return None
+        tstrides = _strides(user.output.tensor_type.shape)
+        cstrides = [0] * rank
+        for j, p in enumerate(perm):
+            cstrides[p] = tstrides[j]
+        self._written_through.add(id(user))
+        return self.ref(user.output), cstrides[-2], cstrides[:-2]
+
     def op_MatMul(self, node: Node) -> None:
         a, b = node.input(0), node.input(1)
         at, bt = a.tensor_type, b.tensor_type
@@ -980,8 +1110,12 @@ class CudaEmitter:
                 self._layout_workspace()
                 bref, b_rs, b_cs = (SPACE_WORKSPACE, 0, 0), 1, k
                 b_bs = batch_strides(bshape, [*_strides(own + [n * k])[:-1], 0, 0] if own else [0, 0])
+        cref, ldc = self.ref(node.output), n
+        through = self._write_through(node)
+        if through is not None:
+            cref, ldc, c_bs = through
         dims, (a_bs, b_bs, c_bs) = _collapse(batch_shape, [a_bs, b_bs, c_bs])
-        self._gemm(m, n, k, aref, a_rs, a_cs, bref, b_rs, b_cs, self.ref(node.output), n, b_lo=blo,
+        self._gemm(m, n, k, aref, a_rs, a_cs, bref, b_rs, b_cs, cref, ldc, b_lo=blo,
                    **self._umma_b(bref, blo), batch=dims, a_bs=a_bs, b_bs=b_bs, c_bs=c_bs, r_bs=[0] * len(dims))
 
     @staticmethod

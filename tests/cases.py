@@ -139,6 +139,8 @@ def op_cases() -> list[Case]:
     C(_simple("transpose_nchw_nhwc", lambda r: op_graph("Transpose", [("in", f32(r, 2, 3, 5, 7))], {"perm": [0, 2, 3, 1]})))
     C(_simple("transpose_2d", lambda r: op_graph("Transpose", [("in", f32(r, 33, 17))])))
     C(_simple("transpose_heads", lambda r: op_graph("Transpose", [("in", f32(r, 2, 8, 4, 16))], {"perm": [0, 2, 1, 3]})))
+    # the tiled-transpose copy: batch dimensions, ragged 32 x 32 tiles on both transposed axes
+    C(_simple("transpose_tiles", lambda r: op_graph("Transpose", [("in", f32(r, 2, 3, 40, 24))], {"perm": [0, 1, 3, 2]})))
     C(_simple("expand", lambda r: op_graph("Expand", [("in", f32(r, 3, 1)), ("const", np.asarray([2, 3, 4]))])))
     C(_simple("slice_steps", lambda r: op_graph("Slice", [("in", f32(r, 6, 9, 5)), ("const", np.asarray([1, -1])), ("const", np.asarray([5, 0])), ("const", np.asarray([0, 1])), ("const", np.asarray([2, -2]))])))
     C(_simple("slice_clamp", lambda r: op_graph("Slice", [("in", f32(r, 6, 9)), ("const", np.asarray([-100])), ("const", np.asarray([1 << 40])), ("const", np.asarray([1]))])))
@@ -353,6 +355,48 @@ def _p_loopfuse(r: np.random.Generator) -> tuple[Graph, dict[str, np.ndarray]]:
     return g, {"x": f32(r, 2, 3, 8, 8), "m": f32(r, 2, 1, 1, 8)}
 
 
+def _p_masked_softmax(r: np.random.Generator) -> tuple[Graph, dict[str, np.ndarray]]:
+    """Attention-score scale and mask feeding a softmax over the last axis: a causal bool mask
+    through Where (GPT-2), an additive fp32 mask broadcast over heads and queries (BERT) into
+    LogSoftmax, and a row too short for groups of four."""
+    g = Graph("masked_softmax")
+    x = g.add_input("x", TensorType("float32", (2, 3, 8, 16)))
+    m = g.add_input("m", TensorType("float32", (2, 1, 1, 16)))
+    z = g.add_input("z", TensorType("float32", (4, 6)))
+    causal = g.constant(np.tril(np.ones((8, 16), dtype=bool)).reshape(1, 1, 8, 16))
+    t = g.add_node("Mul", [x, g.constant(np.float32(0.125))]).output
+    t = g.add_node("Where", [causal, t, g.constant(np.float32(-1e9))]).output
+    g.add_output(g.add_node("Softmax", [t], attrs={"axis": -1}).output, "p")
+    u = g.add_node("Div", [x, g.constant(np.float32(4.0))]).output
+    u = g.add_node("Add", [u, m]).output
+    g.add_output(g.add_node("LogSoftmax", [u], attrs={"axis": 3}).output, "lp")
+    w = g.add_node("Mul", [z, g.constant(np.float32(2.0))]).output
+    g.add_output(g.add_node("Softmax", [w], attrs={"axis": -1}).output, "q")
+    infer_shapes(g)
+    mask = np.where(r.random((2, 1, 1, 16)) > 0.25, 0.0, -10000.0).astype(np.float32)
+    return g, {"x": f32(r, 2, 3, 8, 16, scale=3), "m": mask, "z": f32(r, 4, 6)}
+
+
+def _p_softmax_programs(r: np.random.Generator) -> tuple[Graph, dict[str, np.ndarray]]:
+    """Softmax over elementwise programs of other shapes: a chain with a tensor operand
+    (x * w + 1), a program that reuses an earlier result ((x + 1) * (x - 1), no chain), and rows
+    of 256 (two groups of four per lane)."""
+    g = Graph("softmax_programs")
+    x = g.add_input("x", TensorType("float32", (3, 5, 32)))
+    w = g.add_input("w", TensorType("float32", (5, 1)))
+    z = g.add_input("z", TensorType("float32", (2, 256)))
+    t = g.add_node("Mul", [x, w]).output
+    t = g.add_node("Add", [t, g.constant(np.float32(1.0))]).output
+    g.add_output(g.add_node("Softmax", [t], attrs={"axis": -1}).output, "chain")
+    a = g.add_node("Add", [x, g.constant(np.float32(1.0))]).output
+    b = g.add_node("Sub", [x, g.constant(np.float32(1.0))]).output
+    g.add_output(g.add_node("LogSoftmax", [g.add_node("Mul", [a, b]).output], attrs={"axis": -1}).output, "general")
+    u = g.add_node("Mul", [z, g.constant(np.float32(0.5))]).output
+    g.add_output(g.add_node("Softmax", [u], attrs={"axis": 1}).output, "wide")
+    infer_shapes(g)
+    return g, {"x": f32(r, 3, 5, 32), "w": f32(r, 5, 1), "z": f32(r, 2, 256, scale=4)}
+
+
 def pattern_cases() -> list[Case]:
     return [
         _pattern("conv_block", _p_conv_block),
@@ -361,6 +405,8 @@ def pattern_cases() -> list[Case]:
         _pattern("dense_gelu", _p_dense_gelu),
         _pattern("layer_norm", _p_layer_norm),
         _pattern("loopfuse", _p_loopfuse),
+        _pattern("masked_softmax", _p_masked_softmax),
+        _pattern("softmax_programs", _p_softmax_programs),
     ]
 
 

@@ -176,3 +176,17 @@ def test_input_slice_plan_of_resnet50(strategy: str, records: int) -> None:
 def test_input_slice_plan_needs_a_batch() -> None:
     low = lower_graph(o3(zoo.resnet50(batch=1)), "greedy_by_size", True, "tf32")
     assert lowering.input_slice_plan(low, 4) is None
+
+
+@pytest.mark.parametrize("name", ["bert", "gpt2"])
+def test_attention_scale_and_mask_run_inside_the_softmax(name: str) -> None:
+    """Every layer's score scale + mask program (BERT: additive fp32 mask; GPT-2: causal bool mask
+    through Where) is evaluated by the softmax that reads it: no K_ELEMENTWISE record for it, and
+    one K_SOFTMAX record per layer carrying the program."""
+    g = getattr(zoo, name)(batch=2, seq=128)
+    optimize(g, "O3")
+    schedule(g)
+    low = lower_graph(g)
+    assert low.kernels.get("elementwise into softmax") == 12
+    soft = [r for r in low.launches if r.kind == lowering.K_SOFTMAX]
+    assert len(soft) == 12 and all(r.i[4] == 1 and r.aux_len > 0 for r in soft)
