@@ -253,6 +253,9 @@ class CudaEmitter:
         # id(value) -> (source, element strides) of a Transpose that MatMul reads through (not copied)
         self._through: dict[int, tuple[Value, list[int]]] = {}
         self._pack_regions: list[tuple[int, int]] = []  # (offset, bytes) of each packed image
+        # id(value) -> element strides of a Transpose output stored K-major for MatMul (see
+        # _kmajor_b_only); every reader goes through _view
+        self._stored: dict[int, list[int]] = {}
         # Transposes whose input MatMul wrote their output directly (see _write_through)
         self._written_through: set[int] = set()
         # id(value) -> aux words of the elementwise program that the softmax reading it evaluates
@@ -552,6 +555,24 @@ class CudaEmitter:
                     return False
         return True
 
+    def _kmajor_b_only(self, out: Value, view_strides: list[int]) -> bool:
+        """Whether a Transpose's output is read only as the N-major B operand of batched MatMuls
+        in TF32 mode (attention's values in P @ V), so that it can be stored K-major instead of
+        being copied once more by the MatMul."""
+        t = out.tensor_type
+        if self.precision != "tf32" or t.rank < 3 or t.dtype != "float32" or not out.users:
+            return False
+        if any(v is out for _, v in self.graph.named_outputs()):
+            return False
+        if self.plan.location(out).kind != "arena":
+            return False
+        for user in out.users:
+            if user.op != "MatMul" or user.input(1) is not out or user.input(0) is out:
+                return False
+            if user.input(0).tensor_type.rank < 3:
+                return False
+        return True
+
     def op_Transpose(self, node: Node) -> None:
         if id(node) in self._written_through:
             self.kernels["view"] = self.kernels.get("view", 0) + 1
@@ -563,6 +584,17 @@ class CudaEmitter:
         out = node.output
         if self._read_through(node, x, [ss[p] for p in perm]):
             self._through[id(out)] = (x, [ss[p] for p in perm])
+            return
+        if self._kmajor_b_only(out, [ss[p] for p in perm]):
+            # every reader is a batched MatMul taking it as an N-major B: store it K-major
+            # ([..., n, k]) in its own buffer, so the MatMul reads it as it is
+            kshape = [*shape[:-2], shape[-1], shape[-2]]
+            kst = _strides(kshape)
+            stored = [*kst[:-2], kst[-1], kst[-2]]
+            self._stored[id(out)] = stored
+            src = [ss[p] for p in perm]
+            self._copy(kshape, self.ref(x), [*src[:-2], src[-1], src[-2]], 0, self.ref(out), kst, 0,
+                       x.tensor_type.itemsize, count="transpose")
             return
         users = out.users
         if (len(users) == 1 and users[0].inputs and users[0].inputs[0] is out and self._tap_packed(users[0])
@@ -1024,6 +1056,8 @@ class CudaEmitter:
         if id(value) in self._through:
             src, strides = self._through[id(value)]
             return self.ref(src), list(strides)
+        if id(value) in self._stored:
+            return self.ref(value), list(self._stored[id(value)])
         return self.ref(value), _strides(value.tensor_type.shape)
 
     def _write_through(self, node: Node) -> tuple[RefT, int, list[int]] | None:
