@@ -549,8 +549,9 @@ template <int BN, int MODE, int RB = 0, int PAIR = 0, int SR = 0>
 struct Cfg {
     static_assert(!SR || (!PAIR && MODE == TF32), "a separate residual buffer is a one-CTA TF32 form");
     static_assert(!PAIR || MODE == TF32, "CTA pairs run TF32 mode only");
-    static constexpr bool WIDE = PAIR && BN == 256;
-    static_assert(BN <= 128 || (WIDE && RB == 0), "N tiles of 256 are pair-only, without B residency");
+    static constexpr bool WIDE = PAIR && BN > 128;
+    static_assert(BN <= 128 || (WIDE && RB == 0 && BN % 64 == 0 && BN <= 256),
+                  "N tiles of 192 and 256 are pair-only, without B residency");
     static_assert(MODE != DYN || (!PAIR && !RB && !SR), "dynamic-B GEMMs run one CTA per tile");
     static constexpr bool ONEACC = WIDE || MODE == DYN;     // one accumulator (no B_lo columns)
     static constexpr int REGIONS = MODE == STRICT ? 4 : 1;  // TMEM regions per K block
@@ -581,12 +582,15 @@ struct Cfg {
     static constexpr uint32_t BUF_COLS = MODE == STRICT ? REGIONS * BN : ONEACC ? BN : 2 * BN;
     static constexpr int TBUFS = (512 / BUF_COLS) > 4 ? 4 : (512 / BUF_COLS);  // TMEM buffers in the ring
     static constexpr uint32_t TMEM_COLS = TBUFS * BUF_COLS;
+    // columns allocated: a power of two (two buffers of 192 take 512)
+    static constexpr uint32_t TMEM_ALLOC = TMEM_COLS <= 32 ? 32 : TMEM_COLS <= 64 ? 64 : TMEM_COLS <= 128 ? 128
+                                           : TMEM_COLS <= 256 ? 256 : 512;
     // fixed part; a B-resident launch adds its B panel (b_res_bytes) in front of the stages
     static constexpr uint32_t SMEM_BYTES =
         STAGES * STAGE_BYTES + OUT_BYTES + RES_BYTES + 1024 /*align*/ + BAR_BYTES + BN * 4 /*bias*/;
     static constexpr uint32_t B_RES_MAX = RB ? SMEM_LIMIT - SMEM_BYTES : 0;
     static_assert((3 * 8 + 2 * 4 + 3) * 8 + 4 <= BAR_BYTES, "barrier area");
-    static_assert(TMEM_COLS <= 512 && (TMEM_COLS & (TMEM_COLS - 1)) == 0, "TMEM columns");
+    static_assert(TMEM_COLS <= 512, "TMEM columns");
     static_assert(TBUFS >= 2, "need at least two TMEM buffers");
 };
 
@@ -673,8 +677,8 @@ __global__ void __launch_bounds__(THREADS, 1) umma_gemm_kernel(const __grid_cons
         fence_barrier_init();
     }
     if (warp == 1) {
-        if (PAIR) tmem_alloc_pair(tmem_slot, C::TMEM_COLS);
-        else tmem_alloc(tmem_slot, C::TMEM_COLS);
+        if (PAIR) tmem_alloc_pair(tmem_slot, C::TMEM_ALLOC);
+        else tmem_alloc(tmem_slot, C::TMEM_ALLOC);
     }
     tc_fence_before();
     __syncthreads();
@@ -1261,8 +1265,8 @@ __global__ void __launch_bounds__(THREADS, 1) umma_gemm_kernel(const __grid_cons
     if (PAIR) cluster_sync_all();  // no CTA of a pair leaves while its peer may still signal it
     if (warp == 1) {
         tc_fence_after();
-        if (PAIR) tmem_dealloc_pair(tmem_base, C::TMEM_COLS);
-        else tmem_dealloc(tmem_base, C::TMEM_COLS);
+        if (PAIR) tmem_dealloc_pair(tmem_base, C::TMEM_ALLOC);
+        else tmem_dealloc(tmem_base, C::TMEM_ALLOC);
     }
 }
 
@@ -1513,12 +1517,13 @@ inline int pair_clusters() {
     return n;
 }
 
-// Wide CTA-pair launch: 256 x 256 tiles (p.m_tiles and p.n_tiles count them; p.tmB boxes both
-// planes of 128 rows).
+// Wide CTA-pair launch: 256 x BN tiles, BN 192 or 256 (p.m_tiles and p.n_tiles count them;
+// p.tmB boxes both planes of BN / 2 rows).
+template <int BN>
 inline int launch_wide(Params &p, int clusters, cudaStream_t stream) {
     p.b_res_bytes = 0;
     const long long tiles = (long long)p.n_tiles * p.m_tiles;
-    return launch<256, TF32, 0, 1>(p, 2 * (int)(tiles < clusters ? tiles : clusters), stream);
+    return launch<BN, TF32, 0, 1>(p, 2 * (int)(tiles < clusters ? tiles : clusters), stream);
 }
 
 // CTA-pair launch (TF32 mode, tiled or 32-channel im2col A): p.m_tiles counts 256-row tiles and
@@ -1717,24 +1722,41 @@ inline int try_gemm_umma(const GemmParams &p, cudaStream_t stream, int *taken) {
     }();
     // Wide pairs (256 x 256 tiles: per K block a CTA loads 16 KB of A and 32 KB of B for 128 x
     // 256 outputs, a quarter less than the 256 x 128 pair tile) for N >= 256 and long K.
-    // MGC_CUDA_WIDE=0 never uses them, =1 whenever the form allows.
+    // MGC_CUDA_WIDE=0 never uses them, =1 the 256 form whenever it is allowed (tests).
     static const int wide_env = [] {
         const char *e = getenv("MGC_CUDA_WIDE");
-        return e && e[0] == '0' ? 0 : e && e[0] == '1' ? 1 : 2;
+        return e && e[0] == '0' ? 0 : e && strcmp(e, "192") == 0 ? 3 : e && e[0] == '1' ? 1 : 2;
     }();
     // A wide tile does the work of two 256 x 128 pair tiles in about 0.88 of their time
     // (measured, ResNet-50 3x3 layers), so it is taken when its waves of tiles over the pairs of
-    // SMs cost less than the pair form's.
+    // SMs cost less than the pair form's. Tiles of 256 x 192 (one and a half pair tiles, costed
+    // at 1.38) fill the pairs better where N is a multiple of 192 but not of 256 (the 768-wide
+    // projections of BERT and GPT-2: 64 tiles in one wave instead of 96 pair tiles in two).
+    // MGC_CUDA_WIDE=192 takes the 192 form whenever the form allows.
     if (!strict && pair_env != 0 && wide_env != 0 && (u.im2col == 0 || u.im2col == 1) && bn == 128 && p.N > 128) {
-        const long long pair_m = ceil_div(p.M, 2 * umma::BM), wide_n = ceil_div(p.N, 256);
+        const long long pair_m = ceil_div(p.M, 2 * umma::BM), wide_n = ceil_div(p.N, 256), w3_n = ceil_div(p.N, 192);
         const bool worth = u.num_kb >= (p.res ? 16 : 8);
-        const int clusters = umma::pair_clusters<256, 0>();
+        const int clusters = umma::pair_clusters<256, 0>(), clusters3 = umma::pair_clusters<192, 0>();
         const long long waves_w = clusters > 0 ? ceil_div(pair_m * wide_n, clusters) : 0;
         const long long waves_p = clusters > 0 ? ceil_div(pair_m * u.n_tiles, clusters) : 0;
-        if (clusters > 0 && (wide_env == 1 || (worth && pair_m * wide_n >= clusters && 176 * waves_w < 100 * waves_p))) {
+        const long long waves_3 = clusters3 > 0 ? ceil_div(pair_m * w3_n, clusters3) : 0;
+        const bool w256 = clusters > 0 && (wide_env == 1 || (worth && pair_m * wide_n >= clusters && 176 * waves_w < 100 * waves_p));
+        const bool w192 = !w256 && clusters3 > 0 && clusters3 == clusters &&
+                          (wide_env == 3 || (wide_env == 2 && worth && 138 * waves_3 < 100 * waves_p));
+        CUtensorMap map3;
+        if (w192 && umma::make_map_b(&map3, p.b_umma, p.b_umma_lo, p.N, kp, 96)) {
+            u.tmB = map3;
+            u.m_tiles = (int)pair_m;
+            u.n_tiles = (int)w3_n;
+            const int st = umma::launch_wide<192>(u, clusters3, stream);
+            if (st != MGC_CUDA_OK) return st;
+            *taken = 1;
+            return MGC_CUDA_OK;
+        }
+        if (w256) {
             u.m_tiles = (int)pair_m;
             u.n_tiles = (int)wide_n;
-            const int st = umma::launch_wide(u, clusters, stream);
+            const int st = umma::launch_wide<256>(u, clusters, stream);
             if (st != MGC_CUDA_OK) return st;
             *taken = 1;
             return MGC_CUDA_OK;

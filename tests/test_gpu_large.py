@@ -91,7 +91,10 @@ def _tf32_exact(a: np.ndarray) -> np.ndarray:
 # (M, K, N) reaching each tensor-core form: one CTA per 128-row tile; a CTA pair per 256-row
 # tile with one B plane in each CTA (N tiles of 128, long K, enough pair tiles to fill the
 # GPU); a wide pair (256 x 256 tiles, N > 128; N = 640 leaves a partial last tile)
-GEMM_FORMS = {"single": (1024, 512, 128), "pair": (20480, 512, 128), "wide": (9728, 512, 640)}
+# (M, K, N) that select each tile form; "wide192": 256 x 192 pair tiles, ragged in M and in N
+# (704 = 3 x 192 + 128), chosen because 64 of them fill the SM pairs in one wave
+GEMM_FORMS = {"single": (1024, 512, 128), "pair": (20480, 512, 128), "wide": (9728, 512, 640),
+              "wide192": (4000, 768, 704)}
 
 
 @pytest.mark.parametrize("form", sorted(GEMM_FORMS))
