@@ -43,6 +43,9 @@ struct GemmParams {
     // TMA box (0: not used) and the padded length of one window row (B is [N][KH][win_L])
     int win_rows, win_L;
     int *err;                     // device word for bounded-wait timeouts (may be NULL)
+    // split-K scratch of the model (NULL: no split): room for the partial tiles
+    float *split_ws;
+    long long split_ws_floats;
 };
 
 __device__ __forceinline__ float fetch_a(const GemmParams &p, const float *a, long long m, long long k) {

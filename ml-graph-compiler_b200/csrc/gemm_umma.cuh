@@ -98,6 +98,12 @@ struct Params {
     float alpha, lo, hi;
     int act;
     int *err;
+    // split K (one-CTA TF32 tiles): work unit (tile, ks) runs K blocks [ks * kb_per,
+    // (ks + 1) * kb_per) and leaves its raw partial tile in part ([tile][split][BM][BN]);
+    // split_reduce_kernel sums the partials in split order and applies the epilogue.
+    // splits <= 1: no split.
+    int splits, kb_per;
+    float *part;
 };
 
 // ---- PTX wrappers -----------------------------------------------------------------------------
@@ -646,8 +652,14 @@ __global__ void __launch_bounds__(THREADS, 1) umma_gemm_kernel(const __grid_cons
         b2 = bt / p.nbatch1;
         b1 = bt - b2 * p.nbatch1;
     };
-    // the i-th tile of this CTA (or pair) as (M tile, N tile); false past the last
-    auto tile_at = [&](int i, int &mt, int &nt) -> bool {
+    // split K: the work units are (tile, split) pairs; K blocks [kb_lo(ks), kb_hi(ks)) per unit
+    const int splits = p.splits > 1 ? p.splits : 1;
+    const int kb_per = splits > 1 ? p.kb_per : num_kb;
+    auto kb_lo = [&](int ks) { return ks * kb_per; };
+    auto kb_hi = [&](int ks) { return (ks + 1) * kb_per < num_kb ? (ks + 1) * kb_per : num_kb; };
+    // the i-th work unit of this CTA (or pair) as (M tile, N tile, split); false past the last
+    auto unit_at = [&](int i, int &mt, int &nt, int &ks) -> bool {
+        ks = 0;
         if (RB) {
             const int per = units / p.n_tiles;
             nt = unit % p.n_tiles;
@@ -655,9 +667,15 @@ __global__ void __launch_bounds__(THREADS, 1) umma_gemm_kernel(const __grid_cons
             return unit < per * p.n_tiles && mt < p.m_tiles;
         }
         const int t = unit + i * units;
-        nt = t % p.n_tiles;
-        mt = t / p.n_tiles;
-        return t < total_tiles;
+        const int tt = splits > 1 ? t / splits : t;
+        if (splits > 1) ks = t - tt * splits;
+        nt = tt % p.n_tiles;
+        mt = tt / p.n_tiles;
+        return tt < total_tiles;
+    };
+    auto tile_at = [&](int i, int &mt, int &nt) -> bool {
+        int ks;
+        return unit_at(i, mt, nt, ks);
     };
 
     if (threadIdx.x == 0) {
@@ -784,10 +802,12 @@ __global__ void __launch_bounds__(THREADS, 1) umma_gemm_kernel(const __grid_cons
                     else tma_load_3d(b_tile(0, kb), &p.tmB, bres_full, kb * BK, nt * BN, 0);
                 }
             }
-            for (int i = 0; ok && tile_at(i, mt, nt); ++i) {
+            int ks;
+            for (int i = 0; ok && unit_at(i, mt, nt, ks); ++i) {
                 const int n0 = nt * BN;
                 int m0 = mt * C::TM + row0, db1 = 0, db2 = 0;
                 if (MODE == DYN) dyn_rows(mt, m0, db1, db2);
+                const int klo = kb_lo(ks), khi = kb_hi(ks);
                 int wb = 0, hb = 0, nb = 0;
                 if (p.im2col) {
                     const int hw = p.OH * p.OW;
@@ -801,7 +821,14 @@ __global__ void __launch_bounds__(THREADS, 1) umma_gemm_kernel(const __grid_cons
                 // per block; the tap offsets are kept as the box's 16-bit offsets
                 int cb = 0, kw = 0;
                 uint16_t off_w = 0, off_h = 0;
-                for (int kb = 0; kb < num_kb; ++kb, ++g, pos.advance()) {
+                if (p.im2col && klo > 0) {  // a split's first K block (one division per unit)
+                    const int tap = klo / p.cblocks, kh = tap / p.KW;
+                    cb = klo - tap * p.cblocks;
+                    kw = tap - kh * p.KW;
+                    off_w = (uint16_t)(kw * p.DW);
+                    off_h = (uint16_t)(kh * p.DH);
+                }
+                for (int kb = klo; kb < khi; ++kb, ++g, pos.advance()) {
                     const int s = pos.slot;
                     if (pos.wrapped && !free_next && !mbar_wait(&empty[s], pos.phase ^ 1u)) {
                         set_error(p.err, MGC_CUDA_TIMEOUT);
@@ -854,11 +881,11 @@ __global__ void __launch_bounds__(THREADS, 1) umma_gemm_kernel(const __grid_cons
             RingPos<S> pos;  // stage of the next K block
             bool ok = true;
             bool free_next = false;  // that stage was tested free
-            int mt, nt;
-            for (int i = 0; ok && tile_at(i, mt, nt); ++i) {
+            int mt, nt, ks;
+            for (int i = 0; ok && unit_at(i, mt, nt, ks); ++i) {
                 int dm0 = 0, db1 = 0, db2 = 0;
                 if (MODE == DYN) dyn_rows(mt, dm0, db1, db2);
-                for (int kb = 0; kb < num_kb; ++kb, pos.advance()) {
+                for (int kb = kb_lo(ks); kb < kb_hi(ks); ++kb, pos.advance()) {
                     const int s = pos.slot;
                     if (pos.wrapped && !free_next && !mbar_wait(&empty[s], pos.phase ^ 1u)) {
                         set_error(p.err, MGC_CUDA_TIMEOUT);
@@ -901,12 +928,14 @@ __global__ void __launch_bounds__(THREADS, 1) umma_gemm_kernel(const __grid_cons
             // next K block's stage is tested right after this block's first MMA is issued, and
             // a block whose stage tested complete skips its wait.
             bool have = false;
-            for (int i = 0; ok && tile_at(i, mt, nt); ++i) {
-                for (int kb = 0; kb < num_kb; ++kb, pos.advance()) {
+            int ks;
+            for (int i = 0; ok && unit_at(i, mt, nt, ks); ++i) {
+                const int klo = kb_lo(ks), khi = kb_hi(ks);
+                for (int kb = klo; kb < khi; ++kb, pos.advance()) {
                     const int s = pos.slot;
                     const int b = buf.slot;
                     // a TMEM buffer per K block (strict) or per tile (TF32)
-                    const bool first = MODE == STRICT || kb == 0, last = MODE == STRICT || kb == num_kb - 1;
+                    const bool first = MODE == STRICT || kb == klo, last = MODE == STRICT || kb == khi - 1;
                     if (!have && !mbar_wait(&ready[s], pos.phase)) {
                         set_error(p.err, MGC_CUDA_TIMEOUT);
                         ok = false;
@@ -1112,10 +1141,10 @@ __global__ void __launch_bounds__(THREADS, 1) umma_gemm_kernel(const __grid_cons
             for (int sl = 0; sl < EN / 32; ++sl)
                 tma_load_2d(res_tile + sl * (BM * 128), &p.tmR, res_full, tn0 + sl * 32, tm0);
         };
-        int mt, nt;
+        int mt, nt, ks;
         if (res_tma && issuer && tile_at(0, mt, nt)) issue_residual(mt, nt, 0);
         int local = 0;  // epilogue passes this CTA has finished
-        for (int i = 0; ok && tile_at(i, mt, nt); ++i) {
+        for (int i = 0; ok && unit_at(i, mt, nt, ks); ++i) {
           int m0 = mt * C::TM + row0, db1 = 0, db2 = 0;
           if (MODE == DYN) dyn_rows(mt, m0, db1, db2);
           if (MODE == STRICT) {
@@ -1132,6 +1161,15 @@ __global__ void __launch_bounds__(THREADS, 1) umma_gemm_kernel(const __grid_cons
             if (MODE != STRICT && !load_pass(h)) {
                 ok = false;
                 break;
+            }
+            if (MODE == TF32 && !PAIR && !RB && NH == 1 && splits > 1) {
+                // split K: this unit's raw partial tile (its row, this thread's columns); the
+                // reduce kernel that follows on the stream applies the epilogue
+                float *mine = p.part + ((size_t)(mt * p.n_tiles + nt) * splits + ks) * (BM * BN) + (size_t)row * BN + hc;
+#pragma unroll
+                for (int j = 0; j < HALF; j += 4)
+                    *reinterpret_cast<float4 *>(mine + j) = make_float4(acc[j], acc[j + 1], acc[j + 2], acc[j + 3]);
+                continue;
             }
             // this pass's bias columns into shared memory, one coalesced load (the previous
             // pass's readers have all passed its second barrier)
@@ -1267,6 +1305,27 @@ __global__ void __launch_bounds__(THREADS, 1) umma_gemm_kernel(const __grid_cons
         tc_fence_after();
         if (PAIR) tmem_dealloc_pair(tmem_base, C::TMEM_ALLOC);
         else tmem_dealloc(tmem_base, C::TMEM_ALLOC);
+    }
+}
+
+// Split-K epilogue: out[m][n] = act(alpha * sum_ks part[tile][ks][m % 128][n % BN] + bias[n]
+// (+ res[m][n])), the partials summed in split order (the same result on every run), one
+// output per thread; the same arithmetic as the tile epilogue's direct path.
+__global__ void __launch_bounds__(256) split_reduce_kernel(const float *part, int splits, int n_tiles, int bn, int M,
+                                                           int N, float *c, long long ldc, const float *bias,
+                                                           const float *res, long long ldr, float alpha, int act,
+                                                           float lo, float hi) {
+    const long long total = (long long)M * N;
+    for (long long e = (long long)blockIdx.x * blockDim.x + threadIdx.x; e < total;
+         e += (long long)gridDim.x * blockDim.x) {
+        const int m = (int)(e / N), n = (int)(e - (long long)m * N);
+        const int mt = m / BM, nt = n / bn;
+        const float *src = part + ((size_t)(mt * n_tiles + nt) * splits) * (BM * bn) + (size_t)(m - mt * BM) * bn + (n - nt * bn);
+        float acc = 0.0f;
+        for (int ks = 0; ks < splits; ++ks) acc += src[(size_t)ks * (BM * bn)];
+        float x = alpha * acc + (bias ? bias[n] : 0.0f);
+        if (res) x += res[(long long)m * ldr + n];
+        c[(long long)m * ldc + n] = apply_act(x, act, lo, hi);
     }
 }
 
@@ -1775,6 +1834,45 @@ inline int try_gemm_umma(const GemmParams &p, cudaStream_t stream, int *taken) {
             if (st != MGC_CUDA_OK) return st;
             *taken = 1;
             return MGC_CUDA_OK;
+        }
+    }
+    // Split K when the tiles cover at most half the SMs and K is long (the late layers at batch
+    // 1: a 3x3 C512 convolution is 4 tiles of 144 K blocks): K blocks in runs of at least 4, as
+    // many runs as fill the SMs; the units leave raw partial tiles in the model's split scratch
+    // and split_reduce_kernel sums them and runs the epilogue. MGC_CUDA_SPLIT=0 never splits.
+    static const bool split_env = [] {
+        const char *e = getenv("MGC_CUDA_SPLIT");
+        return !(e && e[0] == '0');
+    }();
+    if (split_env && !strict && p.split_ws && (u.im2col == 0 || u.im2col == 1) && u.num_kb >= 8) {
+        const long long tiles = (long long)u.n_tiles * m_tiles;
+        const int sms = sm_count();
+        if (tiles * 2 <= sms) {
+            const long long want = sms / tiles;
+            long long kb_per = ceil_div(u.num_kb, want);
+            if (kb_per < 4) kb_per = 4;
+            const long long splits = ceil_div(u.num_kb, kb_per);
+            if (splits > 1 && tiles * splits * umma::BM * bn <= p.split_ws_floats) {
+                u.splits = (int)splits;
+                u.kb_per = (int)kb_per;
+                u.part = p.split_ws;
+                u.tma_out = 0;
+                u.tma_res = 0;
+                u.b_res_bytes = 0;
+                const long long units = tiles * splits;
+                const int grid = (int)(units < sms ? units : sms);
+                int st = bn == 64 ? umma::launch<64, umma::TF32, 0, 0, 0>(u, grid, stream)
+                                  : umma::launch<128, umma::TF32, 0, 0, 0>(u, grid, stream);
+                if (st != MGC_CUDA_OK) return st;
+                const long long outs = (long long)p.M * p.N;
+                umma::split_reduce_kernel<<<grid_for(outs, 256), 256, 0, stream>>>(
+                    p.split_ws, (int)splits, u.n_tiles, bn, p.M, p.N, p.c, p.ldc, p.bias, p.res, p.ldr, p.alpha, p.act,
+                    p.lo, p.hi);
+                st = check_launch("split_reduce_kernel");
+                if (st != MGC_CUDA_OK) return st;
+                *taken = 1;
+                return MGC_CUDA_OK;
+            }
         }
     }
     // persistent grid: one CTA per SM (the shared-memory footprint allows no more). With a

@@ -20,6 +20,9 @@ struct Bases {
     char *workspace = nullptr;
     const std::vector<char *> *inputs = nullptr;
     const std::vector<char *> *outputs = nullptr;
+    // split-K scratch of a model (none for raw-pointer calls)
+    float *split_ws = nullptr;
+    long long split_ws_floats = 0;
 };
 
 inline int resolve(const mgc_cuda_ref &r, const Bases &b, void **out) {
@@ -243,6 +246,8 @@ inline int launch_record(const mgc_cuda_launch &L, const int64_t *aux, int64_t a
         GemmParams p;
         MGC_CHECK(decode_gemm(L, bases, p));
         p.err = status_dev;
+        p.split_ws = bases.split_ws;
+        p.split_ws_floats = bases.split_ws_floats;
         st = run_gemm(p, stream);
         break;
     }

@@ -19,6 +19,9 @@ using namespace mgc;
 
 namespace {
 
+// split-K scratch per model: 32 MiB of partial tiles (GEMMs with fewer tiles than SMs)
+constexpr long long SPLIT_WS_FLOATS = 8ll << 20;
+
 struct Model {
     int device = 0;
     cudaStream_t stream = nullptr;
@@ -34,6 +37,7 @@ struct Model {
     std::vector<int64_t> aux;
     int *status_dev = nullptr;
     int *status_host = nullptr;
+    float *split_ws = nullptr;  // split-K partial tiles
     cudaGraph_t graph = nullptr;
     cudaGraphExec_t exec = nullptr;
     int kernel_launches = 0;
@@ -55,6 +59,8 @@ struct Model {
         b.workspace = workspace;
         b.inputs = &inputs;
         b.outputs = &outputs;
+        b.split_ws = split_ws;
+        b.split_ws_floats = split_ws ? SPLIT_WS_FLOATS : 0;
         return b;
     }
 
@@ -114,9 +120,10 @@ struct Model {
         if (workspace) cudaFree(workspace);
         if (status_dev) cudaFree(status_dev);
         if (status_host) cudaFreeHost(status_host);
+        if (split_ws) cudaFree(split_ws);
         if (stream) cudaStreamDestroy(stream);
         exec = nullptr; graph = nullptr; stream = nullptr; arena = nullptr; weights = nullptr; workspace = nullptr;
-        status_dev = nullptr; status_host = nullptr;
+        status_dev = nullptr; status_host = nullptr; split_ws = nullptr;
         inputs.clear(); outputs.clear();
     }
 };
@@ -166,6 +173,7 @@ int create(Model &m, const mgc_cuda_launch *launches, int n_launches, const int6
     }
     MGC_CHECK_CUDA(cudaMalloc((void **)&m.status_dev, sizeof(int)));
     MGC_CHECK_CUDA(cudaMallocHost((void **)&m.status_host, sizeof(int)));
+    MGC_CHECK_CUDA(cudaMalloc((void **)&m.split_ws, (size_t)SPLIT_WS_FLOATS * sizeof(float)));
     // capture the schedule into one CUDA Graph
     MGC_CHECK_CUDA(cudaStreamBeginCapture(m.stream, cudaStreamCaptureModeThreadLocal));
     int kernels = 0;

@@ -92,9 +92,10 @@ def _tf32_exact(a: np.ndarray) -> np.ndarray:
 # tile with one B plane in each CTA (N tiles of 128, long K, enough pair tiles to fill the
 # GPU); a wide pair (256 x 256 tiles, N > 128; N = 640 leaves a partial last tile)
 # (M, K, N) that select each tile form; "wide192": 256 x 192 pair tiles, ragged in M and in N
-# (704 = 3 x 192 + 128), chosen because 64 of them fill the SM pairs in one wave
+# (704 = 3 x 192 + 128), chosen because 64 of them fill the SM pairs in one wave; "split": two
+# tiles of 144 K blocks, split K into 36 runs of 4 whose partial tiles are summed in order
 GEMM_FORMS = {"single": (1024, 512, 128), "pair": (20480, 512, 128), "wide": (9728, 512, 640),
-              "wide192": (4000, 768, 704)}
+              "wide192": (4000, 768, 704), "split": (100, 4608, 256)}
 
 
 @pytest.mark.parametrize("form", sorted(GEMM_FORMS))
@@ -117,8 +118,11 @@ def test_tf32_gemm_keeps_weights_exact(form: str) -> None:
     model = compile_graph(g, precision="tf32")
     try:
         got = model.run({"x": x})["y"].astype(np.float64)
+        # the split form sums its partial tiles in a fixed order: repeated runs agree bit for bit
+        again = model.run({"x": x})["y"].astype(np.float64)
     finally:
         model.close()
+    assert np.array_equal(got, again), f"{form}: two runs differ"
     want = x.astype(np.float64) @ w.astype(np.float64) + bias.astype(np.float64)
     err = float(np.abs(got - want).max() / np.abs(want).max())
     assert err <= 2e-5, f"{form}: max error {err:.3g} of the largest output"
