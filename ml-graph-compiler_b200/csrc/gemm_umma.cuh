@@ -1321,8 +1321,18 @@ __global__ void __launch_bounds__(256) split_reduce_kernel(const float *part, in
         const int m = (int)(e / N), n = (int)(e - (long long)m * N);
         const int mt = m / BM, nt = n / bn;
         const float *src = part + ((size_t)(mt * n_tiles + nt) * splits) * (BM * bn) + (size_t)(m - mt * BM) * bn + (n - nt * bn);
+        // eight partials in flight at a time, added in split order
+        const size_t step = (size_t)BM * bn;
         float acc = 0.0f;
-        for (int ks = 0; ks < splits; ++ks) acc += src[(size_t)ks * (BM * bn)];
+        int ks = 0;
+        for (; ks + 8 <= splits; ks += 8) {
+            float v[8];
+#pragma unroll
+            for (int j = 0; j < 8; ++j) v[j] = __ldcg(src + (size_t)(ks + j) * step);
+#pragma unroll
+            for (int j = 0; j < 8; ++j) acc += v[j];
+        }
+        for (; ks < splits; ++ks) acc += __ldcg(src + (size_t)ks * step);
         float x = alpha * acc + (bias ? bias[n] : 0.0f);
         if (res) x += res[(long long)m * ldr + n];
         c[(long long)m * ldc + n] = apply_act(x, act, lo, hi);
