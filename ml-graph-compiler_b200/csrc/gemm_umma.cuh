@@ -1854,13 +1854,19 @@ inline int try_gemm_umma(const GemmParams &p, cudaStream_t stream, int *taken) {
         const char *e = getenv("MGC_CUDA_SPLIT");
         return !(e && e[0] == '0');
     }();
-    if (split_env && !strict && p.split_ws && (u.im2col == 0 || u.im2col == 1) && u.num_kb >= 8) {
+    // shortest run of K blocks per unit (MGC_CUDA_SPLIT_KB, default 4)
+    static const int split_min_kb = [] {
+        const char *e = getenv("MGC_CUDA_SPLIT_KB");
+        const int v = e ? atoi(e) : 4;
+        return v >= 1 ? v : 4;
+    }();
+    if (split_env && !strict && p.split_ws && (u.im2col == 0 || u.im2col == 1) && u.num_kb >= 2 * split_min_kb) {
         const long long tiles = (long long)u.n_tiles * m_tiles;
         const int sms = sm_count();
         if (tiles * 2 <= sms) {
             const long long want = sms / tiles;
             long long kb_per = ceil_div(u.num_kb, want);
-            if (kb_per < 4) kb_per = 4;
+            if (kb_per < split_min_kb) kb_per = split_min_kb;
             const long long splits = ceil_div(u.num_kb, kb_per);
             if (splits > 1 && tiles * splits * umma::BM * bn <= p.split_ws_floats) {
                 u.splits = (int)splits;
