@@ -527,7 +527,8 @@ class CudaEmitter:
         strides instead of a copy (TF32 mode, where the tensor-core batched GEMM takes strided
         operands): every user is a MatMul that finds k (A) or k or n (B) contiguous in the view,
         the output is no graph output, and no node scheduled before the last such MatMul writes
-        memory the source occupies (the planner may reuse it once the Transpose has run)."""
+        memory the source occupies (the planner may reuse it once the Transpose has run). The
+        MatMul's own destination is checked when it is lowered (op_MatMul)."""
         out = node.output
         if self.precision != "tf32" or out.tensor_type.rank < 3 or x.tensor_type.dtype != "float32":
             return False
@@ -1127,6 +1128,7 @@ class CudaEmitter:
         a_bs = batch_strides(ashape, av if at.rank >= 2 else [0, 0])
         b_bs = batch_strides(bshape, bv if bt.rank >= 2 else [0, 0])
         c_bs = [s * m * n for s in _strides(batch_shape)]
+        ws_used = 0  # workspace bytes of this MatMul's operand copies (from offset 0)
         bconst = b.is_constant or self.plan.location(b).kind == "const"
         if bconst and not any(b_bs) and id(b) not in self._through:
             data = self.const_data(b).reshape(k, n)
@@ -1140,7 +1142,8 @@ class CudaEmitter:
                 tshape = [*own, n, k]
                 self._copy(tshape, bref, [*bv[:-2], b_cs, b_rs], 0, (SPACE_WORKSPACE, 0, 0), _strides(tshape), 0, 4,
                            count="transpose")
-                self._im2col_bytes = max(self._im2col_bytes, int(np.prod(tshape)) * 4)
+                ws_used = int(np.prod(tshape)) * 4
+                self._im2col_bytes = max(self._im2col_bytes, ws_used)
                 self._layout_workspace()
                 bref, b_rs, b_cs = (SPACE_WORKSPACE, 0, 0), 1, k
                 b_bs = batch_strides(bshape, [*_strides(own + [n * k])[:-1], 0, 0] if own else [0, 0])
@@ -1148,6 +1151,39 @@ class CudaEmitter:
         through = self._write_through(node)
         if through is not None:
             cref, ldc, c_bs = through
+        # An operand read through a Transpose whose source lies under this GEMM's destination
+        # (the planner may reuse the source's memory once the Transpose has run, and the GEMM
+        # would overwrite tiles it has yet to read) is first copied into the workspace: B
+        # K-major ([batch][n][k]), A row-major ([batch][m][k]).
+        dst = self._arena_range(node.output.users[0].output if through is not None else node.output)
+
+        def under_dst(v: Value) -> bool:
+            if dst is None or id(v) not in self._through:
+                return False
+            r = self._arena_range(self._through[id(v)][0])
+            return r is not None and r[0] < dst[1] and dst[0] < r[1]
+
+        if bt.rank >= 3 and bref[0] not in (SPACE_WORKSPACE, SPACE_WEIGHTS) and under_dst(b):
+            own = [int(d) for d in bshape[:-2]]
+            tshape = [*own, n, k]
+            off = -(-ws_used // BLOB_ALIGN) * BLOB_ALIGN
+            self._copy(tshape, bref, [*bv[:-2], b_cs, b_rs], 0, (SPACE_WORKSPACE, 0, off), _strides(tshape), 0, 4,
+                       count="transpose")
+            ws_used = off + int(np.prod(tshape)) * 4
+            bref, b_rs, b_cs = (SPACE_WORKSPACE, 0, off), 1, k
+            b_bs = batch_strides(bshape, [*_strides(own + [n * k])[:-1], 0, 0] if own else [0, 0])
+        if at.rank >= 3 and under_dst(a):
+            own = [int(d) for d in ashape[:-2]]
+            tshape = [*own, m, k]
+            off = -(-ws_used // BLOB_ALIGN) * BLOB_ALIGN
+            self._copy(tshape, aref, [*av[:-2], a_rs, a_cs], 0, (SPACE_WORKSPACE, 0, off), _strides(tshape), 0, 4,
+                       count="transpose")
+            ws_used = off + int(np.prod(tshape)) * 4
+            aref, a_rs, a_cs = (SPACE_WORKSPACE, 0, off), k, 1
+            a_bs = batch_strides(ashape, [*_strides(own + [m * k])[:-1], 0, 0] if own else [0, 0])
+        if ws_used > self._im2col_bytes:
+            self._im2col_bytes = ws_used
+            self._layout_workspace()
         dims, (a_bs, b_bs, c_bs) = _collapse(batch_shape, [a_bs, b_bs, c_bs])
         self._gemm(m, n, k, aref, a_rs, a_cs, bref, b_rs, b_cs, cref, ldc, b_lo=blo,
                    **self._umma_b(bref, blo), batch=dims, a_bs=a_bs, b_bs=b_bs, c_bs=c_bs, r_bs=[0] * len(dims))

@@ -397,6 +397,32 @@ def _p_softmax_programs(r: np.random.Generator) -> tuple[Graph, dict[str, np.nda
     return g, {"x": f32(r, 3, 5, 32), "w": f32(r, 5, 1), "z": f32(r, 2, 256, scale=4)}
 
 
+def _p_attention(r: np.random.Generator) -> tuple[Graph, dict[str, np.ndarray]]:
+    """Attention scores: Q Kᵀ (Kᵀ read through its Transpose) scaled, an additive mask over keys,
+    Softmax, then P V (the BERT form); and V Kᵀ divided, a causal Where, LogSoftmax (the GPT-2
+    form), the softmax evaluating the scale-and-mask program as it reads the scores."""
+    g = Graph("attention")
+    q = g.add_input("q", TensorType("float32", (2, 3, 16, 8)))
+    k = g.add_input("k", TensorType("float32", (2, 3, 16, 8)))
+    v = g.add_input("v", TensorType("float32", (2, 3, 16, 8)))
+    m = g.add_input("m", TensorType("float32", (2, 1, 1, 16)))
+    kt = g.add_node("Transpose", [k], attrs={"perm": [0, 1, 3, 2]}).output
+    s = g.add_node("MatMul", [q, kt]).output
+    t = g.add_node("Mul", [s, g.constant(np.float32(0.35))]).output
+    t = g.add_node("Add", [t, m]).output
+    pr = g.add_node("Softmax", [t], attrs={"axis": -1}).output
+    g.add_output(g.add_node("MatMul", [pr, v]).output, "o")
+    kt2 = g.add_node("Transpose", [k], attrs={"perm": [0, 1, 3, 2]}).output
+    s2 = g.add_node("MatMul", [v, kt2]).output
+    u = g.add_node("Div", [s2, g.constant(np.float32(2.5))]).output
+    causal = g.constant(np.tril(np.ones((16, 16), dtype=bool)).reshape(1, 1, 16, 16))
+    u = g.add_node("Where", [causal, u, g.constant(np.float32(-1e9))]).output
+    g.add_output(g.add_node("LogSoftmax", [u], attrs={"axis": -1}).output, "lp")
+    infer_shapes(g)
+    mask = np.where(r.random((2, 1, 1, 16)) > 0.25, 0.0, -10000.0).astype(np.float32)
+    return g, {"q": f32(r, 2, 3, 16, 8), "k": f32(r, 2, 3, 16, 8), "v": f32(r, 2, 3, 16, 8), "m": mask}
+
+
 def pattern_cases() -> list[Case]:
     return [
         _pattern("conv_block", _p_conv_block),
@@ -407,6 +433,7 @@ def pattern_cases() -> list[Case]:
         _pattern("loopfuse", _p_loopfuse),
         _pattern("masked_softmax", _p_masked_softmax),
         _pattern("softmax_programs", _p_softmax_programs),
+        _pattern("attention", _p_attention),
     ]
 
 

@@ -84,6 +84,40 @@ def test_resnet50_batch_is_independent_per_image() -> None:
     m1.close()
 
 
+@pytest.mark.parametrize("name", ["bert", "gpt2"])
+def test_transformer_batch_is_independent_per_sequence(name: str) -> None:
+    """Size-independent property at the benchmark batch: every sequence of a batch-32 TF32 run
+    (attention read through strides, the softmax over the mask program, 192-wide pair tiles,
+    several waves of tiles) equals the strict batch-1 model's output for that
+    sequence within the TF32 budget (2e-2 of the largest output), and so does the argmax along
+    the last axis wherever the strict run's top two values are further apart than twice the
+    budget (random-init GPT-2 logits have near-ties among 50,257 classes). Waves of tiles that
+    overwrote operands still to be read would break it."""
+    make = getattr(zoo, name)
+    g32 = make(batch=32, seq=128)
+    optimize(g32, "O3")
+    schedule(g32)
+    g1 = make(batch=1, seq=128)
+    optimize(g1, "O3")
+    schedule(g1)
+    feeds = zoo.feeds(g32, 7)
+    m32 = compile_graph(g32, precision="tf32")
+    y32 = m32.run(feeds)
+    m32.close()
+    m1 = compile_graph(g1, precision="strict")
+    for i in (0, 13, 31):
+        y1 = m1.run({k: v[i : i + 1] for k, v in feeds.items()})
+        for out, want in y1.items():
+            got = y32[out][i : i + 1]
+            scale = max(float(np.abs(want).max()), 1.0)
+            assert float(np.abs(got - want).max()) <= 2e-2 * scale, f"{name} sequence {i}: {out}"
+            w2 = want.reshape(-1, want.shape[-1])
+            top2 = np.sort(w2, axis=1)[:, -2:]
+            clear = top2[:, 1] - top2[:, 0] > 2 * 2e-2 * scale
+            np.testing.assert_array_equal(got.reshape(-1, got.shape[-1]).argmax(1)[clear], w2.argmax(1)[clear])
+    m1.close()
+
+
 def test_strategies_and_inplace_agree() -> None:
     """All planner strategies x in-place give the same outputs (reference test_codegen.py:414-423;
     the C backend is bit-identical, the CUDA kernels too since only offsets change)."""

@@ -190,3 +190,50 @@ def test_attention_scale_and_mask_run_inside_the_softmax(name: str) -> None:
     assert low.kernels.get("elementwise into softmax") == 12
     soft = [r for r in low.launches if r.kind == lowering.K_SOFTMAX]
     assert len(soft) == 12 and all(r.i[4] == 1 and r.aux_len > 0 for r in soft)
+
+
+def _gemm_span(rec, which: str) -> tuple[int, int] | None:
+    """Arena byte range a K_GEMM record's strided operand touches (None: not in the arena)."""
+    i = rec.i
+    slot = {"a": 0, "b": 1, "c": 2}[which]
+    if rec.r[slot].space != lowering.SPACE_ARENA:
+        return None
+    nb = i[3]
+    dims = [i[4 + d] for d in range(nb)]
+    if which == "a":
+        if i[24] != lowering.STRIDED:
+            return None
+        bs, extents = [i[8 + d] for d in range(nb)], [(i[0], i[25]), (i[2], i[26])]
+    elif which == "b":
+        if i[41] != lowering.STRIDED:
+            return None
+        bs, extents = [i[12 + d] for d in range(nb)], [(i[2], i[42]), (i[1], i[43])]
+    else:
+        bs, extents = [i[16 + d] for d in range(nb)], [(i[0], i[44]), (i[1], 1)]
+    last = sum((e - 1) * abs(s) for e, s in zip(dims, bs)) + sum((e - 1) * abs(s) for e, s in extents)
+    lo = rec.r[slot].offset
+    return lo, lo + (last + 1) * 4
+
+
+@pytest.mark.parametrize("name", ["bert", "gpt2"])
+@pytest.mark.parametrize("precision", ["tf32", "strict"])
+def test_no_gemm_writes_over_an_operand_it_reads(name: str, precision: str) -> None:
+    """A GEMM that reads an operand through strides (a Transpose read through) must not write
+    over that operand's memory: the planner may reuse a Transpose's source once the Transpose
+    has run, so the lowering copies such an operand into the workspace first."""
+    g = getattr(zoo, name)(batch=2, seq=128)
+    optimize(g, "O3")
+    schedule(g)
+    low = lower_graph(g, precision=precision)
+    checked = 0
+    for rec in low.launches:
+        if rec.kind != K_GEMM:
+            continue
+        c = _gemm_span(rec, "c")
+        for which in ("a", "b"):
+            r = _gemm_span(rec, which)
+            if c is None or r is None:
+                continue
+            checked += 1
+            assert not (r[0] < c[1] and c[0] < r[1]), f"GEMM of node {rec.node} writes over its {which} operand"
+    assert checked > 0
