@@ -2,7 +2,7 @@
 run it through ``CudaCompiledModel.run``: the smallest driver of a forward pass, for profiling
 one model at one size with external tools.
 
-    python ml-graph-compiler_b200/mgc_cuda/run_zoo.py bert --batch 32 --seq 128 --runs 1
+    python ml-graph-compiler_b200/mgc_cuda/run_zoo.py bert --batch 32 --seq 128 --strategy naive
     python ml-graph-compiler_b200/mgc_cuda/run_zoo.py resnet50 --batch 1
 
 The model is compiled once; ``--runs`` forward passes follow (the first replay of the CUDA Graph
@@ -38,11 +38,13 @@ def main(argv: list[str] | None = None) -> int:
     ap.add_argument("--seq", type=int, default=128, help="sequence length (bert, gpt2)")
     ap.add_argument("--runs", type=int, default=1)
     ap.add_argument("--precision", default="tf32", choices=["tf32", "strict", "fp32"])
+    ap.add_argument("--strategy", default="greedy_by_size", choices=["greedy_by_size", "first_fit", "naive"],
+                    help="the reference planner's memory strategy")
     args = ap.parse_args(argv)
     g = MODELS[args.model](args)
     optimize(g, "O3")
     schedule(g)
-    model = compile_graph(g, precision=args.precision)
+    model = compile_graph(g, precision=args.precision, strategy=args.strategy)
     try:
         feeds = zoo.feeds(g, 0)
         out = {}
