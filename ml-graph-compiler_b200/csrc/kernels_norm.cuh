@@ -577,6 +577,81 @@ __global__ void __launch_bounds__(256) depthwise_nhwc4_kernel(const __grid_const
     }
 }
 
+// NHWC, C % 4 == 0, KH, KW <= 3, width stride S (1 or 2), width dilation 1, sizes below 2^31:
+// as depthwise_nhwc4_reg_kernel, but a thread computes R consecutive output columns of one output
+// row, loading each input row's (R - 1) * S + 3 columns once for all R of them (4.5 loads per
+// output at stride 1 instead of 9). Taps outside the image contribute a zero product.
+template <int R, int S>
+__global__ void __launch_bounds__(256) depthwise_nhwc4_rows_kernel(const __grid_constant__ DepthwiseParams p) {
+    constexpr int SPAN = (R - 1) * S + 3;
+    const int C4 = p.C >> 2;
+    const int c4 = (int)(threadIdx.x % (unsigned)C4);
+    const unsigned per_block = blockDim.x / C4;
+    const unsigned groups = (unsigned)(p.OW + R - 1) / R;
+    const unsigned items = (unsigned)p.N * p.OH * groups;
+    const float4 *x4 = reinterpret_cast<const float4 *>(p.x);
+    const float4 *w4 = reinterpret_cast<const float4 *>(p.w);
+    const float4 zero = make_float4(0.f, 0.f, 0.f, 0.f);
+    float4 wk[9];  // [kh][kw] of a 3x3 frame, zero outside KH x KW
+#pragma unroll
+    for (int t = 0; t < 9; ++t) {
+        const int kh = t / 3, kw = t % 3;
+        wk[t] = (kh < p.KH && kw < p.KW) ? __ldg(w4 + (kh * p.KW + kw) * C4 + c4) : zero;
+    }
+    const float4 b = p.bias ? __ldg(reinterpret_cast<const float4 *>(p.bias) + c4) : zero;
+    for (unsigned it = blockIdx.x * per_block + threadIdx.x / C4; it < items; it += gridDim.x * per_block) {
+        const unsigned g = it % groups, r = it / groups;
+        const unsigned oh = r % p.OH, n = r / p.OH;
+        const int ow0 = (int)g * R;
+        const int iw0 = ow0 * S - p.PL;
+        float4 acc[R];
+#pragma unroll
+        for (int j = 0; j < R; ++j) acc[j] = b;
+#pragma unroll
+        for (int kh = 0; kh < 3; ++kh) {
+            if (kh >= p.KH) break;
+            const int ih = (int)oh * p.SH - p.PT + kh * p.DH;
+            if (ih < 0 || ih >= p.H) continue;
+            const unsigned rowbase = (n * p.H + ih) * p.W;
+            float4 in[SPAN];
+#pragma unroll
+            for (int t = 0; t < SPAN; ++t) {
+                const int iw = iw0 + t;
+                in[t] = (iw >= 0 && iw < p.W) ? __ldg(x4 + (size_t)(rowbase + iw) * C4 + c4) : zero;
+            }
+#pragma unroll
+            for (int j = 0; j < R; ++j)
+#pragma unroll
+                for (int kw = 0; kw < 3; ++kw) {
+                    if (kw >= p.KW) break;
+                    const float4 v = in[j * S + kw], k = wk[kh * 3 + kw];
+                    acc[j].x = fmaf(v.x, k.x, acc[j].x); acc[j].y = fmaf(v.y, k.y, acc[j].y);
+                    acc[j].z = fmaf(v.z, k.z, acc[j].z); acc[j].w = fmaf(v.w, k.w, acc[j].w);
+                }
+        }
+#pragma unroll
+        for (int j = 0; j < R; ++j) {
+            if (ow0 + j >= p.OW) break;
+            const size_t o = ((size_t)r * p.OW + ow0 + j) * C4 + c4;
+            float4 a = acc[j];
+            if (p.res) {
+                const float4 rr = reinterpret_cast<const float4 *>(p.res)[o];
+                a.x += rr.x; a.y += rr.y; a.z += rr.z; a.w += rr.w;
+            }
+            if (p.act == MGC_ACT_RELU) {
+                a.x = fmaxf(a.x, 0.0f); a.y = fmaxf(a.y, 0.0f); a.z = fmaxf(a.z, 0.0f); a.w = fmaxf(a.w, 0.0f);
+            } else if (p.act == MGC_ACT_CLIP) {
+                a.x = fminf(fmaxf(a.x, p.lo), p.hi); a.y = fminf(fmaxf(a.y, p.lo), p.hi);
+                a.z = fminf(fmaxf(a.z, p.lo), p.hi); a.w = fminf(fmaxf(a.w, p.lo), p.hi);
+            } else if (p.act != MGC_ACT_NONE) {
+                a.x = apply_act(a.x, p.act, p.lo, p.hi); a.y = apply_act(a.y, p.act, p.lo, p.hi);
+                a.z = apply_act(a.z, p.act, p.lo, p.hi); a.w = apply_act(a.w, p.act, p.lo, p.hi);
+            }
+            reinterpret_cast<float4 *>(p.y)[o] = a;
+        }
+    }
+}
+
 // NHWC, C % 4 == 0, KH, KW <= 3, sizes below 2^31: each thread keeps one 4-channel group (the
 // block size is a multiple of C / 4, so the group never changes along the grid-stride loop) with
 // its bias and up to 3x3 weights in registers, and walks output pixels with 32-bit index

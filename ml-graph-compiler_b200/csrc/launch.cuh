@@ -268,7 +268,13 @@ inline int launch_record(const mgc_cuda_launch &L, const int64_t *aux, int64_t a
         const int c4 = p.C / 4;
         const bool reg = vec4 && p.KH <= 3 && p.KW <= 3 && c4 <= 256 &&
                          (long long)p.N * p.H * p.W * c4 < (1ll << 31) && total / 4 < (1ll << 31);
-        if (reg) {
+        if (reg && p.DW == 1 && (p.SW == 1 || p.SW == 2)) {
+            // four output columns per thread
+            const int block = (256 / c4) * c4;
+            const long long items = (long long)p.N * p.OH * ((p.OW + 3) / 4);
+            if (p.SW == 1) depthwise_nhwc4_rows_kernel<4, 1><<<grid_for(items, block / c4), block, 0, stream>>>(p);
+            else depthwise_nhwc4_rows_kernel<4, 2><<<grid_for(items, block / c4), block, 0, stream>>>(p);
+        } else if (reg) {
             const int block = (256 / c4) * c4;  // a multiple of C / 4: each thread keeps its channels
             const long long npix = (long long)p.N * p.OH * p.OW;
             depthwise_nhwc4_reg_kernel<<<grid_for(npix, block / c4), block, 0, stream>>>(p);

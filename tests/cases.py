@@ -190,6 +190,8 @@ def op_cases() -> list[Case]:
     C(_simple("conv_dilated", lambda r: conv(r, (1, 3, 13, 13), (4, 3, 3, 3), kernel_shape=[3, 3], dilations=[2, 2], pads=[2, 2, 2, 2])))
     C(_simple("conv_groups", lambda r: conv(r, (2, 6, 8, 8), (4, 3, 3, 3), kernel_shape=[3, 3], group=2, pads=[1, 1, 1, 1])))
     C(_simple("conv_depthwise", lambda r: conv(r, (2, 8, 9, 9), (8, 1, 3, 3), kernel_shape=[3, 3], group=8, strides=[2, 2], pads=[1, 1, 1, 1])))
+    # stride-1 depthwise with a ragged last group of four output columns (the four-column form)
+    C(_simple("conv_depthwise_s1", lambda r: conv(r, (2, 12, 7, 10), (12, 1, 3, 3), kernel_shape=[3, 3], group=12, pads=[1, 1, 1, 1])))
     C(_simple("conv_same_upper", lambda r: conv(r, (1, 3, 10, 7), (5, 3, 4, 4), kernel_shape=[4, 4], strides=[2, 2], auto_pad="SAME_UPPER")))
     C(_simple("conv_1x1", lambda r: conv(r, (2, 16, 6, 6), (24, 16, 1, 1), bias=False, kernel_shape=[1, 1])))
     C(_simple("conv_stem7x7", lambda r: conv(r, (1, 3, 32, 32), (16, 3, 7, 7), kernel_shape=[7, 7], strides=[2, 2], pads=[3, 3, 3, 3])))
