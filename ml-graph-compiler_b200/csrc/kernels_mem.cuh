@@ -820,6 +820,30 @@ struct PackParams {
     float *out;
 };
 
+// The same packing with 32-bit index arithmetic (pixel counts and source offsets below 2^31).
+__global__ void __launch_bounds__(256) pack_nhwc32_kernel(const __grid_constant__ PackParams p) {
+    const unsigned hw = (unsigned)p.Hp * (unsigned)p.Wp;
+    const unsigned total = (unsigned)p.N * hw;
+    const unsigned stride = gridDim.x * blockDim.x;
+    for (unsigned e = blockIdx.x * blockDim.x + threadIdx.x; e < total; e += stride) {
+        const unsigned n = e / hw;
+        const unsigned r = e - n * hw;
+        const unsigned hq = r / (unsigned)p.Wp;
+        const int h = (int)hq - p.PT, w = (int)(r - hq * (unsigned)p.Wp) - p.PL;
+        const bool inside = h >= 0 && h < p.H && w >= 0 && w < p.W;
+        const float *src =
+            p.x + (inside ? n * (unsigned)p.sn + (unsigned)h * (unsigned)p.sh + (unsigned)w * (unsigned)p.sw : 0u);
+        float4 *dst = reinterpret_cast<float4 *>(p.out) + (size_t)e * (p.cp >> 2);
+        for (int c0 = 0; c0 < p.cp; c0 += 4) {
+            float v[4];
+#pragma unroll
+            for (int t = 0; t < 4; ++t)
+                v[t] = inside && c0 + t < p.C ? __ldg(src + (unsigned)(c0 + t) * (unsigned)p.sc) : 0.0f;
+            dst[c0 >> 2] = make_float4(v[0], v[1], v[2], v[3]);
+        }
+    }
+}
+
 __global__ void __launch_bounds__(256) pack_nhwc_kernel(const __grid_constant__ PackParams p) {
     const long long hw = (long long)p.Hp * p.Wp;
     const long long total = (long long)p.N * hw;

@@ -489,6 +489,63 @@ __global__ void __launch_bounds__(256) pool_kernel(const __grid_constant__ PoolP
 // NHWC pooling, four channels per thread (C % 4 == 0, 16-byte aligned x and y): the same window
 // walk and the same comparisons as pool_kernel (a NaN never replaces the running maximum), with
 // 16-byte loads and stores and 32-bit index arithmetic (the caller checks the sizes fit).
+// Max pooling, NHWC, C % 4 == 0, KH, KW <= 3, width stride S (1 or 2), width dilation 1, sizes
+// below 2^31: a thread takes four consecutive output columns of one output row and one 4-channel
+// group, loading each input row's (3 * S + 3) columns once for all four (6.75 loads per output
+// at stride 2 instead of 9). Columns outside the image read as -inf, which the comparison
+// never takes, the same as skipping them.
+template <int S>
+__global__ void __launch_bounds__(256) maxpool4_nhwc_rows_kernel(const __grid_constant__ PoolParams p) {
+    constexpr int R = 4, SPAN = (R - 1) * S + 3;
+    const int c4n = p.C >> 2;
+    const unsigned groups = (unsigned)(p.OW + R - 1) / R;
+    const unsigned total = (unsigned)p.N * p.OH * groups * c4n;
+    const unsigned stride = gridDim.x * blockDim.x;
+    const float4 *x4 = reinterpret_cast<const float4 *>(p.x);
+    float4 *y4 = reinterpret_cast<float4 *>(p.y);
+    const float4 ninf = make_float4(-INFINITY, -INFINITY, -INFINITY, -INFINITY);
+    for (unsigned e = blockIdx.x * blockDim.x + threadIdx.x; e < total; e += stride) {
+        const int c4 = (int)(e % c4n);
+        unsigned r = e / c4n;
+        const unsigned g = r % groups;
+        r /= groups;
+        const int oh = (int)(r % p.OH);
+        const unsigned n = r / p.OH;
+        const int ow0 = (int)g * R, iw0 = ow0 * S - p.PL;
+        float4 acc[R];
+#pragma unroll
+        for (int j = 0; j < R; ++j) acc[j] = ninf;
+#pragma unroll
+        for (int kh = 0; kh < 3; ++kh) {
+            if (kh >= p.KH) break;
+            const int ih = oh * p.SH - p.PT + kh * p.DH;
+            if (ih < 0 || ih >= p.H) continue;
+            const unsigned rowbase = (n * p.H + ih) * p.W;
+            float4 in[SPAN];
+#pragma unroll
+            for (int t = 0; t < SPAN; ++t) {
+                const int iw = iw0 + t;
+                in[t] = iw >= 0 && iw < p.W ? __ldg(x4 + (size_t)(rowbase + iw) * c4n + c4) : ninf;
+            }
+#pragma unroll
+            for (int j = 0; j < R; ++j)
+#pragma unroll
+                for (int kw = 0; kw < 3; ++kw) {
+                    if (kw >= p.KW) break;
+                    const float4 v = in[j * S + kw];
+                    acc[j].x = v.x > acc[j].x ? v.x : acc[j].x;
+                    acc[j].y = v.y > acc[j].y ? v.y : acc[j].y;
+                    acc[j].z = v.z > acc[j].z ? v.z : acc[j].z;
+                    acc[j].w = v.w > acc[j].w ? v.w : acc[j].w;
+                }
+        }
+        const size_t o = ((size_t)r * p.OW + ow0) * c4n + c4;
+#pragma unroll
+        for (int j = 0; j < R; ++j)
+            if (ow0 + j < p.OW) y4[o + (size_t)j * c4n] = acc[j];
+    }
+}
+
 __global__ void __launch_bounds__(256) pool4_nhwc_kernel(const __grid_constant__ PoolParams p) {
     const int c4n = p.C >> 2;
     const unsigned total = (unsigned)p.N * p.OH * p.OW * c4n;

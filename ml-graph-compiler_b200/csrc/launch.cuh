@@ -298,6 +298,14 @@ inline int launch_record(const mgc_cuda_launch &L, const int64_t *aux, int64_t a
         const bool vec = p.nhwc && (p.C & 3) == 0 && (reinterpret_cast<uintptr_t>(p.x) & 15) == 0 &&
                          (reinterpret_cast<uintptr_t>(p.y) & 15) == 0 &&
                          (long long)p.N * p.H * p.W < (1ll << 31) && total / 4 < (1ll << 31);
+        if (vec && p.is_max && p.KH <= 3 && p.KW <= 3 && p.DW == 1 && (p.SW == 1 || p.SW == 2)) {
+            // four output columns per thread
+            const long long items = (long long)p.N * p.OH * ((p.OW + 3) / 4) * (p.C / 4);
+            if (p.SW == 1) maxpool4_nhwc_rows_kernel<1><<<grid_for(items, 256), 256, 0, stream>>>(p);
+            else maxpool4_nhwc_rows_kernel<2><<<grid_for(items, 256), 256, 0, stream>>>(p);
+            st = check_launch("maxpool4_nhwc_rows_kernel");
+            break;
+        }
         if (vec) {
             pool4_nhwc_kernel<<<grid_for(total / 4, 256), 256, 0, stream>>>(p);
             st = check_launch("pool4_nhwc_kernel");
@@ -497,7 +505,14 @@ inline int launch_record(const mgc_cuda_launch &L, const int64_t *aux, int64_t a
                         p.H, p.W, p.PT, p.PL);
         const long long total = (long long)p.N * p.Hp * p.Wp;
         if (total == 0) { launched = 0; break; }
-        pack_nhwc_kernel<<<grid_for(total, 256), 256, 0, stream>>>(p);
+        // 32-bit indices when every pixel index and source offset fits
+        const long long src_last = (long long)(p.N - 1) * p.sn + (long long)(p.H - 1) * p.sh +
+                                   (long long)(p.W - 1) * p.sw + (long long)(p.C - 1) * p.sc;
+        const bool small = total < (1ll << 31) && src_last < (1ll << 31) && p.sn >= 0 && p.sh >= 0 && p.sw >= 0 &&
+                           p.sc >= 0 && p.sn < (1ll << 31) && p.sh < (1ll << 31) && p.sw < (1ll << 31) &&
+                           p.sc < (1ll << 31);
+        if (small) pack_nhwc32_kernel<<<grid_for(total, 256), 256, 0, stream>>>(p);
+        else pack_nhwc_kernel<<<grid_for(total, 256), 256, 0, stream>>>(p);
         st = check_launch("pack_nhwc_kernel");
         break;
     }

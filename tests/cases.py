@@ -425,6 +425,24 @@ def _p_attention(r: np.random.Generator) -> tuple[Graph, dict[str, np.ndarray]]:
     return g, {"q": f32(r, 2, 3, 16, 8), "k": f32(r, 2, 3, 16, 8), "v": f32(r, 2, 3, 16, 8), "m": mask}
 
 
+def _p_conv_maxpool(r: np.random.Generator) -> tuple[Graph, dict[str, np.ndarray]]:
+    """Conv + ReLU then max pooling in NHWC (the O3 layout): 3x3 stride 2 pad 1 (the ResNet stem
+    pool) and 3x3 stride 1 pad 1, output widths 7 and 13 (ragged groups of four columns), eight
+    channels (two groups of four), negative values kept by a second, unrectified branch."""
+    g = Graph("conv_maxpool")
+    x = g.add_input("x", TensorType("float32", (2, 8, 13, 13)))
+    w = g.constant(f32(r, 8, 8, 3, 3, scale=0.3))
+    h = g.add_node("Conv", [x, w], attrs={"kernel_shape": [3, 3], "pads": [1, 1, 1, 1]}).output
+    a = g.add_node("Relu", [h]).output
+    p1 = g.add_node("MaxPool", [a], attrs={"kernel_shape": [3, 3], "strides": [2, 2], "pads": [1, 1, 1, 1]}).output
+    p2 = g.add_node("MaxPool", [h], attrs={"kernel_shape": [3, 3], "strides": [1, 1], "pads": [1, 1, 1, 1]}).output
+    w2 = g.constant(f32(r, 4, 8, 1, 1, scale=0.3))
+    g.add_output(g.add_node("Conv", [p1, w2], attrs={"kernel_shape": [1, 1]}).output, "a")
+    g.add_output(g.add_node("Conv", [p2, w2], attrs={"kernel_shape": [1, 1]}).output, "b")
+    infer_shapes(g)
+    return g, {"x": f32(r, 2, 8, 13, 13)}
+
+
 def pattern_cases() -> list[Case]:
     return [
         _pattern("conv_block", _p_conv_block),
@@ -436,6 +454,7 @@ def pattern_cases() -> list[Case]:
         _pattern("masked_softmax", _p_masked_softmax),
         _pattern("softmax_programs", _p_softmax_programs),
         _pattern("attention", _p_attention),
+        _pattern("conv_maxpool", _p_conv_maxpool),
     ]
 
 
