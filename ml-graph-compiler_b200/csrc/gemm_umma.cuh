@@ -12,7 +12,7 @@
 //   TF32-exact high part and the fp32 residual (hi + lo == B exactly); for im2col the K axis is
 //   (kh, kw, channel padded to 32).
 //
-// Arithmetic (measured on B200): the tensor core reads fp32 operands by
+// Arithmetic (measured on B200 with TF32-exact operands and TMA round trips): the tensor core reads fp32 operands by
 // truncating them to TF32, and its accumulator rounds toward zero, a bias that compounds through
 // deep networks. Both are handled explicitly:
 // * MGC_PREC_TF32: A is loaded through a TFLOAT32 tensor map, which rounds it to the nearest
