@@ -250,8 +250,12 @@ class CudaEmitter:
         self.workspace_bytes = 0  # scratch regions (im2col patch matrices, channel-packed images)
         self._im2col_bytes = 0    # the im2col region at offset 0, shared by every im2col launch
         self._packed: dict[int, RefT] = {}  # id(value) -> its channel-packed copy in the workspace
-        # id(value) -> (source, element strides) of a Transpose that MatMul reads through (not copied)
-        self._through: dict[int, tuple[Value, list[int]]] = {}
+        # id(value) -> (source, element strides, first element) of a Transpose that MatMul reads
+        # through (not copied)
+        self._through: dict[int, tuple[Value, list[int], int]] = {}
+        # id(Split output) -> (the Split's input, element strides, first element): an output that
+        # only Transposes read, through strides, is never copied (see _split_view)
+        self._split_src: dict[int, tuple[Value, list[int], int]] = {}
         self._pack_regions: list[tuple[int, int]] = []  # (offset, bytes) of each packed image
         # id(value) -> element strides of a Transpose output stored K-major for MatMul (see
         # _kmajor_b_only); every reader goes through _view
@@ -583,8 +587,26 @@ class CudaEmitter:
         ss = _strides(x.tensor_type.shape)
         shape = node.output.tensor_type.shape
         out = node.output
+        view = self._split_view_of(x)
+        if view is not None:
+            # x is a view of a Split's input that was never copied: read it there
+            src, ss, base = view
+            vs = [ss[p] for p in perm]
+            if self._read_through(node, src, vs):
+                self._through[id(out)] = (src, vs, base)
+                return
+            if self._kmajor_b_only(out, vs):
+                kshape = [*shape[:-2], shape[-1], shape[-2]]
+                kst = _strides(kshape)
+                self._stored[id(out)] = [*kst[:-2], kst[-1], kst[-2]]
+                self._copy(kshape, self.ref(src), [*vs[:-2], vs[-1], vs[-2]], base, self.ref(out), kst, 0,
+                           src.tensor_type.itemsize, count="transpose")
+                return
+            self._copy(shape, self.ref(src), vs, base, self.ref(out), _strides(shape), 0, src.tensor_type.itemsize,
+                       count="transpose")
+            return
         if self._read_through(node, x, [ss[p] for p in perm]):
-            self._through[id(out)] = (x, [ss[p] for p in perm])
+            self._through[id(out)] = (x, [ss[p] for p in perm], 0)
             return
         if self._kmajor_b_only(out, [ss[p] for p in perm]):
             # every reader is a batched MatMul taking it as an N-major B: store it K-major
@@ -668,10 +690,78 @@ class CudaEmitter:
         offset = 0
         for out_v in node.outputs:
             t = out_v.tensor_type
-            if out_v.users or out_v in self.graph.outputs:
+            if self._split_view(node, out_v):
+                self._split_src[id(out_v)] = (x, list(ss), offset * ss[axis])
+                self.kernels["view"] = self.kernels.get("view", 0) + 1
+            elif out_v.users or out_v in self.graph.outputs:
                 self._copy(t.shape, self.ref(x), ss, offset * ss[axis], self.ref(out_v), _strides(t.shape), 0,
                            xt.itemsize)
             offset += t.shape[axis]
+
+    @staticmethod
+    def _split_strides(vshape: Sequence[int], strides: list[int], shape: Sequence[int]) -> list[int] | None:
+        """Element strides of a Reshape of a strided view of shape vshape, when the Reshape keeps
+        every leading axis and splits only the last, contiguous one (heads out of the hidden
+        axis); None otherwise."""
+        vshape, shape = list(vshape), list(shape)
+        if vshape == shape:
+            return list(strides)
+        r = len(vshape)
+        if len(shape) < r or shape[: r - 1] != vshape[: r - 1] or strides[-1] != 1:
+            return None
+        if int(np.prod(shape[r - 1 :])) != vshape[-1]:
+            return None
+        return list(strides[:-1]) + _strides(shape[r - 1 :])
+
+    def _split_view(self, node: Node, out_v: Value) -> bool:
+        """Whether a Split output is read only by Transposes (directly or through one Reshape that
+        splits its last axis), which then read the Split's input through strides: no copy. The
+        Split's input must stay untouched until the last of those Transposes (and, when they are
+        read through, until their MatMuls: _read_through checks that against the same source)."""
+        if any(v is out_v for _, v in self.graph.named_outputs()) or not out_v.users:
+            return False
+        x = node.input(0)
+        if self.plan.location(x).kind not in ("arena", "input") or x.tensor_type.dtype != "float32":
+            return False
+        readers: list[Node] = []
+        for u in out_v.users:
+            if u.op == "Transpose" and u.input(0) is out_v:
+                readers.append(u)
+            elif u.op == "Reshape" and u.input(0) is out_v and len(u.outputs) == 1:
+                rv = u.output
+                if any(v is rv for _, v in self.graph.named_outputs()) or not rv.users:
+                    return False
+                if self._split_strides(out_v.tensor_type.shape, [1] * (out_v.tensor_type.rank - 1) + [1],
+                                       rv.tensor_type.shape) is None:
+                    return False
+                for w in rv.users:
+                    if w.op != "Transpose" or w.input(0) is not rv:
+                        return False
+                    readers.append(w)
+            else:
+                return False
+        order = {id(n): k for k, n in enumerate(self.graph.nodes)}
+        last = max(readers, key=lambda n: order[id(n)])
+        return not self._clobbered(node, last, [x]) and not any(
+            self._overlaps(r.output, x) for r in readers)
+
+    def _overlaps(self, a: Value, b: Value) -> bool:
+        ra, rb = self._arena_range(a), self._arena_range(b)
+        return ra is not None and rb is not None and ra[0] < rb[1] and rb[0] < ra[1]
+
+    def _split_view_of(self, v: Value) -> tuple[Value, list[int], int] | None:
+        """(source, element strides, first element) of a value that is a Split view or one
+        Reshape of it (see _split_view), else None."""
+        if id(v) in self._split_src:
+            return self._split_src[id(v)]
+        prod = v.producer
+        if prod is not None and prod.op == "Reshape" and id(prod.input(0)) in self._split_src:
+            src, strides, base = self._split_src[id(prod.input(0))]
+            inner = prod.input(0).tensor_type.shape
+            st = self._split_strides(inner, strides, v.tensor_type.shape)
+            if st is not None:
+                return src, st, base
+        return None
 
     def op_Pad(self, node: Node) -> None:
         if node.attrs.get("mode", "constant") != "constant":
@@ -1055,8 +1145,8 @@ class CudaEmitter:
         """Reference and per-dimension element strides of a MatMul operand: its own contiguous
         buffer, or the source of a Transpose read through."""
         if id(value) in self._through:
-            src, strides = self._through[id(value)]
-            return self.ref(src), list(strides)
+            src, strides, base = self._through[id(value)]
+            return self.ref(src, base * src.tensor_type.itemsize), list(strides)
         if id(value) in self._stored:
             return self.ref(value), list(self._stored[id(value)])
         return self.ref(value), _strides(value.tensor_type.shape)

@@ -84,8 +84,8 @@ def test_resnet50_batch_is_independent_per_image() -> None:
     m1.close()
 
 
-@pytest.mark.parametrize("name", ["bert", "gpt2"])
-def test_transformer_batch_is_independent_per_sequence(name: str) -> None:
+@pytest.mark.parametrize("name,strategy", [("bert", "greedy_by_size"), ("gpt2", "greedy_by_size"), ("gpt2", "naive")])
+def test_transformer_batch_is_independent_per_sequence(name: str, strategy: str) -> None:
     """Size-independent property at the benchmark batch: every sequence of a batch-32 TF32 run
     (attention read through strides, the softmax over the mask program, 192-wide pair tiles,
     several waves of tiles) equals the strict batch-1 model's output for that
@@ -101,7 +101,7 @@ def test_transformer_batch_is_independent_per_sequence(name: str) -> None:
     optimize(g1, "O3")
     schedule(g1)
     feeds = zoo.feeds(g32, 7)
-    m32 = compile_graph(g32, precision="tf32")
+    m32 = compile_graph(g32, precision="tf32", strategy=strategy)
     y32 = m32.run(feeds)
     m32.close()
     m1 = compile_graph(g1, precision="strict")

@@ -217,14 +217,15 @@ def _gemm_span(rec, which: str) -> tuple[int, int] | None:
 
 @pytest.mark.parametrize("name", ["bert", "gpt2"])
 @pytest.mark.parametrize("precision", ["tf32", "strict"])
-def test_no_gemm_writes_over_an_operand_it_reads(name: str, precision: str) -> None:
+@pytest.mark.parametrize("strategy", ["greedy_by_size", "naive"])
+def test_no_gemm_writes_over_an_operand_it_reads(name: str, precision: str, strategy: str) -> None:
     """A GEMM that reads an operand through strides (a Transpose read through) must not write
     over that operand's memory: the planner may reuse a Transpose's source once the Transpose
     has run, so the lowering copies such an operand into the workspace first."""
     g = getattr(zoo, name)(batch=2, seq=128)
     optimize(g, "O3")
     schedule(g)
-    low = lower_graph(g, precision=precision)
+    low = lower_graph(g, precision=precision, strategy=strategy)
     checked = 0
     for rec in low.launches:
         if rec.kind != K_GEMM:
@@ -237,3 +238,15 @@ def test_no_gemm_writes_over_an_operand_it_reads(name: str, precision: str) -> N
             checked += 1
             assert not (r[0] < c[1] and c[0] < r[1]), f"GEMM of node {rec.node} writes over its {which} operand"
     assert checked > 0
+
+
+def test_gpt2_split_outputs_are_views_on_the_naive_plan() -> None:
+    """GPT-2's fused QKV output is split into Q, K and V, each read only by head Transposes: with
+    every buffer in its own memory the Split copies nothing (the Transposes read the QKV buffer
+    through strides); with the greedy plan, whose later buffers reuse that memory, it copies."""
+    g = zoo.gpt2(batch=2, seq=128)
+    optimize(g, "O3")
+    schedule(g)
+    naive = lower_graph(g, strategy="naive")
+    assert "copy" not in naive.kernels
+    assert lower_graph(g).kernels.get("copy") == 36
