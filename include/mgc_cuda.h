@@ -28,7 +28,7 @@
 extern "C" {
 #endif
 
-#define MGC_CUDA_ABI_VERSION 2
+#define MGC_CUDA_ABI_VERSION 3
 
 /* ---- status codes (runtime_lib.py:142-143 maps mgc_run's 1 to GraphError) ---------------- */
 enum {
@@ -203,6 +203,17 @@ int mgc_cuda_profile(void *handle, double *per_node_ms, int n);
 /* Number of kernel launches in one replay of the handle's graph. */
 int mgc_cuda_launch_count(void *handle);
 
+/* Which kernel computes each GEMM-family launch record (FusedConv, FusedGemm, Gemm, MatMul) of
+ * the handle's graphs: per_record[k] for record k < n is MGC_CUDA_PATH_NONE for a record of
+ * another kind, MGC_CUDA_PATH_TCGEN05 when the tcgen05 tensor-core kernel runs it, and
+ * MGC_CUDA_PATH_SIMT when the exact-fp32 CUDA-core kernel does (fp32 precision, or a problem
+ * the tensor-core forms cannot describe). No counterpart in the reference, whose C backend has
+ * one GEMM kernel; the reference's CompileReport.kernels (runtime_lib.py:31-41) counts kernels
+ * by kind only. A record that runs slice by slice (mgc_cuda_set_input_chunks) reports SIMT if
+ * any of its slices does. */
+enum { MGC_CUDA_PATH_NONE = 0, MGC_CUDA_PATH_TCGEN05 = 1, MGC_CUDA_PATH_SIMT = 2 };
+int mgc_cuda_gemm_paths(void *handle, int32_t *per_record, int n);
+
 int64_t mgc_cuda_arena_bytes(void *handle);
 int64_t mgc_cuda_weights_bytes(void *handle);
 void mgc_cuda_destroy(void *handle);
@@ -227,7 +238,15 @@ int mgc_cuda_execute(const mgc_cuda_launch *launches, int n, const int64_t *aux,
  * A is M x K with element (m, k) at a[m*a_rs + k*a_cs], B is K x N at b[k*b_rs + n*b_cs], C and
  * R are M x N with leading dimensions ldc / ldr. Batch item b is offset by b*stride elements
  * (mgc_gemm takes per-item offset arrays; a constant stride covers conv batches and MatMul).
- * bias_mode 1 adds bias[n], 2 adds bias[m]. precision is MGC_PREC_*. */
+ * bias_mode 1 adds bias[n], 2 adds bias[m]. precision:
+ *   MGC_PREC_FP32  exact fp32 FMA on the CUDA cores (the reference's arithmetic), any strides;
+ *   MGC_PREC_TF32  the tcgen05 tensor cores, A and B rounded to TF32 on load, fp32 accumulate;
+ *                  needs A and B K-major (a_cs == 1, b_rs == 1) with 16-byte aligned bases and
+ *                  row strides, K and N multiples of 4, no per-row bias, and for batch > 1 no
+ *                  bias, residual, activation or alpha; anything else returns
+ *                  MGC_CUDA_UNSUPPORTED (nothing runs);
+ *   MGC_PREC_3XTF32 returns MGC_CUDA_UNSUPPORTED: the strict split needs constant weights laid
+ *                  out at load time, which the model ABI (mgc_cuda_create) does. */
 int mgc_cuda_gemm(int M, int N, int K, int batch, const float *a, int64_t a_rs, int64_t a_cs,
                   int64_t a_bstride, const float *b, int64_t b_rs, int64_t b_cs, int64_t b_bstride,
                   float *c, int64_t ldc, int64_t c_bstride, float alpha, const float *bias,
@@ -236,7 +255,10 @@ int mgc_cuda_gemm(int M, int N, int K, int batch, const float *a, int64_t a_rs, 
 
 /* Implicit-GEMM NHWC convolution with the FusedConv epilogue (c.py:1146-1185 lowering onto
  * mgc_gemm with MGC_CONV_NHWC, mgc_kernels.c:103-126): x [N,H,W,C], w HWIO [KH,KW,C,CO],
- * y = act(conv + bias[co] + res), y and res [N,OH,OW,CO]. group must be 1. */
+ * y = act(conv + bias[co] + res), y and res [N,OH,OW,CO]. group must be 1. precision must be
+ * MGC_PREC_FP32 (exact fp32 on the CUDA cores, the reference's arithmetic); TF32 and 3xTF32
+ * return MGC_CUDA_UNSUPPORTED, because their tensor-core forms read the weights in a K-major
+ * layout that the model ABI prepares at load time, not HWIO. */
 int mgc_cuda_conv_nhwc(int N, int H, int W, int C, int KH, int KW, int SH, int SW, int DH, int DW,
                        int PT, int PL, int OH, int OW, int CO, const float *x, const float *w,
                        const float *bias, const float *res, int act, float lo, float hi,

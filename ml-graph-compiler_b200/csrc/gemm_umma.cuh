@@ -1613,34 +1613,47 @@ inline int launch_pair(Params &p, int clusters, cudaStream_t stream) {
 
 }  // namespace umma
 
-// Batched GEMM with a dynamic B (attention's Q K^T and P V; any batched MatMul of activations):
-// TF32 mode, both operands K-major (k contiguous) and rounded to TF32 by their tensor maps, one or
-// two batch dimensions with strides TMA can address (no broadcast), no bias / residual /
-// activation. Each tile lies inside one batch, so rows past M are clipped per batch.
+// GEMM with a dynamic B (an activation, rounded to TF32 by its tensor map like A) on the tensor
+// cores: attention's Q K^T and P V, any MatMul of two activations, and the kernel ABI's TF32
+// GEMM. TF32 mode, both operands K-major (k contiguous), no, one or two batch dimensions with
+// strides TMA can address (no broadcast). Without batch dimensions the FusedGemm epilogue applies
+// (alpha, bias per column, residual, activation); batched products take none. Each tile lies
+// inside one batch, so rows past M are clipped per batch. *taken: kernels launched (0 or 1).
 inline int try_gemm_umma_dyn(const GemmParams &p, cudaStream_t stream, int *taken) {
     *taken = 0;
-    if (p.precision != MGC_PREC_TF32 || p.nb < 1 || p.nb > 2 || p.b_umma || p.b_lo) return MGC_CUDA_OK;
+    if (p.precision != MGC_PREC_TF32 || p.nb < 0 || p.nb > 2 || p.b_umma || p.b_lo) return MGC_CUDA_OK;
     if (p.a_kind != MGC_STRIDED || p.b_kind != MGC_STRIDED || p.a_cs != 1 || p.b_rs != 1) return MGC_CUDA_OK;
-    if (p.bias || p.res || p.act != MGC_ACT_NONE || p.alpha != 1.0f || p.M <= 0 || p.N <= 0 || p.K <= 0)
-        return MGC_CUDA_OK;
+    if (p.M <= 0 || p.N <= 0 || p.K <= 0) return MGC_CUDA_OK;
+    const bool epilogue = p.bias || p.res || p.act != MGC_ACT_NONE || p.alpha != 1.0f;
+    if ((epilogue && p.nb != 0) || (p.bias && p.bias_mode != 1)) return MGC_CUDA_OK;
     auto al = [](const void *q) { return (reinterpret_cast<uintptr_t>(q) & 15) == 0; };
     auto st = [](long long v) { return v > 0 && (v & 3) == 0; };  // a 16-byte multiple, not a broadcast
     if (!al(p.a) || !al(p.b) || !al(p.c) || !st(p.a_rs) || !st(p.b_cs) || !st(p.ldc) || (p.K & 3) || (p.N & 3))
         return MGC_CUDA_OK;
-    const long long b1 = p.bdims[0], b2 = p.nb == 2 ? p.bdims[1] : 1;
+    if (p.res && (!al(p.res) || !st(p.ldr))) return MGC_CUDA_OK;
+    const long long b1 = p.nb >= 1 ? p.bdims[0] : 1, b2 = p.nb == 2 ? p.bdims[1] : 1;
     if (b1 <= 0 || b2 <= 0) return MGC_CUDA_OK;
     for (int d = 0; d < p.nb; ++d)
         if (!st(p.a_bs[d]) || !st(p.b_bs[d]) || !st(p.c_bs[d])) return MGC_CUDA_OK;
-    // strides of a second batch dimension of extent 1 (unused): any valid value
-    const long long a2 = p.nb == 2 ? p.a_bs[1] : p.a_bs[0] * b1, bb2 = p.nb == 2 ? p.b_bs[1] : p.b_bs[0] * b1;
-    const long long c2 = p.nb == 2 ? p.c_bs[1] : p.c_bs[0] * b1;
+    // strides of batch dimensions of extent 1 (unused): any valid value
+    const long long a1 = p.nb >= 1 ? p.a_bs[0] : p.a_rs * p.M, bb1 = p.nb >= 1 ? p.b_bs[0] : p.b_cs * p.N;
+    const long long c1 = p.nb >= 1 ? p.c_bs[0] : p.ldc * p.M;
+    const long long a2 = p.nb == 2 ? p.a_bs[1] : a1 * b1, bb2 = p.nb == 2 ? p.b_bs[1] : bb1 * b1;
+    const long long c2 = p.nb == 2 ? p.c_bs[1] : c1 * b1;
     const int bn = p.N <= 64 ? 64 : 128;
     umma::Params u;
     memset(&u, 0, sizeof u);
-    if (!umma::make_map_4d(&u.tmA, p.a, p.K, p.M, b1, b2, p.a_rs, p.a_bs[0], a2, umma::BM, true) ||
-        !umma::make_map_4d(&u.tmB, p.b, p.K, p.N, b1, b2, p.b_cs, p.b_bs[0], bb2, bn, true) ||
-        !umma::make_map_4d(&u.tmC, p.c, p.N, p.M, b1, b2, p.ldc, p.c_bs[0], c2, umma::BM, false))
+    if (!umma::make_map_4d(&u.tmA, p.a, p.K, p.M, b1, b2, p.a_rs, a1, a2, umma::BM, true) ||
+        !umma::make_map_4d(&u.tmB, p.b, p.K, p.N, b1, b2, p.b_cs, bb1, bb2, bn, true) ||
+        !umma::make_map_4d(&u.tmC, p.c, p.N, p.M, b1, b2, p.ldc, c1, c2, umma::BM, false))
         return MGC_CUDA_OK;
+    if (p.res) {
+        // the residual tile is TMA-loaded into the output staging tile (rows m0.. of the one batch)
+        if (!umma::make_map_2d(&u.tmR, p.res, p.M, p.N, p.ldr, umma::BM)) return MGC_CUDA_OK;
+        u.tma_res = 1;
+        u.res = p.res;
+        u.ldr = p.ldr;
+    }
     const long long m_per = ceil_div(p.M, umma::BM), tiles_m = m_per * b1 * b2;
     const long long n_tiles = ceil_div(p.N, bn);
     if (tiles_m * n_tiles > 0x7FFFFFFF) return MGC_CUDA_OK;
@@ -1654,7 +1667,8 @@ inline int try_gemm_umma_dyn(const GemmParams &p, cudaStream_t stream, int *take
     u.a_bytes = umma::A_TILE_BYTES;
     u.tma_out = 1;
     u.c = p.c; u.ldc = p.ldc;
-    u.alpha = 1.0f; u.lo = p.lo; u.hi = p.hi; u.act = MGC_ACT_NONE;
+    u.bias = p.bias;
+    u.alpha = p.alpha; u.lo = p.lo; u.hi = p.hi; u.act = p.act;
     u.err = p.err;
     const int sms = sm_count();
     const long long tiles = tiles_m * n_tiles;
@@ -1666,13 +1680,14 @@ inline int try_gemm_umma_dyn(const GemmParams &p, cudaStream_t stream, int *take
     return MGC_CUDA_OK;
 }
 
-// Whether the tensor-core kernel takes this GEMM, and its launch. Requirements: tf32 or 3xtf32
+// Whether the tensor-core kernel takes this GEMM, and its launch; *taken is the number of kernels
+// launched (0: not taken, the caller runs the SIMT kernel). Requirements: tf32 or 3xtf32
 // precision, no batch dimensions, a constant K-major B in the layout the lowering provides
 // (b_umma + b_umma_lo), A as a unit-stride row-major matrix or an NHWC im2col operand with
 // 16-byte aligned rows, bias per column (or none), fp32 output.
 inline int try_gemm_umma(const GemmParams &p, cudaStream_t stream, int *taken) {
     *taken = 0;
-    if (p.nb != 0 && !p.b_umma) return try_gemm_umma_dyn(p, stream, taken);
+    if (!p.b_umma) return try_gemm_umma_dyn(p, stream, taken);
     if (p.precision == MGC_PREC_FP32 || p.nb != 0 || !p.b_umma || !p.b_umma_lo || p.M <= 0 || p.N <= 0 || p.K <= 0)
         return MGC_CUDA_OK;
     if (p.bias && p.bias_mode != 1) return MGC_CUDA_OK;
@@ -1886,7 +1901,7 @@ inline int try_gemm_umma(const GemmParams &p, cudaStream_t stream, int *taken) {
                     p.lo, p.hi);
                 st = check_launch("split_reduce_kernel");
                 if (st != MGC_CUDA_OK) return st;
-                *taken = 1;
+                *taken = 2;  // the split GEMM and its reduce
                 return MGC_CUDA_OK;
             }
         }

@@ -62,11 +62,22 @@ inline int resolve(const mgc_cuda_ref &r, const Bases &b, void **out) {
         (ptr) = (decltype(ptr))mgc_p_;                                                       \
     } while (0)
 
-// Run every GEMM-family launch: the tcgen05 kernel when it accepts the problem, else SIMT.
-inline int run_gemm(const GemmParams &p, cudaStream_t stream, int *used_tensor_cores = nullptr) {
+// What one launch record did: how many kernels it launched and, for a GEMM-family record, which
+// kernel computed it (MGC_CUDA_PATH_*, reported per record by mgc_cuda_gemm_paths).
+struct LaunchInfo {
+    int kernels = 0;
+    int gemm_path = MGC_CUDA_PATH_NONE;
+};
+
+// Run every GEMM-family launch of the model ABI: the tcgen05 kernel when it accepts the problem,
+// else the exact-fp32 SIMT kernel; `info` records which (and the split-K reduce's extra launch).
+inline int run_gemm(const GemmParams &p, cudaStream_t stream, LaunchInfo *info = nullptr) {
     int taken = 0;
     MGC_CHECK(try_gemm_umma(p, stream, &taken));
-    if (used_tensor_cores) *used_tensor_cores = taken;
+    if (info) {
+        info->kernels = taken > 0 ? taken : 1;
+        info->gemm_path = taken > 0 ? MGC_CUDA_PATH_TCGEN05 : MGC_CUDA_PATH_SIMT;
+    }
     if (taken) return MGC_CUDA_OK;
     return launch_gemm_simt(p, stream);
 }
@@ -235,12 +246,14 @@ inline int launch_tile_t(const TileParams &P, cudaStream_t s) {
     return check_launch("tile_kernel");
 }
 
-// Launch one record. `kernels`, if not NULL, is incremented by the number of kernel launches.
+// Launch one record. `info`, if not NULL, receives the number of kernel launches and the GEMM
+// path taken.
 inline int launch_record(const mgc_cuda_launch &L, const int64_t *aux, int64_t aux_len,
-                         const Bases &bases, int *status_dev, cudaStream_t stream, int *kernels) {
+                         const Bases &bases, int *status_dev, cudaStream_t stream, LaunchInfo *info) {
     const int64_t *i = L.i;
     int launched = 1;
     int st = MGC_CUDA_OK;
+    LaunchInfo gemm;
     switch (L.kind) {
     case MGC_K_GEMM: {
         GemmParams p;
@@ -248,7 +261,8 @@ inline int launch_record(const mgc_cuda_launch &L, const int64_t *aux, int64_t a
         p.err = status_dev;
         p.split_ws = bases.split_ws;
         p.split_ws_floats = bases.split_ws_floats;
-        st = run_gemm(p, stream);
+        st = run_gemm(p, stream, &gemm);
+        launched = gemm.kernels;
         break;
     }
     case MGC_K_DEPTHWISE: {
@@ -527,7 +541,10 @@ inline int launch_record(const mgc_cuda_launch &L, const int64_t *aux, int64_t a
         return fail(MGC_CUDA_UNSUPPORTED, "unknown launch kind %d (node %d)", L.kind, L.node);
     }
     if (st != MGC_CUDA_OK) return st;
-    if (kernels) *kernels += launched;
+    if (info) {
+        info->kernels = launched;
+        info->gemm_path = gemm.gemm_path;
+    }
     return MGC_CUDA_OK;
 }
 

@@ -9,7 +9,9 @@
 #include <cuda_runtime.h>
 #include <string.h>
 
+#include <atomic>
 #include <memory>
+#include <mutex>
 #include <vector>
 
 #include "launch.cuh"
@@ -41,6 +43,7 @@ struct Model {
     cudaGraph_t graph = nullptr;
     cudaGraphExec_t exec = nullptr;
     int kernel_launches = 0;
+    std::vector<int32_t> gemm_paths;  // MGC_CUDA_PATH_* per launch record
     // input-upload overlap (mgc_cuda_set_input_chunks): a copy stream, one event per slice and
     // the graph whose prefix runs slice by slice
     int chunks = 0, prefix = 0;
@@ -64,12 +67,22 @@ struct Model {
         return b;
     }
 
+    // Record k's kernel count and GEMM path (the worst path seen, when it runs more than once).
+    void note(size_t k, const LaunchInfo &info, int *kernels) {
+        *kernels += info.kernels;
+        if (gemm_paths.size() < launches.size()) gemm_paths.assign(launches.size(), MGC_CUDA_PATH_NONE);
+        if (info.gemm_path > gemm_paths[k]) gemm_paths[k] = info.gemm_path;
+    }
+
     // Enqueue the whole launch list on `stream` (also used under graph capture).
     int enqueue(int *kernels) {
         MGC_CHECK_CUDA(cudaMemsetAsync(status_dev, 0, sizeof(int), stream));
         Bases b = bases();
-        for (const mgc_cuda_launch &L : launches)
-            MGC_CHECK(launch_record(L, aux.data(), (int64_t)aux.size(), b, status_dev, stream, kernels));
+        for (size_t k = 0; k < launches.size(); ++k) {
+            LaunchInfo info;
+            MGC_CHECK(launch_record(launches[k], aux.data(), (int64_t)aux.size(), b, status_dev, stream, &info));
+            note(k, info, kernels);
+        }
         return MGC_CUDA_OK;
     }
 
@@ -87,11 +100,16 @@ struct Model {
                     if (d.what == 0) L.r[d.slot].offset += (int64_t)j * per * d.per_image;
                     else L.i[d.slot] = d.per_image * per;
                 }
-                MGC_CHECK(launch_record(L, aux.data(), (int64_t)aux.size(), b, status_dev, stream, kernels));
+                LaunchInfo info;
+                MGC_CHECK(launch_record(L, aux.data(), (int64_t)aux.size(), b, status_dev, stream, &info));
+                note((size_t)r, info, kernels);
             }
         }
-        for (size_t r = (size_t)prefix; r < launches.size(); ++r)
-            MGC_CHECK(launch_record(launches[r], aux.data(), (int64_t)aux.size(), b, status_dev, stream, kernels));
+        for (size_t r = (size_t)prefix; r < launches.size(); ++r) {
+            LaunchInfo info;
+            MGC_CHECK(launch_record(launches[r], aux.data(), (int64_t)aux.size(), b, status_dev, stream, &info));
+            note(r, info, kernels);
+        }
         return MGC_CUDA_OK;
     }
 
@@ -273,7 +291,7 @@ int mgc_cuda_set_input_chunks(void *handle, int chunks, int prefix, int64_t imag
         m->slice_ready.push_back(e);
     }
     MGC_CHECK_CUDA(cudaStreamBeginCapture(m->stream, cudaStreamCaptureModeThreadLocal));
-    int kernels = 0;
+    int kernels = 0;  // the sliced graph's launches (mgc_cuda_launch_count reports the one-pass graph's)
     const int st = m->enqueue_sliced(&kernels);
     cudaGraph_t graph = nullptr;
     const cudaError_t err = cudaStreamEndCapture(m->stream, &graph);
@@ -363,6 +381,15 @@ int mgc_cuda_launch_count(void *handle) {
     return m ? m->kernel_launches : -1;
 }
 
+int mgc_cuda_gemm_paths(void *handle, int32_t *per_record, int n) {
+    last_error().clear();
+    Model *m = (Model *)handle;
+    if (!m || n < 0 || (n > 0 && !per_record)) return fail(MGC_CUDA_BAD_ARGUMENT, "mgc_cuda_gemm_paths: bad arguments");
+    for (int k = 0; k < n; ++k)
+        per_record[k] = (size_t)k < m->gemm_paths.size() ? m->gemm_paths[(size_t)k] : MGC_CUDA_PATH_NONE;
+    return MGC_CUDA_OK;
+}
+
 int64_t mgc_cuda_arena_bytes(void *handle) {
     Model *m = (Model *)handle;
     return m ? m->arena_bytes : -1;
@@ -390,7 +417,8 @@ int mgc_cuda_profile(void *handle, double *per_node_ms, int n) {
     Bases b = m->bases();
     for (size_t k = 0; k < L && st == MGC_CUDA_OK; ++k) {
         cudaEventRecord(ev[2 * k], m->stream);
-        st = launch_record(m->launches[k], m->aux.data(), (int64_t)m->aux.size(), b, m->status_dev, m->stream, nullptr);
+        st = launch_record(m->launches[k], m->aux.data(), (int64_t)m->aux.size(), b, m->status_dev, m->stream,
+                           nullptr);
         cudaEventRecord(ev[2 * k + 1], m->stream);
     }
     if (st == MGC_CUDA_OK) st = finish(*m);
@@ -442,7 +470,20 @@ int mgc_cuda_gemm(int M, int N, int K, int batch, const float *a, int64_t a_rs, 
     p.alpha = alpha; p.beta = beta; p.bias = bias; p.bias_mode = bias ? bias_mode : 0;
     p.res = res; p.ldr = ldr; p.act = act; p.lo = lo; p.hi = hi; p.precision = precision;
     if (batch == 1) p.nb = 0;
-    return run_gemm(p, (cudaStream_t)stream);
+    if (precision == MGC_PREC_FP32) return launch_gemm_simt(p, (cudaStream_t)stream);
+    if (precision == MGC_PREC_3XTF32)
+        return fail(MGC_CUDA_UNSUPPORTED, "mgc_cuda_gemm: 3xTF32 needs constant weights prepared by "
+                                          "mgc_cuda_create; use MGC_PREC_FP32 for exact fp32");
+    if (precision != MGC_PREC_TF32) return fail(MGC_CUDA_BAD_ARGUMENT, "mgc_cuda_gemm: precision %d", precision);
+    if (M == 0 || N == 0 || batch == 0) return MGC_CUDA_OK;
+    int taken = 0;
+    MGC_CHECK(try_gemm_umma_dyn(p, (cudaStream_t)stream, &taken));
+    if (!taken)
+        return fail(MGC_CUDA_UNSUPPORTED,
+                    "mgc_cuda_gemm: TF32 runs on the tensor cores only with K-major A and B (a_cs == 1, b_rs == 1), "
+                    "16-byte aligned bases and strides, K and N multiples of 4, bias per column, and no epilogue "
+                    "on batched products; use MGC_PREC_FP32 for exact fp32 on the CUDA cores");
+    return MGC_CUDA_OK;
 }
 
 int mgc_cuda_conv_nhwc(int N, int H, int W, int C, int KH, int KW, int SH, int SW, int DH, int DW,
@@ -452,6 +493,10 @@ int mgc_cuda_conv_nhwc(int N, int H, int W, int C, int KH, int KW, int SH, int S
     last_error().clear();
     if (!x || !w || !y || N < 0 || OH < 0 || OW < 0 || CO < 0)
         return fail(MGC_CUDA_BAD_ARGUMENT, "mgc_cuda_conv_nhwc: bad arguments");
+    if (precision == MGC_PREC_TF32 || precision == MGC_PREC_3XTF32)
+        return fail(MGC_CUDA_UNSUPPORTED, "mgc_cuda_conv_nhwc: TF32 / 3xTF32 need the K-major weight layout that "
+                                          "mgc_cuda_create prepares; HWIO weights run with MGC_PREC_FP32");
+    if (precision != MGC_PREC_FP32) return fail(MGC_CUDA_BAD_ARGUMENT, "mgc_cuda_conv_nhwc: precision %d", precision);
     GemmParams p{};
     p.M = N * OH * OW; p.N = CO; p.K = KH * KW * C;
     p.nb = 0;
@@ -463,7 +508,7 @@ int mgc_cuda_conv_nhwc(int N, int H, int W, int C, int KH, int KW, int SH, int S
     p.c = y; p.ldc = CO;
     p.alpha = 1.0f; p.beta = 1.0f; p.bias = bias; p.bias_mode = bias ? 1 : 0;
     p.res = res; p.ldr = CO; p.act = act; p.lo = lo; p.hi = hi; p.precision = precision;
-    return run_gemm(p, (cudaStream_t)stream);
+    return launch_gemm_simt(p, (cudaStream_t)stream);
 }
 
 int mgc_cuda_depthwise_nhwc(int N, int H, int W, int C, int KH, int KW, int SH, int SW, int DH,
@@ -549,19 +594,28 @@ static __device__ __align__(256) float g_noalloc_scratch[MGC_CUDA_NOALLOC_SCRATC
 
 namespace {
 
-// Device address of g_noalloc_scratch on the current device, looked up once per device. In host
-// code the array's name is only a stand-in for the symbol, never a usable device pointer.
+// Device address of g_noalloc_scratch on the current device, looked up once per device (with that
+// device current) and published atomically, so host threads making their first call at once
+// agree on it; a failed lookup is retried by the next call. In host code the array's name is only
+// a stand-in for the symbol, never a usable device pointer.
 int noalloc_scratch(float **out) {
-    static float *addr[64] = {nullptr};
+    static std::atomic<float *> addr[64];
+    static std::mutex lookup;
     int dev = 0;
     MGC_CHECK_CUDA(cudaGetDevice(&dev));
     if (dev < 0 || dev >= 64) return fail(MGC_CUDA_UNSUPPORTED, "device ordinal %d out of range", dev);
-    if (!addr[dev]) {
-        void *p = nullptr;
-        MGC_CHECK_CUDA(cudaGetSymbolAddress(&p, g_noalloc_scratch));
-        addr[dev] = static_cast<float *>(p);
+    float *known = addr[dev].load(std::memory_order_acquire);
+    if (!known) {
+        std::lock_guard<std::mutex> guard(lookup);
+        known = addr[dev].load(std::memory_order_acquire);
+        if (!known) {
+            void *p = nullptr;
+            MGC_CHECK_CUDA(cudaGetSymbolAddress(&p, g_noalloc_scratch));
+            known = static_cast<float *>(p);
+            addr[dev].store(known, std::memory_order_release);
+        }
     }
-    *out = addr[dev];
+    *out = known;
     return MGC_CUDA_OK;
 }
 

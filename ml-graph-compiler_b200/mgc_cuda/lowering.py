@@ -1225,9 +1225,11 @@ class CudaEmitter:
             bref, blo, b_rs, b_cs = self._kmajor_b(data, ("kmajor", id(self._root(b)), 0))
         else:
             blo = NO_REF
-            if self.precision == "tf32" and batch_shape and b_cs == 1 and b_rs != 1 and bt.rank >= 3:
+            if self.precision == "tf32" and b_cs == 1 and b_rs != 1 and bt.rank >= 2 and not (
+                    batch_shape and bt.rank == 2):
                 # N-major B: one transposed copy into the workspace (K-major, [batch][n][k]) for
-                # the tensor-core batched GEMM, which reads B rows along K
+                # the tensor-core GEMM with a dynamic B, which reads B rows along K (a rank-2 B
+                # broadcast over A's batch stays on the exact-fp32 kernel)
                 own = [int(d) for d in bshape[:-2]]
                 tshape = [*own, n, k]
                 self._copy(tshape, bref, [*bv[:-2], b_cs, b_rs], 0, (SPACE_WORKSPACE, 0, 0), _strides(tshape), 0, 4,

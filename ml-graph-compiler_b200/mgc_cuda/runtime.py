@@ -47,6 +47,7 @@ SIGNATURES: dict[str, tuple[Any, list[Any]]] = {
     "mgc_cuda_stream": (_VP, [_VP]),
     "mgc_cuda_profile": (_I, [_VP, ctypes.POINTER(_D), _I]),
     "mgc_cuda_launch_count": (_I, [_VP]),
+    "mgc_cuda_gemm_paths": (_I, [_VP, ctypes.POINTER(ctypes.c_int32), _I]),
     "mgc_cuda_arena_bytes": (_I64, [_VP]),
     "mgc_cuda_weights_bytes": (_I64, [_VP]),
     "mgc_cuda_destroy": (None, [_VP]),
@@ -156,8 +157,6 @@ class CudaCompiledModel:
                                                     len(descs))
             check(st, "mgc_cuda_set_input_chunks", self.lib)
             self.slices = slices
-        self._in_ptrs = (ctypes.c_void_p * max(len(self.inputs), 1))()
-        self._out_ptrs = (ctypes.c_void_p * max(len(self.outputs), 1))()
 
     def __del__(self) -> None:
         self.close()
@@ -175,6 +174,22 @@ class CudaCompiledModel:
     @property
     def launch_count(self) -> int:
         return int(self.lib.mgc_cuda_launch_count(self._handle))
+
+    # MGC_CUDA_PATH_* of include/mgc_cuda.h
+    GEMM_PATHS = {1: "tcgen05", 2: "simt"}
+
+    def gemm_paths(self) -> list[tuple[int, str, str, str]]:
+        """(node index, op, node name, "tcgen05" | "simt") for every GEMM-family launch record:
+        which kernel computes it (mgc_cuda_gemm_paths)."""
+        n = len(self.lowered.launches)
+        buf = (ctypes.c_int32 * max(n, 1))()
+        check(self.lib.mgc_cuda_gemm_paths(self._handle, buf, n), "mgc_cuda_gemm_paths", self.lib)
+        out = []
+        for k, rec in enumerate(self.lowered.launches):
+            if buf[k] in self.GEMM_PATHS:
+                op, name = self.node_names[rec.node] if 0 <= rec.node < len(self.node_names) else ("", "")
+                out.append((int(rec.node), op, name, self.GEMM_PATHS[buf[k]]))
+        return out
 
     def input_ptr(self, i: int) -> int:
         return int(self.lib.mgc_cuda_input_ptr(self._handle, i) or 0)
@@ -204,17 +219,18 @@ class CudaCompiledModel:
         """Copy the inputs in, replay the CUDA Graph, copy the outputs out (runtime_lib.py:117-144).
         ``out`` may supply preallocated (e.g. pinned) output arrays."""
         arrays = self._check_feeds(feeds)
-        for i, a in enumerate(arrays):
-            self._in_ptrs[i] = a.ctypes.data
         results: dict[str, np.ndarray] = {}
-        for j, (name, t) in enumerate(self.outputs):
+        for name, t in self.outputs:
             o = out[name] if out is not None and name in out else np.empty(t.shape, numpy_dtype(t.dtype))
             if o.shape != t.shape or o.dtype != numpy_dtype(t.dtype) or not o.flags.c_contiguous:
                 raise GraphError(f"output buffer {name!r} must be a contiguous {t}")
             results[name] = o
-            self._out_ptrs[j] = o.ctypes.data
+        # pointer tables of this call only: concurrent calls each pass their own buffers, and the
+        # lock serialises the native call that shares the arena
+        in_ptrs = (ctypes.c_void_p * max(len(arrays), 1))(*[a.ctypes.data for a in arrays])
+        out_ptrs = (ctypes.c_void_p * max(len(results), 1))(*[o.ctypes.data for o in results.values()])
         with self._lock:
-            st = self.lib.mgc_cuda_run(self._handle, ctypes.addressof(self._in_ptrs), ctypes.addressof(self._out_ptrs))
+            st = self.lib.mgc_cuda_run(self._handle, ctypes.addressof(in_ptrs), ctypes.addressof(out_ptrs))
         check(st, "mgc_cuda_run", self.lib)
         return results
 
@@ -299,19 +315,22 @@ class CudaCompiledModel:
 
 def compile_graph(
     graph: Graph,
-    precision: str = "tf32",
-    device: int = 0,
+    options: Any = None,
+    cache_dir: str | Path | None = None,
     strategy: Strategy = "greedy_by_size",
     inplace: bool = True,
     name: str = "model",
     profile: bool = False,
-    cache_dir: str | Path | None = None,
-    options: Any = None,
+    *,
+    precision: str = "tf32",
+    device: int = 0,
 ) -> CudaCompiledModel:
     """Lower an (already optimised and scheduled) graph for the cuda target and load it on
-    ``device`` (the cuda form of runtime_lib.py:197-236). ``profile``, ``cache_dir`` and
-    ``options`` are accepted for signature compatibility: profiling is always available through
-    ``CudaCompiledModel.profile`` and the one shared library is cached in tree."""
+    ``device`` (the cuda form of runtime_lib.py:197-236, with the reference's positional
+    parameters in its order; ``precision`` and ``device`` are keyword-only). ``options`` (the C
+    compiler's BuildOptions), ``cache_dir``, ``name`` and ``profile`` are accepted for signature
+    compatibility: there is no per-model build (one shared library, built in tree) and
+    per-node profiling is always available through ``CudaCompiledModel.profile``."""
     del name, profile, cache_dir, options
     start = time.perf_counter()
     lowered = lower_graph(graph, strategy, inplace, precision)

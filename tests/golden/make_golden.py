@@ -15,7 +15,8 @@ Run from the repository root in a checkout where the reference is importable::
     MGC_CC=/usr/bin/gcc python tests/golden/make_golden.py [--big]
 
 It imports the reference's sources from ``$MGC_REFERENCE_SRC`` (the ``src`` directory of a
-reference checkout) when that directory exists, else the installed copy in ``baseline/_ref``.
+reference checkout) when that variable names an existing directory, else the installed copy in
+``baseline/_ref``.
 """
 
 from __future__ import annotations
@@ -31,8 +32,8 @@ import numpy as np
 
 HERE = Path(__file__).resolve().parent
 ROOT = HERE.parents[1]
-_SRC = os.environ.get("MGC_REFERENCE_SRC", "/root/reference/src")
-if Path(_SRC).exists():
+_SRC = os.environ.get("MGC_REFERENCE_SRC", "")
+if _SRC and Path(_SRC).is_dir():
     sys.path.insert(0, _SRC)
 else:
     sys.path.insert(0, str(ROOT / "baseline" / "_ref"))

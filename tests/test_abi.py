@@ -44,11 +44,13 @@ def test_library_is_built_for_sm100a() -> None:
 
 def test_abi_version_and_errors_without_gpu() -> None:
     lib = runtime.library()
-    assert lib.mgc_cuda_abi_version() == 2
+    assert lib.mgc_cuda_abi_version() == 3
     # a NULL handle is rejected on the host, before any CUDA call
     assert lib.mgc_cuda_run(None, None, None) == 2
     assert "NULL" in runtime.last_error(lib)
     assert lib.mgc_cuda_launch_count(None) == -1
+    paths = (ctypes.c_int32 * 4)()
+    assert lib.mgc_cuda_gemm_paths(None, paths, 4) == 2
 
 
 def test_launch_record_layout_matches_header() -> None:

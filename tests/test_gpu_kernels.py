@@ -38,13 +38,26 @@ def ref_lib() -> ctypes.CDLL | None:
     return ctypes.CDLL(str(REF_LIB)) if REF_LIB.exists() else None
 
 
+def tf32_round(a: np.ndarray) -> np.ndarray:
+    """fp32 rounded to the nearest TF32 value (10 mantissa bits, ties away from zero): what a
+    TFLOAT32 tensor map does to an operand on load."""
+    from mgc_cuda.lowering import tf32_split
+
+    return tf32_split(a)[0]
+
+
 @pytest.mark.parametrize("kmajor", [False, True])
 @pytest.mark.parametrize("precision", [0, 1, 2])
 @pytest.mark.parametrize("m,n,k,act", [(1, 1000, 2048, 0), (197, 77, 129, 1), (512, 256, 64, 3), (64, 3072, 768, 4),
                                        (300, 200, 100, 1)])
 def test_gemm_vs_torch(m: int, n: int, k: int, act: int, precision: int, kmajor: bool) -> None:
-    """Row-major and K-major B through the strided kernel ABI (exact fp32 arithmetic); the
-    tensor-core kernel is reached through models, whose constant B the lowering stores split."""
+    """The kernel ABI's GEMM does the arithmetic its precision names, or refuses:
+    * fp32 (0): exact fp32 on the CUDA cores, any layout, within 1e-5 of a float64 product;
+    * tf32 (1): the tcgen05 tensor cores when A and B are K-major with aligned rows (K and N
+      multiples of 4), matching a float64 product of the TF32-rounded operands within 1e-4 of the
+      output scale (fp32 accumulation); any other layout returns MGC_CUDA_UNSUPPORTED and leaves
+      the output untouched;
+    * 3xtf32 (2): MGC_CUDA_UNSUPPORTED (the strict split needs weights prepared at load time)."""
     rng = np.random.default_rng(m + n + k)
     a = rng.standard_normal((m, k)).astype(np.float32)
     b = rng.standard_normal((k, n)).astype(np.float32) * 0.05
@@ -53,28 +66,50 @@ def test_gemm_vs_torch(m: int, n: int, k: int, act: int, precision: int, kmajor:
     A, Bi, R = dev(a), dev(bias), dev(res)
     B = dev(np.ascontiguousarray(b.T)) if kmajor else dev(b)
     b_rs, b_cs = (1, k) if kmajor else (n, 1)
-    C = torch.empty((m, n), device="cuda")
+    C = torch.full((m, n), float("nan"), device="cuda")
     lib = library()
-    ok(lib.mgc_cuda_gemm(m, n, k, 1, ptr(A), k, 1, 0, ptr(B), b_rs, b_cs, 0, ptr(C), n, 0, 1.0, ptr(Bi), 1, ptr(R), n,
-                         0, 1.0, act, 0.0, 6.0, precision, stream()))
-    if kmajor:
-        B = B.t()
+    st = lib.mgc_cuda_gemm(m, n, k, 1, ptr(A), k, 1, 0, ptr(B), b_rs, b_cs, 0, ptr(C), n, 0, 1.0, ptr(Bi), 1, ptr(R), n,
+                           0, 1.0, act, 0.0, 6.0, precision, stream())
     torch.cuda.synchronize()
-    with torch.no_grad():
-        prev = torch.backends.cuda.matmul.allow_tf32
-        torch.backends.cuda.matmul.allow_tf32 = False
-        y = A.double() @ B.double() + Bi.double() + R.double()
-        torch.backends.cuda.matmul.allow_tf32 = prev
-        y = {0: y, 1: torch.relu(y), 3: torch.nn.functional.gelu(y), 4: torch.nn.functional.gelu(y, approximate="tanh")}[act]
-    err = float((C.double() - y).abs().max())
+    supported = precision == 0 or (precision == 1 and kmajor and k % 4 == 0 and n % 4 == 0)
+    if not supported:
+        assert st == 3, (st, last_error())
+        assert "MGC_PREC_FP32" in last_error()
+        assert bool(torch.isnan(C).all())
+        return
+    ok(st)
+    if precision == 1:
+        a, b = tf32_round(a), tf32_round(b)
+    y = a.astype(np.float64) @ b.astype(np.float64) + bias + res
+    y = torch.from_numpy(y)
+    y = {0: y, 1: torch.relu(y), 3: torch.nn.functional.gelu(y), 4: torch.nn.functional.gelu(y, approximate="tanh")}[act]
+    err = float((C.double().cpu() - y).abs().max())
     scale = float(y.abs().max())
-    tol = 2e-2 if precision == 1 else 1e-5
+    tol = 1e-4 if precision == 1 else 1e-5
     assert err <= tol * max(scale, 1.0), f"err {err:.3g} scale {scale:.3g}"
 
 
+def test_gemm_tf32_batched_dynamic_b() -> None:
+    """TF32 batched product of two activations (attention's form) through the kernel ABI: one
+    batch dimension with a constant stride, on the tensor cores."""
+    rng = np.random.default_rng(11)
+    batch, m, n, k = 6, 128, 128, 64
+    a = rng.standard_normal((batch, m, k)).astype(np.float32)
+    bt = rng.standard_normal((batch, n, k)).astype(np.float32)  # K-major B
+    A, B = dev(a), dev(bt)
+    C = torch.empty((batch, m, n), device="cuda")
+    ok(library().mgc_cuda_gemm(m, n, k, batch, ptr(A), k, 1, m * k, ptr(B), 1, k, n * k, ptr(C), n, m * n, 1.0, None, 0,
+                               None, 0, 0, 1.0, 0, 0.0, 6.0, 1, stream()))
+    torch.cuda.synchronize()
+    want = np.einsum("bmk,bnk->bmn", tf32_round(a).astype(np.float64), tf32_round(bt).astype(np.float64))
+    err = float(np.abs(C.cpu().numpy() - want).max())
+    assert err <= 1e-4 * float(np.abs(want).max())
+
+
 @pytest.mark.parametrize("shape", [(2, 14, 14, 64, 3, 1, 1), (1, 56, 56, 64, 1, 1, 0), (2, 28, 28, 32, 3, 2, 1), (1, 32, 32, 3, 7, 2, 3)])
-@pytest.mark.parametrize("precision", [0, 2])
-def test_conv_nhwc_vs_torch(shape: tuple, precision: int) -> None:
+def test_conv_nhwc_vs_torch(shape: tuple) -> None:
+    """Exact fp32 (precision 0) against a float64 convolution; TF32 and 3xTF32 are refused with
+    MGC_CUDA_UNSUPPORTED (their tensor-core forms read weights the lowering lays out K-major)."""
     n, h, w, c, kk, s, p = shape
     co = 48
     rng = np.random.default_rng(h * c)
@@ -85,8 +120,13 @@ def test_conv_nhwc_vs_torch(shape: tuple, precision: int) -> None:
     ow = (w + 2 * p - kk) // s + 1
     X, W, Bi = dev(x), dev(wt), dev(bias)
     Y = torch.empty((n, oh, ow, co), device="cuda")
-    ok(library().mgc_cuda_conv_nhwc(n, h, w, c, kk, kk, s, s, 1, 1, p, p, oh, ow, co, ptr(X), ptr(W), ptr(Bi), None,
-                                    1, 0.0, 6.0, ptr(Y), precision, stream()))
+    lib = library()
+    for precision in (1, 2):
+        st = lib.mgc_cuda_conv_nhwc(n, h, w, c, kk, kk, s, s, 1, 1, p, p, oh, ow, co, ptr(X), ptr(W), ptr(Bi), None,
+                                    1, 0.0, 6.0, ptr(Y), precision, stream())
+        assert st == 3 and "MGC_PREC_FP32" in last_error()
+    ok(lib.mgc_cuda_conv_nhwc(n, h, w, c, kk, kk, s, s, 1, 1, p, p, oh, ow, co, ptr(X), ptr(W), ptr(Bi), None,
+                              1, 0.0, 6.0, ptr(Y), 0, stream()))
     torch.cuda.synchronize()
     ref = torch.nn.functional.conv2d(X.permute(0, 3, 1, 2).double(), W.permute(3, 2, 0, 1).double(), Bi.double(),
                                      stride=s, padding=p).relu().permute(0, 2, 3, 1)

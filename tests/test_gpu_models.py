@@ -84,7 +84,8 @@ def test_resnet50_batch_is_independent_per_image() -> None:
     m1.close()
 
 
-@pytest.mark.parametrize("name,strategy", [("bert", "greedy_by_size"), ("gpt2", "greedy_by_size"), ("gpt2", "naive")])
+@pytest.mark.parametrize("name,strategy", [("bert", "greedy_by_size"), ("bert", "naive"), ("gpt2", "greedy_by_size"),
+                                           ("gpt2", "naive")])
 def test_transformer_batch_is_independent_per_sequence(name: str, strategy: str) -> None:
     """Size-independent property at the benchmark batch: every sequence of a batch-32 TF32 run
     (attention read through strides, the softmax over the mask program, 192-wide pair tiles,

@@ -5,11 +5,13 @@ inside the library instead of a buffer it allocates, so the only memory it touch
 caller's inputs and outputs plus that array.
 
 The test calls it twice in a row through the C ABI, with different shapes, and checks each
-result against the existing mgc_cuda_conv_nhwc on the same inputs (exact-fp32 arithmetic on
-both sides, compared at the kernel tests' 1e-5 relative tolerance). It also checks that a patch
-matrix larger than the array is refused with a clear error. The file is named to be collected
-last, so a run that stops at the first failure has run every other test first; it passes alone
-in a fresh process as well."""
+result against the existing mgc_cuda_conv_nhwc on the same inputs and against a float64
+convolution (exact-fp32 arithmetic, compared at the kernel tests' 1e-5 relative tolerance). It
+checks the property that defines it: after a first call, further calls leave the device's free
+memory unchanged (nothing allocated, nothing freed). It also checks that a patch matrix larger
+than the array is refused with a clear error. The file is named to be collected last, so a run
+that stops at the first failure has run every other test first; it passes alone in a fresh
+process as well."""
 
 from __future__ import annotations
 
@@ -36,11 +38,16 @@ def _conv_args(n: int, h: int, w: int, c: int, k: int, s: int, p: int, co: int, 
     return (n, h, w, c, k, k, s, s, 1, 1, p, p, oh, ow, co), x, wt, bias, res
 
 
-def _run(fn_name: str, geo, x, wt, bias, res, act: int) -> "torch.Tensor":
+def _run(fn_name: str, geo, x, wt, bias, res, act: int, free: list[int] | None = None) -> "torch.Tensor":
+    """One call through the C ABI; with `free`, the device's free bytes just before and just after
+    the call (the output buffer is allocated before the first reading) are appended to it."""
     lib = library()
     n, oh, ow, co = geo[0], geo[12], geo[13], geo[14]
     y = torch.full((n, oh, ow, co), float("nan"), device="cuda")
     stream = torch.cuda.current_stream().cuda_stream
+    torch.cuda.synchronize()
+    if free is not None:
+        free.append(torch.cuda.mem_get_info()[0])
     fn = getattr(lib, fn_name)
     if fn_name == "mgc_cuda_conv_nhwc":
         st = fn(*geo, x.data_ptr(), wt.data_ptr(), bias.data_ptr(), res.data_ptr(), act, 0.0, 6.0, y.data_ptr(),
@@ -50,19 +57,39 @@ def _run(fn_name: str, geo, x, wt, bias, res, act: int) -> "torch.Tensor":
                 stream)
     assert st == 0, last_error()
     torch.cuda.synchronize()
+    if free is not None:
+        free.append(torch.cuda.mem_get_info()[0])
     return y
+
+
+def _float64_conv(geo, x, wt, bias, res, act: int) -> "torch.Tensor":
+    s, p = geo[6], geo[10]
+    y = torch.nn.functional.conv2d(x.permute(0, 3, 1, 2).double(), wt.permute(3, 2, 0, 1).double(), bias.double(),
+                                   stride=s, padding=p).permute(0, 2, 3, 1) + res.double()
+    return y.relu() if act == 1 else y.clamp(0.0, 6.0)
 
 
 def test_noalloc_conv_matches_the_allocating_entry_point_twice_in_a_row() -> None:
     # the stem shape of ResNet-50 (3 channels, 7x7 stride 2) and a 3x3 layer, one after the other
+    free: list[int] = []
     for (n, h, w, c, k, s, p, co, act, seed) in ((1, 64, 64, 3, 7, 2, 3, 64, 1, 1), (2, 14, 14, 24, 3, 1, 1, 40, 2, 2)):
         geo, x, wt, bias, res = _conv_args(n, h, w, c, k, s, p, co, seed)
         want = _run("mgc_cuda_conv_nhwc", geo, x, wt, bias, res, act)
-        got = _run("mgc_cuda_conv_nhwc_noalloc", geo, x, wt, bias, res, act)
+        got = _run("mgc_cuda_conv_nhwc_noalloc", geo, x, wt, bias, res, act, free)
         assert torch.isfinite(got).all()
-        err = float((got.double() - want.double()).abs().max())
         scale = max(float(want.abs().max()), 1.0)
-        assert err <= 1e-5 * scale, f"max abs err {err:.3g} (scale {scale:.3g})"
+        err = float((got.double() - want.double()).abs().max())
+        assert err <= 1e-5 * scale, f"vs mgc_cuda_conv_nhwc: max abs err {err:.3g} (scale {scale:.3g})"
+        err64 = float((got.double() - _float64_conv(geo, x, wt, bias, res, act)).abs().max())
+        assert err64 <= 1e-5 * scale, f"vs float64: max abs err {err64:.3g} (scale {scale:.3g})"
+    # the first call of the process may load the module's device code; every later call allocates
+    # and frees nothing, so the free device memory around it does not move
+    assert free[2] == free[3], f"the second call changed free device memory: {free}"
+    geo, x, wt, bias, res = _conv_args(1, 64, 64, 3, 7, 2, 3, 64, 1, 1)
+    more: list[int] = []
+    for _ in range(3):
+        _run("mgc_cuda_conv_nhwc_noalloc", geo, x, wt, bias, res, 1, more)
+    assert more[0::2] == more[1::2], f"repeated calls changed free device memory: {more}"
 
 
 def test_noalloc_conv_refuses_a_patch_matrix_larger_than_its_scratch() -> None:
