@@ -1,24 +1,27 @@
 """Benchmark of the `cuda` target on its headline workload: ResNet-50 (BASELINE configs 0 and 4).
 
 Default arm (our backend), one process per GPU (``torchrun`` for N > 1, batch-sharded replicas,
-weak scaling: every GPU runs its own batch of ``--batch`` images, no collectives on the data path):
+no collective on the data path):
 
-* ``value``: whole-job img/s of the compiled ResNet-50 (O3 graph, CUDA Graph replay) with the
-  inputs resident in HBM, timed with CUDA events on the model's stream over ``--steps`` replays
-  after ``--warmup`` untimed ones, max over ranks;
+* ``value``: whole-job img/s of the compiled ResNet-50 (O3 graph on the reference planner's
+  default memory plan, CUDA Graph replay) at ``--batch`` images per GPU (weak scaling), inputs
+  resident in HBM, timed with CUDA events on the model's stream over ``--steps`` replays after
+  ``--warmup`` untimed ones, max over ranks;
 * ``e2e``: the same through the public API ``CudaCompiledModel.run`` from pinned host memory
   (host->device input copy, replay, device->host logits copy every step; the input is uploaded
-  in four slices whose copies overlap the stem and layer1 of the earlier slices);
-* ``roofline``: the dominant kernel (the implicit-GEMM convolution / GEMM launches) from one
-  eagerly launched pass with CUDA events around every launch, against MEASURED_PEAKS.json;
-* ``latency_b1``: batch-1 p50 latency (public API and device-only replay);
-* ``bert``: BERT-base sequence-128 batch-32 seq/s, device-timed replays and
-  through ``run``;
-* ``cpu_baseline``: the reference's own C backend (gcc + OpenMP) on this host's cores, on a
-  bounded batch.
+  in four slices whose copies overlap the first layers of the earlier slices);
+* ``roofline``: the dominant kernel family (the implicit-GEMM convolution / GEMM launches) from
+  one eagerly launched pass with CUDA events around every launch, against MEASURED_PEAKS.json;
+* ``fixed_total_batch``: BASELINE config 4 as a fixed total batch (256 and 1024 images) sharded
+  over the N GPUs (strong scaling), whole-job img/s;
+* at N = 1 also: the naive memory plan, strict (3xTF32) mode, batch-1 latency, and the other
+  BASELINE configs (MobileNetV2 b128, BERT-base b32 and b1, GPT-2 b16);
+* ``cpu_baseline``: the reference's own C backend (gcc + OpenMP, every host thread) on a bounded
+  sample of the workload.
 
 ``--impl reference`` runs the reference's C backend (the unmodified reference, installed in
-baseline/_ref, through its public ``compile_graph`` API) on the same workload on the host CPU.
+baseline/_ref, through its public ``compile_graph`` API) on the same workload on the host CPU,
+every host thread, on rank 0 only.
 """
 
 from __future__ import annotations
@@ -149,124 +152,224 @@ class Clocks:
                 "samples": len(sm), "source": "nvml" if self._nvml is not None else "nvidia-smi"}
 
 
-def measured_traffic(batch: int) -> int | None:
-    """DRAM bytes (read + write) of one step's GEMM launches, from the committed ncu summary
-    (measured at batch 32, scaled by the batch)."""
-    f = ROOT / "profiles" / "resnet50_step_launches.md"
-    if not f.exists():
-        return None
-    for line in f.read_text().splitlines():
-        if line.startswith("traffic_bytes_per_step_b32:"):
-            return int(int(line.split(":")[1]) * batch / 32)
-    return None
+def measured_traffic(batch: int) -> tuple[int | None, str]:
+    """DRAM bytes (read + write) of one step's GEMM launches from the committed ncu summary:
+    per-form captures at batch 256 summed over the step's launches
+    (profiles/resnet50_b256_gemm_traffic.md), scaled to `batch` when that differs; else None."""
+    f = ROOT / "profiles" / "resnet50_b256_gemm_traffic.md"
+    if f.exists():
+        for line in f.read_text().splitlines():
+            if line.startswith("traffic_bytes_per_step_b256:"):
+                v = int(line.split(":")[1])
+                note = "ncu at batch 256" + ("" if batch == 256 else f", scaled to batch {batch}")
+                return int(v * batch / 256), note
+    return None, "no batch-256 capture committed"
 
 
-def build_r50(batch: int, seed: int = 4):
+def prepared(name: str, **kw):
+    """A benchmark model (mgc_cuda.zoo: the BASELINE configs built in the reference IR with
+    seeded random-init weights) through the reference's O3 pipeline and scheduler."""
     from mgc_cuda import zoo
     from ml_graph_compiler.passes import optimize
     from ml_graph_compiler.schedule import schedule
 
-    g = zoo.resnet50(batch=batch, seed=0)
+    g = zoo.MODELS[name](**kw)
     optimize(g, "O3")
     schedule(g)
     return g
 
 
-def bert_throughput(precision: str, device: int, steps: int, warmup: int) -> dict:
-    """BERT-base, sequence 128, batch 32 (the metric's seq/s): CUDA Graph
-    replays with resident inputs timed with CUDA events on the model's stream, and the same
-    through ``run`` from pinned host buffers (token ids and mask uploaded, every output read back
-    each step)."""
+def build_r50(batch: int):
+    """ResNet-50 v1.5 (BASELINE configs 0 and 4): weights of config 0 (seed 0)."""
+    return prepared("resnet50", batch=batch, seed=0)
+
+
+def host_threads() -> int:
+    """Host threads this process may run on (the CPU affinity, not the machine's core count)."""
+    try:
+        return len(os.sched_getaffinity(0))
+    except (AttributeError, OSError):
+        return os.cpu_count() or 1
+
+
+def cpu_model() -> str:
+    try:
+        for line in Path("/proc/cpuinfo").read_text().splitlines():
+            if line.startswith("model name"):
+                return line.split(":", 1)[1].strip()
+    except OSError:
+        pass
+    return "unknown"
+
+
+def pinned_like(a: np.ndarray) -> np.ndarray:
+    """A page-locked host copy of `a` (asynchronous host<->device copies)."""
+    import torch
+
+    buf = torch.empty(a.shape, dtype=torch.from_numpy(np.ascontiguousarray(a[:0])).dtype, pin_memory=True).numpy()
+    buf[...] = a
+    return buf
+
+
+def device_ms(model, steps: int, warmup: int, group=None, clocks=None) -> float:
+    """Milliseconds per replay of the model's CUDA Graph with its inputs resident, CUDA events on
+    the model's stream, `warmup` untimed replays first; with a replica group, a barrier on both
+    sides and the max over ranks."""
+    import torch
+
+    stream = torch.cuda.ExternalStream(model.stream)
+    for _ in range(warmup):
+        model.run_device(sync=False)
+    if group is not None:
+        group.barrier()
+    else:
+        torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    if clocks is not None:
+        clocks.__enter__()
+    e0.record(stream)
+    for _ in range(steps):
+        model.run_device(sync=False)
+    e1.record(stream)
+    e1.synchronize()
+    if clocks is not None:
+        clocks.__exit__(None, None, None)
+    ms = e0.elapsed_time(e1)
+    if group is not None:
+        group.barrier()
+        ms = group.max(ms)
+    return ms / steps
+
+
+def e2e_s(model, feeds: dict, steps: int, group=None) -> tuple[float, int, int]:
+    """(seconds per call, H2D bytes, D2H bytes) of ``run`` from pinned host buffers: every call
+    copies the inputs in, replays the graph and copies every output back."""
+    pinned_in = {k: pinned_like(np.asarray(v)) for k, v in feeds.items()}
+    outs = model.run(pinned_in)
+    pinned_out = {k: pinned_like(v) for k, v in outs.items()}
+    for _ in range(2):
+        model.run(pinned_in, out=pinned_out)
+    if group is not None:
+        group.barrier()
+    t0 = time.perf_counter()
+    for _ in range(steps):
+        model.run(pinned_in, out=pinned_out)
+    dt = time.perf_counter() - t0
+    if group is not None:
+        dt = group.max(dt)
+    return (dt / steps, int(sum(a.nbytes for a in pinned_in.values())),
+            int(sum(a.nbytes for a in pinned_out.values())))
+
+
+def measure(name: str, kw: dict, units: int, unit: str, precision: str, device: int, steps: int, warmup: int,
+            strategy: str = "greedy_by_size", seed: int = 0, e2e: bool = True, group=None) -> dict:
+    """Device-timed throughput (and, with `e2e`, through ``run`` from pinned host buffers) of one
+    benchmark model; `units` images or sequences per replay."""
+    from mgc_cuda import zoo
+    from mgc_cuda.runtime import compile_graph
+
+    g = prepared(name, **kw)
+    m = compile_graph(g, precision=precision, device=device, strategy=strategy)
+    try:
+        feeds = zoo.feeds(g, seed)
+        m.run(feeds)  # inputs resident for the device-timed replays
+        ms = device_ms(m, steps, warmup, group)
+        world = group.world if group is not None else 1
+        out = {"value": round(world * units / (ms / 1e3), 2), "unit": unit, "ms_per_step": round(ms, 4),
+               "steps": steps, "warmup": warmup, "precision": precision, "memory_plan": strategy,
+               "gpu_launches_per_step": m.launch_count}
+        if e2e:
+            s, hi, ho = e2e_s(m, feeds, steps, group)
+            out["e2e"] = {"value": round(world * units / s, 2), "unit": unit, "h2d_bytes_per_step": hi,
+                          "d2h_bytes_per_step": ho}
+        return out
+    finally:
+        m.close()
+
+
+def latency(name: str, kw: dict, precision: str, device: int, seed: int) -> dict:
+    """Batch-1 p50 latency: through ``run`` (host buffers, wall clock) and device-only replays."""
     import torch
 
     from mgc_cuda import zoo
     from mgc_cuda.runtime import compile_graph
-    from ml_graph_compiler.passes import optimize
-    from ml_graph_compiler.schedule import schedule
 
-    batch, seq = 32, 128
-    g = zoo.bert(batch=batch, seq=seq, seed=2)
-    optimize(g, "O3")
-    schedule(g)
-    # the planner's naive strategy, as for ResNet-50: every buffer its own memory (3.0 GB), so no
-    # attention operand read through strides lies under a GEMM's output and needs a copy first
-    m = compile_graph(g, precision=precision, device=device, strategy="naive")
-    feeds = zoo.feeds(g, 2)
-    outs = m.run(feeds)
-    stream = torch.cuda.ExternalStream(m.stream)
-    for _ in range(warmup):
-        m.run_device(sync=False)
-    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    e0.record(stream)
-    for _ in range(steps):
-        m.run_device(sync=False)
-    e1.record(stream)
-    e1.synchronize()
-    ms = e0.elapsed_time(e1) / steps
-    # end to end with pinned host buffers, as for ResNet-50
-    pinned_in = {}
-    for k, v in feeds.items():
-        buf = torch.empty(v.shape, dtype=torch.from_numpy(np.ascontiguousarray(v)).dtype, pin_memory=True).numpy()
-        buf[...] = v
-        pinned_in[k] = buf
-    pinned_out = {}
-    for k, v in outs.items():
-        pinned_out[k] = torch.empty(v.shape, dtype=torch.from_numpy(np.ascontiguousarray(v)).dtype, pin_memory=True).numpy()
-    for _ in range(2):
-        m.run(pinned_in, out=pinned_out)
-    t0 = time.perf_counter()
-    for _ in range(steps):
-        m.run(pinned_in, out=pinned_out)
-    e2e_s = (time.perf_counter() - t0) / steps
-    m.close()
-    return {
-        "metric": "BERT-base seq128 seq/s (batch 32, O3 graph)", "value": round(batch / (ms / 1e3), 2),
-        "unit": "seq/s", "ms_per_step": round(ms, 4), "steps": steps, "warmup": warmup,
-        "e2e": {"value": round(batch / e2e_s, 2), "unit": "seq/s",
-                "h2d_bytes_per_step": int(sum(np.asarray(v).nbytes for v in feeds.values())),
-                "d2h_bytes_per_step": int(sum(np.asarray(v).nbytes for v in outs.values()))},
-        "l2": "weights (hi + lo TF32 parts) and activations stream through HBM every step, larger than L2",
-        "memory_plan": "naive",
-    }
+    g = prepared(name, **kw)
+    m = compile_graph(g, precision=precision, device=device)
+    try:
+        feeds = zoo.feeds(g, seed)
+        for _ in range(10):
+            m.run(feeds)
+        ts = []
+        for _ in range(100):
+            t0 = time.perf_counter()
+            m.run(feeds)
+            ts.append(time.perf_counter() - t0)
+        s1 = torch.cuda.ExternalStream(m.stream)
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        dts = []
+        for _ in range(50):
+            e0.record(s1)
+            m.run_device(sync=False)
+            e1.record(s1)
+            e1.synchronize()
+            dts.append(e0.elapsed_time(e1))
+        return {"p50_ms": round(statistics.median(ts) * 1e3, 4), "device_p50_ms": round(statistics.median(dts), 4),
+                "unit": "ms", "precision": precision}
+    finally:
+        m.close()
 
 
 def cpu_reference_run(batch: int, steps: int, warmup: int) -> dict:
-    """The reference C backend on this host: compile_graph(O3 graph) with gcc + OpenMP."""
+    """The reference C backend on this host: compile_graph(O3 graph) with gcc + OpenMP on every
+    host thread this process may use (set explicitly: torchrun exports OMP_NUM_THREADS=1)."""
     os.environ.setdefault("MGC_CC", "/usr/bin/gcc")
     from mgc_cuda import _reference  # noqa: F401  (the unmodified reference, baseline/_ref)
     from ml_graph_compiler.codegen import compile_graph as c_compile
 
     g = build_r50(batch)
     x = np.random.default_rng(4).standard_normal((batch, 3, 224, 224)).astype(np.float32)
+    threads = host_threads()
     with tempfile.TemporaryDirectory() as tmp:
         model = c_compile(g, cache_dir=tmp)
+        model.set_threads(threads)
         times = model.benchmark({"image": x}, warmup=warmup, repeat=steps)
-        threads = model.max_threads()
+        used = model.max_threads()
         openmp = model.openmp
     p50 = statistics.median(times)
-    return {"value": batch / p50, "p50_s": p50, "cores": threads, "openmp": openmp, "batch": batch,
-            "times": times}
+    return {"value": batch / p50, "p50_s": p50, "cores": used, "openmp": openmp, "batch": batch, "times": times}
+
+
+def headline_config(batch: int, world: int) -> dict:
+    """The workload of the headline line, identical in both arms (each arm's arithmetic is in
+    its ``details``)."""
+    return {"workload": f"resnet50 v1.5 O3 (BASELINE config 4), batch {batch} per GPU, fp32 tensors",
+            "batch_per_gpu": batch, "parallelism": f"replicas x{world}",
+            "l2": "inputs larger than L2 (input 154 MB, activations 1.8 GB per step at batch 256)"}
 
 
 def run_reference_arm(args: argparse.Namespace) -> None:
+    """The reference's own implementation of the path (its C backend, the CPU) on the same
+    workload: every timed step runs the whole per-GPU batch. Rank 0 only; other ranks exit."""
     rank = int(os.environ.get("RANK", "0"))
     if rank != 0:
         return
-    batch = args.ref_batch
     try:
-        r = cpu_reference_run(batch, args.steps, args.warmup)
+        r = cpu_reference_run(args.batch, args.steps, args.warmup)
     except Exception as exc:  # the reference could not be built or run on this host
         print(json.dumps({"impl": "reference", "unavailable": f"{type(exc).__name__}: {exc}"[:300]}))
         return
+    sample = (f"reference C backend (gcc + OpenMP, {r['cores']} threads, {cpu_model()}), ResNet-50 O3 batch "
+              f"{args.batch}, p50 of {args.steps} runs after {args.warmup} warm-up runs")
     line = {
         "impl": "reference", "metric": METRIC, "value": round(r["value"], 3), "unit": UNIT,
         "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
         "ms_per_step": round(r["p50_s"] * 1e3, 3), "higher_is_better": True, "scaling": "weak",
         "vs_baseline": None, "dtype": "f32", "data": "synthetic",
-        "config": {"workload": f"resnet50 O3, C backend (gcc+OpenMP), batch {batch} per step",
-                   "batch_per_step": batch, "threads": r["cores"], "openmp": r["openmp"]},
+        "config": headline_config(args.batch, args.gpus),
+        "details": {"precision": "fp32 (C backend)", "threads": r["cores"], "cpu": cpu_model()},
         "cpu_baseline": {"value": round(r["value"], 3), "unit": UNIT, "cores": r["cores"], "kind": "reference",
-                         "sample": f"ResNet-50 O3 batch {batch}, {args.steps} timed runs"},
+                         "sample": sample, "cpu": cpu_model(), "openmp": r["openmp"]},
         "e2e": {"value": round(r["value"], 3), "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
     print(json.dumps(line))
@@ -280,15 +383,12 @@ def main() -> None:
     ap.add_argument("--batch", type=int, default=256, help="images per GPU per step")
     ap.add_argument("--precision", default="tf32", choices=["tf32", "strict", "fp32"])
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
-    ap.add_argument("--ref-batch", type=int, default=16, help="images per step of the CPU reference arm")
-    ap.add_argument("--cpu-batch", type=int, default=8, help="images of the cpu_baseline sample")
+    ap.add_argument("--cpu-batch", type=int, default=64, help="images of the cpu_baseline sample")
     ap.add_argument("--no-cpu-baseline", action="store_true")
-    ap.add_argument("--no-latency", action="store_true")
-    ap.add_argument("--no-bert", action="store_true", help="skip the BERT-base seq/s measurement")
-    ap.add_argument("--strategy", default="naive", choices=["greedy_by_size", "first_fit", "naive"],
-                    help="the reference planner's memory strategy for the benchmark model; naive gives every "
-                         "buffer its own memory (11.7 GB arena at batch 256), which lets run() upload the image in "
-                         "slices that overlap the stem and layer1")
+    ap.add_argument("--no-extras", action="store_true", help="only the headline line: no other configs or modes")
+    ap.add_argument("--strategy", default="greedy_by_size", choices=["greedy_by_size", "first_fit", "naive"],
+                    help="the reference planner's memory strategy for the headline model (its default, "
+                         "greedy_by_size, as the cuda target's north star asks; the naive plan is measured beside it)")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
     if args.impl == "reference":
@@ -312,41 +412,14 @@ def main() -> None:
     flops, nbytes = algorithmic_cost(g)
     model = compile_graph(g, precision=args.precision, device=local, strategy=args.strategy)
     x = np.random.default_rng(4 + rank).standard_normal((args.batch, 3, 224, 224)).astype(np.float32)
-    # resident input for the device-timed loop
-    model.run({"image": x})
-    stream = torch.cuda.ExternalStream(model.stream)
+    model.run({"image": x})  # resident input for the device-timed loop
+    clocks = Clocks(local)
+    ms_per_step = device_ms(model, args.steps, args.warmup, group, clocks)
+    value = world * args.batch / (ms_per_step / 1e3)
+    e2e_step, h2d, d2h = e2e_s(model, {"image": x}, args.steps, group)
+    e2e = world * args.batch / e2e_step
 
-    barrier = group.barrier
-
-    for _ in range(args.warmup):
-        model.run_device(sync=False)
-    barrier()
-    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    with Clocks(local) as clocks:
-        start.record(stream)
-        for _ in range(args.steps):
-            model.run_device(sync=False)
-        end.record(stream)
-        end.synchronize()
-    barrier()
-    ms = group.max(start.elapsed_time(end))
-    ms_per_step = ms / args.steps
-    value = world * args.batch * args.steps / (ms / 1e3)
-
-    # end to end through the public API, pinned host buffers
-    pinned_in = torch.empty((args.batch, 3, 224, 224), dtype=torch.float32, pin_memory=True).numpy()
-    pinned_in[...] = x
-    pinned_out = torch.empty((args.batch, 1000), dtype=torch.float32, pin_memory=True).numpy()
-    for _ in range(2):
-        model.run({"image": pinned_in}, out={"logits": pinned_out})
-    barrier()
-    t0 = time.perf_counter()
-    for _ in range(args.steps):
-        model.run({"image": pinned_in}, out={"logits": pinned_out})
-    e2e_s = group.max(time.perf_counter() - t0)
-    e2e = world * args.batch * args.steps / e2e_s
-
-    # dominant kernel: per-launch CUDA events (eager pass), GEMM-family nodes
+    # dominant kernel family: per-launch CUDA events (eager pass), GEMM-family nodes
     prof_runs = 3
     per_node = [0.0] * len(g.nodes)
     for _ in range(prof_runs):
@@ -355,78 +428,101 @@ def main() -> None:
     gemm_nodes = [i for i, n in enumerate(g.nodes) if n.op in ("FusedConv", "FusedGemm", "Conv", "Gemm", "MatMul")]
     gemm_s = sum(per_node[i] for i in gemm_nodes)
     gemm_flops = sum(ops.flops(g.nodes[i]) for i in gemm_nodes)
-    launches = sum(1 for r in model.lowered.launches if r.kind == 1)
+    paths = model.gemm_paths()
     tf32_peak = pk["bf16_tflops"] / 2.0
     achieved = gemm_flops / gemm_s / 1e12 if gemm_s > 0 else 0.0
     step_bound_s = max(flops / (tf32_peak * 1e12), nbytes / (pk["hbm_gbs"] * 1e9))
     total_prof = sum(per_node)
+    traffic, traffic_src = measured_traffic(args.batch)
 
     line: dict = {
         "metric": METRIC, "value": round(value, 2), "unit": UNIT, "n_gpus": world, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": round(ms_per_step, 4), "higher_is_better": True,
         "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
-        "config": {
-            "workload": f"resnet50 v1.5 O3, batch {args.batch} per GPU, CUDA Graph replay",
-            "batch_per_gpu": args.batch, "precision": args.precision, "parallelism": f"replicas x{world}",
-            "l2": "inputs larger than L2 (input 154 MB, activations 1.8 GB per step)",
-            "flops_per_step_per_gpu": flops, "algorithmic_bytes_per_step_per_gpu": nbytes,
+        "config": headline_config(args.batch, world),
+        "details": {
+            "precision": args.precision,
             "memory_plan": f"{args.strategy} ({model.lowered.arena_bytes / 1e9:.2f} GB arena)",
-            "upload_slices": model.slices,
+            "upload_slices": model.slices, "flops_per_step_per_gpu": flops,
+            "algorithmic_bytes_per_step_per_gpu": nbytes,
+            "gemm_records": {"tcgen05": sum(1 for p in paths if p[3] == "tcgen05"),
+                             "simt": sum(1 for p in paths if p[3] == "simt")},
         },
-        "e2e": {"value": round(e2e, 2), "unit": UNIT, "h2d_bytes_per_step": int(pinned_in.nbytes),
-                "d2h_bytes_per_step": int(pinned_out.nbytes)},
+        "e2e": {"value": round(e2e, 2), "unit": UNIT, "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h},
         "gpu_launches": model.launch_count * args.steps,
         "roofline": {
             "bound": "tensor", "achieved": round(achieved, 3), "peak": round(tf32_peak, 1), "unit": "TFLOP/s",
-            "frac": round(achieved / tf32_peak, 4), "traffic": measured_traffic(args.batch),
-            "traffic_note": "DRAM read+write bytes of the 54 GEMM launches of one step (ncu, batch 32, "
-                            "scaled by the batch; profiles/resnet50_step_launches.md)",
-            "kernel": "implicit-GEMM conv/GEMM launches (54 per step)",
-            "peak_note": f"dense TF32 = half the {pk['source']} bf16 cuBLAS rate",
+            "frac": round(achieved / tf32_peak, 4),
+            "traffic": traffic,
+            "traffic_note": f"DRAM read + write bytes of one step's GEMM launches, the unit `achieved` is "
+                            f"measured over ({traffic_src}; profiles/resnet50_b256_gemm_traffic.md)",
+            "kernel": "implicit-GEMM conv/GEMM launches (umma_gemm_kernel forms)",
+            "peak_note": f"dense TF32 = half the {pk['source']} bf16 cuBLAS burst rate (of {pk['source']})",
             "gemm_share_of_step": round(gemm_s / total_prof, 4) if total_prof else None,
-            "gemm_launches": launches,
+            "gemm_launches": len(gemm_nodes),
         },
         "step_roofline": {"bound_ms": round(step_bound_s * 1e3, 4), "frac": round(step_bound_s * 1e3 / ms_per_step, 4),
                           "note": "max(FLOPs / TF32 peak, algorithmic bytes / HBM peak) / measured step"},
         "clocks": clocks.summary(),
     }
     model.close()
+    del model
 
-    if rank == 0 and world == 1 and not args.no_latency:
-        g1 = build_r50(1)
-        m1 = compile_graph(g1, precision=args.precision, device=local)
-        x1 = np.random.default_rng(0).standard_normal((1, 3, 224, 224)).astype(np.float32)
-        for _ in range(10):
-            m1.run({"image": x1})
-        ts = []
-        for _ in range(100):
-            t0 = time.perf_counter()
-            m1.run({"image": x1})
-            ts.append(time.perf_counter() - t0)
-        s1 = torch.cuda.ExternalStream(m1.stream)
-        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        dts = []
-        for _ in range(50):
-            e0.record(s1)
-            m1.run_device(sync=False)
-            e1.record(s1)
-            e1.synchronize()
-            dts.append(e0.elapsed_time(e1))
-        line["latency_b1"] = {"p50_ms": round(statistics.median(ts) * 1e3, 4),
-                              "device_p50_ms": round(statistics.median(dts), 4), "unit": "ms"}
-        m1.close()
+    # BASELINE config 4 as a fixed total batch sharded over the GPUs (strong scaling): every rank
+    # runs total / N images per step
+    fixed: dict = {}
+    for total in (256, 1024):
+        if total % world:
+            continue
+        if total == args.batch * world and args.strategy == "greedy_by_size":
+            fixed[f"b{total}"] = {"value": round(value, 2), "ms_per_step": round(ms_per_step, 4), "per_gpu": args.batch,
+                                  "e2e": line["e2e"]["value"]}
+            continue
+        r = measure("resnet50", {"batch": total // world, "seed": 0}, total // world, UNIT, args.precision, local,
+                    min(args.steps, 20), 3, seed=4 + rank, e2e=True, group=group)
+        fixed[f"b{total}"] = {"value": r["value"], "ms_per_step": r["ms_per_step"], "per_gpu": total // world,
+                              "e2e": r["e2e"]["value"]}
+    line["fixed_total_batch"] = {**fixed, "unit": UNIT, "scaling": "strong",
+                                 "note": "whole-job img/s with the total batch split over the GPUs"}
 
-    if rank == 0 and world == 1 and not args.no_bert:
-        line["bert"] = bert_throughput(args.precision, local, steps=20, warmup=3)
+    extras = rank == 0 and world == 1 and not args.no_extras
+    if extras:
+        steps = min(args.steps, 20)
+        other = "naive" if args.strategy != "naive" else "greedy_by_size"
+        r = measure("resnet50", {"batch": args.batch, "seed": 0}, args.batch, UNIT, args.precision, local, steps, 3,
+                    strategy=other, seed=4)
+        line[f"{other}_plan"] = r
+        line["strict"] = {
+            "resnet50_b256": measure("resnet50", {"batch": 256, "seed": 0}, 256, UNIT, "strict", local, steps, 3,
+                                     seed=4, e2e=False),
+            "latency_b1": latency("resnet50", {"batch": 1, "seed": 0}, "strict", local, 0),
+            "bert_b32": measure("bert", {"batch": 32, "seq": 128, "seed": 2}, 32, "seq/s", "strict", local, steps, 3,
+                                strategy="naive", seed=2, e2e=False),
+        }
+        line["latency_b1"] = latency("resnet50", {"batch": 1, "seed": 0}, args.precision, local, 0)
+        line["configs"] = {
+            "mobilenet_v2_b1": latency("mobilenet_v2", {"batch": 1, "seed": 1}, args.precision, local, 1),
+            "mobilenet_v2_b128": measure("mobilenet_v2", {"batch": 128, "seed": 1}, 128, UNIT, args.precision, local,
+                                         steps, 3, seed=1),
+            "bert_b1": measure("bert", {"batch": 1, "seq": 128, "seed": 2}, 1, "seq/s", args.precision, local, steps,
+                               3, seed=2),
+            "bert_b32": measure("bert", {"batch": 32, "seq": 128, "seed": 2}, 32, "seq/s", args.precision, local, steps,
+                                3, strategy="naive", seed=2),
+            "gpt2_b1": latency("gpt2", {"batch": 1, "seq": 128, "seed": 3}, args.precision, local, 3),
+            "gpt2_b16": measure("gpt2", {"batch": 16, "seq": 128, "seed": 3}, 16, "seq/s", args.precision, local,
+                                steps, 3, seed=3),
+        }
+        line["bert"] = {"metric": "BERT-base seq128 seq/s (batch 32, O3 graph)", **line["configs"]["bert_b32"]}
 
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         try:
-            r = cpu_reference_run(args.cpu_batch, 5, 1)
-            line["cpu_baseline"] = {"value": round(r["value"], 3), "unit": UNIT, "cores": r["cores"], "kind": "reference",
-                                    "sample": f"reference C backend (gcc+OpenMP), ResNet-50 O3 batch {args.cpu_batch}, "
-                                              "p50 of 5 runs"}
+            r = cpu_reference_run(args.cpu_batch, 3, 1)
+            line["cpu_baseline"] = {
+                "value": round(r["value"], 3), "unit": UNIT, "cores": r["cores"], "kind": "reference",
+                "sample": f"reference C backend (gcc + OpenMP), ResNet-50 O3 batch {args.cpu_batch} of the "
+                          f"{args.batch}-image workload, p50 of 3 runs", "cpu": cpu_model()}
         except Exception as exc:
-            line["cpu_baseline"] = {"value": None, "unit": UNIT, "cores": os.cpu_count(), "kind": "reference",
+            line["cpu_baseline"] = {"value": None, "unit": UNIT, "cores": host_threads(), "kind": "reference",
                                     "sample": f"failed: {type(exc).__name__}: {exc}"[:200]}
     if rank == 0:
         print(json.dumps(line))
