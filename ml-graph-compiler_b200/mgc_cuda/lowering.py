@@ -19,7 +19,7 @@ launch kind is written at its ``_emit_*`` function and read by ``csrc/launch.cuh
 from __future__ import annotations
 
 import ctypes
-import hashlib
+import math
 import struct
 from collections.abc import Sequence
 from dataclasses import dataclass, field
@@ -29,7 +29,7 @@ import numpy as np
 
 from mgc_cuda import _reference  # noqa: F401
 from ml_graph_compiler import ops
-from ml_graph_compiler.codegen.c import CEmitter
+from ml_graph_compiler.codegen.c import CEmitter, WeightsBuilder
 from ml_graph_compiler.errors import CodegenError
 from ml_graph_compiler.ir import Graph, Node, TensorType, Value
 from ml_graph_compiler.memory import ALIAS_OPS, MemoryPlan, Strategy, plan_memory
@@ -123,42 +123,15 @@ def tf32_split(a: np.ndarray) -> tuple[np.ndarray, np.ndarray]:
     return hi, lo
 
 
-@dataclass
-class Blob:
-    """Constants in one device blob with 256-byte aligned chunks (TMA needs 16, we keep lines)."""
-
-    chunks: list[tuple[int, np.ndarray]] = field(default_factory=list)
-    size: int = 0
-    by_key: dict[Any, int] = field(default_factory=dict)
+class Blob(WeightsBuilder):
+    """The constant blob: the reference's ``WeightsBuilder`` (c.py:166-218: chunks kept as
+    references, keyed de-duplication, ``digest``, ``blob``) with every chunk starting on a
+    256-byte boundary instead of 64 (TMA needs 16; whole 256-byte lines for the weight panels)."""
 
     def add(self, array: np.ndarray, key: Any = None) -> int:
-        if key is not None and key in self.by_key:
-            return self.by_key[key]
-        data = np.ascontiguousarray(array)
-        offset = self.size
-        self.chunks.append((offset, data))
-        self.size += data.nbytes
-        self.size += (-self.size) % BLOB_ALIGN
-        if key is not None:
-            self.by_key[key] = offset
+        offset = super().add(array, key)
+        self.size = -(-self.size // BLOB_ALIGN) * BLOB_ALIGN
         return offset
-
-    @property
-    def nbytes(self) -> int:
-        return max(self.size, BLOB_ALIGN)
-
-    def tobytes_array(self) -> np.ndarray:
-        out = np.zeros(self.nbytes, np.uint8)
-        for offset, data in self.chunks:
-            out[offset : offset + data.nbytes] = data.reshape(-1).view(np.uint8)
-        return out
-
-    def digest(self) -> str:
-        h = hashlib.blake2b(digest_size=12)
-        for offset, data in self.chunks:
-            h.update(offset.to_bytes(8, "little"))
-            h.update(memoryview(data.reshape(-1).view(np.uint8)))
-        return h.hexdigest()
 
 
 @dataclass
@@ -197,21 +170,88 @@ def _broadcast_strides(shape: Sequence[int], out_shape: Sequence[int]) -> list[i
 
 
 def _collapse(dims: list[int], strides: list[list[int]]) -> tuple[list[int], list[list[int]]]:
-    """Drop size-1 dimensions and merge neighbours that are contiguous for every operand (the
-    collapsing of ``CEmitter.loops``, c.py:360-379)."""
-    keep = [i for i, d in enumerate(dims) if d != 1]
-    dims = [dims[i] for i in keep]
-    strides = [[s[i] for i in keep] for s in strides]
-    d = len(dims) - 1
-    while d > 0:
-        if all(s[d - 1] == s[d] * dims[d] for s in strides):
-            dims[d - 1] *= dims[d]
-            del dims[d]
-            for s in strides:
-                s[d - 1] = s[d]
-                del s[d]
-        d -= 1
-    return dims, strides
+    """Fewest loop dimensions for a nest over ``dims`` that addresses every operand through
+    ``strides``: size-1 axes are dropped, and an axis joins the group before it when, for every
+    operand, stepping the group once equals stepping this axis across its whole extent (the loop
+    nests of ``CEmitter.loops``, c.py:360-379, collapse the same way)."""
+    out_dims: list[int] = []
+    out_strides: list[list[int]] = [[] for _ in strides]
+    for axis, extent in enumerate(dims):
+        if extent == 1:
+            continue
+        joins = bool(out_dims) and all(o[-1] == s[axis] * extent for o, s in zip(out_strides, strides))
+        if joins:
+            out_dims[-1] *= extent
+        else:
+            out_dims.append(extent)
+        for o, s in zip(out_strides, strides):
+            if joins:
+                o[-1] = s[axis]
+            else:
+                o.append(s[axis])
+    return out_dims, out_strides
+
+
+def _split_at(shape: Sequence[int], first: int, last: int | None = None) -> tuple[int, int, int]:
+    """(outer, n, inner): the products of the extents before axis ``first``, of axes first..last
+    and after ``last`` -- how a reduction, softmax, argmax or gather walks a row-major tensor."""
+    last = first if last is None else last
+    sizes = [int(d) for d in shape]
+    return math.prod(sizes[:first]), math.prod(sizes[first : last + 1]), math.prod(sizes[last + 1 :])
+
+
+def _axis_attr(node: Node, rank: int, default: int) -> int:
+    """The node's ``axis`` attribute made non-negative."""
+    axis = int(node.attrs.get("axis", default))
+    return axis % rank if rank and axis < 0 else axis
+
+
+@dataclass(frozen=True)
+class ConvShape:
+    """Geometry of a Conv / FusedConv node in its own layout: the image is x [N,H,W,C] with HWIO
+    weights after the layout pass (NHWC), else x [N,C,H,W] with OIHW weights."""
+
+    nhwc: bool
+    n: int
+    h: int
+    w: int
+    c: int
+    kh: int
+    kw: int
+    cg: int      # input channels per group
+    cout: int
+    group: int
+    win: Any     # ops.window_geometry: strides, dilations, pads, out_hw
+
+    @property
+    def pointwise(self) -> bool:
+        return self.kh == self.kw == 1 and self.win.strides == (1, 1) and self.win.pads == (0, 0, 0, 0)
+
+    def geo(self) -> dict[str, int]:
+        """The K_GEMM / K_IM2COL convolution slots."""
+        (sh, sw), (dh, dw), (pt, pl, _, _), (oh, ow) = self.win.strides, self.win.dilations, self.win.pads, self.win.out_hw
+        return {"H": self.h, "W": self.w, "C": self.c, "KH": self.kh, "KW": self.kw, "SH": sh, "SW": sw, "DH": dh,
+                "DW": dw, "PT": pt, "PL": pl, "OH": oh, "OW": ow}
+
+
+# positions of (n, h, w, c) in the image shape and of (kh, kw, cin, cout) in the weight shape
+_CONV_AXES = {True: ((0, 1, 2, 3), (0, 1, 2, 3)), False: ((0, 2, 3, 1), (2, 3, 1, 0))}
+
+
+def conv_shape(node: Node) -> ConvShape:
+    nhwc = ops.conv_layout(node) == "NHWC"
+    x_axes, w_axes = _CONV_AXES[nhwc]
+    xs, ws = node.input(0).tensor_type.shape, node.input(1).tensor_type.shape
+    n, h, w, c = (int(xs[a]) for a in x_axes)
+    kh, kw, cg, cout = (int(ws[a]) for a in w_axes)
+    return ConvShape(nhwc, n, h, w, c, kh, kw, cg, cout, int(node.attrs.get("group", 1)),
+                     ops.window_geometry(node, (h, w), (kh, kw)))
+
+
+def _oriented(shape: Sequence[int], transposed: int) -> tuple[int, int]:
+    """(rows, cols) of a 2-D operand as the product reads it."""
+    rows, cols = int(shape[0]), int(shape[1])
+    return (cols, rows) if transposed else (rows, cols)
 
 
 def _bits(value: float) -> int:
@@ -348,6 +388,9 @@ class CudaEmitter:
                     self.kernels["elementwise into softmax"] = self.kernels.get("elementwise into softmax", 0) + 1
                     return
             self._elementwise(node.output, program, list(node.inputs))
+            return
+        if node.op in self.REDUCE_KINDS:
+            self._reduce(node)
             return
         handler = getattr(self, f"op_{node.op}", None)
         if handler is None:
@@ -830,63 +873,45 @@ class CudaEmitter:
         dtype, i[5] element bytes; r[0] data, r[1] indices, r[2] out."""
         x, idx = node.input(0), node.input(1)
         xt, it = x.tensor_type, idx.tensor_type
-        axis = int(node.attrs.get("axis", 0))
-        axis = axis + xt.rank if axis < 0 else axis
-        outer = int(np.prod(xt.shape[:axis])) if axis else 1
-        inner = int(np.prod(xt.shape[axis + 1 :])) if axis + 1 < xt.rank else 1
+        axis = _axis_attr(node, xt.rank, 0)
+        outer, extent, inner = _split_at(xt.shape, axis)
         if it.dtype not in ("int64", "int32"):
             raise CodegenError(f"Gather indices of type {it.dtype} have no cuda kernel")
         if xt.itemsize not in (1, 4, 8):
             raise CodegenError(f"Gather of {xt.dtype} has no cuda kernel")
-        self.emit(K_GATHER, [outer, xt.shape[axis], inner, it.size, DTYPES[it.dtype], xt.itemsize],
+        self.emit(K_GATHER, [outer, extent, inner, it.size, DTYPES[it.dtype], xt.itemsize],
                   refs=[self.ref(x), self.ref(idx), self.ref(node.output)], dtype=DTYPES[xt.dtype])
 
     # -- reductions (c.py:736-821, 1255-1273) -------------------------------------------------------
-    def _reduce(self, node: Node, kind: str) -> None:
+    # K_REDUCE kind codes; the fp32 kinds the row-reduction kernel (K_REDUCE_MID) serves, with its
+    # is_max flag
+    REDUCE_KINDS = {"ReduceSum": 0, "ReduceMean": 1, "ReduceProd": 2, "ReduceMax": 3, "ReduceMin": 4}
+    REDUCE_MID = {"ReduceMean": 0, "ReduceMax": 1}
+
+    def _reduce(self, node: Node) -> None:
         """K_REDUCE_MID slots: i[0] is_max, i[1] outer, i[2] n, i[3] inner; r[0] x, r[1] y.
         K_REDUCE slots: i[0] kind (sum, mean, prod, max, min), i[1] outer, i[2] n, i[3] inner."""
-        x = node.input(0)
+        x, out = node.input(0), node.output
         xt = x.tensor_type
-        axes = ops.reduce_axes(node, xt.rank, self._consts(node))
-        out = node.output
-        if not axes:
+        axes = list(ops.reduce_axes(node, xt.rank, self._consts(node)))
+        if not axes:  # nothing reduced: a copy
             self._copy_value(xt.shape, x, self.ref(out), _strides(xt.shape), 0)
             return
-        if list(axes) != list(range(axes[0], axes[-1] + 1)):
+        if axes != list(range(axes[0], axes[0] + len(axes))):
             raise CodegenError(f"{node.op} over non-adjacent axes {axes} has no cuda kernel")
-        outer = int(np.prod(xt.shape[: axes[0]])) if axes[0] else 1
-        n = int(np.prod([xt.shape[a] for a in axes]))
-        inner = int(np.prod(xt.shape[axes[-1] + 1 :])) if axes[-1] + 1 < xt.rank else 1
-        if kind in ("mean", "max") and xt.dtype == "float32":
-            self.emit(K_REDUCE_MID, [int(kind == "max"), outer, n, inner], refs=[self.ref(x), self.ref(out)])
-            return
-        code = {"sum": 0, "mean": 1, "prod": 2, "max": 3, "min": 4}[kind]
-        self.emit(K_REDUCE, [code, outer, n, inner], refs=[self.ref(x), self.ref(out)], dtype=DTYPES[xt.dtype])
-
-    def op_ReduceMean(self, node: Node) -> None:
-        self._reduce(node, "mean")
-
-    def op_ReduceSum(self, node: Node) -> None:
-        self._reduce(node, "sum")
-
-    def op_ReduceMax(self, node: Node) -> None:
-        self._reduce(node, "max")
-
-    def op_ReduceMin(self, node: Node) -> None:
-        self._reduce(node, "min")
-
-    def op_ReduceProd(self, node: Node) -> None:
-        self._reduce(node, "prod")
+        outer, n, inner = _split_at(xt.shape, axes[0], axes[-1])
+        refs = [self.ref(x), self.ref(out)]
+        if xt.dtype == "float32" and node.op in self.REDUCE_MID:
+            self.emit(K_REDUCE_MID, [self.REDUCE_MID[node.op], outer, n, inner], refs=refs)
+        else:
+            self.emit(K_REDUCE, [self.REDUCE_KINDS[node.op], outer, n, inner], refs=refs, dtype=DTYPES[xt.dtype])
 
     def op_ArgMax(self, node: Node) -> None:
         """K_ARGMAX slots: i[0] outer, i[1] n, i[2] inner; dtype of x; r[0] x, r[1] y (int64)."""
         x = node.input(0)
         xt = x.tensor_type
-        axis = int(node.attrs.get("axis", 0))
-        axis = axis + xt.rank if axis < 0 else axis
-        outer = int(np.prod(xt.shape[:axis])) if axis else 1
-        inner = int(np.prod(xt.shape[axis + 1 :])) if axis + 1 < xt.rank else 1
-        self.emit(K_ARGMAX, [outer, xt.shape[axis], inner], refs=[self.ref(x), self.ref(node.output)],
+        outer, n, inner = _split_at(xt.shape, _axis_attr(node, xt.rank, 0))
+        self.emit(K_ARGMAX, [outer, n, inner], refs=[self.ref(x), self.ref(node.output)],
                   dtype=DTYPES[xt.dtype], count="reduce")
 
     def _global_pool(self, node: Node, is_max: int) -> None:
@@ -916,12 +941,9 @@ class CudaEmitter:
         x = node.input(0)
         xt = x.tensor_type
         self._require_f32(node, xt)
-        axis = int(node.attrs.get("axis", -1))
-        axis = axis + xt.rank if axis < 0 else axis
-        outer = int(np.prod(xt.shape[:axis])) if axis else 1
-        inner = int(np.prod(xt.shape[axis + 1 :])) if axis + 1 < xt.rank else 1
+        outer, n, inner = _split_at(xt.shape, _axis_attr(node, xt.rank, -1))
         program = self._row_programs.pop(id(x), None)
-        self.emit(K_SOFTMAX, [outer, xt.shape[axis], inner, log, 0 if program is None else 1],
+        self.emit(K_SOFTMAX, [outer, n, inner, log, 0 if program is None else 1],
                   refs=[self.ref(x), self.ref(node.output)], aux=program)
 
     def op_Softmax(self, node: Node) -> None:
@@ -944,35 +966,34 @@ class CudaEmitter:
         x = node.input(0)
         xt = x.tensor_type
         self._require_f32(node, xt)
-        axis = int(node.attrs.get("axis", -1))
-        axis = axis + xt.rank if axis < 0 else axis
-        cols = int(np.prod(xt.shape[axis:]))
-        rows = xt.size // max(cols, 1)
+        axis = _axis_attr(node, xt.rank, -1)
+        rows, cols, _ = _split_at(xt.shape, axis, xt.rank - 1)
         scale = self._vector_ref(node.optional_input(1), cols, "LayerNormalization scale")
         bias = self._vector_ref(node.optional_input(2), cols, "LayerNormalization bias")
         self.emit(K_LAYER_NORM, [rows, cols], [float(node.attrs.get("epsilon", 1e-5))],
                   refs=[self.ref(x), scale, bias, self.ref(node.output)])
 
     def op_BatchNormalization(self, node: Node) -> None:
+        """Inference BatchNormalization as the two-instruction program ``x * mul + add`` with
+        mul = gamma / sqrt(var + eps) and add = beta - mean * mul per channel (the channel axis is
+        the last one after the layout pass, else axis 1)."""
         x = node.input(0)
         xt = x.tensor_type
         self._require_f32(node, xt)
-        params = [v.data if v is not None else None for v in node.inputs[1:5]]
-        if any(p is None for p in params):
+        consts = [v.data if v is not None else None for v in node.inputs[1:5]]
+        if any(c is None for c in consts):
             raise CodegenError("BatchNormalization parameters must be constants")
-        scale, bias, mean, var = (np.asarray(p, np.float64) for p in params)
-        inv = scale / np.sqrt(var + float(node.attrs.get("epsilon", 1e-5)))
-        shift = bias - mean * inv
-        c = inv.size
-        nhwc = node.attrs.get("layout") == "NHWC"
-        bshape = (c,) if nhwc else (c,) + (1,) * (xt.rank - 2)
-        # x * inv + shift as a two-instruction program; the folded constants are free-standing
-        # Values (Location "const"), kept alive here because blob keys use id()
+        gamma, beta, mean, var = (np.asarray(c, np.float64).reshape(-1) for c in consts)
+        inv_std = 1.0 / np.sqrt(var + float(node.attrs.get("epsilon", 1e-5)))
+        mul = gamma * inv_std
+        add = beta - mean * mul
+        channel_shape = (mul.size,) if node.attrs.get("layout") == "NHWC" else (mul.size,) + (1,) * (xt.rank - 2)
+        # free-standing constant Values (Location "const"), kept alive because blob keys use id()
         g = Graph("bn")
-        mul = g.constant(inv.astype(np.float32).reshape(bshape), "bn_inv")
-        add = g.constant(shift.astype(np.float32).reshape(bshape), "bn_shift")
-        self._keep_alive += [mul, add]
-        self._elementwise(node.output, [("Mul", {}, [0, 1]), ("Add", {}, [3, 2])], [x, mul, add])
+        operands = [g.constant(v.astype(np.float32).reshape(channel_shape), f"bn_{tag}")
+                    for tag, v in (("mul", mul), ("add", add))]
+        self._keep_alive += operands
+        self._elementwise(node.output, [("Mul", {}, [0, 1]), ("Add", {}, [3, 2])], [x, *operands])
 
     # -- GEMM family (c.py:905-1226) ------------------------------------------------------------------
     def _prec(self) -> int:
@@ -1094,8 +1115,8 @@ class CudaEmitter:
         at, bt = a.tensor_type, b.tensor_type
         self._require_f32(node, at)
         trans = int(node.attrs.get("trans_b", 0))
-        k, n = (bt.shape[1], bt.shape[0]) if trans else bt.shape
-        m = at.size // max(k, 1)
+        k, n = _oriented(bt.shape, trans)
+        m = at.size // max(k, 1)  # every leading axis of A is a row (reshape lifting, fusion.py:364-387)
         if b.is_constant or self.plan.location(b).kind == "const":
             data = self.const_data(b)
             bref, blo, b_rs, b_cs = self._kmajor_b(data.T if trans else data, ("kmajor", id(self._root(b)), trans))
@@ -1113,8 +1134,8 @@ class CudaEmitter:
         at, bt = a.tensor_type, b.tensor_type
         self._require_f32(node, at)
         ta, tb = int(node.attrs.get("transA", 0)), int(node.attrs.get("transB", 0))
-        m, k = (at.shape[1], at.shape[0]) if ta else at.shape
-        n = bt.shape[0] if tb else bt.shape[1]
+        m, k = _oriented(at.shape, ta)
+        n = _oriented(bt.shape, tb)[1]
         alpha = float(node.attrs.get("alpha", 1.0))
         beta = float(node.attrs.get("beta", 1.0))
         a_rs, a_cs = (1, m) if ta else (k, 1)
@@ -1192,10 +1213,10 @@ class CudaEmitter:
         a, b = node.input(0), node.input(1)
         at, bt = a.tensor_type, b.tensor_type
         self._require_f32(node, at)
-        ashape = (1, *at.shape) if at.rank == 1 else at.shape
-        bshape = (*bt.shape, 1) if bt.rank == 1 else bt.shape
-        m, k = ashape[-2], ashape[-1]
-        n = bshape[-1]
+        # ONNX MatMul: a 1-D A is one row, a 1-D B one column; leading axes broadcast
+        ashape = tuple(at.shape) if at.rank > 1 else (1, *at.shape)
+        bshape = tuple(bt.shape) if bt.rank > 1 else (*bt.shape, 1)
+        (m, k), n = ashape[-2:], bshape[-1]
         batch_shape = [int(d) for d in np.broadcast_shapes(ashape[:-2], bshape[:-2])]
         aref, av = self._view(a) if at.rank >= 2 else (self.ref(a), [k, 1])
         if bt.rank == 1:
@@ -1289,39 +1310,30 @@ class CudaEmitter:
 
     def op_FusedConv(self, node: Node) -> None:
         x, w = node.input(0), node.input(1)
-        xt, wt = x.tensor_type, w.tensor_type
-        self._require_f32(node, xt)
-        nhwc = ops.conv_layout(node) == "NHWC"
-        group = int(node.attrs.get("group", 1))
-        if nhwc:
-            nb, h, wd, c = xt.shape
-            kh, kw, cg, kout = wt.shape
-        else:
-            nb, c, h, wd = xt.shape
-            kout, cg, kh, kw = wt.shape
-        g = ops.window_geometry(node, (h, wd), (kh, kw))
-        oh, ow = g.out_hw
-        pt, pl, _, _ = g.pads
-        bias_v, res_v = node.optional_input(2), node.optional_input(3)
-        act = self._act(node) if node.op == "FusedConv" else (0, 0.0, 6.0)
-        bias = self._vector_ref(bias_v, kout, "Conv bias")
-        res = self.ref(res_v)
+        self._require_f32(node, x.tensor_type)
+        cs = conv_shape(node)
         if not (w.is_constant or self.plan.location(w).kind == "const"):
             raise CodegenError("convolution weights must be constant for the cuda backend")
         wdata = self.const_data(w)
+        bias_v, res_v = node.optional_input(2), node.optional_input(3)
+        bias = self._vector_ref(bias_v, cs.cout, "Conv bias")
+        res = self.ref(res_v)
+        act = self._act(node) if node.op == "FusedConv" else (0, 0.0, 6.0)
+        geo = cs.geo()
+        nb, h, wd, c, kh, kw, cg, kout, group = cs.n, cs.h, cs.w, cs.c, cs.kh, cs.kw, cs.cg, cs.cout, cs.group
+        oh, ow = geo["OH"], geo["OW"]
+        nhwc = cs.nhwc
         if self._depthwise(node):
             # K_DEPTHWISE slots: i[0..13] N, H, W, C, KH, KW, SH, SW, DH, DW, PT, PL, OH, OW,
             # i[14] NHWC, i[15] activation; f[0..1] clip bounds; r[0] x, r[1] w, r[2] bias,
             # r[3] residual, r[4] y. Weights HWC (NHWC) or CHW (NCHW), as mgc_depthwise_*.
             wref = self.weights_ref(np.ascontiguousarray(wdata, np.float32), key=("raw", id(self._root(w))))
-            ints = [nb, h, wd, c, kh, kw, g.strides[0], g.strides[1], g.dilations[0], g.dilations[1],
-                    pt, pl, oh, ow, int(nhwc), act[0]]
+            ints = [nb, h, wd, c, kh, kw, geo["SH"], geo["SW"], geo["DH"], geo["DW"], geo["PT"], geo["PL"], oh, ow,
+                    int(nhwc), act[0]]
             self.emit(K_DEPTHWISE, ints, [act[1], act[2]], [self.ref(x), wref, bias, res, self.ref(node.output)])
             return
         kg = kout // group
-        geo = {"H": h, "W": wd, "C": c, "KH": kh, "KW": kw, "SH": g.strides[0], "SW": g.strides[1],
-               "DH": g.dilations[0], "DW": g.dilations[1], "PT": pt, "PL": pl, "OH": oh, "OW": ow}
-        pointwise = kh == kw == 1 and g.strides == (1, 1) and g.pads == (0, 0, 0, 0)
+        pointwise = cs.pointwise
         if self._tap_packed(node):
             self._conv_tap_packed(node, wdata, geo, nb, bias, res, act)
             return

@@ -133,7 +133,7 @@ class CudaCompiledModel:
         self.report = report
         self._lock = threading.Lock()
         self._handle = ctypes.c_void_p()
-        blob = lowered.weights.tobytes_array()
+        blob = lowered.weights.blob()
         launches = lowered.launch_array()
         ins = (ctypes.c_int64 * max(len(self.inputs), 1))(*[t.nbytes for _, t in self.inputs])
         outs = (ctypes.c_int64 * max(len(self.outputs), 1))(*[t.nbytes for _, t in self.outputs])
@@ -269,7 +269,7 @@ class CudaCompiledModel:
         arr = self.lowered.launch_array()
         (d / "launches.bin").write_bytes(bytes(memoryview(arr))[: ctypes.sizeof(Launch) * len(self.lowered.launches)])
         np.asarray(self.lowered.aux, np.int64).tofile(d / "aux.bin")
-        self.lowered.weights.tobytes_array().tofile(d / "weights.bin")
+        self.lowered.weights.blob().tofile(d / "weights.bin")
         meta = {
             "format": "mgc-cuda-1",
             "arena_bytes": self.lowered.arena_bytes,
