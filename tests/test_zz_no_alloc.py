@@ -85,7 +85,7 @@ def test_noalloc_conv_matches_the_allocating_entry_point_twice_in_a_row() -> Non
     # the first call of the process may load the module's device code; every later call allocates
     # and frees nothing, so the free device memory around it does not move
     assert free[2] == free[3], f"the second call changed free device memory: {free}"
-    geo, x, wt, bias, res = _conv_args(1, 64, 64, 3, 7, 2, 3, 64, 1, 1)
+    geo, x, wt, bias, res = _conv_args(1, 64, 64, 3, 7, 2, 3, 64, 1)
     more: list[int] = []
     for _ in range(3):
         _run("mgc_cuda_conv_nhwc_noalloc", geo, x, wt, bias, res, 1, more)
