@@ -64,14 +64,17 @@ constexpr long long WAIT_LIMIT_CYCLES = 1ll << 31;  // ~1.1 s at 1.9 GHz
 // plane, one accumulator, tiles batched over up to two batch dimensions of 4-D tensor maps.
 enum Mode { TF32 = 0, STRICT = 1, DYN = 2 };
 
-// Mean relative shrink toward zero of one kind::tf32 MMA step (eight exact TF32 products summed
-// into a fresh fp32 accumulator), measured on B200 with TF32-exact random operands: -2.4e-8 to
-// -2.6e-8. Strict mode keeps every K=8 step in its own TMEM region, so every output carries the
-// same factor (1 - STEP_BIAS); that is below half an fp32 ulp per value but compounds coherently
-// through deep networks (about 1e-4 on ResNet-50 logits). The strict epilogue therefore forms
-// alpha * acc * (1 + STEP_BIAS) + bias + residual in fp64 and rounds once, which makes the
-// rounding of each output unbiased in expectation.
-constexpr double STEP_BIAS = 2.5e-8;
+// The tensor core's fp32 accumulation rounds toward zero. Strict mode keeps every K = 8 step in
+// its own TMEM region, where three products land (A_lo*B_hi, A_hi*B_lo, A_hi*B_hi), so every
+// output carries about the same relative shrink per region; below half an fp32 ulp per value, it
+// compounds coherently through deep networks. Measured on B200 through this kernel with raw fp32
+// operands and K = 512 (mean relative shrink of the outputs before compensation): 4.3e-8
+// (uniform [0.5, 1.5)), 4.3e-8 (uniform [0, 1)), 4.1e-8 (half-normal), 5.0e-8 (uniform [1, 2));
+// with TF32-exact operands (one product per region) 2.5e-8 to 3.9e-8. Batch-1 strict logits
+// against the float64 oracle with this constant / with 2.5e-8 / without compensation: ResNet-50
+// 1.5e-5 / 3.1e-5 / 9.2e-5, the other benchmark models unchanged at <= 2.1e-6. The strict epilogue
+// forms alpha * acc * (1 + STEP_BIAS) + bias + residual in fp64 and rounds once.
+constexpr double STEP_BIAS = 4.3e-8;
 
 struct Params {
     CUtensorMap tmA;
@@ -1150,11 +1153,13 @@ __global__ void __launch_bounds__(THREADS, 1) umma_gemm_kernel(const __grid_cons
           if (MODE == STRICT) {
 #pragma unroll
             for (int j = 0; j < HALF; ++j) acc[j] = AccT(0);
-            for (int kb = 0; kb < num_kb && ok; ++kb) {
+            // this unit's K blocks (all of them unless split K)
+            const int klo = kb_lo(ks), khi = kb_hi(ks);
+            for (int kb = klo; kb < khi && ok; ++kb) {
                 if (!split_one()) ok = false;
-                else if (kb >= 1 && !drain()) ok = false;  // one block behind the split
+                else if (kb > klo && !drain()) ok = false;  // one block behind the split
             }
-            if (ok && num_kb >= 1 && !drain()) ok = false;
+            if (ok && khi > klo && !drain()) ok = false;
           }
           for (int h = 0; ok && h < NH; ++h, ++local) {
             const int n0 = nt * BN + h * EN;
@@ -1162,13 +1167,17 @@ __global__ void __launch_bounds__(THREADS, 1) umma_gemm_kernel(const __grid_cons
                 ok = false;
                 break;
             }
-            if (MODE == TF32 && !PAIR && !RB && NH == 1 && splits > 1) {
+            if ((MODE == TF32 || MODE == STRICT) && !PAIR && !RB && NH == 1 && splits > 1) {
                 // split K: this unit's raw partial tile (its row, this thread's columns); the
-                // reduce kernel that follows on the stream applies the epilogue
+                // reduce kernel that follows on the stream applies the epilogue. A strict partial
+                // is its fp64 sum with the step-bias compensation, rounded once to fp32.
                 float *mine = p.part + ((size_t)(mt * p.n_tiles + nt) * splits + ks) * (BM * BN) + (size_t)row * BN + hc;
+                constexpr double comp = MODE == STRICT ? 1.0 + STEP_BIAS : 1.0;
 #pragma unroll
                 for (int j = 0; j < HALF; j += 4)
-                    *reinterpret_cast<float4 *>(mine + j) = make_float4(acc[j], acc[j + 1], acc[j + 2], acc[j + 3]);
+                    *reinterpret_cast<float4 *>(mine + j) =
+                        make_float4((float)(comp * acc[j]), (float)(comp * acc[j + 1]), (float)(comp * acc[j + 2]),
+                                    (float)(comp * acc[j + 3]));
                 continue;
             }
             // this pass's bias columns into shared memory, one coalesced load (the previous
@@ -1864,7 +1873,8 @@ inline int try_gemm_umma(const GemmParams &p, cudaStream_t stream, int *taken) {
     // Split K when the tiles cover at most half the SMs and K is long (the late layers at batch
     // 1: a 3x3 C512 convolution is 4 tiles of 144 K blocks): K blocks in runs of at least 4, as
     // many runs as fill the SMs; the units leave raw partial tiles in the model's split scratch
-    // and split_reduce_kernel sums them and runs the epilogue. MGC_CUDA_SPLIT=0 never splits.
+    // and split_reduce_kernel sums them and runs the epilogue. Strict mode splits the same way
+    // (its partials are fp64 sums rounded once to fp32). MGC_CUDA_SPLIT=0 never splits.
     static const bool split_env = [] {
         const char *e = getenv("MGC_CUDA_SPLIT");
         return !(e && e[0] == '0');
@@ -1875,7 +1885,7 @@ inline int try_gemm_umma(const GemmParams &p, cudaStream_t stream, int *taken) {
         const int v = e ? atoi(e) : 4;
         return v >= 1 ? v : 4;
     }();
-    if (split_env && !strict && p.split_ws && (u.im2col == 0 || u.im2col == 1) && u.num_kb >= 2 * split_min_kb) {
+    if (split_env && p.split_ws && (u.im2col == 0 || u.im2col == 1) && u.num_kb >= 2 * split_min_kb) {
         const long long tiles = (long long)u.n_tiles * m_tiles;
         const int sms = sm_count();
         if (tiles * 2 <= sms) {
@@ -1892,8 +1902,9 @@ inline int try_gemm_umma(const GemmParams &p, cudaStream_t stream, int *taken) {
                 u.b_res_bytes = 0;
                 const long long units = tiles * splits;
                 const int grid = (int)(units < sms ? units : sms);
-                int st = bn == 64 ? umma::launch<64, umma::TF32, 0, 0, 0>(u, grid, stream)
-                                  : umma::launch<128, umma::TF32, 0, 0, 0>(u, grid, stream);
+                int st = strict ? umma::launch<64, umma::STRICT, 0, 0, 0>(u, grid, stream)
+                         : bn == 64 ? umma::launch<64, umma::TF32, 0, 0, 0>(u, grid, stream)
+                                    : umma::launch<128, umma::TF32, 0, 0, 0>(u, grid, stream);
                 if (st != MGC_CUDA_OK) return st;
                 const long long outs = (long long)p.M * p.N;
                 umma::split_reduce_kernel<<<grid_for(outs, 256), 256, 0, stream>>>(

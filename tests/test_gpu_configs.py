@@ -167,15 +167,15 @@ def test_strict_gemm_paths(name: str) -> None:
 
 
 def test_strict_step_bias_is_compensated() -> None:
-    """The strict epilogue multiplies every output by (1 + STEP_BIAS), STEP_BIAS = 2.5e-8, to
-    cancel the measured shrink toward zero of one kind::tf32 MMA step (each K = 8 step of strict
-    mode lands in its own TMEM region). This re-measures it: a strict GEMM with a constant B on
-    positive data, where every step shrinks its partial sum by the same relative amount, must be
-    unbiased after the compensation. The shrink implied by the result (STEP_BIAS minus the mean
-    signed relative error) must lie within 20 % of STEP_BIAS, so that a change of the tensor
-    core's accumulation (driver, firmware) shows here instead of silently shifting every strict
-    result."""
-    step_bias = 2.5e-8
+    """The strict epilogue multiplies every output by (1 + STEP_BIAS), STEP_BIAS = 4.3e-8, to
+    cancel the shrink toward zero of the tensor core's fp32 accumulation in one strict TMEM region
+    (one K = 8 step, three products). This re-measures it: a strict GEMM with a constant B on
+    positive raw fp32 data (uniform [0.5, 1.5), K = 512, the data the constant was measured on),
+    where every region shrinks its partial sum by the same relative amount, must be unbiased after
+    the compensation. The shrink implied by the result (STEP_BIAS minus the mean signed relative
+    error) must lie within 20 % of STEP_BIAS, so that a change of the tensor core's accumulation
+    (driver, firmware) shows here instead of silently shifting every strict result."""
+    step_bias = 4.3e-8
     m_, k_, n_ = 4096, 512, 512
     rng = np.random.default_rng(21)
     g = Graph("strict_bias")
