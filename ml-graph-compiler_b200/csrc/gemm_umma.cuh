@@ -1169,15 +1169,21 @@ __global__ void __launch_bounds__(THREADS, 1) umma_gemm_kernel(const __grid_cons
             }
             if ((MODE == TF32 || MODE == STRICT) && !PAIR && !RB && NH == 1 && splits > 1) {
                 // split K: this unit's raw partial tile (its row, this thread's columns); the
-                // reduce kernel that follows on the stream applies the epilogue. A strict partial
-                // is its fp64 sum with the step-bias compensation, rounded once to fp32.
-                float *mine = p.part + ((size_t)(mt * p.n_tiles + nt) * splits + ks) * (BM * BN) + (size_t)row * BN + hc;
-                constexpr double comp = MODE == STRICT ? 1.0 + STEP_BIAS : 1.0;
+                // reduce kernel that follows on the stream applies the epilogue. Strict partials are
+                // the fp64 sums themselves (the reduce finishes in fp64, as the tile epilogue does).
+                const size_t at = ((size_t)(mt * p.n_tiles + nt) * splits + ks) * (BM * BN) + (size_t)row * BN + hc;
+                if (MODE == STRICT) {
+                    double *mine = reinterpret_cast<double *>(p.part) + at;
 #pragma unroll
-                for (int j = 0; j < HALF; j += 4)
-                    *reinterpret_cast<float4 *>(mine + j) =
-                        make_float4((float)(comp * acc[j]), (float)(comp * acc[j + 1]), (float)(comp * acc[j + 2]),
-                                    (float)(comp * acc[j + 3]));
+                    for (int j = 0; j < HALF; j += 2)
+                        *reinterpret_cast<double2 *>(mine + j) = make_double2((double)acc[j], (double)acc[j + 1]);
+                } else {
+                    float *mine = p.part + at;
+#pragma unroll
+                    for (int j = 0; j < HALF; j += 4)
+                        *reinterpret_cast<float4 *>(mine + j) =
+                            make_float4((float)acc[j], (float)acc[j + 1], (float)acc[j + 2], (float)acc[j + 3]);
+                }
                 continue;
             }
             // this pass's bias columns into shared memory, one coalesced load (the previous
@@ -1345,6 +1351,28 @@ __global__ void __launch_bounds__(256) split_reduce_kernel(const float *part, in
         float x = alpha * acc + (bias ? bias[n] : 0.0f);
         if (res) x += res[(long long)m * ldr + n];
         c[(long long)m * ldc + n] = apply_act(x, act, lo, hi);
+    }
+}
+
+// Strict split K: the fp64 partials summed in split order in fp64, then the strict tile epilogue's
+// arithmetic: alpha * (1 + STEP_BIAS) * acc + bias (+ res) in fp64, rounded once, activation.
+__global__ void __launch_bounds__(256) split_reduce_f64_kernel(const double *part, int splits, int n_tiles, int bn,
+                                                               int M, int N, float *c, long long ldc, const float *bias,
+                                                               const float *res, long long ldr, float alpha, int act,
+                                                               float lo, float hi) {
+    const long long total = (long long)M * N;
+    const double sa = (double)alpha * (1.0 + STEP_BIAS);
+    for (long long e = (long long)blockIdx.x * blockDim.x + threadIdx.x; e < total;
+         e += (long long)gridDim.x * blockDim.x) {
+        const int m = (int)(e / N), n = (int)(e - (long long)m * N);
+        const int mt = m / BM, nt = n / bn;
+        const double *src = part + ((size_t)(mt * n_tiles + nt) * splits) * (BM * bn) + (size_t)(m - mt * BM) * bn + (n - nt * bn);
+        const size_t step = (size_t)BM * bn;
+        double acc = 0.0;
+        for (int ks = 0; ks < splits; ++ks) acc += __ldcg(src + (size_t)ks * step);
+        double x = sa * acc + (bias ? (double)bias[n] : 0.0);
+        if (res) x += (double)res[(long long)m * ldr + n];
+        c[(long long)m * ldc + n] = apply_act((float)x, act, lo, hi);
     }
 }
 
@@ -1873,8 +1901,8 @@ inline int try_gemm_umma(const GemmParams &p, cudaStream_t stream, int *taken) {
     // Split K when the tiles cover at most half the SMs and K is long (the late layers at batch
     // 1: a 3x3 C512 convolution is 4 tiles of 144 K blocks): K blocks in runs of at least 4, as
     // many runs as fill the SMs; the units leave raw partial tiles in the model's split scratch
-    // and split_reduce_kernel sums them and runs the epilogue. Strict mode splits the same way
-    // (its partials are fp64 sums rounded once to fp32). MGC_CUDA_SPLIT=0 never splits.
+    // and split_reduce_kernel sums them and runs the epilogue. Strict mode splits the same way with
+    // fp64 partials and an fp64 reduce (split_reduce_f64_kernel). MGC_CUDA_SPLIT=0 never splits.
     static const bool split_env = [] {
         const char *e = getenv("MGC_CUDA_SPLIT");
         return !(e && e[0] == '0');
@@ -1893,7 +1921,8 @@ inline int try_gemm_umma(const GemmParams &p, cudaStream_t stream, int *taken) {
             long long kb_per = ceil_div(u.num_kb, want);
             if (kb_per < split_min_kb) kb_per = split_min_kb;
             const long long splits = ceil_div(u.num_kb, kb_per);
-            if (splits > 1 && tiles * splits * umma::BM * bn <= p.split_ws_floats) {
+            // strict partials are fp64: twice the scratch
+            if (splits > 1 && (strict ? 2 : 1) * tiles * splits * umma::BM * bn <= p.split_ws_floats) {
                 u.splits = (int)splits;
                 u.kb_per = (int)kb_per;
                 u.part = p.split_ws;
@@ -1907,9 +1936,14 @@ inline int try_gemm_umma(const GemmParams &p, cudaStream_t stream, int *taken) {
                                     : umma::launch<128, umma::TF32, 0, 0, 0>(u, grid, stream);
                 if (st != MGC_CUDA_OK) return st;
                 const long long outs = (long long)p.M * p.N;
-                umma::split_reduce_kernel<<<grid_for(outs, 256), 256, 0, stream>>>(
-                    p.split_ws, (int)splits, u.n_tiles, bn, p.M, p.N, p.c, p.ldc, p.bias, p.res, p.ldr, p.alpha, p.act,
-                    p.lo, p.hi);
+                if (strict)
+                    umma::split_reduce_f64_kernel<<<grid_for(outs, 256), 256, 0, stream>>>(
+                        reinterpret_cast<const double *>(p.split_ws), (int)splits, u.n_tiles, bn, p.M, p.N, p.c, p.ldc,
+                        p.bias, p.res, p.ldr, p.alpha, p.act, p.lo, p.hi);
+                else
+                    umma::split_reduce_kernel<<<grid_for(outs, 256), 256, 0, stream>>>(
+                        p.split_ws, (int)splits, u.n_tiles, bn, p.M, p.N, p.c, p.ldc, p.bias, p.res, p.ldr, p.alpha,
+                        p.act, p.lo, p.hi);
                 st = check_launch("split_reduce_kernel");
                 if (st != MGC_CUDA_OK) return st;
                 *taken = 2;  // the split GEMM and its reduce

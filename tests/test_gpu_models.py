@@ -207,9 +207,13 @@ def test_profile_save_load_and_device_run(tmp_path) -> None:
 @pytest.mark.parametrize("strategy", ["greedy_by_size", "naive"])
 def test_sliced_upload_matches_one_pass(strategy: str, monkeypatch: pytest.MonkeyPatch) -> None:
     """run() with the input uploaded in four slices, the leading layers running slice by slice
-    as each lands, gives the one-pass graph's outputs bit for bit (strict mode: the kernels see
-    fewer rows per launch, each row computed the same way). The slice row threshold is lowered so
-    that the small model's convolutions join the prefix."""
+    as each lands, gives the one-pass graph's outputs (strict mode). A slice has fewer rows per
+    launch, so a GEMM may take the split-K form in one graph and not in the other; strict split K
+    sums fp64 partials, so the two differ at most by the rounding of a differently associated fp64
+    sum: the test allows 1e-6 of the largest logit, far below the strict budget (1e-4), and far
+    below what a slice reading or overwriting the wrong rows would cause. Repeated sliced runs
+    agree bit for bit. The slice row threshold is lowered so that the small model's convolutions
+    join the prefix."""
     from mgc_cuda import lowering
 
     g = zoo.resnet50(batch=8)
@@ -230,5 +234,6 @@ def test_sliced_upload_matches_one_pass(strategy: str, monkeypatch: pytest.Monke
         again = sliced.run({"image": x})["logits"]
     finally:
         sliced.close()
-    np.testing.assert_array_equal(got, want)
-    np.testing.assert_array_equal(again, want)
+    np.testing.assert_array_equal(again, got)
+    scale = float(np.abs(want).max())
+    assert float(np.abs(got.astype(np.float64) - want).max()) <= 1e-6 * scale
