@@ -42,6 +42,10 @@ struct GemmParams {
     // window-row layout of an im2col convolution over a spatially padded image: output pixels per
     // TMA box (0: not used) and the padded length of one window row (B is [N][KH][win_L])
     int win_rows, win_L;
+    // phase-split rows (narrow stride-2 convolutions, TF32): A is a packed image whose rows hold
+    // the even-tap and the odd-tap column phases of `phase_w` 4-channel pixels each (K_PACK with
+    // phases); B is [N][KH][32] in the matching tap order. 0: not used
+    int phase_w;
     int *err;                     // device word for bounded-wait timeouts (may be NULL)
     // split-K scratch of the model (NULL: no split): room for the partial tiles
     float *split_ws;

@@ -83,12 +83,17 @@ struct Params {
     CUtensorMap tmR;                 // residual tile load (when tma_res)
     int tma_out, tma_res;
     int M, N, num_kb, n_tiles;
-    int im2col;                      // 0 tiled A, 1 im2col (32-channel blocks), 2 tap-packed im2col
+    int im2col;                      // 0 tiled A, 1 im2col (32-channel blocks), 2 tap-packed im2col,
+                                     // 3 window rows, 4 row tiles, 5 phase-split row tiles
     int KW, DH, DW, cblocks;         // im2col: K block kb -> (kh, kw, channel block)
     int cpix, kreal;                 // tap-packed: channels per pixel (4..28), real K = KH*KW*cpix
     int wrows;                       // window rows (im2col 3): output pixels per box (divides OW)
-    int rt_rows, rt_per_img;         // row tiles (im2col 4): output rows per tile, tiles per image
+    int rt_rows, rt_per_img;         // row tiles (im2col 4, 5): output rows per tile, tiles per image
+    const char *a_rows;              // phase-split row tiles (im2col 5): the packed image's first row
+    long long prow_bytes;            // bytes of one packed row (both phases)
+    int prows, phase_bytes;          // packed rows per image; bytes of one phase of a row
     uint32_t a_bytes;                // bytes of one K block's A boxes (row tiles fill rt_rows*OW rows)
+    uint32_t res_box_bytes;          // row tiles: bytes of one 32-column residual box (rt_rows*OW rows)
     int m_tiles;                     // ceil(M / 128) (DYN: times the batches)
     int m_per_batch, nbatch1;        // DYN: M tiles per batch; extent of the first batch dimension
     uint32_t b_res_bytes;            // B-resident kernels: bytes of this CTA's whole B panel
@@ -262,6 +267,15 @@ __device__ __forceinline__ void tma_load_im2col_4d_pair(void *dst, const CUtenso
         " [%0], [%1, {%3, %4, %5, %6}], [%2], {%7, %8};"
         ::"r"(smem_addr(dst)), "l"(reinterpret_cast<uint64_t>(map)), "r"(bar), "r"(c), "r"(w), "r"(h), "r"(n),
         "h"(off_w), "h"(off_h)
+        : "memory");
+}
+
+// Plain bulk copy of `bytes` (a multiple of 16, both addresses 16-byte aligned) from global to
+// this CTA's shared memory, completing on `bar`.
+__device__ __forceinline__ void bulk_load(void *dst, const void *src, uint32_t bytes, uint64_t *bar) {
+    asm volatile(
+        "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];"
+        ::"r"(smem_addr(dst)), "l"(reinterpret_cast<uint64_t>(src)), "r"(bytes), "r"(smem_addr(bar))
         : "memory");
 }
 
@@ -732,8 +746,8 @@ __global__ void __launch_bounds__(THREADS, 1) umma_gemm_kernel(const __grid_cons
             const int wb = ow0 * p.SW - p.PL, hb = oh0 * p.SH - p.PT;
             // row tiles: the tile's image and first output row; window rows / row tiles: the K
             // block's filter row kh and first column x0, advanced per block (no division)
-            const int rimg = p.im2col == 4 ? mt / p.rt_per_img : 0;
-            const int roh0 = p.im2col == 4 ? (mt - rimg * p.rt_per_img) * p.rt_rows : 0;
+            const int rimg = p.im2col >= 4 ? mt / p.rt_per_img : 0;
+            const int roh0 = p.im2col >= 4 ? (mt - rimg * p.rt_per_img) * p.rt_rows : 0;
             int kh_w = 0, cb_w = 0;
             for (int kb = 0; kb < num_kb; ++kb, ++g, pos.advance()) {
                 const int s = pos.slot;
@@ -752,7 +766,13 @@ __global__ void __launch_bounds__(THREADS, 1) umma_gemm_kernel(const __grid_cons
                     ok = false;
                     break;
                 }
-                if (p.im2col == 4) {
+                if (p.im2col == 5) {
+                    // phase-split row tiles: the K block is filter row kh; both column phases of
+                    // the packed input row it reads, one contiguous bulk copy
+                    if (lane == 0)
+                        bulk_load(a_tile(s), p.a_rows + ((long long)rimg * p.prows + roh0 * p.SH + kh * p.DH) * p.prow_bytes,
+                                  p.a_bytes, &full[s]);
+                } else if (p.im2col == 4) {
                     // row tiles: one box of rt_rows whole output rows (OW pixels each) of one
                     // image; the tile's remaining smem rows are never loaded and never stored
                     if (lane == 0) tma_load_5d(a_tile(s), &p.tmA, &full[s], x0, 0, roh0, rimg, kh);
@@ -962,12 +982,17 @@ __global__ void __launch_bounds__(THREADS, 1) umma_gemm_kernel(const __grid_cons
                     const RingPos<S> nx = pos.next();
                     uint64_t *const next_ready = &ready[nx.slot];
                     const uint32_t next_parity = nx.phase;
-                    const bool packed = p.im2col == 2;
+                    const bool packed = p.im2col == 2, phased = p.im2col == 5;
                     // the block's descriptors, all before the first MMA: 8 tf32 = 32 bytes per step
                     uint64_t ad[BK / 8], bd[BK / 8], bld[BK / 8];
 #pragma unroll
                     for (int k = 0; k < BK / 8; ++k) {
-                        ad[k] = packed ? plain_desc(a_addr + k * 2 * PACKED_BOX_BYTES, PACKED_BOX_BYTES, 128)
+                        // phase-split rows: output pixel m's four taps of one phase are pixels m..m+3
+                        // of that phase's buffer, so row m of the operand starts 16 bytes after row
+                        // m - 1 and the K-adjacent core matrix 16 bytes after this one; steps 0-1
+                        // read the even-tap phase, steps 2-3 the odd-tap phase
+                        ad[k] = phased ? plain_desc(a_addr + (k < 2 ? 32 * k : p.phase_bytes + 32 * (k - 2)), 16, 128)
+                              : packed ? plain_desc(a_addr + k * 2 * PACKED_BOX_BYTES, PACKED_BOX_BYTES, 128)
                                        : sw128_desc(a_addr + k * 32);
                         bd[k] = sw128_desc(b_addr + k * 32);
                         bld[k] = sw128_desc(bl_addr + k * 32);
@@ -1126,14 +1151,14 @@ __global__ void __launch_bounds__(THREADS, 1) umma_gemm_kernel(const __grid_cons
         const bool issuer = warp == 2 && lane == 0;
         if (issuer && p.tma_out) prefetch_tmap(&p.tmC);
         if (issuer && p.tma_res) prefetch_tmap(&p.tmR);
-        const bool rows = p.im2col == 4;
+        const bool rows = p.im2col >= 4;
         // the residual of pass h_ of tile (mt_, nt_) into its staging (the output staging tile,
         // or with SR its own)
         auto issue_residual = [&](int mt_, int nt_, int h_) {
             const int tn0 = nt_ * BN + h_ * EN, tm0 = mt_ * C::TM + row0;
             if (rows) {
                 const int img = mt_ / p.rt_per_img, oh0 = (mt_ - img * p.rt_per_img) * p.rt_rows;
-                mbar_expect_tx(res_full, (uint32_t)(EN / 32) * p.a_bytes);
+                mbar_expect_tx(res_full, (uint32_t)(EN / 32) * p.res_box_bytes);
 #pragma unroll 1
                 for (int sl = 0; sl < EN / 32; ++sl)
                     tma_load_4d(res_tile + sl * (BM * 128), &p.tmR, res_full, tn0 + sl * 32, 0, oh0, img);
@@ -1748,18 +1773,38 @@ inline int try_gemm_umma(const GemmParams &p, cudaStream_t stream, int *taken) {
     } else if (p.a_kind == MGC_CONV_NHWC) {
         if (p.cg != p.C || p.c_off != 0 || (p.C & 3) || p.b_cpad <= 0) return MGC_CUDA_OK;
         if (p.M % (p.OH * p.OW)) return MGC_CUDA_OK;
-        // window rows when the lowering laid B out as [N][KH][L] over a padded image (win_rows);
+        // phase-split row tiles when the lowering packed the image by column phase (phase_w);
+        // window rows when it laid B out as [N][KH][L] over a padded image (win_rows);
         // tap-packed when B is K-major over (kh, kw, channel) without channel padding (b_cpad ==
         // C < 32); otherwise one K block per filter tap and 32-channel block
-        const bool window = p.win_rows > 0;
-        const bool packed = !window && p.b_cpad == p.C && p.C < umma::BK;
-        if (!window) {  // limits of the im2col tensor map: corner offsets, traversal strides
+        const bool phase = p.phase_w > 0;
+        const bool window = !phase && p.win_rows > 0;
+        const bool packed = !phase && !window && p.b_cpad == p.C && p.C < umma::BK;
+        if (!window && !phase) {  // limits of the im2col tensor map: corner offsets, traversal strides
             const int lw = -p.PL, lh = -p.PT;
             const int uw = (p.OW - 1) * p.SW - p.PL - (p.W - 1), uh = (p.OH - 1) * p.SH - p.PT - (p.H - 1);
             if (lw < -128 || lh < -128 || uw > 127 || uh > 127 || uw < -128 || uh < -128) return MGC_CUDA_OK;
             if (p.SW > 8 || p.SH > 8 || (p.KW - 1) * p.DW > 65535 || (p.KH - 1) * p.DH > 65535) return MGC_CUDA_OK;
         }
-        if (window) {
+        if (phase) {
+            // the packed rows hold both phases of phase_w pixels of 4 channels (the image's padding
+            // included); every tile row reads pixels m .. m + 3 of each phase, rows past OW too
+            const long long row_bytes = 2ll * p.phase_w * 16;
+            if (strict || p.C != 4 || p.W != 2 * p.phase_w || p.PT || p.PL || p.SW != 2 || p.DW != 1 || p.KW > 8 ||
+                p.OW > umma::BM || p.phase_w < umma::BM + 4 || p.b_cpad != 4 ||
+                (long long)(p.OH - 1) * p.SH + (long long)(p.KH - 1) * p.DH >= p.H ||
+                (reinterpret_cast<uintptr_t>(p.a) & 15) || row_bytes > umma::A_TILE_BYTES)
+                return MGC_CUDA_OK;
+            u.im2col = 5;
+            u.cblocks = 1;
+            u.num_kb = p.KH;
+            kp = p.KH * umma::BK;
+            u.a_rows = reinterpret_cast<const char *>(p.a);
+            u.prow_bytes = row_bytes;
+            u.prows = p.H;
+            u.phase_bytes = p.phase_w * 16;
+            u.a_bytes = (uint32_t)row_bytes;
+        } else if (window) {
             if (p.PT || p.PL || p.DW != 1 || p.OW % p.win_rows || umma::BM % p.win_rows ||
                 p.win_L != (int)ceil_div(p.KW * p.C, umma::BK) * umma::BK ||
                 (long long)(p.OW - 1) * p.SW + p.KW > p.W ||
@@ -1797,7 +1842,7 @@ inline int try_gemm_umma(const GemmParams &p, cudaStream_t stream, int *taken) {
     if (!umma::make_map_b(&u.tmB, p.b_umma, p.b_umma_lo, p.N, kp, bn)) return MGC_CUDA_OK;
     u.n_tiles = (int)ceil_div(p.N, bn);
     long long m_tiles = ceil_div(p.M, umma::BM);
-    u.a_bytes = umma::A_TILE_BYTES;
+    if (u.im2col != 5) u.a_bytes = umma::A_TILE_BYTES;
     const long long tiles = (long long)u.n_tiles * m_tiles;
     if (tiles > 0x7FFFFFFF) return MGC_CUDA_OK;
     u.c = p.c; u.ldc = p.ldc; u.bias = p.bias; u.res = p.res; u.ldr = p.ldr;
@@ -1829,7 +1874,23 @@ inline int try_gemm_umma(const GemmParams &p, cudaStream_t stream, int *taken) {
             u.rt_per_img = (int)ceil_div(p.OH, rows);
             m_tiles = nimg * u.rt_per_img;
             u.a_bytes = (uint32_t)rows * p.OW * 128;
+            u.res_box_bytes = u.a_bytes;
         }
+    }
+    // Phase-split row tiles: one output row per tile (its output and residual through 4-D maps
+    // that clip the tile's rows past OW), A read by bulk copies of packed rows.
+    if (u.im2col == 5) {
+        const long long nimg = (long long)p.M / ((long long)p.OH * p.OW);
+        CUtensorMap c4, r4;
+        if (!u.tma_out || !umma::make_map_rows(&c4, p.c, p.N, p.ldc, p.OW, p.OH, nimg, 1) ||
+            (u.tma_res && !umma::make_map_rows(&r4, p.res, p.N, p.ldr, p.OW, p.OH, nimg, 1)))
+            return MGC_CUDA_OK;
+        u.tmC = c4;
+        if (u.tma_res) u.tmR = r4;
+        u.rt_rows = 1;
+        u.rt_per_img = p.OH;
+        m_tiles = nimg * p.OH;
+        u.res_box_bytes = (uint32_t)p.OW * 128;
     }
     u.m_tiles = (int)m_tiles;
     // CTA pairs (256-row tiles, B planes split between the two CTAs: a third less shared-memory

@@ -818,7 +818,45 @@ struct PackParams {
     long long sn, sh, sw, sc;
     const float *x;
     float *out;
+    // phase-split rows (phases = 2, cp = 4, Wp = 2 * Wq): packed row r of an image holds, for
+    // phase f = 0, 1 and i < Wq, image column 2 i + f - PL of image row r - PT (zero outside the
+    // image), every value rounded to the nearest TF32 value (the tensor core truncates what a
+    // bulk copy brings in). phases = 0: plain NHWC pixels at (r - PT, w - PL).
+    int phases;
 };
+
+// Round fp32 to the nearest TF32 value (10 explicit mantissa bits; ties away from zero), as a
+// TFLOAT32 tensor map does on load; infinities and NaNs pass unchanged.
+__device__ __forceinline__ float round_tf32(float x) {
+    const uint32_t b = __float_as_uint(x);
+    return (b & 0x7F800000u) == 0x7F800000u ? x : __uint_as_float((b + 0x1000u) & 0xFFFFE000u);
+}
+
+// Phase-split packing (PackParams.phases = 2), one packed 4-channel pixel per thread and
+// iteration, 32-bit indices (the launcher checks the sizes).
+__global__ void __launch_bounds__(256) pack_phase_kernel(const __grid_constant__ PackParams p) {
+    const unsigned wq = (unsigned)p.Wp >> 1;
+    const unsigned per_row = (unsigned)p.Wp;  // both phases
+    const unsigned per_img = (unsigned)p.Hp * per_row;
+    const unsigned total = (unsigned)p.N * per_img;
+    const unsigned stride = gridDim.x * blockDim.x;
+    for (unsigned e = blockIdx.x * blockDim.x + threadIdx.x; e < total; e += stride) {
+        const unsigned n = e / per_img;
+        const unsigned r = e - n * per_img;
+        const unsigned row = r / per_row;
+        const unsigned q = r - row * per_row;
+        const unsigned f = q >= wq ? 1u : 0u;
+        const int h = (int)row - p.PT;
+        const int w = 2 * (int)(q - f * wq) + (int)f - p.PL;
+        const bool inside = h >= 0 && h < p.H && w >= 0 && w < p.W;
+        const float *src =
+            p.x + (inside ? n * (unsigned)p.sn + (unsigned)h * (unsigned)p.sh + (unsigned)w * (unsigned)p.sw : 0u);
+        float v[4];
+#pragma unroll
+        for (int t = 0; t < 4; ++t) v[t] = inside && t < p.C ? round_tf32(__ldg(src + (unsigned)t * (unsigned)p.sc)) : 0.0f;
+        reinterpret_cast<float4 *>(p.out)[e] = make_float4(v[0], v[1], v[2], v[3]);
+    }
+}
 
 // The same packing with 32-bit index arithmetic (pixel counts and source offsets below 2^31).
 __global__ void __launch_bounds__(256) pack_nhwc32_kernel(const __grid_constant__ PackParams p) {

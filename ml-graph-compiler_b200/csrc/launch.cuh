@@ -79,6 +79,9 @@ inline int run_gemm(const GemmParams &p, cudaStream_t stream, LaunchInfo *info =
         info->gemm_path = taken > 0 ? MGC_CUDA_PATH_TCGEN05 : MGC_CUDA_PATH_SIMT;
     }
     if (taken) return MGC_CUDA_OK;
+    if (p.phase_w > 0)  // a phase-split packed image is no NHWC operand for the exact-fp32 kernel
+        return fail(MGC_CUDA_UNSUPPORTED, "gemm: the tensor-core kernel declined a phase-split convolution "
+                                          "(M %d, N %d, OW %d)", p.M, p.N, p.OW);
     return launch_gemm_simt(p, stream);
 }
 
@@ -110,6 +113,7 @@ inline int decode_gemm(const mgc_cuda_launch &L, const Bases &bases, GemmParams 
     MGC_RESOLVE(L.r[7], p.b_umma_lo);
     p.b_cpad = (int)i[50];
     p.win_rows = (int)i[51]; p.win_L = (int)i[52];
+    p.phase_w = (int)i[53];
     if (!p.a || !p.b || !p.c) return fail(MGC_CUDA_BAD_ARGUMENT, "gemm: missing operand");
     return MGC_CUDA_OK;
 }
@@ -511,9 +515,24 @@ inline int launch_record(const mgc_cuda_launch &L, const int64_t *aux, int64_t a
         p.N = (int)i[0]; p.H = (int)i[1]; p.W = (int)i[2]; p.C = (int)i[3]; p.cp = (int)i[4];
         p.sn = i[5]; p.sh = i[6]; p.sw = i[7]; p.sc = i[8];
         p.PT = (int)i[9]; p.PL = (int)i[10]; p.Hp = (int)i[11]; p.Wp = (int)i[12];
+        p.phases = (int)i[13];
         MGC_RESOLVE(L.r[0], p.x); MGC_RESOLVE(L.r[1], p.out);
         if (p.cp <= 0 || (p.cp & 3) || p.C > p.cp || (reinterpret_cast<uintptr_t>(p.out) & 15))
             return fail(MGC_CUDA_BAD_ARGUMENT, "pack: %d of %d channels / output alignment", p.C, p.cp);
+        if (p.phases) {
+            const long long total = (long long)p.N * p.Hp * p.Wp;
+            const long long src_last = (long long)(p.N - 1) * p.sn + (long long)(p.H - 1) * p.sh +
+                                       (long long)(p.W - 1) * p.sw + (long long)(p.C - 1) * p.sc;
+            if (p.phases != 2 || p.cp != 4 || (p.Wp & 1) || p.PT < 0 || p.Hp < p.PT + p.H || total >= (1ll << 31) ||
+                src_last >= (1ll << 31) || p.sn < 0 || p.sh < 0 || p.sw < 0 || p.sc < 0 ||
+                2ll * (p.Wp / 2) < (long long)p.W + p.PL)
+                return fail(MGC_CUDA_BAD_ARGUMENT, "pack: phase-split layout %dx%d of a %dx%dx%d image", p.Hp, p.Wp,
+                            p.H, p.W, p.C);
+            if (total == 0) { launched = 0; break; }
+            pack_phase_kernel<<<grid_for(total, 256), 256, 0, stream>>>(p);
+            st = check_launch("pack_phase_kernel");
+            break;
+        }
         if (p.PT < 0 || p.PL < 0 || p.Hp < p.PT + p.H || p.Wp < p.PL + p.W)
             return fail(MGC_CUDA_BAD_ARGUMENT, "pack: padded %dx%d cannot hold %dx%d at (%d, %d)", p.Hp, p.Wp,
                         p.H, p.W, p.PT, p.PL);

@@ -61,6 +61,7 @@ EW_OPS = [
 EW_CODE = {name: i for i, name in enumerate(EW_OPS)}
 EW_MAX_RANK, EW_MAX_LEAVES, EW_MAX_INSTR, COPY_MAX_RANK = 6, 20, 40, 8
 SOFTMAX_ROW_MAX = 1024  # longest row the register-resident softmax holds (kernels_norm.cuh)
+PHASE_TILE_ROWS = 128  # output pixels of one phase-split row tile (the tensor-core M tile)
 HEAD_FLOP_SHARE = 0.02  # largest share of a graph's GEMM FLOPs an output head computed in 3xTF32 may have
 _EW_BINARY = {"Add", "Sub", "Mul", "Div", "Pow", "Max", "Min"}
 _EW_FLOAT_ONLY = {"Clip", "Relu", "Sigmoid", "Tanh", "Erf", "Sqrt", "Exp", "Log", "Neg", "Abs", "Reciprocal",
@@ -668,7 +669,7 @@ class CudaEmitter:
         if (len(users) == 1 and users[0].inputs and users[0].inputs[0] is out and self._tap_packed(users[0])
                 and all(v is not out for _, v in self.graph.named_outputs())):
             plan = self._narrow_plan(users[0])
-            if shape[3] % 4 or plan["wrows"]:
+            if shape[3] % 4 or plan["wrows"] or plan["phase"]:
                 # the only use is a narrow-channel convolution that reads a padded copy: write
                 # it straight from the source (the plain transposed copy would be unused)
                 self._packed[id(out)] = self._emit_pack(self.ref(x), shape[0], shape[1], shape[2], shape[3],
@@ -1105,6 +1106,7 @@ class CudaEmitter:
         b_cpad: int = 0,
         win_rows: int = 0,
         win_L: int = 0,
+        phase_w: int = 0,
     ) -> None:
         """K_GEMM slots: i[0..2] M, N, K; i[3] batch dims; i[4..7] batch extents; i[8..11],
         i[12..15], i[16..19], i[20..23] per-dimension batch strides of A, B, C, residual;
@@ -1114,13 +1116,15 @@ class CudaEmitter:
         i[50] padded channel count of the tensor-core B layout of an im2col convolution (0 when
         B is plain K-major). i[51] output pixels per window-row box and i[52] the padded window-row
         length L when the tensor-core B is laid out [N][KH][L] over a spatially padded image (0
-        otherwise). f[0..3] alpha, beta, clip lo, clip hi. r[0] A, r[1] B, r[2] C,
+        otherwise). i[53] pixels per phase of a phase-split packed image row (A is such an image
+        and B is [N][KH][32] in phase-split tap order; 0 otherwise). f[0..3] alpha, beta, clip lo,
+        clip hi. r[0] A, r[1] B, r[2] C,
         r[3] bias, r[4] residual, r[5] residual of a split constant B, r[6] / r[7] the
         tensor-core layout of a constant B (TF32-rounded part / residual), absent otherwise."""
         if len(batch) > 4:
             raise CodegenError(f"GEMM with {len(batch)} batch dimensions")
-        ints = [0] * 53
-        ints[50], ints[51], ints[52] = b_cpad, win_rows, win_L
+        ints = [0] * 54
+        ints[50], ints[51], ints[52], ints[53] = b_cpad, win_rows, win_L, phase_w
         ints[0], ints[1], ints[2], ints[3] = m, n, k, len(batch)
         for d in range(len(batch)):
             ints[4 + d] = batch[d]
@@ -1465,7 +1469,14 @@ class CudaEmitter:
         and, for the window-row form (unit width dilation, OW a multiple of 8), the image padded
         spatially to Hp x Wp with the convolution's own top / left padding, so that every window
         row is KW * cp contiguous floats inside the image; ``wrows`` output pixels per TMA box,
-        ``L`` the window row rounded up to whole 32-float K blocks."""
+        ``L`` the window row rounded up to whole 32-float K blocks.
+
+        ``phase`` (TF32 mode, width stride 2, unit width dilation, at most 4 channels, KW <= 8,
+        OW <= 128: the stems): the image is packed phase-split instead (K_PACK with phases, the
+        rows padded to Hp, each row holding its even-tap and odd-tap column phases of ``Wq``
+        pixels), so that a filter row's window for output pixel m is pixels m..m+3 of each phase;
+        a tile is one output row and reads each filter row's packed input row with one bulk
+        copy instead of one TMA row per output pixel."""
         xt, wt = node.input(0).tensor_type, node.input(1).tensor_type
         _, h, w, _ = xt.shape
         kh, kw, cg, _ = wt.shape
@@ -1474,21 +1485,28 @@ class CudaEmitter:
         pt, pl, _, _ = g.pads
         cp = (cg + 3) // 4 * 4
         wrows = 16 if ow % 16 == 0 else 8 if ow % 8 == 0 else 0
-        plan = {"cp": cp, "wrows": 0, "L": 0, "PT": 0, "PL": 0, "Hp": h, "Wp": w}
+        plan = {"cp": cp, "wrows": 0, "L": 0, "PT": 0, "PL": 0, "Hp": h, "Wp": w, "phase": 0, "Wq": 0}
+        hp = max(pt + h, (oh - 1) * g.strides[0] + (kh - 1) * g.dilations[0] + 1)
+        if (self.precision == "tf32" and g.strides[1] == 2 and g.dilations[1] == 1 and cp == 4 and kw <= 8
+                and ow <= PHASE_TILE_ROWS):
+            wq = PHASE_TILE_ROWS + 4  # tile rows past OW read 3 pixels further, as the last real row does
+            plan.update(phase=1, Wq=wq, PT=pt, PL=pl, Hp=hp, Wp=2 * wq)
+            return plan
         if wrows and g.dilations[1] == 1:
             sh, sw = g.strides
-            plan.update(wrows=wrows, L=(kw * cp + 31) // 32 * 32, PT=pt, PL=pl,
-                        Hp=max(pt + h, (oh - 1) * sh + (kh - 1) * g.dilations[0] + 1),
+            plan.update(wrows=wrows, L=(kw * cp + 31) // 32 * 32, PT=pt, PL=pl, Hp=hp,
                         Wp=max(pl + w, (ow - 1) * sw + kw))
         return plan
 
     def _emit_pack(self, src: RefT, nb: int, h: int, w: int, c: int, strides: Sequence[int],
                    plan: dict[str, int]) -> RefT:
         """K_PACK slots: i[0..4] N, H, W, C, padded C; i[5..8] source element strides of n, h, w,
-        c; i[9..12] PT, PL, padded H, padded W; r[0] source, r[1] packed NHWC destination."""
+        c; i[9..12] PT, PL, padded H, padded W (both phases' pixels of a phase-split row); i[13] 2
+        for the phase-split layout, else 0; r[0] source, r[1] packed NHWC destination."""
         cp, hp, wp = plan["cp"], plan["Hp"], plan["Wp"]
         dst = self._pack_region(nb * hp * wp * cp * 4)
-        self.emit(K_PACK, [nb, h, w, c, cp, *strides, plan["PT"], plan["PL"], hp, wp], refs=[src, dst])
+        self.emit(K_PACK, [nb, h, w, c, cp, *strides, plan["PT"], plan["PL"], hp, wp, 2 if plan["phase"] else 0],
+                  refs=[src, dst])
         return dst
 
     def _conv_tap_packed(self, node: Node, w_hwio: np.ndarray, geo: dict[str, int], nb: int, bias: RefT,
@@ -1501,7 +1519,7 @@ class CudaEmitter:
         x = node.input(0)
         kh, kw, cg, kg = w_hwio.shape
         plan = self._narrow_plan(node)
-        cp, window = plan["cp"], plan["wrows"] > 0
+        cp, window = plan["cp"], plan["wrows"] > 0 or plan["phase"] > 0
         if cp == cg and not window:
             xref = self.ref(x)
         elif id(x) in self._packed:
@@ -1515,7 +1533,18 @@ class CudaEmitter:
         bref, blo, b_rs, b_cs = self._kmajor_b(wpad.reshape(kh * kw * cp, kg), ("tap-packed", wkey))
         umma = {"b_umma": bref, "b_umma_lo": blo}
         conv = {**geo, "C": cp, "c_off": 0, "cg": cp}
-        if window:
+        if plan["phase"]:
+            # the packed image holds the padding; its rows are the two phases of Wq pixels each
+            conv.update(H=plan["Hp"], W=plan["Wp"], PT=0, PL=0)
+            # tensor-core B as [N][KH][32]: filter row kh's taps kw = 0, 2, 4, 6 (the phase read
+            # at pixels m..m+3 of the first half of a packed row), then kw = 1, 3, 5, 7, four
+            # channels each, absent taps zero
+            rows = np.zeros((kh, 2, 4, cp, kg), np.float32)
+            for k_w in range(kw):
+                rows[:, k_w % 2, k_w // 2, :, :] = wpad[:, k_w, :, :]
+            uhi, ulo, _, _ = self._kmajor_b(rows.reshape(kh * 32, kg), ("phase-rows", wkey))
+            umma = {"b_umma": uhi, "b_umma_lo": ulo, "phase_w": plan["Wq"]}
+        elif window:
             # the image is read from its padded copy: no padding left for the kernels to apply
             conv.update(H=plan["Hp"], W=plan["Wp"], PT=0, PL=0)
             # tensor-core B as [N][KH][L]: filter row kh's KW * cp weights, zero up to L
