@@ -568,9 +568,13 @@ constexpr uint32_t SMEM_LIMIT = 232448;  // dynamic shared memory per block on s
 // SR (one CTA per tile, TF32, with a residual): the residual moves through its own staging
 // buffer, so the next pass's residual loads while this pass's output is stored; SR = 2 runs the
 // epilogue in passes of 64 columns, so that both buffers take the shared memory of one.
-template <int BN, int MODE, int RB = 0, int PAIR = 0, int SR = 0>
+// PH: phase-split row tiles (im2col 5): a stage's A part is one packed input row (both phases),
+// a few KB, so the ring holds many more stages to keep enough bytes in flight.
+constexpr uint32_t PHASE_STAGE_BYTES = 5120;  // the A part of a phase-split stage (1024-aligned)
+template <int BN, int MODE, int RB = 0, int PAIR = 0, int SR = 0, int PH = 0>
 struct Cfg {
     static_assert(!SR || (!PAIR && MODE == TF32), "a separate residual buffer is a one-CTA TF32 form");
+    static_assert(!PH || (!PAIR && !SR && MODE == TF32 && BN == 64), "phase-split tiles: one CTA, TF32, N tile 64");
     static_assert(!PAIR || MODE == TF32, "CTA pairs run TF32 mode only");
     static constexpr bool WIDE = PAIR && BN > 128;
     static_assert(BN <= 128 || (WIDE && RB == 0 && BN % 64 == 0 && BN <= 256),
@@ -585,8 +589,9 @@ struct Cfg {
     static constexpr int EN = WIDE || SR == 2 ? 64 : BN;     // columns of one epilogue pass
     static constexpr int NH = BN / EN;                       // epilogue passes per tile
     // stage: A (| A_lo) (| B_hi | B_lo), or A | this rank's B plane
+    static constexpr uint32_t A_BYTES = PH ? PHASE_STAGE_BYTES : A_TILE_BYTES;
     static constexpr uint32_t STAGE_BYTES =
-        A_TILE_BYTES + (MODE == STRICT ? A_TILE_BYTES : 0) + (RB ? 0 : B_PLANES * B_TILE_BYTES);
+        A_BYTES + (MODE == STRICT ? A_TILE_BYTES : 0) + (RB ? 0 : B_PLANES * B_TILE_BYTES);
     // output staging of one epilogue pass: EN/32 slabs of [128 rows][32 fp32] in the
     // 128B-swizzled TMA layout
     static constexpr uint32_t OUT_BYTES = BM * EN * 4;
@@ -594,8 +599,9 @@ struct Cfg {
     // everything else: output staging, alignment slack, barriers, the tile's bias
     static constexpr uint32_t RES_BYTES = SR ? OUT_BYTES : 0;       // the residual's own staging
     static constexpr uint32_t STAGE_BUDGET = SMEM_LIMIT - OUT_BYTES - RES_BYTES - 1024 - BAR_BYTES - BN * 4;
-    static constexpr int MAX_STAGES = 8;
-    static constexpr int STAGES = RB ? (MODE == STRICT || SR ? 2 : 4)
+    static constexpr int MAX_STAGES = PH ? 16 : 8;
+    static constexpr int STAGES = RB && PH ? 16
+                                  : RB ? (MODE == STRICT || SR ? 2 : 4)
                                   : (STAGE_BUDGET / STAGE_BYTES) < 2 ? 2
                                   : (int)(STAGE_BUDGET / STAGE_BYTES) > MAX_STAGES ? MAX_STAGES
                                   : (STAGE_BUDGET / STAGE_BYTES);
@@ -612,7 +618,7 @@ struct Cfg {
     static constexpr uint32_t SMEM_BYTES =
         STAGES * STAGE_BYTES + OUT_BYTES + RES_BYTES + 1024 /*align*/ + BAR_BYTES + BN * 4 /*bias*/;
     static constexpr uint32_t B_RES_MAX = RB ? SMEM_LIMIT - SMEM_BYTES : 0;
-    static_assert((3 * 8 + 2 * 4 + 3) * 8 + 4 <= BAR_BYTES, "barrier area");
+    static_assert((3 * STAGES + 2 * TBUFS + 3) * 8 + 4 <= BAR_BYTES, "barrier area");
     static_assert(TMEM_COLS <= 512, "TMEM columns");
     static_assert(TBUFS >= 2, "need at least two TMEM buffers");
 };
@@ -622,9 +628,9 @@ struct Cfg {
 // and walks the M tiles b / n_tiles, + gridDim.x / n_tiles, ... The shared-memory stage ring and
 // the TMEM buffer ring run on a K-block counter that continues across tiles, so the next tile's
 // loads and MMAs overlap this tile's drain and epilogue.
-template <int BN, int MODE, int RB, int PAIR, int SR>
+template <int BN, int MODE, int RB, int PAIR, int SR, int PH>
 __global__ void __launch_bounds__(THREADS, 1) umma_gemm_kernel(const __grid_constant__ Params p) {
-    using C = Cfg<BN, MODE, RB, PAIR, SR>;
+    using C = Cfg<BN, MODE, RB, PAIR, SR, PH>;
     constexpr int S = C::STAGES;
     constexpr int R = C::REGIONS;
     constexpr int TB = C::TBUFS;
@@ -634,11 +640,11 @@ __global__ void __launch_bounds__(THREADS, 1) umma_gemm_kernel(const __grid_cons
     uint8_t *b_panel = smem;
     uint8_t *stages = smem + (RB ? p.b_res_bytes : 0u);
     auto a_tile = [&](int s) { return stages + (size_t)s * C::STAGE_BYTES; };
-    auto alo_tile = [&](int s) { return stages + (size_t)s * C::STAGE_BYTES + A_TILE_BYTES; };
+    auto alo_tile = [&](int s) { return stages + (size_t)s * C::STAGE_BYTES + C::A_BYTES; };
     // B_hi of K block kb (B_lo follows it directly: the stacked [B_hi; B_lo] operand)
     auto b_tile = [&](int s, int kb) {
         return RB ? b_panel + (size_t)kb * C::B_PLANES * C::B_TILE_BYTES
-                  : stages + (size_t)s * C::STAGE_BYTES + A_TILE_BYTES + (MODE == STRICT ? A_TILE_BYTES : 0);
+                  : stages + (size_t)s * C::STAGE_BYTES + C::A_BYTES + (MODE == STRICT ? A_TILE_BYTES : 0);
     };
     uint8_t *out_tile = stages + (size_t)S * C::STAGE_BYTES;  // 1024-aligned
     uint8_t *res_tile = SR ? out_tile + C::OUT_BYTES : out_tile;  // where a residual pass lands
@@ -1539,21 +1545,21 @@ inline bool make_map_4d(CUtensorMap *map, const void *base, long long cols, long
     return r == CUDA_SUCCESS;
 }
 
-template <int BN, int MODE, int RB, int PAIR, int SR = 0>
+template <int BN, int MODE, int RB, int PAIR, int SR = 0, int PH = 0>
 inline uint32_t launch_smem(const Params &p) {
-    using C = Cfg<BN, MODE, RB, PAIR, SR>;
+    using C = Cfg<BN, MODE, RB, PAIR, SR, PH>;
     const uint32_t smem = C::SMEM_BYTES + (RB ? p.b_res_bytes : 0u);
     return PAIR && smem < SMEM_LIMIT / 2 + 1024 ? SMEM_LIMIT / 2 + 1024 : smem;
 }
 
-template <int BN, int MODE, int RB, int PAIR, int SR = 0>
+template <int BN, int MODE, int RB, int PAIR, int SR = 0, int PH = 0>
 inline int launch(const Params &p, int grid, cudaStream_t stream) {
-    const uint32_t smem = launch_smem<BN, MODE, RB, PAIR, SR>(p);
+    const uint32_t smem = launch_smem<BN, MODE, RB, PAIR, SR, PH>(p);
     // per device (the attribute belongs to the current context); cheap, and allowed under capture
-    MGC_CHECK_CUDA(cudaFuncSetAttribute(umma_gemm_kernel<BN, MODE, RB, PAIR, SR>,
+    MGC_CHECK_CUDA(cudaFuncSetAttribute(umma_gemm_kernel<BN, MODE, RB, PAIR, SR, PH>,
                                         cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
     if (!PAIR) {
-        umma_gemm_kernel<BN, MODE, RB, PAIR, SR><<<grid, THREADS, smem, stream>>>(p);
+        umma_gemm_kernel<BN, MODE, RB, PAIR, SR, PH><<<grid, THREADS, smem, stream>>>(p);
         return check_launch("umma_gemm_kernel");
     }
     cudaLaunchConfig_t cfg = {};
@@ -1568,7 +1574,7 @@ inline int launch(const Params &p, int grid, cudaStream_t stream) {
     cfg.stream = stream;
     cfg.attrs = attr;
     cfg.numAttrs = 1;
-    MGC_CHECK_CUDA(cudaLaunchKernelEx(&cfg, umma_gemm_kernel<BN, MODE, RB, PAIR, SR>, p));
+    MGC_CHECK_CUDA(cudaLaunchKernelEx(&cfg, umma_gemm_kernel<BN, MODE, RB, PAIR, SR, PH>, p));
     return check_launch("umma_gemm_kernel (pair)");
 }
 
@@ -1586,6 +1592,22 @@ inline int launch_best(Params &p, long long m_tiles, cudaStream_t stream) {
     p.b_res_bytes = 0;
     const long long tiles = (long long)p.n_tiles * m_tiles;
     return launch<BN, MODE, 0, 0>(p, (int)(tiles < sms ? tiles : sms), stream);
+}
+
+// Phase-split row tiles (N tiles of 64, TF32): B-resident when the panel fits beside the deep
+// ring of small stages and every CTA walks at least two tiles.
+inline int launch_phase(Params &p, long long m_tiles, cudaStream_t stream) {
+    using C1 = Cfg<64, TF32, 1, 0, 0, 1>;
+    const int sms = sm_count();
+    const uint32_t panel = (uint32_t)p.num_kb * 2u * C1::B_TILE_BYTES;
+    const int per = p.n_tiles <= sms ? sms / p.n_tiles : 0;
+    if (per > 0 && panel <= C1::B_RES_MAX && m_tiles >= 2LL * per) {
+        p.b_res_bytes = panel;
+        return launch<64, TF32, 1, 0, 0, 1>(p, per * p.n_tiles, stream);
+    }
+    p.b_res_bytes = 0;
+    const long long tiles = (long long)p.n_tiles * m_tiles;
+    return launch<64, TF32, 0, 0, 0, 1>(p, (int)(tiles < sms ? tiles : sms), stream);
 }
 
 // One CTA per tile with a residual through its own staging buffer (N tiles of 128, TF32), when
@@ -1627,7 +1649,7 @@ inline int pair_clusters() {
     memset(&dummy, 0, sizeof dummy);
     const uint32_t smem = launch_smem<BN, TF32, RB, 1>(dummy);
     int n = 0;
-    if (cudaFuncSetAttribute(umma_gemm_kernel<BN, TF32, RB, 1, 0>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+    if (cudaFuncSetAttribute(umma_gemm_kernel<BN, TF32, RB, 1, 0, 0>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                              (int)SMEM_LIMIT) == cudaSuccess) {
         cudaLaunchConfig_t cfg = {};
         cudaLaunchAttribute attr[1] = {};
@@ -1640,7 +1662,7 @@ inline int pair_clusters() {
         cfg.dynamicSmemBytes = smem;
         cfg.attrs = attr;
         cfg.numAttrs = 1;
-        if (cudaOccupancyMaxActiveClusters(&n, umma_gemm_kernel<BN, TF32, RB, 1, 0>, &cfg) != cudaSuccess) n = 0;
+        if (cudaOccupancyMaxActiveClusters(&n, umma_gemm_kernel<BN, TF32, RB, 1, 0, 0>, &cfg) != cudaSuccess) n = 0;
     }
     cudaGetLastError();
     cached[dev] = n;
@@ -1791,9 +1813,9 @@ inline int try_gemm_umma(const GemmParams &p, cudaStream_t stream, int *taken) {
             // included); every tile row reads pixels m .. m + 3 of each phase, rows past OW too
             const long long row_bytes = 2ll * p.phase_w * 16;
             if (strict || p.C != 4 || p.W != 2 * p.phase_w || p.PT || p.PL || p.SW != 2 || p.DW != 1 || p.KW > 8 ||
-                p.OW > umma::BM || p.phase_w < umma::BM + 4 || p.b_cpad != 4 ||
+                p.OW > umma::BM || p.phase_w < umma::BM + 4 || p.b_cpad != 4 || p.N > 64 ||
                 (long long)(p.OH - 1) * p.SH + (long long)(p.KH - 1) * p.DH >= p.H ||
-                (reinterpret_cast<uintptr_t>(p.a) & 15) || row_bytes > umma::A_TILE_BYTES)
+                (reinterpret_cast<uintptr_t>(p.a) & 15) || row_bytes > umma::PHASE_STAGE_BYTES)
                 return MGC_CUDA_OK;
             u.im2col = 5;
             u.cblocks = 1;
@@ -2019,7 +2041,8 @@ inline int try_gemm_umma(const GemmParams &p, cudaStream_t stream, int *taken) {
         return !(e && e[0] == '0');
     }();
     int st;
-    if (strict) st = umma::launch_best<64, umma::STRICT>(u, m_tiles, stream);
+    if (u.im2col == 5) st = umma::launch_phase(u, m_tiles, stream);
+    else if (strict) st = umma::launch_best<64, umma::STRICT>(u, m_tiles, stream);
     else if (bn == 64) st = umma::launch_best<64, umma::TF32>(u, m_tiles, stream);
     else if (u.tma_res && sr_env) st = umma::launch_best_sr(u, m_tiles, stream);
     else st = umma::launch_best<128, umma::TF32>(u, m_tiles, stream);

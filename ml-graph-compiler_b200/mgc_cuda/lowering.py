@@ -1472,7 +1472,7 @@ class CudaEmitter:
         ``L`` the window row rounded up to whole 32-float K blocks.
 
         ``phase`` (TF32 mode, width stride 2, unit width dilation, at most 4 channels, KW <= 8,
-        OW <= 128: the stems): the image is packed phase-split instead (K_PACK with phases, the
+        OW <= 128, at most 64 output channels: the stems): the image is packed phase-split instead (K_PACK with phases, the
         rows padded to Hp, each row holding its even-tap and odd-tap column phases of ``Wq``
         pixels), so that a filter row's window for output pixel m is pixels m..m+3 of each phase;
         a tile is one output row and reads each filter row's packed input row with one bulk
@@ -1488,7 +1488,7 @@ class CudaEmitter:
         plan = {"cp": cp, "wrows": 0, "L": 0, "PT": 0, "PL": 0, "Hp": h, "Wp": w, "phase": 0, "Wq": 0}
         hp = max(pt + h, (oh - 1) * g.strides[0] + (kh - 1) * g.dilations[0] + 1)
         if (self.precision == "tf32" and g.strides[1] == 2 and g.dilations[1] == 1 and cp == 4 and kw <= 8
-                and ow <= PHASE_TILE_ROWS):
+                and ow <= PHASE_TILE_ROWS and wt.shape[3] <= 64):
             wq = PHASE_TILE_ROWS + 4  # tile rows past OW read 3 pixels further, as the last real row does
             plan.update(phase=1, Wq=wq, PT=pt, PL=pl, Hp=hp, Wp=2 * wq)
             return plan
