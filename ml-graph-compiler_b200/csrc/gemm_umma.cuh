@@ -1046,6 +1046,7 @@ __global__ void __launch_bounds__(THREADS, 1) umma_gemm_kernel(const __grid_cons
         // A tile's epilogue runs in NH passes of EN columns (one pass unless wide); each pass
         // stages, stores and (with a residual) prefetches EN columns.
         constexpr int EN = C::EN, NH = C::NH;
+        static_assert(EN <= EPI_THREADS, "one bias column per epilogue thread");
         constexpr int HALF = EN / 2;        // columns per epilogue thread and pass
         const int et = threadIdx.x - 64;    // 0..255
         const int q = warp & 3;             // TMEM lane quadrant this warp may access
@@ -1194,6 +1195,9 @@ __global__ void __launch_bounds__(THREADS, 1) umma_gemm_kernel(const __grid_cons
           }
           for (int h = 0; ok && h < NH; ++h, ++local) {
             const int n0 = nt * BN + h * EN;
+            // this pass's bias column, loaded before the TMEM wait so that its latency overlaps it
+            // (EN <= EPI_THREADS: one column per thread)
+            const float bias_v = p.bias && et < EN && n0 + et < p.N ? __ldg(p.bias + n0 + et) : 0.0f;
             if (MODE != STRICT && !load_pass(h)) {
                 ok = false;
                 break;
@@ -1217,14 +1221,13 @@ __global__ void __launch_bounds__(THREADS, 1) umma_gemm_kernel(const __grid_cons
                 }
                 continue;
             }
-            // this pass's bias columns into shared memory, one coalesced load (the previous
-            // pass's readers have all passed its second barrier)
-            if (p.bias) {
-                for (int c = et; c < EN; c += EPI_THREADS) bias_s[c] = n0 + c < p.N ? __ldg(p.bias + n0 + c) : 0.0f;
-            }
-            // the staging tile is free (the previous TMA store was read out: SR waits for it
-            // here) and the residual staging holds this pass's residual
-            if (SR && issuer) tma_store_wait_read();
+            // this pass's bias columns into shared memory (the previous pass's readers have all
+            // passed its second barrier)
+            if (p.bias && et < EN) bias_s[et] = bias_v;
+            // the staging tile is free (the previous TMA store was read out: SR, and every form
+            // without a residual, waits for it here rather than right after issuing it) and the
+            // residual staging holds this pass's residual
+            if ((SR || !res_tma) && issuer) tma_store_wait_read();
             epilogue_sync();
             if (res_tma && !mbar_wait(res_full, (uint32_t)(local & 1))) {
                 ok = false;
@@ -1325,7 +1328,7 @@ __global__ void __launch_bounds__(THREADS, 1) umma_gemm_kernel(const __grid_cons
                             else tma_store_2d(&p.tmC, out_tile + sl * (BM * 128), n0 + sl * 32, m0);
                         }
                     }
-                    if (SR) {
+                    if (SR || !res_tma) {
                         tma_store_commit();  // read out before the next pass writes the staging tile
                     } else {
                         tma_store_commit_and_wait();
@@ -1341,7 +1344,7 @@ __global__ void __launch_bounds__(THREADS, 1) umma_gemm_kernel(const __grid_cons
         // a residual prefetch that no tile consumed must land, and the last store must have read
         // the staging tile, before the CTA exits
         if (res_tma && issuer && !ok) mbar_wait(res_full, (uint32_t)(local & 1));
-        if (SR && issuer) tma_store_wait_read();
+        if ((SR || !res_tma) && issuer) tma_store_wait_read();
         (void)et;
     }
     tc_fence_before();
