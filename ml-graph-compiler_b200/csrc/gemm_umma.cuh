@@ -568,13 +568,14 @@ constexpr uint32_t SMEM_LIMIT = 232448;  // dynamic shared memory per block on s
 // SR (one CTA per tile, TF32, with a residual): the residual moves through its own staging
 // buffer, so the next pass's residual loads while this pass's output is stored; SR = 2 runs the
 // epilogue in passes of 64 columns, so that both buffers take the shared memory of one.
-// PH: phase-split row tiles (im2col 5): a stage's A part is one packed input row (both phases),
-// a few KB, so the ring holds many more stages to keep enough bytes in flight.
-constexpr uint32_t PHASE_STAGE_BYTES = 5120;  // the A part of a phase-split stage (1024-aligned)
+// PH: phase-split row tiles (im2col 5): a stage holds one tile's KH packed input rows (both
+// phases each), brought in by one bulk copy; B stays resident.
+constexpr uint32_t PHASE_STAGE_BYTES = 30720;  // up to 7 packed rows of 4,352 bytes (1024-aligned)
 template <int BN, int MODE, int RB = 0, int PAIR = 0, int SR = 0, int PH = 0>
 struct Cfg {
     static_assert(!SR || (!PAIR && MODE == TF32), "a separate residual buffer is a one-CTA TF32 form");
-    static_assert(!PH || (!PAIR && !SR && MODE == TF32 && BN == 64), "phase-split tiles: one CTA, TF32, N tile 64");
+    static_assert(!PH || (!PAIR && !SR && RB && MODE == TF32 && BN == 64),
+                  "phase-split tiles: one CTA, TF32, N tile 64, B resident");
     static_assert(!PAIR || MODE == TF32, "CTA pairs run TF32 mode only");
     static constexpr bool WIDE = PAIR && BN > 128;
     static_assert(BN <= 128 || (WIDE && RB == 0 && BN % 64 == 0 && BN <= 256),
@@ -599,8 +600,8 @@ struct Cfg {
     // everything else: output staging, alignment slack, barriers, the tile's bias
     static constexpr uint32_t RES_BYTES = SR ? OUT_BYTES : 0;       // the residual's own staging
     static constexpr uint32_t STAGE_BUDGET = SMEM_LIMIT - OUT_BYTES - RES_BYTES - 1024 - BAR_BYTES - BN * 4;
-    static constexpr int MAX_STAGES = PH ? 16 : 8;
-    static constexpr int STAGES = RB && PH ? 16
+    static constexpr int MAX_STAGES = 8;
+    static constexpr int STAGES = PH ? 2
                                   : RB ? (MODE == STRICT || SR ? 2 : 4)
                                   : (STAGE_BUDGET / STAGE_BYTES) < 2 ? 2
                                   : (int)(STAGE_BUDGET / STAGE_BYTES) > MAX_STAGES ? MAX_STAGES
@@ -727,7 +728,38 @@ __global__ void __launch_bounds__(THREADS, 1) umma_gemm_kernel(const __grid_cons
     tc_fence_after();
     const uint32_t tmem_base = *tmem_slot;
 
-    if (warp == 0 && !PAIR && p.im2col >= 2) {
+    if (PH && warp == 0) {
+        // ---------------- producer, phase-split row tiles (lane 0) ----------------
+        // A tile's KH packed input rows are consecutive in memory: one bulk copy per tile, into
+        // a stage that holds them all (a copy holds its issuing thread for hundreds of cycles,
+        // so one per K block would starve the MMAs of a 7-block tile).
+        if (lane == 0) {
+            long long g = 0;  // tiles issued
+            RingPos<S> pos;   // stage of tile g
+            int mt, nt;
+            if (tile_at(0, mt, nt)) {  // the B panel, once
+                mbar_expect_tx(bres_full, p.b_res_bytes);
+                for (int kb = 0; kb < num_kb; ++kb) tma_load_3d(b_tile(0, kb), &p.tmB, bres_full, kb * BK, nt * BN, 0);
+            }
+            const uint32_t bytes = (uint32_t)num_kb * p.a_bytes;
+            for (int i = 0; tile_at(i, mt, nt); ++i, ++g, pos.advance()) {
+                const int s = pos.slot;
+                if (pos.wrapped && !mbar_wait(&empty[s], pos.phase ^ 1u)) {
+                    set_error(p.err, MGC_CUDA_TIMEOUT);
+                    break;
+                }
+                const int img = mt / p.rt_per_img, oh = mt - img * p.rt_per_img;
+                mbar_expect_tx(&full[s], bytes);
+                bulk_load(a_tile(s), p.a_rows + ((long long)img * p.prows + (long long)oh * p.SH) * p.prow_bytes, bytes,
+                          &full[s]);
+            }
+            // the copies of the last (up to S) issued tiles must have landed before exit
+            for (long long k = g - 1; k >= 0 && k >= g - S; --k) {
+                if (!mbar_wait(&full[k % S], (uint32_t)((k / S) & 1))) set_error(p.err, MGC_CUDA_TIMEOUT);
+            }
+            if (tile_at(0, mt, nt) && !mbar_wait(bres_full, 0)) set_error(p.err, MGC_CUDA_TIMEOUT);
+        }
+    } else if (warp == 0 && !PAIR && p.im2col >= 2) {
         // ---------------- TMA producer, narrow-channel forms (the whole warp) ----------------
         // A TMA instruction holds its issuing thread for a few hundred cycles. These forms need
         // eight or more A boxes per K block, so lane j issues box j, all in one instruction.
@@ -940,6 +972,50 @@ __global__ void __launch_bounds__(THREADS, 1) umma_gemm_kernel(const __grid_cons
     } else if (warp == 1) {
         if (lane == 0 && rank == 0) {
             // ---------------- MMA issuer (a pair's rank 0 issues for both CTAs) ----------------
+            if (PH) {
+                // phase-split row tiles: one stage per tile, the KH filter rows of the tile in
+                // it (K block kh: packed row kh; steps 0-1 the even-tap phase, 2-3 the odd-tap)
+                constexpr uint32_t idesc_t = instr_desc_tf32(2 * BN);
+                RingPos<S> pos;
+                RingPos<TB> buf;
+                bool ok = true;
+                int mt, nt;
+                if (tile_at(0, mt, nt) && !mbar_wait(bres_full, 0)) {  // the B panel (CTAs with tiles)
+                    set_error(p.err, MGC_CUDA_TIMEOUT);
+                    ok = false;
+                }
+                for (int i = 0; ok && tile_at(i, mt, nt); ++i, pos.advance()) {
+                    const int s = pos.slot, b = buf.slot;
+                    if (!mbar_wait(&full[s], pos.phase)) {
+                        set_error(p.err, MGC_CUDA_TIMEOUT);
+                        break;
+                    }
+                    if (buf.wrapped) {  // the epilogue has drained this TMEM buffer
+                        if (!mbar_wait(&tempty[b], buf.phase ^ 1u)) {
+                            set_error(p.err, MGC_CUDA_TIMEOUT);
+                            break;
+                        }
+                        tc_fence_after();
+                    }
+                    const uint32_t dbase = tmem_base + (uint32_t)(b * C::BUF_COLS);
+                    const uint32_t a0 = smem_addr(a_tile(s));
+                    for (int kb = 0; kb < num_kb; ++kb) {
+                        const uint32_t a_addr = a0 + (uint32_t)(kb * p.a_bytes), b_addr = smem_addr(b_tile(s, kb));
+                        uint64_t ad[BK / 8], bd[BK / 8];
+#pragma unroll
+                        for (int k = 0; k < BK / 8; ++k) {
+                            ad[k] = plain_desc(a_addr + (k < 2 ? 32 * k : p.phase_bytes + 32 * (k - 2)), 16, 128);
+                            bd[k] = sw128_desc(b_addr + k * 32);
+                        }
+                        (void)mma_block4<0>(dbase, ad, bd, idesc_t, kb == 0 ? 0u : 1u, &full[s], pos.phase);
+                    }
+                    mma_commit(&empty[s]);
+                    mma_commit(&tfull[b]);
+                    buf.advance();
+                }
+                mma_commit(mma_done);
+                if (!mbar_wait(mma_done, 0)) set_error(p.err, MGC_CUDA_TIMEOUT);
+            } else {
             constexpr uint32_t idesc = instr_desc_tf32(BN);
             // the stacked [B_hi; B_lo] tile, or (wide, DYN) one plane of all BN columns
             constexpr uint32_t idesc2 = instr_desc_tf32(C::ONEACC ? BN : 2 * BN, C::TM);
@@ -1040,6 +1116,7 @@ __global__ void __launch_bounds__(THREADS, 1) umma_gemm_kernel(const __grid_cons
             if (PAIR) mma_commit_pair_local(mma_done);
             else mma_commit(mma_done);
             if (!mbar_wait(mma_done, 0)) set_error(p.err, MGC_CUDA_TIMEOUT);
+            }
         }
     } else {
         // ---------------- epilogue warps (2..9): A split (strict), TMEM drain, epilogue ----------------
@@ -1597,20 +1674,19 @@ inline int launch_best(Params &p, long long m_tiles, cudaStream_t stream) {
     return launch<BN, MODE, 0, 0>(p, (int)(tiles < sms ? tiles : sms), stream);
 }
 
-// Phase-split row tiles (N tiles of 64, TF32): B-resident when the panel fits beside the deep
-// ring of small stages and every CTA walks at least two tiles.
+// Phase-split row tiles (one N tile of 64, TF32, B resident; the caller checked that the panel
+// and a tile's rows fit): one CTA per SM, or one per tile when there are fewer tiles.
 inline int launch_phase(Params &p, long long m_tiles, cudaStream_t stream) {
     using C1 = Cfg<64, TF32, 1, 0, 0, 1>;
+    p.b_res_bytes = (uint32_t)p.num_kb * 2u * C1::B_TILE_BYTES;
     const int sms = sm_count();
-    const uint32_t panel = (uint32_t)p.num_kb * 2u * C1::B_TILE_BYTES;
-    const int per = p.n_tiles <= sms ? sms / p.n_tiles : 0;
-    if (per > 0 && panel <= C1::B_RES_MAX && m_tiles >= 2LL * per) {
-        p.b_res_bytes = panel;
-        return launch<64, TF32, 1, 0, 0, 1>(p, per * p.n_tiles, stream);
-    }
-    p.b_res_bytes = 0;
-    const long long tiles = (long long)p.n_tiles * m_tiles;
-    return launch<64, TF32, 0, 0, 0, 1>(p, (int)(tiles < sms ? tiles : sms), stream);
+    return launch<64, TF32, 1, 0, 0, 1>(p, (int)(m_tiles < sms ? m_tiles : sms), stream);
+}
+
+// Whether a phase-split launch fits: the B panel beside the stages, a tile's rows in a stage.
+inline bool phase_fits(int num_kb, uint32_t row_bytes) {
+    using C1 = Cfg<64, TF32, 1, 0, 0, 1>;
+    return (uint32_t)num_kb * 2u * C1::B_TILE_BYTES <= C1::B_RES_MAX && (uint32_t)num_kb * row_bytes <= PHASE_STAGE_BYTES;
 }
 
 // One CTA per tile with a residual through its own staging buffer (N tiles of 128, TF32), when
@@ -1813,12 +1889,13 @@ inline int try_gemm_umma(const GemmParams &p, cudaStream_t stream, int *taken) {
         }
         if (phase) {
             // the packed rows hold both phases of phase_w pixels of 4 channels (the image's padding
-            // included); every tile row reads pixels m .. m + 3 of each phase, rows past OW too
+            // included); every tile row reads pixels m .. m + 3 of each phase, rows past OW too; a
+            // tile's KH rows are consecutive (unit height dilation) and arrive in one copy
             const long long row_bytes = 2ll * p.phase_w * 16;
-            if (strict || p.C != 4 || p.W != 2 * p.phase_w || p.PT || p.PL || p.SW != 2 || p.DW != 1 || p.KW > 8 ||
+            if (strict || p.C != 4 || p.W != 2 * p.phase_w || p.PT || p.PL || p.SW != 2 || p.DW != 1 || p.DH != 1 || p.KW > 8 ||
                 p.OW > umma::BM || p.phase_w < umma::BM + 4 || p.b_cpad != 4 || p.N > 64 ||
                 (long long)(p.OH - 1) * p.SH + (long long)(p.KH - 1) * p.DH >= p.H ||
-                (reinterpret_cast<uintptr_t>(p.a) & 15) || row_bytes > umma::PHASE_STAGE_BYTES)
+                (reinterpret_cast<uintptr_t>(p.a) & 15) || !umma::phase_fits(p.KH, (uint32_t)row_bytes))
                 return MGC_CUDA_OK;
             u.im2col = 5;
             u.cblocks = 1;

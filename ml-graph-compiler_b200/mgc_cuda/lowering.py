@@ -62,6 +62,7 @@ EW_CODE = {name: i for i, name in enumerate(EW_OPS)}
 EW_MAX_RANK, EW_MAX_LEAVES, EW_MAX_INSTR, COPY_MAX_RANK = 6, 20, 40, 8
 SOFTMAX_ROW_MAX = 1024  # longest row the register-resident softmax holds (kernels_norm.cuh)
 PHASE_TILE_ROWS = 128  # output pixels of one phase-split row tile (the tensor-core M tile)
+PHASE_MAX_KH = 7  # filter rows of a phase-split tile (its packed rows fill one shared-memory stage)
 HEAD_FLOP_SHARE = 0.02  # largest share of a graph's GEMM FLOPs an output head computed in 3xTF32 may have
 _EW_BINARY = {"Add", "Sub", "Mul", "Div", "Pow", "Max", "Min"}
 _EW_FLOAT_ONLY = {"Clip", "Relu", "Sigmoid", "Tanh", "Erf", "Sqrt", "Exp", "Log", "Neg", "Abs", "Reciprocal",
@@ -1471,8 +1472,8 @@ class CudaEmitter:
         row is KW * cp contiguous floats inside the image; ``wrows`` output pixels per TMA box,
         ``L`` the window row rounded up to whole 32-float K blocks.
 
-        ``phase`` (TF32 mode, width stride 2, unit width dilation, at most 4 channels, KW <= 8,
-        OW <= 128, at most 64 output channels: the stems): the image is packed phase-split instead (K_PACK with phases, the
+        ``phase`` (TF32 mode, width stride 2, no dilation, at most 4 channels, KW <= 8,
+        OW <= 128, KH <= 7, at most 64 output channels: the stems): the image is packed phase-split instead (K_PACK with phases, the
         rows padded to Hp, each row holding its even-tap and odd-tap column phases of ``Wq``
         pixels), so that a filter row's window for output pixel m is pixels m..m+3 of each phase;
         a tile is one output row and reads each filter row's packed input row with one bulk
@@ -1487,8 +1488,8 @@ class CudaEmitter:
         wrows = 16 if ow % 16 == 0 else 8 if ow % 8 == 0 else 0
         plan = {"cp": cp, "wrows": 0, "L": 0, "PT": 0, "PL": 0, "Hp": h, "Wp": w, "phase": 0, "Wq": 0}
         hp = max(pt + h, (oh - 1) * g.strides[0] + (kh - 1) * g.dilations[0] + 1)
-        if (self.precision == "tf32" and g.strides[1] == 2 and g.dilations[1] == 1 and cp == 4 and kw <= 8
-                and ow <= PHASE_TILE_ROWS and wt.shape[3] <= 64):
+        if (self.precision == "tf32" and g.strides[1] == 2 and g.dilations == (1, 1) and cp == 4 and kw <= 8
+                and ow <= PHASE_TILE_ROWS and wt.shape[3] <= 64 and kh <= PHASE_MAX_KH):
             wq = PHASE_TILE_ROWS + 4  # tile rows past OW read 3 pixels further, as the last real row does
             plan.update(phase=1, Wq=wq, PT=pt, PL=pl, Hp=hp, Wp=2 * wq)
             return plan
