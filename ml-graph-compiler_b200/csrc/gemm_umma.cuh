@@ -569,8 +569,9 @@ constexpr uint32_t SMEM_LIMIT = 232448;  // dynamic shared memory per block on s
 // buffer, so the next pass's residual loads while this pass's output is stored; SR = 2 runs the
 // epilogue in passes of 64 columns, so that both buffers take the shared memory of one.
 // PH: phase-split row tiles (im2col 5): a stage holds one tile's KH packed input rows (both
-// phases each), brought in by one bulk copy; B stays resident.
-constexpr uint32_t PHASE_STAGE_BYTES = 30720;  // up to 7 packed rows of 4,352 bytes (1024-aligned)
+// phases each), brought in by one bulk copy; B stays resident. Tile rows past OW read past the
+// end of a packed row (into the next row, or the stage's slack): they are never stored.
+constexpr uint32_t PHASE_STAGE_BYTES = 26624;  // 7 packed rows of 3,712 bytes plus slack (1024-aligned)
 template <int BN, int MODE, int RB = 0, int PAIR = 0, int SR = 0, int PH = 0>
 struct Cfg {
     static_assert(!SR || (!PAIR && MODE == TF32), "a separate residual buffer is a one-CTA TF32 form");
@@ -601,7 +602,7 @@ struct Cfg {
     static constexpr uint32_t RES_BYTES = SR ? OUT_BYTES : 0;       // the residual's own staging
     static constexpr uint32_t STAGE_BUDGET = SMEM_LIMIT - OUT_BYTES - RES_BYTES - 1024 - BAR_BYTES - BN * 4;
     static constexpr int MAX_STAGES = 8;
-    static constexpr int STAGES = PH ? 2
+    static constexpr int STAGES = PH ? 3
                                   : RB ? (MODE == STRICT || SR ? 2 : 4)
                                   : (STAGE_BUDGET / STAGE_BYTES) < 2 ? 2
                                   : (int)(STAGE_BUDGET / STAGE_BYTES) > MAX_STAGES ? MAX_STAGES
@@ -1683,10 +1684,12 @@ inline int launch_phase(Params &p, long long m_tiles, cudaStream_t stream) {
     return launch<64, TF32, 1, 0, 0, 1>(p, (int)(m_tiles < sms ? m_tiles : sms), stream);
 }
 
-// Whether a phase-split launch fits: the B panel beside the stages, a tile's rows in a stage.
-inline bool phase_fits(int num_kb, uint32_t row_bytes) {
+// Whether a phase-split launch fits: the B panel beside the stages, and every byte the MMAs read
+// inside a stage (the last K block's odd-tap phase, read at pixel offsets up to BM - 1 + 3).
+inline bool phase_fits(int num_kb, uint32_t row_bytes, uint32_t phase_bytes) {
     using C1 = Cfg<64, TF32, 1, 0, 0, 1>;
-    return (uint32_t)num_kb * 2u * C1::B_TILE_BYTES <= C1::B_RES_MAX && (uint32_t)num_kb * row_bytes <= PHASE_STAGE_BYTES;
+    const uint32_t last = (uint32_t)(num_kb - 1) * row_bytes + phase_bytes + 32 + (BM - 1) * 16 + 32;
+    return (uint32_t)num_kb * 2u * C1::B_TILE_BYTES <= C1::B_RES_MAX && last <= PHASE_STAGE_BYTES;
 }
 
 // One CTA per tile with a residual through its own staging buffer (N tiles of 128, TF32), when
@@ -1889,13 +1892,15 @@ inline int try_gemm_umma(const GemmParams &p, cudaStream_t stream, int *taken) {
         }
         if (phase) {
             // the packed rows hold both phases of phase_w pixels of 4 channels (the image's padding
-            // included); every tile row reads pixels m .. m + 3 of each phase, rows past OW too; a
-            // tile's KH rows are consecutive (unit height dilation) and arrive in one copy
+            // included); output pixel m reads pixels m .. m + 3 of each phase (tile rows past OW
+            // read on into the stage and are never stored); a tile's KH rows are consecutive
+            // (unit height dilation) and arrive in one copy
             const long long row_bytes = 2ll * p.phase_w * 16;
             if (strict || p.C != 4 || p.W != 2 * p.phase_w || p.PT || p.PL || p.SW != 2 || p.DW != 1 || p.DH != 1 || p.KW > 8 ||
-                p.OW > umma::BM || p.phase_w < umma::BM + 4 || p.b_cpad != 4 || p.N > 64 ||
+                p.OW > umma::BM || p.phase_w < p.OW + 3 || p.b_cpad != 4 || p.N > 64 ||
                 (long long)(p.OH - 1) * p.SH + (long long)(p.KH - 1) * p.DH >= p.H ||
-                (reinterpret_cast<uintptr_t>(p.a) & 15) || !umma::phase_fits(p.KH, (uint32_t)row_bytes))
+                (reinterpret_cast<uintptr_t>(p.a) & 15) ||
+                !umma::phase_fits(p.KH, (uint32_t)row_bytes, (uint32_t)p.phase_w * 16))
                 return MGC_CUDA_OK;
             u.im2col = 5;
             u.cblocks = 1;

@@ -1490,7 +1490,7 @@ class CudaEmitter:
         hp = max(pt + h, (oh - 1) * g.strides[0] + (kh - 1) * g.dilations[0] + 1)
         if (self.precision == "tf32" and g.strides[1] == 2 and g.dilations == (1, 1) and cp == 4 and kw <= 8
                 and ow <= PHASE_TILE_ROWS and wt.shape[3] <= 64 and kh <= PHASE_MAX_KH):
-            wq = PHASE_TILE_ROWS + 4  # tile rows past OW read 3 pixels further, as the last real row does
+            wq = (ow + 3 + 3) // 4 * 4  # output pixel m reads pixels m .. m + 3 of each phase
             plan.update(phase=1, Wq=wq, PT=pt, PL=pl, Hp=hp, Wp=2 * wq)
             return plan
         if wrows and g.dilations[1] == 1:

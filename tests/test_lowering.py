@@ -38,17 +38,18 @@ def test_resnet50_o3_matches_published_structure(r50: Graph) -> None:
     assert low.workspace_bytes == 0
     # in TF32 mode the input transpose writes the image phase-split into the workspace: 229 rows
     # (3 of top padding; the last window row ends at row 2 * 111 + 7), each holding the even-tap
-    # and the odd-tap column phases of 132 four-channel pixels, TF32-rounded; the stem reads one
-    # packed row per filter row (B laid out [64][7][32] in that tap order)
+    # and the odd-tap column phases of 116 four-channel pixels (output pixel m reads pixels
+    # m..m+3 of each), TF32-rounded; the stem reads one packed row per filter row (B laid out
+    # [64][7][32] in that tap order)
     tc = lower_graph(r50, precision="tf32")
     assert tc.kernels == {"gemm": 54, "pack": 1, "pool": 1, "reduce": 1, "view": 1}
     assert tc.arena_bytes == 7_225_344
-    assert tc.workspace_bytes == (229 * 264 * 4 * 4 + 255) // 256 * 256
+    assert tc.workspace_bytes == (229 * 232 * 4 * 4 + 255) // 256 * 256
     pack, stem = tc.launches[0], tc.launches[1]
     assert pack.kind == K_PACK
-    assert list(pack.i[:14]) == [1, 224, 224, 3, 4, 3 * 224 * 224, 224, 1, 224 * 224, 3, 3, 229, 264, 2]
-    assert stem.kind == K_GEMM and stem.i[2] == 7 * 7 * 4 and list(stem.i[50:54]) == [4, 0, 0, 132]
-    assert (stem.i[27], stem.i[28], stem.i[29], stem.i[36], stem.i[37]) == (229, 264, 4, 0, 0)
+    assert list(pack.i[:14]) == [1, 224, 224, 3, 4, 3 * 224 * 224, 224, 1, 224 * 224, 3, 3, 229, 232, 2]
+    assert stem.kind == K_GEMM and stem.i[2] == 7 * 7 * 4 and list(stem.i[50:54]) == [4, 0, 0, 116]
+    assert (stem.i[27], stem.i[28], stem.i[29], stem.i[36], stem.i[37]) == (229, 232, 4, 0, 0)
     assert (stem.r[0].space, stem.r[0].offset) == (pack.r[1].space, pack.r[1].offset)
     # strict mode keeps the window-row form: the image with its channels padded to 4 and its
     # 3-pixel border (229 x 229), window rows of 32 floats per filter row
@@ -176,9 +177,9 @@ def test_input_slice_plan_of_resnet50(strategy: str, records: int) -> None:
     stem = low.launches[1]
     assert stem.kind == K_GEMM and low.launches[0].kind == K_PACK
     fields = {(d.what, d.slot): d.per_image for d in descs if d.launch == 1}
-    # M = images * 112 * 112; A = the phase-split image (229 rows of 2 x 132 four-channel
+    # M = images * 112 * 112; A = the phase-split image (229 rows of 2 x 116 four-channel
     # pixels); C = 112 * 112 * 64 floats
-    assert fields == {(1, 0): 112 * 112, (0, 0): 229 * 264 * 4 * 4, (0, 2): 112 * 112 * 64 * 4}
+    assert fields == {(1, 0): 112 * 112, (0, 0): 229 * 232 * 4 * 4, (0, 2): 112 * 112 * 64 * 4}
     assert all(d.launch < prefix for d in descs)
 
 
