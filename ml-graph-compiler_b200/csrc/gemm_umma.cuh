@@ -569,8 +569,9 @@ constexpr uint32_t SMEM_LIMIT = 232448;  // dynamic shared memory per block on s
 // buffer, so the next pass's residual loads while this pass's output is stored; SR = 2 runs the
 // epilogue in passes of 64 columns, so that both buffers take the shared memory of one.
 // PH: phase-split row tiles (im2col 5): a stage holds one tile's KH packed input rows (both
-// phases each), brought in by one bulk copy; B stays resident. Tile rows past OW read past the
-// end of a packed row (into the next row, or the stage's slack): they are never stored.
+// phases each), brought in by one bulk copy; B stays resident as one TF32 plane (N = BN MMAs,
+// one accumulator). Tile rows past OW read past the end of a packed row (into the next row, or
+// the stage's slack): they are never stored.
 constexpr uint32_t PHASE_STAGE_BYTES = 26624;  // 7 packed rows of 3,712 bytes plus slack (1024-aligned)
 template <int BN, int MODE, int RB = 0, int PAIR = 0, int SR = 0, int PH = 0>
 struct Cfg {
@@ -582,11 +583,11 @@ struct Cfg {
     static_assert(BN <= 128 || (WIDE && RB == 0 && BN % 64 == 0 && BN <= 256),
                   "N tiles of 192 and 256 are pair-only, without B residency");
     static_assert(MODE != DYN || (!PAIR && !RB && !SR), "dynamic-B GEMMs run one CTA per tile");
-    static constexpr bool ONEACC = WIDE || MODE == DYN;     // one accumulator (no B_lo columns)
+    static constexpr bool ONEACC = WIDE || MODE == DYN || PH;  // one accumulator (no B_lo columns)
     static constexpr int REGIONS = MODE == STRICT ? 4 : 1;  // TMEM regions per K block
     static constexpr int BROWS = WIDE ? BN / 2 : BN;         // B rows of one plane in this CTA
     static constexpr uint32_t B_TILE_BYTES = BROWS * BK * 4;
-    static constexpr int B_PLANES = (PAIR && !WIDE) || MODE == DYN ? 1 : 2;  // B planes in this CTA's smem
+    static constexpr int B_PLANES = (PAIR && !WIDE) || MODE == DYN || PH ? 1 : 2;  // B planes in this CTA's smem
     static constexpr int TM = PAIR ? 2 * BM : BM;            // rows of one tile
     static constexpr int EN = WIDE || SR == 2 ? 64 : BN;     // columns of one epilogue pass
     static constexpr int NH = BN / EN;                       // epilogue passes per tile
@@ -976,7 +977,7 @@ __global__ void __launch_bounds__(THREADS, 1) umma_gemm_kernel(const __grid_cons
             if (PH) {
                 // phase-split row tiles: one stage per tile, the KH filter rows of the tile in
                 // it (K block kh: packed row kh; steps 0-1 the even-tap phase, 2-3 the odd-tap)
-                constexpr uint32_t idesc_t = instr_desc_tf32(2 * BN);
+                constexpr uint32_t idesc_t = instr_desc_tf32(BN);  // one TF32 plane of B
                 RingPos<S> pos;
                 RingPos<TB> buf;
                 bool ok = true;
@@ -1552,6 +1553,21 @@ inline bool make_map_b(CUtensorMap *map, const float *hi, const float *lo, long 
     return r == CUDA_SUCCESS;
 }
 
+// One K-major plane of a constant B ([N][Kp], TF32-exact) as a 3-D tensor [1][N][Kp], boxes {32,
+// box_rows, 1}: the coordinates the two-plane map takes, with plane 0 only.
+inline bool make_map_b1(CUtensorMap *map, const float *plane, long long rows, long long kp, int box_rows) {
+    auto fn = encode_tiled_fn();
+    if (!fn) return false;
+    cuuint64_t dims[3] = {(cuuint64_t)kp, (cuuint64_t)rows, 1};
+    cuuint64_t strides[2] = {(cuuint64_t)(kp * 4), (cuuint64_t)(rows * kp * 4)};
+    cuuint32_t box[3] = {(cuuint32_t)BK, (cuuint32_t)box_rows, 1};
+    cuuint32_t estr[3] = {1, 1, 1};
+    CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 3, const_cast<float *>(plane), dims, strides, box, estr,
+                    CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                    CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    return r == CUDA_SUCCESS;
+}
+
 // NHWC fp32 image, im2col boxes of `chans` channels x 128 output pixels: 32 channels in 128-byte
 // swizzled rows, or 4 channels in plain 16-byte rows (tap-packed).
 inline bool make_map_im2col(CUtensorMap *map, const GemmParams &g, bool tf32, int chans = BK) {
@@ -1679,7 +1695,7 @@ inline int launch_best(Params &p, long long m_tiles, cudaStream_t stream) {
 // and a tile's rows fit): one CTA per SM, or one per tile when there are fewer tiles.
 inline int launch_phase(Params &p, long long m_tiles, cudaStream_t stream) {
     using C1 = Cfg<64, TF32, 1, 0, 0, 1>;
-    p.b_res_bytes = (uint32_t)p.num_kb * 2u * C1::B_TILE_BYTES;
+    p.b_res_bytes = (uint32_t)p.num_kb * C1::B_PLANES * C1::B_TILE_BYTES;
     const int sms = sm_count();
     return launch<64, TF32, 1, 0, 0, 1>(p, (int)(m_tiles < sms ? m_tiles : sms), stream);
 }
@@ -1689,7 +1705,7 @@ inline int launch_phase(Params &p, long long m_tiles, cudaStream_t stream) {
 inline bool phase_fits(int num_kb, uint32_t row_bytes, uint32_t phase_bytes) {
     using C1 = Cfg<64, TF32, 1, 0, 0, 1>;
     const uint32_t last = (uint32_t)(num_kb - 1) * row_bytes + phase_bytes + 32 + (BM - 1) * 16 + 32;
-    return (uint32_t)num_kb * 2u * C1::B_TILE_BYTES <= C1::B_RES_MAX && last <= PHASE_STAGE_BYTES;
+    return (uint32_t)num_kb * C1::B_PLANES * C1::B_TILE_BYTES <= C1::B_RES_MAX && last <= PHASE_STAGE_BYTES;
 }
 
 // One CTA per tile with a residual through its own staging buffer (N tiles of 128, TF32), when
@@ -1854,13 +1870,16 @@ inline int try_gemm_umma_dyn(const GemmParams &p, cudaStream_t stream, int *take
 inline int try_gemm_umma(const GemmParams &p, cudaStream_t stream, int *taken) {
     *taken = 0;
     if (!p.b_umma) return try_gemm_umma_dyn(p, stream, taken);
-    if (p.precision == MGC_PREC_FP32 || p.nb != 0 || !p.b_umma || !p.b_umma_lo || p.M <= 0 || p.N <= 0 || p.K <= 0)
+    // a constant B in two planes (TF32 part + residual), or one TF32 plane for phase-split tiles
+    if (p.precision == MGC_PREC_FP32 || p.nb != 0 || !p.b_umma || (!p.b_umma_lo && p.phase_w <= 0) || p.M <= 0 ||
+        p.N <= 0 || p.K <= 0)
         return MGC_CUDA_OK;
     if (p.bias && p.bias_mode != 1) return MGC_CUDA_OK;
     const bool strict = p.precision == MGC_PREC_3XTF32;
     if ((reinterpret_cast<uintptr_t>(p.a) & 15) || (reinterpret_cast<uintptr_t>(p.b_umma) & 15) ||
         (reinterpret_cast<uintptr_t>(p.b_umma_lo) & 15))
         return MGC_CUDA_OK;
+    if (p.phase_w > 0 && p.b_umma_lo) return MGC_CUDA_OK;  // phase-split tiles read one TF32 plane
     umma::Params u;
     memset(&u, 0, sizeof u);
     u.M = p.M;
@@ -1946,7 +1965,9 @@ inline int try_gemm_umma(const GemmParams &p, cudaStream_t stream, int *taken) {
     }
     // strict mode keeps four TMEM regions per K block, which fits only N tiles of 64
     const int bn = (strict || p.N <= 64) ? 64 : 128;
-    if (!umma::make_map_b(&u.tmB, p.b_umma, p.b_umma_lo, p.N, kp, bn)) return MGC_CUDA_OK;
+    if (u.im2col == 5 ? !umma::make_map_b1(&u.tmB, p.b_umma, p.N, kp, bn)
+                      : !umma::make_map_b(&u.tmB, p.b_umma, p.b_umma_lo, p.N, kp, bn))
+        return MGC_CUDA_OK;
     u.n_tiles = (int)ceil_div(p.N, bn);
     long long m_tiles = ceil_div(p.M, umma::BM);
     if (u.im2col != 5) u.a_bytes = umma::A_TILE_BYTES;
