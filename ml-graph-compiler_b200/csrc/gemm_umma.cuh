@@ -744,13 +744,24 @@ __global__ void __launch_bounds__(THREADS, 1) umma_gemm_kernel(const __grid_cons
                 for (int kb = 0; kb < num_kb; ++kb) tma_load_3d(b_tile(0, kb), &p.tmB, bres_full, kb * BK, nt * BN, 0);
             }
             const uint32_t bytes = (uint32_t)num_kb * p.a_bytes;
+            // the B-resident walk: M tiles unit, unit + units, ... (one N tile); (image, output
+            // row) advanced without divisions
+            const int step = units, img_step = step / p.rt_per_img, oh_step = step - img_step * p.rt_per_img;
+            int img = unit / p.rt_per_img, oh = unit - img * p.rt_per_img;
             for (int i = 0; tile_at(i, mt, nt); ++i, ++g, pos.advance()) {
                 const int s = pos.slot;
                 if (pos.wrapped && !mbar_wait(&empty[s], pos.phase ^ 1u)) {
                     set_error(p.err, MGC_CUDA_TIMEOUT);
                     break;
                 }
-                const int img = mt / p.rt_per_img, oh = mt - img * p.rt_per_img;
+                if (i > 0) {
+                    img += img_step;
+                    oh += oh_step;
+                    if (oh >= p.rt_per_img) {
+                        oh -= p.rt_per_img;
+                        ++img;
+                    }
+                }
                 mbar_expect_tx(&full[s], bytes);
                 bulk_load(a_tile(s), p.a_rows + ((long long)img * p.prows + (long long)oh * p.SH) * p.prow_bytes, bytes,
                           &full[s]);
@@ -986,7 +997,9 @@ __global__ void __launch_bounds__(THREADS, 1) umma_gemm_kernel(const __grid_cons
                     set_error(p.err, MGC_CUDA_TIMEOUT);
                     ok = false;
                 }
-                for (int i = 0; ok && tile_at(i, mt, nt); ++i, pos.advance()) {
+                // this CTA's tiles (one N tile): unit, unit + units, ... below m_tiles
+                const int my_tiles = unit < p.m_tiles ? (p.m_tiles - 1 - unit) / units + 1 : 0;
+                for (int i = 0; ok && i < my_tiles; ++i, pos.advance()) {
                     const int s = pos.slot, b = buf.slot;
                     if (!mbar_wait(&full[s], pos.phase)) {
                         set_error(p.err, MGC_CUDA_TIMEOUT);
