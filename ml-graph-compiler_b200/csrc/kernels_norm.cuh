@@ -709,6 +709,117 @@ __global__ void __launch_bounds__(256) depthwise_nhwc4_rows_kernel(const __grid_
     }
 }
 
+// NHWC, C % (4 * CG) == 0, KH, KW <= 3, height and width stride S (1 or 2), no dilation, sizes
+// below 2^31: a block computes a tile of TH output rows x TW output columns x CG 4-channel groups
+// (TW * CG = 256 threads). It first copies the tile's input window ((TH - 1) * S + 3 rows x
+// (TW - 1) * S + 3 columns x CG groups, zero outside the image) into shared memory with coalesced
+// 16-byte loads, so every input value crosses L2 once per tile instead of once per tap; then each
+// thread walks one output column's TH rows for one channel group, its 3x3 weights and bias in
+// registers, and, at stride 1, slides a 3-row window of inputs down the column (three shared
+// loads per output row). Same accumulation order as the other depthwise forms (bias, then taps
+// row by row).
+template <int S, int CG>
+struct DwTile {
+    static constexpr int TW = 256 / CG;
+    static constexpr int TH = S == 1 ? 8 : 4;
+    static constexpr int IH = (TH - 1) * S + 3, IW = (TW - 1) * S + 3;
+    static constexpr unsigned SMEM = (unsigned)IH * IW * CG * 16;
+};
+
+template <int S, int CG>
+__global__ void __launch_bounds__(256) depthwise_nhwc4_tile_kernel(const __grid_constant__ DepthwiseParams p,
+                                                                  unsigned row_tiles, unsigned col_tiles,
+                                                                  unsigned chunks) {
+    using T = DwTile<S, CG>;
+    extern __shared__ float4 tile[];  // [IH][IW][CG]
+    const int C4 = p.C >> 2;
+    // block -> (image, row tile, column tile, channel chunk)
+    unsigned b = blockIdx.x;
+    const unsigned chunk = b % chunks;
+    b /= chunks;
+    const unsigned ct = b % col_tiles;
+    b /= col_tiles;
+    const unsigned rt = b % row_tiles;
+    const unsigned n = b / row_tiles;
+    const int oh0 = (int)rt * T::TH, ow0 = (int)ct * T::TW;
+    const int ih0 = oh0 * S - p.PT, iw0 = ow0 * S - p.PL;
+    const int c0 = (int)chunk * CG;  // first 4-channel group of the chunk
+    const float4 *x4 = reinterpret_cast<const float4 *>(p.x);
+    const float4 zero = make_float4(0.f, 0.f, 0.f, 0.f);
+    // 1) the input window: consecutive threads take consecutive (pixel, group) float4s
+    for (unsigned e = threadIdx.x; e < (unsigned)(T::IH * T::IW * CG); e += 256) {
+        const unsigned g = e % CG, pix = e / CG;
+        const int r = (int)(pix / T::IW), c = (int)(pix % T::IW);
+        const int ih = ih0 + r, iw = iw0 + c;
+        tile[e] = (ih >= 0 && ih < p.H && iw >= 0 && iw < p.W)
+                      ? __ldg(x4 + ((size_t)(n * p.H + ih) * p.W + iw) * C4 + c0 + g)
+                      : zero;
+    }
+    // this thread's column and channel group, its weights and bias
+    const int g = (int)(threadIdx.x % CG), col = (int)(threadIdx.x / CG);
+    const float4 *w4 = reinterpret_cast<const float4 *>(p.w);
+    float4 wk[9];
+#pragma unroll
+    for (int t = 0; t < 9; ++t) {
+        const int kh = t / 3, kw = t % 3;
+        wk[t] = (kh < p.KH && kw < p.KW) ? __ldg(w4 + (kh * p.KW + kw) * C4 + c0 + g) : zero;
+    }
+    const float4 bias = p.bias ? __ldg(reinterpret_cast<const float4 *>(p.bias) + c0 + g) : zero;
+    __syncthreads();
+    const int ow = ow0 + col;
+    if (ow >= p.OW) return;
+    auto at = [&](int r, int c) -> float4 { return tile[(r * T::IW + c) * CG + g]; };
+    auto fma4 = [](float4 &a, const float4 v, const float4 k) {
+        a.x = fmaf(v.x, k.x, a.x); a.y = fmaf(v.y, k.y, a.y); a.z = fmaf(v.z, k.z, a.z); a.w = fmaf(v.w, k.w, a.w);
+    };
+    const int cx = col * S;  // the column's first input column in the tile
+    float4 win[3][3];        // stride 1: input rows r .. r + 2 of this column's three taps
+    if (S == 1) {
+#pragma unroll
+        for (int kh = 0; kh < 2; ++kh)
+#pragma unroll
+            for (int kw = 0; kw < 3; ++kw) win[kh + 1][kw] = at(kh, cx + kw);
+    }
+#pragma unroll 1
+    for (int r = 0; r < T::TH; ++r) {
+        const int oh = oh0 + r;
+        if (oh >= p.OH) break;
+        float4 acc = bias;
+        if (S == 1) {
+#pragma unroll
+            for (int kw = 0; kw < 3; ++kw) {
+                win[0][kw] = win[1][kw];
+                win[1][kw] = win[2][kw];
+                win[2][kw] = at(r + 2, cx + kw);
+            }
+#pragma unroll
+            for (int kh = 0; kh < 3; ++kh)
+#pragma unroll
+                for (int kw = 0; kw < 3; ++kw) fma4(acc, win[kh][kw], wk[kh * 3 + kw]);
+        } else {
+#pragma unroll
+            for (int kh = 0; kh < 3; ++kh)
+#pragma unroll
+                for (int kw = 0; kw < 3; ++kw) fma4(acc, at(r * S + kh, cx + kw), wk[kh * 3 + kw]);
+        }
+        const size_t o = (((size_t)n * p.OH + oh) * p.OW + ow) * C4 + c0 + g;
+        if (p.res) {
+            const float4 rr = reinterpret_cast<const float4 *>(p.res)[o];
+            acc.x += rr.x; acc.y += rr.y; acc.z += rr.z; acc.w += rr.w;
+        }
+        if (p.act == MGC_ACT_RELU) {
+            acc.x = fmaxf(acc.x, 0.0f); acc.y = fmaxf(acc.y, 0.0f); acc.z = fmaxf(acc.z, 0.0f); acc.w = fmaxf(acc.w, 0.0f);
+        } else if (p.act == MGC_ACT_CLIP) {
+            acc.x = fminf(fmaxf(acc.x, p.lo), p.hi); acc.y = fminf(fmaxf(acc.y, p.lo), p.hi);
+            acc.z = fminf(fmaxf(acc.z, p.lo), p.hi); acc.w = fminf(fmaxf(acc.w, p.lo), p.hi);
+        } else if (p.act != MGC_ACT_NONE) {
+            acc.x = apply_act(acc.x, p.act, p.lo, p.hi); acc.y = apply_act(acc.y, p.act, p.lo, p.hi);
+            acc.z = apply_act(acc.z, p.act, p.lo, p.hi); acc.w = apply_act(acc.w, p.act, p.lo, p.hi);
+        }
+        reinterpret_cast<float4 *>(p.y)[o] = acc;
+    }
+}
+
 // NHWC, C % 4 == 0, KH, KW <= 3, sizes below 2^31: each thread keeps one 4-channel group (the
 // block size is a multiple of C / 4, so the group never changes along the grid-stride loop) with
 // its bias and up to 3x3 weights in registers, and walks output pixels with 32-bit index

@@ -244,6 +244,21 @@ inline int launch_copy_t(const CopyParams &P, cudaStream_t s) {
     return check_launch("copy_kernel");
 }
 
+// Depthwise convolution in shared-memory tiles (depthwise_nhwc4_tile_kernel): one block per
+// (image, row tile, column tile, channel chunk).
+template <int S, int CG>
+inline int launch_dw_tile(const DepthwiseParams &p, cudaStream_t s) {
+    using T = DwTile<S, CG>;
+    const unsigned row_tiles = (unsigned)ceil_div(p.OH, T::TH), col_tiles = (unsigned)ceil_div(p.OW, T::TW);
+    const unsigned chunks = (unsigned)(p.C / 4 / CG);
+    const long long blocks = (long long)p.N * row_tiles * col_tiles * chunks;
+    if (blocks >= (1ll << 31)) return fail(MGC_CUDA_UNSUPPORTED, "depthwise: %lld tiles", blocks);
+    MGC_CHECK_CUDA(cudaFuncSetAttribute(depthwise_nhwc4_tile_kernel<S, CG>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                        (int)T::SMEM));
+    depthwise_nhwc4_tile_kernel<S, CG><<<(unsigned)blocks, 256, T::SMEM, s>>>(p, row_tiles, col_tiles, chunks);
+    return check_launch("depthwise_nhwc4_tile_kernel");
+}
+
 template <typename T>
 inline int launch_tile_t(const TileParams &P, cudaStream_t s) {
     tile_kernel<T><<<grid_for(P.total, 256), 256, 0, s>>>(P);
@@ -286,6 +301,12 @@ inline int launch_record(const mgc_cuda_launch &L, const int64_t *aux, int64_t a
         const int c4 = p.C / 4;
         const bool reg = vec4 && p.KH <= 3 && p.KW <= 3 && c4 <= 256 &&
                          (long long)p.N * p.H * p.W * c4 < (1ll << 31) && total / 4 < (1ll << 31);
+        if (reg && p.DH == 1 && p.DW == 1 && p.SH == p.SW && (p.SW == 1 || p.SW == 2) && c4 % 4 == 0 && p.OW >= 16) {
+            // shared-memory tiles: the input window of a tile crosses L2 once
+            st = p.SW == 1 ? (c4 % 8 == 0 ? launch_dw_tile<1, 8>(p, stream) : launch_dw_tile<1, 4>(p, stream))
+                           : (c4 % 8 == 0 ? launch_dw_tile<2, 8>(p, stream) : launch_dw_tile<2, 4>(p, stream));
+            break;
+        }
         if (reg && p.DW == 1 && (p.SW == 1 || p.SW == 2)) {
             // four output columns per thread
             const int block = (256 / c4) * c4;

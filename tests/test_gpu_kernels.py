@@ -183,3 +183,26 @@ def test_pool_and_depthwise_vs_torch() -> None:
     ref = torch.nn.functional.conv2d(X.permute(0, 3, 1, 2).double(), W.permute(2, 0, 1).unsqueeze(1).double(),
                                      B.double(), stride=2, padding=1, groups=32).clamp(0, 6).permute(0, 2, 3, 1)
     np.testing.assert_allclose(Y.cpu().numpy(), ref.cpu().numpy(), rtol=1e-5, atol=1e-5)
+
+
+@pytest.mark.parametrize("n,h,w,c,s,act", [(2, 30, 45, 48, 1, 2), (1, 57, 33, 64, 2, 1), (3, 19, 70, 32, 1, 0),
+                                           (2, 40, 36, 16, 2, 2)])
+def test_depthwise_tiles_vs_torch(n: int, h: int, w: int, c: int, s: int, act: int) -> None:
+    """The shared-memory tiled depthwise form (3x3, stride 1 or 2, 16 or more output columns;
+    channel chunks of 32 or 16) against a float64 depthwise convolution, with a residual and
+    ReLU / Clip; sizes that leave partial row, column and channel tiles."""
+    rng = np.random.default_rng(h * w + c)
+    oh, ow = (h + 2 - 3) // s + 1, (w + 2 - 3) // s + 1
+    x = rng.standard_normal((n, h, w, c)).astype(np.float32)
+    wt = (rng.standard_normal((3, 3, c)) * 0.3).astype(np.float32)
+    b = rng.standard_normal(c).astype(np.float32)
+    r = rng.standard_normal((n, oh, ow, c)).astype(np.float32)
+    X, W, B, R = dev(x), dev(wt), dev(b), dev(r)
+    Y = torch.full((n, oh, ow, c), float("nan"), device="cuda")
+    ok(library().mgc_cuda_depthwise_nhwc(n, h, w, c, 3, 3, s, s, 1, 1, 1, 1, oh, ow, ptr(X), ptr(W), ptr(B), ptr(R), act,
+                                         0.0, 6.0, ptr(Y), stream()))
+    torch.cuda.synchronize()
+    ref = torch.nn.functional.conv2d(X.permute(0, 3, 1, 2).double(), W.permute(2, 0, 1).unsqueeze(1).double(),
+                                     B.double(), stride=s, padding=1, groups=c).permute(0, 2, 3, 1) + R.double()
+    ref = {0: ref, 1: ref.relu(), 2: ref.clamp(0, 6)}[act]
+    np.testing.assert_allclose(Y.cpu().numpy(), ref.cpu().numpy(), rtol=1e-5, atol=1e-5)
