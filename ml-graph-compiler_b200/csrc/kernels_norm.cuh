@@ -746,15 +746,22 @@ __global__ void __launch_bounds__(256) depthwise_nhwc4_tile_kernel(const __grid_
     const int c0 = (int)chunk * CG;  // first 4-channel group of the chunk
     const float4 *x4 = reinterpret_cast<const float4 *>(p.x);
     const float4 zero = make_float4(0.f, 0.f, 0.f, 0.f);
-    // 1) the input window: consecutive threads take consecutive (pixel, group) float4s
+    // 1) the input window: consecutive threads take consecutive (pixel, group) float4s, copied
+    // by cp.async (all of a thread's copies in flight at once; a source size of 0 writes zeros
+    // for the pixels outside the image)
+    const uint32_t tile_s = static_cast<uint32_t>(__cvta_generic_to_shared(tile));
+#pragma unroll 4
     for (unsigned e = threadIdx.x; e < (unsigned)(T::IH * T::IW * CG); e += 256) {
         const unsigned g = e % CG, pix = e / CG;
         const int r = (int)(pix / T::IW), c = (int)(pix % T::IW);
         const int ih = ih0 + r, iw = iw0 + c;
-        tile[e] = (ih >= 0 && ih < p.H && iw >= 0 && iw < p.W)
-                      ? __ldg(x4 + ((size_t)(n * p.H + ih) * p.W + iw) * C4 + c0 + g)
-                      : zero;
+        const bool inside = ih >= 0 && ih < p.H && iw >= 0 && iw < p.W;
+        const float4 *src = inside ? x4 + ((size_t)(n * p.H + ih) * p.W + iw) * C4 + c0 + g : x4;
+        asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(tile_s + e * 16u), "l"(src),
+                     "r"(inside ? 16 : 0)
+                     : "memory");
     }
+    asm volatile("cp.async.wait_all;" ::: "memory");
     // this thread's column and channel group, its weights and bias
     const int g = (int)(threadIdx.x % CG), col = (int)(threadIdx.x / CG);
     const float4 *w4 = reinterpret_cast<const float4 *>(p.w);
