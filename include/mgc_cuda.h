@@ -110,10 +110,14 @@ enum {
     MGC_K_IM2COL = 15,      /* explicit im2col of an NHWC image into the workspace, for
                                convolutions whose channel rows TMA cannot address (C % 4 != 0);
                                the packing of pack_a's MGC_CONV_NHWC branch, mgc_kernels.c:103-126 */
-    MGC_K_PACK = 16         /* copy of a 4-D image with any strides into NHWC with the channels
+    MGC_K_PACK = 16,        /* copy of a 4-D image with any strides into NHWC with the channels
                                zero-padded to a multiple of 4, so that TMA can address its pixels
                                (a narrow-channel convolution input, e.g. the 3-channel stem); no
                                counterpart in the reference, whose C kernels read 3-float rows */
+    MGC_K_ATTENTION = 17    /* TF32 mode: MatMul(Q, K^T) -> score program (scale, mask) ->
+                               Softmax -> MatMul(P, V) as one tcgen05 kernel, the scores kept
+                               on chip; the reference's C backend runs the four nodes as
+                               separate loops (c.py:823-852, 974-1226) */
 };
 
 typedef struct {
@@ -203,9 +207,9 @@ int mgc_cuda_profile(void *handle, double *per_node_ms, int n);
 /* Number of kernel launches in one replay of the handle's graph. */
 int mgc_cuda_launch_count(void *handle);
 
-/* Which kernel computes each GEMM-family launch record (FusedConv, FusedGemm, Gemm, MatMul) of
- * the handle's graphs: per_record[k] for record k < n is MGC_CUDA_PATH_NONE for a record of
- * another kind, MGC_CUDA_PATH_TCGEN05 when the tcgen05 tensor-core kernel runs it, and
+/* Which kernel computes each GEMM-family launch record (FusedConv, FusedGemm, Gemm, MatMul, and
+ * the fused attention of MGC_K_ATTENTION, whose two products run on tcgen05) of the handle's
+ * graphs: per_record[k] for record k < n is MGC_CUDA_PATH_NONE for a record of another kind, MGC_CUDA_PATH_TCGEN05 when the tcgen05 tensor-core kernel runs it, and
  * MGC_CUDA_PATH_SIMT when the exact-fp32 CUDA-core kernel does (fp32 precision, or a problem
  * the tensor-core forms cannot describe). No counterpart in the reference, whose C backend has
  * one GEMM kernel; the reference's CompileReport.kernels (runtime_lib.py:31-41) counts kernels

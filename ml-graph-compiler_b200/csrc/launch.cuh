@@ -7,6 +7,7 @@
 
 #include "common.cuh"
 #include "gemm_simt.cuh"
+#include "attention.cuh"
 #include "gemm_umma.cuh"
 #include "kernels_mem.cuh"
 #include "kernels_norm.cuh"
@@ -361,6 +362,24 @@ inline int launch_record(const mgc_cuda_launch &L, const int64_t *aux, int64_t a
         if (total == 0) { launched = 0; break; }
         reduce_mid_kernel<<<grid_for(total, 256), 256, 0, stream>>>((int)i[0], i[1], i[2], i[3], x, y);
         st = check_launch("reduce_mid_kernel");
+        break;
+    }
+    case MGC_K_ATTENTION: {
+        // fused softmax(program(Q K^T)) V: slots documented at CudaEmitter._emit_attention
+        attn::AttnArgs a{};
+        a.nb1 = (int)i[0]; a.nb2 = (int)i[1]; a.sq = (int)i[2]; a.sk = (int)i[3]; a.dqk = (int)i[4]; a.dv = (int)i[5];
+        a.q_rs = i[6]; a.q_b1 = i[7]; a.q_b2 = i[8];
+        a.k_mn = (int)i[9]; a.k_rs = i[10]; a.k_b1 = i[11]; a.k_b2 = i[12];
+        a.v_mn = (int)i[13]; a.v_rs = i[14]; a.v_b1 = i[15]; a.v_b2 = i[16];
+        a.o_rs = i[17]; a.o_b1 = i[18]; a.o_b2 = i[19];
+        a.mode = (int)i[20]; a.div = (int)i[21]; a.mask_dt = (int)i[22];
+        a.m_b1 = i[23]; a.m_b2 = i[24]; a.m_q = i[25]; a.m_s = i[26];
+        a.scale = (float)L.f[0]; a.lit = (float)L.f[1];
+        MGC_RESOLVE(L.r[0], a.q); MGC_RESOLVE(L.r[1], a.k); MGC_RESOLVE(L.r[2], a.v);
+        MGC_RESOLVE(L.r[3], a.o); MGC_RESOLVE(L.r[4], a.mask);
+        a.err = status_dev;
+        st = attn::launch_attention(a, stream);
+        gemm.gemm_path = MGC_CUDA_PATH_TCGEN05;
         break;
     }
     case MGC_K_SOFTMAX: {

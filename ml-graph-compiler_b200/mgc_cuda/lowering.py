@@ -43,11 +43,12 @@ PACKED_REGION = 1  # workspace reference index of a packed image until its offse
 PRECISIONS = {"fp32": 0, "tf32": 1, "strict": 2}
 K_GEMM, K_DEPTHWISE, K_POOL, K_REDUCE_MID, K_SOFTMAX, K_LAYER_NORM = 1, 2, 3, 4, 5, 6
 K_ELEMENTWISE, K_COPY, K_FILL, K_GATHER, K_REDUCE, K_ARGMAX, K_RANGE, K_MEMCPY, K_IM2COL, K_PACK = range(7, 17)
+K_ATTENTION = 17
 KIND_NAMES = {
     K_GEMM: "gemm", K_DEPTHWISE: "depthwise", K_POOL: "pool", K_REDUCE_MID: "reduce",
     K_SOFTMAX: "softmax", K_LAYER_NORM: "layer_norm", K_ELEMENTWISE: "elementwise",
     K_COPY: "copy", K_FILL: "fill", K_GATHER: "gather", K_REDUCE: "reduce", K_ARGMAX: "argmax",
-    K_RANGE: "range", K_MEMCPY: "memcpy", K_IM2COL: "im2col", K_PACK: "pack",
+    K_RANGE: "range", K_MEMCPY: "memcpy", K_IM2COL: "im2col", K_PACK: "pack", K_ATTENTION: "attention",
 }
 LAUNCH_INTS, LAUNCH_FLOATS, LAUNCH_REFS = 64, 8, 8
 # Elementwise program operations, numbered as csrc/kernels_mem.cuh EwOp.
@@ -61,6 +62,18 @@ EW_OPS = [
 EW_CODE = {name: i for i, name in enumerate(EW_OPS)}
 EW_MAX_RANK, EW_MAX_LEAVES, EW_MAX_INSTR, COPY_MAX_RANK = 6, 20, 40, 8
 SOFTMAX_ROW_MAX = 1024  # longest row the register-resident softmax holds (kernels_norm.cuh)
+# fused attention (csrc/attention.cuh): keys per row, head widths, shared memory per CTA
+ATTN_MAX_SK, ATTN_MAX_D, ATTN_SMEM_LIMIT = 256, 128, 232448 - 1024
+ATTN_NONE, ATTN_ADD, ATTN_SUB, ATTN_KEEP, ATTN_FILL = range(5)  # score program masks (attention.cuh)
+
+
+def _attn_fits(sk: int, dqk: int, dv: int) -> bool:
+    """Whether the fused attention kernel takes these extents (attention.cuh attn_fits)."""
+    if not (1 <= sk <= ATTN_MAX_SK and 4 <= dqk <= ATTN_MAX_D and 4 <= dv <= ATTN_MAX_D) or dqk % 4 or dv % 4:
+        return False
+    skp, dqp, dvp = (-(-x // 32) * 32 for x in (sk, dqk, dv))
+    region0 = max(skp * 512, dqp * 512 + skp * dqp * 4, dvp * 512)
+    return 1024 + region0 + skp * dvp * 4 <= ATTN_SMEM_LIMIT
 PHASE_TILE_ROWS = 128  # output pixels of one phase-split row tile (the tensor-core M tile)
 PHASE_MAX_KH = 7  # filter rows of a phase-split tile (its packed rows fill one shared-memory stage)
 HEAD_FLOP_SHARE = 0.02  # largest share of a graph's GEMM FLOPs an output head computed in 3xTF32 may have
@@ -308,6 +321,10 @@ class CudaEmitter:
         # id(value) -> aux words of the elementwise program that the softmax reading it evaluates
         self._row_programs: dict[int, list[int]] = {}
         self._heads = self._output_heads()  # nodes computed in 3xTF32 in TF32 mode
+        # fused attention chains (_attention_plan): id(second MatMul) -> its K_ATTENTION record
+        # (ints, floats, refs), and the ids of the nodes the record absorbs
+        self._attn_emit: dict[int, tuple[list[int], list[float], list[RefT]]] = {}
+        self._attn_skip: set[int] = set()
 
     # -- references ----------------------------------------------------------------------------
     def _root(self, value: Value) -> Value:
@@ -373,6 +390,9 @@ class CudaEmitter:
 
     # -- dispatch ------------------------------------------------------------------------------------
     def node(self, node: Node) -> None:
+        if id(node) in self._attn_skip:
+            self.kernels["fused into attention"] = self.kernels.get("fused into attention", 0) + 1
+            return
         if node.op in ALIAS_OPS:
             if node.op == "Dropout" and len(node.outputs) > 1:
                 mask = node.outputs[1]
@@ -1204,12 +1224,14 @@ class CudaEmitter:
             return self.ref(value), list(self._stored[id(value)])
         return self.ref(value), _strides(value.tensor_type.shape)
 
-    def _write_through(self, node: Node) -> tuple[RefT, int, list[int]] | None:
+    def _write_through(self, node: Node, reads: list[Value] | None = None,
+                       mark: bool = True) -> tuple[RefT, int, list[int]] | None:
         """Where a batched MatMul whose only reader is a Transpose keeping the last axis in place
         (attention's (b, h, s, d) -> (b, s, h, d) before the output projection) writes its product
         straight into the Transpose's output, through strides: (reference, row stride, batch
-        strides), and the Transpose emits nothing. Only when the Transpose runs right after the
-        MatMul and its output memory is clear of everything the MatMul reads."""
+        strides), and the Transpose emits nothing (once ``mark``ed). Only when the Transpose runs
+        right after the MatMul and its output memory is clear of everything the MatMul reads
+        (``reads``: by default its operands and the sources they are read through)."""
         out = node.output
         rank = out.tensor_type.rank
         if rank < 3 or len(out.users) != 1 or any(v is out for _, v in self.graph.named_outputs()):
@@ -1228,8 +1250,9 @@ class CudaEmitter:
         order = {id(n): k for k, n in enumerate(self.graph.nodes)}
         if any(n.op not in ALIAS_OPS for n in self.graph.nodes[order[id(node)] + 1 : order[id(user)]]):
             return None
-        reads = [node.input(0), node.input(1)]
-        reads += [self._through[id(v)][0] for v in reads if id(v) in self._through]
+        if reads is None:
+            reads = [node.input(0), node.input(1)]
+            reads += [self._through[id(v)][0] for v in reads if id(v) in self._through]
         for v in reads:
             r = self._arena_range(v)
             if r is not None and r[0] < dst[1] and dst[0] < r[1]:
@@ -1238,10 +1261,245 @@ class CudaEmitter:
         cstrides = [0] * rank
         for j, p in enumerate(perm):
             cstrides[p] = tstrides[j]
-        self._written_through.add(id(user))
+        if mark:
+            self._written_through.add(id(user))
         return self.ref(user.output), cstrides[-2], cstrides[:-2]
 
+    # -- fused attention ------------------------------------------------------------------------------
+    def _score_program(self, enode: Node, scores: Value) -> tuple[int, float, int, Value | None, float] | None:
+        """The score program of ``enode`` on ``scores`` in the form the fused attention kernel
+        evaluates (attention.cuh score_program; the unfused softmax's ScaleMask form,
+        kernels_norm.cuh): t = X * s, s * X or X / s (s an fp32 scalar constant), then optionally
+        t + M, M + t or t - M (M an fp32 tensor), Where(C, t, lit) or Where(C, lit, t) (C a bool /
+        uint8 tensor, lit an fp32 scalar constant). Returns (div, s, mode, M or C, lit) or None.
+        The reference's fusion pass (passes/fusion.py) builds these programs from attention's
+        Div / Mul, Add and Where nodes."""
+        if enode.op == "FusedElementwise":
+            program = [(str(op), [int(x) for x in args]) for op, _, args in enode.attrs["program"]]
+        else:
+            program = [(enode.op, list(range(len(enode.inputs))))]
+        leaves = list(enode.inputs)
+        nl = len(leaves)
+        if not 1 <= len(program) <= 2 or sum(1 for v in leaves if v is scores) != 1:
+            return None
+
+        def scalar(a: int) -> float | None:
+            v = leaves[a] if 0 <= a < nl else None
+            if v is None or not v.is_constant or v.tensor_type.dtype != "float32" or v.tensor_type.size != 1:
+                return None
+            return float(np.float32(self.const_data(v).reshape(())))
+
+        def tensor(a: int, dtypes: tuple[str, ...]) -> Value | None:
+            v = leaves[a] if 0 <= a < nl else None
+            if v is None or v is scores or v.tensor_type.dtype not in dtypes or v.tensor_type.size == 0:
+                return None
+            if v.is_constant and v.tensor_type.size == 1:
+                return None
+            return v
+
+        def is_x(a: int) -> bool:
+            return 0 <= a < nl and leaves[a] is scores
+
+        op0, a0 = program[0]
+        if len(a0) != 2:
+            return None
+        if op0 == "Mul" and is_x(a0[0]) and scalar(a0[1]) is not None:
+            div, scale = 0, scalar(a0[1])
+        elif op0 == "Mul" and is_x(a0[1]) and scalar(a0[0]) is not None:
+            div, scale = 0, scalar(a0[0])
+        elif op0 == "Div" and is_x(a0[0]) and scalar(a0[1]) is not None:
+            div, scale = 1, scalar(a0[1])
+        else:
+            return None
+        if len(program) == 1:
+            return div, float(scale), ATTN_NONE, None, 0.0  # type: ignore[arg-type]
+        op1, a1 = program[1]
+        t = nl  # the register of the first instruction's result
+        if op1 == "Add" and len(a1) == 2 and t in a1:
+            m = tensor(a1[1] if a1[0] == t else a1[0], ("float32",))
+            return None if m is None else (div, float(scale), ATTN_ADD, m, 0.0)  # type: ignore[arg-type]
+        if op1 == "Sub" and len(a1) == 2 and a1[0] == t:
+            m = tensor(a1[1], ("float32",))
+            return None if m is None else (div, float(scale), ATTN_SUB, m, 0.0)  # type: ignore[arg-type]
+        if op1 == "Where" and len(a1) == 3:
+            c = tensor(a1[0], ("bool", "uint8"))
+            if c is not None and a1[1] == t and scalar(a1[2]) is not None:
+                return div, float(scale), ATTN_KEEP, c, scalar(a1[2])  # type: ignore[return-value]
+            if c is not None and a1[2] == t and scalar(a1[1]) is not None:
+                return div, float(scale), ATTN_FILL, c, scalar(a1[1])  # type: ignore[return-value]
+        return None
+
+    def _attention_plan(self, m1: Node) -> bool:
+        """Whether this MatMul starts an attention chain that one K_ATTENTION record computes
+        (TF32 mode): MatMul(Q, K^T) -> [score program, _score_program] -> Softmax over the last
+        axis -> MatMul(P, V), every intermediate read only by the next node and no graph output,
+        the same batch shape throughout, Sk <= 256 and head widths <= 128 (multiples of 4), Q
+        and the output with a contiguous head width, K and V with either axis contiguous. The
+        record (built now, while the views of Q, K and V are known) is emitted at the second
+        MatMul, where its output memory is free; it reads Q, K and the mask later than the
+        unfused nodes would, so nothing scheduled in between may write their memory, and its
+        output (through the head-merge Transpose when there is one) must lie clear of everything
+        it reads."""
+        if self.precision != "tf32":
+            return False
+        a, b = m1.input(0), m1.input(1)
+        at, bt = a.tensor_type, b.tensor_type
+        if at.rank < 3 or bt.rank != at.rank or at.dtype != "float32" or bt.dtype != "float32":
+            return False
+        batch = [int(d) for d in at.shape[:-2]]
+        if [int(d) for d in bt.shape[:-2]] != batch:
+            return False
+        outs = {id(v) for _, v in self.graph.named_outputs()}
+
+        def single(v: Value) -> bool:
+            return len(v.users) == 1 and id(v) not in outs
+
+        s = m1.output
+        if not single(s):
+            return False
+        nxt = s.users[0]
+        div, scale, mode, mask, lit = 0, 1.0, ATTN_NONE, None, 0.0
+        enode = None
+        if nxt.op != "Softmax":
+            if nxt.op != "FusedElementwise" and not ops.is_elementwise(nxt.op):
+                return False
+            prog = self._score_program(nxt, s)
+            e_out = nxt.output
+            if prog is None or not single(e_out) or e_out.tensor_type.dtype != "float32" or \
+                    tuple(e_out.tensor_type.shape) != tuple(s.tensor_type.shape):
+                return False
+            div, scale, mode, mask, lit = prog
+            enode, nxt = nxt, e_out.users[0]
+        sm = nxt
+        rank = s.tensor_type.rank
+        if sm.op != "Softmax" or _axis_attr(sm, rank, -1) != rank - 1:
+            return False
+        p = sm.output
+        if not single(p):
+            return False
+        m2 = p.users[0]
+        if m2.op != "MatMul" or m2.input(0) is not p or m2.input(1) is p:
+            return False
+        v = m2.input(1)
+        vt = v.tensor_type
+        if vt.rank != at.rank or vt.dtype != "float32" or [int(d) for d in vt.shape[:-2]] != batch:
+            return False
+        sq, dqk = (int(d) for d in at.shape[-2:])
+        sk, dv = int(bt.shape[-1]), int(vt.shape[-1])
+        if int(bt.shape[-2]) != dqk or int(vt.shape[-2]) != sk or sq < 1 or not _attn_fits(sk, dqk, dv):
+            return False
+        order = {id(n): k for k, n in enumerate(self.graph.nodes)}
+        if v.producer is not None and order.get(id(v.producer), len(order)) > order[id(m1)]:
+            return False  # V's view is not known yet
+        (qref, qv), (kref, kv), (vref, vv) = self._view(a), self._view(b), self._view(v)
+        if qv[-1] != 1:
+            return False
+        if kv[-2] == 1:
+            k_mn, k_rs = 0, kv[-1]
+        elif kv[-1] == 1:
+            k_mn, k_rs = 1, kv[-2]
+        else:
+            return False
+        if vv[-1] == 1:
+            v_mn, v_rs = 1, vv[-2]
+        elif vv[-2] == 1:
+            v_mn, v_rs = 0, vv[-1]
+        else:
+            return False
+
+        def source(val: Value) -> Value:
+            return self._through[id(val)][0] if id(val) in self._through else val
+
+        sources = [source(a), source(b), source(v)] + ([mask] if mask is not None else [])
+        # nothing scheduled between the two MatMuls (the absorbed nodes write nothing) may write
+        # what the record reads
+        skip = {id(sm)} | ({id(enode)} if enode is not None else set())
+        ranges = [r for r in (self._arena_range(x) for x in sources) if r is not None]
+        for later in self.graph.nodes[order[id(m1)] + 1 : order[id(m2)]]:
+            if later.op in ALIAS_OPS or id(later) in skip:
+                continue
+            for w in later.outputs:
+                r = self._arena_range(w)
+                if r is not None and any(r[0] < hi and lo < r[1] for lo, hi in ranges):
+                    return False
+        through = self._write_through(m2, reads=[], mark=False)
+        if through is not None:
+            oref, o_rs, o_bs = through
+            o_value = m2.output.users[0].output
+        else:
+            ost = _strides(m2.output.tensor_type.shape)
+            oref, o_rs, o_bs = self.ref(m2.output), ost[-2], ost[:-2]
+            o_value = m2.output
+        dst = self._arena_range(o_value)
+        if dst is not None:
+            # The output may lie exactly on an operand it replaces element for element (the same
+            # reference and strides): each CTA reads its rows of that operand whole before it
+            # writes the same bytes, and no other CTA reads them (Q always; K or V only with one
+            # query tile, whose rows are then all the keys). Any other overlap is refused.
+            one_tile = sq == sk and sq <= 128 and dqk == dv
+            same = [(source(a), qref, qv[-2], list(qv[:-2]), dqk == dv),
+                    (source(b), kref, k_rs, list(kv[:-2]), one_tile and k_mn == 0),
+                    (source(v), vref, v_rs, list(vv[:-2]), one_tile and v_mn == 1)]
+            if mask is not None:
+                same.append((mask, NO_REF, 0, [], False))
+            for val, xref, xrs, xbs, allowed in same:
+                r = self._arena_range(val)
+                if r is None or not (r[0] < dst[1] and dst[0] < r[1]):
+                    continue
+                if not (allowed and xref == oref and xrs == o_rs and xbs == list(o_bs)):
+                    return False
+                if sum(1 for other, *_ in same if other is val) > 1:
+                    return False  # another operand read from the same buffer
+        if any(ref[2] % 16 for ref in (qref, kref, vref, oref)):
+            return False
+        m_full = _broadcast_strides(mask.tensor_type.shape, s.tensor_type.shape) if mask is not None \
+            else [0] * rank
+        dims, (qb, kb, vb, ob, mb) = _collapse(batch, [list(qv[:-2]), list(kv[:-2]), list(vv[:-2]), list(o_bs),
+                                                      m_full[:-2]])
+        if len(dims) > 2:
+            return False
+        for st in (qv[-2], k_rs, v_rs, o_rs, *qb, *kb, *vb, *ob):
+            if st <= 0 or st % 4:
+                return False
+
+        def inner_outer(strides: list[int]) -> tuple[int, int]:
+            # (b1, b2): the kernel's inner and outer batch dimensions
+            return (strides[-1], strides[0] if len(strides) == 2 else 0) if strides else (0, 0)
+
+        nb1 = dims[-1] if dims else 1
+        nb2 = dims[0] if len(dims) == 2 else 1
+        ints = [nb1, nb2, sq, sk, dqk, dv,
+                qv[-2], *inner_outer(qb),
+                k_mn, k_rs, *inner_outer(kb),
+                v_mn, v_rs, *inner_outer(vb),
+                o_rs, *inner_outer(ob),
+                mode, div, DTYPES[mask.tensor_type.dtype] if mask is not None else 0,
+                *inner_outer(mb), m_full[-2], m_full[-1]]
+        refs = [qref, kref, vref, oref, self.ref(mask) if mask is not None else NO_REF]
+        if through is not None:
+            self._write_through(m2, reads=[], mark=True)
+        self._attn_emit[id(m2)] = (ints, [scale, lit], refs)
+        self._attn_skip.update(skip)
+        return True
+
+    def _emit_attention(self, node: Node) -> None:
+        """K_ATTENTION slots (csrc/launch.cuh): i[0] nb1 (inner batch extent), i[1] nb2 (outer),
+        i[2] Sq, i[3] Sk, i[4] Dqk, i[5] Dv; element strides of rows and of the inner / outer
+        batch dimension: Q i[6..8]; K i[9] 1 when Sk is its contiguous axis (K^T stored with
+        the keys contiguous), i[10..12]; V i[13] 1 when Dv is contiguous, i[14..16]; output
+        i[17..19] (Dv contiguous); score program i[20] mask mode (ATTN_*), i[21] 1 for X / s,
+        i[22] mask dtype, mask strides i[23] b1, i[24] b2, i[25] query, i[26] key; f[0] s,
+        f[1] the Where literal; r[0] Q, r[1] K, r[2] V, r[3] output, r[4] mask."""
+        ints, floats, refs = self._attn_emit.pop(id(node))
+        self.emit(K_ATTENTION, ints, floats, refs, count="attention")
+
     def op_MatMul(self, node: Node) -> None:
+        if id(node) in self._attn_emit:
+            self._emit_attention(node)
+            return
+        if self._attention_plan(node):
+            self.kernels["fused into attention"] = self.kernels.get("fused into attention", 0) + 1
+            return
         a, b = node.input(0), node.input(1)
         at, bt = a.tensor_type, b.tensor_type
         self._require_f32(node, at)

@@ -140,15 +140,19 @@ def test_gpt2_b16_tf32(golden_models: dict) -> None:
                                                   ("gpt2", 16, "greedy_by_size")])
 def test_transformer_gemms_run_on_tensor_cores(name: str, batch: int, strategy: str) -> None:
     """Every GEMM-family record of BERT-base (the benchmark's batch 32 on its naive plan, and
-    batch 1) and GPT-2 (batch 16) runs on tcgen05 in TF32 mode."""
+    batch 1) and GPT-2 (batch 16) runs on tcgen05 in TF32 mode: per layer the projections and the
+    FFN (BERT: Q, K, V, output, two FFN; GPT-2: QKV, output, two FFN) and one fused attention
+    record (its two products)."""
     g = prepared(getattr(zoo, name), batch=batch, seq=128)
     m = compile_graph(g, precision="tf32", strategy=strategy)
     try:
         paths = gemm_kernels(m)
+        kernels = dict(m.lowered.kernels)
     finally:
         m.close()
     assert not paths["simt"], paths["simt"]
-    assert len(paths["tcgen05"]) >= 12 * 6
+    assert kernels.get("attention") == 12
+    assert len(paths["tcgen05"]) >= 12 * ((6 if name == "bert" else 4) + 1)
 
 
 @pytest.mark.parametrize("name", ["resnet50", "mobilenet_v2", "bert", "gpt2"])

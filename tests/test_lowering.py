@@ -75,13 +75,19 @@ def test_workspace_regions_do_not_overlap() -> None:
 
 
 def test_same_kernel_mix_and_arena_as_the_c_backend() -> None:
+    """The same arena and kernel mix as the reference's C backend; in TF32 mode each fused
+    attention record stands for two of its GEMMs and its softmax."""
     for make in (lambda: zoo.tiny_cnn(batch=2), lambda: zoo.tiny_transformer(kind="gpt"), zoo.mlp):
         g = o3(make())
-        ours = lower_graph(g)
         theirs = generate_c(g)
-        assert ours.arena_bytes == max(theirs.arena_bytes, 64)
-        for kind in ("gemm", "depthwise", "pool", "softmax", "layer_norm", "gather"):
-            assert ours.kernels.get(kind, 0) == theirs.kernels.get(kind, 0), kind
+        for precision in ("strict", "tf32"):
+            ours = lower_graph(g, precision=precision)
+            assert ours.arena_bytes == max(theirs.arena_bytes, 64)
+            fused = ours.kernels.get("attention", 0)
+            assert fused == 0 or precision == "tf32"
+            for kind in ("gemm", "depthwise", "pool", "softmax", "layer_norm", "gather"):
+                per = {"gemm": 2, "softmax": 1}.get(kind, 0)
+                assert ours.kernels.get(kind, 0) + per * fused == theirs.kernels.get(kind, 0), kind
 
 
 def test_every_arena_reference_stays_inside_the_arena(r50: Graph) -> None:
@@ -153,13 +159,20 @@ def test_algorithmic_cost_of_resnet50(r50: Graph) -> None:
 
 def test_tensor_core_b_planes_are_ordered(r50: Graph) -> None:
     """The kernel loads B's TF32 part and residual as the two planes of one 3-D tensor map, which
-    needs the residual stored after the TF32 part at a 16-byte multiple."""
+    needs the residual stored after the TF32 part at a 16-byte multiple. A phase-split stem
+    (i[53] > 0, TF32 mode) reads one TF32-rounded plane and has no residual."""
     for precision in ("tf32", "strict"):
         low = lower_graph(r50, precision=precision)
+        single = 0
         for rec in low.launches:
             if rec.kind == lowering.K_GEMM and rec.r[6].space == lowering.SPACE_WEIGHTS:
+                if rec.i[53] > 0:
+                    assert precision == "tf32" and rec.r[7].space == lowering.SPACE_NONE
+                    single += 1
+                    continue
                 gap = rec.r[7].offset - rec.r[6].offset
                 assert gap > 0 and gap % 16 == 0
+        assert single == (1 if precision == "tf32" else 0)
 
 
 @pytest.mark.parametrize("strategy,records", [("greedy_by_size", 3), ("naive", 14)])
@@ -190,16 +203,107 @@ def test_input_slice_plan_needs_a_batch() -> None:
 
 @pytest.mark.parametrize("name", ["bert", "gpt2"])
 def test_attention_scale_and_mask_run_inside_the_softmax(name: str) -> None:
-    """Every layer's score scale + mask program (BERT: additive fp32 mask; GPT-2: causal bool mask
-    through Where) is evaluated by the softmax that reads it: no K_ELEMENTWISE record for it, and
-    one K_SOFTMAX record per layer carrying the program."""
+    """Strict mode (no fused attention): every layer's score scale + mask program (BERT: additive
+    fp32 mask; GPT-2: causal bool mask through Where) is evaluated by the softmax that reads it:
+    no K_ELEMENTWISE record for it, and one K_SOFTMAX record per layer carrying the program."""
     g = getattr(zoo, name)(batch=2, seq=128)
     optimize(g, "O3")
     schedule(g)
-    low = lower_graph(g)
+    low = lower_graph(g, precision="strict")
     assert low.kernels.get("elementwise into softmax") == 12
+    assert "attention" not in low.kernels
     soft = [r for r in low.launches if r.kind == lowering.K_SOFTMAX]
     assert len(soft) == 12 and all(r.i[4] == 1 and r.aux_len > 0 for r in soft)
+
+
+def _attn_spans(rec) -> dict[str, tuple[int, int, tuple]]:
+    """Arena byte range and layout (offset, row stride, batch strides) of each operand of a
+    K_ATTENTION record (slots documented at CudaEmitter._emit_attention)."""
+    i = [int(x) for x in rec.i[:27]]
+    nb1, nb2, sq, sk, dqk, dv = i[:6]
+    batch = [(nb1, i[7]), (nb2, i[8])]
+    shapes = {
+        "q": (0, [(sq, i[6]), (dqk, 1), (nb1, i[7]), (nb2, i[8])], 4),
+        "k": (1, [(dqk if i[9] else sk, i[10]), (sk if i[9] else dqk, 1), (nb1, i[11]), (nb2, i[12])], 4),
+        "v": (2, [(sk if i[13] else dv, i[14]), (dv if i[13] else sk, 1), (nb1, i[15]), (nb2, i[16])], 4),
+        "o": (3, [(sq, i[17]), (dv, 1), (nb1, i[18]), (nb2, i[19])], 4),
+        "mask": (4, [(nb1, i[23]), (nb2, i[24]), (sq, i[25]), (sk, i[26])], 1 if i[22] in (5, 6) else 4),
+    }
+    del batch
+    out = {}
+    for name, (slot, dims, esize) in shapes.items():
+        if rec.r[slot].space != lowering.SPACE_ARENA:
+            continue
+        last = sum((e - 1) * abs(st) for e, st in dims)
+        lo = rec.r[slot].offset
+        out[name] = (lo, lo + (last + 1) * esize, (lo, dims[0][1], dims[2][1], dims[3][1]))
+    return out
+
+
+@pytest.mark.parametrize("name,batch", [("bert", 2), ("gpt2", 2), ("tiny_transformer", 3)])
+@pytest.mark.parametrize("strategy", ["greedy_by_size", "naive"])
+def test_attention_is_one_record_per_layer_in_tf32(name: str, batch: int, strategy: str) -> None:
+    """TF32 mode: each layer's MatMul(Q, K^T) -> scale / mask -> Softmax -> MatMul(P, V) is one
+    K_ATTENTION record (no softmax, no score GEMMs), and its output lies clear of every operand
+    it reads, or exactly on Q, K or V with their layout (each CTA reads its rows of that operand
+    before it writes the same bytes)."""
+    kw = {"seq": 128} if name != "tiny_transformer" else {}
+    g = getattr(zoo, name)(batch=batch, **kw)
+    optimize(g, "O3")
+    schedule(g)
+    low = lower_graph(g, precision="tf32", strategy=strategy)
+    layers = 2 if name == "tiny_transformer" else 12
+    att = [r for r in low.launches if r.kind == lowering.K_ATTENTION]
+    assert len(att) == layers and "softmax" not in low.kernels
+    assert low.kernels.get("fused into attention") == 3 * layers  # Q K^T, score program, softmax
+    for rec in att:
+        spans = _attn_spans(rec)
+        o = spans.get("o")
+        if o is None:
+            continue
+        for which in ("q", "k", "v", "mask"):
+            r = spans.get(which)
+            if r is None or not (r[0] < o[1] and o[0] < r[1]):
+                continue
+            assert which != "mask" and r[2] == o[2], f"attention of node {rec.node} writes over its {which}"
+            if which != "q":
+                assert rec.i[2] <= 128  # one query tile
+
+
+def test_attention_record_slots_of_bert_and_gpt2() -> None:
+    """The record of BERT's layer (Q, K, V read through the projections' [b, s, h * d] outputs,
+    the output written through the head merge, scores * 0.125 + the fp32 mask [b, 1, 1, s]) and
+    of GPT-2's (Q, K, V read through the fused QKV output's [b, s, 3 * h * d] rows, the causal
+    mask as Where(upper, fmin, t) over a bool [1, 1, s, s] constant)."""
+    got = {}
+    for name in ("bert", "gpt2"):
+        g = getattr(zoo, name)(batch=2, seq=128)
+        optimize(g, "O3")
+        schedule(g)
+        low = lower_graph(g, precision="tf32", strategy="naive")
+        got[name] = next(r for r in low.launches if r.kind == lowering.K_ATTENTION)
+    bert, gpt2 = got["bert"], got["gpt2"]
+    seq = 128 * 768
+    assert list(bert.i[:27]) == [12, 2, 128, 128, 64, 64, 768, 64, seq, 0, 768, 64, seq, 1, 768, 64, seq,
+                                 768, 64, seq, lowering.ATTN_ADD, 0, 0, 0, 128, 0, 1]
+    assert list(bert.f[:2]) == [0.125, 0.0]
+    row = 3 * 768
+    assert list(gpt2.i[:27]) == [12, 2, 128, 128, 64, 64, row, 64, 128 * row, 0, row, 64, 128 * row, 1, row, 64,
+                                 128 * row, 768, 64, seq, lowering.ATTN_FILL, 0, 6, 0, 0, 128, 1]
+    assert gpt2.f[0] == 0.125 and gpt2.f[1] == float(np.finfo(np.float32).min)
+    # Q, K and V: column offsets 0, 768 and 1536 of the same rows
+    assert gpt2.r[1].offset - gpt2.r[0].offset == 768 * 4 and gpt2.r[2].offset - gpt2.r[1].offset == 768 * 4
+
+
+def test_attention_stays_unfused_where_the_kernel_does_not_apply() -> None:
+    """Strict and fp32 modes keep the unfused nodes (their products are exact-fp32 or 3xTF32); so
+    do rows longer than the kernel's 256 keys."""
+    for precision in ("strict", "fp32"):
+        g = o3(zoo.tiny_transformer(batch=2))
+        assert "attention" not in lower_graph(g, precision=precision).kernels
+    g = o3(zoo.tiny_transformer(batch=1, seq=320))
+    low = lower_graph(g, precision="tf32")
+    assert "attention" not in low.kernels and low.kernels.get("softmax") == 2
 
 
 def _gemm_span(rec, which: str) -> tuple[int, int] | None:
