@@ -46,6 +46,9 @@ struct GemmParams {
     // the even-tap and the odd-tap column phases of `phase_w` 4-channel pixels each (K_PACK with
     // phases); B is [N][KH][32] in the matching tap order. 0: not used
     int phase_w;
+    // phase-split convolution followed by a 3x3 / stride-2 / pad-1 max pooling computed in its
+    // epilogue: the pooled output's rows and columns (c is then the pooled output); 0: no pooling
+    int pool_ph, pool_pw;
     int *err;                     // device word for bounded-wait timeouts (may be NULL)
     // split-K scratch of the model (NULL: no split): room for the partial tiles
     float *split_ws;

@@ -112,6 +112,11 @@ struct Params {
     // splits <= 1: no split.
     int splits, kb_per;
     float *part;
+    // phase-split row tiles with the 3x3 / stride-2 / pad-1 max pooling in the epilogue (pool_bp
+    // > 0): CTA b walks bands b, b + gridDim.x, ... of pool_bp pooled rows; a band's tiles are
+    // its 2 pool_bp + 1 output rows from 2 p0 - 1 (the row above the image is a dummy tile);
+    // c is the pooled output [image][pool_ph][pool_pw][ldc]
+    int pool_bp, pool_nbp, pool_nbands, pool_ph, pool_pw;
 };
 
 // ---- PTX wrappers -----------------------------------------------------------------------------
@@ -573,6 +578,7 @@ constexpr uint32_t SMEM_LIMIT = 232448;  // dynamic shared memory per block on s
 // one accumulator). Tile rows past OW read past the end of a packed row (into the next row, or
 // the stage's slack): they are never stored.
 constexpr uint32_t PHASE_STAGE_BYTES = 26624;  // 7 packed rows of 3,712 bytes plus slack (1024-aligned)
+constexpr int POOL_PER_THREAD = 4;             // pooled bands: pooled columns per epilogue thread (PW <= 64)
 template <int BN, int MODE, int RB = 0, int PAIR = 0, int SR = 0, int PH = 0>
 struct Cfg {
     static_assert(!SR || (!PAIR && MODE == TF32), "a separate residual buffer is a one-CTA TF32 form");
@@ -686,6 +692,12 @@ __global__ void __launch_bounds__(THREADS, 1) umma_gemm_kernel(const __grid_cons
     // the i-th work unit of this CTA (or pair) as (M tile, N tile, split); false past the last
     auto unit_at = [&](int i, int &mt, int &nt, int &ks) -> bool {
         ks = 0;
+        if (PH && p.pool_bp > 0) {  // pooled bands: mt is the band
+            const int band = unit + (i / (2 * p.pool_bp + 1)) * units;
+            nt = 0;
+            mt = band;
+            return band < p.pool_nbands;
+        }
         if (RB) {
             const int per = units / p.n_tiles;
             nt = unit % p.n_tiles;
@@ -702,6 +714,16 @@ __global__ void __launch_bounds__(THREADS, 1) umma_gemm_kernel(const __grid_cons
     auto tile_at = [&](int i, int &mt, int &nt) -> bool {
         int ks;
         return unit_at(i, mt, nt, ks);
+    };
+    // pooled bands: tile i's image and output row (-1: the dummy row above the image), and
+    // whether it is its band's first
+    auto pool_row = [&](int i, int &img, int &oh, bool &first) {
+        const int rows = 2 * p.pool_bp + 1;
+        const int bj = i / rows, r = i - bj * rows;
+        const int band = unit + bj * units;
+        img = band / p.pool_nbp;
+        oh = 2 * (band - img * p.pool_nbp) * p.pool_bp - 1 + r;
+        first = r == 0;
     };
 
     if (threadIdx.x == 0) {
@@ -754,7 +776,11 @@ __global__ void __launch_bounds__(THREADS, 1) umma_gemm_kernel(const __grid_cons
                     set_error(p.err, MGC_CUDA_TIMEOUT);
                     break;
                 }
-                if (i > 0) {
+                if (p.pool_bp > 0) {  // pooled bands (the dummy row loads row 0; never stored)
+                    bool first;
+                    pool_row(i, img, oh, first);
+                    if (oh < 0) oh = 0;
+                } else if (i > 0) {
                     img += img_step;
                     oh += oh_step;
                     if (oh >= p.rt_per_img) {
@@ -997,8 +1023,11 @@ __global__ void __launch_bounds__(THREADS, 1) umma_gemm_kernel(const __grid_cons
                     set_error(p.err, MGC_CUDA_TIMEOUT);
                     ok = false;
                 }
-                // this CTA's tiles (one N tile): unit, unit + units, ... below m_tiles
-                const int my_tiles = unit < p.m_tiles ? (p.m_tiles - 1 - unit) / units + 1 : 0;
+                // this CTA's tiles (one N tile): unit, unit + units, ... below m_tiles; pooled,
+                // the rows of its bands unit, unit + units, ...
+                const int my_tiles = p.pool_bp > 0
+                    ? (unit < p.pool_nbands ? ((p.pool_nbands - 1 - unit) / units + 1) * (2 * p.pool_bp + 1) : 0)
+                    : unit < p.m_tiles ? (p.m_tiles - 1 - unit) / units + 1 : 0;
                 for (int i = 0; ok && i < my_tiles; ++i, pos.advance()) {
                     const int s = pos.slot, b = buf.slot;
                     if (!mbar_wait(&full[s], pos.phase)) {
@@ -1152,6 +1181,8 @@ __global__ void __launch_bounds__(THREADS, 1) umma_gemm_kernel(const __grid_cons
         // first); TF32 mode accumulates in fp32
         using AccT = typename std::conditional<MODE == STRICT, double, float>::type;
         AccT acc[HALF];
+        // pooled bands: this thread's running maxima of the pooled row being built
+        float4 pool_acc[PH ? POOL_PER_THREAD : 1];
         // hand TMEM buffer b back to the MMA warp (a pair: one arrival per warp, on rank 0's barrier)
         auto release = [&](int b) {
             tc_fence_before();
@@ -1380,7 +1411,45 @@ __global__ void __launch_bounds__(THREADS, 1) umma_gemm_kernel(const __grid_cons
                     *slot = o;
                 }
             }
-            if (direct) {
+            if (PH && p.pool_bp > 0) {
+                // 3x3 / stride-2 / pad-1 max pooling of the output rows, in order: thread et keeps
+                // channels 4 (et % 16) .. + 3 of pooled columns et / 16, + 16, ... (PW <= 64); a
+                // pooled row ph is complete at output row 2 ph + 1 (padding: -inf, never the
+                // maximum)
+                epilogue_sync();
+                int img, oh;
+                bool first;
+                pool_row(i, img, oh, first);
+                const int c4 = (et & 15) * 4, pw0 = et >> 4;
+                const bool live_c = c4 < p.N;
+                if (oh < 0) {
+#pragma unroll
+                    for (int k = 0; k < POOL_PER_THREAD; ++k)
+                        pool_acc[k] = make_float4(-INFINITY, -INFINITY, -INFINITY, -INFINITY);
+                } else {
+                    const int mode = first ? 0 : (oh & 1) ? 2 : 1;  // 0 start, 1 accumulate, 2 complete
+                    float *orow = p.c + ((long long)img * p.pool_ph + (oh >> 1)) * p.pool_pw * p.ldc + c4;
+                    auto mx4 = [](float4 a, float4 b) {
+                        return make_float4(fmaxf(a.x, b.x), fmaxf(a.y, b.y), fmaxf(a.z, b.z), fmaxf(a.w, b.w));
+                    };
+#pragma unroll
+                    for (int k = 0; k < POOL_PER_THREAD; ++k) {
+                        const int pw = pw0 + 16 * k;
+                        if (pw >= p.pool_pw || !live_c) continue;
+                        float4 h = mx4(*stage_slot(2 * pw, c4), *stage_slot(2 * pw + 1, c4));
+                        if (pw > 0) h = mx4(h, *stage_slot(2 * pw - 1, c4));
+                        if (mode == 0) {
+                            pool_acc[k] = h;
+                        } else if (mode == 1) {
+                            pool_acc[k] = mx4(pool_acc[k], h);
+                        } else {
+                            *reinterpret_cast<float4 *>(orow + (long long)pw * p.ldc) = mx4(pool_acc[k], h);
+                            pool_acc[k] = h;
+                        }
+                    }
+                }
+                epilogue_sync();  // the next tile may overwrite the staging tile
+            } else if (direct) {
                 epilogue_sync();
 #pragma unroll 1
                 for (int rr = 0; rr < 32; ++rr) {
@@ -2020,7 +2089,36 @@ inline int try_gemm_umma(const GemmParams &p, cudaStream_t stream, int *taken) {
     }
     // Phase-split row tiles: one output row per tile (its output and residual through 4-D maps
     // that clip the tile's rows past OW), A read by bulk copies of packed rows.
-    if (u.im2col == 5) {
+    if (u.im2col == 5 && p.pool_ph > 0) {
+        // with the 3x3 / stride-2 / pad-1 max pooling in the epilogue: one N tile, even output
+        // extents, the pooled image stored by the epilogue threads (no output map, no residual).
+        // Bands of bp pooled rows cost 2 bp + 1 tiles each (one output row shared with the band
+        // above, recomputed); bp is the divisor of the pooled height with the fewest tiles on the
+        // busiest CTA (batch 256 at 56 pooled rows: bp 14, 7 bands per CTA, 203 tiles).
+        const long long nimg = (long long)p.M / ((long long)p.OH * p.OW);
+        if (p.N > 64 || (p.N & 3) || p.res || p.OH != 2 * p.pool_ph || p.OW != 2 * p.pool_pw ||
+            p.pool_pw > 16 * umma::POOL_PER_THREAD || p.ldc < p.N || (p.ldc & 3) ||
+            (reinterpret_cast<uintptr_t>(p.c) & 15) || nimg * p.pool_ph > 0x7FFFFFFF)
+            return MGC_CUDA_OK;
+        const long long sms = sm_count();
+        int best = 0;
+        long long best_cost = 0;
+        for (int bp = 1; bp <= p.pool_ph; ++bp) {
+            if (p.pool_ph % bp) continue;
+            const long long cost = ceil_div(nimg * (p.pool_ph / bp), sms) * (2 * bp + 1);
+            if (best == 0 || cost <= best_cost) { best = bp; best_cost = cost; }
+        }
+        u.tma_out = 0;
+        u.tma_res = 0;
+        u.rt_rows = 1;
+        u.rt_per_img = p.OH;
+        u.pool_bp = best;
+        u.pool_nbp = p.pool_ph / best;
+        u.pool_nbands = (int)(nimg * u.pool_nbp);
+        u.pool_ph = p.pool_ph;
+        u.pool_pw = p.pool_pw;
+        m_tiles = u.pool_nbands;  // the launch's grid: one CTA per band at most
+    } else if (u.im2col == 5) {
         const long long nimg = (long long)p.M / ((long long)p.OH * p.OW);
         CUtensorMap c4, r4;
         if (!u.tma_out || !umma::make_map_rows(&c4, p.c, p.N, p.ldc, p.OW, p.OH, nimg, 1) ||
@@ -2032,6 +2130,8 @@ inline int try_gemm_umma(const GemmParams &p, cudaStream_t stream, int *taken) {
         u.rt_per_img = p.OH;
         m_tiles = nimg * p.OH;
         u.res_box_bytes = (uint32_t)p.OW * 128;
+    } else if (p.pool_ph > 0) {
+        return MGC_CUDA_OK;  // pooling runs only in the phase-split epilogue
     }
     u.m_tiles = (int)m_tiles;
     // CTA pairs (256-row tiles, B planes split between the two CTAs: a third less shared-memory

@@ -80,9 +80,10 @@ inline int run_gemm(const GemmParams &p, cudaStream_t stream, LaunchInfo *info =
         info->gemm_path = taken > 0 ? MGC_CUDA_PATH_TCGEN05 : MGC_CUDA_PATH_SIMT;
     }
     if (taken) return MGC_CUDA_OK;
-    if (p.phase_w > 0)  // a phase-split packed image is no NHWC operand for the exact-fp32 kernel
+    if (p.phase_w > 0 || p.pool_ph > 0)  // a phase-split packed image is no NHWC operand for the
+                                           // exact-fp32 kernel, which has no pooling epilogue either
         return fail(MGC_CUDA_UNSUPPORTED, "gemm: the tensor-core kernel declined a phase-split convolution "
-                                          "(M %d, N %d, OW %d)", p.M, p.N, p.OW);
+                                          "(M %d, N %d, OW %d, pooled %d x %d)", p.M, p.N, p.OW, p.pool_ph, p.pool_pw);
     return launch_gemm_simt(p, stream);
 }
 
@@ -115,6 +116,7 @@ inline int decode_gemm(const mgc_cuda_launch &L, const Bases &bases, GemmParams 
     p.b_cpad = (int)i[50];
     p.win_rows = (int)i[51]; p.win_L = (int)i[52];
     p.phase_w = (int)i[53];
+    p.pool_ph = (int)i[54]; p.pool_pw = (int)i[55];
     if (!p.a || !p.b || !p.c) return fail(MGC_CUDA_BAD_ARGUMENT, "gemm: missing operand");
     return MGC_CUDA_OK;
 }

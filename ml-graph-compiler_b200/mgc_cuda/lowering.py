@@ -20,6 +20,7 @@ from __future__ import annotations
 
 import ctypes
 import math
+import os
 import struct
 from collections.abc import Sequence
 from dataclasses import dataclass, field
@@ -325,6 +326,8 @@ class CudaEmitter:
         # (ints, floats, refs), and the ids of the nodes the record absorbs
         self._attn_emit: dict[int, tuple[list[int], list[float], list[RefT]]] = {}
         self._attn_skip: set[int] = set()
+        # MaxPool nodes computed in the epilogue of the convolution before them (_pooled_by)
+        self._pool_skip: set[int] = set()
 
     # -- references ----------------------------------------------------------------------------
     def _root(self, value: Value) -> Value:
@@ -392,6 +395,9 @@ class CudaEmitter:
     def node(self, node: Node) -> None:
         if id(node) in self._attn_skip:
             self.kernels["fused into attention"] = self.kernels.get("fused into attention", 0) + 1
+            return
+        if id(node) in self._pool_skip:
+            self.kernels["pool fused into convolution"] = self.kernels.get("pool fused into convolution", 0) + 1
             return
         if node.op in ALIAS_OPS:
             if node.op == "Dropout" and len(node.outputs) > 1:
@@ -1128,6 +1134,7 @@ class CudaEmitter:
         win_rows: int = 0,
         win_L: int = 0,
         phase_w: int = 0,
+        pool: tuple[int, int] = (0, 0),
     ) -> None:
         """K_GEMM slots: i[0..2] M, N, K; i[3] batch dims; i[4..7] batch extents; i[8..11],
         i[12..15], i[16..19], i[20..23] per-dimension batch strides of A, B, C, residual;
@@ -1138,14 +1145,17 @@ class CudaEmitter:
         B is plain K-major). i[51] output pixels per window-row box and i[52] the padded window-row
         length L when the tensor-core B is laid out [N][KH][L] over a spatially padded image (0
         otherwise). i[53] pixels per phase of a phase-split packed image row (A is such an image
-        and B is [N][KH][32] in phase-split tap order; 0 otherwise). f[0..3] alpha, beta, clip lo,
+        and B is [N][KH][32] in phase-split tap order; 0 otherwise). i[54], i[55] the rows and
+        columns of the 3x3 / stride-2 / pad-1 max pooling computed in a phase-split convolution's
+        epilogue (C is then the pooled image; 0 otherwise). f[0..3] alpha, beta, clip lo,
         clip hi. r[0] A, r[1] B, r[2] C,
         r[3] bias, r[4] residual, r[5] residual of a split constant B, r[6] / r[7] the
         tensor-core layout of a constant B (TF32-rounded part / residual), absent otherwise."""
         if len(batch) > 4:
             raise CodegenError(f"GEMM with {len(batch)} batch dimensions")
-        ints = [0] * 54
+        ints = [0] * 56
         ints[50], ints[51], ints[52], ints[53] = b_cpad, win_rows, win_L, phase_w
+        ints[54], ints[55] = pool
         ints[0], ints[1], ints[2], ints[3] = m, n, k, len(batch)
         for d in range(len(batch)):
             ints[4 + d] = batch[d]
@@ -1792,6 +1802,7 @@ class CudaEmitter:
         bref, blo, b_rs, b_cs = self._kmajor_b(wpad.reshape(kh * kw * cp, kg), ("tap-packed", wkey))
         umma = {"b_umma": bref, "b_umma_lo": blo}
         conv = {**geo, "C": cp, "c_off": 0, "cg": cp}
+        out_ref = self.ref(node.output)
         if plan["phase"]:
             # the packed image holds the padding; its rows are the two phases of Wq pixels each
             conv.update(H=plan["Hp"], W=plan["Wp"], PT=0, PL=0)
@@ -1808,6 +1819,11 @@ class CudaEmitter:
             if key not in self.weights.by_key:
                 self.weights.add(tf32_split(np.ascontiguousarray(rows.reshape(kh * 32, kg).T))[0], key=key)
             umma = {"b_umma": (SPACE_WEIGHTS, 0, self.weights.by_key[key]), "phase_w": plan["Wq"]}
+            pool = self._pooled_by(node, res)
+            if pool is not None:
+                out_ref = self.ref(pool.output)
+                umma["pool"] = (geo["OH"] // 2, geo["OW"] // 2)
+                self._pool_skip.add(id(pool))
         elif window:
             # the image is read from its padded copy: no padding left for the kernels to apply
             conv.update(H=plan["Hp"], W=plan["Wp"], PT=0, PL=0)
@@ -1818,9 +1834,43 @@ class CudaEmitter:
             umma = {"b_umma": uhi, "b_umma_lo": ulo, "win_rows": plan["wrows"], "win_L": plan["L"]}
         m = nb * geo["OH"] * geo["OW"]
         self._gemm(
-            m, kg, kh * kw * cp, xref, cp, 1, bref, b_rs, b_cs, self.ref(node.output), kg, b_lo=blo,
+            m, kg, kh * kw * cp, xref, cp, 1, bref, b_rs, b_cs, out_ref, kg, b_lo=blo,
             conv=conv, a_kind=CONV_NHWC, bias=bias, bias_mode=1, res=res, ldr=kg, act=act, b_cpad=cp, **umma,
         )
+
+    def _pooled_by(self, node: Node, res: RefT) -> Node | None:
+        """The MaxPool that a phase-split convolution computes in its epilogue (the stem's 3x3 /
+        stride-2 / pad-1 max pooling: reference c.py:1228-1253 lowers it as its own loop), or None.
+        It must be the convolution output's only reader, come next in the schedule (only views
+        between), work in NHWC on even output extents, with at most 64 output channels and no
+        residual; the convolution's output then never reaches memory. The pooled output's memory is
+        written when the convolution runs: nothing else is live there then, since every value live
+        at the convolution but not at the pool is one of its inputs, and a phase-split convolution
+        reads its image from the workspace copy."""
+        out = node.output
+        if os.environ.get("MGC_CUDA_POOL_FUSION") == "0":  # the separate MaxPool kernel (measurements)
+            return None
+        if res != NO_REF or len(out.users) != 1 or any(v is out for _, v in self.graph.named_outputs()):
+            return None
+        pool = out.users[0]
+        if pool.op != "MaxPool" or pool.input(0) is not out or ops.conv_layout(pool) != "NHWC":
+            return None
+        if len(pool.outputs) > 1 and any(v is not None and (v.users or any(v is o for _, o in self.graph.named_outputs()))
+                                         for v in pool.outputs[1:]):
+            return None
+        nb, oh, ow, c = (int(d) for d in out.tensor_type.shape)
+        if c > 64 or oh % 2 or ow % 2 or [int(k) for k in pool.attrs.get("kernel_shape", [])] != [3, 3]:
+            return None
+        g = ops.window_geometry(pool, (oh, ow), (3, 3), bool(pool.attrs.get("ceil_mode", 0)))
+        if tuple(g.strides) != (2, 2) or tuple(g.dilations) != (1, 1) or tuple(g.pads) != (1, 1, 1, 1) or \
+                tuple(g.out_hw) != (oh // 2, ow // 2) or int(pool.attrs.get("storage_order", 0)):
+            return None
+        if tuple(int(d) for d in pool.output.tensor_type.shape) != (nb, oh // 2, ow // 2, c):
+            return None
+        order = {id(n): k for k, n in enumerate(self.graph.nodes)}
+        if any(n.op not in ALIAS_OPS for n in self.graph.nodes[order[id(node)] + 1 : order[id(pool)]]):
+            return None
+        return pool
 
     # -- pooling (c.py:1228-1253) ---------------------------------------------------------------------
     def _pool(self, node: Node, is_max: int) -> None:
@@ -1942,7 +1992,9 @@ def _slice_fields(rec: Launch, images: int, per: int) -> list[tuple[int, int, in
             a_img = h * w * c * 4
         else:
             return None
-        out = [(1, 0, oh * ow), (0, 0, a_img), (0, 2, oh * ow * i[44] * 4)]
+        # C per image: the output image, or the pooled one its epilogue writes
+        c_img = (i[54] * i[55] if i[54] > 0 else oh * ow) * i[44] * 4
+        out = [(1, 0, oh * ow), (0, 0, a_img), (0, 2, c_img)]
         if r[4].space != SPACE_NONE:
             out.append((0, 4, oh * ow * i[46] * 4))
         return out

@@ -63,6 +63,28 @@ def test_model_logits_within_budget(case: cases.Case, precision: str, prepared: 
         assert float(np.abs(got[name].reshape(-1)[: head.size] - head).max()) <= BUDGET[precision] * 1.01
 
 
+@pytest.mark.parametrize("batch", [1, 5, 33])
+def test_stem_pooling_in_the_epilogue_is_exact(batch: int, monkeypatch: pytest.MonkeyPatch) -> None:
+    """TF32 ResNet-50: the stem convolution computing the 3x3 / stride-2 MaxPool in its epilogue
+    (bands of pooled rows per CTA; batch 1, 5 and 33 take different band heights) gives the
+    logits of the separate MaxPool kernel bit for bit: the pooling is a maximum of the same
+    values. MGC_CUDA_POOL_FUSION=0 selects the separate kernel."""
+    g = zoo.resnet50(batch=batch, seed=0)
+    optimize(g, "O3")
+    schedule(g)
+    x = {"image": np.random.default_rng(batch).standard_normal((batch, 3, 224, 224)).astype(np.float32)}
+    got = {}
+    for flag in ("1", "0"):
+        monkeypatch.setenv("MGC_CUDA_POOL_FUSION", flag)
+        m = compile_graph(g, precision="tf32")
+        try:
+            assert ("pool" in m.lowered.kernels) == (flag == "0"), m.lowered.kernels
+            got[flag] = m.run(x)["logits"]
+        finally:
+            m.close()
+    np.testing.assert_array_equal(got["1"], got["0"])
+
+
 def test_resnet50_batch_is_independent_per_image() -> None:
     """Size-independent property at a larger batch: every image of a batch-8 run equals the
     batch-1 model's output for that image (strict mode, bit-level batch independence is not

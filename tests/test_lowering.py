@@ -40,15 +40,20 @@ def test_resnet50_o3_matches_published_structure(r50: Graph) -> None:
     # (3 of top padding; the last window row ends at row 2 * 111 + 7), each holding the even-tap
     # and the odd-tap column phases of 116 four-channel pixels (output pixel m reads pixels
     # m..m+3 of each), TF32-rounded; the stem reads one packed row per filter row (B laid out
-    # [64][7][32] in that tap order)
+    # [64][7][32] in that tap order) and computes the 3x3 / stride-2 MaxPool in its epilogue,
+    # writing the pooled 56 x 56 image where the MaxPool's output lives
     tc = lower_graph(r50, precision="tf32")
-    assert tc.kernels == {"gemm": 54, "pack": 1, "pool": 1, "reduce": 1, "view": 1}
+    assert tc.kernels == {"gemm": 54, "pack": 1, "pool fused into convolution": 1, "reduce": 1, "view": 1}
     assert tc.arena_bytes == 7_225_344
     assert tc.workspace_bytes == (229 * 232 * 4 * 4 + 255) // 256 * 256
     pack, stem = tc.launches[0], tc.launches[1]
     assert pack.kind == K_PACK
     assert list(pack.i[:14]) == [1, 224, 224, 3, 4, 3 * 224 * 224, 224, 1, 224 * 224, 3, 3, 229, 232, 2]
-    assert stem.kind == K_GEMM and stem.i[2] == 7 * 7 * 4 and list(stem.i[50:54]) == [4, 0, 0, 116]
+    assert stem.kind == K_GEMM and stem.i[2] == 7 * 7 * 4 and list(stem.i[50:56]) == [4, 0, 0, 116, 56, 56]
+    pool = next(n for n in r50.nodes if n.op == "MaxPool")
+    assert (stem.r[2].space, stem.r[2].offset) == (lowering.SPACE_ARENA, CudaEmitter(r50, "greedy_by_size", True,
+                                                   "tf32").plan.location(pool.output).index)
+    assert not any(r.kind == lowering.K_POOL for r in tc.launches)
     assert (stem.i[27], stem.i[28], stem.i[29], stem.i[36], stem.i[37]) == (229, 232, 4, 0, 0)
     assert (stem.r[0].space, stem.r[0].offset) == (pack.r[1].space, pack.r[1].offset)
     # strict mode keeps the window-row form: the image with its channels padded to 4 and its
@@ -56,7 +61,8 @@ def test_resnet50_o3_matches_published_structure(r50: Graph) -> None:
     st = lower_graph(r50, precision="strict")
     pack, stem = st.launches[0], st.launches[1]
     assert list(pack.i[:14]) == [1, 224, 224, 3, 4, 3 * 224 * 224, 224, 1, 224 * 224, 3, 3, 229, 229, 0]
-    assert list(stem.i[50:54]) == [4, 16, 32, 0]
+    assert list(stem.i[50:56]) == [4, 16, 32, 0, 0, 0]  # strict: MaxPool stays a kernel of its own
+    assert sum(r.kind == lowering.K_POOL for r in st.launches) == 1
     assert (stem.i[27], stem.i[28], stem.i[29], stem.i[36], stem.i[37]) == (229, 229, 4, 0, 0)
 
 
@@ -76,7 +82,8 @@ def test_workspace_regions_do_not_overlap() -> None:
 
 def test_same_kernel_mix_and_arena_as_the_c_backend() -> None:
     """The same arena and kernel mix as the reference's C backend; in TF32 mode each fused
-    attention record stands for two of its GEMMs and its softmax."""
+    attention record stands for two of its GEMMs and its softmax, and a MaxPool computed in its
+    convolution's epilogue for that pool."""
     for make in (lambda: zoo.tiny_cnn(batch=2), lambda: zoo.tiny_transformer(kind="gpt"), zoo.mlp):
         g = o3(make())
         theirs = generate_c(g)
@@ -85,9 +92,12 @@ def test_same_kernel_mix_and_arena_as_the_c_backend() -> None:
             assert ours.arena_bytes == max(theirs.arena_bytes, 64)
             fused = ours.kernels.get("attention", 0)
             assert fused == 0 or precision == "tf32"
+            pooled = ours.kernels.get("pool fused into convolution", 0)
+            assert pooled == 0 or precision == "tf32"
             for kind in ("gemm", "depthwise", "pool", "softmax", "layer_norm", "gather"):
                 per = {"gemm": 2, "softmax": 1}.get(kind, 0)
-                assert ours.kernels.get(kind, 0) + per * fused == theirs.kernels.get(kind, 0), kind
+                extra = pooled if kind == "pool" else 0
+                assert ours.kernels.get(kind, 0) + per * fused + extra == theirs.kernels.get(kind, 0), kind
 
 
 def test_every_arena_reference_stays_inside_the_arena(r50: Graph) -> None:
@@ -175,12 +185,12 @@ def test_tensor_core_b_planes_are_ordered(r50: Graph) -> None:
         assert single == (1 if precision == "tf32" else 0)
 
 
-@pytest.mark.parametrize("strategy,records", [("greedy_by_size", 3), ("naive", 14)])
+@pytest.mark.parametrize("strategy,records", [("greedy_by_size", 4), ("naive", 13)])
 def test_input_slice_plan_of_resnet50(strategy: str, records: int) -> None:
-    """The sliced prefix at batch 256: pack, stem and MaxPool under the default plan (the
-    planner then reuses the stem's memory for layer1 buffers of other layouts that later slices
-    would overwrite); with private buffers (naive) layer1 and the first layer2 convolution too,
-    up to the first GEMM whose slice has too few rows."""
+    """The sliced prefix at batch 256: pack, the stem with its pooling and the first two layer1
+    convolutions under the default plan (the planner then reuses memory for layer1 buffers of
+    other layouts that later slices would overwrite); with private buffers (naive) layer1 and the
+    first layer2 convolution too, up to the first GEMM whose slice has too few rows."""
     g = o3(zoo.resnet50(batch=256))
     low = lower_graph(g, strategy, True, "tf32")
     plan = lowering.input_slice_plan(low, 4)
@@ -191,8 +201,8 @@ def test_input_slice_plan_of_resnet50(strategy: str, records: int) -> None:
     assert stem.kind == K_GEMM and low.launches[0].kind == K_PACK
     fields = {(d.what, d.slot): d.per_image for d in descs if d.launch == 1}
     # M = images * 112 * 112; A = the phase-split image (229 rows of 2 x 116 four-channel
-    # pixels); C = 112 * 112 * 64 floats
-    assert fields == {(1, 0): 112 * 112, (0, 0): 229 * 232 * 4 * 4, (0, 2): 112 * 112 * 64 * 4}
+    # pixels); C = the pooled image, 56 * 56 * 64 floats
+    assert fields == {(1, 0): 112 * 112, (0, 0): 229 * 232 * 4 * 4, (0, 2): 56 * 56 * 64 * 4}
     assert all(d.launch < prefix for d in descs)
 
 
