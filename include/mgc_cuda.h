@@ -176,14 +176,17 @@ int mgc_cuda_run(void *handle, const void *const *inputs_host, void *const *outp
  * batch-major tensors whose memory is not shared between different layouts. Each descriptor
  * names one batch-dependent field of a prefix record: `what` 0, reference r[slot] advances by
  * `per_image` bytes per image of the slice's start; `what` 1, integer i[slot] becomes `per_image`
- * times the slice's images. mgc_cuda_run_device keeps the one-pass graph. Requires one graph
- * input; chunks 2..16 dividing `images`, which divides input 0's bytes. */
+ * times the slice's images; `what` 2, reference r[slot] becomes workspace byte `per_image`, the
+ * same for every slice (a buffer that only the prefix reads, moved out of memory it shares with
+ * one the rest of the graph reads into a private region of one slice's size, which the caller
+ * includes in the handle's workspace). mgc_cuda_run_device keeps the one-pass graph. Requires one
+ * graph input; chunks 2..16 dividing `images`, which divides input 0's bytes. */
 typedef struct {
     int32_t launch;    /* index of the record, below `prefix` */
-    int32_t what;      /* 0 reference offset, 1 integer field */
+    int32_t what;      /* 0 reference offset, 1 integer field, 2 reference into the workspace */
     int32_t slot;      /* r[] or i[] index */
     int32_t reserved;
-    int64_t per_image; /* bytes (what 0) or count (what 1) per image */
+    int64_t per_image; /* bytes (what 0) or count (what 1) per image; workspace offset (what 2) */
 } mgc_cuda_chunk;
 
 int mgc_cuda_set_input_chunks(void *handle, int chunks, int prefix, int64_t images,

@@ -97,8 +97,16 @@ struct Model {
                 mgc_cuda_launch L = launches[(size_t)r];
                 for (const mgc_cuda_chunk &d : chunk_descs) {
                     if (d.launch != r) continue;
-                    if (d.what == 0) L.r[d.slot].offset += (int64_t)j * per * d.per_image;
-                    else L.i[d.slot] = d.per_image * per;
+                    if (d.what == 0) {
+                        L.r[d.slot].offset += (int64_t)j * per * d.per_image;
+                    } else if (d.what == 2) {  // a buffer only the prefix reads, in one slice's
+                                               // private region (the same for every slice)
+                        L.r[d.slot].space = MGC_SPACE_WORKSPACE;
+                        L.r[d.slot].index = 0;
+                        L.r[d.slot].offset = d.per_image;
+                    } else {
+                        L.i[d.slot] = d.per_image * per;
+                    }
                 }
                 LaunchInfo info;
                 MGC_CHECK(launch_record(L, aux.data(), (int64_t)aux.size(), b, status_dev, stream, &info));
@@ -272,8 +280,9 @@ int mgc_cuda_set_input_chunks(void *handle, int chunks, int prefix, int64_t imag
         return fail(MGC_CUDA_BAD_ARGUMENT, "mgc_cuda_set_input_chunks: invalid arguments");
     for (int k = 0; k < n_descs; ++k) {
         const mgc_cuda_chunk &d = descs[k];
-        if (d.launch < 0 || d.launch >= prefix || d.what < 0 || d.what > 1 || d.slot < 0 ||
-            d.slot >= (d.what == 0 ? MGC_LAUNCH_REFS : MGC_LAUNCH_INTS) || d.per_image < 0)
+        if (d.launch < 0 || d.launch >= prefix || d.what < 0 || d.what > 2 || d.slot < 0 ||
+            d.slot >= (d.what == 1 ? MGC_LAUNCH_INTS : MGC_LAUNCH_REFS) || d.per_image < 0 ||
+            (d.what == 2 && d.per_image >= m->workspace_bytes))
             return fail(MGC_CUDA_BAD_ARGUMENT, "mgc_cuda_set_input_chunks: descriptor %d is invalid", k);
     }
     MGC_CHECK_CUDA(cudaSetDevice(m->device));

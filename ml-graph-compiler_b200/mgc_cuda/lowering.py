@@ -2005,8 +2005,9 @@ def _slice_fields(rec: Launch, images: int, per: int) -> list[tuple[int, int, in
 _SLICE_WRITES = {K_PACK: (1,), K_POOL: (1,), K_GEMM: (2,)}
 
 
-def input_slice_plan(lowered: LoweredModel, chunks: int = 4) -> tuple[int, int, list[Chunk]] | None:
-    """(prefix records, images, descriptors) for mgc_cuda_set_input_chunks, or None.
+def input_slice_plan(lowered: LoweredModel, chunks: int = 4,
+                     workspace_base: int | None = None) -> tuple[int, int, list[Chunk], int] | None:
+    """(prefix records, images, descriptors, private bytes) for mgc_cuda_set_input_chunks, or None.
 
     The prefix is the longest run of leading nodes whose records all work image by image on
     batch-major tensors (_slice_fields), cut back until slicing it is safe. Slicing reorders the
@@ -2014,7 +2015,11 @@ def input_slice_plan(lowered: LoweredModel, chunks: int = 4) -> tuple[int, int, 
     the prefix and read only inside it is consumed within its own slice's pass, so the planner's
     reuse of memory stays valid there. A buffer that the rest of the graph reads must survive the
     later slices' passes: no other prefix buffer may share its memory unless both have the same
-    start and bytes per image (then every slice keeps to its own range)."""
+    start and bytes per image (then every slice keeps to its own range). When the other buffer is
+    read only inside the prefix, it moves instead to a private region of one slice's size after
+    the workspace (``workspace_base``, the lowered workspace's bytes by default): every reference
+    of the prefix to it is repointed there (descriptor ``what`` 2), the same for every slice. The
+    private bytes are what the workspace must grow by."""
     if len(lowered.inputs) != 1:
         return None
     shape = lowered.inputs[0][1].shape
@@ -2023,6 +2028,8 @@ def input_slice_plan(lowered: LoweredModel, chunks: int = 4) -> tuple[int, int, 
     images = int(shape[0])
     per = images // chunks
     recs = lowered.launches
+    base = lowered.workspace_bytes if workspace_base is None else workspace_base
+    base = -(-base // BLOB_ALIGN) * BLOB_ALIGN
     # the longest sliceable run of whole nodes
     fields: list[list[tuple[int, int, int]]] = []
     end, k = 0, 0
@@ -2036,8 +2043,10 @@ def input_slice_plan(lowered: LoweredModel, chunks: int = 4) -> tuple[int, int, 
         fields += fs
         end, k = j, j
     tracked = (SPACE_ARENA, SPACE_OUTPUT, SPACE_WORKSPACE)
+    moved: dict[tuple[int, int], tuple[int, int, int]] = {}  # (record, slot) -> (ws offset, lo, per image)
     while end > 0:
-        # buffers the prefix writes: (space, index, start, end, bytes per image, record)
+        moved = {}
+        # buffers the prefix writes: (space, index, start, end, bytes per image, record, slot)
         writes = []
         for n in range(end):
             per_image = {slot: b for what, slot, b in fields[n] if what == 0}
@@ -2046,27 +2055,81 @@ def input_slice_plan(lowered: LoweredModel, chunks: int = 4) -> tuple[int, int, 
                 if ref.space not in tracked:
                     return None
                 writes.append((ref.space, ref.index, ref.offset, ref.offset + per_image[slot] * images,
-                               per_image[slot], n))
+                               per_image[slot], n, slot))
         suffix_refs = [(recs[n].r[t].space, recs[n].r[t].index, recs[n].r[t].offset)
                        for n in range(end, len(recs)) for t in range(len(recs[n].r))]
+
+        def last_writer(sp: int, ix: int, o: int, before: int) -> tuple | None:
+            """The prefix write that memory (sp, ix, o) holds before record `before`."""
+            owner = None
+            for w2 in writes:
+                if w2[5] < before and (w2[0], w2[1]) == (sp, ix) and w2[2] <= o < w2[3]:
+                    if owner is None or w2[5] > owner[5]:
+                        owner = w2
+            return owner
+
+        def escapes(w: tuple) -> bool:
+            """Whether the rest of the graph may read buffer w: a graph output, or memory of w's
+            that no later prefix write covers and a later record refers to."""
+            sp, ix, lo, hi = w[:4]
+            return sp == SPACE_OUTPUT or any(s2 == sp and i2 == ix and lo <= o < hi and last_writer(sp, ix, o, end) is w
+                                             for s2, i2, o in suffix_refs)
+
+        def readers(w: tuple) -> list[tuple[int, int]] | None:
+            """(record, slot) of every prefix reference to buffer w, or None when one may not be
+            moved: a reference to w's memory is w's when w is its last writer before it."""
+            sp, ix, lo, hi, pi, n0, _ = w
+            out = []
+            for r in range(n0 + 1, end):
+                per_image = {slot: b for what, slot, b in fields[r] if what == 0}
+                for t in range(len(recs[r].r)):
+                    ref = recs[r].r[t]
+                    if (ref.space, ref.index) != (sp, ix) or not lo <= ref.offset < hi or t in _SLICE_WRITES[recs[r].kind]:
+                        continue
+                    if last_writer(sp, ix, ref.offset, r) is not w:
+                        continue
+                    if t not in per_image or per_image[t] != pi or ref.offset - lo >= pi:
+                        return None  # not read image by image like it was written
+                    out.append((r, t))
+            return out
+
+        # conflicts: an escaping buffer and another prefix buffer over the same memory with a
+        # different layout; the other moves when only the prefix reads it, else the prefix ends
         cut = None
-        for sp, ix, lo, hi, pi, n in writes:
-            escapes = sp == SPACE_OUTPUT or any(s2 == sp and i2 == ix and lo <= o < hi for s2, i2, o in suffix_refs)
-            if not escapes:
+        relocate: dict[int, tuple] = {}
+        for x in writes:
+            if not escapes(x):
                 continue
-            for sp2, ix2, lo2, hi2, pi2, n2 in writes:
-                if (sp2, ix2) == (sp, ix) and lo2 < hi and lo < hi2 and (lo2, pi2) != (lo, pi):
-                    later = max(n, n2)
-                    cut = later if cut is None else min(cut, later)
-        if cut is None:
-            break
-        # drop the node holding record `cut` and everything after it
-        node = recs[cut].node
-        while cut > 0 and recs[cut - 1].node == node:
-            cut -= 1
-        end = cut
-        fields = fields[:end]
+            for y in writes:
+                if y is x or (y[0], y[1]) != (x[0], x[1]) or not (y[2] < x[3] and x[2] < y[3]) or (y[2], y[4]) == (x[2], x[4]):
+                    continue
+                if not escapes(y) and y[0] != SPACE_OUTPUT and readers(y) is not None:
+                    relocate[y[5] * 16 + y[6]] = y
+                    continue
+                later = max(x[5], y[5])
+                cut = later if cut is None else min(cut, later)
+        if cut is not None:
+            node = recs[cut].node
+            while cut > 0 and recs[cut - 1].node == node:
+                cut -= 1
+            end = cut
+            fields = fields[:end]
+            continue
+        off = base
+        for y in relocate.values():
+            moved[(y[5], y[6])] = (off, y[2], y[4])
+            for r, t in readers(y) or []:
+                moved[(r, t)] = (off + recs[r].r[t].offset - y[2], y[2], y[4])
+            off = -(-(off + y[4] * per) // BLOB_ALIGN) * BLOB_ALIGN
+        break
     if end == 0 or not any(recs[n].kind == K_GEMM for n in range(end)):
         return None
-    descs = [Chunk(n, what, slot, 0, b) for n in range(end) for what, slot, b in fields[n]]
-    return end, images, descs
+    descs = []
+    for n in range(end):
+        for what, slot, b in fields[n]:
+            if what == 0 and (n, slot) in moved:
+                descs.append(Chunk(n, 2, slot, 0, moved[(n, slot)][0]))
+            else:
+                descs.append(Chunk(n, what, slot, 0, b))
+    private = (max((o + per * pi for o, _, pi in moved.values()), default=base) - base) if moved else 0
+    return end, images, descs, -(-private // BLOB_ALIGN) * BLOB_ALIGN

@@ -24,7 +24,7 @@ import numpy as np
 
 from mgc_cuda import _reference  # noqa: F401
 from mgc_cuda import build as _build
-from mgc_cuda.lowering import Chunk, Launch, LoweredModel, input_slice_plan, lower_graph
+from mgc_cuda.lowering import BLOB_ALIGN, Chunk, Launch, LoweredModel, input_slice_plan, lower_graph
 from ml_graph_compiler.errors import CodegenError, GraphError
 from ml_graph_compiler.ir import Graph, TensorType, numpy_dtype
 from ml_graph_compiler.memory import Strategy
@@ -138,20 +138,24 @@ class CudaCompiledModel:
         ins = (ctypes.c_int64 * max(len(self.inputs), 1))(*[t.nbytes for _, t in self.inputs])
         outs = (ctypes.c_int64 * max(len(self.outputs), 1))(*[t.nbytes for _, t in self.outputs])
         aux = np.ascontiguousarray(lowered.aux, np.int64)
+        # run(): upload the input in slices that overlap the first layers' compute
+        # (MGC_CUDA_SLICES=0 turns it off, =k uses k slices; 4 by default); buffers the sliced
+        # prefix moves out of shared memory live after the lowered workspace
+        self.slices = 0
+        slices = int(os.environ.get("MGC_CUDA_SLICES", "4") or 0)
+        plan = input_slice_plan(lowered, slices) if slices >= 2 else None
+        workspace = lowered.workspace_bytes
+        if plan is not None and plan[3]:
+            workspace = -(-workspace // BLOB_ALIGN) * BLOB_ALIGN + plan[3]
         st = self.lib.mgc_cuda_create(
             ctypes.addressof(launches), len(lowered.launches), aux.ctypes.data, aux.size,
-            blob.ctypes.data, blob.nbytes, lowered.arena_bytes, lowered.workspace_bytes, ctypes.addressof(ins),
+            blob.ctypes.data, blob.nbytes, lowered.arena_bytes, workspace, ctypes.addressof(ins),
             len(self.inputs),
             ctypes.addressof(outs), len(self.outputs), device, ctypes.byref(self._handle),
         )
         check(st, "mgc_cuda_create", self.lib)
-        # run(): upload the input in slices that overlap the first layers' compute
-        # (MGC_CUDA_SLICES=0 turns it off, =k uses k slices; 4 by default)
-        self.slices = 0
-        slices = int(os.environ.get("MGC_CUDA_SLICES", "4") or 0)
-        plan = input_slice_plan(lowered, slices) if slices >= 2 else None
         if plan is not None:
-            prefix, images, descs = plan
+            prefix, images, descs, _ = plan
             arr = (Chunk * len(descs))(*descs)
             st = self.lib.mgc_cuda_set_input_chunks(self._handle, slices, prefix, images, ctypes.addressof(arr),
                                                     len(descs))

@@ -185,25 +185,97 @@ def test_tensor_core_b_planes_are_ordered(r50: Graph) -> None:
         assert single == (1 if precision == "tf32" else 0)
 
 
-@pytest.mark.parametrize("strategy,records", [("greedy_by_size", 4), ("naive", 13)])
-def test_input_slice_plan_of_resnet50(strategy: str, records: int) -> None:
-    """The sliced prefix at batch 256: pack, the stem with its pooling and the first two layer1
-    convolutions under the default plan (the planner then reuses memory for layer1 buffers of
-    other layouts that later slices would overwrite); with private buffers (naive) layer1 and the
-    first layer2 convolution too, up to the first GEMM whose slice has too few rows."""
+def _sliced_writes_keep_escaping_buffers(low, plan) -> int:
+    """Replay the sliced order of the prefix symbolically: every buffer the rest of the graph reads
+    (the last prefix write of memory a later record refers to) keeps, for every slice, what that
+    slice wrote: no write after it in the sliced order (later records of its slice, or any record
+    of a later slice) touches that slice's part of it. Returns how many slice parts were checked."""
+    prefix, images, descs, _ = plan
+    slices = 4
+    per = images // slices
+    by = {}
+    for d in descs:
+        by.setdefault((d.launch, d.slot), []).append(d)
+    fields = [lowering._slice_fields(low.launches[n], images, per) for n in range(prefix)]
+
+    def write_range(n: int, slot: int, j: int):
+        ref = low.launches[n].r[slot]
+        pi = next(b for what, sl, b in fields[n] if what == 0 and sl == slot)
+        ds = by.get((n, slot), [])
+        if any(d.what == 2 for d in ds):
+            off = next(d.per_image for d in ds if d.what == 2)
+            return (lowering.SPACE_WORKSPACE, 0, off, off + per * pi)
+        return (ref.space, ref.index, ref.offset + j * per * pi, ref.offset + (j + 1) * per * pi)
+
+    order = [(j, n, slot) for j in range(slices) for n in range(prefix)
+             for slot in lowering._SLICE_WRITES[low.launches[n].kind]]
+    unsliced = [(n, slot) for n in range(prefix) for slot in lowering._SLICE_WRITES[low.launches[n].kind]]
+    moved = {key for key, ds in by.items() if any(d.what == 2 for d in ds)}
+
+    def orig(n: int, slot: int):  # the buffer in the planner's memory (the one-pass graph)
+        ref = low.launches[n].r[slot]
+        pi = next(b for what, sl, b in fields[n] if what == 0 and sl == slot)
+        return ref.space, ref.index, ref.offset, ref.offset + images * pi
+
+    suffix = [(r.space, r.index, r.offset) for rec in low.launches[prefix:] for r in rec.r]
+    checked = 0
+    for s2, i2, o in suffix:
+        covering = [w for w in unsliced if orig(*w)[:2] == (s2, i2) and orig(*w)[2] <= o < orig(*w)[3]]
+        if not covering:
+            continue
+        n, slot = max(covering)  # the buffer the rest of the graph reads there
+        assert (n, slot) not in moved, f"record {n}'s output is read after the prefix but was moved"
+        for j in range(slices):
+            mine = write_range(n, slot, j)
+            at = order.index((j, n, slot))
+            for j2, n2, slot2 in order[at + 1:]:
+                other = write_range(n2, slot2, j2)
+                assert not (other[:2] == mine[:2] and other[2] < mine[3] and mine[2] < other[3]), \
+                    f"slice {j2} record {n2} overwrites slice {j}'s part of record {n}'s output"
+            checked += 1
+    return checked
+
+
+@pytest.mark.parametrize("strategy,records,moved", [("greedy_by_size", 12, 4), ("naive", 13, 0)])
+def test_input_slice_plan_of_resnet50(strategy: str, records: int, moved: int) -> None:
+    """The sliced prefix at batch 256: pack, the stem with its pooling, layer1 and (naive) the
+    first layer2 convolution, up to the first GEMM whose slice has too few rows. Under the default
+    plan layer1's 64-channel buffers share memory with the 256-channel block outputs the rest of
+    the graph reads; read only inside the prefix, they move to private regions of one slice each
+    (4 x 64 images x 56 x 56 x 64 floats), and the symbolic replay of the sliced order finds every
+    escaping buffer intact."""
     g = o3(zoo.resnet50(batch=256))
     low = lower_graph(g, strategy, True, "tf32")
     plan = lowering.input_slice_plan(low, 4)
     assert plan is not None
-    prefix, images, descs = plan
+    prefix, images, descs, private = plan
     assert (prefix, images) == (records, 256)
+    writers = {(d.launch, d.slot) for d in descs if d.what == 2 and d.slot in lowering._SLICE_WRITES[low.launches[d.launch].kind]}
+    assert len(writers) == moved
+    assert private == moved * 64 * 56 * 56 * 64 * 4
+    assert all(d.per_image >= -(-low.workspace_bytes // 256) * 256 for d in descs if d.what == 2)
     stem = low.launches[1]
     assert stem.kind == K_GEMM and low.launches[0].kind == K_PACK
     fields = {(d.what, d.slot): d.per_image for d in descs if d.launch == 1}
     # M = images * 112 * 112; A = the phase-split image (229 rows of 2 x 116 four-channel
-    # pixels); C = the pooled image, 56 * 56 * 64 floats
-    assert fields == {(1, 0): 112 * 112, (0, 0): 229 * 232 * 4 * 4, (0, 2): 56 * 56 * 64 * 4}
+    # pixels); C = the pooled image, 56 * 56 * 64 floats (greedy: in a private region)
+    assert fields[(1, 0)] == 112 * 112 and fields[(0, 0)] == 229 * 232 * 4 * 4
+    assert fields.get((0, 2)) == (None if moved else 56 * 56 * 64 * 4)
     assert all(d.launch < prefix for d in descs)
+    assert _sliced_writes_keep_escaping_buffers(low, plan) > 0
+    if moved:
+        # the same prefix without the moves: later slices overwrite block outputs the rest of the
+        # graph reads (what the check exists to catch)
+        per = images // 4
+        plain = []
+        for d in descs:
+            if d.what == 2:
+                pi = next(b for what, sl, b in lowering._slice_fields(low.launches[d.launch], images, per)
+                          if what == 0 and sl == d.slot)
+                d = lowering.Chunk(d.launch, 0, d.slot, 0, pi)
+            plain.append(d)
+        with pytest.raises(AssertionError, match="overwrites"):
+            _sliced_writes_keep_escaping_buffers(low, (prefix, images, plain, 0))
 
 
 def test_input_slice_plan_needs_a_batch() -> None:
