@@ -3,7 +3,7 @@ TF32 mode, for every operand layout the lowering hands it (Q and the output with
 contiguous; K^T read with the head width or the keys contiguous; V with the head width or the
 keys contiguous), every score program of the unfused softmax's ScaleMask form (X * s, X / s, then
 + M, - M, Where(C, t, lit), Where(C, lit, t)), ragged key counts, two query tiles and head widths
-other than 64; the forms the kernel compiles without runtime tests (X * s alone, + fp32 mask,
+other than 64, and grids of more CTAs than fit at once; the forms the kernel compiles without runtime tests (X * s alone, + fp32 mask,
 Where with a byte mask either way round) and its generic form (X / s, - M, ragged masks). Each
 case is compared with a float64 emulation of the kernel's arithmetic: Q, K and
 V rounded to TF32 on load (ties away from zero, what a TFLOAT32 tensor map does), the scores and
@@ -117,6 +117,9 @@ CASES = [
     (2, 4, 8, 8, 8, 8, False, True, "mul", True),                 # tiny heads, no mask
     (1, 2, 130, 36, 96, 64, True, False, "div_add", True),
     (2, 3, 96, 64, 64, 64, False, False, "mul_keep", True),
+    # more (batch, head) items than the CTAs the GPU holds at once (two waves and a tail)
+    (26, 12, 128, 128, 64, 64, False, False, "mul_add", True),
+    (4, 80, 64, 96, 32, 32, True, True, "div_keep", False),
 ]
 
 
