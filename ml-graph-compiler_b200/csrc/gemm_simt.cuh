@@ -49,6 +49,9 @@ struct GemmParams {
     // phase-split convolution followed by a 3x3 / stride-2 / pad-1 max pooling computed in its
     // epilogue: the pooled output's rows and columns (c is then the pooled output); 0: no pooling
     int pool_ph, pool_pw;
+    // the output only feeds a GlobalAveragePool of gap_hw pixels per image: c receives the
+    // tensor-core epilogue's 32-row partial sums instead (0: the output itself)
+    int gap_hw;
     int *err;                     // device word for bounded-wait timeouts (may be NULL)
     // split-K scratch of the model (NULL: no split): room for the partial tiles
     float *split_ws;

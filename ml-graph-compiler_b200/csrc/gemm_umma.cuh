@@ -117,6 +117,11 @@ struct Params {
     // its 2 pool_bp + 1 output rows from 2 p0 - 1 (the row above the image is a dummy tile);
     // c is the pooled output [image][pool_ph][pool_pw][ldc]
     int pool_bp, pool_nbp, pool_nbands, pool_ph, pool_pw;
+    // GlobalAveragePool partials (gap_hw > 0: rows per image, >= 32): instead of the output, each
+    // 32-row group g of rows writes the column sums of the rows of its first image to c[2 g][.]
+    // and of its second image (if any) to c[2 g + 1][.] (row stride ldc); K_REDUCE_MID mode 2
+    // adds them per image
+    int gap_hw;
 };
 
 // ---- PTX wrappers -----------------------------------------------------------------------------
@@ -1411,7 +1416,43 @@ __global__ void __launch_bounds__(THREADS, 1) umma_gemm_kernel(const __grid_cons
                     *slot = o;
                 }
             }
-            if (PH && p.pool_bp > 0) {
+            if (!PH && p.gap_hw > 0) {
+                // GlobalAveragePool partials from the staged pass (thread et: column et % EN of the
+                // 32-row groups of row part et / EN), in place of the output stores
+                static_assert(EPI_THREADS % EN == 0 && (BM / 32) % (EPI_THREADS / EN) == 0, "GAP row groups");
+                constexpr int RG = EPI_THREADS / EN, PER = (BM / 32) / RG;  // threads per column, groups each
+                epilogue_sync();
+                const int gc = et % EN, rg = et / EN;
+                if (n0 + gc < p.N) {
+#pragma unroll 1
+                    for (int g = rg * PER; g < (rg + 1) * PER; ++g) {
+                        const long long mg = (long long)m0 + g * 32;
+                        if (mg >= p.M) break;
+                        // rows of the group that exist, and the first of them in the next image
+                        const int lim = p.M - mg < 32 ? (int)(p.M - mg) : 32;
+                        const int split = (int)((mg / p.gap_hw + 1) * p.gap_hw - mg);
+                        float s0 = 0.0f, s1 = 0.0f;
+#pragma unroll
+                        for (int r = 0; r < 32; ++r) {
+                            const float x = reinterpret_cast<const float *>(out_tile + stage_offset(g * 32 + r, gc & ~3))[gc & 3];
+                            if (r < lim) {
+                                if (r < split) s0 += x;
+                                else s1 += x;
+                            }
+                        }
+                        float *dst = p.c + (mg / 32) * 2 * p.ldc + n0 + gc;
+                        dst[0] = s0;
+                        dst[p.ldc] = s1;
+                    }
+                }
+                fence_proxy_async_smem();
+                epilogue_sync();  // the staged pass is read out
+                if (issuer && res_tma) {  // the next pass's residual: this tile's, or the next tile's first
+                    int mt2, nt2;
+                    if (h + 1 < NH) issue_residual(mt, nt, h + 1);
+                    else if (tile_at(i + 1, mt2, nt2)) issue_residual(mt2, nt2, 0);
+                }
+            } else if (PH && p.pool_bp > 0) {
                 // 3x3 / stride-2 / pad-1 max pooling of the output rows, in order: thread et keeps
                 // channels 4 (et % 16) .. + 3 of pooled columns et / 16, + 16, ... (PW <= 64); a
                 // pooled row ph is complete at output row 2 ph + 1 (padding: -inf, never the
@@ -2058,6 +2099,7 @@ inline int try_gemm_umma(const GemmParams &p, cudaStream_t stream, int *taken) {
     u.c = p.c; u.ldc = p.ldc; u.bias = p.bias; u.res = p.res; u.ldr = p.ldr;
     u.alpha = p.alpha; u.lo = p.lo; u.hi = p.hi; u.act = p.act;
     u.err = p.err;
+    u.gap_hw = p.gap_hw;  // the pixels of one image, when the output is only pooled
     // output through a TMA store of the staged tile when C's rows are 16-byte aligned, with the
     // residual tile TMA-loaded into the staging buffer (both, or neither)
     u.tma_out = ((reinterpret_cast<uintptr_t>(p.c) & 15) == 0 && (p.ldc & 3) == 0 &&
@@ -2089,6 +2131,7 @@ inline int try_gemm_umma(const GemmParams &p, cudaStream_t stream, int *taken) {
     }
     // Phase-split row tiles: one output row per tile (its output and residual through 4-D maps
     // that clip the tile's rows past OW), A read by bulk copies of packed rows.
+    if (p.gap_hw > 0 && (u.im2col == 5 || p.gap_hw < 32)) return MGC_CUDA_OK;  // partials: not these forms
     if (u.im2col == 5 && p.pool_ph > 0) {
         // with the 3x3 / stride-2 / pad-1 max pooling in the epilogue: one N tile, even output
         // extents, the pooled image stored by the epilogue threads (no output map, no residual).
@@ -2215,7 +2258,7 @@ inline int try_gemm_umma(const GemmParams &p, cudaStream_t stream, int *taken) {
         const int v = e ? atoi(e) : 4;
         return v >= 1 ? v : 4;
     }();
-    if (split_env && p.split_ws && (u.im2col == 0 || u.im2col == 1) && u.num_kb >= 2 * split_min_kb) {
+    if (split_env && p.split_ws && (u.im2col == 0 || u.im2col == 1) && u.num_kb >= 2 * split_min_kb && p.gap_hw == 0) {
         const long long tiles = (long long)u.n_tiles * m_tiles;
         const int sms = sm_count();
         if (tiles * 2 <= sms) {

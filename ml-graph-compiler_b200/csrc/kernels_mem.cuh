@@ -970,6 +970,24 @@ __global__ void __launch_bounds__(256) reduce_mid_kernel(int is_max, long long o
     }
 }
 
+// GlobalAveragePool from the producing GEMM's partials (its epilogue's gap_hw form): y[o][c] =
+// (sum over the 32-row groups g holding rows of image o, in order, of part[2 g + (o - first image
+// of g)][c]) * (1 / n), n >= 32 pixels per image (a group holds rows of at most two images). The
+// mean's scale as reduce_mid_kernel's; the sum's order is by groups instead of row by row.
+__global__ void __launch_bounds__(256) gap_partials_kernel(long long outer, long long n, long long inner,
+                                                           const float *part, float *y) {
+    const long long total = outer * inner;
+    const long long stride = (long long)gridDim.x * blockDim.x;
+    const float inv = 1.0f / (float)n;
+    for (long long e = (long long)blockIdx.x * blockDim.x + threadIdx.x; e < total; e += stride) {
+        const long long o = e / inner, c = e % inner;
+        const long long g0 = o * n / 32, g1 = ((o + 1) * n - 1) / 32;
+        float acc = 0.0f;
+        for (long long g = g0; g <= g1; ++g) acc += part[(2 * g + (o - g * 32 / n)) * inner + c];
+        y[e] = acc * inv;
+    }
+}
+
 // Generic ReduceSum/Mean/Prod/Max/Min (c.py:736-784): double accumulator for float sum, mean
 // and prod, the element type otherwise.
 enum { RED_SUM = 0, RED_MEAN = 1, RED_PROD = 2, RED_MAX = 3, RED_MIN = 4 };

@@ -80,8 +80,9 @@ inline int run_gemm(const GemmParams &p, cudaStream_t stream, LaunchInfo *info =
         info->gemm_path = taken > 0 ? MGC_CUDA_PATH_TCGEN05 : MGC_CUDA_PATH_SIMT;
     }
     if (taken) return MGC_CUDA_OK;
-    if (p.phase_w > 0 || p.pool_ph > 0)  // a phase-split packed image is no NHWC operand for the
-                                           // exact-fp32 kernel, which has no pooling epilogue either
+    if (p.phase_w > 0 || p.pool_ph > 0 || p.gap_hw > 0)  // a phase-split packed image is no NHWC
+                                                         // operand for the exact-fp32 kernel, which
+                                                         // has no pooling epilogues either
         return fail(MGC_CUDA_UNSUPPORTED, "gemm: the tensor-core kernel declined a phase-split convolution "
                                           "(M %d, N %d, OW %d, pooled %d x %d)", p.M, p.N, p.OW, p.pool_ph, p.pool_pw);
     return launch_gemm_simt(p, stream);
@@ -117,6 +118,7 @@ inline int decode_gemm(const mgc_cuda_launch &L, const Bases &bases, GemmParams 
     p.win_rows = (int)i[51]; p.win_L = (int)i[52];
     p.phase_w = (int)i[53];
     p.pool_ph = (int)i[54]; p.pool_pw = (int)i[55];
+    p.gap_hw = (int)i[56];
     if (!p.a || !p.b || !p.c) return fail(MGC_CUDA_BAD_ARGUMENT, "gemm: missing operand");
     return MGC_CUDA_OK;
 }
@@ -362,6 +364,12 @@ inline int launch_record(const mgc_cuda_launch &L, const int64_t *aux, int64_t a
         MGC_RESOLVE(L.r[0], x); MGC_RESOLVE(L.r[1], y);
         const long long total = i[1] * i[3];
         if (total == 0) { launched = 0; break; }
+        if (i[0] == 2) {  // mean from the producing GEMM's 32-row partial sums (gap_hw)
+            if (i[2] < 32) return fail(MGC_CUDA_BAD_ARGUMENT, "reduce: partials need >= 32 rows per image");
+            gap_partials_kernel<<<grid_for(total, 256), 256, 0, stream>>>(i[1], i[2], i[3], x, y);
+            st = check_launch("gap_partials_kernel");
+            break;
+        }
         reduce_mid_kernel<<<grid_for(total, 256), 256, 0, stream>>>((int)i[0], i[1], i[2], i[3], x, y);
         st = check_launch("reduce_mid_kernel");
         break;

@@ -328,6 +328,8 @@ class CudaEmitter:
         self._attn_skip: set[int] = set()
         # MaxPool nodes computed in the epilogue of the convolution before them (_pooled_by)
         self._pool_skip: set[int] = set()
+        # GlobalAveragePool nodes that add their producer's epilogue partial sums (_gap_partials)
+        self._gap_from_partials: set[int] = set()
 
     # -- references ----------------------------------------------------------------------------
     def _root(self, value: Value) -> Value:
@@ -945,6 +947,8 @@ class CudaEmitter:
                   dtype=DTYPES[xt.dtype], count="reduce")
 
     def _global_pool(self, node: Node, is_max: int) -> None:
+        """K_REDUCE_MID slots: i[0] 0 mean, 1 max, 2 mean of the producing GEMM's 32-row partial
+        sums (_gap_partials), i[1] outer, i[2] n, i[3] inner; r[0] x, r[1] y."""
         x = node.input(0)
         xt = x.tensor_type
         self._require_f32(node, xt)
@@ -952,7 +956,31 @@ class CudaEmitter:
             outer, n, inner = xt.shape[0], int(np.prod(xt.shape[1:-1])), xt.shape[-1]
         else:
             outer, n, inner = xt.shape[0] * xt.shape[1], int(np.prod(xt.shape[2:])), 1
-        self.emit(K_REDUCE_MID, [is_max, outer, n, inner], refs=[self.ref(x), self.ref(node.output)])
+        mode = 2 if id(node) in self._gap_from_partials else is_max
+        self.emit(K_REDUCE_MID, [mode, outer, n, inner], refs=[self.ref(x), self.ref(node.output)])
+
+    def _gap_partials(self, node: Node) -> Node | None:
+        """The GlobalAveragePool whose mean a convolution's epilogue prepares (TF32 mode), or None:
+        the convolution's output (NHWC, >= 32 pixels per image, no graph output) is read only by
+        that pool, over enough tiles that the GEMM needs no split K. The epilogue then writes, in
+        place of the output, the column sums of each 32-row group's rows per image into the
+        output's own memory (the pool reads nothing else from it), and the pool adds them
+        (reference c.py:1254-1273 reduces the whole output instead)."""
+        if self.precision != "tf32" or os.environ.get("MGC_CUDA_GAP_FUSION") == "0":
+            return None
+        out = node.output
+        if len(out.users) != 1 or any(v is out for _, v in self.graph.named_outputs()):
+            return None
+        gap = out.users[0]
+        if gap.op != "GlobalAveragePool" or gap.input(0) is not out or ops.conv_layout(gap) != "NHWC":
+            return None
+        t = out.tensor_type
+        if t.rank != 4 or t.dtype != "float32":
+            return None
+        nb, oh, ow, c = (int(d) for d in t.shape)
+        if oh * ow < 32 or -(-nb * oh * ow // 128) * -(-c // 128) < 148:
+            return None
+        return gap
 
     def op_GlobalAveragePool(self, node: Node) -> None:
         self._global_pool(node, 0)
@@ -1135,6 +1163,7 @@ class CudaEmitter:
         win_L: int = 0,
         phase_w: int = 0,
         pool: tuple[int, int] = (0, 0),
+        gap_hw: int = 0,
     ) -> None:
         """K_GEMM slots: i[0..2] M, N, K; i[3] batch dims; i[4..7] batch extents; i[8..11],
         i[12..15], i[16..19], i[20..23] per-dimension batch strides of A, B, C, residual;
@@ -1147,15 +1176,18 @@ class CudaEmitter:
         otherwise). i[53] pixels per phase of a phase-split packed image row (A is such an image
         and B is [N][KH][32] in phase-split tap order; 0 otherwise). i[54], i[55] the rows and
         columns of the 3x3 / stride-2 / pad-1 max pooling computed in a phase-split convolution's
-        epilogue (C is then the pooled image; 0 otherwise). f[0..3] alpha, beta, clip lo,
+        epilogue (C is then the pooled image; 0 otherwise). i[56] the pixels per image when the
+        output only feeds a GlobalAveragePool: C then receives the epilogue's 32-row partial sums
+        (_gap_partials; 0 otherwise). f[0..3] alpha, beta, clip lo,
         clip hi. r[0] A, r[1] B, r[2] C,
         r[3] bias, r[4] residual, r[5] residual of a split constant B, r[6] / r[7] the
         tensor-core layout of a constant B (TF32-rounded part / residual), absent otherwise."""
         if len(batch) > 4:
             raise CodegenError(f"GEMM with {len(batch)} batch dimensions")
-        ints = [0] * 56
+        ints = [0] * 57
         ints[50], ints[51], ints[52], ints[53] = b_cpad, win_rows, win_L, phase_w
         ints[54], ints[55] = pool
+        ints[56] = gap_hw
         ints[0], ints[1], ints[2], ints[3] = m, n, k, len(batch)
         for d in range(len(batch)):
             ints[4 + d] = batch[d]
@@ -1656,10 +1688,14 @@ class CudaEmitter:
                     umma = {"b_umma": uhi, "b_umma_lo": ulo, "b_cpad": cp}
                 else:
                     umma = {}
+                gap = self._gap_partials(node) if group == 1 and umma else None
+                if gap is not None:
+                    self._gap_from_partials.add(id(gap))
                 self._gemm(
                     nb * oh * ow, kg, kh * kw * cg, xref, c, 1, bref, b_rs, b_cs, out_ref, kout, b_lo=blo,
                     conv={**geo, "c_off": gi * cg, "cg": cg}, a_kind=STRIDED if pointwise else CONV_NHWC,
                     bias=bias_g, bias_mode=1, res=res_g, ldr=kout, act=act, **umma,
+                    gap_hw=oh * ow if gap is not None else 0,
                 )
             else:
                 plane = oh * ow

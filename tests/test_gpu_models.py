@@ -85,6 +85,29 @@ def test_stem_pooling_in_the_epilogue_is_exact(batch: int, monkeypatch: pytest.M
     np.testing.assert_array_equal(got["1"], got["0"])
 
 
+def test_global_average_pool_from_epilogue_partials(monkeypatch: pytest.MonkeyPatch) -> None:
+    """TF32 ResNet-50 at batch 32: the last convolution's epilogue writes 32-row partial column
+    sums per image instead of its 7 x 7 x 2048 output, and the GlobalAveragePool adds them. Only
+    the order of the pool's sum changes against the separate kernel (MGC_CUDA_GAP_FUSION=0): the
+    logits agree within 1e-5 of their scale, far below what a row or image mix-up would cause."""
+    g = zoo.resnet50(batch=32, seed=0)
+    optimize(g, "O3")
+    schedule(g)
+    x = {"image": np.random.default_rng(3).standard_normal((32, 3, 224, 224)).astype(np.float32)}
+    got = {}
+    for flag in ("1", "0"):
+        monkeypatch.setenv("MGC_CUDA_GAP_FUSION", flag)
+        m = compile_graph(g, precision="tf32")
+        try:
+            fused = [r for r in m.lowered.launches if r.kind == 4 and r.i[0] == 2]
+            assert len(fused) == (1 if flag == "1" else 0)
+            got[flag] = m.run(x)["logits"].astype(np.float64)
+        finally:
+            m.close()
+    scale = float(np.abs(got["0"]).max())
+    assert float(np.abs(got["1"] - got["0"]).max()) <= 1e-5 * scale
+
+
 def test_resnet50_batch_is_independent_per_image() -> None:
     """Size-independent property at a larger batch: every image of a batch-8 run equals the
     batch-1 model's output for that image (strict mode, bit-level batch independence is not

@@ -278,6 +278,22 @@ def test_input_slice_plan_of_resnet50(strategy: str, records: int, moved: int) -
             _sliced_writes_keep_escaping_buffers(low, (prefix, images, plain, 0))
 
 
+@pytest.mark.parametrize("batch,precision,fused", [(256, "tf32", True), (1, "tf32", False), (256, "strict", False)])
+def test_global_average_pool_from_partials(batch: int, precision: str, fused: bool) -> None:
+    """TF32 ResNet-50 at a batch with enough tiles: the last convolution's record carries the
+    pixels per image (49) and the pool adds its epilogue's partial sums (K_REDUCE_MID mode 2) from
+    the convolution's own output memory; batch 1 (a split-K GEMM) and strict mode keep the pool."""
+    low = lower_graph(o3(zoo.resnet50(batch=batch)), "greedy_by_size", True, precision)
+    red = [r for r in low.launches if r.kind == lowering.K_REDUCE_MID]
+    gap = [r for r in low.launches if r.kind == K_GEMM and r.i[56] > 0]
+    assert len(red) == 1 and red[0].i[0] == (2 if fused else 0)
+    if fused:
+        assert len(gap) == 1 and gap[0].i[56] == 49 and (gap[0].i[0], gap[0].i[1]) == (batch * 49, 2048)
+        assert (gap[0].r[2].space, gap[0].r[2].offset) == (red[0].r[0].space, red[0].r[0].offset)
+    else:
+        assert not gap
+
+
 def test_input_slice_plan_needs_a_batch() -> None:
     low = lower_graph(o3(zoo.resnet50(batch=1)), "greedy_by_size", True, "tf32")
     assert lowering.input_slice_plan(low, 4) is None
