@@ -858,6 +858,39 @@ __global__ void __launch_bounds__(256) pack_phase_kernel(const __grid_constant__
     }
 }
 
+// The same packing, one block per packed row (blockIdx.y = image * Hp + row, no divisions) and one
+// thread per pixel index j of both phases: the phase-0 pixel reads input column 2 j - PL + 0 and
+// the phase-1 pixel column 2 j - PL + 1 (adjacent), so a warp
+// reads 64 consecutive columns of each channel plane and writes two runs of 32 packed pixels;
+// the other kernel's threads each read every other column. Same values (round_tf32 of the same
+// elements, zeros outside the image).
+__global__ void __launch_bounds__(128) pack_phase_rows_kernel(const __grid_constant__ PackParams p) {
+    const unsigned wq = (unsigned)p.Wp >> 1;
+    const unsigned j = blockIdx.x * blockDim.x + threadIdx.x;
+    if (j >= wq) return;
+    const unsigned n = blockIdx.y / (unsigned)p.Hp, row = blockIdx.y - n * (unsigned)p.Hp;
+    const int h = (int)row - p.PT;
+    float4 *dst = reinterpret_cast<float4 *>(p.out) + (size_t)blockIdx.y * p.Wp + j;
+    if (h < 0 || h >= p.H) {
+        dst[0] = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+        dst[wq] = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+        return;
+    }
+    const float *base = p.x + n * (unsigned)p.sn + (unsigned)h * (unsigned)p.sh;
+    float v[2][4];
+#pragma unroll
+    for (int f = 0; f < 2; ++f) {
+        const int w = 2 * (int)j + f - p.PL;
+        const bool inside = w >= 0 && w < p.W;
+#pragma unroll
+        for (int t = 0; t < 4; ++t)
+            v[f][t] = inside && t < p.C ? round_tf32(__ldg(base + (unsigned)w * (unsigned)p.sw + (unsigned)t * (unsigned)p.sc))
+                                        : 0.0f;
+    }
+    dst[0] = make_float4(v[0][0], v[0][1], v[0][2], v[0][3]);
+    dst[wq] = make_float4(v[1][0], v[1][1], v[1][2], v[1][3]);
+}
+
 // The same packing with 32-bit index arithmetic (pixel counts and source offsets below 2^31).
 __global__ void __launch_bounds__(256) pack_nhwc32_kernel(const __grid_constant__ PackParams p) {
     const unsigned hw = (unsigned)p.Hp * (unsigned)p.Wp;

@@ -579,6 +579,16 @@ inline int launch_record(const mgc_cuda_launch &L, const int64_t *aux, int64_t a
                 return fail(MGC_CUDA_BAD_ARGUMENT, "pack: phase-split layout %dx%d of a %dx%dx%d image", p.Hp, p.Wp,
                             p.H, p.W, p.C);
             if (total == 0) { launched = 0; break; }
+            static const bool rows_env = [] {  // MGC_CUDA_PACK_ROWS=0: the one-pixel-per-thread kernel
+                const char *e = getenv("MGC_CUDA_PACK_ROWS");
+                return !(e && e[0] == '0');
+            }();
+            if (rows_env && (long long)p.N * p.Hp <= 65535) {  // one block per packed row
+                pack_phase_rows_kernel<<<dim3((unsigned)((p.Wp / 2 + 127) / 128), (unsigned)(p.N * p.Hp)), 128, 0,
+                                         stream>>>(p);
+                st = check_launch("pack_phase_rows_kernel");
+                break;
+            }
             pack_phase_kernel<<<grid_for(total, 256), 256, 0, stream>>>(p);
             st = check_launch("pack_phase_kernel");
             break;

@@ -3,6 +3,8 @@ plus the behaviour of the compiled-model API (runtime_lib.py semantics)."""
 
 from __future__ import annotations
 
+from pathlib import Path
+
 import numpy as np
 import pytest
 
@@ -82,6 +84,41 @@ def test_stem_pooling_in_the_epilogue_is_exact(batch: int, monkeypatch: pytest.M
             got[flag] = m.run(x)["logits"]
         finally:
             m.close()
+    np.testing.assert_array_equal(got["1"], got["0"])
+
+
+def test_phase_pack_kernels_agree_bit_for_bit() -> None:
+    """The phase-split pack of the TF32 stem input, one block per packed row (two adjacent input
+    columns per thread), against the one-pixel-per-thread kernel (MGC_CUDA_PACK_ROWS=0, read once
+    per process, so a child process runs it): the same logits bit for bit (ResNet-50 and
+    MobileNetV2, batch 3)."""
+    import os
+    import subprocess
+    import sys
+
+    code = (
+        "import sys, numpy as np; sys.path[:0] = sys.argv[1:3]\n"
+        "from mgc_cuda import zoo\nfrom mgc_cuda.runtime import compile_graph\n"
+        "from ml_graph_compiler.passes import optimize\nfrom ml_graph_compiler.schedule import schedule\n"
+        "out = []\n"
+        "for make in (zoo.resnet50, zoo.mobilenet_v2):\n"
+        "    g = make(batch=3); optimize(g, 'O3'); schedule(g)\n"
+        "    m = compile_graph(g, precision='tf32')\n"
+        "    x = np.random.default_rng(5).standard_normal((3, 3, 224, 224)).astype(np.float32)\n"
+        "    out.append(m.run({'image': x})['logits']); m.close()\n"
+        "np.save(sys.argv[3], np.concatenate([o.reshape(-1) for o in out]))\n"
+    )
+    root = Path(__file__).resolve().parents[1]
+    paths = [str(root / "ml-graph-compiler_b200"), str(root)]
+    got = {}
+    for flag in ("1", "0"):
+        out = root / "gpurun_out" / f"pack_rows_{flag}.npy" if (root / "gpurun_out").is_dir() else Path(f"/tmp/pack_rows_{flag}.npy")
+        env = {**os.environ, "MGC_CUDA_PACK_ROWS": flag}
+        r = subprocess.run([sys.executable, "-c", code, *paths, str(out)], env=env, capture_output=True, text=True,
+                           timeout=600)
+        assert r.returncode == 0, r.stderr[-2000:]
+        got[flag] = np.load(out)
+        out.unlink()
     np.testing.assert_array_equal(got["1"], got["0"])
 
 
