@@ -596,6 +596,7 @@ struct DepthwiseParams {
     float lo, hi;
     const float *x, *w, *bias, *res;
     float *y;
+    int *err;  // the handle's status word (bounded waits that give up record MGC_CUDA_TIMEOUT), or NULL
 };
 
 // NHWC: one thread per (pixel, 4 channels) when C % 4 == 0, channels contiguous; weights HWC.

@@ -11,6 +11,7 @@
 #include "gemm_umma.cuh"
 #include "kernels_mem.cuh"
 #include "kernels_norm.cuh"
+#include "depthwise.cuh"
 
 namespace mgc {
 
@@ -264,6 +265,96 @@ inline int launch_dw_tile(const DepthwiseParams &p, cudaStream_t s) {
     return check_launch("depthwise_nhwc4_tile_kernel");
 }
 
+// Depthwise convolution in row bands (depthwise.cuh). The block shape: the divisor `cg` of the
+// C / VEC channel vectors (at most 32) whose column tiles of at most 256 / cg columns (and at most
+// `max_tw`) leave the fewest warp lanes idle (ties: the larger cg, so that a block reads longer
+// pieces of each pixel); then the band height that minimises (waves of blocks) x (input rows per
+// block + `fill` rows of fixed cost per block), waves counted with the kernel's occupancy at
+// `smem_per_vec` bytes of shared memory per input column and channel vector plus `smem_extra`.
+inline int dw_band_shape(const DepthwiseParams &p, int vec, int S, const void *kernel, int fill, int max_tw,
+                         unsigned smem_per_vec, unsigned smem_extra, DwBand &t, unsigned &smem) {
+    const int cv = p.C / vec;
+    t = DwBand{};
+    double best = -1.0;
+    for (int cg = cv < 32 ? cv : 32; cg >= 1; --cg) {
+        if (cv % cg) continue;
+        const int wmax = 256 / cg < max_tw ? 256 / cg : max_tw;
+        const int tiles = (int)ceil_div(p.OW, wmax);
+        const int tw = (int)ceil_div(p.OW, tiles);
+        const double eff = (double)p.OW * cg / ((double)tiles * ceil_div(tw * cg, 32) * 32);
+        if (eff > best + 1e-9) {
+            best = eff;
+            t.cg = cg;
+            t.tw = tw;
+            t.tiles = (unsigned)tiles;
+        }
+    }
+    t.chunks = (unsigned)(cv / t.cg);
+    const int threads = t.tw * t.cg;
+    smem = smem_per_vec * (unsigned)(((t.tw - 1) * S + 3) * t.cg) + smem_extra;
+    if (smem > 48 * 1024)
+        MGC_CHECK_CUDA(cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+    int per_sm = 0;
+    MGC_CHECK_CUDA(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kernel, threads, smem));
+    int dev = 0, sms = 148;
+    MGC_CHECK_CUDA(cudaGetDevice(&dev));
+    MGC_CHECK_CUDA(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev));
+    const long long slots = (long long)sms * (per_sm > 0 ? per_sm : 1);
+    const long long per_band = (long long)p.N * t.tiles * t.chunks;
+    long long best_cost = -1;
+    for (int bh = 1; bh <= p.OH; ++bh) {
+        const long long bands = ceil_div(p.OH, bh);
+        const long long waves = ceil_div(per_band * bands, slots);
+        const long long cost = waves * ((long long)(bh - 1) * S + 3 + fill);
+        if (best_cost < 0 || cost < best_cost) {
+            best_cost = cost;
+            t.bh = bh;
+            t.bands = (unsigned)bands;
+        }
+    }
+    if (per_band * t.bands >= (1ll << 31)) return fail(MGC_CUDA_UNSUPPORTED, "depthwise: %lld bands", per_band * t.bands);
+    return MGC_CUDA_OK;
+}
+
+// Ring slots of the band forms: 5 rows in flight (4 and 10 measured slower on MobileNetV2's layers).
+constexpr int DW_SLOTS = 6;
+
+template <int S, int VEC, int D = DW_SLOTS>
+inline int launch_dw_ring(const DepthwiseParams &p, cudaStream_t s) {
+    DwBand t;
+    unsigned smem = 0;
+    const void *k = (const void *)depthwise_ring_kernel<S, VEC, D>;
+    MGC_CHECK(dw_band_shape(p, VEC, S, k, D, 256, D * VEC * 4, 0, t, smem));
+    const long long blocks = (long long)p.N * t.tiles * t.chunks * t.bands;
+    depthwise_ring_kernel<S, VEC, D><<<(unsigned)blocks, t.tw * t.cg, smem, s>>>(p, t);
+    return check_launch("depthwise_ring_kernel");
+}
+
+// The TMA form: a 4-D map of the input (channels, columns, rows, images) with boxes of one band
+// row (cg * 4 channels x (tw - 1) * S + 3 columns); out-of-range boxes read zeros.
+template <int S, int D = DW_SLOTS>
+inline int launch_dw_tma(const DepthwiseParams &p, cudaStream_t s) {
+    DwBand t;
+    unsigned smem = 0;
+    const void *k = (const void *)depthwise_tma_kernel<S, D>;
+    // each slot rounded up to 128 bytes, D barriers, 128 bytes of alignment slack
+    MGC_CHECK(dw_band_shape(p, 4, S, k, D, (256 - 3) / S + 1, D * 16, D * (128 + 8) + 128, t, smem));
+    auto fn = umma::encode_tiled_fn();
+    if (!fn) return fail(MGC_CUDA_UNSUPPORTED, "depthwise: no cuTensorMapEncodeTiled");
+    CUtensorMap map;
+    const cuuint64_t dims[4] = {(cuuint64_t)p.C, (cuuint64_t)p.W, (cuuint64_t)p.H, (cuuint64_t)p.N};
+    const cuuint64_t strides[3] = {(cuuint64_t)p.C * 4, (cuuint64_t)p.W * p.C * 4, (cuuint64_t)p.H * p.W * p.C * 4};
+    const cuuint32_t box[4] = {(cuuint32_t)(t.cg * 4), (cuuint32_t)((t.tw - 1) * S + 3), 1, 1};
+    const cuuint32_t estr[4] = {1, 1, 1, 1};
+    const CUresult r = fn(&map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, const_cast<float *>(p.x), dims, strides, box, estr,
+                          CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_128B,
+                          CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS) return fail(MGC_CUDA_UNSUPPORTED, "depthwise: tensor map (%d)", (int)r);
+    const long long blocks = (long long)p.N * t.tiles * t.chunks * t.bands;
+    depthwise_tma_kernel<S, D><<<(unsigned)blocks, t.tw * t.cg, smem, s>>>(p, t, map);
+    return check_launch("depthwise_tma_kernel");
+}
+
 template <typename T>
 inline int launch_tile_t(const TileParams &P, cudaStream_t s) {
     tile_kernel<T><<<grid_for(P.total, 256), 256, 0, s>>>(P);
@@ -298,6 +389,7 @@ inline int launch_record(const mgc_cuda_launch &L, const int64_t *aux, int64_t a
         p.lo = (float)L.f[0]; p.hi = (float)L.f[1];
         MGC_RESOLVE(L.r[0], p.x); MGC_RESOLVE(L.r[1], p.w); MGC_RESOLVE(L.r[2], p.bias);
         MGC_RESOLVE(L.r[3], p.res); MGC_RESOLVE(L.r[4], p.y);
+        p.err = status_dev;
         const long long total = (long long)p.N * p.OH * p.OW * p.C;
         if (total == 0) { launched = 0; break; }
         const bool vec4 = p.nhwc && p.C % 4 == 0 &&
@@ -306,6 +398,26 @@ inline int launch_record(const mgc_cuda_launch &L, const int64_t *aux, int64_t a
         const int c4 = p.C / 4;
         const bool reg = vec4 && p.KH <= 3 && p.KW <= 3 && c4 <= 256 &&
                          (long long)p.N * p.H * p.W * c4 < (1ll << 31) && total / 4 < (1ll << 31);
+        const uintptr_t any_ptr = ((uintptr_t)p.x) | ((uintptr_t)p.w) | ((uintptr_t)p.y) | ((uintptr_t)p.bias) |
+                                  ((uintptr_t)p.res);
+        // 3x3, stride 1 or 2: row bands (depthwise.cuh), the ring filled by TMA when C % 4 == 0 and
+        // the tensors are 16-byte aligned, else by cp.async. MGC_CUDA_DW selects a form for
+        // comparisons: "ring" (cp.async, four channels per thread where possible), "ring2" (two),
+        // "legacy" (the forms below).
+        const char *form_env = getenv("MGC_CUDA_DW");
+        const std::string form = form_env ? form_env : "tma";
+        const bool band = form != "legacy" && p.nhwc && p.KH == 3 && p.KW == 3 && p.DH == 1 && p.DW == 1 &&
+                          p.SH == p.SW && (p.SW == 1 || p.SW == 2) && p.C % 2 == 0 && any_ptr % 8 == 0;
+        if (band) {
+            const bool v4 = p.C % 4 == 0 && any_ptr % 16 == 0;
+            if (v4 && form == "tma")
+                st = p.SW == 1 ? launch_dw_tma<1>(p, stream) : launch_dw_tma<2>(p, stream);
+            else if (v4 && form != "ring2")
+                st = p.SW == 1 ? launch_dw_ring<1, 4>(p, stream) : launch_dw_ring<2, 4>(p, stream);
+            else
+                st = p.SW == 1 ? launch_dw_ring<1, 2>(p, stream) : launch_dw_ring<2, 2>(p, stream);
+            break;
+        }
         if (reg && p.DH == 1 && p.DW == 1 && p.SH == p.SW && (p.SW == 1 || p.SW == 2) && c4 % 4 == 0 && p.OW >= 16) {
             // shared-memory tiles: the input window of a tile crosses L2 once
             st = p.SW == 1 ? (c4 % 8 == 0 ? launch_dw_tile<1, 8>(p, stream) : launch_dw_tile<1, 4>(p, stream))

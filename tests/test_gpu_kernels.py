@@ -185,6 +185,52 @@ def test_pool_and_depthwise_vs_torch() -> None:
     np.testing.assert_allclose(Y.cpu().numpy(), ref.cpu().numpy(), rtol=1e-5, atol=1e-5)
 
 
+@pytest.mark.parametrize("n,h,w,c,s,pad,act,res", [
+    (2, 14, 14, 384, 1, 1, 2, False),  # MobileNetV2's 14 x 14 layers: four channels per thread
+    (3, 7, 7, 960, 1, 1, 2, True),      # 7 x 7, 30 channel vectors per block, residual
+    (2, 15, 9, 18, 2, 1, 1, True),      # C % 4 == 2: two channels per thread, odd sizes
+    (1, 20, 33, 6, 1, 0, 0, False),     # no padding, two channels per thread
+    (2, 28, 28, 144, 2, 1, 2, False),   # stride 2, even input
+    (1, 5, 4, 40, 2, 0, 1, True),       # one output row and column per band
+    (4, 112, 112, 32, 1, 1, 2, False),  # MobileNetV2's first depthwise layer
+])
+def test_depthwise_bands_vs_torch(n: int, h: int, w: int, c: int, s: int, pad: int, act: int, res: bool) -> None:
+    """The row-band depthwise forms (3x3, stride 1 or 2; a shared-memory ring of input rows
+    filled by TMA, or by cp.async with four or two channels per thread; any padding) against a
+    float64 depthwise convolution, and bit-identical to each other (the same order of
+    accumulation); the older forms (MGC_CUDA_DW=legacy) give the same values to the same
+    tolerance."""
+    import os
+
+    rng = np.random.default_rng(h * w * c + s)
+    oh, ow = (h + 2 * pad - 3) // s + 1, (w + 2 * pad - 3) // s + 1
+    x = rng.standard_normal((n, h, w, c)).astype(np.float32)
+    wt = (rng.standard_normal((3, 3, c)) * 0.3).astype(np.float32)
+    b = rng.standard_normal(c).astype(np.float32)
+    r = rng.standard_normal((n, oh, ow, c)).astype(np.float32)
+    X, W, B, R = dev(x), dev(wt), dev(b), dev(r)
+    ref = torch.nn.functional.conv2d(X.permute(0, 3, 1, 2).double(), W.permute(2, 0, 1).unsqueeze(1).double(),
+                                     B.double(), stride=s, padding=pad, groups=c).permute(0, 2, 3, 1)
+    if res:
+        ref = ref + R.double()
+    ref = {0: ref, 1: ref.relu(), 2: ref.clamp(0, 6)}[act]
+    outs = []
+    forms = ("tma", "ring", "ring2", "legacy")
+    for form in forms:
+        os.environ["MGC_CUDA_DW"] = form
+        try:
+            Y = torch.full((n, oh, ow, c), float("nan"), device="cuda")
+            ok(library().mgc_cuda_depthwise_nhwc(n, h, w, c, 3, 3, s, s, 1, 1, pad, pad, oh, ow, ptr(X), ptr(W),
+                                                 ptr(B), ptr(R) if res else None, act, 0.0, 6.0, ptr(Y), stream()))
+            torch.cuda.synchronize()
+        finally:
+            del os.environ["MGC_CUDA_DW"]
+        np.testing.assert_allclose(Y.cpu().numpy(), ref.cpu().numpy(), rtol=1e-5, atol=1e-5, err_msg=f"form {form}")
+        outs.append(Y.cpu().numpy())
+    for form, out in zip(forms[1:-1], outs[1:-1]):
+        np.testing.assert_array_equal(out, outs[0], err_msg=form)
+
+
 @pytest.mark.parametrize("n,h,w,c,s,act", [(2, 30, 45, 48, 1, 2), (1, 57, 33, 64, 2, 1), (3, 19, 70, 32, 1, 0),
                                            (2, 40, 36, 16, 2, 2)])
 def test_depthwise_tiles_vs_torch(n: int, h: int, w: int, c: int, s: int, act: int) -> None:
