@@ -83,16 +83,21 @@ __device__ __forceinline__ void dw_weights(const DepthwiseParams &p, int c, floa
     }
 }
 
+// Activations the band forms apply in the store: compile-time cases for the common ones.
+enum DwAct { DW_NONE = 0, DW_RELU = 1, DW_CLIP = 2, DW_ANY = 3 /* p.act at run time */ };
+
 // The walk of one thread down output rows [oh0, oh1) of its column; `next_row(v)` delivers the
 // next input row's three taps (false: stop, the block gave up waiting). o_off: the element
 // offset of output row oh0 of this thread's column and channels; `active`: the column exists.
-template <int S, int VEC, typename NextRow>
+template <int S, int VEC, int ACT, typename NextRow>
 __device__ __forceinline__ void dw_walk(const DepthwiseParams &p, const float2 (&wk)[9][VEC / 2],
                                         const float2 (&bias)[VEC / 2], int oh0, int oh1, long long o_off,
                                         bool active, NextRow &next_row) {
     constexpr int P = VEC / 2;
     using V = typename DwVec<VEC>::T;
-    const long long ostride = (long long)p.OW * p.C;
+    V *yp = reinterpret_cast<V *>(p.y + o_off);
+    const long long vstride = (long long)p.OW * p.C / VEC;  // output row stride in vectors
+    const long long res_delta = p.res ? p.res - p.y : 0;   // the residual's element offset from the output
     auto taps = [&](float2 (&acc)[P], const float2 (&v)[3][P], int kh, bool fresh) {
 #pragma unroll
         for (int j = 0; j < P; ++j) {
@@ -108,24 +113,24 @@ __device__ __forceinline__ void dw_walk(const DepthwiseParams &p, const float2 (
         if (active) {
             if (p.res) {
                 float2 r[P];
-                DwVec<VEC>::split(*reinterpret_cast<const V *>(p.res + o_off), r);
+                DwVec<VEC>::split(*reinterpret_cast<const V *>(reinterpret_cast<const float *>(yp) + res_delta), r);
 #pragma unroll
                 for (int j = 0; j < P; ++j) acc[j] = __fadd2_rn(acc[j], r[j]);
             }
 #pragma unroll
             for (int j = 0; j < P; ++j) {
                 float2 &a = acc[j];
-                if (p.act == MGC_ACT_RELU) {
+                if (ACT == DW_RELU || (ACT == DW_ANY && p.act == MGC_ACT_RELU)) {
                     a.x = fmaxf(a.x, 0.0f); a.y = fmaxf(a.y, 0.0f);
-                } else if (p.act == MGC_ACT_CLIP) {
+                } else if (ACT == DW_CLIP || (ACT == DW_ANY && p.act == MGC_ACT_CLIP)) {
                     a.x = fminf(fmaxf(a.x, p.lo), p.hi); a.y = fminf(fmaxf(a.y, p.lo), p.hi);
-                } else if (p.act != MGC_ACT_NONE) {
+                } else if (ACT == DW_ANY && p.act != MGC_ACT_NONE) {
                     a.x = apply_act(a.x, p.act, p.lo, p.hi); a.y = apply_act(a.y, p.act, p.lo, p.hi);
                 }
             }
-            *reinterpret_cast<V *>(p.y + o_off) = DwVec<VEC>::join(acc);
+            *yp = DwVec<VEC>::join(acc);
         }
-        o_off += ostride;
+        yp += vstride;
     };
     float2 v[3][P];
     float2 a0[P], a1[P], a2[P];
@@ -167,13 +172,13 @@ __device__ __forceinline__ void dw_walk(const DepthwiseParams &p, const float2 (
     (void)a2;
 }
 
-template <int S, int D>
+template <int S, int D, int ACT>
 __global__ void __launch_bounds__(256, 3) depthwise_tma_kernel(const __grid_constant__ DepthwiseParams p, const DwBand t,
                                                             const __grid_constant__ CUtensorMap map) {
     constexpr int VEC = 4;
     extern __shared__ uint8_t dw_smem_raw[];
-    // [D slots, each 128-byte aligned][D full barriers]
-    uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(dw_smem_raw) + 127) & ~uintptr_t(127));
+    // [D slots, each 128-byte aligned][D full barriers]; aligned by an offset into the window
+    uint8_t *smem = dw_smem_raw + ((128u - (umma::smem_addr(dw_smem_raw) & 127u)) & 127u);
     const DwPlace at(t);
     const int g = (int)threadIdx.x % t.cg, col = (int)threadIdx.x / t.cg;
     const int ow = (int)at.ct * t.tw + col;
@@ -190,42 +195,56 @@ __global__ void __launch_bounds__(256, 3) depthwise_tma_kernel(const __grid_cons
     }
     __syncthreads();
     const int cx = (int)at.chunk * t.cg * VEC, wx = (int)at.ct * t.tw * S - p.PL, hy = oh0 * S - p.PT;
-    int issued = 0;  // rows whose loads were issued (the same count in every thread)
-    auto issue = [&]() {
-        if (issued < rows) {
-            if (leader) {
-                const int s = issued % D;
-                umma::mbar_expect_tx(&full[s], slot_bytes);
-                umma::tma_load_4d(smem + (size_t)s * slot_stride, &map, &full[s], cx, wx, hy + issued, (int)at.n);
-            }
-            ++issued;
+    // the leader loads band row r into slot s
+    auto issue = [&](int r, int s) {
+        if (leader && r < rows) {
+            umma::mbar_expect_tx(&full[s], slot_bytes);
+            umma::tma_load_4d(smem + (size_t)s * slot_stride, &map, &full[s], cx, wx, hy + r, (int)at.n);
         }
     };
-    for (int r = 0; r < D - 1; ++r) issue();
+    for (int r = 0; r < D - 1; ++r) issue(r, r);
     float2 wk[9][2], bias[2];
     const int c = cx + g * VEC;
     dw_weights<VEC>(p, c, wk, bias);
+    // this thread's first tap in a slot, the slot in use and its barrier's phase parity
+    const uint32_t ring_s = umma::smem_addr(smem);
+    const uint32_t tap0 = (uint32_t)(col * S * t.cg + g) * 16u, kw_bytes = (uint32_t)t.cg * 16u;
+    int s_use = 0;
+    uint32_t parity = 0, slot_addr = ring_s;
     int used = 0;  // rows taken from the ring
     bool failed = false;
     auto next_row = [&](float2 (&v)[3][2]) -> bool {
         // every thread is done with the previous row's slot, which the next load refills
         if (__syncthreads_or(failed)) return false;
-        issue();
-        const int s = used % D;
-        if (!umma::mbar_wait(&full[s], (uint32_t)((used / D) & 1))) {
+        issue(used + D - 1, s_use == 0 ? D - 1 : s_use - 1);
+        if (!umma::mbar_wait(&full[s_use], parity)) {
             failed = true;
             umma::set_error(p.err, MGC_CUDA_TIMEOUT);
         }
-        const float4 *row = reinterpret_cast<const float4 *>(smem + (size_t)s * slot_stride) + col * S * t.cg + g;
+        const uint32_t a = slot_addr + tap0;
 #pragma unroll
-        for (int kw = 0; kw < 3; ++kw) DwVec<VEC>::split(row[kw * t.cg], v[kw]);
+        for (int kw = 0; kw < 3; ++kw) {
+            float4 x;
+            asm volatile("ld.shared.v4.f32 {%0, %1, %2, %3}, [%4];"
+                         : "=f"(x.x), "=f"(x.y), "=f"(x.z), "=f"(x.w)
+                         : "r"(a + (uint32_t)kw * kw_bytes));
+            DwVec<VEC>::split(x, v[kw]);
+        }
         ++used;
+        if (++s_use == D) {
+            s_use = 0;
+            parity ^= 1u;
+            slot_addr = ring_s;
+        } else {
+            slot_addr += slot_stride;
+        }
         return true;
     };
     const long long o_off = (((long long)at.n * p.OH + oh0) * p.OW + ow) * p.C + c;
-    dw_walk<S, VEC>(p, wk, bias, oh0, oh1, o_off, ow < p.OW, next_row);
+    dw_walk<S, VEC, ACT>(p, wk, bias, oh0, oh1, o_off, ow < p.OW, next_row);
     // a block that gave up waits (bounded) for the loads it issued before its shared memory goes
     if (__syncthreads_or(failed) && leader) {
+        const int issued = min(rows, used + D - 1);
         for (int r = used; r < issued; ++r) (void)umma::mbar_wait(&full[r % D], (uint32_t)((r / D) & 1));
     }
 }
@@ -305,7 +324,7 @@ __global__ void __launch_bounds__(256, VEC == 4 ? 3 : 4) depthwise_ring_kernel(c
         return true;
     };
     const long long o_off = (((long long)at.n * p.OH + oh0) * p.OW + ow) * p.C + c;
-    dw_walk<S, VEC>(p, wk, bias, oh0, oh1, o_off, ow < p.OW, next_row);
+    dw_walk<S, VEC, DW_ANY>(p, wk, bias, oh0, oh1, o_off, ow < p.OW, next_row);
     asm volatile("cp.async.wait_all;" ::: "memory");
 }
 

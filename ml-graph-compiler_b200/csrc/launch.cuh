@@ -332,11 +332,11 @@ inline int launch_dw_ring(const DepthwiseParams &p, cudaStream_t s) {
 
 // The TMA form: a 4-D map of the input (channels, columns, rows, images) with boxes of one band
 // row (cg * 4 channels x (tw - 1) * S + 3 columns); out-of-range boxes read zeros.
-template <int S, int D = DW_SLOTS>
-inline int launch_dw_tma(const DepthwiseParams &p, cudaStream_t s) {
+template <int S, int ACT, int D = DW_SLOTS>
+inline int launch_dw_tma_act(const DepthwiseParams &p, cudaStream_t s) {
     DwBand t;
     unsigned smem = 0;
-    const void *k = (const void *)depthwise_tma_kernel<S, D>;
+    const void *k = (const void *)depthwise_tma_kernel<S, D, ACT>;
     // each slot rounded up to 128 bytes, D barriers, 128 bytes of alignment slack
     MGC_CHECK(dw_band_shape(p, 4, S, k, D, (256 - 3) / S + 1, D * 16, D * (128 + 8) + 128, t, smem));
     auto fn = umma::encode_tiled_fn();
@@ -351,8 +351,19 @@ inline int launch_dw_tma(const DepthwiseParams &p, cudaStream_t s) {
                           CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
     if (r != CUDA_SUCCESS) return fail(MGC_CUDA_UNSUPPORTED, "depthwise: tensor map (%d)", (int)r);
     const long long blocks = (long long)p.N * t.tiles * t.chunks * t.bands;
-    depthwise_tma_kernel<S, D><<<(unsigned)blocks, t.tw * t.cg, smem, s>>>(p, t, map);
+    depthwise_tma_kernel<S, D, ACT><<<(unsigned)blocks, t.tw * t.cg, smem, s>>>(p, t, map);
     return check_launch("depthwise_tma_kernel");
+}
+
+// The TMA band form with the activation resolved at compile time for none, ReLU and Clip.
+template <int S>
+inline int launch_dw_tma(const DepthwiseParams &p, cudaStream_t s) {
+    switch (p.act) {
+    case MGC_ACT_NONE: return launch_dw_tma_act<S, DW_NONE>(p, s);
+    case MGC_ACT_RELU: return launch_dw_tma_act<S, DW_RELU>(p, s);
+    case MGC_ACT_CLIP: return launch_dw_tma_act<S, DW_CLIP>(p, s);
+    default: return launch_dw_tma_act<S, DW_ANY>(p, s);
+    }
 }
 
 template <typename T>
