@@ -193,6 +193,8 @@ def test_pool_and_depthwise_vs_torch() -> None:
     (2, 28, 28, 144, 2, 1, 2, False),   # stride 2, even input
     (1, 5, 4, 40, 2, 0, 1, True),       # one output row and column per band
     (4, 112, 112, 32, 1, 1, 2, False),  # MobileNetV2's first depthwise layer
+    (130, 7, 7, 960, 1, 1, 2, True),    # more blocks than one wave, residual
+    (300, 8, 8, 512, 2, 1, 1, False),   # more blocks than one wave at stride 2
 ])
 def test_depthwise_bands_vs_torch(n: int, h: int, w: int, c: int, s: int, pad: int, act: int, res: bool) -> None:
     """The row-band depthwise forms (3x3, stride 1 or 2; a shared-memory ring of input rows
