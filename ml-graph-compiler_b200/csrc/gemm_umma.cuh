@@ -82,6 +82,8 @@ struct Params {
     CUtensorMap tmC;                 // output tile store (when tma_out)
     CUtensorMap tmR;                 // residual tile load (when tma_res)
     int tma_out, tma_res;
+    int out2;                        // a second output staging tile (after the bias), used by
+                                     // alternate epilogue passes: set by launch() when it fits
     int M, N, num_kb, n_tiles;
     int im2col;                      // 0 tiled A, 1 im2col (32-channel blocks), 2 tap-packed im2col,
                                      // 3 window rows, 4 row tiles, 5 phase-split row tiles
@@ -323,6 +325,10 @@ __device__ __forceinline__ void tma_store_commit() { asm volatile("cp.async.bulk
 
 // Every committed store of this thread has finished reading shared memory.
 __device__ __forceinline__ void tma_store_wait_read() { asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory"); }
+// Every committed store group but the most recent one has read its shared memory.
+__device__ __forceinline__ void tma_store_wait_read_but_one() {
+    asm volatile("cp.async.bulk.wait_group.read 1;" ::: "memory");
+}
 
 // Epilogue warps: two per TMEM lane quadrant, each taking half of the tile's columns.
 constexpr int EPI_THREADS = 256;
@@ -672,6 +678,8 @@ __global__ void __launch_bounds__(THREADS, 1) umma_gemm_kernel(const __grid_cons
     uint64_t *bres_full = res_full + 1; // the B panel has landed (B-resident)
     uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(bres_full + 1);
     float *bias_s = reinterpret_cast<float *>(out_tile + C::OUT_BYTES + C::RES_BYTES + C::BAR_BYTES);  // [BN] bias
+    // the second staging tile (p.out2): the next 1024-byte boundary after the bias
+    uint8_t *out_tile2 = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(bias_s + BN) + 1023) & ~uintptr_t(1023));
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int num_kb = p.num_kb;
@@ -1272,7 +1280,10 @@ __global__ void __launch_bounds__(THREADS, 1) umma_gemm_kernel(const __grid_cons
             const int sl = c0 >> 5, j = (c0 & 31) >> 2;
             return (uint32_t)(sl * (BM * 128) + r * 128 + ((j ^ (r & 7)) << 4));
         };
-        auto stage_slot = [&](int r, int c0) { return reinterpret_cast<float4 *>(out_tile + stage_offset(r, c0)); };
+        // the staging tile of the current pass: with p.out2 the passes alternate between two, so
+        // that a pass stages while the previous pass's TMA store still reads its tile
+        uint8_t *stg = out_tile;
+        auto stage_slot = [&](int r, int c0) { return reinterpret_cast<float4 *>(stg + stage_offset(r, c0)); };
         // Output path. Step 1 (unrolled over the accumulator registers, no calls): alpha * acc +
         // bias (+ the residual, TMA-prefetched into the staging tile) and a ReLU / Clip, into the
         // 128B-swizzled staging tile. Step 2 (compact, own row): GELU / tanh / sigmoid. Then one
@@ -1355,7 +1366,13 @@ __global__ void __launch_bounds__(THREADS, 1) umma_gemm_kernel(const __grid_cons
             // the staging tile is free (the previous TMA store was read out: SR, and every form
             // without a residual, waits for it here rather than right after issuing it) and the
             // residual staging holds this pass's residual
-            if ((SR || !res_tma) && issuer) tma_store_wait_read();
+            stg = p.out2 && (local & 1) ? out_tile2 : out_tile;
+            if ((SR || !res_tma) && issuer) {
+                // with two staging tiles only the store that read this pass's tile (two passes
+                // back; one commit group per pass) must be done
+                if (p.out2) tma_store_wait_read_but_one();
+                else tma_store_wait_read();
+            }
             epilogue_sync();
             if (res_tma && !mbar_wait(res_full, (uint32_t)(local & 1))) {
                 ok = false;
@@ -1363,7 +1380,7 @@ __global__ void __launch_bounds__(THREADS, 1) umma_gemm_kernel(const __grid_cons
             }
             // 32 columns at a time: the residual and bias loads of a chunk are all issued before
             // its stores, so no load waits behind a store to the same staging tile
-            const uint32_t out_s = smem_addr(out_tile), res_s = smem_addr(res_tile);
+            const uint32_t out_s = smem_addr(stg), res_s = smem_addr(res_tile);
             const uint32_t bias_addr = smem_addr(bias_s);
 #pragma unroll
             for (int a0 = 0; a0 < HALF; a0 += 32) {  // a0: accumulator index; column hc + a0
@@ -1434,7 +1451,7 @@ __global__ void __launch_bounds__(THREADS, 1) umma_gemm_kernel(const __grid_cons
                         float s0 = 0.0f, s1 = 0.0f;
 #pragma unroll
                         for (int r = 0; r < 32; ++r) {
-                            const float x = reinterpret_cast<const float *>(out_tile + stage_offset(g * 32 + r, gc & ~3))[gc & 3];
+                            const float x = reinterpret_cast<const float *>(stg + stage_offset(g * 32 + r, gc & ~3))[gc & 3];
                             if (r < lim) {
                                 if (r < split) s0 += x;
                                 else s1 += x;
@@ -1521,13 +1538,13 @@ __global__ void __launch_bounds__(THREADS, 1) umma_gemm_kernel(const __grid_cons
                         const int img = mt / p.rt_per_img, oh0 = (mt - img * p.rt_per_img) * p.rt_rows;
 #pragma unroll 1
                         for (int sl = 0; sl < EN / 32; ++sl)
-                            tma_store_4d(&p.tmC, out_tile + sl * (BM * 128), n0 + sl * 32, 0, oh0, img);
+                            tma_store_4d(&p.tmC, stg + sl * (BM * 128), n0 + sl * 32, 0, oh0, img);
                     } else if (m0 < p.M && n0 < p.N) {  // (a pair's second half, or a wide tile's last
                                                          // passes, may lie wholly past the edge)
 #pragma unroll 1
                         for (int sl = 0; sl < EN / 32; ++sl) {
-                            if (MODE == DYN) tma_store_4d(&p.tmC, out_tile + sl * (BM * 128), n0 + sl * 32, m0, db1, db2);
-                            else tma_store_2d(&p.tmC, out_tile + sl * (BM * 128), n0 + sl * 32, m0);
+                            if (MODE == DYN) tma_store_4d(&p.tmC, stg + sl * (BM * 128), n0 + sl * 32, m0, db1, db2);
+                            else tma_store_2d(&p.tmC, stg + sl * (BM * 128), n0 + sl * 32, m0);
                         }
                     }
                     if (SR || !res_tma) {
@@ -1773,8 +1790,21 @@ inline uint32_t launch_smem(const Params &p) {
 }
 
 template <int BN, int MODE, int RB, int PAIR, int SR = 0, int PH = 0>
-inline int launch(const Params &p, int grid, cudaStream_t stream) {
-    const uint32_t smem = launch_smem<BN, MODE, RB, PAIR, SR, PH>(p);
+inline int launch(const Params &p_in, int grid, cudaStream_t stream) {
+    using C = Cfg<BN, MODE, RB, PAIR, SR, PH>;
+    Params p = p_in;
+    uint32_t smem = launch_smem<BN, MODE, RB, PAIR, SR, PH>(p);
+    // a second output staging tile where shared memory has room for it and the epilogue stores
+    // by TMA without a residual staged in the output tile (MGC_CUDA_OUT2=0 keeps one, for
+    // comparisons)
+    p.out2 = 0;
+    if (MODE != STRICT && !SR && p.tma_out && !p.tma_res && p.splits <= 1 &&
+        C::SMEM_BYTES + (RB ? p.b_res_bytes : 0u) + C::OUT_BYTES + 1024 <= SMEM_LIMIT &&
+        !(getenv("MGC_CUDA_OUT2") && getenv("MGC_CUDA_OUT2")[0] == '0')) {
+        p.out2 = 1;
+        const uint32_t need = C::SMEM_BYTES + (RB ? p.b_res_bytes : 0u) + C::OUT_BYTES + 1024;
+        if (need > smem) smem = need;
+    }
     // per device (the attribute belongs to the current context); cheap, and allowed under capture
     MGC_CHECK_CUDA(cudaFuncSetAttribute(umma_gemm_kernel<BN, MODE, RB, PAIR, SR, PH>,
                                         cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
