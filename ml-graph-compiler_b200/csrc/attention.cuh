@@ -486,7 +486,7 @@ inline int launch_attention(const AttnArgs &a, cudaStream_t stream) {
     else if (!a.div && p.mask_vec && a.mode == MASK_FILL && p.mask_u8) form = FORM_MUL_FILL;
     else if (!a.div && p.mask_vec && a.mode == MASK_KEEP && p.mask_u8) form = FORM_MUL_KEEP;
     auto go = [&](auto kern) -> int {
-        MGC_CHECK_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+        MGC_CHECK(raise_smem_ceiling((const void *)kern));
         kern<<<(unsigned)grid, THREADS, smem, stream>>>(p);
         return check_launch("attention_kernel");
     };

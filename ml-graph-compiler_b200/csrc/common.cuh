@@ -5,7 +5,10 @@
 #include <stdint.h>
 #include <stdio.h>
 #include <stdarg.h>
+#include <mutex>
+#include <set>
 #include <string>
+#include <utility>
 
 #include "mgc_cuda.h"
 
@@ -87,6 +90,28 @@ inline int sm_count() {
 
 // Grid size for a grid-stride loop over `n` items: a multiple of the SM count (148 on B200),
 // capped, never zero.
+// Let `kernel` launch with up to the device's opt-in maximum of dynamic shared memory, once per
+// device. The ceiling goes to the maximum rather than to each launch's own size: a kernel whose
+// launches need different sizes (a B panel, a second output staging tile) would otherwise be
+// left with the last launch's ceiling, below what an earlier launch captured into a CUDA Graph
+// needs when that node is launched again on its own (as a profiler replays graph nodes).
+inline int raise_smem_ceiling(const void *kernel) {
+    static std::mutex mu;
+    static std::set<std::pair<const void *, int>> done;
+    int dev = 0;
+    MGC_CHECK_CUDA(cudaGetDevice(&dev));
+    std::lock_guard<std::mutex> guard(mu);
+    if (done.count({kernel, dev})) return MGC_CUDA_OK;
+    int optin = 0;
+    MGC_CHECK_CUDA(cudaDeviceGetAttribute(&optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev));
+    cudaFuncAttributes fa;
+    MGC_CHECK_CUDA(cudaFuncGetAttributes(&fa, kernel));
+    MGC_CHECK_CUDA(cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                        optin - (int)fa.sharedSizeBytes));
+    done.insert({kernel, dev});
+    return MGC_CUDA_OK;
+}
+
 inline unsigned grid_for(int64_t n, int threads, int sms = 148, int per_sm = 8) {
     int64_t blocks = ceil_div(n, threads);
     int64_t cap = (int64_t)sms * per_sm;

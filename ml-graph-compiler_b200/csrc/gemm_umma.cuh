@@ -1805,9 +1805,8 @@ inline int launch(const Params &p_in, int grid, cudaStream_t stream) {
         const uint32_t need = C::SMEM_BYTES + (RB ? p.b_res_bytes : 0u) + C::OUT_BYTES + 1024;
         if (need > smem) smem = need;
     }
-    // per device (the attribute belongs to the current context); cheap, and allowed under capture
-    MGC_CHECK_CUDA(cudaFuncSetAttribute(umma_gemm_kernel<BN, MODE, RB, PAIR, SR, PH>,
-                                        cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+    // per device (the attribute belongs to the current context); allowed under capture
+    MGC_CHECK(raise_smem_ceiling((const void *)umma_gemm_kernel<BN, MODE, RB, PAIR, SR, PH>));
     if (!PAIR) {
         umma_gemm_kernel<BN, MODE, RB, PAIR, SR, PH><<<grid, THREADS, smem, stream>>>(p);
         return check_launch("umma_gemm_kernel");

@@ -259,8 +259,7 @@ inline int launch_dw_tile(const DepthwiseParams &p, cudaStream_t s) {
     const unsigned chunks = (unsigned)(p.C / 4 / CG);
     const long long blocks = (long long)p.N * row_tiles * col_tiles * chunks;
     if (blocks >= (1ll << 31)) return fail(MGC_CUDA_UNSUPPORTED, "depthwise: %lld tiles", blocks);
-    MGC_CHECK_CUDA(cudaFuncSetAttribute(depthwise_nhwc4_tile_kernel<S, CG>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                        (int)T::SMEM));
+    MGC_CHECK(raise_smem_ceiling((const void *)depthwise_nhwc4_tile_kernel<S, CG>));
     depthwise_nhwc4_tile_kernel<S, CG><<<(unsigned)blocks, 256, T::SMEM, s>>>(p, row_tiles, col_tiles, chunks);
     return check_launch("depthwise_nhwc4_tile_kernel");
 }
@@ -292,8 +291,7 @@ inline int dw_band_shape(const DepthwiseParams &p, int vec, int S, const void *k
     t.chunks = (unsigned)(cv / t.cg);
     const int threads = t.tw * t.cg;
     smem = smem_per_vec * (unsigned)(((t.tw - 1) * S + 3) * t.cg) + smem_extra;
-    if (smem > 48 * 1024)
-        MGC_CHECK_CUDA(cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+    MGC_CHECK(raise_smem_ceiling(kernel));
     int per_sm = 0;
     MGC_CHECK_CUDA(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kernel, threads, smem));
     int dev = 0, sms = 148;
