@@ -145,6 +145,26 @@ def test_global_average_pool_from_epilogue_partials(monkeypatch: pytest.MonkeyPa
     assert float(np.abs(got["1"] - got["0"]).max()) <= 1e-5 * scale
 
 
+def test_second_output_staging_tile_is_exact(monkeypatch: pytest.MonkeyPatch) -> None:
+    """TF32 MobileNetV2 at batch 32, whose write-heavy 1x1 GEMMs stage their output in two
+    shared-memory tiles where the B panel leaves room: the passes alternate between the tiles,
+    which changes when a store may start but no arithmetic, so the logits equal those with one
+    staging tile (MGC_CUDA_OUT2=0) bit for bit."""
+    g = zoo.mobilenet_v2(batch=32, seed=1)
+    optimize(g, "O3")
+    schedule(g)
+    x = {"image": np.random.default_rng(5).standard_normal((32, 3, 224, 224)).astype(np.float32)}
+    got = {}
+    for flag in ("1", "0"):
+        monkeypatch.setenv("MGC_CUDA_OUT2", flag)
+        m = compile_graph(g, precision="tf32")
+        try:
+            got[flag] = m.run(x)["logits"]
+        finally:
+            m.close()
+    np.testing.assert_array_equal(got["1"], got["0"])
+
+
 def test_resnet50_batch_is_independent_per_image() -> None:
     """Size-independent property at a larger batch: every image of a batch-8 run equals the
     batch-1 model's output for that image (strict mode, bit-level batch independence is not
