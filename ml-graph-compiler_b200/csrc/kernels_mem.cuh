@@ -635,6 +635,35 @@ __global__ void __launch_bounds__(256) ew_vec4_kernel(const __grid_constant__ Ew
 // ---------------------------------------------------------------------------------------------
 constexpr int COPY_MAX_RANK = 8;
 
+// A Split along the last axis into up to SPLIT_MAX_OUT contiguous outputs in one pass over the
+// input: source [rows][total], output j [rows][start[j + 1] - start[j]] (in units of T, one
+// fp32 or four). Each thread moves one unit: reads are coalesced along the input row, writes
+// along each output row.
+constexpr int SPLIT_MAX_OUT = 4;
+
+template <typename T>
+struct SplitParams {
+    const T *src;
+    T *dst[SPLIT_MAX_OUT];
+    long long rows;
+    int total, k;
+    int start[SPLIT_MAX_OUT + 1];
+};
+
+template <typename T>
+__global__ void __launch_bounds__(256) split_last_kernel(const __grid_constant__ SplitParams<T> p) {
+    const long long n = p.rows * p.total;
+    for (long long e = (long long)blockIdx.x * blockDim.x + threadIdx.x; e < n; e += (long long)gridDim.x * blockDim.x) {
+        const long long r = e / p.total;
+        const int c = (int)(e - r * p.total);
+        int j = 0;
+#pragma unroll
+        for (int t = 1; t < SPLIT_MAX_OUT; ++t) j += (t < p.k && c >= p.start[t]) ? 1 : 0;
+        const int w = p.start[j + 1] - p.start[j];
+        p.dst[j][r * w + (c - p.start[j])] = p.src[e];
+    }
+}
+
 struct CopyParams {
     long long shape[COPY_MAX_RANK];
     long long sstr[COPY_MAX_RANK];

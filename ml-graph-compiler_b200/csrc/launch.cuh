@@ -579,6 +579,40 @@ inline int launch_record(const mgc_cuda_launch &L, const int64_t *aux, int64_t a
         long long total = 1;
         for (int d = 0; d < rank; ++d) total *= i[2 + d];
         if (total == 0) { launched = 0; break; }
+        if (i[28] == 2) {  // Split along the last axis: i[29] outputs of widths i[30..33], i[34] rows
+            const int k = (int)i[29];
+            if (esize != 4 || k < 1 || k > SPLIT_MAX_OUT) return fail(MGC_CUDA_UNSUPPORTED, "split: %d outputs", k);
+            char *outs[SPLIT_MAX_OUT] = {};
+            uintptr_t any = (uintptr_t)src;
+            long long width = 0;
+            bool vec = true;
+            for (int j = 0; j < k; ++j) {
+                MGC_RESOLVE(L.r[1 + j], outs[j]);
+                any |= (uintptr_t)outs[j];
+                vec = vec && i[30 + j] % 4 == 0;
+                width += i[30 + j];
+            }
+            const long long rows = i[34];
+            vec = vec && any % 16 == 0;
+            if (rows * width == 0) { launched = 0; break; }
+            if (width >= (1ll << 31)) return fail(MGC_CUDA_UNSUPPORTED, "split: row of %lld", width);
+            auto go = [&](auto unit, int per) -> int {
+                using T = decltype(unit);
+                SplitParams<T> P{};
+                P.src = reinterpret_cast<const T *>(src);
+                P.rows = rows;
+                P.k = k;
+                P.total = (int)(width / per);
+                for (int j = 0; j < k; ++j) {
+                    P.dst[j] = reinterpret_cast<T *>(outs[j]);
+                    P.start[j + 1] = P.start[j] + (int)(i[30 + j] / per);
+                }
+                split_last_kernel<T><<<grid_for(rows * P.total, 256), 256, 0, stream>>>(P);
+                return check_launch("split_last_kernel");
+            };
+            st = vec ? go(uint4{}, 4) : go(uint32_t{}, 1);
+            break;
+        }
         if (i[28] == 1) {  // Tile
             TileParams P{};
             P.rank = rank; P.esize = esize; P.total = total; P.src = src; P.dst = dst;

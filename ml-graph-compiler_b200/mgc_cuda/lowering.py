@@ -62,6 +62,7 @@ EW_OPS = [
 ]
 EW_CODE = {name: i for i, name in enumerate(EW_OPS)}
 EW_MAX_RANK, EW_MAX_LEAVES, EW_MAX_INSTR, COPY_MAX_RANK = 6, 20, 40, 8
+SPLIT_MAX_OUT = 4  # outputs of one split-mode copy (csrc/kernels_mem.cuh)
 SOFTMAX_ROW_MAX = 1024  # longest row the register-resident softmax holds (kernels_norm.cuh)
 # fused attention (csrc/attention.cuh): keys per row, head widths, shared memory per CTA
 ATTN_MAX_SK, ATTN_MAX_D, ATTN_SMEM_LIMIT = 256, 128, 232448 - 1024
@@ -570,7 +571,7 @@ class CudaEmitter:
     ) -> None:
         """K_COPY slots: i[0] rank, i[1] element bytes, i[2..9] shape, i[10..17] source strides,
         i[18] source base, i[19..26] destination strides, i[27] destination base (elements),
-        i[28] 0 (1 selects Tile); r[0] source, r[1] destination."""
+        i[28] 0 (1 selects Tile, 2 the split mode of _split_copy); r[0] source, r[1] destination."""
         if int(np.prod([int(d) for d in shape])) == 0:
             return
         dims, (ss, ds) = _collapse([int(d) for d in shape], [list(src_strides), list(dst_strides)])
@@ -763,15 +764,36 @@ class CudaEmitter:
         axis = axis + xt.rank if axis < 0 else axis
         ss = _strides(xt.shape)
         offset = 0
-        for out_v in node.outputs:
+        views = [self._split_view(node, out_v) for out_v in node.outputs]
+        wanted = [bool(out_v.users) or out_v in self.graph.outputs for out_v in node.outputs]
+        if (axis == xt.rank - 1 and xt.itemsize == 4 and 2 <= len(node.outputs) <= SPLIT_MAX_OUT
+                and not any(views) and all(wanted) and xt.size):
+            # every output copied: one pass over the input writes them all (K_COPY split mode)
+            self._split_copy(x, list(node.outputs))
+            return
+        for out_v, view in zip(node.outputs, views, strict=True):
             t = out_v.tensor_type
-            if self._split_view(node, out_v):
+            if view:
                 self._split_src[id(out_v)] = (x, list(ss), offset * ss[axis])
                 self.kernels["view"] = self.kernels.get("view", 0) + 1
             elif out_v.users or out_v in self.graph.outputs:
                 self._copy(t.shape, self.ref(x), ss, offset * ss[axis], self.ref(out_v), _strides(t.shape), 0,
                            xt.itemsize)
             offset += t.shape[axis]
+
+    def _split_copy(self, x: Value, outs: list[Value]) -> None:
+        """K_COPY in split mode: i[28] 2, i[0] 2 and i[2..3] (rows, row width) for the generic
+        checks, i[1] element bytes, i[29] outputs, i[30..33] their widths along the last axis,
+        i[34] rows; r[0] the input, r[1..] the outputs (each contiguous)."""
+        xt = x.tensor_type
+        width = int(xt.shape[-1])
+        rows = int(xt.size) // width
+        ints = [0] * 35
+        ints[0], ints[1], ints[2], ints[3] = 2, xt.itemsize, rows, width
+        ints[28], ints[29], ints[34] = 2, len(outs), rows
+        for j, o in enumerate(outs):
+            ints[30 + j] = int(o.tensor_type.shape[-1])
+        self.emit(K_COPY, ints, refs=[self.ref(x)] + [self.ref(o) for o in outs], count="split")
 
     @staticmethod
     def _split_strides(vshape: Sequence[int], strides: list[int], shape: Sequence[int]) -> list[int] | None:

@@ -66,3 +66,26 @@ def test_cases_match_reference_interpreter_fixtures(golden_ops: dict) -> None:
         want = {k.split("|")[2]: v for k, v in golden_ops.items() if k.startswith(f"{case.name}|out|")}
         assert_parity(got, want, "strict", case.name)
         model.close()
+
+
+@pytest.mark.parametrize("shape,sizes", [((3, 5, 24), [8, 12, 4]), ((7, 9), [2, 3, 4]), ((4, 33, 16), [4, 12]),
+                                         ((2, 6, 20), [4, 4, 4, 4, 4])])
+def test_split_along_the_last_axis(shape: tuple, sizes: list) -> None:
+    """A Split along the last axis whose outputs are all copied: up to four outputs in one
+    split-mode copy record (four floats per thread when every width is a multiple of four and the
+    buffers are 16-byte aligned, else one), more as one copy per output. Bit-exact with the
+    oracle."""
+    rng = np.random.default_rng(sum(shape) + len(sizes))
+    g, feeds = cases.op_graph("Split", [("in", cases.f32(rng, *shape)), ("const", np.asarray(sizes))],
+                              {"axis": -1}, n_outputs=len(sizes))
+    want = runner.run(g, feeds)
+    model = compile_graph(g, precision="tf32")
+    try:
+        splits = [r for r in model.lowered.launches if r.kind == 8 and r.i[28] == 2]
+        assert len(splits) == (1 if len(sizes) <= 4 else 0)
+        got = model.run(feeds)
+        assert set(got) == set(want)
+        for name, w in want.items():
+            np.testing.assert_array_equal(got[name], w)
+    finally:
+        model.close()

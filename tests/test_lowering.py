@@ -455,10 +455,16 @@ def test_no_gemm_writes_over_an_operand_it_reads(name: str, precision: str, stra
 def test_gpt2_split_outputs_are_views_on_the_naive_plan() -> None:
     """GPT-2's fused QKV output is split into Q, K and V, each read only by head Transposes: with
     every buffer in its own memory the Split copies nothing (the Transposes read the QKV buffer
-    through strides); with the greedy plan, whose later buffers reuse that memory, it copies."""
+    through strides); with the greedy plan, whose later buffers reuse that memory, each layer's
+    Split copies its three outputs in one split-mode copy record (one pass over the QKV rows)."""
     g = zoo.gpt2(batch=2, seq=128)
     optimize(g, "O3")
     schedule(g)
     naive = lower_graph(g, strategy="naive")
-    assert "copy" not in naive.kernels
-    assert lower_graph(g).kernels.get("copy") == 36
+    assert "copy" not in naive.kernels and "split" not in naive.kernels
+    greedy = lower_graph(g)
+    assert greedy.kernels.get("split") == 12 and "copy" not in greedy.kernels
+    splits = [r for r in greedy.launches if r.kind == lowering.K_COPY and r.i[28] == 2]
+    assert len(splits) == 12
+    for rec in splits:
+        assert rec.i[29] == 3 and list(rec.i[30:33]) == [768, 768, 768] and rec.i[34] == 2 * 128
