@@ -633,8 +633,26 @@ class CudaEmitter:
             for v in later.outputs:
                 r = self._arena_range(v)
                 if own is not None and r is not None and r[0] < own[1] and own[0] < r[1]:
+                    # a later Transpose that is itself read through its source writes nothing
+                    if later.op == "Transpose" and self._transpose_reads_through(later):
+                        continue
                     return False
         return True
+
+    def _transpose_reads_through(self, node: Node) -> bool:
+        """Whether op_Transpose will lower this Transpose to nothing by letting its MatMuls read its
+        source through strides: the same test, on the same source and strides, that op_Transpose
+        applies when it reaches the node (a Split view's source, else the Transpose's input)."""
+        if id(node) in self._written_through:
+            return True
+        x = node.input(0)
+        perm = ops.transpose_perm(node, x.tensor_type.rank)
+        view = self._split_view_of(x)
+        if view is not None:
+            src, ss, _ = view
+            return self._read_through(node, src, [ss[p] for p in perm])
+        ss = _strides(x.tensor_type.shape)
+        return self._read_through(node, x, [ss[p] for p in perm])
 
     def _kmajor_b_only(self, out: Value, view_strides: list[int]) -> bool:
         """Whether a Transpose's output is read only as the N-major B operand of batched MatMuls
