@@ -52,6 +52,8 @@ struct GemmParams {
     // the output only feeds a GlobalAveragePool of gap_hw pixels per image: c receives the
     // tensor-core epilogue's 32-row partial sums instead (0: the output itself)
     int gap_hw;
+    // TF32 mode: B may enter as its TF32 part alone (one weight plane; the wide pair forms use it)
+    int one_plane;
     int *err;                     // device word for bounded-wait timeouts (may be NULL)
     // split-K scratch of the model (NULL: no split): room for the partial tiles
     float *split_ws;

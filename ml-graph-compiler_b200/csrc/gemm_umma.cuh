@@ -580,7 +580,8 @@ constexpr uint32_t SMEM_LIMIT = 232448;  // dynamic shared memory per block on s
 // panel (every K block, hi and lo) into shared memory once; the stages then carry A only.
 // PAIR: CTA-pair variant (TF32 mode): 256-row tiles, each CTA holding one plane of B.
 // WIDE (a pair with BN = 256): 256 x 256 tiles; each CTA holds both planes of its 128 B rows and
-// the hi and lo products go to one accumulator through two N = 256 MMAs per K step.
+// the hi and lo products go to one accumulator through two N = 256 MMAs per K step. SP (wide
+// only): the weights in one TF32 plane (B_hi, B rounded to the nearest TF32), one MMA per K step.
 // SR (one CTA per tile, TF32, with a residual): the residual moves through its own staging
 // buffer, so the next pass's residual loads while this pass's output is stored; SR = 2 runs the
 // epilogue in passes of 64 columns, so that both buffers take the shared memory of one.
@@ -590,13 +591,14 @@ constexpr uint32_t SMEM_LIMIT = 232448;  // dynamic shared memory per block on s
 // the stage's slack): they are never stored.
 constexpr uint32_t PHASE_STAGE_BYTES = 26624;  // 7 packed rows of 3,712 bytes plus slack (1024-aligned)
 constexpr int POOL_PER_THREAD = 4;             // pooled bands: pooled columns per epilogue thread (PW <= 64)
-template <int BN, int MODE, int RB = 0, int PAIR = 0, int SR = 0, int PH = 0>
+template <int BN, int MODE, int RB = 0, int PAIR = 0, int SR = 0, int PH = 0, int SP = 0>
 struct Cfg {
     static_assert(!SR || (!PAIR && MODE == TF32), "a separate residual buffer is a one-CTA TF32 form");
     static_assert(!PH || (!PAIR && !SR && RB && MODE == TF32 && BN == 64),
                   "phase-split tiles: one CTA, TF32, N tile 64, B resident");
     static_assert(!PAIR || MODE == TF32, "CTA pairs run TF32 mode only");
     static constexpr bool WIDE = PAIR && BN > 128;
+    static_assert(!SP || WIDE, "one weight plane: wide pairs only");
     static_assert(BN <= 128 || (WIDE && RB == 0 && BN % 64 == 0 && BN <= 256),
                   "N tiles of 192 and 256 are pair-only, without B residency");
     static_assert(MODE != DYN || (!PAIR && !RB && !SR), "dynamic-B GEMMs run one CTA per tile");
@@ -604,7 +606,7 @@ struct Cfg {
     static constexpr int REGIONS = MODE == STRICT ? 4 : 1;  // TMEM regions per K block
     static constexpr int BROWS = WIDE ? BN / 2 : BN;         // B rows of one plane in this CTA
     static constexpr uint32_t B_TILE_BYTES = BROWS * BK * 4;
-    static constexpr int B_PLANES = (PAIR && !WIDE) || MODE == DYN || PH ? 1 : 2;  // B planes in this CTA's smem
+    static constexpr int B_PLANES = (PAIR && !WIDE) || MODE == DYN || PH || SP ? 1 : 2;  // B planes in this CTA's smem
     static constexpr int TM = PAIR ? 2 * BM : BM;            // rows of one tile
     static constexpr int EN = WIDE || SR == 2 ? 64 : BN;     // columns of one epilogue pass
     static constexpr int NH = BN / EN;                       // epilogue passes per tile
@@ -648,9 +650,9 @@ struct Cfg {
 // and walks the M tiles b / n_tiles, + gridDim.x / n_tiles, ... The shared-memory stage ring and
 // the TMEM buffer ring run on a K-block counter that continues across tiles, so the next tile's
 // loads and MMAs overlap this tile's drain and epilogue.
-template <int BN, int MODE, int RB, int PAIR, int SR, int PH>
+template <int BN, int MODE, int RB, int PAIR, int SR, int PH, int SP = 0>
 __global__ void __launch_bounds__(THREADS, 1) umma_gemm_kernel(const __grid_constant__ Params p) {
-    using C = Cfg<BN, MODE, RB, PAIR, SR, PH>;
+    using C = Cfg<BN, MODE, RB, PAIR, SR, PH, SP>;
     constexpr int S = C::STAGES;
     constexpr int R = C::REGIONS;
     constexpr int TB = C::TBUFS;
@@ -1149,14 +1151,14 @@ __global__ void __launch_bounds__(THREADS, 1) umma_gemm_kernel(const __grid_cons
                             if (k == 0) peek = mbar_test_wait(next_ready, next_parity);
                         }
                         have = peek;
-                    } else if (C::WIDE) {
+                    } else if (C::WIDE && !SP) {
                         // B_hi's and B_lo's products into one accumulator
                         have = mma_block4_wide(dbase, ad, bd, bld, idesc2, first ? 0u : 1u, next_ready, next_parity);
                     } else {
                         // B_lo's tile directly follows B_hi's in the stage with the same
                         // 128B-swizzled row layout, so one descriptor spans both as 2 BN rows: one
                         // MMA, A read once per K step (a pair: the same descriptor names B_hi in
-                        // rank 0, B_lo in rank 1)
+                        // rank 0, B_lo in rank 1; SP: each rank's BN / 2 rows of the one plane)
                         have = mma_block4<PAIR>(dbase, ad, bd, idesc2, first ? 0u : 1u, next_ready, next_parity);
                     }
                     // shared-memory slot free once these MMAs read it (in both CTAs of a pair)
@@ -1782,18 +1784,18 @@ inline bool make_map_4d(CUtensorMap *map, const void *base, long long cols, long
     return r == CUDA_SUCCESS;
 }
 
-template <int BN, int MODE, int RB, int PAIR, int SR = 0, int PH = 0>
+template <int BN, int MODE, int RB, int PAIR, int SR = 0, int PH = 0, int SP = 0>
 inline uint32_t launch_smem(const Params &p) {
-    using C = Cfg<BN, MODE, RB, PAIR, SR, PH>;
+    using C = Cfg<BN, MODE, RB, PAIR, SR, PH, SP>;
     const uint32_t smem = C::SMEM_BYTES + (RB ? p.b_res_bytes : 0u);
     return PAIR && smem < SMEM_LIMIT / 2 + 1024 ? SMEM_LIMIT / 2 + 1024 : smem;
 }
 
-template <int BN, int MODE, int RB, int PAIR, int SR = 0, int PH = 0>
+template <int BN, int MODE, int RB, int PAIR, int SR = 0, int PH = 0, int SP = 0>
 inline int launch(const Params &p_in, int grid, cudaStream_t stream) {
-    using C = Cfg<BN, MODE, RB, PAIR, SR, PH>;
+    using C = Cfg<BN, MODE, RB, PAIR, SR, PH, SP>;
     Params p = p_in;
-    uint32_t smem = launch_smem<BN, MODE, RB, PAIR, SR, PH>(p);
+    uint32_t smem = launch_smem<BN, MODE, RB, PAIR, SR, PH, SP>(p);
     // a second output staging tile where shared memory has room for it and the epilogue stores
     // by TMA without a residual staged in the output tile (MGC_CUDA_OUT2=0 keeps one, for
     // comparisons)
@@ -1806,9 +1808,9 @@ inline int launch(const Params &p_in, int grid, cudaStream_t stream) {
         if (need > smem) smem = need;
     }
     // per device (the attribute belongs to the current context); allowed under capture
-    MGC_CHECK(raise_smem_ceiling((const void *)umma_gemm_kernel<BN, MODE, RB, PAIR, SR, PH>));
+    MGC_CHECK(raise_smem_ceiling((const void *)umma_gemm_kernel<BN, MODE, RB, PAIR, SR, PH, SP>));
     if (!PAIR) {
-        umma_gemm_kernel<BN, MODE, RB, PAIR, SR, PH><<<grid, THREADS, smem, stream>>>(p);
+        umma_gemm_kernel<BN, MODE, RB, PAIR, SR, PH, SP><<<grid, THREADS, smem, stream>>>(p);
         return check_launch("umma_gemm_kernel");
     }
     cudaLaunchConfig_t cfg = {};
@@ -1823,7 +1825,7 @@ inline int launch(const Params &p_in, int grid, cudaStream_t stream) {
     cfg.stream = stream;
     cfg.attrs = attr;
     cfg.numAttrs = 1;
-    MGC_CHECK_CUDA(cudaLaunchKernelEx(&cfg, umma_gemm_kernel<BN, MODE, RB, PAIR, SR, PH>, p));
+    MGC_CHECK_CUDA(cudaLaunchKernelEx(&cfg, umma_gemm_kernel<BN, MODE, RB, PAIR, SR, PH, SP>, p));
     return check_launch("umma_gemm_kernel (pair)");
 }
 
@@ -1921,12 +1923,12 @@ inline int pair_clusters() {
 }
 
 // Wide CTA-pair launch: 256 x BN tiles, BN 192 or 256 (p.m_tiles and p.n_tiles count them;
-// p.tmB boxes both planes of BN / 2 rows).
-template <int BN>
+// p.tmB boxes both planes of BN / 2 rows, or with SP the TF32 plane only).
+template <int BN, int SP = 0>
 inline int launch_wide(Params &p, int clusters, cudaStream_t stream) {
     p.b_res_bytes = 0;
     const long long tiles = (long long)p.n_tiles * p.m_tiles;
-    return launch<BN, TF32, 0, 1>(p, 2 * (int)(tiles < clusters ? tiles : clusters), stream);
+    return launch<BN, TF32, 0, 1, 0, 0, SP>(p, 2 * (int)(tiles < clusters ? tiles : clusters), stream);
 }
 
 // CTA-pair launch (TF32 mode, tiled or 32-channel im2col A): p.m_tiles counts 256-row tiles and
@@ -2238,20 +2240,25 @@ inline int try_gemm_umma(const GemmParams &p, cudaStream_t stream, int *taken) {
         const bool w256 = clusters > 0 && (wide_env == 1 || (worth && pair_m * wide_n >= clusters && 176 * waves_w < 100 * waves_p));
         const bool w192 = !w256 && clusters3 > 0 && clusters3 == clusters &&
                           (wide_env == 3 || (wide_env == 2 && worth && 138 * waves_3 < 100 * waves_p));
-        CUtensorMap map3;
-        if (w192 && umma::make_map_b(&map3, p.b_umma, p.b_umma_lo, p.N, kp, 96)) {
+        // one weight plane (p.one_plane): boxes of the TF32 part only, one MMA per K step
+        const int planes = p.one_plane ? 1 : 2;
+        CUtensorMap map3, map1;
+        if (w192 && umma::make_map_b(&map3, p.b_umma, p.b_umma_lo, p.N, kp, 96, planes)) {
             u.tmB = map3;
             u.m_tiles = (int)pair_m;
             u.n_tiles = (int)w3_n;
-            const int st = umma::launch_wide<192>(u, clusters3, stream);
+            const int st = p.one_plane ? umma::launch_wide<192, 1>(u, clusters3, stream)
+                                       : umma::launch_wide<192>(u, clusters3, stream);
             if (st != MGC_CUDA_OK) return st;
             *taken = 1;
             return MGC_CUDA_OK;
         }
-        if (w256) {
+        if (w256 && (!p.one_plane || umma::make_map_b(&map1, p.b_umma, p.b_umma_lo, p.N, kp, 128, 1))) {
+            if (p.one_plane) u.tmB = map1;
             u.m_tiles = (int)pair_m;
             u.n_tiles = (int)wide_n;
-            const int st = umma::launch_wide<256>(u, clusters, stream);
+            const int st = p.one_plane ? umma::launch_wide<256, 1>(u, clusters, stream)
+                                       : umma::launch_wide<256>(u, clusters, stream);
             if (st != MGC_CUDA_OK) return st;
             *taken = 1;
             return MGC_CUDA_OK;

@@ -120,6 +120,7 @@ inline int decode_gemm(const mgc_cuda_launch &L, const Bases &bases, GemmParams 
     p.phase_w = (int)i[53];
     p.pool_ph = (int)i[54]; p.pool_pw = (int)i[55];
     p.gap_hw = (int)i[56];
+    p.one_plane = (int)i[57];
     if (!p.a || !p.b || !p.c) return fail(MGC_CUDA_BAD_ARGUMENT, "gemm: missing operand");
     return MGC_CUDA_OK;
 }

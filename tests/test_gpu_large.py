@@ -14,6 +14,7 @@ import numpy as np
 import pytest
 
 import cases
+from mgc_cuda.lowering import tf32_split
 from mgc_cuda.runtime import compile_graph
 from ml_graph_compiler.ir import Graph, TensorType
 from ml_graph_compiler.passes import optimize
@@ -98,13 +99,9 @@ GEMM_FORMS = {"single": (1024, 512, 128), "pair": (20480, 512, 128), "wide": (97
               "wide192": (4000, 768, 704), "split": (100, 4608, 256)}
 
 
-@pytest.mark.parametrize("form", sorted(GEMM_FORMS))
-def test_tf32_gemm_keeps_weights_exact(form: str) -> None:
-    """With TF32-exact activations, the only error TF32 mode has left is the fp32 accumulation:
-    the weights enter exactly, as their TF32 part plus the residual, in every kernel form
-    (without the residual the error would be about 3e-4 of the largest output)."""
-    m, k, n = GEMM_FORMS[form]
-    r = np.random.default_rng(3)
+def _run_gemm(form: str, m: int, k: int, n: int, seed: int = 3) -> tuple[np.ndarray, ...]:
+    """A one-Gemm graph (TF32 mode) on TF32-exact activations: (x, w, bias, output)."""
+    r = np.random.default_rng(seed)
     x = _tf32_exact(r.standard_normal((m, k)).astype(np.float32))
     w = r.standard_normal((k, n)).astype(np.float32)
     bias = r.standard_normal(n).astype(np.float32)
@@ -123,9 +120,36 @@ def test_tf32_gemm_keeps_weights_exact(form: str) -> None:
     finally:
         model.close()
     assert np.array_equal(got, again), f"{form}: two runs differ"
+    return x, w, bias, got
+
+
+@pytest.mark.parametrize("form", sorted(GEMM_FORMS))
+def test_tf32_gemm_keeps_weights_exact(form: str, monkeypatch: pytest.MonkeyPatch) -> None:
+    """With TF32-exact activations and exact weights asked for (MGC_CUDA_WEIGHT_PLANES=2, what
+    TF32 mode does for graphs with convolutions), the only error left is the fp32 accumulation:
+    the weights enter as their TF32 part plus the residual in every kernel form (without the
+    residual the error would be about 3e-4 of the largest output)."""
+    monkeypatch.setenv("MGC_CUDA_WEIGHT_PLANES", "2")
+    x, w, bias, got = _run_gemm(form, *GEMM_FORMS[form])
     want = x.astype(np.float64) @ w.astype(np.float64) + bias.astype(np.float64)
     err = float(np.abs(got - want).max() / np.abs(want).max())
     assert err <= 2e-5, f"{form}: max error {err:.3g} of the largest output"
+
+
+@pytest.mark.parametrize("form,shape", [("wide192", GEMM_FORMS["wide192"]), ("wide256", (8192, 512, 1024))])
+def test_tf32_wide_pairs_take_one_weight_plane(form: str, shape: tuple) -> None:
+    """A graph without convolutions lets the wide CTA-pair forms (256 x 192 and 256 x 256 tiles
+    chosen here by the cost model) take the weights as their TF32 part alone, one MMA per K step:
+    the result is the product with B_hi (the weights rounded to the nearest TF32 value) up to the
+    fp32 accumulation, and measurably not the product with exact weights."""
+    x, w, bias, got = _run_gemm(form, *shape, seed=5)
+    hi, _ = tf32_split(w)
+    xs = x.astype(np.float64)
+    want = xs @ hi.astype(np.float64) + bias.astype(np.float64)
+    exact = xs @ w.astype(np.float64) + bias.astype(np.float64)
+    scale = float(np.abs(want).max())
+    assert float(np.abs(got - want).max()) <= 2e-5 * scale, form
+    assert float(np.abs(got - exact).max()) > 1e-4 * scale, f"{form}: the weights entered exactly"
 
 
 def test_tf32_batched_matmul_of_activations_is_exact_for_tf32_inputs() -> None:
