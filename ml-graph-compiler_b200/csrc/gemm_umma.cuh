@@ -581,7 +581,8 @@ constexpr uint32_t SMEM_LIMIT = 232448;  // dynamic shared memory per block on s
 // PAIR: CTA-pair variant (TF32 mode): 256-row tiles, each CTA holding one plane of B.
 // WIDE (a pair with BN = 256): 256 x 256 tiles; each CTA holds both planes of its 128 B rows and
 // the hi and lo products go to one accumulator through two N = 256 MMAs per K step. SP (wide
-// only): the weights in one TF32 plane (B_hi, B rounded to the nearest TF32), one MMA per K step.
+// pairs, or one-CTA TF32 tiles): the weights in one TF32 plane (B_hi, B rounded to the nearest
+// TF32), one N = BN MMA per K step into one accumulator.
 // SR (one CTA per tile, TF32, with a residual): the residual moves through its own staging
 // buffer, so the next pass's residual loads while this pass's output is stored; SR = 2 runs the
 // epilogue in passes of 64 columns, so that both buffers take the shared memory of one.
@@ -598,11 +599,11 @@ struct Cfg {
                   "phase-split tiles: one CTA, TF32, N tile 64, B resident");
     static_assert(!PAIR || MODE == TF32, "CTA pairs run TF32 mode only");
     static constexpr bool WIDE = PAIR && BN > 128;
-    static_assert(!SP || WIDE, "one weight plane: wide pairs only");
+    static_assert(!SP || WIDE || (!PAIR && !PH && MODE == TF32), "one weight plane: wide pairs or one-CTA TF32");
     static_assert(BN <= 128 || (WIDE && RB == 0 && BN % 64 == 0 && BN <= 256),
                   "N tiles of 192 and 256 are pair-only, without B residency");
     static_assert(MODE != DYN || (!PAIR && !RB && !SR), "dynamic-B GEMMs run one CTA per tile");
-    static constexpr bool ONEACC = WIDE || MODE == DYN || PH;  // one accumulator (no B_lo columns)
+    static constexpr bool ONEACC = WIDE || MODE == DYN || PH || SP;  // one accumulator (no B_lo columns)
     static constexpr int REGIONS = MODE == STRICT ? 4 : 1;  // TMEM regions per K block
     static constexpr int BROWS = WIDE ? BN / 2 : BN;         // B rows of one plane in this CTA
     static constexpr uint32_t B_TILE_BYTES = BROWS * BK * 4;
@@ -2342,7 +2343,16 @@ inline int try_gemm_umma(const GemmParams &p, cudaStream_t stream, int *taken) {
     if (u.im2col == 5) st = umma::launch_phase(u, m_tiles, stream);
     else if (strict) st = umma::launch_best<64, umma::STRICT>(u, m_tiles, stream);
     else if (bn == 64) st = umma::launch_best<64, umma::TF32>(u, m_tiles, stream);
-    else if (u.tma_res && sr_env) st = umma::launch_best_sr(u, m_tiles, stream);
+    else if (u.tma_res && sr_env && p.one_plane) {
+        // one weight plane: the streamed form with 64-column passes, B boxes of the TF32 part
+        CUtensorMap map1;
+        if (!umma::make_map_b(&map1, p.b_umma, p.b_umma_lo, p.N, kp, bn, 1)) return MGC_CUDA_OK;
+        u.tmB = map1;
+        u.b_res_bytes = 0;
+        const long long tiles = (long long)u.n_tiles * m_tiles;
+        const int sms = sm_count();
+        st = umma::launch<128, umma::TF32, 0, 0, 2, 0, 1>(u, (int)(tiles < sms ? tiles : sms), stream);
+    } else if (u.tma_res && sr_env) st = umma::launch_best_sr(u, m_tiles, stream);
     else st = umma::launch_best<128, umma::TF32>(u, m_tiles, stream);
     if (st != MGC_CUDA_OK) return st;
     *taken = 1;

@@ -152,6 +152,48 @@ def test_tf32_wide_pairs_take_one_weight_plane(form: str, shape: tuple) -> None:
     assert float(np.abs(got - exact).max()) > 1e-4 * scale, f"{form}: the weights entered exactly"
 
 
+def test_tf32_residual_gemm_takes_one_weight_plane(monkeypatch: pytest.MonkeyPatch) -> None:
+    """GPT-2's output projection shape (2048 x 768 x 768 + residual, one-CTA tiles with the residual
+    in its own staging): in a graph without convolutions the weights enter as their TF32 part
+    alone (one N = 128 MMA per K step), so the result is the product with B_hi up to the fp32
+    accumulation; with MGC_CUDA_WEIGHT_PLANES=2 it is the exact-weight product."""
+    m, k, n = 2048, 768, 768
+    r = np.random.default_rng(11)
+    x = _tf32_exact(r.standard_normal((m, k)).astype(np.float32))
+    w = r.standard_normal((k, n)).astype(np.float32)
+    bias = r.standard_normal(n).astype(np.float32)
+    res = r.standard_normal((m, n)).astype(np.float32)
+
+    def run() -> np.ndarray:
+        g = Graph("gemm_residual")
+        xi = g.add_input("x", TensorType("float32", (m, k)))
+        ri = g.add_input("r", TensorType("float32", (m, n)))
+        y = g.add_node("Gemm", [xi, g.constant(w), g.constant(bias)]).output
+        z = g.add_node("Add", [y, ri]).output
+        g.add_output(z, "z")
+        infer_shapes(g)
+        optimize(g, "O3")
+        schedule(g)
+        assert [nd.op for nd in g.nodes] == ["FusedGemm"]
+        model = compile_graph(g, precision="tf32")
+        try:
+            return model.run({"x": x, "r": res})["z"].astype(np.float64)
+        finally:
+            model.close()
+
+    hi, _ = tf32_split(w)
+    base = bias.astype(np.float64) + res.astype(np.float64)
+    want1 = x.astype(np.float64) @ hi.astype(np.float64) + base
+    want2 = x.astype(np.float64) @ w.astype(np.float64) + base
+    scale = float(np.abs(want2).max())
+    got1 = run()
+    assert float(np.abs(got1 - want1).max()) <= 2e-5 * scale
+    assert float(np.abs(got1 - want2).max()) > 1e-4 * scale
+    monkeypatch.setenv("MGC_CUDA_WEIGHT_PLANES", "2")
+    got2 = run()
+    assert float(np.abs(got2 - want2).max()) <= 2e-5 * scale
+
+
 def test_tf32_batched_matmul_of_activations_is_exact_for_tf32_inputs() -> None:
     """Attention-shaped batched MatMuls on the tensor cores: Q K^T with both operands read through
     their head Transposes (two batch dimensions, strided rows), and P V with V N-major (copied
