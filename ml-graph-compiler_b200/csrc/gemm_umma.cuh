@@ -598,7 +598,9 @@ struct Cfg {
     static_assert(!PH || (!PAIR && !SR && RB && MODE == TF32 && BN == 64),
                   "phase-split tiles: one CTA, TF32, N tile 64, B resident");
     static_assert(!PAIR || MODE == TF32, "CTA pairs run TF32 mode only");
-    static constexpr bool WIDE = PAIR && BN > 128;
+    // wide layout: each CTA of the pair holds the B rows of its half of the N tile (N tiles of
+    // 192 and 256; with one weight plane, also 128)
+    static constexpr bool WIDE = PAIR && (BN > 128 || SP);
     static_assert(!SP || WIDE || (!PAIR && !PH && MODE == TF32), "one weight plane: wide pairs or one-CTA TF32");
     static_assert(BN <= 128 || (WIDE && RB == 0 && BN % 64 == 0 && BN <= 256),
                   "N tiles of 192 and 256 are pair-only, without B residency");
@@ -1923,8 +1925,8 @@ inline int pair_clusters() {
     return n;
 }
 
-// Wide CTA-pair launch: 256 x BN tiles, BN 192 or 256 (p.m_tiles and p.n_tiles count them;
-// p.tmB boxes both planes of BN / 2 rows, or with SP the TF32 plane only).
+// Wide CTA-pair launch: 256 x BN tiles, BN 192 or 256, or 128 with SP (p.m_tiles and p.n_tiles
+// count them; p.tmB boxes both planes of BN / 2 rows, or with SP the TF32 plane only).
 template <int BN, int SP = 0>
 inline int launch_wide(Params &p, int clusters, cudaStream_t stream) {
     p.b_res_bytes = 0;
@@ -2270,11 +2272,14 @@ inline int try_gemm_umma(const GemmParams &p, cudaStream_t stream, int *taken) {
         const bool worth = bn == 128 && u.num_kb >= (p.res ? 16 : 8);
         const int clusters = bn == 64 ? umma::pair_clusters<64, 0>() : umma::pair_clusters<128, 0>();
         CUtensorMap plane_map;
+        // one weight plane (N tiles of 128): the wide layout, each CTA with 64 rows of B_hi
+        const bool sp = p.one_plane && bn == 128;
         if (clusters > 0 && (pair_env == 1 || (worth && pair_m * u.n_tiles >= clusters)) &&
-            umma::make_map_b(&plane_map, p.b_umma, p.b_umma_lo, p.N, kp, bn, 1)) {
+            umma::make_map_b(&plane_map, p.b_umma, p.b_umma_lo, p.N, kp, sp ? 64 : bn, 1)) {
             u.tmB = plane_map;
             u.m_tiles = (int)pair_m;
-            const int st = bn == 64 ? umma::launch_pair<64>(u, clusters, stream) : umma::launch_pair<128>(u, clusters, stream);
+            const int st = sp ? umma::launch_wide<128, 1>(u, clusters, stream)
+                         : bn == 64 ? umma::launch_pair<64>(u, clusters, stream) : umma::launch_pair<128>(u, clusters, stream);
             if (st != MGC_CUDA_OK) return st;
             *taken = 1;
             return MGC_CUDA_OK;

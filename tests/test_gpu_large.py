@@ -136,10 +136,12 @@ def test_tf32_gemm_keeps_weights_exact(form: str, monkeypatch: pytest.MonkeyPatc
     assert err <= 2e-5, f"{form}: max error {err:.3g} of the largest output"
 
 
-@pytest.mark.parametrize("form,shape", [("wide192", GEMM_FORMS["wide192"]), ("wide256", (8192, 512, 1024))])
+@pytest.mark.parametrize("form,shape", [("wide192", GEMM_FORMS["wide192"]), ("wide256", (8192, 512, 1024)),
+                                        ("pair128", GEMM_FORMS["pair"])])
 def test_tf32_wide_pairs_take_one_weight_plane(form: str, shape: tuple) -> None:
-    """A graph without convolutions lets the wide CTA-pair forms (256 x 192 and 256 x 256 tiles
-    chosen here by the cost model) take the weights as their TF32 part alone, one MMA per K step:
+    """A graph without convolutions lets the CTA-pair forms (256 x 192, 256 x 256 and 256 x 128
+    tiles chosen here by the cost model; the last in the wide layout, each CTA holding 64 rows of
+    B_hi) take the weights as their TF32 part alone, one MMA per K step:
     the result is the product with B_hi (the weights rounded to the nearest TF32 value) up to the
     fp32 accumulation, and measurably not the product with exact weights."""
     x, w, bias, got = _run_gemm(form, *shape, seed=5)
