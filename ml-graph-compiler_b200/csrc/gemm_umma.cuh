@@ -2318,9 +2318,15 @@ inline int try_gemm_umma(const GemmParams &p, cudaStream_t stream, int *taken) {
                 u.b_res_bytes = 0;
                 const long long units = tiles * splits;
                 const int grid = (int)(units < sms ? units : sms);
+                // one weight plane: boxes of the TF32 part, one N = BN MMA per K step
+                CUtensorMap map1;
+                const bool sp = !strict && p.one_plane && umma::make_map_b(&map1, p.b_umma, p.b_umma_lo, p.N, kp, bn, 1);
+                if (sp) u.tmB = map1;
                 int st = strict ? umma::launch<64, umma::STRICT, 0, 0, 0>(u, grid, stream)
-                         : bn == 64 ? umma::launch<64, umma::TF32, 0, 0, 0>(u, grid, stream)
-                                    : umma::launch<128, umma::TF32, 0, 0, 0>(u, grid, stream);
+                         : bn == 64 ? (sp ? umma::launch<64, umma::TF32, 0, 0, 0, 0, 1>(u, grid, stream)
+                                          : umma::launch<64, umma::TF32, 0, 0, 0>(u, grid, stream))
+                                    : (sp ? umma::launch<128, umma::TF32, 0, 0, 0, 0, 1>(u, grid, stream)
+                                          : umma::launch<128, umma::TF32, 0, 0, 0>(u, grid, stream));
                 if (st != MGC_CUDA_OK) return st;
                 const long long outs = (long long)p.M * p.N;
                 if (strict)
@@ -2358,7 +2364,18 @@ inline int try_gemm_umma(const GemmParams &p, cudaStream_t stream, int *taken) {
         const int sms = sm_count();
         st = umma::launch<128, umma::TF32, 0, 0, 2, 0, 1>(u, (int)(tiles < sms ? tiles : sms), stream);
     } else if (u.tma_res && sr_env) st = umma::launch_best_sr(u, m_tiles, stream);
-    else st = umma::launch_best<128, umma::TF32>(u, m_tiles, stream);
+    else if (p.one_plane && !u.tma_res) {
+        // one weight plane without a residual: streamed one-CTA tiles on boxes of the TF32 part
+        CUtensorMap map1;
+        if (umma::make_map_b(&map1, p.b_umma, p.b_umma_lo, p.N, kp, bn, 1)) {
+            u.tmB = map1;
+            const long long tiles = (long long)u.n_tiles * m_tiles;
+            const int sms = sm_count();
+            st = umma::launch<128, umma::TF32, 0, 0, 0, 0, 1>(u, (int)(tiles < sms ? tiles : sms), stream);
+        } else {
+            st = umma::launch_best<128, umma::TF32>(u, m_tiles, stream);
+        }
+    } else st = umma::launch_best<128, umma::TF32>(u, m_tiles, stream);
     if (st != MGC_CUDA_OK) return st;
     *taken = 1;
     return MGC_CUDA_OK;

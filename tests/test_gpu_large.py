@@ -137,11 +137,12 @@ def test_tf32_gemm_keeps_weights_exact(form: str, monkeypatch: pytest.MonkeyPatc
 
 
 @pytest.mark.parametrize("form,shape", [("wide192", GEMM_FORMS["wide192"]), ("wide256", (8192, 512, 1024)),
-                                        ("pair128", GEMM_FORMS["pair"])])
-def test_tf32_wide_pairs_take_one_weight_plane(form: str, shape: tuple) -> None:
-    """A graph without convolutions lets the CTA-pair forms (256 x 192, 256 x 256 and 256 x 128
-    tiles chosen here by the cost model; the last in the wide layout, each CTA holding 64 rows of
-    B_hi) take the weights as their TF32 part alone, one MMA per K step:
+                                        ("pair128", GEMM_FORMS["pair"]), ("single", GEMM_FORMS["single"]),
+                                        ("split", GEMM_FORMS["split"])])
+def test_tf32_gemms_take_one_weight_plane(form: str, shape: tuple) -> None:
+    """A graph without convolutions lets the tile forms (256 x 192, 256 x 256 and 256 x 128 CTA
+    pairs chosen here by the cost model, the last in the wide layout with 64 rows of B_hi per CTA;
+    one-CTA 128 x 128 tiles; split K) take the weights as their TF32 part alone, one MMA per K step:
     the result is the product with B_hi (the weights rounded to the nearest TF32 value) up to the
     fp32 accumulation, and measurably not the product with exact weights."""
     x, w, bias, got = _run_gemm(form, *shape, seed=5)
