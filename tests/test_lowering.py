@@ -471,3 +471,19 @@ def test_gpt2_split_outputs_are_views_on_the_naive_plan() -> None:
     assert len(splits) == 12
     for rec in splits:
         assert rec.i[29] == 3 and list(rec.i[30:33]) == [768, 768, 768] and rec.i[34] == 2 * 128
+
+
+def test_weight_plane_policy(monkeypatch: pytest.MonkeyPatch) -> None:
+    """TF32 mode marks the GEMM records of a graph without convolutions (slot i[57]) so that the
+    tile forms may take the weights as their TF32 part alone; graphs with convolutions keep exact
+    weights, as do strict mode and MGC_CUDA_WEIGHT_PLANES=2."""
+    def flags(g: Graph, precision: str) -> set[int]:
+        return {int(r.i[57]) for r in lower_graph(g, precision=precision).launches if r.kind == K_GEMM}
+
+    gpt = o3(zoo.tiny_transformer(kind="gpt"))
+    cnn = o3(zoo.tiny_cnn(batch=2))
+    assert flags(gpt, "tf32") == {1}
+    assert flags(gpt, "strict") == {0}
+    assert flags(cnn, "tf32") == {0}
+    monkeypatch.setenv("MGC_CUDA_WEIGHT_PLANES", "2")
+    assert flags(gpt, "tf32") == {0}
